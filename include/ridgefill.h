@@ -1,0 +1,345 @@
+/* ridgefill.h -- the C ABI of the B200 RidgeFill kernel library: operand positions, the formulas that
+ * define each op's answer, the parsed-operand structs the CUDA kernels take by value, and the
+ * extern "C" entry points.
+ *
+ * Interface it replaces: the reference's kernels/ridgefill.h (operand enums :50-57, shared formulas
+ * :62-104, parsed structs :112-272, entry points :278-310). The op names, operand order, parameter
+ * keys, refusal codes and the fail-safe rules are the reference's; the structs are this library's
+ * own (they never cross the ABI: a row receives a RadArgs and parses it here).
+ *
+ * The formulas below are compiled for host and device alike (RIDGEFILL_HD), so the parse and the
+ * kernels of one op read one definition.
+ */
+#ifndef RIDGEFILL_B200_H
+#define RIDGEFILL_B200_H
+
+#include "rad_abi.h"
+#include "rad_plugin.h"
+
+#include <math.h>
+#include <stdint.h>
+
+#if defined(__CUDACC__)
+#define RIDGEFILL_HD __host__ __device__ __forceinline__
+#else
+#define RIDGEFILL_HD static inline
+#endif
+
+/* ------------------------------------------------------------------ limits
+ * RIDGEFILL_MASK_MAX_ROWS: the window's keys live in one CTA's shared memory (4 bytes a row); the
+ * reference's device row stopped at 8,192 rows (kernels/ridgefill.h:32), this one at 49,152. The
+ * host-side refusal is b > this (RAD_E_SHAPE), as the reference refuses b > 8,192
+ * (kernels/mask.hip:82). */
+enum { RIDGEFILL_MASK_MAX_ROWS = 49152, RIDGEFILL_SELECT_PAIRS = 3 };
+
+/* Above this, softplus(x) is x to every bit f32 holds (kernels/ridgefill.h:37). */
+#define RIDGEFILL_SOFTPLUS_THRESHOLD 20.0f
+
+/* ridgefill_mask's `mode` (kernels/ridgefill.h:42). */
+enum { RIDGEFILL_MODE_NONE = 0, RIDGEFILL_MODE_CLASS = 1, RIDGEFILL_MODE_RANDOM = 2, RIDGEFILL_MODE_ALL = 3,
+       RIDGEFILL_MODE_STEP = 4 };
+
+/* ------------------------------------------------------------------ operand positions (schema order)
+ * The reference ops (kernels/ridgefill.h:51-57) and this library's new ones. */
+enum { MK_CU = 0, MK_TOKENS, MK_POS, MK_SCORE, MK_MASK, MK_BOUNDS, MK_ZEROS };
+enum { RH_A = 0, RH_MASK, RH_ALOG, RH_DTBIAS, RH_ND, RH_SIDX, RH_BOUNDS };
+enum { SC_STATE = 0, SC_STATE_IDX, SC_APPLIED, SC_APPLIED_IDX, SC_C, SC_ND, SC_ND_IDX, SC_BOUNDS };
+enum { SR_STATE = 0, SR_STATE_IDX, SR_OUT };
+enum { SL_MASK = 0, SL_X_SRC, SL_Q_SRC, SL_S_SRC, SL_X, SL_Q, SL_S };
+enum { DR_MASK = 0, DR_IDS };
+enum { HZ_CU = 0, HZ_POS, HZ_BOUNDS, HZ_SPAN, HZ_META, HZ_META_IDX, HZ_COUNT };
+/* ridgefill_gemm_nt_q (kernels/rows.cpp:74-76): a, a_scale, b, b_scale, y, a_sum, b_ref. */
+enum { GQ_A = 0, GQ_A_SCALE, GQ_B, GQ_B_SCALE, GQ_Y, GQ_A_SUM, GQ_B_REF };
+/* ridgefill_gemm_nt_q_bias (new): gemm_nt_q's operands, then the bias and an int32 debug output. */
+enum { GB_A = 0, GB_A_SCALE, GB_B, GB_B_SCALE, GB_BIAS, GB_Y, GB_ACC };
+/* ridgefill_quant_act_i8g (new; libr4d's quant_act_i8g operands, arch/ridgefill_layer.h:74-76). */
+enum { QA_X = 0, QA_Q, QA_S };
+/* ridgefill_gdn_fill (new; the chunk scan's operands, arch/qwen4exp_fill.h:55-60, without kkt:
+ * the intra-chunk transform is computed inside the op). */
+enum { GD_Q = 0, GD_K, GD_V, GD_G, GD_BETA, GD_STATE, GD_STATE_IDX, GD_CU, GD_O };
+
+/* ------------------------------------------------------------------ the shared formulas */
+
+/* Wellons' lowbias32 finaliser (kernels/ridgefill.h:66-71). */
+RIDGEFILL_HD uint32_t ridgefill_mix32(uint32_t x) {
+    x ^= x >> 16;
+    x *= 0x7feb352dU;
+    x ^= x >> 15;
+    x *= 0x846ca68bU;
+    x ^= x >> 16;
+    return x;
+}
+
+/* The random selector's rank key of absolute position `position` under `seed`
+ * (kernels/ridgefill.h:77-81): both seed halves folded through mix32, then the position's golden-ratio
+ * step mixed in. */
+RIDGEFILL_HD uint32_t ridgefill_row_hash(long long seed, uint32_t position) {
+    const unsigned long long s = (unsigned long long)seed;
+    const uint32_t folded = ridgefill_mix32((uint32_t)s ^ ridgefill_mix32((uint32_t)(s >> 32)));
+    return ridgefill_mix32(folded ^ (position * 0x9E3779B9U + 0x7F4A7C15U));
+}
+
+/* rho = clamp(N / D, 0, 1), 1 while D is not positive; a NaN ratio lands on 0
+ * (kernels/ridgefill.h:86-91). */
+RIDGEFILL_HD float ridgefill_rho(float n, float d) {
+    if (!(d > 0.0f)) return 1.0f;
+    const float r = n / d;
+    if (!(r > 0.0f)) return 0.0f;
+    return r < 1.0f ? r : 1.0f;
+}
+
+/* Two-sided softplus with the threshold above (kernels/ridgefill.h:94-97). */
+RIDGEFILL_HD float ridgefill_softplus(float x) {
+    if (x > RIDGEFILL_SOFTPLUS_THRESHOLD) return x;
+    return x > 0.0f ? x + log1pf(expf(-x)) : log1pf(expf(x));
+}
+
+RIDGEFILL_HD float ridgefill_bf16_to_f32(uint16_t h) {
+    const uint32_t bits = (uint32_t)h << 16;
+    float f;
+    memcpy(&f, &bits, sizeof f);
+    return f;
+}
+
+/* ridgefill_mask's window (kernels/ridgefill.h:130-139): s, e from cu_last, b the bulk end, n the mask's
+ * extent; w = {start, bulk end b', end}. False when cu_last is out of order; the window is then empty
+ * inside the clamped [s, e] (the device fail-safe). */
+RIDGEFILL_HD int ridgefill_mask_window(int64_t s, int64_t e, int64_t b, int64_t n, int64_t* w) {
+    const int valid = s >= 0 && s <= e && e <= n;
+    const int64_t end = e < 0 ? 0 : (e > n ? n : e);
+    const int64_t start = s < 0 ? 0 : (s > end ? end : s);
+    const int64_t bulk = b < start ? start : (b > end ? end : b);
+    w[0] = start;
+    w[1] = valid ? bulk : start;
+    w[2] = end;
+    return valid;
+}
+
+/* Where the 1s may start: row 0 in step mode with a non-empty window, else the window start
+ * (kernels/ridgefill.h:46-48). */
+RIDGEFILL_HD int64_t ridgefill_mask_from(int mode, const int64_t* w) {
+    return mode == RIDGEFILL_MODE_STEP && w[1] > w[0] ? 0 : w[0];
+}
+
+/* ------------------------------------------------------------------ parsed operands
+ * Plain scalars and pointers only: each is a kernel argument passed by value. */
+
+typedef struct RidgeFillMask {
+    const int32_t* cu_last;                       /* [2] {s, e}, device memory */
+    const int32_t* tokens;   int64_t b;           /* [b] ids of rows [0, b) */
+    const int32_t* positions; int64_t pos_stride;
+    const float*   score;    int64_t vocab;       /* null in none / all mode when absent */
+    int32_t*       mask;     int64_t n;
+    int32_t*       bounds;                        /* [4] {s, b', b', e} */
+    int32_t*       zeros;    int64_t n_zeros;
+    double         share;
+    long long      seed;
+    int            mode;
+} RidgeFillMask;
+
+/* Row i's class score: -inf for an id outside the table or a non-finite score
+ * (kernels/ridgefill.h:143-147). */
+RIDGEFILL_HD float ridgefill_mask_score(const RidgeFillMask* g, int64_t i) {
+    const int32_t id = g->tokens[i];
+    const float s = id >= 0 && id < g->vocab ? g->score[id] : -INFINITY;
+    return s > -INFINITY && s < INFINITY ? s : -INFINITY;
+}
+
+typedef struct RidgeFillRho {
+    const void*    a;        int64_t a_pitch, a_col; int a_bf16;
+    const int32_t* mask;
+    const float*   a_log;
+    const float*   dt_bias;
+    float*         nd;       int64_t nd_slot, nd_head, nd_inner, n_states;
+    const int32_t* state_idx;
+    const int32_t* bounds;                        /* [>=1] or null */
+    int64_t        n, n_head;
+} RidgeFillRho;
+
+/* First row of the recurrence: bounds[0] clamped into [0, n], 0 without bounds
+ * (kernels/ridgefill.h:163-167). */
+RIDGEFILL_HD int64_t ridgefill_rho_first_row(const RidgeFillRho* g) {
+    if (!g->bounds) return 0;
+    const int64_t s = g->bounds[0];
+    return s < 0 ? 0 : (s > g->n ? g->n : s);
+}
+
+typedef struct RidgeFillCorrect {
+    float*         state;    int64_t st_slot, st_head, st_row, st_col;
+    float*         applied;  int64_t ap_slot, ap_head;
+    const float*   c;        int64_t c_head, c_row;
+    const float*   nd;       int64_t nd_slot, nd_head, nd_inner;
+    const int32_t* st_idx;   const int32_t* ap_idx;  const int32_t* nd_idx;
+    int64_t        st_pitch, ap_pitch, nd_pitch;
+    int64_t        st_states, ap_states, nd_states;
+    int64_t        n_seq, n_head, sd0, sd1;
+    const int32_t* bounds;                        /* [>=2] or null */
+    float          alpha;
+    int            apply;                         /* 1 apply, 0 undo */
+} RidgeFillCorrect;
+
+/* False when the step's last sequence had no bulk row: the op then writes nothing
+ * (kernels/ridgefill.h:188-190). */
+RIDGEFILL_HD int ridgefill_correct_has_bulk(const RidgeFillCorrect* g) {
+    return !g->bounds || g->bounds[1] > g->bounds[0];
+}
+
+/* Sequence s's slot in each pool; false when any is outside its pool (kernels/ridgefill.h:194-201). */
+RIDGEFILL_HD int ridgefill_correct_slots(const RidgeFillCorrect* g, int64_t s, int64_t* st, int64_t* ap,
+                                         int64_t* nd) {
+    *st = g->st_idx[s * g->st_pitch];
+    *ap = g->ap_idx[s * g->ap_pitch];
+    *nd = g->nd ? g->nd_idx[s * g->nd_pitch] : 0;
+    return *st >= 0 && *st < g->st_states && *ap >= 0 && *ap < g->ap_states &&
+           (!g->nd || (*nd >= 0 && *nd < g->nd_states));
+}
+
+typedef struct RidgeFillStateRead {
+    const float*   state;    int64_t st_slot, st_head, st_row, st_col, n_states;
+    const int32_t* idx;      int64_t idx_pitch;
+    float*         out;
+    int64_t        n_seq, n_head, sd0, sd1;
+} RidgeFillStateRead;
+
+typedef struct RidgeFillHazard {
+    const int32_t* cu_last;
+    const int32_t* positions; int64_t pos_stride;
+    const int32_t* bounds;
+    int64_t        span;
+    float*         meta;     int64_t meta_slot, meta_states;
+    const int32_t* meta_idx;
+    float*         count;
+} RidgeFillHazard;
+
+/* The branch hazard rule on the step's last sequence (kernels/ridgefill.h:232-249): tail positions
+ * that came from the prefix cache at or below the slot's last approximated position are counted
+ * once; an approximate pass then records its last bulk position. */
+RIDGEFILL_HD void ridgefill_hazard_step(const RidgeFillHazard* g) {
+    const int32_t slot = g->meta_idx[0];
+    if (slot < 0 || slot >= g->meta_states) return;
+    float* m = g->meta + slot * g->meta_slot;
+    const int64_t s = g->cu_last[0], e = g->cu_last[1];
+    if (g->span > 0 && e > s) {
+        const int64_t p0 = g->positions[s * g->pos_stride];
+        const int64_t before = g->span - (e - s);
+        const int64_t counted = (int64_t)m[1], last = (int64_t)m[0];
+        const int64_t lo = p0 - before > counted ? p0 - before : counted;
+        const int64_t hi = p0 < last ? p0 : last;
+        if (before > 0 && hi > lo) {
+            g->count[0] += (float)(hi - lo);
+            m[1] = (float)hi;
+        }
+    }
+    if (g->bounds && g->bounds[1] > g->bounds[0])
+        m[0] = (float)(g->positions[(int64_t)(g->bounds[1] - 1) * g->pos_stride] + 1);
+}
+
+/* One ridgefill_select (source, destination) pair in bytes; `word` is 16, 4 or 1 (the widest unit every
+ * address, pitch and width is a multiple of), 0 when the pair is absent (kernels/ridgefill.h:254-259). */
+typedef struct RidgeFillCopy {
+    const unsigned char* src;
+    unsigned char*       dst;
+    int64_t              src_pitch, dst_pitch, row_bytes;
+    int                  word;
+} RidgeFillCopy;
+
+typedef struct RidgeFillSelect {
+    const int32_t* mask;     int64_t n;
+    RidgeFillCopy  pair[RIDGEFILL_SELECT_PAIRS];
+} RidgeFillSelect;
+
+typedef struct RidgeFillDrop {
+    const int32_t* mask;     int64_t n;
+    int32_t*       ids;      int64_t pitch, top_k;
+} RidgeFillDrop;
+
+/* ridgefill_gemm_nt_q / _bias: y[m, n] = sum over K blocks of a_scale[m, j] * b_scale[n, j] * (int32 dot of
+ * the block), folded in f32 in block order, rounded once to bf16; with a bias, rounded again after
+ * adding it (the gemm_nt_q + add pair of arch/ridgefill_layer.h:77-79, bit for bit). */
+typedef struct RidgeFillGemmQ {
+    const int8_t*  a;        int64_t lda;         /* [M, K] codes, row pitch lda (bytes) */
+    const float*   a_scale;  int64_t ldas;        /* [M, K/group] f32 */
+    const int8_t*  b;        int64_t ldb;         /* [N, K] codes (stored form == canonical) */
+    const float*   b_scale;                       /* stored form: f32 [K/group, N] */
+    const uint16_t* bias;                         /* [N] bf16 or null */
+    uint16_t*      y;        int64_t ldy;         /* [M, N] bf16 */
+    int32_t*       acc;                           /* optional [M, N, K/group] int32 block sums (debug) */
+    int64_t        M, N, K, group;
+} RidgeFillGemmQ;
+
+/* ridgefill_quant_act_i8g: x bf16 [M, K] -> q i8 [M, K], s f32 [M, K/group]: per group of `group` columns,
+ * s = absmax / 127 (1 for an all-zero group), q = round-half-even(x / s) clamped to [-127, 127]. */
+typedef struct RidgeFillQuant {
+    const uint16_t* x;       int64_t ldx;
+    int8_t*        q;        int64_t ldq;
+    float*         s;        int64_t lds;
+    int64_t        M, K, group;
+} RidgeFillQuant;
+
+/* ridgefill_gdn_fill: the gated delta rule over each sequence of cu_seqlens, state [slot, Hv, V, K] f32
+ * carried in place; per v-head h (k-head h / (Hv / Hk)) and row t:
+ *   S <- exp(g[t, h]) * S;  S <- S + beta[t, h] * (v_t - S k_t) k_t^T;  o_t = scale * S q_t.
+ * q, k [T, Hk, dk] bf16; v [T, Hv, dv] bf16; g (log decay) and beta f32 [T, Hv]; o [T, Hv, dv] bf16 or
+ * absent (state-only fill). */
+typedef struct RidgeFillGdn {
+    const uint16_t* q;       int64_t q_row, q_head;
+    const uint16_t* k;       int64_t k_row, k_head;
+    const uint16_t* v;       int64_t v_row, v_head;
+    const float*   g;        int64_t g_row;
+    const float*   beta;     int64_t b_row;
+    float*         state;    int64_t st_slot, st_head, n_states;
+    const int32_t* state_idx; int64_t idx_pitch;
+    const int32_t* cu;       int64_t n_seq;
+    uint16_t*      o;        int64_t o_row, o_head;
+    int64_t        T, n_head_k, n_head_v, dk, dv, chunk;
+    float          scale;
+} RidgeFillGdn;
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ entry points
+ * Parses shared by every row of an op: RAD_OK or a named refusal (kernels/ridgefill.h:278-285). */
+int ridgefill_mask_parse(const RadArgs* a, RidgeFillMask* out);
+int ridgefill_rho_parse(const RadArgs* a, RidgeFillRho* out);
+int ridgefill_correct_parse(const RadArgs* a, RidgeFillCorrect* out);
+int ridgefill_state_read_parse(const RadArgs* a, RidgeFillStateRead* out);
+int ridgefill_select_parse(const RadArgs* a, RidgeFillSelect* out);
+int ridgefill_drop_parse(const RadArgs* a, RidgeFillDrop* out);
+int ridgefill_hazard_parse(const RadArgs* a, RidgeFillHazard* out);
+int ridgefill_gemm_q_parse(const RadArgs* a, int with_bias, RidgeFillGemmQ* out);
+int ridgefill_quant_parse(const RadArgs* a, RidgeFillQuant* out);
+int ridgefill_gdn_parse(const RadArgs* a, RidgeFillGdn* out);
+
+/* The device rows (kernels/ridgefill.h:304-310 and the new ops): async launches on `s` (a
+ * cudaStream_t); no allocation, no synchronisation. */
+int ridgefill_mask_device(const RadArgs* a, RadStream s);
+int ridgefill_rho_device(const RadArgs* a, RadStream s);
+int ridgefill_correct_device(const RadArgs* a, RadStream s);
+int ridgefill_state_read_device(const RadArgs* a, RadStream s);
+int ridgefill_select_device(const RadArgs* a, RadStream s);
+int ridgefill_drop_device(const RadArgs* a, RadStream s);
+int ridgefill_hazard_device(const RadArgs* a, RadStream s);
+int ridgefill_gemm_nt_q_device(const RadArgs* a, RadStream s);
+int ridgefill_gemm_nt_q_bias_device(const RadArgs* a, RadStream s);
+int ridgefill_quant_act_device(const RadArgs* a, RadStream s);
+int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s);
+
+/* ridgefill_gdn_fill's scratch hook: device bytes the row needs in RadArgs::scratch. */
+int64_t ridgefill_gdn_fill_scratch(const RadArgs* a);
+
+/* ridgefill_gemm_nt_q's stored-form hooks for operand 2 (codes) and 3 (scale) of encoding
+ * i8*bf16[1x128] (the hooks arch/ridgefill_int8.h:87-130 calls). */
+int ridgefill_gemm_q_layout(const RadParam* p, int n_p, int operand, const RadEncoding* enc, const int* sel,
+                            const RadTensor* geom, int n_geom, RadLayout* out);
+int ridgefill_gemm_q_relayout(const RadParam* p, int n_p, int operand, const RadEncoding* enc, const int* sel,
+                              const RadTensor* src, int n_src, void* dst, int64_t dst_bytes);
+int ridgefill_gemm_q_unrelayout(const RadParam* p, int n_p, int operand, const RadEncoding* enc, const int* sel,
+                                const RadTensor* src, int n_src, void* dst, int64_t dst_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RIDGEFILL_B200_H */

@@ -1,0 +1,41 @@
+/* common.cuh -- helpers shared by the B200 RidgeFill device rows. */
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ridgefill.h"
+
+namespace rf {
+
+constexpr int kSMs = 148;   /* B200: 2 dies x 74 SMs; grids are sized in multiples of it */
+
+/* RAD_OK when the launch just issued on this thread was accepted, RAD_E_DEVICE otherwise. */
+inline int launch_status() { return cudaGetLastError() == cudaSuccess ? RAD_OK : RAD_E_DEVICE; }
+
+inline cudaStream_t as_stream(RadStream s) { return (cudaStream_t)s; }
+
+/* The number of SMs of the current device (148 on B200), queried once per process. */
+inline int sm_count() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0, v = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+            n = v;
+        else
+            n = kSMs;
+    }
+    return n;
+}
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
+
+/* f32 -> bf16 bits, round to nearest even (NaN kept quiet), the same rule as the host rad_f32_to_bf16. */
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x7fffffu)) return (uint16_t)((u >> 16) | 0x40u);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+}  // namespace rf

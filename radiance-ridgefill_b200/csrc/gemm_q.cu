@@ -1,0 +1,348 @@
+/* gemm_q.cu -- the int8 projector on B200: ridgefill_gemm_nt_q, ridgefill_gemm_nt_q_bias and the
+ * activation quantiser ridgefill_quant_act_i8g.
+ *
+ * The reference forwards this GEMM to radiance libr4d's int8 gemm_nt_q (kernels/forward.cpp:53-57;
+ * issue site arch/ridgefill_layer.h:73-80), whose source is not available; its schema
+ * (kernels/rows.cpp:72-76, 161-167) and its test's arithmetic comment (tests/kernel_test.cpp:2114-2117:
+ * int32 within a 128-K block, f32 fold, one bf16 rounding) are the contract. This library fixes the
+ * fold exactly:
+ *     acc = 0;  for each K block j in order:  acc = fma(float(dot_j) * a_scale[m, j], b_scale[j, n], acc)
+ *     y = bf16(acc);   with a bias: y = bf16(float(y) + bias[n])
+ * so the result is reproducible bit for bit by the CPU oracle.
+ *
+ * Kernel: persistent, one CTA per SM, 128 x 256 output tiles, 128-byte K steps.
+ *   warp 0      TMA producer: A [128 x 128] and B [256 x 128] int8 tiles, 128-byte swizzle, 4-stage ring
+ *   warp 1      tensor-memory allocator and MMA issuer: tcgen05.mma kind::i8 M128 N256 K32, four a step,
+ *               int32 accumulators in tensor memory, two 256-column buffers so a block's MMAs overlap
+ *               the previous block's fold
+ *   warps 2-9   epilogue: each warp owns a 32-lane quarter of the tile rows and one 128-column half;
+ *               it folds each finished K block into f32 registers and stores bf16 at the tile's end
+ * A K block is `group` columns: 128 for the projector folder's i8*bf16[1x128] encoding, K itself
+ * for per-row / per-column scaling (one fold a tile, the int32 accumulation running over all of K).
+ */
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 128;
+constexpr int kStages = 4;
+constexpr int kABytes = BM * BK, kBBytes = BN * BK, kStageBytes = kABytes + kBBytes;
+constexpr uint32_t kTmemCols = 512;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 32 * (2 + kEpiWarps);
+constexpr int kSmemBytes = kStages * kStageBytes + 1024 /* alignment slack */ + 256 /* barriers */;
+
+/* Instruction descriptor: D s32 (bits 4-5 = 2), A and B signed int8 (bits 7-9, 10-12 = 1), both
+ * K-major, N >> 3 at bit 17, M >> 4 at bit 24. */
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+struct GemmPlan {
+    RidgeFillGemmQ g;
+    int n_tiles, tiles, folds, steps_per_fold;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, const GemmPlan p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* tile_a = smem;
+    uint8_t* tile_b = smem + kStages * kABytes;
+    uint64_t* full = (uint64_t*)(smem + kStages * kStageBytes);
+    uint64_t* empty = full + kStages;
+    uint64_t* acc_full = empty + kStages;
+    uint64_t* acc_empty = acc_full + 2;
+    uint32_t* tmem_slot = (uint32_t*)(acc_empty + 2);
+    volatile int* abort = (volatile int*)(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            rf::mbar_init(&full[s], 1);
+            rf::mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            rf::mbar_init(&acc_full[b], 1);
+            rf::mbar_init(&acc_empty[b], kEpiWarps);
+        }
+        *abort = 0;
+        rf::mbar_init_fence();
+        rf::tma_prefetch_map(&map_a);
+        rf::tma_prefetch_map(&map_b);
+    }
+    if (warp == 1) rf::tmem_alloc<kTmemCols>(tmem_slot);
+    rf::tc_fence_before();
+    __syncthreads();
+    rf::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const RidgeFillGemmQ& g = p.g;
+
+    if (warp == 0) {
+        /* ---------------------------------------------------------- producer */
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0;
+            int64_t issued = 0;
+            const int steps = p.folds * p.steps_per_fold;
+            for (int tile = blockIdx.x; tile < p.tiles && !*abort; tile += gridDim.x) {
+                const int m0 = (tile / p.n_tiles) * BM, n0 = (tile % p.n_tiles) * BN;
+                for (int ks = 0; ks < steps; ++ks) {
+                    if (!rf::mbar_wait(&empty[stage], phase ^ 1, abort, rf::kErrGemmWaitProducer)) break;
+                    rf::mbar_arrive_expect_tx(&full[stage], kStageBytes);
+                    rf::tma_load_2d(tile_a + stage * kABytes, &map_a, &full[stage], ks * BK, m0);
+                    rf::tma_load_2d(tile_b + stage * kBBytes, &map_b, &full[stage], ks * BK, n0);
+                    ++issued;
+                    if (++stage == kStages) { stage = 0; phase ^= 1; }
+                }
+            }
+            /* Drain: every load this CTA issued has landed before its shared memory is released. */
+            const int64_t first = issued > kStages ? issued - kStages : 0;
+            for (int64_t i = first; i < issued; ++i) {
+                const uint64_t t0 = rf::global_ns();
+                while (!rf::mbar_try_wait(&full[i % kStages], (uint32_t)((i / kStages) & 1))) {
+                    if (rf::global_ns() - t0 > rf::kWaitTimeoutNs) {
+                        atomicCAS(&rf::g_device_error, 0, (int)rf::kErrGemmDrain);
+                        break;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        /* ---------------------------------------------------------- MMA issuer */
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0, fold = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
+                for (int f = 0; f < p.folds && ok; ++f, ++fold) {
+                    const uint32_t buf = fold & 1, use = (fold >> 1) & 1;
+                    if (!(ok = rf::mbar_wait(&acc_empty[buf], use ^ 1, abort, rf::kErrGemmWaitMma))) break;
+                    rf::tc_fence_after();
+                    const uint32_t d = tmem_base + buf * BN;
+                    for (int ks = 0; ks < p.steps_per_fold; ++ks) {
+                        if (!(ok = rf::mbar_wait(&full[stage], phase, abort, rf::kErrGemmWaitMma))) break;
+                        rf::tc_fence_after();
+                        const uint32_t a_addr = rf::smem_addr(tile_a + stage * kABytes);
+                        const uint32_t b_addr = rf::smem_addr(tile_b + stage * kBBytes);
+#pragma unroll
+                        for (int kk = 0; kk < BK / 32; ++kk)
+                            rf::mma_i8(d, rf::sw128_kmajor_desc(a_addr + kk * 32), rf::sw128_kmajor_desc(b_addr + kk * 32),
+                                       kIdesc, (ks | kk) != 0);
+                        rf::mma_commit(&empty[stage]);   /* the stage is free once these MMAs have read it */
+                        if (++stage == kStages) { stage = 0; phase ^= 1; }
+                    }
+                    if (ok) rf::mma_commit(&acc_full[buf]);   /* the block's sums are final */
+                }
+            }
+        }
+    } else {
+        /* ---------------------------------------------------------- epilogue */
+        const int quarter = warp & 3, half = (warp - 2) >> 2;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + half * 128;
+        uint32_t fold = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
+            const int64_t m = (int64_t)(tile / p.n_tiles) * BM + row;
+            const int64_t n0 = (int64_t)(tile % p.n_tiles) * BN + half * 128;
+            const bool row_live = m < g.M;
+            float acc[128];
+#pragma unroll
+            for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+            for (int f = 0; f < p.folds; ++f, ++fold) {
+                const uint32_t buf = fold & 1, use = (fold >> 1) & 1;
+                if (!(ok = rf::mbar_wait(&acc_full[buf], use, abort, rf::kErrGemmWaitEpilogue))) break;
+                rf::tc_fence_after();
+                const float sa = row_live ? g.a_scale[m * g.ldas + f] : 0.0f;
+                const float* sb = g.b_scale + (int64_t)f * g.N + n0;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t r[32];
+                    rf::tmem_ld32(lane_addr + buf * BN + c * 32, r);
+                    rf::tmem_ld_wait();
+                    if (g.acc && row_live) {
+                        const int64_t blocks = p.folds;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const int64_t n = n0 + c * 32 + i;
+                            if (n < g.N) g.acc[(m * g.N + n) * blocks + f] = (int32_t)r[i];
+                        }
+                    }
+#pragma unroll
+                    for (int i4 = 0; i4 < 8; ++i4) {
+                        const int64_t n = n0 + c * 32 + i4 * 4;
+                        const float4 s4 = n < g.N ? __ldg((const float4*)(sb + c * 32 + i4 * 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        const float sv[4] = { s4.x, s4.y, s4.z, s4.w };
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const int i = c * 32 + i4 * 4 + e;
+                            const float t = __fmul_rn(__int2float_rn((int)r[i4 * 4 + e]), sa);
+                            acc[i] = __fmaf_rn(t, sv[e], acc[i]);
+                        }
+                    }
+                }
+                rf::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) rf::mbar_arrive(&acc_empty[buf]);
+            }
+            if (!ok) break;
+            if (row_live) {
+                uint16_t* yrow = g.y + m * g.ldy;
+#pragma unroll
+                for (int v = 0; v < 16; ++v) {
+                    const int64_t n = n0 + v * 8;
+                    if (n >= g.N) break;
+                    uint32_t o[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        o[e] = (uint32_t)rf::f32_to_bf16_bits(acc[v * 8 + 2 * e]) |
+                               ((uint32_t)rf::f32_to_bf16_bits(acc[v * 8 + 2 * e + 1]) << 16);
+                    if (g.bias) {
+                        const uint4 bv = __ldg((const uint4*)(g.bias + n));
+                        const uint32_t bw[4] = { bv.x, bv.y, bv.z, bv.w };
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float lo = __fadd_rn(__uint_as_float(o[e] << 16), __uint_as_float(bw[e] << 16));
+                            const float hi = __fadd_rn(__uint_as_float(o[e] & 0xffff0000u), __uint_as_float(bw[e] & 0xffff0000u));
+                            o[e] = (uint32_t)rf::f32_to_bf16_bits(lo) | ((uint32_t)rf::f32_to_bf16_bits(hi) << 16);
+                        }
+                    }
+                    *(uint4*)(yrow + n) = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+            }
+        }
+    }
+
+    rf::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        rf::tc_fence_after();
+        rf::tmem_free<kTmemCols>(tmem_base);
+    }
+}
+
+/* ------------------------------------------------------------------ quantiser */
+
+/* One warp per (row, group); lane l reads 4-element chunks l, l + 32, ... of the group (coalesced
+ * 256-byte warp reads). Pass 1 finds the group's absmax, pass 2 writes the codes. */
+__global__ void __launch_bounds__(256) quant_kernel(RidgeFillQuant g) {
+    const int lane = threadIdx.x & 31;
+    const int64_t groups = g.K / g.group, work = g.M * groups;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int chunks = (int)(g.group / 4);
+    for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < work; w += warps) {
+        const int64_t m = w / groups, j = w - m * groups;
+        const uint16_t* x = g.x + m * g.ldx + j * g.group;
+        float amax = 0.0f;
+        for (int c = lane; c < chunks; c += 32) {
+            const uint2 v = *(const uint2*)(x + 4 * c);
+            amax = fmaxf(amax, fabsf(__uint_as_float(v.x << 16)));
+            amax = fmaxf(amax, fabsf(__uint_as_float(v.x & 0xffff0000u)));
+            amax = fmaxf(amax, fabsf(__uint_as_float(v.y << 16)));
+            amax = fmaxf(amax, fabsf(__uint_as_float(v.y & 0xffff0000u)));
+        }
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float s = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 127.0f);
+        if (lane == 0) g.s[m * g.lds + j] = s;
+        int8_t* q = g.q + m * g.ldq + j * g.group;
+        for (int c = lane; c < chunks; c += 32) {
+            const uint2 v = *(const uint2*)(x + 4 * c);
+            const float xs[4] = { __uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u),
+                                  __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xffff0000u) };
+            uint32_t packed = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                int r = __float2int_rn(__fdiv_rn(xs[e], s));
+                r = r > 127 ? 127 : (r < -127 ? -127 : r);
+                packed |= (uint32_t)(uint8_t)(int8_t)r << (8 * e);
+            }
+            *(uint32_t*)(q + 4 * c) = packed;
+        }
+    }
+}
+
+/* ------------------------------------------------------------------ host side */
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)f;
+    }
+    return fn;
+}
+
+/* A [rows, cols] int8 matrix with row pitch `pitch` bytes, read in [box_rows, 128] tiles with 128-byte
+ * swizzle; rows past the end read as zero. */
+bool int8_tile_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t pitch, uint32_t box_rows) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = { (cuuint64_t)cols, (cuuint64_t)rows };
+    const cuuint64_t strides[1] = { (cuuint64_t)pitch };
+    const cuuint32_t box[2] = { (cuuint32_t)BK, box_rows };
+    const cuuint32_t estr[2] = { 1, 1 };
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int launch_gemm(const RidgeFillGemmQ& g, cudaStream_t stream) {
+    if (g.M == 0) return RAD_OK;
+    if (g.M > 0x7fffffffLL || g.N > 0x7fffffffLL || g.K > 0x7fffffffLL) return RAD_E_SHAPE;
+    CUtensorMap map_a, map_b;
+    if (!int8_tile_map(&map_a, g.a, g.M, g.K, g.lda, BM) || !int8_tile_map(&map_b, g.b, g.N, g.K, g.ldb, BN))
+        return RAD_E_DEVICE;
+    GemmPlan p;
+    p.g = g;
+    p.n_tiles = (int)((g.N + BN - 1) / BN);
+    const int64_t tiles = ((g.M + BM - 1) / BM) * p.n_tiles;
+    if (tiles > 0x7fffffffLL) return RAD_E_SHAPE;
+    p.tiles = (int)tiles;
+    p.folds = (int)(g.K / g.group);
+    p.steps_per_fold = (int)(g.group / BK);
+    if (cudaFuncSetAttribute(gemm_q_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+        return RAD_E_DEVICE;
+    const int grid = p.tiles < rf::sm_count() ? p.tiles : rf::sm_count();
+    gemm_q_kernel<<<grid, kThreads, kSmemBytes, stream>>>(map_a, map_b, p);
+    return rf::launch_status();
+}
+
+}  // namespace
+
+extern "C" int ridgefill_gemm_nt_q_device(const RadArgs* a, RadStream s) {
+    RidgeFillGemmQ g;
+    const int rc = ridgefill_gemm_q_parse(a, 0, &g);
+    return rc != RAD_OK ? rc : launch_gemm(g, rf::as_stream(s));
+}
+
+extern "C" int ridgefill_gemm_nt_q_bias_device(const RadArgs* a, RadStream s) {
+    RidgeFillGemmQ g;
+    const int rc = ridgefill_gemm_q_parse(a, 1, &g);
+    return rc != RAD_OK ? rc : launch_gemm(g, rf::as_stream(s));
+}
+
+extern "C" int ridgefill_quant_act_device(const RadArgs* a, RadStream s) {
+    RidgeFillQuant g;
+    const int rc = ridgefill_quant_parse(a, &g);
+    if (rc != RAD_OK) return rc;
+    if (g.M == 0) return RAD_OK;
+    const int64_t warps = g.M * (g.K / g.group);
+    const int64_t blocks = (warps + 7) / 8, cap = (int64_t)rf::sm_count() * 8;
+    quant_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, rf::as_stream(s)>>>(g);
+    return rf::launch_status();
+}
+
+/* The first device-side wait error any kernel of this library recorded (0: none), optionally
+ * clearing it. Synchronises the current device: a diagnostic, never called on the launch path. */
+extern "C" int ridgefill_device_error(int reset) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, rf::g_device_error, sizeof v) != cudaSuccess) return -1;
+    if (reset) {
+        const int zero = 0;
+        if (cudaMemcpyToSymbol(rf::g_device_error, &zero, sizeof zero) != cudaSuccess) return -1;
+    }
+    return v;
+}
