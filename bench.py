@@ -1,0 +1,266 @@
+"""bench.py -- prefill tokens/s of one RidgeFill approximate pass at 32K on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mine|reference]
+
+A step is one pass of the RidgeFill hot path over a 32,768-row prefill chunk (ridgefill_step.Step):
+mask -> activation codes -> int8 projector (d 2,048, per-column scales, fused bias) -> select ->
+state undo -> Gated DeltaNet chunk fill (16 q/k heads, 32 v heads, 128 dims, state [32,128,128] f32)
+-> rho -> state apply -> hazard, every op a launch of the library's sm_100a device rows through the C
+ABI. Synthetic inputs with BASELINE's shapes and distributions, seeded; inputs (> 700 MB) exceed the
+126 MB L2, so no flush is needed between steps.
+
+value   device time of K passes with inputs resident in HBM (CUDA events, max over ranks)
+e2e     the same passes with each step's inputs copied host->device from pinned memory and the results
+        (projected block input x, DeltaNet state, mask) copied back, inside the timed region
+N > 1   one process per GPU (torchrun), each rank an independent 32K prompt: prompts are independent
+        units, no data-path collective ("scaling": "weak"); value = all ranks' tokens / max rank time.
+--impl reference   the CPU arm: the reference's own host rows (compiled from kernels/host_ref.cpp into
+        oracle/_ref) plus the CPU restatement of the projector and the fill it lacks, on a 2,048-row
+        sample of the workload, all host threads; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "radiance-ridgefill_b200"))
+sys.path.insert(0, str(ROOT / "oracle"))
+
+METRIC = "prefill tokens/s at 32K (RidgeFill step)"
+T_FULL = 32768
+CPU_SAMPLE_ROWS = 2048
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while the timed region runs."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx, self.rows, self.proc = gpu_index, [], None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm = [float(r[1]) for r in self.rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) >= 9 for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_arm(steps: int, warmup: int) -> dict:
+    import cpu_path
+    s = cpu_path.CpuStep(CPU_SAMPLE_ROWS)
+    sec = s.time_steps(steps, warmup)
+    return {"value": CPU_SAMPLE_ROWS / sec, "unit": "tokens/s", "cores": s.threads, "kind": s.kind,
+            "sample": f"the same pass on a {CPU_SAMPLE_ROWS}-row chunk (T={CPU_SAMPLE_ROWS} of {T_FULL}; "
+                      f"the mask's rank count is O(w^2), so the full chunk is slower per row on the CPU), "
+                      f"{steps} timed passes", "sec_per_pass": sec}
+
+
+def run_reference(args):
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    base = cpu_arm(args.steps, args.warmup)
+    line = {"metric": METRIC, "value": base["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": base["sec_per_pass"] * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "i8/bf16/f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"RidgeFill approximate pass, {CPU_SAMPLE_ROWS}-row sample of the 32K chunk, host CPU",
+                       "rows": CPU_SAMPLE_ROWS, "d": 2048, "delta_heads": "16 qk / 32 v x 128"},
+            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_mine(args):
+    import torch
+    import torch.distributed as dist
+    import ridgefill_step as RS
+
+    world, rank, local = dist_setup()
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    step = RS.Step(RS.StepShape(T=T_FULL), device=str(dev), seed=1234 + rank)
+    stream = torch.cuda.Stream(device=dev)
+    alg = step.algorithmic()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # per-op device times (untimed pass), to name the dominant kernel
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            step.run(stream.cuda_stream)
+        ops = {name: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for name in {c[0] for c in step.calls}}
+        per_op = {n: 0.0 for n in ops}
+        for _ in range(3):
+            step.run(stream.cuda_stream, events=ops)
+            stream.synchronize()
+            for n, (a, b) in ops.items():
+                per_op[n] += a.elapsed_time(b) / 3
+    dominant = max(per_op, key=per_op.get)
+
+    # ---------------------------------------------------------- device-resident timing
+    dom_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step.run(stream.cuda_stream)
+        stream.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        clocks.start()
+        start.record()
+        for i in range(args.steps):
+            step.run(stream.cuda_stream, events={dominant: dom_ev[i]})
+        end.record()
+        stream.synchronize()
+    clock_info = clocks.stop()
+    torch.cuda.synchronize()
+    barrier()
+    ms = start.elapsed_time(end) / args.steps
+    dom_ms = statistics.mean(a.elapsed_time(b) for a, b in dom_ev)
+
+    # ---------------------------------------------------------- end to end through the C ABI, host buffers
+    inputs = [step.h_s, step.k, step.v, step.g, step.beta, step.ab, step.token_ids, step.positions]
+    outputs = [step.x, step.state, step.mask]
+    host_in = [t.cpu().pin_memory() for t in inputs]
+    host_out = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in outputs]
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            for d_, h in zip(inputs, host_in):
+                d_.copy_(h, non_blocking=True)
+            step.run(stream.cuda_stream)
+            for h, d_ in zip(host_out, outputs):
+                h.copy_(d_, non_blocking=True)
+        stream.synchronize()
+        barrier()
+        e_start.record()
+        for _ in range(args.steps):
+            for d_, h in zip(inputs, host_in):
+                d_.copy_(h, non_blocking=True)
+            step.run(stream.cuda_stream)
+            for h, d_ in zip(host_out, outputs):
+                h.copy_(d_, non_blocking=True)
+        e_end.record()
+        stream.synchronize()
+    barrier()
+    e2e_ms = e_start.elapsed_time(e_end) / args.steps
+
+    # max over ranks
+    vals = torch.tensor([ms, e2e_ms, dom_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, dom_ms = vals.tolist()
+
+    if rank == 0:
+        pk = peaks()
+        if dominant == "ridgefill_gemm_nt_q_bias":
+            int8_peak = 2.0 * pk["bf16_tflops"]
+            roof = {"bound": "tensor", "achieved": alg["gemm_ops"] / (dom_ms * 1e-3) / 1e12, "peak": int8_peak,
+                    "unit": "TOP/s", "traffic": None,
+                    "note": f"int8 dense peak = 2 x the {pk['source']} bf16 figure ({pk['bf16_tflops']} TF/s)"}
+        else:
+            by = {"ridgefill_gdn_fill": alg["gdn_bytes"], "ridgefill_quant_act_i8g": alg["quant_bytes"],
+                  "ridgefill_select": alg["select_bytes"]}.get(dominant, 0)
+            roof = {"bound": "hbm", "achieved": by / (dom_ms * 1e-3) / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                    "traffic": None, "note": f"peak {pk['source']}"}
+        roof["frac"] = roof["achieved"] / roof["peak"]
+        roof["kernel"] = dominant
+        roof["kernel_ms"] = dom_ms
+        line = {"metric": METRIC, "value": world * T_FULL / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "i8/bf16/f32", "data": "synthetic",
+                "config": {"workload": "RidgeFill approximate pass over a 32,768-row prefill chunk: projector d 2,048 "
+                                       "(int8, per-column scales), Gated DeltaNet fill 16 qk / 32 v heads x 128, "
+                                       "class mask share 0.30",
+                           "rows": T_FULL, "d": 2048, "l2": "inputs larger than L2 (no flush)",
+                           "parallelism": f"independent prompts x{world}"},
+                "gpu_launches": Step_launches(step) * args.steps,
+                "per_op_ms": {k: round(v, 4) for k, v in sorted(per_op.items(), key=lambda kv: -kv[1])},
+                "roofline": roof, "clocks": clock_info,
+                "e2e": {"value": world * T_FULL / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                        "d2h_bytes_per_step": d2h}}
+        if world == 1 and not args.no_cpu:
+            line["cpu_baseline"] = {k: v for k, v in cpu_arm(2, 1).items() if k != "sec_per_pass"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def Step_launches(step) -> int:
+    return step.LAUNCHES_PER_PASS
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_mine(args)
+
+
+if __name__ == "__main__":
+    main()

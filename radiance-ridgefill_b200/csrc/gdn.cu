@@ -51,17 +51,27 @@ __device__ __forceinline__ uint8_t* slot_ptr(const GdnPlan& p, int64_t slot, int
     return p.scratch + (slot * p.g.n_head_v + h) * (int64_t)kSlotBytes;
 }
 
+/* Sequence i's rows [*r0, *r1): cu_seqlens read on the device and clamped into [0, T] (a value the host
+ * cannot check never sends a load outside the operands). */
+__device__ __forceinline__ void seq_rows(const RidgeFillGdn& g, int64_t i, int64_t* r0, int64_t* r1) {
+    const int64_t a = min(max((int64_t)g.cu[i], (int64_t)0), g.T);
+    const int64_t b = min(max((int64_t)g.cu[i + 1], a), g.T);
+    *r0 = a;
+    *r1 = b;
+}
+
 /* The sequence holding chunk `slot` (chunks of each sequence numbered consecutively, sequence by
  * sequence), its chunk's first row and length; false past the last chunk. */
 __device__ bool locate_chunk(const RidgeFillGdn& g, int64_t slot, int64_t* row0, int* len) {
     int64_t base = 0;
     for (int64_t i = 0; i < g.n_seq; ++i) {
-        const int64_t rows = (int64_t)g.cu[i + 1] - g.cu[i];
-        const int64_t chunks = rows > 0 ? (rows + C - 1) / C : 0;
+        int64_t r0, r1;
+        seq_rows(g, i, &r0, &r1);
+        const int64_t chunks = (r1 - r0 + C - 1) / C;
         if (slot < base + chunks) {
             const int64_t c = slot - base;
-            *row0 = g.cu[i] + c * C;
-            *len = (int)min((int64_t)C, rows - c * C);
+            *row0 = r0 + c * C;
+            *len = (int)min((int64_t)C, r1 - r0 - c * C);
             return true;
         }
         base += chunks;
@@ -260,13 +270,15 @@ __global__ void __launch_bounds__(128, 1) gdn_chain_kernel(const GdnPlan p) {
     const int v0 = vsl * VS;
 
     /* This sequence's rows and first chunk slot. */
-    int64_t base = 0;
+    int64_t base = 0, r0 = 0, r1 = 0;
     for (int64_t i = 0; i < seq; ++i) {
-        const int64_t rows = (int64_t)g.cu[i + 1] - g.cu[i];
-        base += rows > 0 ? (rows + C - 1) / C : 0;
+        seq_rows(g, i, &r0, &r1);
+        base += (r1 - r0 + C - 1) / C;
     }
-    const int64_t r0 = g.cu[seq], r1 = g.cu[seq + 1];
-    const int64_t chunks = r1 > r0 ? (r1 - r0 + C - 1) / C : 0;
+    seq_rows(g, seq, &r0, &r1);
+    /* Overlapping sequences (cu not increasing) could number more chunks than phase 1 had slots for:
+     * those chunks are not read. */
+    const int64_t chunks = max((int64_t)0, min((r1 - r0 + C - 1) / C, (int64_t)p.max_slots - base));
 
     /* The state slice: S[v0 + 16 vh + m][64 kh + n] as C tiles over dk (8 tiles of 8 columns). */
     float S[8][4];

@@ -1,0 +1,104 @@
+"""ridgefill_gdn_fill on B200 against the sequential gated delta rule in float64 (the oracle): the final
+state within 1e-3 relative L2 (the tolerance the task states for the fp32 DeltaNet state), untouched
+slots and skipped sequences bit for bit, and at the full 32,768-row configuration the size-independent
+property that splitting a sequence at a chunk boundary (two calls, the state carried) is the same
+arithmetic as one call, bit for bit."""
+import numpy as np
+import pytest
+
+import harness as H
+from harness import abi
+
+pytestmark = pytest.mark.gpu
+STATE_TOL = 1e-3
+
+
+def run_fill(product_lib, torch, k, v, g, beta, state, idx, cu, hk, hv, q=None, o=False):
+    T = k.shape[0]
+    K = torch.from_numpy(k.view(np.int16)).cuda()
+    V = torch.from_numpy(v.view(np.int16)).cuda()
+    G, BT = torch.from_numpy(g).cuda(), torch.from_numpy(beta).cuda()
+    S = torch.from_numpy(state.copy()).cuda()
+    I = torch.tensor(np.asarray(idx, np.int32)).cuda()
+    CU = torch.tensor(np.asarray(cu, np.int32)).cuda()
+    Q = torch.from_numpy(q.view(np.int16)).cuda() if q is not None else None
+    O = torch.zeros((T, hv, 128), dtype=torch.int16, device="cuda") if o else None
+    rc = H.launch(product_lib, "ridgefill_gdn_fill",
+                  [H.dev(Q, abi.BF16), H.dev(K, abi.BF16), H.dev(V, abi.BF16), H.dev(G), H.dev(BT), H.dev(S), H.dev(I),
+                   H.dev(CU), H.dev(O, abi.BF16)], H.gdn_params(T, hk, hv))
+    return rc, S.cpu().numpy(), (O.cpu().numpy().view(np.uint16) if o else None)
+
+
+@pytest.mark.parametrize("T,hk,hv,decay", [(64, 1, 1, "fast"), (130, 2, 4, "fast"), (1000, 2, 4, "slow"),
+                                           (777, 1, 2, "very slow"), (2048, 16, 32, "fast")])
+def test_fill_state_matches_sequential_rule(cuda, product_lib, T, hk, hv, decay):
+    torch = cuda
+    q, k, v, g, beta, state = H.gdn_inputs(T + hv, T, hk, hv, decay)
+    rc, got, _ = run_fill(product_lib, torch, k, v, g, beta, state, [1], [0, T], hk, hv)
+    assert rc == abi.OK
+    want, _ = H.oracle_gdn(k, v, g, beta, state, [1], [0, T])
+    err = H.rel_l2(got[1], want[1])
+    assert err <= STATE_TOL, err
+    assert np.array_equal(got[0], state[0]) and np.array_equal(got[2], state[2])   # other slots untouched
+
+
+def test_fill_varlen_sequences_and_skipped_slots(cuda, product_lib):
+    """Three sequences of 1, 100 and 300 rows (chunks anchored at each start), the second with no state
+    (slot -1: skipped, its rows read by nobody), slots in reverse order."""
+    torch = cuda
+    q, k, v, g, beta, state = H.gdn_inputs(5, 401, 2, 4, "slow", slots=4)
+    cu, idx = [0, 1, 101, 401], [3, -1, 0]
+    rc, got, _ = run_fill(product_lib, torch, k, v, g, beta, state, idx, cu, 2, 4)
+    assert rc == abi.OK
+    want, _ = H.oracle_gdn(k, v, g, beta, state, idx, cu)
+    for slot in (3, 0):
+        assert H.rel_l2(got[slot], want[slot]) <= STATE_TOL
+    assert np.array_equal(got[1], state[1]) and np.array_equal(got[2], state[2])
+
+
+def test_fill_empty_sequence_keeps_state(cuda, product_lib):
+    torch = cuda
+    q, k, v, g, beta, state = H.gdn_inputs(6, 64, 1, 2, "fast")
+    rc, got, _ = run_fill(product_lib, torch, k, v, g, beta, state, [2, 1], [0, 0, 64], 1, 2)
+    assert rc == abi.OK and np.array_equal(got[2], state[2])
+    want, _ = H.oracle_gdn(k, v, g, beta, state, [2, 1], [0, 0, 64])
+    assert H.rel_l2(got[1], want[1]) <= STATE_TOL
+
+
+def test_fill_full_size_split_is_one_call(cuda, product_lib):
+    """Config 2 at full size: T = 32,768, 16 q/k heads, 32 v heads. Two calls over [0, T/2) and [T/2, T)
+    with the state carried equal one call over [0, T) bit for bit (chunks are anchored at the call's
+    sequence start and T/2 is a chunk boundary); two heads checked against the float64 rule."""
+    torch = cuda
+    T, hk, hv = 32768, 16, 32
+    q, k, v, g, beta, state = H.gdn_inputs(32, T, hk, hv, "fast", slots=1)
+    rc, one, _ = run_fill(product_lib, torch, k, v, g, beta, state, [0], [0, T], hk, hv)
+    assert rc == abi.OK
+    h = T // 2
+    rc1, mid, _ = run_fill(product_lib, torch, k[:h], v[:h], g[:h], beta[:h], state, [0], [0, h], hk, hv)
+    rc2, two, _ = run_fill(product_lib, torch, k[h:], v[h:], g[h:], beta[h:], mid, [0], [0, T - h], hk, hv)
+    assert rc1 == rc2 == abi.OK
+    assert np.array_equal(one.view(np.uint32), two.view(np.uint32))
+    want, _ = H.oracle_gdn(k, v, g, beta, state, [0], [0, T], heads=(5, 7))
+    assert H.rel_l2(one[0, 5:7], want[0, 5:7]) <= STATE_TOL
+
+
+def test_fill_refusals(cuda, product_lib):
+    torch = cuda
+    q, k, v, g, beta, state = H.gdn_inputs(7, 64, 1, 2, "fast")
+    K = torch.from_numpy(k.view(np.int16)).cuda()
+    V = torch.from_numpy(v.view(np.int16)).cuda()
+    G, BT, S = torch.from_numpy(g).cuda(), torch.from_numpy(beta).cuda(), torch.from_numpy(state).cuda()
+    I, CU = torch.tensor([1], dtype=torch.int32).cuda(), torch.tensor([0, 64], dtype=torch.int32).cuda()
+    ops = [abi.absent(), H.dev(K, abi.BF16), H.dev(V, abi.BF16), H.dev(G), H.dev(BT), H.dev(S), H.dev(I), H.dev(CU), abi.absent()]
+    assert H.launch(product_lib, "ridgefill_gdn_fill", ops, H.gdn_params(64, 1, 2)) == abi.OK
+    assert H.launch(product_lib, "ridgefill_gdn_fill", ops, H.gdn_params(64, 1, 2), scratch_bytes=0) == abi.E_INVAL
+    p = H.gdn_params(64, 1, 2)
+    p[5] = H.pint("chunk", 32)
+    assert H.launch(product_lib, "ridgefill_gdn_fill", ops, p) == abi.E_UNSUPPORTED
+    bad = list(ops)
+    bad[3] = H.dev(G.to(torch.bfloat16))
+    assert H.launch(product_lib, "ridgefill_gdn_fill", bad, H.gdn_params(64, 1, 2)) == abi.E_DTYPE
+    bad = list(ops)
+    bad[0] = H.dev(K, abi.BF16)   # q without o
+    assert H.launch(product_lib, "ridgefill_gdn_fill", bad, H.gdn_params(64, 1, 2)) == abi.E_INVAL

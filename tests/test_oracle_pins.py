@@ -1,0 +1,236 @@
+"""Pins of the CPU oracle (oracle/ridgefill_oracle.cpp) before anything is checked against it:
+ - the reference's own test harness (tests/kernel_test.cpp, compiled here from its source into
+   oracle/_ref) passes against the oracle library, golden fixtures included;
+ - the oracle equals the reference's host rows (compiled from kernels/host_ref.cpp) bit for bit on
+   random operands of every op;
+ - the golden fixtures made from the reference's own Python (tests/golden/make_golden.py) hold.
+"""
+import json
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+import cases as K
+import harness as H
+from harness import abi, Buf
+
+
+def test_reference_harness_passes_on_oracle(oracle_lib):
+    if not H.REF_TEST.exists():
+        pytest.skip("oracle/_ref/kernel_test is not built (make -C oracle ref needs the reference sources)")
+    env = dict(os.environ, RIDGEFILL_RHO_FIXTURE=str(H.GOLDEN / "rho_numpy.txt"),
+               RIDGEFILL_ROWSEL_FIXTURE=str(H.GOLDEN / "rowsel_keys.json"))
+    res = subprocess.run([str(H.REF_TEST), str(H.ORACLE_SO), "host"], capture_output=True, text=True, env=env, timeout=600)
+    assert res.returncode == 0, res.stderr[-3000:]
+    assert "FAIL" not in res.stderr
+    checks = [l for l in res.stderr.splitlines() if "check(s)" in l]
+    assert checks and int(checks[-1].split()[0]) >= 900
+    assert "== fnlev.rules" in res.stderr and "rho vs NumPy" in res.stderr
+
+
+def _both():
+    ref = H.reference()
+    if ref is None:
+        pytest.skip("oracle/_ref/ridgefill_ref.so is not built")
+    return H.oracle(), ref
+
+
+def test_oracle_equals_reference_mask():
+    o, ref = _both()
+    r = H.Rng(41)
+    table = [[-np.inf, -np.inf, 1.0, 2.0, 2.5, 3.0][r.below(6)] for _ in range(1000)]
+    runs = 0
+    for n in (1, 7, 300, 2048, 5000):
+        for layout in range(4):
+            c = K.random_window(r, n, layout)
+            c.table, c.seed, c.first_pos = table, 12345, 4096
+            for mode in ("none", "class", "random", "all", "step"):
+                for share in (0.25, 0.5, 1.0):
+                    c.mode, c.share, c.components, c.n_zeros = mode, share, 3 if runs % 2 else 1, 0 if runs % 3 else 33
+                    a = K.run_mask(o, o.find_row("ridgefill_mask", 0), c)
+                    b = K.run_mask(ref, ref.find_row("ridgefill_mask", 0), c)
+                    assert a[0] == b[0]
+                    for x, y in zip(a[1:], b[1:]):
+                        assert np.array_equal(x, y)
+                    runs += 1
+    assert runs == 300
+
+
+def test_oracle_equals_reference_rho_and_correct():
+    o, ref = _both()
+    r = H.Rng(51)
+    for heads in (48, 12):
+        for exact in (0.0, 0.3):
+            base = K.random_rho(r, 700, heads, exact, True)
+            base.pitch = 2 * heads
+            for bounds in ([], [5, 600, 600, 700], [-3], [900, 0]):
+                a, b = base.copy(), base.copy()
+                a.bounds = b.bounds = bounds
+                for _ in range(2):
+                    assert K.run_rho(o, o.find_row("ridgefill_rho_update", 0), a) == abi.OK
+                    assert K.run_rho(ref, ref.find_row("ridgefill_rho_update", 0), b) == abi.OK
+                assert np.array_equal(np.asarray(a.nd, np.float32).view(np.uint32), np.asarray(b.nd, np.float32).view(np.uint32))
+    for heads in (24, 15):
+        k = K.random_correct(r, heads, sd=32, pad=4)
+        for mode, alpha, nd, bounds in (("undo", 1.0, False, ()), ("apply", 0.7, True, ()), ("apply", 1.0, False, (2, 6, 6, 9)),
+                                        ("undo", 1.0, False, (5, 5)), ("apply", 0.0, True, ())):
+            a, b = k.copy(), k.copy()
+            assert K.run_correct(o, o.find_row("ridgefill_state_correct", 0), a, mode, alpha, nd, bounds) == abi.OK
+            assert K.run_correct(ref, ref.find_row("ridgefill_state_correct", 0), b, mode, alpha, nd, bounds) == abi.OK
+            assert np.array_equal(a.state.bytes, b.state.bytes) and np.array_equal(a.applied.bytes, b.applied.bytes)
+            k = a
+
+
+def test_oracle_equals_reference_select_drop_read_hazard():
+    o, ref = _both()
+    r = H.Rng(111)
+    for n in (1, 300, 2000):
+        mask = [2 if r.uniform() < 0.02 else (0 if r.uniform() < 0.4 else 1) for _ in range(n)]
+        for variant in range(3):
+            xw, qw = 64 * (1 + variant), 33 + 16 * variant
+            k = {"mask": K.mask_buf(mask), "xs": Buf(abi.BF16, [n, xw], [xw + 8, 1]), "qs": Buf(abi.I8, [n, qw]),
+                 "ss": Buf(abi.F32, [n + 1, 3]), "x": Buf(abi.BF16, [n + 1, xw]), "q": Buf(abi.I8, [n, qw], [qw + 5, 1]),
+                 "s": Buf(abi.F32, [n, 3], [4, 1])}
+            for i, name in enumerate(("xs", "qs", "ss")):
+                K.fill_pattern(k[name], 4 + i + variant)
+            for name in ("x", "q", "s"):
+                K.fill_sentinel(k[name])
+            if variant == 2:
+                k["qs"] = k["ss"] = k["q"] = k["s"] = None
+            a = {n_: (v.copy() if v is not None else None) for n_, v in k.items()}
+            b = {n_: (v.copy() if v is not None else None) for n_, v in k.items()}
+            assert K.run_select(o, o.find_row("ridgefill_select", 0), a) == abi.OK
+            assert K.run_select(ref, ref.find_row("ridgefill_select", 0), b) == abi.OK
+            for name in ("x", "q", "s"):
+                if a[name] is not None:
+                    assert np.array_equal(a[name].bytes, b[name].bytes)
+        for top_k in (0, 1, 7, 300):
+            ids = Buf(abi.I32, [n + 1, top_k + 4], [top_k + 7, 1])
+            ids.flat()[:] = [r.below(1 << 20) for _ in range(len(ids.flat()))]
+            a, b = ids.copy(), ids.copy()
+            assert K.run_drop(o, o.find_row("ridgefill_drop_rows", 0), K.mask_buf(mask), a, top_k) == abi.OK
+            assert K.run_drop(ref, ref.find_row("ridgefill_drop_rows", 0), K.mask_buf(mask), b, top_k) == abi.OK
+            assert np.array_equal(a.bytes, b.bytes)
+    k = K.random_correct(r, 12, sd=16, pad=3)
+    idx = K.slot_index([4, -1, 1, 7, 4])
+    ra, oa = K.run_state_read(o, o.find_row("ridgefill_state_read", 0), k, idx)
+    rb, ob = K.run_state_read(ref, ref.find_row("ridgefill_state_read", 0), k, idx)
+    assert ra == rb == abi.OK and np.array_equal(oa.bytes, ob.bytes)
+    for _ in range(64):
+        c = K.HazardCall()
+        c.e = 1 + r.below(2048)
+        c.s = r.below(c.e)
+        c.first_pos, c.span = r.below(40000), r.below(3000)
+        c.b = c.s + r.below(c.e - c.s + 1) if r.below(2) else 0
+        c.m0, c.m1, c.count = float(r.below(45000)), float(r.below(40000)), float(r.below(100))
+        assert K.run_hazard(o, o.find_row("ridgefill_hazard", 0), c) == K.run_hazard(ref, ref.find_row("ridgefill_hazard", 0), c)
+
+
+# ----------------------------------------------------------------- golden fixtures
+
+def read_rho_fixture():
+    words = (H.GOLDEN / "rho_numpy.txt").read_text().split()
+    assert words[:2] == ["ridgefill-rho-fixture", "1"]
+    heads, chunks = int(words[3]), int(words[5])
+    pos = 8
+
+    def lst(name):
+        nonlocal pos
+        assert words[pos] == name, (words[pos], name)
+        n = int(words[pos + 1])
+        vals = [float(x) for x in words[pos + 2: pos + 2 + n]]
+        pos += 2 + n
+        return vals
+
+    a_log, dt_bias = lst("A_log"), lst("dt_bias")
+    out = []
+    for _ in range(chunks):
+        assert words[pos] == "chunk"
+        rows = int(words[pos + 3])
+        pos += 4
+        out.append((rows, lst("a"), lst("mask"), lst("N"), lst("D"), lst("rho")))
+    return heads, a_log, dt_bias, out
+
+
+def test_oracle_matches_rho_fixture(oracle_lib):
+    """tests/rho_ref.py's closed form over three chunks, ND carried: |rho diff| <= 1e-5, rel N/D <= 1e-4
+    (the reference's own bound, tests/kernel_test.cpp:1318-1342)."""
+    heads, a_log, dt_bias, chunks = read_rho_fixture()
+    nd = [0.0] * (4 * heads * 2)
+    row = oracle_lib.find_row("ridgefill_rho_update", 0)
+    for rows, a, mask, N, D, rho in chunks:
+        c = K.RhoRun()
+        c.n, c.heads, c.slot, c.a, c.mask, c.a_log, c.dt_bias, c.nd = rows, heads, 0, a, [int(m) for m in mask], a_log, dt_bias, nd
+        assert K.run_rho(oracle_lib, row, c) == abi.OK
+        nd = c.nd
+        for h in range(heads):
+            n, d = nd[h * 2], nd[h * 2 + 1]
+            assert abs(n - N[h]) / N[h] <= 1e-4 and abs(d - D[h]) / D[h] <= 1e-4
+            assert abs(K.nd_rho(c, h) - rho[h]) <= 1e-5
+
+
+def test_oracle_matches_rowsel_fixture(oracle_lib):
+    """ridgefill_mask class mode over each 2,048-row document keeps exactly the fixture's rows, and the
+    same rows + 64 when the window starts at row 64 (tests/kernel_test.cpp:1404-1456)."""
+    fx = json.loads((H.GOLDEN / "rowsel_keys.json").read_text())
+    table = np.full(fx["vocab"], -np.inf, np.float32)
+    table[fx["kept_ids"]] = fx["kept_scores"]
+    best = int(fx["kept_ids"][int(np.argmax(table[fx["kept_ids"]]))])
+    row = oracle_lib.find_row("ridgefill_mask", 0)
+    for doc in fx["docs"]:
+        ids, want = doc["token_ids"], doc["rows"]
+        w = len(ids)
+        rc, mask, bounds, _ = K.run_mask(oracle_lib, row, K.MaskCall(ids, w, 0, w, table, fx["share"], 0, "class"))
+        assert rc == abi.OK and list(np.flatnonzero(mask == 0)) == want and len(want) == doc["k"]
+        rc, mask, bounds, _ = K.run_mask(oracle_lib, row, K.MaskCall([best] * 64 + ids, w + 64, 64, w + 64, table,
+                                                                     fx["share"], 0, "class"))
+        assert rc == abi.OK and list(np.flatnonzero(mask[64:] == 0) + 64) == [r + 64 for r in want]
+        assert np.all(mask[:64] == 0) and list(bounds) == [64, w + 64, w + 64, w + 64]
+
+
+def test_oracle_matches_quantise_i8_fixture(oracle_lib):
+    """The folder's weight encoder (tools/ridgefill_projector.py quantise_i8) reproduced bit for bit."""
+    fx = np.load(H.GOLDEN / "quantise_i8.npz")
+    codes, scale = H.oracle_quantise_weight(H.bf16_bits_to_f32(fx["w_bf16"]))
+    assert np.array_equal(codes, fx["codes"]) and np.array_equal(scale, fx["scale"])
+    assert np.all(H.bf16_bits_to_f32(scale[3, 1]) == 1.0)   # the all-zero group
+
+
+def test_oracle_gemm_definition():
+    """The GEMM oracle against an independent float64 evaluation of the same definition on small shapes:
+    the int32 block sums exactly, y within one bf16 ulp (the f32 fold rounds per block)."""
+    rng = np.random.default_rng(5)
+    for M, N, K, group in ((3, 32, 256, 128), (17, 48, 384, 384), (8, 16, 128, 128)):
+        a = rng.integers(-127, 128, (M, K)).astype(np.int8)
+        b = rng.integers(-127, 128, (N, K)).astype(np.int8)
+        sa = rng.uniform(1e-3, 1e-2, (M, K // group)).astype(np.float32)
+        sb = rng.uniform(1e-3, 1e-2, (K // group, N)).astype(np.float32)
+        bias = H.f32_to_bf16_bits(rng.standard_normal(N).astype(np.float32))
+        y, acc = H.oracle_gemm(a, sa, b, sb, None, group, with_acc=True)
+        blocks = np.einsum("mjk,njk->mnj", a.astype(np.int64).reshape(M, -1, group), b.astype(np.int64).reshape(N, -1, group))
+        assert np.array_equal(acc, blocks)
+        exact = np.einsum("mnj,mj,jn->mn", blocks.astype(np.float64), sa.astype(np.float64), sb.astype(np.float64))
+        got = H.bf16_bits_to_f32(y).astype(np.float64)
+        assert np.all(np.abs(got - exact) <= np.abs(exact) * 2.0 ** -7 + 1e-30)
+        yb = H.oracle_gemm(a, sa, b, sb, bias, group)
+        want = H.f32_to_bf16_bits(H.bf16_bits_to_f32(y) + H.bf16_bits_to_f32(bias)[None, :])
+        assert np.array_equal(yb, want)
+
+
+def test_oracle_gdn_f32_tracks_f64():
+    """The timed f32 baseline stays within the state tolerance of the f64 reference value."""
+    rng = np.random.default_rng(9)
+    T, Hk, Hv, d = 200, 2, 4, 128
+    k = rng.standard_normal((T, Hk, d)).astype(np.float32)
+    k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    v = rng.standard_normal((T, Hv, d)).astype(np.float32)
+    g = -np.log1p(np.exp(rng.standard_normal((T, Hv)))).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.standard_normal((T, Hv))))).astype(np.float32)
+    state = np.zeros((2, Hv, d, d), np.float32)
+    kb, vb = H.f32_to_bf16_bits(k), H.f32_to_bf16_bits(v)
+    s64, _ = H.oracle_gdn(kb, vb, g, beta, state, [1], [0, T])
+    s32, _ = H.oracle_gdn(kb, vb, g, beta, state, [1], [0, T], f64=False)
+    assert np.linalg.norm(s32 - s64) / np.linalg.norm(s64) < 1e-5
+    assert np.all(s64[0] == 0)   # slot 0 untouched
