@@ -326,6 +326,11 @@ int ridgefill_gemm_nt_q_bias_device(const RadArgs* a, RadStream s);
 int ridgefill_quant_act_device(const RadArgs* a, RadStream s);
 int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s);
 
+/* The first error code a tensor-core kernel of this library recorded after giving up on a bounded
+ * wait (0: none), optionally cleared. Synchronises the current device: a diagnostic, never called on
+ * a launch path. -1 when the device could not be read. */
+int ridgefill_device_error(int reset);
+
 /* ridgefill_gdn_fill's scratch hook: device bytes the row needs in RadArgs::scratch. */
 int64_t ridgefill_gdn_fill_scratch(const RadArgs* a);
 
