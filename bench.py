@@ -244,6 +244,35 @@ def run_mine(args):
         dist.destroy_process_group()
 
 
+def run_only(args):
+    """Launch one op of the pass repeatedly at --rows rows (after --warmup full passes that fill its
+    inputs): a small, self-contained command for an ncu capture of that op's kernels."""
+    import torch
+    import ridgefill_step as RS
+    step = RS.Step(RS.StepShape(T=args.rows), device="cuda", seed=1234)
+    stream = torch.cuda.Stream()
+    calls = [c for c in step._args if c[0] == args.only]
+    if not calls:
+        raise SystemExit(f"--only {args.only}: not an op of the pass")
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step.run(stream.cuda_stream)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        stream.synchronize()
+        a.record()
+        for _ in range(args.steps):
+            for name, r, tens, params in calls:
+                sb = step.gdn_scratch if name == "ridgefill_gdn_fill" else 0
+                rc = step.lib.launch(r, tens, params, stream=stream.cuda_stream,
+                                     scratch=step.scratch.data_ptr() if sb else None, scratch_bytes=sb)
+                if rc != 0:
+                    raise SystemExit(f"{name}: rc {rc}")
+        b.record()
+        stream.synchronize()
+    print(json.dumps({"op": args.only, "rows": args.rows, "launches": args.steps * len(calls),
+                      "ms_per_launch": a.elapsed_time(b) / (args.steps * len(calls))}), flush=True)
+
+
 def Step_launches(step) -> int:
     return step.LAUNCHES_PER_PASS
 
@@ -255,8 +284,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--only", default=None, help="profile mode: launch only this op of the pass")
+    ap.add_argument("--rows", type=int, default=T_FULL, help="rows of the chunk in --only mode")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.only:
+        run_only(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_mine(args)
