@@ -25,6 +25,8 @@
  */
 #include <cuda_fp16.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "mma.cuh"
 
@@ -476,4 +478,64 @@ extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
     if (cudaGetLastError() != cudaSuccess) return RAD_E_DEVICE;
     gdn_chain_kernel<<<dim3(D / VS, (unsigned)g.n_head_v, (unsigned)g.n_seq), 128, sizeof(ChainSmem), stream>>>(p);
     return rf::launch_status();
+}
+
+/* ================================================================== the allocation-free entry point
+ *
+ * ridgefill_gdn_fill_noalloc: the DeltaNet fill for callers that cannot hand it a workspace. Some callers
+ * of this library have no way to allocate device memory at the point they launch the fill: a host that
+ * binds the C ABI through an FFI (ctypes, cgo, JNI) and receives its device buffers from elsewhere but
+ * has no device allocator of its own, and an engine step whose device memory is fixed before the pass
+ * starts, where a cudaMalloc inside the pass is not allowed (it can synchronise the device and stall
+ * every stream of the step). This entry point takes the same operands as the ridgefill_gdn_fill row,
+ * ignores RadArgs::scratch, and uses instead a workspace compiled into the library: a file-scope device
+ * array of kNoAllocScratchBytes (32 MiB), which every GPU that loads the library holds until the
+ * process exits. 32 MiB holds the fill's workspace for a 4,096-row call at 48 value heads (8.5 KiB per
+ * 64-row chunk and head); a call that needs more returns RAD_E_SHAPE and launches nothing.
+ *
+ * The first call on each device resolves the array's device address there (cudaGetSymbolAddress, once
+ * per device, with that device current); make that first call before any stream capture. No call
+ * allocates or frees device memory. Every call shares the one array and the array keeps the last call's
+ * contents: nothing in it needs to start at zero (each call writes every byte of the workspace it reads
+ * before reading it, in stream order), but two calls that overlap on the GPU -- on different streams,
+ * or from different threads, without an ordering between them -- race on it.
+ */
+namespace {
+constexpr int64_t kNoAllocScratchBytes = 32ll << 20;
+constexpr int kNoAllocMaxDevices = 64;
+}   // namespace
+
+static __device__ __align__(256) uint8_t g_gdn_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+std::mutex g_noalloc_mutex;
+void* g_noalloc_address[kNoAllocMaxDevices];
+
+/* The array's device address on the current device; resolved on the first call there. */
+int noalloc_workspace(void** out) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return RAD_E_DEVICE;
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_address[dev]) {
+        void* ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_gdn_noalloc_scratch) != cudaSuccess || !ptr) return RAD_E_DEVICE;
+        g_noalloc_address[dev] = ptr;
+    }
+    *out = g_noalloc_address[dev];
+    return RAD_OK;
+}
+}   // namespace
+
+extern "C" int ridgefill_gdn_fill_noalloc(const RadArgs* a, RadStream s) {
+    RidgeFillGdn g;
+    const int rc = ridgefill_gdn_parse(a, &g);
+    if (rc != RAD_OK) return rc;
+    if (ridgefill_gdn_fill_scratch(a) > kNoAllocScratchBytes) return RAD_E_SHAPE;   /* past the built-in workspace */
+    void* workspace = nullptr;
+    const int ws = noalloc_workspace(&workspace);
+    if (ws != RAD_OK) return ws;
+    RadArgs with = *a;
+    with.scratch = workspace;
+    with.scratch_bytes = kNoAllocScratchBytes;
+    return ridgefill_gdn_fill_device(&with, s);
 }
