@@ -338,11 +338,7 @@ extern "C" int ridgefill_quant_act_device(const RadArgs* a, RadStream s) {
 /* The first device-side wait error any kernel of this library recorded (0: none), optionally
  * clearing it. Synchronises the current device: a diagnostic, never called on the launch path. */
 extern "C" int ridgefill_device_error(int reset) {
-    int v = 0;
-    if (cudaMemcpyFromSymbol(&v, rf::g_device_error, sizeof v) != cudaSuccess) return -1;
-    if (reset) {
-        const int zero = 0;
-        if (cudaMemcpyToSymbol(rf::g_device_error, &zero, sizeof zero) != cudaSuccess) return -1;
-    }
-    return v;
+    const int gemm = rf::read_device_error(reset), fill = rf::gdn_device_error(reset);
+    if (gemm < 0 || fill < 0) return -1;
+    return gemm ? gemm : fill;
 }

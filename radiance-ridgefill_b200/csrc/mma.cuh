@@ -65,12 +65,29 @@ __device__ __forceinline__ void load_b_kn(uint32_t (&b)[4], const void* base, in
     ldsm_x4_t(b, saddr(p));
 }
 
+/* Shared-memory byte address of element (row, col) of a [64][128] b16 tile stored as two 64-column
+ * halves of [64][64], each written by TMA with 128-byte swizzle (16-byte chunk j of row r at chunk
+ * j ^ (r & 7)); `tile` 1024-byte aligned, col a multiple of 8. */
+__device__ __forceinline__ uint32_t sw128_addr(uint32_t tile, int row, int col) {
+    return tile + (uint32_t)((col >> 6) * 8192 + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4));
+}
+
+/* load_a / load_b_nk on such a tile. */
+__device__ __forceinline__ void load_a_sw(uint32_t (&a)[4], uint32_t tile, int row0, int col0) {
+    const int l = threadIdx.x & 31, mi = l >> 3, r = l & 7;
+    ldsm_x4(a, sw128_addr(tile, row0 + r + (mi & 1) * 8, col0 + (mi >> 1) * 8));
+}
+__device__ __forceinline__ void load_b_nk_sw(uint32_t (&b)[4], uint32_t tile, int n0, int k0) {
+    const int l = threadIdx.x & 31, mi = l >> 3, r = l & 7;
+    ldsm_x4(b, sw128_addr(tile, n0 + r + (mi >> 1) * 8, k0 + (mi & 1) * 8));
+}
+
 __device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
     const __half2 h = __floats2half2_rn(lo, hi);
     return *(const uint32_t*)&h;
 }
 
-/* The A fragment of k-step s from two f32 C tiles c[2s], c[2s+1] (each [4]), each value times `mul`. */
+/* The A fragment of k-step s from two f32 C tiles c[2s], c[2s+1] (each [4]), rounded to f16. */
 __device__ __forceinline__ void c_to_a(uint32_t (&a)[4], const float (&lo)[4], const float (&hi)[4]) {
     a[0] = pack_f16(lo[0], lo[1]);
     a[1] = pack_f16(lo[2], lo[3]);

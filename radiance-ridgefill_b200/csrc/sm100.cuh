@@ -9,6 +9,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -18,6 +19,20 @@ namespace rf {
  * per translation unit that includes this header (no relocatable device code); the library's accessor
  * reads every copy. */
 static __device__ int g_device_error = 0;
+
+/* This translation unit's copy of g_device_error (host code; synchronises). `reset` clears it. */
+static inline int read_device_error(int reset) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof v) != cudaSuccess) return -1;
+    if (reset) {
+        const int zero = 0;
+        if (cudaMemcpyToSymbol(g_device_error, &zero, sizeof zero) != cudaSuccess) return -1;
+    }
+    return v;
+}
+
+/* The DeltaNet fill's copy (gdn.cu). */
+int gdn_device_error(int reset);
 
 enum DeviceError : int {
     kErrNone = 0,
@@ -92,8 +107,37 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
         : "memory");
 }
 
+/* 3-D TMA tile load (coordinates innermost first, in elements), completing on `bar`. No multicast. */
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t x, int32_t y, int32_t z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(smem_addr(dst)), "l"((uint64_t)map), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+/* Bulk (non-tensor) copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from global to
+ * shared memory, completing on `bar`. No multicast. */
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar))
+                 : "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)map) : "memory");
+}
+
+/* The driver's tensor-map encoder, resolved once through the runtime (no link against libcuda). */
+inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (PFN_cuTensorMapEncodeTiled_v12000)f;
+    }
+    return fn;
 }
 
 /* ------------------------------------------------------------------ tensor memory */
