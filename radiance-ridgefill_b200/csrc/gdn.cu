@@ -10,18 +10,21 @@
  * cumulative log decay and gamma = exp(G), the chunk's corrected values u solve
  *     (I + A) u = diag(beta) v - diag(beta gamma) K S0^T,   A_ij = beta_i exp(G_i - G_j) k_i.k_j (j < i)
  * so with T = (I + A)^-1:  U = T (beta v) - T (beta gamma K) S0^T = U~ - W S0^T, and at the chunk end
- *     S_L = gamma_L S0 + U^T diag(exp(G_L - G)) K.
+ *     S_L = gamma_L S0 + U^T K~,   K~ = diag(exp(G_L - G)) K.
  *
- *   phase 1 (gdn_prep_kernel), every (chunk, head) in parallel, persistent CTAs, the next item's k rows
+ *   plan (gdn_plan_kernel), one CTA: each sequence's clamped rows and the number of chunks before it,
+ *     into the head of the scratch, so neither phase walks cu_seqlens.
+ *   phase 1 (gdn_prep_kernel), every (chunk, v-head) in parallel, persistent CTAs, the next item's k rows
  *     arriving by TMA (two 128-byte-swizzled boxes) while the current one is computed: K K^T on tensor
- *     cores (bf16, exact inputs), A, T by blocked inversion (16x16 diagonal blocks by substitution in
- *     f32, off-diagonal blocks by f16 tensor-core products) and W = T (beta gamma K). T and W (f16) are
- *     written to the chunk's scratch slot already in phase 2's shared-memory layout, with G and beta.
+ *     cores (bf16, exact inputs), A, T by blocked inversion (16x16 diagonal blocks by column-parallel
+ *     substitution in f32, off-diagonal blocks by f16 tensor-core products), W = T (beta gamma K) and
+ *     K~. The chunk's scratch slot receives W, K~, T (f16), G and beta in phase 2's shared-memory layout
+ *     (W and T|G|beta by bulk stores from shared memory, K~ straight from registers).
  *   phase 2 (gdn_chain_kernel), one CTA per (32-row slice of dv, head, sequence), sequential over the
  *     sequence's chunks, warp-specialised:
  *       4 producer warps prepare chunk c+1 while the chain runs chunk c: each chunk's inputs arrive in
- *       five copies two chunks ahead (T, W, G|beta by bulk copy; k rows and the slice's v columns by TMA
- *       boxes); they form K~ = k * exp(G_L - G) (f16) and U~ = T (beta v) for the slice;
+ *       three copies two chunks ahead (W|K~ and T|G|beta by bulk copy, the slice's v columns by a TMA
+ *       box); they form U~ = T (beta v) for the slice and gamma_L;
  *       4 chain warps (2 dv row halves x 2 dk halves) hold the state slice in registers and run
  *       V' = U~ - W S^T,  S <- gamma_L S + V'^T K~ on f16 mma.sync with f32 accumulation.
  *     The roles hand chunks over through mbarriers (bounded waits, taken by one thread a role and
@@ -31,6 +34,7 @@
  */
 #include <cuda_fp16.h>
 
+#include <cstddef>
 #include <mutex>
 
 #include "common.cuh"
@@ -49,22 +53,28 @@ constexpr int AP = C + 4;      /* pitch of the f32 A matrix */
 constexpr int UP = VS + 4;     /* pitch of the f32 U~ slice */
 constexpr int PP = C + 4;      /* pitch of the f32 exchange tiles */
 
-/* A chunk's scratch slot, per (chunk, v-head), in phase 2's shared-memory layout: T f16 [64][TP],
- * W f16 [64][KP], then G f32 [64] and beta f32 [64]. */
-constexpr int kSlotT = 0, kSlotW = C * TP * 2, kSlotMeta = kSlotW + C * KP * 2;
+/* A chunk's scratch slot, per (chunk, v-head), in phase 2's shared-memory layout: W f16 [64][KP],
+ * K~ f16 [64][KP], T f16 [64][TP], G f32 [64], beta f32 [64]. */
+constexpr int kSlotW = 0, kSlotK = C * KP * 2, kSlotT = kSlotK + C * KP * 2, kSlotMeta = kSlotT + C * TP * 2;
 constexpr int kSlotBytes = kSlotMeta + 2 * C * 4;
+constexpr uint32_t kWKBytes = 2 * C * KP * 2, kTMBytes = C * TP * 2 + 2 * C * 4;
 constexpr uint32_t kKBoxBytes = C * D * 2, kVBoxBytes = C * VS * 2;
 
 enum { kBarProducers = 1, kBarChain = 2, kBarPair0 = 3 };   /* named barriers (0 is __syncthreads) */
 
+/* The scratch: the sequence table (int32 r0[n], r1[n], base[n + 1], padded to 256 bytes), then the
+ * chunk slots. base[i] is the number of chunks before sequence i, capped at max_slots. */
+int64_t table_bytes(int64_t n_seq) { return (3 * n_seq + 1) * 4 + 255 & ~(int64_t)255; }
+
 struct GdnPlan {
     RidgeFillGdn g;
-    uint8_t* scratch;
+    int32_t* tab;     /* the sequence table */
+    uint8_t* slots;   /* the chunk slots */
     int max_slots;
 };
 
 __device__ __forceinline__ uint8_t* slot_ptr(const GdnPlan& p, int64_t slot, int64_t h) {
-    return p.scratch + (slot * p.g.n_head_v + h) * (int64_t)kSlotBytes;
+    return p.slots + (slot * p.g.n_head_v + h) * (int64_t)kSlotBytes;
 }
 
 __device__ __forceinline__ void bar_sync(int id, int threads) {
@@ -76,60 +86,112 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src, int src_by
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(rf::saddr(dst)), "l"(src), "r"(src_bytes) : "memory");
 }
 
-/* Sequence i's rows [*r0, *r1): cu_seqlens read on the device and clamped into [0, T] (a value the host
- * cannot check never sends a load outside the operands). */
-__device__ __forceinline__ void seq_rows(const RidgeFillGdn& g, int64_t i, int64_t* r0, int64_t* r1) {
-    const int64_t a = min(max((int64_t)g.cu[i], (int64_t)0), g.T);
-    const int64_t b = min(max((int64_t)g.cu[i + 1], a), g.T);
-    *r0 = a;
-    *r1 = b;
-}
+/* ------------------------------------------------------------------ plan */
 
-/* The sequence holding chunk `slot` (chunks of each sequence numbered consecutively, sequence by
- * sequence), its chunk's first row and length; false past the last chunk. */
-__device__ bool locate_chunk(const RidgeFillGdn& g, int64_t slot, int64_t* row0, int* len) {
-    int64_t base = 0;
-    for (int64_t i = 0; i < g.n_seq; ++i) {
-        int64_t r0, r1;
-        seq_rows(g, i, &r0, &r1);
-        const int64_t chunks = (r1 - r0 + C - 1) / C;
-        if (slot < base + chunks) {
-            const int64_t c = slot - base;
-            *row0 = r0 + c * C;
-            *len = (int)min((int64_t)C, r1 - r0 - c * C);
-            return true;
+constexpr int kPlanThreads = 1024;
+
+/* Sequence i's rows [r0, r1): cu_seqlens read on the device and clamped into [0, T] (a value the host
+ * cannot check never sends a load outside the operands), and base[i] by a block-wide scan. */
+__global__ void __launch_bounds__(kPlanThreads) gdn_plan_kernel(const GdnPlan p) {
+    __shared__ long long warp_sum[32];
+    __shared__ long long carry;
+    const RidgeFillGdn& g = p.g;
+    const int n = (int)g.n_seq, l = threadIdx.x & 31, w = threadIdx.x >> 5;
+    int32_t* r0t = p.tab;
+    int32_t* r1t = p.tab + n;
+    int32_t* bt = p.tab + 2 * n;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    for (int i0 = 0; i0 < n; i0 += kPlanThreads) {
+        const int i = i0 + threadIdx.x;
+        long long chunks = 0;
+        if (i < n) {
+            const int64_t a = min(max((int64_t)g.cu[i], (int64_t)0), g.T);
+            const int64_t b = min(max((int64_t)g.cu[i + 1], a), g.T);
+            r0t[i] = (int32_t)a;
+            r1t[i] = (int32_t)b;
+            chunks = (b - a + C - 1) / C;
         }
-        base += chunks;
+        long long x = chunks;
+        for (int o = 1; o < 32; o <<= 1) {
+            const long long y = __shfl_up_sync(0xffffffffu, x, o);
+            if (l >= o) x += y;
+        }
+        if (l == 31) warp_sum[w] = x;
+        __syncthreads();
+        if (w == 0) {
+            long long t = warp_sum[l];
+            for (int o = 1; o < 32; o <<= 1) {
+                const long long y = __shfl_up_sync(0xffffffffu, t, o);
+                if (l >= o) t += y;
+            }
+            warp_sum[l] = t;
+        }
+        __syncthreads();
+        const long long incl = carry + (w ? warp_sum[w - 1] : 0) + x;
+        if (i < n) bt[i] = (int32_t)min(incl - chunks, (long long)p.max_slots);
+        __syncthreads();
+        if (threadIdx.x == kPlanThreads - 1) carry = incl;
+        __syncthreads();
     }
-    return false;
-}
-
-__device__ int64_t total_chunks(const GdnPlan& p) {
-    int64_t n = 0, r0, r1;
-    for (int64_t i = 0; i < p.g.n_seq; ++i) {
-        seq_rows(p.g, i, &r0, &r1);
-        n += (r1 - r0 + C - 1) / C;
-    }
-    return min(n, (int64_t)p.max_slots);
+    if (threadIdx.x == 0) bt[n] = (int32_t)min(carry, (long long)p.max_slots);
 }
 
 /* ------------------------------------------------------------------ phase 1 */
 
 constexpr int kPrepThreads = 256;
+constexpr int kSeqCache = 256;   /* sequences whose table rows a phase-1 CTA keeps in shared memory */
 
 struct PrepSmem {
     uint16_t kraw[2][2][C][C];   /* k rows of the current and the next item: two 128-byte-swizzled halves */
     float graw[2][C], braw[2][C];
     float a32[C][AP];            /* A, f32 */
     uint16_t l16[C][TP];         /* A, f16 (the off-diagonal blocks of I + A) */
-    uint16_t t16[C][TP];         /* T = (I + A)^-1, f16 */
-    uint16_t x1[C][KP];          /* beta gamma k, f16 */
-    uint16_t w16[C][KP];         /* W = T x1, f16 */
-    uint16_t tmp[3][16][24];     /* per-warp 16x16 staging */
+    uint16_t w16[C][KP];         /* W = T x1, f16: bulk-stored to the slot */
+    uint16_t t16[C][TP];         /* T = (I + A)^-1, f16, then G and beta: bulk-stored together */
     float G[C], beta[C];
+    uint16_t x1[C][KP];          /* beta gamma k, f16 */
+    uint16_t tmp[3][16][24];     /* per-warp 16x16 staging */
+    int32_t r0[kSeqCache], base[kSeqCache + 1];
     uint64_t landed[2];          /* the k rows of buffer b have landed */
-    int abort, ok;
+    int abort, ok, n_cached;
 };
+static_assert(offsetof(PrepSmem, G) == offsetof(PrepSmem, t16) + sizeof(uint16_t) * C * TP, "T|G|beta contiguous");
+static_assert(offsetof(PrepSmem, beta) == offsetof(PrepSmem, G) + sizeof(float) * C, "T|G|beta contiguous");
+static_assert(offsetof(PrepSmem, w16) % 16 == 0 && offsetof(PrepSmem, t16) % 16 == 0, "bulk-store sources");
+
+/* Chunk `slot` (< the table's base[n]): its first row and length. The largest i with base[i] <= slot,
+ * searched in the cached rows of the table when the slot lies there, else in the table. */
+__device__ void locate_chunk(const GdnPlan& p, const PrepSmem& s, int64_t slot, int64_t* row0, int* len) {
+    const int n = (int)p.g.n_seq;
+    const int32_t* r0t = p.tab;
+    const int32_t* r1t = p.tab + n;
+    const int32_t* bt = p.tab + 2 * n;
+    int lo, hi, i;
+    if (slot < s.base[s.n_cached]) {
+        lo = 0;
+        hi = s.n_cached - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (s.base[mid] <= slot) lo = mid;
+            else hi = mid - 1;
+        }
+        i = lo;
+        const int64_t c = slot - s.base[i];
+        *row0 = s.r0[i] + c * C;
+    } else {
+        lo = s.n_cached;
+        hi = n - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (bt[mid] <= slot) lo = mid;
+            else hi = mid - 1;
+        }
+        i = lo;
+        *row0 = r0t[i] + (slot - bt[i]) * C;
+    }
+    *len = (int)min((int64_t)C, (int64_t)r1t[i] - *row0);
+}
 
 /* T[bi][bj] = -T[bi][bi] * sum_{k=bj}^{bi-1} L[bi][k] T[k][bj] for one 16x16 block, one warp. */
 __device__ void tri_offdiag_block(PrepSmem& s, int bi, int bj, int w) {
@@ -168,7 +230,7 @@ __device__ void prep_issue(const GdnPlan& p, const CUtensorMap* kmap, PrepSmem& 
     const int64_t slot = item / g.n_head_v, h = item % g.n_head_v, hk = h / (g.n_head_v / g.n_head_k);
     int64_t row0 = 0;
     int len = 0;
-    locate_chunk(g, slot, &row0, &len);
+    locate_chunk(p, s, slot, &row0, &len);
     if (threadIdx.x == 0) {
         rf::mbar_arrive_expect_tx(&s.landed[buf], kKBoxBytes);
         rf::tma_load_3d(&s.kraw[buf][0][0][0], kmap, &s.landed[buf], 0, (int)hk, (int)row0);
@@ -187,15 +249,22 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_kernel(const __grid_
     PrepSmem& s = *(PrepSmem*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const RidgeFillGdn& g = p.g;
     const int tid = threadIdx.x, w = tid >> 5, l = tid & 31, gq = l >> 2, tq = l & 3;
-    const int64_t items = total_chunks(p) * g.n_head_v;
+    const int n_seq = (int)g.n_seq;
+    const int n_cached = n_seq < kSeqCache ? n_seq : kSeqCache;
+    for (int i = tid; i <= n_cached; i += kPrepThreads) {
+        if (i < n_cached) s.r0[i] = p.tab[i];
+        s.base[i] = p.tab[2 * n_seq + i];
+    }
     if (tid == 0) {
         rf::mbar_init(&s.landed[0], 1);
         rf::mbar_init(&s.landed[1], 1);
         s.abort = 0;
+        s.n_cached = n_cached;
         rf::mbar_init_fence();
         rf::tma_prefetch_map(&kmap);
     }
     __syncthreads();
+    const int64_t items = (int64_t)p.tab[3 * n_seq] * g.n_head_v;
 
     if ((int64_t)blockIdx.x < items) prep_issue(p, &kmap, s, blockIdx.x, 0);
     rf::cp_async_commit();
@@ -208,14 +277,18 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_kernel(const __grid_
         }
         rf::cp_async_commit();
         rf::cp_async_wait<1>();
-        if (tid == 0) s.ok = rf::mbar_wait(&s.landed[buf], (uint32_t)((waited >> 1) & 1), &s.abort, rf::kErrGdnWait);
+        if (tid == 0) {
+            s.ok = rf::mbar_wait(&s.landed[buf], (uint32_t)((waited >> 1) & 1), &s.abort, rf::kErrGdnWait);
+            rf::bulk_store_wait_read();   /* the previous item's stores have read w16, t16, G, beta */
+        }
         __syncthreads();
         if (!s.ok) break;
         ++waited;
         const int64_t slot = item / g.n_head_v, h = item % g.n_head_v;
         int64_t row0 = 0;
         int len = 0;
-        locate_chunk(g, slot, &row0, &len);
+        locate_chunk(p, s, slot, &row0, &len);
+        uint8_t* out = slot_ptr(p, slot, h);
         const uint32_t ktile = rf::saddr(&s.kraw[buf][0][0][0]);
 
         /* G (inclusive cumulative log decay; zero past the chunk) and beta. */
@@ -231,23 +304,35 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_kernel(const __grid_
         __syncthreads();
         if (tid >= 32 && tid < C) s.G[tid] += s.G[31];
         __syncthreads();
+        const float gl = s.G[len - 1];
 
-        /* x1 = beta gamma k in f16 (rows past the chunk: beta 0); K K^T (warp w: rows 16 (w & 3),
-         * columns 32 (w >> 2)..+32) and A. */
-        for (int i = tid; i < C * (D / 8); i += kPrepThreads) {
-            const int r = i >> 4, seg = i & 15;
+        /* x1 = beta gamma k (shared) and K~ = k exp(G_L - G) (to the slot), f16, both zero past the
+         * chunk; the upper blocks of T zero. */
+#pragma unroll
+        for (int it = 0; it < 4; ++it) {
+            const int r = (tid >> 4) + 16 * it, seg = tid & 15;
             uint4 raw;
             asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(raw.x), "=r"(raw.y), "=r"(raw.z), "=r"(raw.w)
                          : "r"(rf::sw128_addr(ktile, r, seg * 8)));
             const uint32_t rw[4] = { raw.x, raw.y, raw.z, raw.w };
-            const float f = r < len ? s.beta[r] * __expf(s.G[r]) : 0.0f;
-            uint32_t xx[4];
+            const bool in = r < len;
+            const float fx = in ? s.beta[r] * __expf(s.G[r]) : 0.0f, fk = in ? __expf(gl - s.G[r]) : 0.0f;
+            uint32_t xx[4], kk[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-                xx[e] = r < len ? rf::pack_f16(f * __uint_as_float(rw[e] << 16), f * __uint_as_float(rw[e] & 0xffff0000u)) : 0u;
+            for (int e = 0; e < 4; ++e) {
+                const float lo = __uint_as_float(rw[e] << 16), hi = __uint_as_float(rw[e] & 0xffff0000u);
+                xx[e] = in ? rf::pack_f16(fx * lo, fx * hi) : 0u;
+                kk[e] = in ? rf::pack_f16(fk * lo, fk * hi) : 0u;
+            }
             *(uint4*)&s.x1[r][seg * 8] = make_uint4(xx[0], xx[1], xx[2], xx[3]);
+            *(uint4*)(out + kSlotK + (r * KP + seg * 8) * 2) = make_uint4(kk[0], kk[1], kk[2], kk[3]);
         }
-        {
+        for (int i = tid; i < 6 * 16 * 8; i += kPrepThreads) {   /* blocks (0,1) (0,2) (0,3) (1,2) (1,3) (2,3) */
+            const int blk = i >> 7, r = (i >> 3) & 15, cp = i & 7;
+            const int bi = blk < 3 ? 0 : blk < 5 ? 1 : 2, bj = blk < 3 ? blk + 1 : blk < 5 ? blk - 1 : 3;
+            *(uint32_t*)&s.t16[16 * bi + r][16 * bj + 2 * cp] = 0u;
+        }
+        {   /* K K^T (warp w: rows 16 (w & 3), columns 32 (w >> 2)..+32) and A */
             const int rb = 16 * (w & 3), cb = 32 * (w >> 2);
             float acc[4][4] = {};
 #pragma unroll
@@ -274,23 +359,31 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_kernel(const __grid_
         }
         __syncthreads();
 
-        /* Diagonal blocks: column c of block b by forward substitution in f32; upper blocks zero. */
-        if (tid < C) {
-            const int b = tid >> 4, c = tid & 15;
-            float col[16];
+        /* Diagonal blocks of T, by substitution in f32: warp w solves block w >> 1 for columns
+         * 8 (w & 1)..+8, lane l holding row l & 15 of 4 columns; row j is final at step j and is
+         * broadcast to the rows below it. */
+        {
+            const int b = w >> 1, r = l & 15, c0 = 8 * (w & 1) + 4 * (l >> 4);
+            float a[16];
 #pragma unroll
-            for (int r = 0; r < 16; ++r) {
-                float x = r == c ? 1.0f : 0.0f;
+            for (int q = 0; q < 4; ++q) {
+                const float4 v = *(const float4*)&s.a32[16 * b + r][16 * b + 4 * q];
+                a[4 * q] = v.x;
+                a[4 * q + 1] = v.y;
+                a[4 * q + 2] = v.z;
+                a[4 * q + 3] = v.w;
+            }
+            float x[4];
 #pragma unroll
-                for (int j = 0; j < r; ++j) x -= s.a32[16 * b + r][16 * b + j] * col[j];
-                col[r] = x;
-                s.t16[16 * b + r][16 * b + c] = __half_as_ushort(__float2half_rn(x));
-            }
-        } else {
-            for (int i = tid - C; i < C * C; i += kPrepThreads - C) {
-                const int r = i >> 6, c = i & 63;
-                if ((c >> 4) > (r >> 4)) s.t16[r][c] = 0;
-            }
+            for (int cc = 0; cc < 4; ++cc) x[cc] = r == c0 + cc ? 1.0f : 0.0f;
+#pragma unroll
+            for (int j = 0; j < 15; ++j)
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                    const float xj = __shfl_sync(0xffffffffu, x[cc], (l & 16) | j);
+                    x[cc] = fmaf(-a[j], xj, x[cc]);   /* a[j] = 0 for j >= r */
+                }
+            *(uint2*)&s.t16[16 * b + r][16 * b + c0] = make_uint2(rf::pack_f16(x[0], x[1]), rf::pack_f16(x[2], x[3]));
         }
         __syncthreads();
         if (w < 3) tri_offdiag_block(s, w + 1, w, w);            /* T10, T21, T32 */
@@ -323,91 +416,86 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_kernel(const __grid_
                 }
             }
         }
+        rf::fence_proxy_async_smem();
         __syncthreads();
-
-        /* The slot, in phase 2's layout: T and W byte for byte as they sit here, then G and beta. */
-        uint8_t* out = slot_ptr(p, slot, h);
-        for (int i = tid; i < (int)(sizeof(s.t16) / 16); i += kPrepThreads)
-            *(uint4*)(out + kSlotT + i * 16) = *((const uint4*)&s.t16[0][0] + i);
-        for (int i = tid; i < (int)(sizeof(s.w16) / 16); i += kPrepThreads)
-            *(uint4*)(out + kSlotW + i * 16) = *((const uint4*)&s.w16[0][0] + i);
-        float* meta = (float*)(out + kSlotMeta);
-        if (tid < C) meta[tid] = s.G[tid];
-        else if (tid < 2 * C) meta[tid] = s.beta[tid - C];
-        __syncthreads();   /* this item's buffers are read before the next item's loads land in them */
+        if (tid == 0) {   /* W, and T|G|beta, to the slot; read back by the next item's first wait */
+            rf::bulk_store(out + kSlotW, &s.w16[0][0], sizeof(s.w16));
+            rf::bulk_store(out + kSlotT, &s.t16[0][0], kTMBytes);
+            rf::bulk_store_commit();
+        }
     }
     rf::cp_async_wait<0>();
-    /* After a timed-out wait: let the copies already issued land before the CTA's shared memory is
-     * released (bounded too). */
-    if (tid == 0)
+    if (tid == 0) {
+        rf::bulk_store_wait();
+        /* After a timed-out wait: let the copies already issued land before the CTA's shared memory is
+         * released (bounded too). */
         for (int64_t i = waited; i < issued; ++i) {
             const uint64_t t0 = rf::global_ns();
             while (!rf::mbar_try_wait(&s.landed[i & 1], (uint32_t)((i >> 1) & 1)) && rf::global_ns() - t0 < rf::kWaitTimeoutNs) {
             }
         }
+    }
 }
 
 /* ------------------------------------------------------------------ phase 2 */
 
 constexpr int kChainThreads = 256;   /* warps 0-3: the chain; warps 4-7: producers */
 
+struct WKStage {                 /* bulk copy of the slot's W|K~ */
+    uint16_t w16[C][KP];
+    uint16_t kt16[C][KP];
+};
+
 struct RawStage {
-    uint16_t t16[C][TP];      /* T, f16 (bulk copy of the slot) */
-    float meta[2 * C];        /* G, beta */
-    uint16_t kraw[C][D];      /* k rows, bf16 (TMA box; rows past the chunk are the next rows or zero) */
-    uint16_t vraw[C][VS];     /* this CTA's 32 columns of v, bf16 (TMA box) */
+    uint16_t t16[C][TP];         /* T, f16, then G and beta (bulk copy of the slot's T|G|beta) */
+    float meta[2 * C];
+    uint16_t vraw[C][VS];        /* this CTA's 32 columns of v, bf16 (TMA box) */
 };
 
 struct ChainSmem {
     RawStage raw[2];             /* producers' inputs, two chunks in flight */
-    uint16_t w16[3][C][KP];      /* W of chunks c, c+1, c+2 (the chain reads W of c) */
-    uint16_t kt16[2][C][KP];     /* K~ = k * exp(G_L - G), f16, per chunk */
+    WKStage wk[3];               /* W and K~ of chunks c, c+1, c+2 (the chain reads chunk c's) */
     float u32[2][C][UP];         /* U~ = T (beta v) for the slice, f32, per chunk */
     uint16_t x2[C][VP];          /* beta v, f16 (producers only) */
     float part[2][4][16][PP];    /* the chain warps' partial V'^T, double-buffered */
     float gl[2];                 /* gamma_L per chunk */
-    uint64_t landed[2];          /* raw stage b (and its W stage) has landed */
+    uint64_t landed[2];          /* raw stage b (and its W|K~ stage) has landed */
     uint64_t ready[2], consumed[2];
     int abort, ok_producers, ok_chain;
 };
+static_assert(offsetof(RawStage, meta) == sizeof(uint16_t) * C * TP && offsetof(RawStage, vraw) % 128 == 0 &&
+                  sizeof(RawStage) % 128 == 0 && offsetof(ChainSmem, wk) % 16 == 0 && sizeof(WKStage) == kWKBytes,
+              "stage layout");
 
-/* Start chunk `slot`'s inputs into raw stage `rbuf` and W stage `wbuf`: T, W and G|beta by one bulk copy
- * each from its scratch slot, the k rows and this CTA's v columns by one TMA box each; all complete on
- * landed[rbuf]. One producer thread. */
-__device__ void chain_issue(const GdnPlan& p, const CUtensorMap* kmap, const CUtensorMap* vmap, ChainSmem& s, int64_t slot,
-                            int64_t row0, int64_t h, int64_t hk, int v0, int rbuf, int wbuf) {
+/* Start chunk `slot`'s inputs into raw stage `rbuf` and W|K~ stage `wbuf`: W|K~ and T|G|beta by one bulk
+ * copy each from its scratch slot, this CTA's v columns by one TMA box; all complete on landed[rbuf].
+ * One producer thread. */
+__device__ void chain_issue(const GdnPlan& p, const CUtensorMap* vmap, ChainSmem& s, int64_t slot, int64_t row0,
+                            int64_t h, int v0, int rbuf, int wbuf) {
     const uint8_t* src = slot_ptr(p, slot, h);
     RawStage& st = s.raw[rbuf];
     uint64_t* bar = &s.landed[rbuf];
-    rf::mbar_arrive_expect_tx(bar, (uint32_t)(sizeof(st.t16) + sizeof(s.w16[0]) + sizeof(st.meta)) + kKBoxBytes + kVBoxBytes);
-    rf::bulk_load(&st.t16[0][0], src + kSlotT, sizeof(st.t16), bar);
-    rf::bulk_load(&s.w16[wbuf][0][0], src + kSlotW, sizeof(s.w16[0]), bar);
-    rf::bulk_load(&st.meta[0], src + kSlotMeta, sizeof(st.meta), bar);
-    rf::tma_load_3d(&st.kraw[0][0], kmap, bar, 0, (int)hk, (int)row0);
+    rf::mbar_arrive_expect_tx(bar, kWKBytes + kTMBytes + kVBoxBytes);
+    rf::bulk_load(&s.wk[wbuf], src + kSlotW, kWKBytes, bar);
+    rf::bulk_load(&st.t16[0][0], src + kSlotT, kTMBytes, bar);
     rf::tma_load_3d(&st.vraw[0][0], vmap, bar, v0, (int)h, (int)row0);
 }
 
-__global__ void __launch_bounds__(kChainThreads, 1)
-gdn_chain_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const GdnPlan p) {
+__global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const __grid_constant__ CUtensorMap vmap, const GdnPlan p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     ChainSmem& s = *(ChainSmem*)(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
     const RidgeFillGdn& g = p.g;
     const int vsl = blockIdx.x;
-    const int64_t h = blockIdx.y, seq = blockIdx.z, hk = h / (g.n_head_v / g.n_head_k);
+    const int64_t h = blockIdx.y, seq = blockIdx.z;
     const int64_t state_slot = g.state_idx[seq * g.idx_pitch];
     if (state_slot < 0 || state_slot >= g.n_states) return;
     const int tid = threadIdx.x, w = tid >> 5, l = tid & 31, gq = l >> 2, tq = l & 3;
     const int v0 = vsl * VS;
 
-    /* This sequence's rows and first chunk slot. */
-    int64_t base = 0, r0 = 0, r1 = 0;
-    for (int64_t i = 0; i < seq; ++i) {
-        seq_rows(g, i, &r0, &r1);
-        base += (r1 - r0 + C - 1) / C;
-    }
-    seq_rows(g, seq, &r0, &r1);
-    /* Overlapping sequences (cu not increasing) could number more chunks than phase 1 had slots for:
-     * those chunks are not read. */
+    /* This sequence's rows and first chunk slot. Chunks past max_slots (only overlapping sequences
+     * number that many) are not read. */
+    const int n = (int)g.n_seq;
+    const int64_t r0 = p.tab[seq], r1 = p.tab[n + seq], base = p.tab[2 * n + seq];
     const int64_t chunks = max((int64_t)0, min((r1 - r0 + C - 1) / C, (int64_t)p.max_slots - base));
     auto chunk_len = [&](int64_t c) { return (int)min((int64_t)C, r1 - r0 - c * C); };
 
@@ -419,7 +507,6 @@ gdn_chain_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
         }
         s.abort = 0;
         rf::mbar_init_fence();
-        rf::tma_prefetch_map(&kmap);
         rf::tma_prefetch_map(&vmap);
     }
     __syncthreads();
@@ -430,11 +517,11 @@ gdn_chain_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
         int64_t issued = 0, landed = 0;
         if (pt == 0)
             for (; issued < 2 && issued < chunks; ++issued)
-                chain_issue(p, &kmap, &vmap, s, base + issued, r0 + issued * C, h, hk, v0, (int)issued, (int)issued);
+                chain_issue(p, &vmap, s, base + issued, r0 + issued * C, h, v0, (int)issued, (int)issued);
         for (int64_t c = 0; c < chunks; ++c) {
             const int b = (int)(c & 1);
             const int len = chunk_len(c);
-            if (pt == 0) {   /* chunk c's inputs have landed, and chunk c-2 is consumed (its K~, U~ buffers are free) */
+            if (pt == 0) {   /* chunk c's inputs have landed, and chunk c-2 is consumed (its U~ buffer is free) */
                 s.ok_producers = rf::mbar_wait(&s.landed[b], (uint32_t)((c >> 1) & 1), &s.abort, rf::kErrGdnWait) &&
                                  (c < 2 || rf::mbar_wait(&s.consumed[b], (uint32_t)(((c - 2) >> 1) & 1), &s.abort, rf::kErrGdnWait));
                 s.gl[b] = __expf(s.raw[b].meta[len - 1]);
@@ -443,20 +530,7 @@ gdn_chain_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
             if (!s.ok_producers) break;
             landed = c + 1;
             RawStage& st = s.raw[b];
-            const float* G = st.meta;
             const float* beta = st.meta + C;
-            const float gl = G[len - 1];
-            for (int i = pt; i < C * (D / 8); i += 128) {   /* K~ = k * exp(G_L - G); rows past the chunk 0 */
-                const int r = i >> 4, seg = i & 15;
-                const uint4 raw = *(const uint4*)&st.kraw[r][seg * 8];
-                const uint32_t rw[4] = { raw.x, raw.y, raw.z, raw.w };
-                const float f = r < len ? __expf(gl - G[r]) : 0.0f;
-                uint32_t kk[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    kk[e] = r < len ? rf::pack_f16(f * __uint_as_float(rw[e] << 16), f * __uint_as_float(rw[e] & 0xffff0000u)) : 0u;
-                *(uint4*)&s.kt16[b][r][seg * 8] = make_uint4(kk[0], kk[1], kk[2], kk[3]);
-            }
             for (int i = pt; i < C * (VS / 8); i += 128) {  /* x2 = beta v; rows past the chunk 0 */
                 const int r = i >> 2, seg = i & 3;
                 const uint4 raw = *(const uint4*)&st.vraw[r][seg * 8];
@@ -489,13 +563,13 @@ gdn_chain_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
                     }
                 }
             }
-            rf::mbar_arrive(&s.ready[b]);   /* chunk c's K~, U~, gamma_L and W (landed above) are the chain's */
-            if (pt == 0)   /* chunk c-1 is consumed: W stage (c+2) % 3 is free */
+            rf::mbar_arrive(&s.ready[b]);   /* chunk c's U~, gamma_L and W|K~ (landed above) are the chain's */
+            if (pt == 0)   /* chunk c-1 is consumed: W|K~ stage (c+2) % 3 is free */
                 s.ok_producers = c < 1 || rf::mbar_wait(&s.consumed[b ^ 1], (uint32_t)(((c - 1) >> 1) & 1), &s.abort, rf::kErrGdnWait);
             bar_sync(kBarProducers, 128);   /* also: every producer is done with raw stage b and x2 */
             if (!s.ok_producers) break;
             if (pt == 0 && c + 2 < chunks) {
-                chain_issue(p, &kmap, &vmap, s, base + c + 2, r0 + (c + 2) * C, h, hk, v0, b, (int)((c + 2) % 3));
+                chain_issue(p, &vmap, s, base + c + 2, r0 + (c + 2) * C, h, v0, b, (int)((c + 2) % 3));
                 ++issued;
             }
         }
@@ -530,7 +604,7 @@ gdn_chain_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
         if (tid == 0) s.ok_chain = rf::mbar_wait(&s.ready[b], (uint32_t)((c >> 1) & 1), &s.abort, rf::kErrGdnWait);
         bar_sync(kBarChain, 128);
         if (!(ok = s.ok_chain)) break;
-        const uint16_t* W = &s.w16[c % 3][0][0];
+        const WKStage& wk = s.wk[c % 3];
 
         /* V'^T partial over this warp's dk half: [16 dv rows] x [64 chunk rows]. */
         float pv[8][4] = {};
@@ -541,7 +615,7 @@ gdn_chain_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
 #pragma unroll
             for (int pr = 0; pr < 4; ++pr) {
                 uint32_t bb[4];
-                rf::load_b_nk(bb, W, KP, 16 * pr, 64 * kh + 16 * ks);
+                rf::load_b_nk(bb, &wk.w16[0][0], KP, 16 * pr, 64 * kh + 16 * ks);
                 rf::mma_f16(pv[2 * pr], a, bb[0], bb[1]);
                 rf::mma_f16(pv[2 * pr + 1], a, bb[2], bb[3]);
             }
@@ -557,8 +631,8 @@ gdn_chain_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
         for (int j = 0; j < 8; ++j)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const int m = gq + (e >> 1) * 8, n = 8 * j + 2 * tq + (e & 1);
-                pv[j][e] = s.u32[b][n][16 * vh + m] - (pv[j][e] + s.part[b][w ^ 2][m][n]);
+                const int m = gq + (e >> 1) * 8, nn = 8 * j + 2 * tq + (e & 1);
+                pv[j][e] = s.u32[b][nn][16 * vh + m] - (pv[j][e] + s.part[b][w ^ 2][m][nn]);
             }
 
         /* S <- gamma_L S + V'^T K~ over this warp's dk half. */
@@ -566,7 +640,6 @@ gdn_chain_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
         for (int j = 0; j < 8; ++j)
 #pragma unroll
             for (int e = 0; e < 4; ++e) S[j][e] *= gamma_l;
-        const uint16_t* Kt = &s.kt16[b][0][0];
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
             uint32_t a[4];
@@ -574,7 +647,7 @@ gdn_chain_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant
 #pragma unroll
             for (int pr = 0; pr < 4; ++pr) {
                 uint32_t bb[4];
-                rf::load_b_kn(bb, Kt, KP, 16 * ks, 64 * kh + 16 * pr);
+                rf::load_b_kn(bb, &wk.kt16[0][0], KP, 16 * ks, 64 * kh + 16 * pr);
                 rf::mma_f16(S[2 * pr], a, bb[0], bb[1]);
                 rf::mma_f16(S[2 * pr + 1], a, bb[2], bb[3]);
             }
@@ -613,7 +686,7 @@ bool head_rows_map(CUtensorMap* map, const void* base, int64_t T, int64_t heads,
 extern "C" int64_t ridgefill_gdn_fill_scratch(const RadArgs* a) {
     RidgeFillGdn g;
     if (ridgefill_gdn_parse(a, &g) != RAD_OK) return 0;
-    return max_slots_of(g) * g.n_head_v * (int64_t)kSlotBytes;
+    return table_bytes(g.n_seq) + max_slots_of(g) * g.n_head_v * (int64_t)kSlotBytes;
 }
 
 extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
@@ -624,7 +697,7 @@ extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
     if (g.n_seq == 0 || g.T == 0) return RAD_OK;
     if (g.n_seq > 65535 || g.n_head_v > 65535 || g.T > 0x7fffffffLL) return RAD_E_SHAPE;
     const int64_t slots = max_slots_of(g);
-    const int64_t need = slots * g.n_head_v * (int64_t)kSlotBytes;
+    const int64_t need = table_bytes(g.n_seq) + slots * g.n_head_v * (int64_t)kSlotBytes;
     if (!a->scratch || a->scratch_bytes < need || (uintptr_t)a->scratch % 16) return RAD_E_INVAL;
     if (slots > 0x7fffffffLL) return RAD_E_SHAPE;
     /* k and v are read through TMA tensor maps: positive strides below 2^39 elements. */
@@ -632,25 +705,29 @@ extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
     if (g.k_row <= 0 || g.k_head <= 0 || g.v_row <= 0 || g.v_head <= 0 || g.k_row >= lim || g.k_head >= lim ||
         g.v_row >= lim || g.v_head >= lim)
         return RAD_E_STRIDE;
-    CUtensorMap kmap_sw, kmap, vmap;
-    if (!head_rows_map(&kmap_sw, g.k, g.T, g.n_head_k, g.k_row, g.k_head, C, true) ||
-        !head_rows_map(&kmap, g.k, g.T, g.n_head_k, g.k_row, g.k_head, D, false) ||
+    CUtensorMap kmap, vmap;
+    if (!head_rows_map(&kmap, g.k, g.T, g.n_head_k, g.k_row, g.k_head, C, true) ||
         !head_rows_map(&vmap, g.v, g.T, g.n_head_v, g.v_row, g.v_head, VS, false))
         return RAD_E_DEVICE;
     GdnPlan p;
     p.g = g;
-    p.scratch = (uint8_t*)a->scratch;
+    p.tab = (int32_t*)a->scratch;
+    p.slots = (uint8_t*)a->scratch + table_bytes(g.n_seq);
     p.max_slots = (int)slots;
     cudaStream_t stream = rf::as_stream(s);
     const int smem1 = (int)sizeof(PrepSmem) + 1024, smem2 = (int)sizeof(ChainSmem) + 128;
     if (cudaFuncSetAttribute(gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1) != cudaSuccess ||
         cudaFuncSetAttribute(gdn_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2) != cudaSuccess)
         return RAD_E_DEVICE;
+    gdn_plan_kernel<<<1, kPlanThreads, 0, stream>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return RAD_E_DEVICE;
+    /* Phase 1 sizes its grid by the rows alone (the chunk count is on the device); CTAs past the
+     * chunk count find no item. */
     const int64_t items = slots * g.n_head_v;
     const int64_t grid1 = items < 2LL * rf::sm_count() ? items : 2LL * rf::sm_count();
-    gdn_prep_kernel<<<(unsigned)grid1, kPrepThreads, smem1, stream>>>(kmap_sw, p);
+    gdn_prep_kernel<<<(unsigned)grid1, kPrepThreads, smem1, stream>>>(kmap, p);
     if (cudaGetLastError() != cudaSuccess) return RAD_E_DEVICE;
-    gdn_chain_kernel<<<dim3(D / VS, (unsigned)g.n_head_v, (unsigned)g.n_seq), kChainThreads, smem2, stream>>>(kmap, vmap, p);
+    gdn_chain_kernel<<<dim3(D / VS, (unsigned)g.n_head_v, (unsigned)g.n_seq), kChainThreads, smem2, stream>>>(vmap, p);
     return rf::launch_status();
 }
 
@@ -668,10 +745,10 @@ int gdn_device_error(int reset) { return read_device_error(reset); }
  * starts, where a cudaMalloc inside the pass is not allowed (it can synchronise the device and stall
  * every stream of the step). This entry point takes the same operands as the ridgefill_gdn_fill row,
  * ignores RadArgs::scratch, and uses instead a workspace compiled into the library: a file-scope device
- * array of kNoAllocScratchBytes (48 MiB), which every GPU that loads the library holds until the
- * process exits. 48 MiB holds the fill's workspace (26.5 KiB per 64-row chunk and value head, one chunk
- * more per sequence) for a one-sequence 2,048-row call -- the engine's default chunk -- at up to 56 value
- * heads, or a 4,096-row call at up to 28; a call that needs more returns RAD_E_SHAPE and launches nothing.
+ * array of kNoAllocScratchBytes (64 MiB), which every GPU that loads the library holds until the
+ * process exits. 64 MiB holds the fill's workspace (43.5 KiB per 64-row chunk and value head, one chunk
+ * more per sequence) for a one-sequence 2,048-row call -- the engine's default chunk -- at up to 45 value
+ * heads, or a 4,096-row call at up to 23; a call that needs more returns RAD_E_SHAPE and launches nothing.
  *
  * The first call on each device resolves the array's device address there (cudaGetSymbolAddress, once
  * per device, with that device current); make that first call before any stream capture. No call
@@ -681,7 +758,7 @@ int gdn_device_error(int reset) { return read_device_error(reset); }
  * or from different threads, without an ordering between them -- race on it.
  */
 namespace {
-constexpr int64_t kNoAllocScratchBytes = 48ll << 20;
+constexpr int64_t kNoAllocScratchBytes = 64ll << 20;
 constexpr int kNoAllocMaxDevices = 64;
 }   // namespace
 

@@ -1,6 +1,6 @@
 """ridgefill_gdn_fill_noalloc -- the DeltaNet fill for callers that cannot allocate device memory where
 they launch it (an FFI host without a device allocator, an engine step whose memory is fixed before the
-pass). It takes the row's operands without a workspace and uses the 48 MiB workspace compiled into the
+pass). It takes the row's operands without a workspace and uses the 64 MiB workspace compiled into the
 library. Called here through the C ABI, twice in a row with different inputs (the shared workspace keeps
 the first call's contents), each result checked against the ridgefill_gdn_fill row given an allocated
 workspace, within the state tolerance the fill's tests use. This file is collected last on purpose."""
@@ -56,10 +56,10 @@ def test_noalloc_fill_matches_the_row_on_two_calls_in_a_row(cuda, product_lib):
 
 
 def test_noalloc_refuses_past_its_workspace(cuda, product_lib):
-    """A call whose workspace would exceed 48 MiB is refused with RAD_E_SHAPE before any launch (its
+    """A call whose workspace would exceed 64 MiB is refused with RAD_E_SHAPE before any launch (its
     state is left alone)."""
     torch = cuda
-    T, hk, hv = 8192, 16, 32          # 129 chunk slots x 32 heads x 27,136 B = 112.0 MB > 48 MiB
+    T, hk, hv = 8192, 16, 32          # 129 chunk slots x 32 heads x 44,544 B = 183.9 MB > 64 MiB
     t, state = _operands(torch, 7, T, hk, hv)
     S = torch.from_numpy(state.copy()).cuda()
     assert _noalloc(product_lib, _tensors(t, S), H.gdn_params(T, hk, hv), torch) == abi.E_SHAPE
