@@ -221,6 +221,15 @@ def run_mine(args):
                   "ridgefill_select": alg["select_bytes"]}.get(dominant, 0)
             roof = {"bound": "hbm", "achieved": by / (dom_ms * 1e-3) / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
                     "traffic": None, "note": f"peak {pk['source']}"}
+            if dominant == "ridgefill_gdn_fill":
+                # DRAM bytes of one fill from an ncu capture at 16,384 rows (plan + prep + chain kernels:
+                # 0.007 + 389.6 + 507.4 MB), scaled by rows: every term (k, v, g, beta reads, the chunk slots
+                # written and read back) grows in proportion to the rows.
+                roof["traffic"] = 897.0e6 * T_FULL / 16384
+                roof["traffic_note"] = "ncu dram__bytes_read+write at 16,384 rows, scaled by rows"
+                roof["tensor"] = {"achieved": alg["gdn_chunk_flops"] / (dom_ms * 1e-3) / 1e12, "peak": pk["bf16_tflops"],
+                                  "unit": "TFLOP/s"}
+                roof["tensor"]["frac"] = roof["tensor"]["achieved"] / roof["tensor"]["peak"]
         roof["frac"] = roof["achieved"] / roof["peak"]
         roof["kernel"] = dominant
         roof["kernel_ms"] = dom_ms

@@ -172,5 +172,8 @@ class Step:
             "gdn_bytes": 2 * T * hk * D + 2 * T * hv * D + 8 * T * hv + 2 * 4 * hv * D * D,
             # the gated delta rule's state-only arithmetic per (row, v-head): decay, S k, the rank-1 update
             "gdn_flops": T * hv * (4 * D * D),
+            # the chunked form's state-only arithmetic per (64-row chunk, v-head): K K^T, W, U~ (2 C^2 d each),
+            # V' and the state update (2 C d^2 each), the triangular solve (C^3 / 1.5)
+            "gdn_chunk_flops": (T // 64) * hv * (6 * 64 * 64 * D + 4 * 64 * D * D + 64 ** 3 * 2 // 3),
             "select_bytes": 4 * T + 2 * 2 * d * int(T * (1 - s.share)),
         }
