@@ -38,4 +38,9 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
     return (uint16_t)(u >> 16);
 }
 
+/* Two f32 values as a pair of bf16 (lo in the low half), each rounded as f32_to_bf16_bits. */
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+    return (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
+}
+
 }  // namespace rf

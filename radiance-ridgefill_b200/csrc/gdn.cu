@@ -66,12 +66,23 @@ enum { kBarProducers = 1, kBarChain = 2, kBarPair0 = 3 };   /* named barriers (0
  * chunk slots. base[i] is the number of chunks before sequence i, capped at max_slots. */
 int64_t table_bytes(int64_t n_seq) { return (3 * n_seq + 1) * 4 + 255 & ~(int64_t)255; }
 
+/* Output form only: per (chunk slot, v-head), the state at the chunk's start S0 f16 [dv][SP] and the
+ * corrected values U^T f16 [dv][TP] (rows of the chunk along the pitch), written by phase 2 for the
+ * output kernel. */
+constexpr int SP = D + 8;
+constexpr int kOutS0 = 0, kOutU = D * SP * 2, kOutBytes = kOutU + D * TP * 2;
+
 struct GdnPlan {
     RidgeFillGdn g;
     int32_t* tab;     /* the sequence table */
     uint8_t* slots;   /* the chunk slots */
+    uint8_t* outws;   /* output form: S0 and U^T per chunk slot and v-head; null for the state-only fill */
     int max_slots;
 };
+
+__device__ __forceinline__ uint8_t* out_ptr(const GdnPlan& p, int64_t slot, int64_t h) {
+    return p.outws + (slot * p.g.n_head_v + h) * (int64_t)kOutBytes;
+}
 
 __device__ __forceinline__ uint8_t* slot_ptr(const GdnPlan& p, int64_t slot, int64_t h) {
     return p.slots + (slot * p.g.n_head_v + h) * (int64_t)kSlotBytes;
@@ -160,27 +171,30 @@ static_assert(offsetof(PrepSmem, G) == offsetof(PrepSmem, t16) + sizeof(uint16_t
 static_assert(offsetof(PrepSmem, beta) == offsetof(PrepSmem, G) + sizeof(float) * C, "T|G|beta contiguous");
 static_assert(offsetof(PrepSmem, w16) % 16 == 0 && offsetof(PrepSmem, t16) % 16 == 0, "bulk-store sources");
 
-/* Chunk `slot` (< the table's base[n]): its first row and length. The largest i with base[i] <= slot,
- * searched in the cached rows of the table when the slot lies there, else in the table. */
-__device__ void locate_chunk(const GdnPlan& p, const PrepSmem& s, int64_t slot, int64_t* row0, int* len) {
+/* Chunk `slot` (< the table's base[n]): its first row, length and sequence (when `seq` is given). The
+ * sequence is the largest i with base[i] <= slot,
+ * searched in the first n_cached rows of the table (r0c, basec: shared-memory copies) when the slot lies
+ * there, else in the table. */
+__device__ void locate_chunk(const GdnPlan& p, const int32_t* r0c, const int32_t* basec, int n_cached, int64_t slot,
+                             int64_t* row0, int* len, int* seq = nullptr) {
     const int n = (int)p.g.n_seq;
     const int32_t* r0t = p.tab;
     const int32_t* r1t = p.tab + n;
     const int32_t* bt = p.tab + 2 * n;
     int lo, hi, i;
-    if (slot < s.base[s.n_cached]) {
+    if (slot < basec[n_cached]) {
         lo = 0;
-        hi = s.n_cached - 1;
+        hi = n_cached - 1;
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;
-            if (s.base[mid] <= slot) lo = mid;
+            if (basec[mid] <= slot) lo = mid;
             else hi = mid - 1;
         }
         i = lo;
-        const int64_t c = slot - s.base[i];
-        *row0 = s.r0[i] + c * C;
+        const int64_t c = slot - basec[i];
+        *row0 = r0c[i] + c * C;
     } else {
-        lo = s.n_cached;
+        lo = n_cached;
         hi = n - 1;
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;
@@ -191,6 +205,7 @@ __device__ void locate_chunk(const GdnPlan& p, const PrepSmem& s, int64_t slot, 
         *row0 = r0t[i] + (slot - bt[i]) * C;
     }
     *len = (int)min((int64_t)C, (int64_t)r1t[i] - *row0);
+    if (seq) *seq = i;
 }
 
 /* T[bi][bj] = -T[bi][bi] * sum_{k=bj}^{bi-1} L[bi][k] T[k][bj] for one 16x16 block, one warp. */
@@ -230,7 +245,7 @@ __device__ void prep_issue(const GdnPlan& p, const CUtensorMap* kmap, PrepSmem& 
     const int64_t slot = item / g.n_head_v, h = item % g.n_head_v, hk = h / (g.n_head_v / g.n_head_k);
     int64_t row0 = 0;
     int len = 0;
-    locate_chunk(p, s, slot, &row0, &len);
+    locate_chunk(p, s.r0, s.base, s.n_cached, slot, &row0, &len);
     if (threadIdx.x == 0) {
         rf::mbar_arrive_expect_tx(&s.landed[buf], kKBoxBytes);
         rf::tma_load_3d(&s.kraw[buf][0][0][0], kmap, &s.landed[buf], 0, (int)hk, (int)row0);
@@ -287,7 +302,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_kernel(const __grid_
         const int64_t slot = item / g.n_head_v, h = item % g.n_head_v;
         int64_t row0 = 0;
         int len = 0;
-        locate_chunk(p, s, slot, &row0, &len);
+        locate_chunk(p, s.r0, s.base, s.n_cached, slot, &row0, &len);
         uint8_t* out = slot_ptr(p, slot, h);
         const uint32_t ktile = rf::saddr(&s.kraw[buf][0][0][0]);
 
@@ -605,6 +620,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const __gri
         bar_sync(kBarChain, 128);
         if (!(ok = s.ok_chain)) break;
         const WKStage& wk = s.wk[c % 3];
+        uint8_t* ow = p.outws ? out_ptr(p, base + c, h) : nullptr;
 
         /* V'^T partial over this warp's dk half: [16 dv rows] x [64 chunk rows]. */
         float pv[8][4] = {};
@@ -612,6 +628,14 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const __gri
         for (int ks = 0; ks < 4; ++ks) {
             uint32_t a[4];
             rf::c_to_a(a, S[2 * ks], S[2 * ks + 1]);
+            if (ow) {   /* output form: S0 in f16, this warp's quarter */
+                uint16_t* s0 = (uint16_t*)(ow + kOutS0);
+                const int vr = v0 + 16 * vh + gq, kc = 64 * kh + 16 * ks + 2 * tq;
+                *(uint32_t*)&s0[vr * SP + kc] = a[0];
+                *(uint32_t*)&s0[(vr + 8) * SP + kc] = a[1];
+                *(uint32_t*)&s0[vr * SP + kc + 8] = a[2];
+                *(uint32_t*)&s0[(vr + 8) * SP + kc + 8] = a[3];
+            }
 #pragma unroll
             for (int pr = 0; pr < 4; ++pr) {
                 uint32_t bb[4];
@@ -644,6 +668,14 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const __gri
         for (int ks = 0; ks < 4; ++ks) {
             uint32_t a[4];
             rf::c_to_a(a, pv[2 * ks], pv[2 * ks + 1]);
+            if (ow && (ks >> 1) == kh) {   /* output form: U^T in f16 (the two dk halves hold the same V') */
+                uint16_t* ut = (uint16_t*)(ow + kOutU);
+                const int vr = v0 + 16 * vh + gq, rc = 16 * ks + 2 * tq;
+                *(uint32_t*)&ut[vr * TP + rc] = a[0];
+                *(uint32_t*)&ut[(vr + 8) * TP + rc] = a[1];
+                *(uint32_t*)&ut[vr * TP + rc + 8] = a[2];
+                *(uint32_t*)&ut[(vr + 8) * TP + rc + 8] = a[3];
+            }
 #pragma unroll
             for (int pr = 0; pr < 4; ++pr) {
                 uint32_t bb[4];
@@ -661,6 +693,174 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const __gri
         for (int hr = 0; hr < 2; ++hr) {
             const int v = v0 + 16 * vh + gq + 8 * hr, k = 64 * kh + 8 * j + 2 * tq;
             *(float2*)(st + (int64_t)v * D + k) = make_float2(S[j][2 * hr], S[j][2 * hr + 1]);
+        }
+}
+
+/* ------------------------------------------------------------------ output (o present) */
+
+/* o_i = scale * S_i q_i over a chunk, from its start state S0 and corrected values U:
+ *     S_i = Gamma_i S0 + sum_{j <= i} exp(G_i - G_j) U_j k_j^T,   Gamma_i = exp(G_i)
+ * so  O = scale * (diag(Gamma) Q S0^T + ((Q K^T) .* Dm) U),   Dm_ij = exp(G_i - G_j) for j <= i, else 0.
+ * Every (chunk, v-head) in parallel, persistent CTAs: q and k rows by TMA (128-byte swizzled), S0, U^T
+ * and G from the scratch by bulk copy; Q K^T on bf16 tensor cores, then q in f16 for the f16 products. */
+constexpr int kOutThreads = 256;
+
+struct OutSmem {
+    uint16_t qraw[2][C][C];      /* q rows: two 128-byte-swizzled halves (then f16 in place) */
+    uint16_t kraw[2][C][C];      /* k rows */
+    uint16_t s0[D][SP];          /* S0, f16 */
+    uint16_t ut[D][TP];          /* U^T, f16 */
+    float meta[2 * C];           /* G, beta of the chunk */
+    uint16_t pm[C][TP];          /* (Q K^T) .* Dm, f16 */
+    int32_t r0[kSeqCache], base[kSeqCache + 1];
+    uint64_t landed;
+    int abort, ok, n_cached;
+};
+static_assert(offsetof(OutSmem, s0) % 16 == 0 && offsetof(OutSmem, ut) % 16 == 0 && offsetof(OutSmem, meta) % 16 == 0,
+              "bulk destinations");
+
+__global__ void __launch_bounds__(kOutThreads, 2)
+gdn_out_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap, const GdnPlan p) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    OutSmem& s = *(OutSmem*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const RidgeFillGdn& g = p.g;
+    const int tid = threadIdx.x, w = tid >> 5, l = tid & 31, gq = l >> 2, tq = l & 3;
+    const int n_seq = (int)g.n_seq;
+    const int n_cached = n_seq < kSeqCache ? n_seq : kSeqCache;
+    for (int i = tid; i <= n_cached; i += kOutThreads) {
+        if (i < n_cached) s.r0[i] = p.tab[i];
+        s.base[i] = p.tab[2 * n_seq + i];
+    }
+    if (tid == 0) {
+        rf::mbar_init(&s.landed, 1);
+        s.abort = 0;
+        s.n_cached = n_cached;
+        rf::mbar_init_fence();
+        rf::tma_prefetch_map(&qmap);
+        rf::tma_prefetch_map(&kmap);
+    }
+    __syncthreads();
+    const int64_t items = (int64_t)p.tab[3 * n_seq] * g.n_head_v;
+    const uint32_t qtile = rf::saddr(&s.qraw[0][0][0]), ktile = rf::saddr(&s.kraw[0][0][0]);
+    int64_t waited = 0, issued = 0;
+    for (int64_t item = blockIdx.x; item < items; item += gridDim.x) {
+        const int64_t slot = item / g.n_head_v, h = item % g.n_head_v, hk = h / (g.n_head_v / g.n_head_k);
+        int64_t row0 = 0;
+        int len = 0, sq = 0;
+        locate_chunk(p, s.r0, s.base, s.n_cached, slot, &row0, &len, &sq);
+        const int64_t state_slot = g.state_idx[(int64_t)sq * g.idx_pitch];
+        if (state_slot < 0 || state_slot >= g.n_states) continue;   /* a skipped sequence: its o rows are left as they are */
+        if (tid == 0) {
+            const uint8_t* ow = out_ptr(p, slot, h);
+            rf::mbar_arrive_expect_tx(&s.landed, 2 * kKBoxBytes + (uint32_t)(sizeof(s.s0) + sizeof(s.ut) + sizeof(s.meta)));
+            rf::tma_load_3d(&s.qraw[0][0][0], &qmap, &s.landed, 0, (int)hk, (int)row0);
+            rf::tma_load_3d(&s.qraw[1][0][0], &qmap, &s.landed, C, (int)hk, (int)row0);
+            rf::tma_load_3d(&s.kraw[0][0][0], &kmap, &s.landed, 0, (int)hk, (int)row0);
+            rf::tma_load_3d(&s.kraw[1][0][0], &kmap, &s.landed, C, (int)hk, (int)row0);
+            rf::bulk_load(&s.s0[0][0], ow + kOutS0, sizeof(s.s0), &s.landed);
+            rf::bulk_load(&s.ut[0][0], ow + kOutU, sizeof(s.ut), &s.landed);
+            rf::bulk_load(&s.meta[0], slot_ptr(p, slot, h) + kSlotMeta, sizeof(s.meta), &s.landed);
+            ++issued;
+            s.ok = rf::mbar_wait(&s.landed, (uint32_t)(waited & 1), &s.abort, rf::kErrGdnWait);
+        }
+        __syncthreads();
+        if (!s.ok) break;
+        ++waited;
+        const float* G = s.meta;
+
+        {   /* (Q K^T) .* Dm (warp w: rows 16 (w & 3), columns 32 (w >> 2)..+32), f16 */
+            const int rb = 16 * (w & 3), cb = 32 * (w >> 2);
+            float acc[4][4] = {};
+#pragma unroll
+            for (int ks = 0; ks < D / 16; ++ks) {
+                uint32_t a[4];
+                rf::load_a_sw(a, qtile, rb, 16 * ks);
+#pragma unroll
+                for (int pr = 0; pr < 2; ++pr) {
+                    uint32_t b[4];
+                    rf::load_b_nk_sw(b, ktile, cb + 16 * pr, 16 * ks);
+                    rf::mma_bf16(acc[2 * pr], a, b[0], b[1]);
+                    rf::mma_bf16(acc[2 * pr + 1], a, b[2], b[3]);
+                }
+            }
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr) {
+                    const int i = rb + gq + 8 * hr, j = cb + 8 * nt + 2 * tq;
+                    const float v0 = (j <= i && i < len) ? __expf(G[i] - G[j]) * acc[nt][2 * hr] : 0.0f;
+                    const float v1 = (j + 1 <= i && i < len) ? __expf(G[i] - G[j + 1]) * acc[nt][2 * hr + 1] : 0.0f;
+                    *(uint32_t*)&s.pm[i][j] = rf::pack_f16(v0, v1);
+                }
+        }
+        __syncthreads();
+        /* q to f16 in place (16-byte chunks keep their swizzled places) */
+        for (int i = tid; i < C * (D / 8); i += kOutThreads) {
+            const int r = i >> 4, seg = i & 15;
+            const uint32_t a = rf::sw128_addr(qtile, r, seg * 8);
+            uint4 raw;
+            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(raw.x), "=r"(raw.y), "=r"(raw.z), "=r"(raw.w) : "r"(a));
+            const uint32_t rw[4] = { raw.x, raw.y, raw.z, raw.w };
+            uint32_t hh[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) hh[e] = rf::pack_f16(__uint_as_float(rw[e] << 16), __uint_as_float(rw[e] & 0xffff0000u));
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(hh[0]), "r"(hh[1]), "r"(hh[2]), "r"(hh[3]) : "memory");
+        }
+        __syncthreads();
+        {   /* O = scale * (diag(Gamma) Q S0^T + Pm U) (warp w: rows 16 (w & 3), dv columns 64 (w >> 2)..+64) */
+            const int rb = 16 * (w & 3), cb = 64 * (w >> 2);
+            float acc[8][4] = {};
+#pragma unroll
+            for (int ks = 0; ks < D / 16; ++ks) {
+                uint32_t a[4];
+                rf::load_a_sw(a, qtile, rb, 16 * ks);
+#pragma unroll
+                for (int pr = 0; pr < 4; ++pr) {
+                    uint32_t b[4];
+                    rf::load_b_nk(b, &s.s0[0][0], SP, cb + 16 * pr, 16 * ks);
+                    rf::mma_f16(acc[2 * pr], a, b[0], b[1]);
+                    rf::mma_f16(acc[2 * pr + 1], a, b[2], b[3]);
+                }
+            }
+            const float ga = __expf(G[rb + gq]), gb = __expf(G[rb + gq + 8]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                acc[j][0] *= ga;
+                acc[j][1] *= ga;
+                acc[j][2] *= gb;
+                acc[j][3] *= gb;
+            }
+#pragma unroll
+            for (int ks = 0; ks < C / 16; ++ks) {
+                uint32_t a[4];
+                rf::load_a(a, &s.pm[0][0], TP, rb, 16 * ks);
+#pragma unroll
+                for (int pr = 0; pr < 4; ++pr) {
+                    uint32_t b[4];
+                    rf::load_b_nk(b, &s.ut[0][0], TP, cb + 16 * pr, 16 * ks);
+                    rf::mma_f16(acc[2 * pr], a, b[0], b[1]);
+                    rf::mma_f16(acc[2 * pr + 1], a, b[2], b[3]);
+                }
+            }
+#pragma unroll
+            for (int hr = 0; hr < 2; ++hr) {
+                const int i = rb + gq + 8 * hr;
+                if (i >= len) continue;
+                uint16_t* orow = g.o + (row0 + i) * g.o_row + h * g.o_head + cb + 2 * tq;
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    *(uint32_t*)(orow + 8 * j) = rf::pack_bf16(g.scale * acc[j][2 * hr], g.scale * acc[j][2 * hr + 1]);
+            }
+        }
+        __syncthreads();   /* every read of this item's shared memory precedes the next item's loads */
+    }
+    /* After a timed-out wait: let the copies already issued land before the CTA's shared memory is
+     * released (bounded too). */
+    if (tid == 0)
+        for (int64_t i = waited; i < issued; ++i) {
+            const uint64_t t0 = rf::global_ns();
+            while (!rf::mbar_try_wait(&s.landed, (uint32_t)(i & 1)) && rf::global_ns() - t0 < rf::kWaitTimeoutNs) {
+            }
         }
 }
 
@@ -686,38 +886,42 @@ bool head_rows_map(CUtensorMap* map, const void* base, int64_t T, int64_t heads,
 extern "C" int64_t ridgefill_gdn_fill_scratch(const RadArgs* a) {
     RidgeFillGdn g;
     if (ridgefill_gdn_parse(a, &g) != RAD_OK) return 0;
-    return table_bytes(g.n_seq) + max_slots_of(g) * g.n_head_v * (int64_t)kSlotBytes;
+    const int64_t per_slot = kSlotBytes + (g.o ? kOutBytes : 0);
+    return table_bytes(g.n_seq) + max_slots_of(g) * g.n_head_v * per_slot;
 }
 
 extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
     RidgeFillGdn g;
     const int rc = ridgefill_gdn_parse(a, &g);
     if (rc != RAD_OK) return rc;
-    if (g.o) return RAD_E_UNSUPPORTED;   /* the output form (o) is not served by this row yet */
     if (g.n_seq == 0 || g.T == 0) return RAD_OK;
     if (g.n_seq > 65535 || g.n_head_v > 65535 || g.T > 0x7fffffffLL) return RAD_E_SHAPE;
     const int64_t slots = max_slots_of(g);
-    const int64_t need = table_bytes(g.n_seq) + slots * g.n_head_v * (int64_t)kSlotBytes;
+    const int64_t slot_bytes = slots * g.n_head_v * (int64_t)kSlotBytes;
+    const int64_t need = table_bytes(g.n_seq) + slot_bytes + (g.o ? slots * g.n_head_v * (int64_t)kOutBytes : 0);
     if (!a->scratch || a->scratch_bytes < need || (uintptr_t)a->scratch % 16) return RAD_E_INVAL;
     if (slots > 0x7fffffffLL) return RAD_E_SHAPE;
     /* k and v are read through TMA tensor maps: positive strides below 2^39 elements. */
     const int64_t lim = 1LL << 39;
     if (g.k_row <= 0 || g.k_head <= 0 || g.v_row <= 0 || g.v_head <= 0 || g.k_row >= lim || g.k_head >= lim ||
-        g.v_row >= lim || g.v_head >= lim)
+        g.v_row >= lim || g.v_head >= lim || (g.q && (g.q_row <= 0 || g.q_head <= 0 || g.q_row >= lim || g.q_head >= lim)))
         return RAD_E_STRIDE;
-    CUtensorMap kmap, vmap;
+    CUtensorMap kmap, vmap, qmap;
     if (!head_rows_map(&kmap, g.k, g.T, g.n_head_k, g.k_row, g.k_head, C, true) ||
-        !head_rows_map(&vmap, g.v, g.T, g.n_head_v, g.v_row, g.v_head, VS, false))
+        !head_rows_map(&vmap, g.v, g.T, g.n_head_v, g.v_row, g.v_head, VS, false) ||
+        (g.q && !head_rows_map(&qmap, g.q, g.T, g.n_head_k, g.q_row, g.q_head, C, true)))
         return RAD_E_DEVICE;
     GdnPlan p;
     p.g = g;
     p.tab = (int32_t*)a->scratch;
     p.slots = (uint8_t*)a->scratch + table_bytes(g.n_seq);
+    p.outws = g.o ? p.slots + slot_bytes : nullptr;
     p.max_slots = (int)slots;
     cudaStream_t stream = rf::as_stream(s);
-    const int smem1 = (int)sizeof(PrepSmem) + 1024, smem2 = (int)sizeof(ChainSmem) + 128;
+    const int smem1 = (int)sizeof(PrepSmem) + 1024, smem2 = (int)sizeof(ChainSmem) + 128, smem3 = (int)sizeof(OutSmem) + 1024;
     if (cudaFuncSetAttribute(gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1) != cudaSuccess ||
-        cudaFuncSetAttribute(gdn_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2) != cudaSuccess)
+        cudaFuncSetAttribute(gdn_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2) != cudaSuccess ||
+        cudaFuncSetAttribute(gdn_out_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem3) != cudaSuccess)
         return RAD_E_DEVICE;
     gdn_plan_kernel<<<1, kPlanThreads, 0, stream>>>(p);
     if (cudaGetLastError() != cudaSuccess) return RAD_E_DEVICE;
@@ -728,6 +932,9 @@ extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
     gdn_prep_kernel<<<(unsigned)grid1, kPrepThreads, smem1, stream>>>(kmap, p);
     if (cudaGetLastError() != cudaSuccess) return RAD_E_DEVICE;
     gdn_chain_kernel<<<dim3(D / VS, (unsigned)g.n_head_v, (unsigned)g.n_seq), kChainThreads, smem2, stream>>>(vmap, p);
+    if (!g.o) return rf::launch_status();
+    if (cudaGetLastError() != cudaSuccess) return RAD_E_DEVICE;
+    gdn_out_kernel<<<(unsigned)grid1, kOutThreads, smem3, stream>>>(qmap, kmap, p);
     return rf::launch_status();
 }
 

@@ -11,6 +11,7 @@ from harness import abi
 
 pytestmark = pytest.mark.gpu
 STATE_TOL = 1e-3
+O_TOL = 1e-2   # o is bf16; relative L2 over every written row and head
 
 
 def run_fill(product_lib, torch, k, v, g, beta, state, idx, cu, hk, hv, q=None, o=False):
@@ -81,6 +82,36 @@ def test_fill_full_size_split_is_one_call(cuda, product_lib):
     assert np.array_equal(one.view(np.uint32), two.view(np.uint32))
     want, _ = H.oracle_gdn(k, v, g, beta, state, [0], [0, T], heads=(5, 7))
     assert H.rel_l2(one[0, 5:7], want[0, 5:7]) <= STATE_TOL
+
+
+@pytest.mark.parametrize("T,hk,hv,decay", [(64, 1, 1, "fast"), (130, 2, 4, "slow"), (777, 1, 2, "very slow"),
+                                           (2048, 16, 32, "fast")])
+def test_fill_output_matches_sequential_rule(cuda, product_lib, T, hk, hv, decay):
+    """The output form: o_t = scale * S_t q_t for every row (scale 1/sqrt(128)), and the same state."""
+    torch = cuda
+    q, k, v, g, beta, state = H.gdn_inputs(T + 3 * hv, T, hk, hv, decay)
+    rc, got, o = run_fill(product_lib, torch, k, v, g, beta, state, [1], [0, T], hk, hv, q=q, o=True)
+    assert rc == abi.OK
+    want, want_o = H.oracle_gdn(k, v, g, beta, state, [1], [0, T], q=q)
+    assert H.rel_l2(got[1], want[1]) <= STATE_TOL
+    err = H.rel_l2(H.bf16_bits_to_f32(o), H.bf16_bits_to_f32(want_o))
+    assert err <= O_TOL, err
+
+
+def test_fill_output_varlen_and_skipped(cuda, product_lib):
+    """Output form over three sequences (1, 100 and 300 rows), the second without a state slot: its o rows
+    are left as they were (zero here), the others match the rule."""
+    torch = cuda
+    q, k, v, g, beta, state = H.gdn_inputs(9, 401, 2, 4, "fast", slots=4)
+    cu, idx = [0, 1, 101, 401], [3, -1, 0]
+    rc, got, o = run_fill(product_lib, torch, k, v, g, beta, state, idx, cu, 2, 4, q=q, o=True)
+    assert rc == abi.OK
+    want, want_o = H.oracle_gdn(k, v, g, beta, state, idx, cu, q=q)
+    assert not o[1:101].any()
+    for r0, r1 in ((0, 1), (101, 401)):
+        assert H.rel_l2(H.bf16_bits_to_f32(o[r0:r1]), H.bf16_bits_to_f32(want_o[r0:r1])) <= O_TOL
+    for slot in (3, 0):
+        assert H.rel_l2(got[slot], want[slot]) <= STATE_TOL
 
 
 def test_fill_refusals(cuda, product_lib):
