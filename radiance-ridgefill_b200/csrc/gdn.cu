@@ -14,21 +14,20 @@
  *
  *   plan (gdn_plan_kernel), one CTA: each sequence's clamped rows and the number of chunks before it,
  *     into the head of the scratch, so neither phase walks cu_seqlens.
- *   phase 1 (gdn_prep_kernel), every (chunk, v-head) in parallel, persistent CTAs, the next item's k rows
- *     arriving by TMA (two 128-byte-swizzled boxes) while the current one is computed: K K^T on tensor
+ *   phase 1 (gdn_prep_kernel), every (chunk, v-head) in parallel, persistent CTAs, the next item's k and
+ *     v rows arriving by TMA (128-byte-swizzled boxes) while the current one is computed: K K^T on tensor
  *     cores (bf16, exact inputs), A, T by blocked inversion (16x16 diagonal blocks by column-parallel
- *     substitution in f32, off-diagonal blocks by f16 tensor-core products), W = T (beta gamma K) and
- *     K~. The chunk's scratch slot receives W, K~, T (f16), G and beta in phase 2's shared-memory layout
- *     (W and T|G|beta by bulk stores from shared memory, K~ straight from registers).
+ *     substitution in f32, off-diagonal blocks by f16 tensor-core products), then W = T (beta gamma K),
+ *     U~ = T (beta V) and K~, all f16. The chunk's scratch slot receives W, K~, U~^T (128-byte-swizzled
+ *     f16 tiles), G, beta and gamma_L: W and U~^T staged over the consumed input tiles and bulk-stored,
+ *     K~ straight from registers.
  *   phase 2 (gdn_chain_kernel), one CTA per (32-row slice of dv, head, sequence), sequential over the
- *     sequence's chunks, warp-specialised:
- *       4 producer warps prepare chunk c+1 while the chain runs chunk c: each chunk's inputs arrive in
- *       three copies two chunks ahead (W|K~ and T|G|beta by bulk copy, the slice's v columns by a TMA
- *       box); they form U~ = T (beta v) for the slice and gamma_L;
- *       4 chain warps (2 dv row halves x 2 dk halves) hold the state slice in registers and run
- *       V' = U~ - W S^T,  S <- gamma_L S + V'^T K~ on f16 mma.sync with f32 accumulation.
- *     The roles hand chunks over through mbarriers (bounded waits, taken by one thread a role and
- *     broadcast through the role's named barrier, so a role always leaves its loop as a whole).
+ *     sequence's chunks: one loader lane keeps four chunks in flight (W|K~, the slice of U~^T and gamma_L,
+ *     three bulk copies a chunk); 4 chain warps (2 dv row halves x 2 dk halves) hold the state slice in
+ *     registers and run V' = U~ - W S^T,  S <- gamma_L S + V'^T K~ on f16 mma.sync with f32
+ *     accumulation. Loader and chain hand stages over through mbarriers (bounded waits; the chain's wait
+ *     is taken by one thread and broadcast through a named barrier, so the chain leaves its loop as a
+ *     whole).
  * f16 operands with f32 accumulation keep the state within 4e-4 relative L2 of the f64 sequential
  * rule in the configurations this library is tested on (bf16 operands would not: ~3e-3).
  */
@@ -45,22 +44,19 @@ namespace {
 
 constexpr int C = 64;          /* rows a chunk */
 constexpr int D = 128;         /* head dims (dk = dv) */
-constexpr int KP = D + 8;      /* pitch of 128-wide b16 rows in shared memory (conflict-free ldmatrix) */
-constexpr int TP = C + 8;      /* pitch of 64-wide b16 rows */
+constexpr int TP = C + 8;      /* pitch of 64-wide b16 rows in shared memory (conflict-free ldmatrix) */
 constexpr int VS = 32;         /* dv rows per phase-2 CTA */
-constexpr int VP = VS + 8;     /* pitch of 32-wide b16 rows */
-constexpr int AP = C + 4;      /* pitch of the f32 A matrix */
-constexpr int UP = VS + 4;     /* pitch of the f32 U~ slice */
-constexpr int PP = C + 4;      /* pitch of the f32 exchange tiles */
+constexpr int PP = C + 8;      /* pitch of the f32 exchange tiles (float2 stores and loads without conflicts) */
+constexpr int kStages = 4;     /* phase 2: chunks in flight */
 
-/* A chunk's scratch slot, per (chunk, v-head), in phase 2's shared-memory layout: W f16 [64][KP],
- * K~ f16 [64][KP], T f16 [64][TP], G f32 [64], beta f32 [64]. */
-constexpr int kSlotW = 0, kSlotK = C * KP * 2, kSlotT = kSlotK + C * KP * 2, kSlotMeta = kSlotT + C * TP * 2;
-constexpr int kSlotBytes = kSlotMeta + 2 * C * 4;
-constexpr uint32_t kWKBytes = 2 * C * KP * 2, kTMBytes = C * TP * 2 + 2 * C * 4;
-constexpr uint32_t kKBoxBytes = C * D * 2, kVBoxBytes = C * VS * 2;
+/* A chunk's scratch slot, per (chunk, v-head), f16 tiles in the 128-byte-swizzled layout of sw128_off:
+ * W [64 rows][128 dk] and K~ [64][128] (two 64-column halves each), U~^T [128 dv][64 rows] (dv slice s of
+ * phase 2 at 4096 s), then G f32 [64], beta f32 [64] and gamma_L (16 bytes). */
+constexpr int kSlotW = 0, kSlotK = 16384, kSlotU = 32768, kSlotMeta = 49152, kSlotGl = kSlotMeta + 512;
+constexpr int kSlotBytes = kSlotGl + 16;
+constexpr uint32_t kTileBytes = C * D * 2;   /* one [64][128] b16 tile, and one TMA pair of [64][64] boxes */
 
-enum { kBarProducers = 1, kBarChain = 2, kBarPair0 = 3 };   /* named barriers (0 is __syncthreads) */
+enum { kBarChain = 1, kBarPair0 = 2 };   /* named barriers (0 is __syncthreads) */
 
 /* The scratch: the sequence table (int32 r0[n], r1[n], base[n + 1], padded to 256 bytes), then the
  * chunk slots. base[i] is the number of chunks before sequence i, capped at max_slots. */
@@ -95,6 +91,31 @@ __device__ __forceinline__ void bar_sync(int id, int threads) {
 /* cp.async of 4 bytes (src_bytes 0: zero fill). */
 __device__ __forceinline__ void cp_async4(void* dst, const void* src, int src_bytes) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(rf::saddr(dst)), "l"(src), "r"(src_bytes) : "memory");
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(a));
+    return r;
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
+    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
+__device__ __forceinline__ void sts32(uint32_t a, uint32_t v) { asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory"); }
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+
+/* Eight bf16 (one 16-byte chunk) times f, as eight f16; zero when !in. */
+__device__ __forceinline__ uint4 scale_bf16x8_to_f16(uint4 raw, float f, bool in) {
+    const uint32_t rw[4] = { raw.x, raw.y, raw.z, raw.w };
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+        o[e] = in ? rf::pack_f16(f * __uint_as_float(rw[e] << 16), f * __uint_as_float(rw[e] & 0xffff0000u)) : 0u;
+    return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 /* ------------------------------------------------------------------ plan */
@@ -151,30 +172,30 @@ __global__ void __launch_bounds__(kPlanThreads) gdn_plan_kernel(const GdnPlan p)
 /* ------------------------------------------------------------------ phase 1 */
 
 constexpr int kPrepThreads = 256;
-constexpr int kSeqCache = 256;   /* sequences whose table rows a phase-1 CTA keeps in shared memory */
+constexpr int kSeqCache = 256;   /* sequences whose table rows a CTA keeps in shared memory */
 
 struct PrepSmem {
-    uint16_t kraw[2][2][C][C];   /* k rows of the current and the next item: two 128-byte-swizzled halves */
+    uint16_t kraw[2][2][C][C];   /* k rows of the current and the next item (TMA, 128-byte swizzled); then
+                                    beta gamma k in f16 in place; then W (staging for the slot) */
+    uint16_t vraw[2][2][C][C];   /* v rows; then beta v in f16 in place; then U~^T (staging) */
     float graw[2][C], braw[2][C];
-    float a32[C][AP];            /* A, f32 */
-    uint16_t l16[C][TP];         /* A, f16 (the off-diagonal blocks of I + A) */
-    uint16_t w16[C][KP];         /* W = T x1, f16: bulk-stored to the slot */
-    uint16_t t16[C][TP];         /* T = (I + A)^-1, f16, then G and beta: bulk-stored together */
-    float G[C], beta[C];
-    uint16_t x1[C][KP];          /* beta gamma k, f16 */
+    float a32[4][16][20];        /* the diagonal 16x16 blocks of A, f32 */
+    uint16_t l16[C][TP];         /* A, f16 (its off-diagonal blocks are read) */
+    uint16_t t16[C][TP];         /* T = (I + A)^-1, f16 */
+    float G[C], beta[C], gl[4];  /* the slot's meta, bulk-stored together */
     uint16_t tmp[3][16][24];     /* per-warp 16x16 staging */
     int32_t r0[kSeqCache], base[kSeqCache + 1];
-    uint64_t landed[2];          /* the k rows of buffer b have landed */
+    uint64_t landed[2];          /* the k and v rows of buffer b have landed */
     int abort, ok, n_cached;
 };
-static_assert(offsetof(PrepSmem, G) == offsetof(PrepSmem, t16) + sizeof(uint16_t) * C * TP, "T|G|beta contiguous");
-static_assert(offsetof(PrepSmem, beta) == offsetof(PrepSmem, G) + sizeof(float) * C, "T|G|beta contiguous");
-static_assert(offsetof(PrepSmem, w16) % 16 == 0 && offsetof(PrepSmem, t16) % 16 == 0, "bulk-store sources");
+static_assert(offsetof(PrepSmem, vraw) % 1024 == 0, "TMA 128-byte swizzle destinations");
+static_assert(offsetof(PrepSmem, beta) == offsetof(PrepSmem, G) + C * 4 && offsetof(PrepSmem, gl) == offsetof(PrepSmem, G) + 2 * C * 4 &&
+                  offsetof(PrepSmem, G) % 16 == 0,
+              "G|beta|gamma_L contiguous, one bulk store");
 
 /* Chunk `slot` (< the table's base[n]): its first row, length and sequence (when `seq` is given). The
- * sequence is the largest i with base[i] <= slot,
- * searched in the first n_cached rows of the table (r0c, basec: shared-memory copies) when the slot lies
- * there, else in the table. */
+ * sequence is the largest i with base[i] <= slot, searched in the first n_cached rows of the table
+ * (r0c, basec: shared-memory copies) when the slot lies there, else in the table. */
 __device__ void locate_chunk(const GdnPlan& p, const int32_t* r0c, const int32_t* basec, int n_cached, int64_t slot,
                              int64_t* row0, int* len, int* seq = nullptr) {
     const int n = (int)p.g.n_seq;
@@ -191,8 +212,7 @@ __device__ void locate_chunk(const GdnPlan& p, const int32_t* r0c, const int32_t
             else hi = mid - 1;
         }
         i = lo;
-        const int64_t c = slot - basec[i];
-        *row0 = r0c[i] + c * C;
+        *row0 = r0c[i] + (slot - basec[i]) * C;
     } else {
         lo = n_cached;
         hi = n - 1;
@@ -238,18 +258,22 @@ __device__ void tri_offdiag_block(PrepSmem& s, int bi, int bj, int w) {
     }
 }
 
-/* Item i = (chunk slot i / Hv, v-head i % Hv): start its k rows (two TMA boxes of [64 rows][64], rows
- * past the end of k read as zero) completing on landed[buf], and g, beta (cp.async; zero past the chunk). */
-__device__ void prep_issue(const GdnPlan& p, const CUtensorMap* kmap, PrepSmem& s, int64_t item, int buf) {
+/* Item i = (chunk slot i / Hv, v-head i % Hv): start its k and v rows (two TMA boxes of [64 rows][64]
+ * each, rows past the end read as zero) completing on landed[buf], and g, beta (cp.async; zero past the
+ * chunk). */
+__device__ void prep_issue(const GdnPlan& p, const CUtensorMap* kmap, const CUtensorMap* vmap, PrepSmem& s, int64_t item,
+                           int buf) {
     const RidgeFillGdn& g = p.g;
     const int64_t slot = item / g.n_head_v, h = item % g.n_head_v, hk = h / (g.n_head_v / g.n_head_k);
     int64_t row0 = 0;
     int len = 0;
     locate_chunk(p, s.r0, s.base, s.n_cached, slot, &row0, &len);
     if (threadIdx.x == 0) {
-        rf::mbar_arrive_expect_tx(&s.landed[buf], kKBoxBytes);
+        rf::mbar_arrive_expect_tx(&s.landed[buf], 2 * kTileBytes);
         rf::tma_load_3d(&s.kraw[buf][0][0][0], kmap, &s.landed[buf], 0, (int)hk, (int)row0);
         rf::tma_load_3d(&s.kraw[buf][1][0][0], kmap, &s.landed[buf], C, (int)hk, (int)row0);
+        rf::tma_load_3d(&s.vraw[buf][0][0][0], vmap, &s.landed[buf], 0, (int)h, (int)row0);
+        rf::tma_load_3d(&s.vraw[buf][1][0][0], vmap, &s.landed[buf], C, (int)h, (int)row0);
     }
     if (threadIdx.x < C) {
         const int r = threadIdx.x;
@@ -259,7 +283,8 @@ __device__ void prep_issue(const GdnPlan& p, const CUtensorMap* kmap, PrepSmem& 
     }
 }
 
-__global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const GdnPlan p) {
+__global__ void __launch_bounds__(kPrepThreads, 2)
+gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const GdnPlan p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     PrepSmem& s = *(PrepSmem*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const RidgeFillGdn& g = p.g;
@@ -277,25 +302,25 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_kernel(const __grid_
         s.n_cached = n_cached;
         rf::mbar_init_fence();
         rf::tma_prefetch_map(&kmap);
+        rf::tma_prefetch_map(&vmap);
     }
     __syncthreads();
     const int64_t items = (int64_t)p.tab[3 * n_seq] * g.n_head_v;
 
-    if ((int64_t)blockIdx.x < items) prep_issue(p, &kmap, s, blockIdx.x, 0);
+    if ((int64_t)blockIdx.x < items) prep_issue(p, &kmap, &vmap, s, blockIdx.x, 0);
     rf::cp_async_commit();
     int buf = 0;
     int64_t waited = 0, issued = (int64_t)blockIdx.x < items ? 1 : 0;
     for (int64_t item = blockIdx.x; item < items; item += gridDim.x, buf ^= 1) {
+        /* The previous item's slot stores have read its buffers and the meta before they are written again. */
+        if (tid == 0) rf::bulk_store_wait_read();
         if (item + gridDim.x < items) {
-            prep_issue(p, &kmap, s, item + gridDim.x, buf ^ 1);
+            prep_issue(p, &kmap, &vmap, s, item + gridDim.x, buf ^ 1);
             ++issued;
         }
         rf::cp_async_commit();
         rf::cp_async_wait<1>();
-        if (tid == 0) {
-            s.ok = rf::mbar_wait(&s.landed[buf], (uint32_t)((waited >> 1) & 1), &s.abort, rf::kErrGdnWait);
-            rf::bulk_store_wait_read();   /* the previous item's stores have read w16, t16, G, beta */
-        }
+        if (tid == 0) s.ok = rf::mbar_wait(&s.landed[buf], (uint32_t)((waited >> 1) & 1), &s.abort, rf::kErrGdnWait);
         __syncthreads();
         if (!s.ok) break;
         ++waited;
@@ -304,9 +329,9 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_kernel(const __grid_
         int len = 0;
         locate_chunk(p, s.r0, s.base, s.n_cached, slot, &row0, &len);
         uint8_t* out = slot_ptr(p, slot, h);
-        const uint32_t ktile = rf::saddr(&s.kraw[buf][0][0][0]);
+        const uint32_t ktile = rf::saddr(&s.kraw[buf][0][0][0]), vtile = rf::saddr(&s.vraw[buf][0][0][0]);
 
-        /* G (inclusive cumulative log decay; zero past the chunk) and beta. */
+        /* G (inclusive cumulative log decay; zero past the chunk), beta, gamma_L. */
         if (tid < C) {
             float x = s.graw[buf][tid];
             for (int o = 1; o < 32; o <<= 1) {
@@ -320,34 +345,11 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_kernel(const __grid_
         if (tid >= 32 && tid < C) s.G[tid] += s.G[31];
         __syncthreads();
         const float gl = s.G[len - 1];
+        if (tid < 4) s.gl[tid] = tid == 0 ? __expf(gl) : 0.0f;
 
-        /* x1 = beta gamma k (shared) and K~ = k exp(G_L - G) (to the slot), f16, both zero past the
-         * chunk; the upper blocks of T zero. */
-#pragma unroll
-        for (int it = 0; it < 4; ++it) {
-            const int r = (tid >> 4) + 16 * it, seg = tid & 15;
-            uint4 raw;
-            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(raw.x), "=r"(raw.y), "=r"(raw.z), "=r"(raw.w)
-                         : "r"(rf::sw128_addr(ktile, r, seg * 8)));
-            const uint32_t rw[4] = { raw.x, raw.y, raw.z, raw.w };
-            const bool in = r < len;
-            const float fx = in ? s.beta[r] * __expf(s.G[r]) : 0.0f, fk = in ? __expf(gl - s.G[r]) : 0.0f;
-            uint32_t xx[4], kk[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float lo = __uint_as_float(rw[e] << 16), hi = __uint_as_float(rw[e] & 0xffff0000u);
-                xx[e] = in ? rf::pack_f16(fx * lo, fx * hi) : 0u;
-                kk[e] = in ? rf::pack_f16(fk * lo, fk * hi) : 0u;
-            }
-            *(uint4*)&s.x1[r][seg * 8] = make_uint4(xx[0], xx[1], xx[2], xx[3]);
-            *(uint4*)(out + kSlotK + (r * KP + seg * 8) * 2) = make_uint4(kk[0], kk[1], kk[2], kk[3]);
-        }
-        for (int i = tid; i < 6 * 16 * 8; i += kPrepThreads) {   /* blocks (0,1) (0,2) (0,3) (1,2) (1,3) (2,3) */
-            const int blk = i >> 7, r = (i >> 3) & 15, cp = i & 7;
-            const int bi = blk < 3 ? 0 : blk < 5 ? 1 : 2, bj = blk < 3 ? blk + 1 : blk < 5 ? blk - 1 : 3;
-            *(uint32_t*)&s.t16[16 * bi + r][16 * bj + 2 * cp] = 0u;
-        }
-        {   /* K K^T (warp w: rows 16 (w & 3), columns 32 (w >> 2)..+32) and A */
+        /* K K^T (bf16, exact inputs) and A: warp w, rows 16 (w & 3), columns 32 (w >> 2)..+32 (warps 4, 5
+         * hold only blocks above the diagonal, which A does not use). */
+        if (w != 4 && w != 5) {
             const int rb = 16 * (w & 3), cb = 32 * (w >> 2);
             float acc[4][4] = {};
 #pragma unroll
@@ -365,12 +367,36 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_kernel(const __grid_
 #pragma unroll
             for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int i = rb + gq + (e >> 1) * 8, j = cb + 8 * nt + 2 * tq + (e & 1);
-                    const float v = (j < i && i < len) ? s.beta[i] * __expf(s.G[i] - s.G[j]) * acc[nt][e] : 0.0f;
-                    s.a32[i][j] = v;
-                    s.l16[i][j] = __half_as_ushort(__float2half_rn(v));
+                for (int hr = 0; hr < 2; ++hr) {
+                    const int i = rb + gq + 8 * hr, j = cb + 8 * nt + 2 * tq;
+                    float v[2];
+#pragma unroll
+                    for (int e = 0; e < 2; ++e)
+                        v[e] = (j + e < i && i < len) ? s.beta[i] * __expf(s.G[i] - s.G[j + e]) * acc[nt][2 * hr + e] : 0.0f;
+                    *(uint32_t*)&s.l16[i][j] = rf::pack_f16(v[0], v[1]);
+                    if ((i >> 4) == (j >> 4)) *(float2*)&s.a32[i >> 4][i & 15][j & 15] = make_float2(v[0], v[1]);
                 }
+        }
+        __syncthreads();
+
+        /* In place, 16-byte chunks at their swizzled places: k -> x1 = beta gamma k (f16) and K~ = k
+         * exp(G_L - G) (f16, to the slot); v -> x2 = beta v (f16); rows past the chunk zero. The blocks of
+         * T above the diagonal zero. */
+#pragma unroll
+        for (int it = 0; it < 4; ++it) {
+            const int r = (tid >> 4) + 16 * it, seg = tid & 15;
+            const bool in = r < len;
+            const uint32_t off = rf::sw128_off(r, seg * 8);
+            const uint4 kr = lds128(ktile + off), vr = lds128(vtile + off);
+            const float gr = s.G[r], br = s.beta[r];
+            *(uint4*)(out + kSlotK + off) = scale_bf16x8_to_f16(kr, __expf(gl - gr), in);
+            sts128(ktile + off, scale_bf16x8_to_f16(kr, br * __expf(gr), in));
+            sts128(vtile + off, scale_bf16x8_to_f16(vr, br, in));
+        }
+        for (int i = tid; i < 6 * 16 * 8; i += kPrepThreads) {   /* blocks (0,1) (0,2) (0,3) (1,2) (1,3) (2,3) */
+            const int blk = i >> 7, r = (i >> 3) & 15, cp = i & 7;
+            const int bi = blk < 3 ? 0 : blk < 5 ? 1 : 2, bj = blk < 3 ? blk + 1 : blk < 5 ? blk - 1 : 3;
+            *(uint32_t*)&s.t16[16 * bi + r][16 * bj + 2 * cp] = 0u;
         }
         __syncthreads();
 
@@ -382,7 +408,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_kernel(const __grid_
             float a[16];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                const float4 v = *(const float4*)&s.a32[16 * b + r][16 * b + 4 * q];
+                const float4 v = *(const float4*)&s.a32[b][r][4 * q];
                 a[4 * q] = v.x;
                 a[4 * q + 1] = v.y;
                 a[4 * q + 2] = v.z;
@@ -396,7 +422,7 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_kernel(const __grid_
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc) {
                     const float xj = __shfl_sync(0xffffffffu, x[cc], (l & 16) | j);
-                    x[cc] = fmaf(-a[j], xj, x[cc]);   /* a[j] = 0 for j >= r */
+                    x[cc] = fmaf(-(j < r ? a[j] : 0.0f), xj, x[cc]);
                 }
             *(uint2*)&s.t16[16 * b + r][16 * b + c0] = make_uint2(rf::pack_f16(x[0], x[1]), rf::pack_f16(x[2], x[3]));
         }
@@ -408,34 +434,60 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_kernel(const __grid_
         if (w == 0) tri_offdiag_block(s, 3, 0, 0);               /* T30 */
         __syncthreads();
 
-        /* W = T x1 (warp w: rows 16 (w & 3), columns 64 (w >> 2)..+64). */
+        /* W = T x1 (warp w: rows 16 (w & 3), dk 64 (w >> 2)..+64), staged over x1 once every warp has
+         * read it. */
         {
             const int rb = 16 * (w & 3), cb = 64 * (w >> 2);
             uint32_t ta[4][4];
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) rf::load_a(ta[ks], &s.t16[0][0], TP, rb, 16 * ks);
+            float acc[8][4] = {};
 #pragma unroll
-            for (int pr = 0; pr < 4; ++pr) {
-                float acc[2][4] = {};
+            for (int pr = 0; pr < 4; ++pr)
 #pragma unroll
                 for (int ks = 0; ks < 4; ++ks) {
                     uint32_t b[4];
-                    rf::load_b_kn(b, &s.x1[0][0], KP, 16 * ks, cb + 16 * pr);
-                    rf::mma_f16(acc[0], ta[ks], b[0], b[1]);
-                    rf::mma_f16(acc[1], ta[ks], b[2], b[3]);
+                    rf::load_b_kn_sw(b, ktile, 16 * ks, cb + 16 * pr);
+                    rf::mma_f16(acc[2 * pr], ta[ks], b[0], b[1]);
+                    rf::mma_f16(acc[2 * pr + 1], ta[ks], b[2], b[3]);
                 }
+            __syncthreads();
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                    *(uint32_t*)&s.w16[rb + gq][cb + 16 * pr + 8 * nt + 2 * tq] = rf::pack_f16(acc[nt][0], acc[nt][1]);
-                    *(uint32_t*)&s.w16[rb + gq + 8][cb + 16 * pr + 8 * nt + 2 * tq] = rf::pack_f16(acc[nt][2], acc[nt][3]);
+            for (int j = 0; j < 8; ++j) {
+                const int c = cb + 8 * j + 2 * tq;
+                sts32(ktile + rf::sw128_off(rb + gq, c), rf::pack_f16(acc[j][0], acc[j][1]));
+                sts32(ktile + rf::sw128_off(rb + gq + 8, c), rf::pack_f16(acc[j][2], acc[j][3]));
+            }
+        }
+        /* U~^T = x2^T T^T (warp w: dv rows 16 w..+16, all 64 chunk rows), staged over x2 the same way. */
+        {
+            float acc[8][4] = {};
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+                uint32_t a[4];
+                rf::load_a_t_sw(a, vtile, 16 * ks, 16 * w);
+#pragma unroll
+                for (int pr = 0; pr < 4; ++pr) {
+                    uint32_t b[4];
+                    rf::load_b_nk(b, &s.t16[0][0], TP, 16 * pr, 16 * ks);
+                    rf::mma_f16(acc[2 * pr], a, b[0], b[1]);
+                    rf::mma_f16(acc[2 * pr + 1], a, b[2], b[3]);
                 }
+            }
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int c = 8 * j + 2 * tq;
+                sts32(vtile + rf::sw128_off(16 * w + gq, c, 0), rf::pack_f16(acc[j][0], acc[j][1]));
+                sts32(vtile + rf::sw128_off(16 * w + gq + 8, c, 0), rf::pack_f16(acc[j][2], acc[j][3]));
             }
         }
         rf::fence_proxy_async_smem();
         __syncthreads();
-        if (tid == 0) {   /* W, and T|G|beta, to the slot; read back by the next item's first wait */
-            rf::bulk_store(out + kSlotW, &s.w16[0][0], sizeof(s.w16));
-            rf::bulk_store(out + kSlotT, &s.t16[0][0], kTMBytes);
+        if (tid == 0) {   /* W, U~^T and G|beta|gamma_L to the slot; the next issue into this buffer waits for them */
+            rf::bulk_store(out + kSlotW, &s.kraw[buf][0][0][0], kTileBytes);
+            rf::bulk_store(out + kSlotU, &s.vraw[buf][0][0][0], kTileBytes);
+            rf::bulk_store(out + kSlotMeta, &s.G[0], kSlotBytes - kSlotMeta);
             rf::bulk_store_commit();
         }
     }
@@ -454,49 +506,24 @@ __global__ void __launch_bounds__(kPrepThreads, 2) gdn_prep_kernel(const __grid_
 
 /* ------------------------------------------------------------------ phase 2 */
 
-constexpr int kChainThreads = 256;   /* warps 0-3: the chain; warps 4-7: producers */
+constexpr int kChainThreads = 160;   /* warps 0-3: the chain; warp 4: the loader */
 
-struct WKStage {                 /* bulk copy of the slot's W|K~ */
-    uint16_t w16[C][KP];
-    uint16_t kt16[C][KP];
-};
-
-struct RawStage {
-    uint16_t t16[C][TP];         /* T, f16, then G and beta (bulk copy of the slot's T|G|beta) */
-    float meta[2 * C];
-    uint16_t vraw[C][VS];        /* this CTA's 32 columns of v, bf16 (TMA box) */
+struct Stage {                       /* one chunk's inputs, three bulk copies from its slot */
+    uint16_t w[2][C][C];             /* W, swizzled */
+    uint16_t kt[2][C][C];            /* K~, swizzled */
+    uint16_t u[VS][C];               /* U~^T for this CTA's 32 dv rows, swizzled */
+    float gl[32];                    /* gamma_L (first word) */
 };
 
 struct ChainSmem {
-    RawStage raw[2];             /* producers' inputs, two chunks in flight */
-    WKStage wk[3];               /* W and K~ of chunks c, c+1, c+2 (the chain reads chunk c's) */
-    float u32[2][C][UP];         /* U~ = T (beta v) for the slice, f32, per chunk */
-    uint16_t x2[C][VP];          /* beta v, f16 (producers only) */
-    float part[2][4][16][PP];    /* the chain warps' partial V'^T, double-buffered */
-    float gl[2];                 /* gamma_L per chunk */
-    uint64_t landed[2];          /* raw stage b (and its W|K~ stage) has landed */
-    uint64_t ready[2], consumed[2];
-    int abort, ok_producers, ok_chain;
+    Stage st[kStages];
+    float part[2][4][16][PP];        /* the chain warps' partial V'^T, double-buffered */
+    uint64_t landed[kStages], consumed[kStages];
+    int abort, ok_chain;
 };
-static_assert(offsetof(RawStage, meta) == sizeof(uint16_t) * C * TP && offsetof(RawStage, vraw) % 128 == 0 &&
-                  sizeof(RawStage) % 128 == 0 && offsetof(ChainSmem, wk) % 16 == 0 && sizeof(WKStage) == kWKBytes,
-              "stage layout");
+static_assert(sizeof(Stage) % 128 == 0, "stage layout");
 
-/* Start chunk `slot`'s inputs into raw stage `rbuf` and W|K~ stage `wbuf`: W|K~ and T|G|beta by one bulk
- * copy each from its scratch slot, this CTA's v columns by one TMA box; all complete on landed[rbuf].
- * One producer thread. */
-__device__ void chain_issue(const GdnPlan& p, const CUtensorMap* vmap, ChainSmem& s, int64_t slot, int64_t row0,
-                            int64_t h, int v0, int rbuf, int wbuf) {
-    const uint8_t* src = slot_ptr(p, slot, h);
-    RawStage& st = s.raw[rbuf];
-    uint64_t* bar = &s.landed[rbuf];
-    rf::mbar_arrive_expect_tx(bar, kWKBytes + kTMBytes + kVBoxBytes);
-    rf::bulk_load(&s.wk[wbuf], src + kSlotW, kWKBytes, bar);
-    rf::bulk_load(&st.t16[0][0], src + kSlotT, kTMBytes, bar);
-    rf::tma_load_3d(&st.vraw[0][0], vmap, bar, v0, (int)h, (int)row0);
-}
-
-__global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const __grid_constant__ CUtensorMap vmap, const GdnPlan p) {
+__global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const GdnPlan p) {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     ChainSmem& s = *(ChainSmem*)(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
     const RidgeFillGdn& g = p.g;
@@ -512,90 +539,41 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const __gri
     const int n = (int)g.n_seq;
     const int64_t r0 = p.tab[seq], r1 = p.tab[n + seq], base = p.tab[2 * n + seq];
     const int64_t chunks = max((int64_t)0, min((r1 - r0 + C - 1) / C, (int64_t)p.max_slots - base));
-    auto chunk_len = [&](int64_t c) { return (int)min((int64_t)C, r1 - r0 - c * C); };
 
     if (tid == 0) {
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < kStages; ++b) {
             rf::mbar_init(&s.landed[b], 1);
-            rf::mbar_init(&s.ready[b], 128);
-            rf::mbar_init(&s.consumed[b], 128);
+            rf::mbar_init(&s.consumed[b], 4);
         }
         s.abort = 0;
         rf::mbar_init_fence();
-        rf::tma_prefetch_map(&vmap);
     }
     __syncthreads();
 
-    if (w >= 4) {
-        /* ---------------------------------------------------------- producers */
-        const int pt = tid - 128, pw = w - 4;
-        int64_t issued = 0, landed = 0;
-        if (pt == 0)
-            for (; issued < 2 && issued < chunks; ++issued)
-                chain_issue(p, &vmap, s, base + issued, r0 + issued * C, h, v0, (int)issued, (int)issued);
+    if (w == 4) {
+        /* ------------------------------------------------------------ the loader (one lane) */
+        if (l != 0) return;
+        int64_t issued = 0;
         for (int64_t c = 0; c < chunks; ++c) {
-            const int b = (int)(c & 1);
-            const int len = chunk_len(c);
-            if (pt == 0) {   /* chunk c's inputs have landed, and chunk c-2 is consumed (its U~ buffer is free) */
-                s.ok_producers = rf::mbar_wait(&s.landed[b], (uint32_t)((c >> 1) & 1), &s.abort, rf::kErrGdnWait) &&
-                                 (c < 2 || rf::mbar_wait(&s.consumed[b], (uint32_t)(((c - 2) >> 1) & 1), &s.abort, rf::kErrGdnWait));
-                s.gl[b] = __expf(s.raw[b].meta[len - 1]);
-            }
-            bar_sync(kBarProducers, 128);
-            if (!s.ok_producers) break;
-            landed = c + 1;
-            RawStage& st = s.raw[b];
-            const float* beta = st.meta + C;
-            for (int i = pt; i < C * (VS / 8); i += 128) {  /* x2 = beta v; rows past the chunk 0 */
-                const int r = i >> 2, seg = i & 3;
-                const uint4 raw = *(const uint4*)&st.vraw[r][seg * 8];
-                const uint32_t rw[4] = { raw.x, raw.y, raw.z, raw.w };
-                uint32_t xx[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    xx[e] = r < len ? rf::pack_f16(beta[r] * __uint_as_float(rw[e] << 16), beta[r] * __uint_as_float(rw[e] & 0xffff0000u)) : 0u;
-                *(uint4*)&s.x2[r][seg * 8] = make_uint4(xx[0], xx[1], xx[2], xx[3]);
-            }
-            bar_sync(kBarProducers, 128);
-            {   /* U~ = T x2: producer warp pw, rows 16 pw..+16, the slice's 32 columns */
-                uint32_t ta[4][4];
-#pragma unroll
-                for (int ks = 0; ks < 4; ++ks) rf::load_a(ta[ks], &st.t16[0][0], TP, 16 * pw, 16 * ks);
-#pragma unroll
-                for (int pr = 0; pr < 2; ++pr) {
-                    float acc[2][4] = {};
-#pragma unroll
-                    for (int ks = 0; ks < 4; ++ks) {
-                        uint32_t bb[4];
-                        rf::load_b_kn(bb, &s.x2[0][0], VP, 16 * ks, 16 * pr);
-                        rf::mma_f16(acc[0], ta[ks], bb[0], bb[1]);
-                        rf::mma_f16(acc[1], ta[ks], bb[2], bb[3]);
-                    }
-#pragma unroll
-                    for (int nt = 0; nt < 2; ++nt) {
-                        *(float2*)&s.u32[b][16 * pw + gq][16 * pr + 8 * nt + 2 * tq] = make_float2(acc[nt][0], acc[nt][1]);
-                        *(float2*)&s.u32[b][16 * pw + gq + 8][16 * pr + 8 * nt + 2 * tq] = make_float2(acc[nt][2], acc[nt][3]);
-                    }
-                }
-            }
-            rf::mbar_arrive(&s.ready[b]);   /* chunk c's U~, gamma_L and W|K~ (landed above) are the chain's */
-            if (pt == 0)   /* chunk c-1 is consumed: W|K~ stage (c+2) % 3 is free */
-                s.ok_producers = c < 1 || rf::mbar_wait(&s.consumed[b ^ 1], (uint32_t)(((c - 1) >> 1) & 1), &s.abort, rf::kErrGdnWait);
-            bar_sync(kBarProducers, 128);   /* also: every producer is done with raw stage b and x2 */
-            if (!s.ok_producers) break;
-            if (pt == 0 && c + 2 < chunks) {
-                chain_issue(p, &vmap, s, base + c + 2, r0 + (c + 2) * C, h, v0, b, (int)((c + 2) % 3));
-                ++issued;
+            const int st = (int)(c % kStages);
+            if (c >= kStages && !rf::mbar_wait(&s.consumed[st], (uint32_t)((c / kStages - 1) & 1), &s.abort, rf::kErrGdnWait))
+                break;
+            const uint8_t* src = slot_ptr(p, base + c, h);
+            Stage& sg = s.st[st];
+            rf::mbar_arrive_expect_tx(&s.landed[st], 2 * kTileBytes + (uint32_t)sizeof(sg.u) + 16);
+            rf::bulk_load(&sg.w[0][0][0], src + kSlotW, 2 * kTileBytes, &s.landed[st]);
+            rf::bulk_load(&sg.u[0][0], src + kSlotU + vsl * (int)sizeof(sg.u), sizeof(sg.u), &s.landed[st]);
+            rf::bulk_load(&sg.gl[0], src + kSlotGl, 16, &s.landed[st]);
+            ++issued;
+        }
+        /* Before the CTA's shared memory is released: the copies of the last stages have landed (only the
+         * most recent copy of a stage can still be in flight; bounded). */
+        for (int64_t i = issued > kStages ? issued - kStages : 0; i < issued; ++i) {
+            const uint64_t t0 = rf::global_ns();
+            while (!rf::mbar_try_wait(&s.landed[i % kStages], (uint32_t)((i / kStages) & 1)) &&
+                   rf::global_ns() - t0 < rf::kWaitTimeoutNs) {
             }
         }
-        /* After a timed-out hand-over: let the copies already issued land before the CTA's shared memory
-         * is released (bounded too). */
-        if (pt == 0)
-            for (int64_t i = landed; i < issued; ++i) {
-                const uint64_t t0 = rf::global_ns();
-                while (!rf::mbar_try_wait(&s.landed[i & 1], (uint32_t)((i >> 1) & 1)) && rf::global_ns() - t0 < rf::kWaitTimeoutNs) {
-                }
-            }
         return;
     }
 
@@ -603,26 +581,27 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const __gri
     const int vh = w & 1, kh = w >> 1;
     /* The state slice: S[v0 + 16 vh + m][64 kh + n] as C tiles over dk (8 tiles of 8 columns). */
     float S[8][4];
-    float* st = g.state + state_slot * g.st_slot + h * g.st_head;
+    float* stp = g.state + state_slot * g.st_slot + h * g.st_head;
 #pragma unroll
     for (int j = 0; j < 8; ++j)
 #pragma unroll
         for (int hr = 0; hr < 2; ++hr) {
             const int v = v0 + 16 * vh + gq + 8 * hr, k = 64 * kh + 8 * j + 2 * tq;
-            const float2 x = *(const float2*)(st + (int64_t)v * D + k);
+            const float2 x = *(const float2*)(stp + (int64_t)v * D + k);
             S[j][2 * hr] = x.x;
             S[j][2 * hr + 1] = x.y;
         }
     bool ok = true;
     for (int64_t c = 0; c < chunks; ++c) {
-        const int b = (int)(c & 1);
-        if (tid == 0) s.ok_chain = rf::mbar_wait(&s.ready[b], (uint32_t)((c >> 1) & 1), &s.abort, rf::kErrGdnWait);
+        const int st = (int)(c % kStages), b = (int)(c & 1);
+        if (tid == 0) s.ok_chain = rf::mbar_wait(&s.landed[st], (uint32_t)((c / kStages) & 1), &s.abort, rf::kErrGdnWait);
         bar_sync(kBarChain, 128);
         if (!(ok = s.ok_chain)) break;
-        const WKStage& wk = s.wk[c % 3];
+        const Stage& sg = s.st[st];
+        const uint32_t wtile = rf::saddr(&sg.w[0][0][0]), kttile = rf::saddr(&sg.kt[0][0][0]), utile = rf::saddr(&sg.u[0][0]);
         uint8_t* ow = p.outws ? out_ptr(p, base + c, h) : nullptr;
 
-        /* V'^T partial over this warp's dk half: [16 dv rows] x [64 chunk rows]. */
+        /* V'^T partial over this warp's dk half: [16 dv rows] x [64 chunk rows] = S W^T. */
         float pv[8][4] = {};
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
@@ -639,7 +618,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const __gri
 #pragma unroll
             for (int pr = 0; pr < 4; ++pr) {
                 uint32_t bb[4];
-                rf::load_b_nk(bb, &wk.w16[0][0], KP, 16 * pr, 64 * kh + 16 * ks);
+                rf::load_b_nk_sw(bb, wtile, 16 * pr, 64 * kh + 16 * ks);
                 rf::mma_f16(pv[2 * pr], a, bb[0], bb[1]);
                 rf::mma_f16(pv[2 * pr + 1], a, bb[2], bb[3]);
             }
@@ -650,13 +629,18 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const __gri
             *(float2*)&s.part[b][w][gq + 8][8 * j + 2 * tq] = make_float2(pv[j][2], pv[j][3]);
         }
         bar_sync(kBarPair0 + vh, 64);
-        const float gamma_l = s.gl[b];
+        const float gamma_l = sg.gl[0];
+        /* V' = U~ - (both halves of S W^T). */
 #pragma unroll
         for (int j = 0; j < 8; ++j)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int m = gq + (e >> 1) * 8, nn = 8 * j + 2 * tq + (e & 1);
-                pv[j][e] = s.u32[b][nn][16 * vh + m] - (pv[j][e] + s.part[b][w ^ 2][m][nn]);
+            for (int hr = 0; hr < 2; ++hr) {
+                const int m = gq + 8 * hr, nn = 8 * j + 2 * tq;
+                const uint32_t uw = lds32(utile + rf::sw128_off(16 * vh + m, nn, 0));
+                const float2 uf = __half22float2(*(const __half2*)&uw);
+                const float2 pt = *(const float2*)&s.part[b][w ^ 2][m][nn];
+                pv[j][2 * hr] = uf.x - (pv[j][2 * hr] + pt.x);
+                pv[j][2 * hr + 1] = uf.y - (pv[j][2 * hr + 1] + pt.y);
             }
 
         /* S <- gamma_L S + V'^T K~ over this warp's dk half. */
@@ -679,12 +663,13 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const __gri
 #pragma unroll
             for (int pr = 0; pr < 4; ++pr) {
                 uint32_t bb[4];
-                rf::load_b_kn(bb, &wk.kt16[0][0], KP, 16 * ks, 64 * kh + 16 * pr);
+                rf::load_b_kn_sw(bb, kttile, 16 * ks, 64 * kh + 16 * pr);
                 rf::mma_f16(S[2 * pr], a, bb[0], bb[1]);
                 rf::mma_f16(S[2 * pr + 1], a, bb[2], bb[3]);
             }
         }
-        rf::mbar_arrive(&s.consumed[b]);
+        __syncwarp();
+        if (l == 0) rf::mbar_arrive(&s.consumed[st]);
     }
     if (!ok) return;   /* a hand-over timed out (recorded in ridgefill_device_error): leave the state as it was */
 #pragma unroll
@@ -692,7 +677,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const __gri
 #pragma unroll
         for (int hr = 0; hr < 2; ++hr) {
             const int v = v0 + 16 * vh + gq + 8 * hr, k = 64 * kh + 8 * j + 2 * tq;
-            *(float2*)(st + (int64_t)v * D + k) = make_float2(S[j][2 * hr], S[j][2 * hr + 1]);
+            *(float2*)(stp + (int64_t)v * D + k) = make_float2(S[j][2 * hr], S[j][2 * hr + 1]);
         }
 }
 
@@ -752,7 +737,7 @@ gdn_out_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__
         if (state_slot < 0 || state_slot >= g.n_states) continue;   /* a skipped sequence: its o rows are left as they are */
         if (tid == 0) {
             const uint8_t* ow = out_ptr(p, slot, h);
-            rf::mbar_arrive_expect_tx(&s.landed, 2 * kKBoxBytes + (uint32_t)(sizeof(s.s0) + sizeof(s.ut) + sizeof(s.meta)));
+            rf::mbar_arrive_expect_tx(&s.landed, 2 * kTileBytes + (uint32_t)(sizeof(s.s0) + sizeof(s.ut) + sizeof(s.meta)));
             rf::tma_load_3d(&s.qraw[0][0][0], &qmap, &s.landed, 0, (int)hk, (int)row0);
             rf::tma_load_3d(&s.qraw[1][0][0], &qmap, &s.landed, C, (int)hk, (int)row0);
             rf::tma_load_3d(&s.kraw[0][0][0], &kmap, &s.landed, 0, (int)hk, (int)row0);
@@ -908,7 +893,7 @@ extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
         return RAD_E_STRIDE;
     CUtensorMap kmap, vmap, qmap;
     if (!head_rows_map(&kmap, g.k, g.T, g.n_head_k, g.k_row, g.k_head, C, true) ||
-        !head_rows_map(&vmap, g.v, g.T, g.n_head_v, g.v_row, g.v_head, VS, false) ||
+        !head_rows_map(&vmap, g.v, g.T, g.n_head_v, g.v_row, g.v_head, C, true) ||
         (g.q && !head_rows_map(&qmap, g.q, g.T, g.n_head_k, g.q_row, g.q_head, C, true)))
         return RAD_E_DEVICE;
     GdnPlan p;
@@ -929,9 +914,9 @@ extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
      * chunk count find no item. */
     const int64_t items = slots * g.n_head_v;
     const int64_t grid1 = items < 2LL * rf::sm_count() ? items : 2LL * rf::sm_count();
-    gdn_prep_kernel<<<(unsigned)grid1, kPrepThreads, smem1, stream>>>(kmap, p);
+    gdn_prep_kernel<<<(unsigned)grid1, kPrepThreads, smem1, stream>>>(kmap, vmap, p);
     if (cudaGetLastError() != cudaSuccess) return RAD_E_DEVICE;
-    gdn_chain_kernel<<<dim3(D / VS, (unsigned)g.n_head_v, (unsigned)g.n_seq), kChainThreads, smem2, stream>>>(vmap, p);
+    gdn_chain_kernel<<<dim3(D / VS, (unsigned)g.n_head_v, (unsigned)g.n_seq), kChainThreads, smem2, stream>>>(p);
     if (!g.o) return rf::launch_status();
     if (cudaGetLastError() != cudaSuccess) return RAD_E_DEVICE;
     gdn_out_kernel<<<(unsigned)grid1, kOutThreads, smem3, stream>>>(qmap, kmap, p);
@@ -953,9 +938,9 @@ int gdn_device_error(int reset) { return read_device_error(reset); }
  * every stream of the step). This entry point takes the same operands as the ridgefill_gdn_fill row,
  * ignores RadArgs::scratch, and uses instead a workspace compiled into the library: a file-scope device
  * array of kNoAllocScratchBytes (64 MiB), which every GPU that loads the library holds until the
- * process exits. 64 MiB holds the fill's workspace (43.5 KiB per 64-row chunk and value head, one chunk
- * more per sequence) for a one-sequence 2,048-row call -- the engine's default chunk -- at up to 45 value
- * heads, or a 4,096-row call at up to 23; a call that needs more returns RAD_E_SHAPE and launches nothing.
+ * process exits. 64 MiB holds the fill's workspace (48.5 KiB per 64-row chunk and value head, one chunk
+ * more per sequence) for a one-sequence 2,048-row call -- the engine's default chunk -- at up to 40 value
+ * heads, or a 4,096-row call at up to 20; a call that needs more returns RAD_E_SHAPE and launches nothing.
  *
  * The first call on each device resolves the array's device address there (cudaGetSymbolAddress, once
  * per device, with that device current); make that first call before any stream capture. No call

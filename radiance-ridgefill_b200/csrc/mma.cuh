@@ -65,14 +65,19 @@ __device__ __forceinline__ void load_b_kn(uint32_t (&b)[4], const void* base, in
     ldsm_x4_t(b, saddr(p));
 }
 
-/* Shared-memory byte address of element (row, col) of a [64][128] b16 tile stored as two 64-column
- * halves of [64][64], each written by TMA with 128-byte swizzle (16-byte chunk j of row r at chunk
- * j ^ (r & 7)); `tile` 1024-byte aligned, col a multiple of 8. */
-__device__ __forceinline__ uint32_t sw128_addr(uint32_t tile, int row, int col) {
-    return tile + (uint32_t)((col >> 6) * 8192 + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4));
+/* Byte offset of element (row, col) in a b16 tile of 64-column halves, each half [rows][64] with its rows
+ * of 128 bytes and 128-byte swizzle (16-byte chunk j of row r at chunk j ^ (r & 7)), halves `half` bytes
+ * apart: the layout TMA writes for a [64 rows][64] box with CU_TENSOR_MAP_SWIZZLE_128B, and the layout
+ * this library keeps its own f16 tiles in. col & 7 selects the element inside the chunk. */
+__device__ __forceinline__ uint32_t sw128_off(int row, int col, int half = 8192) {
+    return (uint32_t)((col >> 6) * half + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4) + (col & 7) * 2);
 }
 
-/* load_a / load_b_nk on such a tile. */
+/* Shared-memory byte address of element (row, col) of a [64][128] tile in that layout (two halves of
+ * [64][64]); `tile` 1024-byte aligned when TMA wrote it. */
+__device__ __forceinline__ uint32_t sw128_addr(uint32_t tile, int row, int col) { return tile + sw128_off(row, col); }
+
+/* load_a / load_b_nk / load_b_kn on such a tile. */
 __device__ __forceinline__ void load_a_sw(uint32_t (&a)[4], uint32_t tile, int row0, int col0) {
     const int l = threadIdx.x & 31, mi = l >> 3, r = l & 7;
     ldsm_x4(a, sw128_addr(tile, row0 + r + (mi & 1) * 8, col0 + (mi >> 1) * 8));
@@ -80,6 +85,15 @@ __device__ __forceinline__ void load_a_sw(uint32_t (&a)[4], uint32_t tile, int r
 __device__ __forceinline__ void load_b_nk_sw(uint32_t (&b)[4], uint32_t tile, int n0, int k0) {
     const int l = threadIdx.x & 31, mi = l >> 3, r = l & 7;
     ldsm_x4(b, sw128_addr(tile, n0 + r + (mi >> 1) * 8, k0 + (mi & 1) * 8));
+}
+__device__ __forceinline__ void load_b_kn_sw(uint32_t (&b)[4], uint32_t tile, int k0, int n0) {
+    const int l = threadIdx.x & 31, mi = l >> 3, r = l & 7;
+    ldsm_x4_t(b, sw128_addr(tile, k0 + r + (mi & 1) * 8, n0 + (mi >> 1) * 8));
+}
+/* The A fragment of the 16x16 block (m0, k0) of A = X^T, X [k][m] stored in such a tile (transposing load). */
+__device__ __forceinline__ void load_a_t_sw(uint32_t (&a)[4], uint32_t tile, int k0, int m0) {
+    const int l = threadIdx.x & 31, mi = l >> 3, r = l & 7;
+    ldsm_x4_t(a, sw128_addr(tile, k0 + r + (mi >> 1) * 8, m0 + (mi & 1) * 8));
 }
 
 __device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {

@@ -59,7 +59,7 @@ def test_noalloc_refuses_past_its_workspace(cuda, product_lib):
     """A call whose workspace would exceed 64 MiB is refused with RAD_E_SHAPE before any launch (its
     state is left alone)."""
     torch = cuda
-    T, hk, hv = 8192, 16, 32          # 129 chunk slots x 32 heads x 44,544 B = 183.9 MB > 64 MiB
+    T, hk, hv = 8192, 16, 32          # 129 chunk slots x 32 heads x 49,680 B = 205.1 MB > 64 MiB
     t, state = _operands(torch, 7, T, hk, hv)
     S = torch.from_numpy(state.copy()).cuda()
     assert _noalloc(product_lib, _tensors(t, S), H.gdn_params(T, hk, hv), torch) == abi.E_SHAPE
