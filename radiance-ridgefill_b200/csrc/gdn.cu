@@ -182,16 +182,16 @@ struct PrepSmem {
     float a32[4][16][20];        /* the diagonal 16x16 blocks of A, f32 */
     uint16_t l16[C][TP];         /* A, f16 (its off-diagonal blocks are read) */
     uint16_t t16[C][TP];         /* T = (I + A)^-1, f16 */
-    float G[C], beta[C], gl[4];  /* the slot's meta, bulk-stored together */
+    struct Meta {
+        float G[C], beta[C], gl[4];
+    } meta[2];                   /* the slot's meta per buffer, bulk-stored whole */
     uint16_t tmp[3][16][24];     /* per-warp 16x16 staging */
     int32_t r0[kSeqCache], base[kSeqCache + 1];
     uint64_t landed[2];          /* the k and v rows of buffer b have landed */
     int abort, ok, n_cached;
 };
 static_assert(offsetof(PrepSmem, vraw) % 1024 == 0, "TMA 128-byte swizzle destinations");
-static_assert(offsetof(PrepSmem, beta) == offsetof(PrepSmem, G) + C * 4 && offsetof(PrepSmem, gl) == offsetof(PrepSmem, G) + 2 * C * 4 &&
-                  offsetof(PrepSmem, G) % 16 == 0,
-              "G|beta|gamma_L contiguous, one bulk store");
+static_assert(sizeof(PrepSmem::Meta) == kSlotBytes - kSlotMeta && offsetof(PrepSmem, meta) % 16 == 0, "the slot's meta, one bulk store");
 
 /* Chunk `slot` (< the table's base[n]): its first row, length and sequence (when `seq` is given). The
  * sequence is the largest i with base[i] <= slot, searched in the first n_cached rows of the table
@@ -312,14 +312,7 @@ gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
     int buf = 0;
     int64_t waited = 0, issued = (int64_t)blockIdx.x < items ? 1 : 0;
     for (int64_t item = blockIdx.x; item < items; item += gridDim.x, buf ^= 1) {
-        /* The previous item's slot stores have read its buffers and the meta before they are written again. */
-        if (tid == 0) rf::bulk_store_wait_read();
-        if (item + gridDim.x < items) {
-            prep_issue(p, &kmap, &vmap, s, item + gridDim.x, buf ^ 1);
-            ++issued;
-        }
-        rf::cp_async_commit();
-        rf::cp_async_wait<1>();
+        rf::cp_async_wait<0>();
         if (tid == 0) s.ok = rf::mbar_wait(&s.landed[buf], (uint32_t)((waited >> 1) & 1), &s.abort, rf::kErrGdnWait);
         __syncthreads();
         if (!s.ok) break;
@@ -331,37 +324,47 @@ gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
         uint8_t* out = slot_ptr(p, slot, h);
         const uint32_t ktile = rf::saddr(&s.kraw[buf][0][0][0]), vtile = rf::saddr(&s.vraw[buf][0][0][0]);
 
-        /* G (inclusive cumulative log decay; zero past the chunk), beta, gamma_L. */
-        if (tid < C) {
-            float x = s.graw[buf][tid];
+        /* G (inclusive cumulative log decay; zero past the chunk) by warp 0, two rows a lane; beta; gamma_L. */
+        PrepSmem::Meta& mt = s.meta[buf];
+        if (w == 0) {
+            const float2 gg = *(const float2*)&s.graw[buf][2 * l];
+            const float pair = gg.x + gg.y;
+            float x = pair;
             for (int o = 1; o < 32; o <<= 1) {
                 const float y = __shfl_up_sync(0xffffffffu, x, o);
                 if (l >= o) x += y;
             }
-            s.G[tid] = x;
-            s.beta[tid] = s.braw[buf][tid];
+            *(float2*)&mt.G[2 * l] = make_float2(x - pair + gg.x, x);
+        } else if (w == 1) {
+            *(float2*)&mt.beta[2 * l] = *(const float2*)&s.braw[buf][2 * l];
         }
         __syncthreads();
-        if (tid >= 32 && tid < C) s.G[tid] += s.G[31];
-        __syncthreads();
-        const float gl = s.G[len - 1];
-        if (tid < 4) s.gl[tid] = tid == 0 ? __expf(gl) : 0.0f;
+        const float gl = mt.G[len - 1];
+        if (tid < 4) mt.gl[tid] = tid == 0 ? __expf(gl) : 0.0f;
+        const float* G = mt.G;
+        const float* beta = mt.beta;
 
         /* K K^T (bf16, exact inputs) and A: warp w, rows 16 (w & 3), columns 32 (w >> 2)..+32 (warps 4, 5
          * hold only blocks above the diagonal, which A does not use). */
         if (w != 4 && w != 5) {
             const int rb = 16 * (w & 3), cb = 32 * (w >> 2);
             float acc[4][4] = {};
+            uint32_t fa[2][4], fbk[2][2][4];   /* fragments of k-step ks (buffer ks & 1), the next loaded ahead */
+            rf::load_a_sw(fa[0], ktile, rb, 0);
+            rf::load_b_nk_sw(fbk[0][0], ktile, cb, 0);
+            rf::load_b_nk_sw(fbk[0][1], ktile, cb + 16, 0);
 #pragma unroll
             for (int ks = 0; ks < D / 16; ++ks) {
-                uint32_t a[4];
-                rf::load_a_sw(a, ktile, rb, 16 * ks);
+                const int cur = ks & 1, nx = cur ^ 1;
+                if (ks + 1 < D / 16) {
+                    rf::load_a_sw(fa[nx], ktile, rb, 16 * (ks + 1));
+                    rf::load_b_nk_sw(fbk[nx][0], ktile, cb, 16 * (ks + 1));
+                    rf::load_b_nk_sw(fbk[nx][1], ktile, cb + 16, 16 * (ks + 1));
+                }
 #pragma unroll
                 for (int pr = 0; pr < 2; ++pr) {
-                    uint32_t b[4];
-                    rf::load_b_nk_sw(b, ktile, cb + 16 * pr, 16 * ks);
-                    rf::mma_bf16(acc[2 * pr], a, b[0], b[1]);
-                    rf::mma_bf16(acc[2 * pr + 1], a, b[2], b[3]);
+                    rf::mma_bf16(acc[2 * pr], fa[cur], fbk[cur][pr][0], fbk[cur][pr][1]);
+                    rf::mma_bf16(acc[2 * pr + 1], fa[cur], fbk[cur][pr][2], fbk[cur][pr][3]);
                 }
             }
 #pragma unroll
@@ -372,11 +375,18 @@ gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
                     float v[2];
 #pragma unroll
                     for (int e = 0; e < 2; ++e)
-                        v[e] = (j + e < i && i < len) ? s.beta[i] * __expf(s.G[i] - s.G[j + e]) * acc[nt][2 * hr + e] : 0.0f;
+                        v[e] = (j + e < i && i < len) ? beta[i] * __expf(G[i] - G[j + e]) * acc[nt][2 * hr + e] : 0.0f;
                     *(uint32_t*)&s.l16[i][j] = rf::pack_f16(v[0], v[1]);
                     if ((i >> 4) == (j >> 4)) *(float2*)&s.a32[i >> 4][i & 15][j & 15] = make_float2(v[0], v[1]);
                 }
         }
+        /* The next item's loads, into the other buffer once the previous item's slot stores have read it. */
+        if (item + gridDim.x < items) {
+            if (tid == 0) rf::bulk_store_wait_read();
+            prep_issue(p, &kmap, &vmap, s, item + gridDim.x, buf ^ 1);
+            ++issued;
+        }
+        rf::cp_async_commit();
         __syncthreads();
 
         /* In place, 16-byte chunks at their swizzled places: k -> x1 = beta gamma k (f16) and K~ = k
@@ -388,7 +398,7 @@ gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
             const bool in = r < len;
             const uint32_t off = rf::sw128_off(r, seg * 8);
             const uint4 kr = lds128(ktile + off), vr = lds128(vtile + off);
-            const float gr = s.G[r], br = s.beta[r];
+            const float gr = G[r], br = beta[r];
             *(uint4*)(out + kSlotK + off) = scale_bf16x8_to_f16(kr, __expf(gl - gr), in);
             sts128(ktile + off, scale_bf16x8_to_f16(kr, br * __expf(gr), in));
             sts128(vtile + off, scale_bf16x8_to_f16(vr, br, in));
@@ -442,15 +452,20 @@ gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) rf::load_a(ta[ks], &s.t16[0][0], TP, rb, 16 * ks);
             float acc[8][4] = {};
+            uint32_t fw[2][4][4];   /* B fragments of column pair pr (buffer pr & 1), the next loaded ahead */
 #pragma unroll
-            for (int pr = 0; pr < 4; ++pr)
+            for (int ks = 0; ks < 4; ++ks) rf::load_b_kn_sw(fw[0][ks], ktile, 16 * ks, cb);
+#pragma unroll
+            for (int pr = 0; pr < 4; ++pr) {
+                if (pr < 3)
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) rf::load_b_kn_sw(fw[(pr + 1) & 1][ks], ktile, 16 * ks, cb + 16 * (pr + 1));
 #pragma unroll
                 for (int ks = 0; ks < 4; ++ks) {
-                    uint32_t b[4];
-                    rf::load_b_kn_sw(b, ktile, 16 * ks, cb + 16 * pr);
-                    rf::mma_f16(acc[2 * pr], ta[ks], b[0], b[1]);
-                    rf::mma_f16(acc[2 * pr + 1], ta[ks], b[2], b[3]);
+                    rf::mma_f16(acc[2 * pr], ta[ks], fw[pr & 1][ks][0], fw[pr & 1][ks][1]);
+                    rf::mma_f16(acc[2 * pr + 1], ta[ks], fw[pr & 1][ks][2], fw[pr & 1][ks][3]);
                 }
+            }
             __syncthreads();
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
@@ -462,16 +477,22 @@ gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
         /* U~^T = x2^T T^T (warp w: dv rows 16 w..+16, all 64 chunk rows), staged over x2 the same way. */
         {
             float acc[8][4] = {};
+            uint32_t fa[2][4], fu[2][4][4];   /* fragments of k-step ks (buffer ks & 1), the next loaded ahead */
+            rf::load_a_t_sw(fa[0], vtile, 0, 16 * w);
+#pragma unroll
+            for (int pr = 0; pr < 4; ++pr) rf::load_b_nk(fu[0][pr], &s.t16[0][0], TP, 16 * pr, 0);
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
-                uint32_t a[4];
-                rf::load_a_t_sw(a, vtile, 16 * ks, 16 * w);
+                const int cur = ks & 1, nx = cur ^ 1;
+                if (ks < 3) {
+                    rf::load_a_t_sw(fa[nx], vtile, 16 * (ks + 1), 16 * w);
+#pragma unroll
+                    for (int pr = 0; pr < 4; ++pr) rf::load_b_nk(fu[nx][pr], &s.t16[0][0], TP, 16 * pr, 16 * (ks + 1));
+                }
 #pragma unroll
                 for (int pr = 0; pr < 4; ++pr) {
-                    uint32_t b[4];
-                    rf::load_b_nk(b, &s.t16[0][0], TP, 16 * pr, 16 * ks);
-                    rf::mma_f16(acc[2 * pr], a, b[0], b[1]);
-                    rf::mma_f16(acc[2 * pr + 1], a, b[2], b[3]);
+                    rf::mma_f16(acc[2 * pr], fa[cur], fu[cur][pr][0], fu[cur][pr][1]);
+                    rf::mma_f16(acc[2 * pr + 1], fa[cur], fu[cur][pr][2], fu[cur][pr][3]);
                 }
             }
             __syncthreads();
@@ -487,7 +508,7 @@ gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
         if (tid == 0) {   /* W, U~^T and G|beta|gamma_L to the slot; the next issue into this buffer waits for them */
             rf::bulk_store(out + kSlotW, &s.kraw[buf][0][0][0], kTileBytes);
             rf::bulk_store(out + kSlotU, &s.vraw[buf][0][0][0], kTileBytes);
-            rf::bulk_store(out + kSlotMeta, &s.G[0], kSlotBytes - kSlotMeta);
+            rf::bulk_store(out + kSlotMeta, &mt, sizeof(mt));
             rf::bulk_store_commit();
         }
     }
@@ -603,8 +624,14 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const GdnPl
 
         /* V'^T partial over this warp's dk half: [16 dv rows] x [64 chunk rows] = S W^T. */
         float pv[8][4] = {};
+        uint32_t fb[2][4][4];   /* B fragments of k-step ks (buffer ks & 1), the next step's loaded ahead */
+#pragma unroll
+        for (int pr = 0; pr < 4; ++pr) rf::load_b_nk_sw(fb[0][pr], wtile, 16 * pr, 64 * kh);
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
+            if (ks < 3)
+#pragma unroll
+                for (int pr = 0; pr < 4; ++pr) rf::load_b_nk_sw(fb[(ks + 1) & 1][pr], wtile, 16 * pr, 64 * kh + 16 * (ks + 1));
             uint32_t a[4];
             rf::c_to_a(a, S[2 * ks], S[2 * ks + 1]);
             if (ow) {   /* output form: S0 in f16, this warp's quarter */
@@ -617,12 +644,13 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const GdnPl
             }
 #pragma unroll
             for (int pr = 0; pr < 4; ++pr) {
-                uint32_t bb[4];
-                rf::load_b_nk_sw(bb, wtile, 16 * pr, 64 * kh + 16 * ks);
-                rf::mma_f16(pv[2 * pr], a, bb[0], bb[1]);
-                rf::mma_f16(pv[2 * pr + 1], a, bb[2], bb[3]);
+                rf::mma_f16(pv[2 * pr], a, fb[ks & 1][pr][0], fb[ks & 1][pr][1]);
+                rf::mma_f16(pv[2 * pr + 1], a, fb[ks & 1][pr][2], fb[ks & 1][pr][3]);
             }
         }
+        /* K~'s first k-step, ahead of the exchange. */
+#pragma unroll
+        for (int pr = 0; pr < 4; ++pr) rf::load_b_kn_sw(fb[0][pr], kttile, 0, 64 * kh + 16 * pr);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             *(float2*)&s.part[b][w][gq][8 * j + 2 * tq] = make_float2(pv[j][0], pv[j][1]);
@@ -650,6 +678,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const GdnPl
             for (int e = 0; e < 4; ++e) S[j][e] *= gamma_l;
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
+            if (ks < 3)
+#pragma unroll
+                for (int pr = 0; pr < 4; ++pr) rf::load_b_kn_sw(fb[(ks + 1) & 1][pr], kttile, 16 * (ks + 1), 64 * kh + 16 * pr);
             uint32_t a[4];
             rf::c_to_a(a, pv[2 * ks], pv[2 * ks + 1]);
             if (ow && (ks >> 1) == kh) {   /* output form: U^T in f16 (the two dk halves hold the same V') */
@@ -662,10 +693,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const GdnPl
             }
 #pragma unroll
             for (int pr = 0; pr < 4; ++pr) {
-                uint32_t bb[4];
-                rf::load_b_kn_sw(bb, kttile, 16 * ks, 64 * kh + 16 * pr);
-                rf::mma_f16(S[2 * pr], a, bb[0], bb[1]);
-                rf::mma_f16(S[2 * pr + 1], a, bb[2], bb[3]);
+                rf::mma_f16(S[2 * pr], a, fb[ks & 1][pr][0], fb[ks & 1][pr][1]);
+                rf::mma_f16(S[2 * pr + 1], a, fb[ks & 1][pr][2], fb[ks & 1][pr][3]);
             }
         }
         __syncwarp();
