@@ -44,30 +44,17 @@ __device__ int block_sum(int v, int* scratch) {
     return t;
 }
 
-/* Exclusive prefix (in thread order) of one 0/1 flag per thread, and the block total. */
-__device__ int block_exclusive_flag(bool flag, int* scratch, int* total) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const unsigned ballot = __ballot_sync(0xffffffffu, flag);
-    const int before_in_warp = __popc(ballot & ((1u << lane) - 1u));
-    __syncthreads();
-    if (lane == 0) scratch[warp] = __popc(ballot);
-    __syncthreads();
-    int warp_base = 0, sum = 0;
-    for (int w = 0; w < kWarps; ++w) {
-        const int c = scratch[w];
-        warp_base += w < warp ? c : 0;
-        sum += c;
-    }
-    *total = sum;
-    return warp_base + before_in_warp;
-}
+constexpr int kKeyBatch = 8;     /* rows whose loads a thread issues together */
+constexpr int kHists = 16;       /* private histograms, one per two warps */
 
 __global__ void __launch_bounds__(kThreads, 1) mask_kernel(RidgeFillMask g) {
     extern __shared__ uint32_t keys[];
+    __shared__ int hist_w[kHists][256];
     __shared__ int hist[256];
     __shared__ int scratch[kWarps];
     __shared__ uint32_t s_prefix;
     __shared__ int s_remaining;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
     int64_t win[3];
     ridgefill_mask_window(g.cu_last[0], g.cu_last[1], g.b, g.n, win);   /* invalid: empty window */
@@ -91,37 +78,64 @@ __global__ void __launch_bounds__(kThreads, 1) mask_kernel(RidgeFillMask g) {
         return;
     }
 
-    /* Keys and the match count. */
+    /* Keys and the match count (rows whose token has a finite score, in both modes), kKeyBatch rows'
+     * loads issued together. */
     int matches = 0;
-    for (int j = threadIdx.x; j < w; j += kThreads) {
-        const float sc = ridgefill_mask_score(&g, from + j);
-        matches += sc > -INFINITY ? 1 : 0;
-        keys[j] = g.mode == RIDGEFILL_MODE_CLASS ? class_key(sc)
-                                                  : ridgefill_row_hash(g.seed, (uint32_t)g.positions[(from + j) * g.pos_stride]);
+    const bool cls = g.mode == RIDGEFILL_MODE_CLASS;
+    for (int j0 = threadIdx.x; j0 < w; j0 += kThreads * kKeyBatch) {
+        int32_t id[kKeyBatch], pos[kKeyBatch];
+#pragma unroll
+        for (int u = 0; u < kKeyBatch; ++u) {
+            const int j = j0 + u * kThreads;
+            id[u] = j < w ? g.tokens[from + j] : -1;
+            pos[u] = j < w && !cls ? g.positions[(from + j) * g.pos_stride] : 0;
+        }
+        float sc[kKeyBatch];
+#pragma unroll
+        for (int u = 0; u < kKeyBatch; ++u) sc[u] = id[u] >= 0 && id[u] < g.vocab ? g.score[id[u]] : -INFINITY;
+#pragma unroll
+        for (int u = 0; u < kKeyBatch; ++u) {
+            const int j = j0 + u * kThreads;
+            if (j >= w) break;
+            const float s = sc[u] > -INFINITY && sc[u] < INFINITY ? sc[u] : -INFINITY;   /* ridgefill_mask_score */
+            matches += s > -INFINITY ? 1 : 0;
+            keys[j] = cls ? class_key(s) : ridgefill_row_hash(g.seed, (uint32_t)pos[u]);
+        }
     }
     const int total_matches = block_sum(matches, scratch);
     const long long k = (long long)rint(g.share * (double)total_matches);
 
-    /* Radix select of the k-th smallest key (1-based). */
+    /* Radix select of the k-th smallest key (1-based): four 8-bit passes, each a histogram of the keys
+     * that match the threshold's known bits (private per two warps, equal bins of a warp added once). */
     if (threadIdx.x == 0) {
         s_prefix = 0;
         s_remaining = (int)k;
     }
     uint32_t known = 0;   /* bits of the threshold fixed so far */
     if (k > 0 && k <= w) {
+        int* myhist = hist_w[warp % kHists];
         for (int shift = 24; shift >= 0; shift -= 8) {
-            for (int i = threadIdx.x; i < 256; i += kThreads) hist[i] = 0;
+            for (int i = threadIdx.x; i < kHists * 256; i += kThreads) (&hist_w[0][0])[i] = 0;
             __syncthreads();
             const uint32_t prefix = s_prefix;
             const int want = s_remaining;
-            for (int j = threadIdx.x; j < w; j += kThreads) {
-                const uint32_t key = keys[j];
-                if ((key & known) == prefix) atomicAdd(&hist[(key >> shift) & 0xff], 1);
+            for (int j0 = warp * 32; j0 < w; j0 += kThreads) {   /* whole warps: match_any needs every lane */
+                const int j = j0 + lane;
+                const uint32_t key = j < w ? keys[j] : 0u;
+                const int bin = j < w && (key & known) == prefix ? (int)((key >> shift) & 0xff) : 256;
+                const unsigned same = __match_any_sync(0xffffffffu, bin);
+                if (bin < 256 && lane == __ffs(same) - 1) atomicAdd(&myhist[bin], __popc(same));
+            }
+            __syncthreads();
+            if (threadIdx.x < 256) {
+                int t = 0;
+#pragma unroll
+                for (int q = 0; q < kHists; ++q) t += hist_w[q][threadIdx.x];
+                hist[threadIdx.x] = t;
             }
             __syncthreads();
             if (threadIdx.x < 32) {
                 /* Warp 0 finds the bin holding the remaining-th key: 8 bins a lane, then a scan. */
-                const int lane = threadIdx.x;
                 int local[8], sum = 0;
                 for (int b = 0; b < 8; ++b) { local[b] = hist[lane * 8 + b]; sum += local[b]; }
                 int incl = sum;
@@ -147,25 +161,35 @@ __global__ void __launch_bounds__(kThreads, 1) mask_kernel(RidgeFillMask g) {
     __syncthreads();
     const uint32_t threshold = s_prefix;
     const int need_equal = s_remaining;   /* rows with key == threshold to keep, in row order */
+    const bool selecting = k > 0 && k <= w;
 
-    /* Decide each row in row order, 1024 rows at a time: the equal-key rank is a block prefix. */
-    int equal_before = 0;
-    for (int base = 0; base < w; base += kThreads) {
-        const int j = base + threadIdx.x;
-        const bool inside = j < w;
+    /* Decide each row in row order. Warp w owns the block of rows [w B, w B + B), walked 32 rows at a
+     * time (lane l: row + l); a row's equal-key rank is the equal keys of the blocks before its warp's
+     * (one scan over the warps) plus those before it in its block (ballots). */
+    const int B = ((w + kThreads - 1) / kThreads) * 32;
+    const int b0 = warp * B, b1 = min(w, b0 + B);
+    int equal_here = 0;
+    if (selecting)
+        for (int j = b0 + lane; j - lane < b1; j += 32)
+            equal_here += __popc(__ballot_sync(0xffffffffu, j < b1 && keys[j] == threshold));
+    if (lane == 0) scratch[warp] = equal_here;
+    __syncthreads();
+    int rank = 0;
+    for (int q = 0; q < warp; ++q) rank += scratch[q];
+    for (int j = b0 + lane; j - lane < b1; j += 32) {
+        const bool inside = j < b1;
         const uint32_t key = inside ? keys[j] : 0xffffffffu;
-        const bool equal = inside && k > 0 && k <= w && key == threshold;
-        int chunk_equal = 0;
-        const int rank = block_exclusive_flag(equal, scratch, &chunk_equal);
-        if (inside) {
-            bool kept;
-            if (k <= 0) kept = false;
-            else if (k > w) kept = g.mode == RIDGEFILL_MODE_RANDOM || key != 0xffffffffu;   /* every candidate */
-            else kept = key < threshold || (equal && equal_before + rank < need_equal);
-            if (g.mode == RIDGEFILL_MODE_CLASS && key == 0xffffffffu) kept = false;
-            g.mask[from + j] = kept ? 0 : 1;
-        }
-        equal_before += chunk_equal;
+        const bool equal = selecting && inside && key == threshold;
+        const unsigned eq = __ballot_sync(0xffffffffu, equal);
+        const int my_rank = rank + __popc(eq & ((1u << lane) - 1u));
+        rank += __popc(eq);
+        if (!inside) continue;
+        bool kept;
+        if (k <= 0) kept = false;
+        else if (k > w) kept = g.mode == RIDGEFILL_MODE_RANDOM || key != 0xffffffffu;   /* every candidate */
+        else kept = equal ? my_rank < need_equal : key < threshold;
+        if (g.mode == RIDGEFILL_MODE_CLASS && key == 0xffffffffu) kept = false;
+        g.mask[from + j] = kept ? 0 : 1;
     }
 }
 

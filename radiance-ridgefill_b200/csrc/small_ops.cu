@@ -151,9 +151,10 @@ __global__ void hazard_kernel(RidgeFillHazard g) {
 
 /* ------------------------------------------------------------------ rho_update */
 
-constexpr int kRhoHeads = 32;   /* heads per CTA (threadIdx.x) */
-constexpr int kRhoRuns = 32;    /* runs per CTA (threadIdx.y) */
+constexpr int kRhoHeads = 4;    /* heads per CTA (threadIdx.x) */
+constexpr int kRhoRuns = 256;   /* runs per CTA (threadIdx.y) */
 constexpr int kRhoCluster = 8;  /* CTAs per cluster, each a segment of the rows */
+constexpr int kRhoBatch = 8;    /* rows whose loads a thread issues together */
 
 struct Affine { float a, bn, bd; };   /* x -> a*x + b, for N and D */
 
@@ -181,13 +182,26 @@ rho_kernel(RidgeFillRho g) {
         const float rate = expf(g.a_log[h]), bias = g.dt_bias[h];
         const int64_t t0 = first + r * len;
         const int64_t t1 = min(g.n, t0 + len);
-        for (int64_t t = t0; t < t1; ++t) {
-            const int64_t at = t * g.a_pitch + h * g.a_col;
-            const float x = g.a_bf16 ? rf::bf16_bits_to_f32(((const uint16_t*)g.a)[at]) : ((const float*)g.a)[at];
-            const float e = expf(-rate * ridgefill_softplus(x + bias));
-            m.a = e * m.a;
-            m.bn = e * m.bn + (float)g.mask[t];
-            m.bd = e * m.bd + 1.0f;
+        /* Rows in batches of kRhoBatch: the batch's loads are issued together, then the recurrence runs
+         * over them in row order. */
+        for (int64_t tb = t0; tb < t1; tb += kRhoBatch) {
+            float x[kRhoBatch];
+            int32_t mk[kRhoBatch];
+#pragma unroll
+            for (int u = 0; u < kRhoBatch; ++u) {
+                const int64_t t = tb + u < t1 ? tb + u : t1 - 1;
+                const int64_t at = t * g.a_pitch + h * g.a_col;
+                x[u] = g.a_bf16 ? rf::bf16_bits_to_f32(((const uint16_t*)g.a)[at]) : ((const float*)g.a)[at];
+                mk[u] = g.mask[t];
+            }
+#pragma unroll
+            for (int u = 0; u < kRhoBatch; ++u) {
+                if (tb + u >= t1) break;
+                const float e = expf(-rate * ridgefill_softplus(x[u] + bias));
+                m.a = e * m.a;
+                m.bn = e * m.bn + (float)mk[u];
+                m.bd = e * m.bd + 1.0f;
+            }
         }
     }
     part[run][hx] = m;
