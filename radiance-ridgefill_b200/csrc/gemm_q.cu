@@ -16,7 +16,9 @@
  *               int32 accumulators in tensor memory, two 256-column buffers so a block's MMAs overlap
  *               the previous block's fold
  *   warps 2-9   epilogue: each warp owns a 32-lane quarter of the tile rows and one 128-column half;
- *               it folds each finished K block into f32 registers and stores bf16 at the tile's end
+ *               it folds each finished K block into f32 registers and, at the tile's end, writes its
+ *               32 x 128 bf16 block into its own 128-byte-swizzled staging tiles in shared memory and
+ *               stores them with two TMA tile stores (rows and columns past y's edge are clipped)
  * A K block is `group` columns: 128 for the projector folder's i8*bf16[1x128] encoding, K itself
  * for per-row / per-column scaling (one fold a tile, the int32 accumulation running over all of K).
  */
@@ -28,12 +30,14 @@
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 128;
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr int kABytes = BM * BK, kBBytes = BN * BK, kStageBytes = kABytes + kBBytes;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 32 * (2 + kEpiWarps);
-constexpr int kSmemBytes = kStages * kStageBytes + 1024 /* alignment slack */ + 256 /* barriers */;
+constexpr int kOutBox = 32 * 64 * 2;                  /* one [32 rows][64 cols] bf16 store box */
+constexpr int kStageOut = kEpiWarps * 2 * kOutBox;    /* the epilogue warps' staging tiles */
+constexpr int kSmemBytes = kStages * kStageBytes + kStageOut + 1024 /* alignment slack */ + 256 /* barriers */;
 
 /* Instruction descriptor: D s32 (bits 4-5 = 2), A and B signed int8 (bits 7-9, 10-12 = 1), both
  * K-major, N >> 3 at bit 17, M >> 4 at bit 24. */
@@ -45,12 +49,14 @@ struct GemmPlan {
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
-gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, const GemmPlan p) {
+gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+              const __grid_constant__ CUtensorMap map_y, const GemmPlan p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* tile_a = smem;
     uint8_t* tile_b = smem + kStages * kABytes;
-    uint64_t* full = (uint64_t*)(smem + kStages * kStageBytes);
+    uint8_t* stage_out = smem + kStages * kStageBytes;   /* 1024-byte aligned: kStageBytes is */
+    uint64_t* full = (uint64_t*)(stage_out + kStageOut);
     uint64_t* empty = full + kStages;
     uint64_t* acc_full = empty + kStages;
     uint64_t* acc_empty = acc_full + 2;
@@ -71,6 +77,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
         rf::mbar_init_fence();
         rf::tma_prefetch_map(&map_a);
         rf::tma_prefetch_map(&map_b);
+        rf::tma_prefetch_map(&map_y);
     }
     if (warp == 1) rf::tmem_alloc<kTmemCols>(tmem_slot);
     rf::tc_fence_before();
@@ -186,31 +193,41 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
                 if (lane == 0) rf::mbar_arrive(&acc_empty[buf]);
             }
             if (!ok) break;
-            if (row_live) {
-                uint16_t* yrow = g.y + m * g.ldy;
+            /* bf16 (and the bias) into this warp's staging tiles, once the previous tile's stores have read them. */
+            uint8_t* stg = stage_out + (warp - 2) * 2 * kOutBox;
+            if (lane == 0) rf::bulk_store_wait_read();
+            __syncwarp();
 #pragma unroll
-                for (int v = 0; v < 16; ++v) {
-                    const int64_t n = n0 + v * 8;
-                    if (n >= g.N) break;
-                    uint32_t o[4];
+            for (int v = 0; v < 16; ++v) {
+                const int64_t n = n0 + v * 8;
+                uint32_t o[4];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        o[e] = (uint32_t)rf::f32_to_bf16_bits(acc[v * 8 + 2 * e]) |
-                               ((uint32_t)rf::f32_to_bf16_bits(acc[v * 8 + 2 * e + 1]) << 16);
-                    if (g.bias) {
-                        const uint4 bv = __ldg((const uint4*)(g.bias + n));
-                        const uint32_t bw[4] = { bv.x, bv.y, bv.z, bv.w };
+                for (int e = 0; e < 4; ++e)
+                    o[e] = (uint32_t)rf::f32_to_bf16_bits(acc[v * 8 + 2 * e]) |
+                           ((uint32_t)rf::f32_to_bf16_bits(acc[v * 8 + 2 * e + 1]) << 16);
+                if (g.bias && n < g.N) {
+                    const uint4 bv = __ldg((const uint4*)(g.bias + n));
+                    const uint32_t bw[4] = { bv.x, bv.y, bv.z, bv.w };
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float lo = __fadd_rn(__uint_as_float(o[e] << 16), __uint_as_float(bw[e] << 16));
-                            const float hi = __fadd_rn(__uint_as_float(o[e] & 0xffff0000u), __uint_as_float(bw[e] & 0xffff0000u));
-                            o[e] = (uint32_t)rf::f32_to_bf16_bits(lo) | ((uint32_t)rf::f32_to_bf16_bits(hi) << 16);
-                        }
+                    for (int e = 0; e < 4; ++e) {
+                        const float lo = __fadd_rn(__uint_as_float(o[e] << 16), __uint_as_float(bw[e] << 16));
+                        const float hi = __fadd_rn(__uint_as_float(o[e] & 0xffff0000u), __uint_as_float(bw[e] & 0xffff0000u));
+                        o[e] = (uint32_t)rf::f32_to_bf16_bits(lo) | ((uint32_t)rf::f32_to_bf16_bits(hi) << 16);
                     }
-                    *(uint4*)(yrow + n) = make_uint4(o[0], o[1], o[2], o[3]);
                 }
+                /* box v >> 3, row lane, 16-byte chunk (v & 7) at its 128-byte-swizzled place */
+                *(uint4*)(stg + (v >> 3) * kOutBox + lane * 128 + (((v & 7) ^ (lane & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+            rf::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                const int32_t y0 = (int32_t)((tile / p.n_tiles) * BM + quarter * 32);
+                rf::tma_store_2d(&map_y, stg, (int32_t)n0, y0);
+                rf::tma_store_2d(&map_y, stg + kOutBox, (int32_t)(n0 + 64), y0);
+                rf::bulk_store_commit();
             }
         }
+        if (lane == 0) rf::bulk_store_wait();   /* the tile stores are complete before the CTA leaves */
     }
 
     rf::tc_fence_before();
@@ -275,6 +292,19 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
+/* y bf16 [M, N] with row pitch `pitch` elements, written in [32 rows][64 cols] boxes from 128-byte-swizzled
+ * shared memory. */
+bool bf16_store_map(CUtensorMap* map, void* base, int64_t rows, int64_t cols, int64_t pitch) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = { (cuuint64_t)cols, (cuuint64_t)rows };
+    const cuuint64_t strides[1] = { (cuuint64_t)pitch * 2 };
+    const cuuint32_t box[2] = { 64, 32 };
+    const cuuint32_t estr[2] = { 1, 1 };
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 /* A [rows, cols] int8 matrix with row pitch `pitch` bytes, read in [box_rows, 128] tiles with 128-byte
  * swizzle; rows past the end read as zero. */
 bool int8_tile_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t pitch, uint32_t box_rows) {
@@ -292,8 +322,9 @@ bool int8_tile_map(CUtensorMap* map, const void* base, int64_t rows, int64_t col
 int launch_gemm(const RidgeFillGemmQ& g, cudaStream_t stream) {
     if (g.M == 0) return RAD_OK;
     if (g.M > 0x7fffffffLL || g.N > 0x7fffffffLL || g.K > 0x7fffffffLL) return RAD_E_SHAPE;
-    CUtensorMap map_a, map_b;
-    if (!int8_tile_map(&map_a, g.a, g.M, g.K, g.lda, BM) || !int8_tile_map(&map_b, g.b, g.N, g.K, g.ldb, BN))
+    CUtensorMap map_a, map_b, map_y;
+    if (!int8_tile_map(&map_a, g.a, g.M, g.K, g.lda, BM) || !int8_tile_map(&map_b, g.b, g.N, g.K, g.ldb, BN) ||
+        !bf16_store_map(&map_y, g.y, g.M, g.N, g.ldy))
         return RAD_E_DEVICE;
     GemmPlan p;
     p.g = g;
@@ -306,7 +337,7 @@ int launch_gemm(const RidgeFillGemmQ& g, cudaStream_t stream) {
     if (cudaFuncSetAttribute(gemm_q_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
         return RAD_E_DEVICE;
     const int grid = p.tiles < rf::sm_count() ? p.tiles : rf::sm_count();
-    gemm_q_kernel<<<grid, kThreads, kSmemBytes, stream>>>(map_a, map_b, p);
+    gemm_q_kernel<<<grid, kThreads, kSmemBytes, stream>>>(map_a, map_b, map_y, p);
     return rf::launch_status();
 }
 

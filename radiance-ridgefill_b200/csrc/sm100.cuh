@@ -123,6 +123,15 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                  : "memory");
 }
 
+/* 2-D TMA tile store from shared memory (the tensor map's box and swizzle), in the current bulk group;
+ * rows and columns outside the tensor are not written. The writers of the source make it visible first
+ * (fence_proxy_async_smem). */
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int32_t x, int32_t y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                 ::"l"((uint64_t)map), "r"(smem_addr(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+
 /* Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from shared to global memory
  * in the current bulk group. The writers of the source make it visible first (fence_proxy_async_smem,
  * then a barrier); bulk_store_commit closes the group. */
