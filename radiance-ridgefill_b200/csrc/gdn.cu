@@ -50,8 +50,9 @@ constexpr int PP = C + 8;      /* pitch of the f32 exchange tiles (float2 stores
 constexpr int kStages = 4;     /* phase 2: chunks in flight */
 
 /* A chunk's scratch slot, per (chunk, v-head), f16 tiles in the 128-byte-swizzled layout of sw128_off:
- * W [64 rows][128 dk] and K~ [64][128] (two 64-column halves each), U~^T [128 dv][64 rows] (dv slice s of
- * phase 2 at 4096 s), then G f32 [64], beta f32 [64] and gamma_L (16 bytes). */
+ * W [64 rows][128 dk] (two 64-column halves), K~^T [128 dk][64 rows] and U~^T [128 dv][64 rows] (dv slice s
+ * of phase 2 at 4096 s), then G f32 [64], beta f32 [64] and gamma_L (16 bytes). Every tile is K-major for
+ * the chain's products (its rows are the products' M or N). */
 constexpr int kSlotW = 0, kSlotK = 16384, kSlotU = 32768, kSlotMeta = 49152, kSlotGl = kSlotMeta + 512;
 constexpr int kSlotBytes = kSlotGl + 16;
 constexpr uint32_t kTileBytes = C * D * 2;   /* one [64][128] b16 tile, and one TMA pair of [64][64] boxes */
@@ -389,19 +390,31 @@ gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
         rf::cp_async_commit();
         __syncthreads();
 
-        /* In place, 16-byte chunks at their swizzled places: k -> x1 = beta gamma k (f16) and K~ = k
-         * exp(G_L - G) (f16, to the slot); v -> x2 = beta v (f16); rows past the chunk zero. The blocks of
-         * T above the diagonal zero. */
-#pragma unroll
-        for (int it = 0; it < 4; ++it) {
-            const int r = (tid >> 4) + 16 * it, seg = tid & 15;
+        /* In place, 16-byte chunks at their swizzled places: k -> x1 = beta gamma k (f16); v -> x2 = beta v
+         * (f16); and K~^T (K~ = k exp(G_L - G), f16) to the slot, transposed: lane l of warp w holds row
+         * 32 (w & 1) + l, so each 2-byte store of a warp fills 64 contiguous bytes of one K~^T row. Rows past
+         * the chunk zero. The blocks of T above the diagonal zero. */
+        {
+            const int r = 32 * (w & 1) + l;
             const bool in = r < len;
-            const uint32_t off = rf::sw128_off(r, seg * 8);
-            const uint4 kr = lds128(ktile + off), vr = lds128(vtile + off);
             const float gr = G[r], br = beta[r];
-            *(uint4*)(out + kSlotK + off) = scale_bf16x8_to_f16(kr, __expf(gl - gr), in);
-            sts128(ktile + off, scale_bf16x8_to_f16(kr, br * __expf(gr), in));
-            sts128(vtile + off, scale_bf16x8_to_f16(vr, br, in));
+            const float fk = in ? __expf(gl - gr) : 0.0f, fx = in ? br * __expf(gr) : 0.0f;
+            uint16_t* kt = (uint16_t*)(out + kSlotK);
+#pragma unroll
+            for (int it = 0; it < 4; ++it) {
+                const int seg = (w >> 1) + 4 * it;
+                const uint32_t off = rf::sw128_off(r, seg * 8);
+                const uint4 kr = lds128(ktile + off), vr = lds128(vtile + off);
+                const uint32_t rw[4] = { kr.x, kr.y, kr.z, kr.w };
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const uint32_t pk = in ? rf::pack_f16(fk * __uint_as_float(rw[e] << 16), fk * __uint_as_float(rw[e] & 0xffff0000u)) : 0u;
+                    kt[rf::sw128_off(seg * 8 + 2 * e, r, 0) >> 1] = (uint16_t)pk;
+                    kt[rf::sw128_off(seg * 8 + 2 * e + 1, r, 0) >> 1] = (uint16_t)(pk >> 16);
+                }
+                sts128(ktile + off, scale_bf16x8_to_f16(kr, fx, in));
+                sts128(vtile + off, scale_bf16x8_to_f16(vr, br, in));
+            }
         }
         for (int i = tid; i < 6 * 16 * 8; i += kPrepThreads) {   /* blocks (0,1) (0,2) (0,3) (1,2) (1,3) (2,3) */
             const int blk = i >> 7, r = (i >> 3) & 15, cp = i & 7;
@@ -648,9 +661,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const GdnPl
                 rf::mma_f16(pv[2 * pr + 1], a, fb[ks & 1][pr][2], fb[ks & 1][pr][3]);
             }
         }
-        /* K~'s first k-step, ahead of the exchange. */
+        /* K~'s first k-step, ahead of the exchange (K~^T [dk][rows]: B[k = row][n = dk]). */
 #pragma unroll
-        for (int pr = 0; pr < 4; ++pr) rf::load_b_kn_sw(fb[0][pr], kttile, 0, 64 * kh + 16 * pr);
+        for (int pr = 0; pr < 4; ++pr) rf::load_b_nk_sw(fb[0][pr], kttile, 64 * kh + 16 * pr, 0);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             *(float2*)&s.part[b][w][gq][8 * j + 2 * tq] = make_float2(pv[j][0], pv[j][1]);
@@ -680,7 +693,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const GdnPl
         for (int ks = 0; ks < 4; ++ks) {
             if (ks < 3)
 #pragma unroll
-                for (int pr = 0; pr < 4; ++pr) rf::load_b_kn_sw(fb[(ks + 1) & 1][pr], kttile, 16 * (ks + 1), 64 * kh + 16 * pr);
+                for (int pr = 0; pr < 4; ++pr) rf::load_b_nk_sw(fb[(ks + 1) & 1][pr], kttile, 64 * kh + 16 * pr, 16 * (ks + 1));
             uint32_t a[4];
             rf::c_to_a(a, pv[2 * ks], pv[2 * ks + 1]);
             if (ow && (ks >> 1) == kh) {   /* output form: U^T in f16 (the two dk halves hold the same V') */
