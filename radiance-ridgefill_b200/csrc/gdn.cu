@@ -723,6 +723,243 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const GdnPl
         }
 }
 
+/* ------------------------------------------------------------------ phase 2 on tensor memory (state-only form) */
+
+/* One CTA per (v-head, sequence): the whole 128 x 128 state in tensor memory, the chunk's two products as
+ * tcgen05.mma (kind::f16, f32 accumulation, every operand K-major in 128-byte-swizzled shared memory):
+ *     D1 = S W^T           (M 128 dv, N 64 chunk rows, K 128 dk)      eight K-16 steps
+ *     D2 += V'^T K~        (M 128 dv, N 128 dk, K 64 chunk rows)      four K-16 steps, D2 = gamma_L S before
+ * Roles, handing over through mbarriers only (every wait bounded):
+ *   warps 0-7   tensor-memory lane quarter w & 3 (dv rows 32 (w & 3)..+32), column half w >> 2; a thread is
+ *               one dv row: V' = U~ - D1 in f16 (the second product's A), then the next chunk's f16 state
+ *               (the first product's A) and gamma_L(next) S back into D2
+ *   warp 8      lane 0 keeps three chunks' inputs in flight (bulk copies of the slot's W|K~^T, U~^T, gamma_L)
+ *   warp 9      lane 0 issues the products as their operands are ready */
+constexpr int kTcEpi = 8, kTcThreads = 32 * (kTcEpi + 2), kTcStages = 3;
+constexpr uint32_t kTmemTc = 256;   /* D1 at column 0 (64 columns), D2 at column 128 (128 columns) */
+/* Instruction descriptors, kind::f16: D f32 (bit 4), A and B f16, both K-major, N >> 3 at bit 17, M >> 4 at 24. */
+constexpr uint32_t kIdescPv = (1u << 4) | ((uint32_t)(64 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+constexpr uint32_t kIdescUp = (1u << 4) | ((uint32_t)(128 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+
+struct TcStage {
+    uint16_t w[2][C][C];       /* W [64 rows][128 dk]: two 64-column halves */
+    uint16_t kt[D][C];         /* K~^T [128 dk][64 rows] */
+    uint16_t u[D][C];          /* U~^T [128 dv][64 rows] */
+    float gl[256];             /* gamma_L (first word); the stage padded to 1024 bytes */
+};
+
+struct TcSmem {
+    uint16_t a_s[2][D][C];     /* the state in f16, [128 dv][128 dk]: two 64-column halves (first product's A) */
+    uint16_t a_v[D][C];        /* V'^T in f16, [128 dv][64 rows] (second product's A) */
+    TcStage st[kTcStages];
+    uint64_t landed[kTcStages], consumed[kTcStages];
+    uint64_t d1_full, d2_full;           /* a product completed (tcgen05.commit) */
+    uint64_t as_ready, av_ready, d2_ready; /* the lanes wrote A_S / A_V / gamma S into D2 (one arrival a warp) */
+    uint32_t tmem;
+    int abort;
+};
+/* the hardware swizzles by shared-memory address bits: every tile starts on 1024 bytes */
+static_assert(offsetof(TcSmem, a_v) % 1024 == 0 && offsetof(TcSmem, st) % 1024 == 0 && sizeof(TcStage) % 1024 == 0,
+              "tile alignment");
+
+__global__ void __launch_bounds__(kTcThreads, 1) gdn_chain_tc_kernel(const GdnPlan p) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    TcSmem& s = *(TcSmem*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const RidgeFillGdn& g = p.g;
+    const int64_t h = blockIdx.x, seq = blockIdx.y;
+    const int64_t state_slot = g.state_idx[seq * g.idx_pitch];
+    if (state_slot < 0 || state_slot >= g.n_states) return;
+    const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+    const int n = (int)g.n_seq;
+    const int64_t r0 = p.tab[seq], r1 = p.tab[n + seq], base = p.tab[2 * n + seq];
+    const int64_t chunks = max((int64_t)0, min((r1 - r0 + C - 1) / C, (int64_t)p.max_slots - base));
+    if (chunks == 0) return;
+
+    if (tid == 0) {
+        for (int b = 0; b < kTcStages; ++b) {
+            rf::mbar_init(&s.landed[b], 1);
+            rf::mbar_init(&s.consumed[b], 1);
+        }
+        rf::mbar_init(&s.d1_full, 1);
+        rf::mbar_init(&s.d2_full, 1);
+        rf::mbar_init(&s.as_ready, kTcEpi);
+        rf::mbar_init(&s.av_ready, kTcEpi);
+        rf::mbar_init(&s.d2_ready, kTcEpi);
+        s.abort = 0;
+        rf::mbar_init_fence();
+    }
+    if (w == 0) rf::tmem_alloc<kTmemTc>(&s.tmem);
+    rf::tc_fence_before();
+    __syncthreads();
+    rf::tc_fence_after();
+    const uint32_t tmem = s.tmem;
+    volatile int* abort = &s.abort;
+    const uint32_t a_s = rf::saddr(&s.a_s[0][0][0]), a_v = rf::saddr(&s.a_v[0][0]);
+
+    if (w == kTcEpi) {
+        /* ------------------------------------------------------------ the loader (one lane) */
+        if (l == 0) {
+            int64_t issued = 0;
+            for (int64_t c = 0; c < chunks; ++c) {
+                const int st = (int)(c % kTcStages);
+                if (c >= kTcStages && !rf::mbar_wait(&s.consumed[st], (uint32_t)((c / kTcStages - 1) & 1), abort, rf::kErrGdnWait))
+                    break;
+                const uint8_t* src = slot_ptr(p, base + c, h);
+                TcStage& sg = s.st[st];
+                rf::mbar_arrive_expect_tx(&s.landed[st], 3 * kTileBytes + 16);
+                rf::bulk_load(&sg.w[0][0][0], src + kSlotW, 2 * kTileBytes, &s.landed[st]);   /* W and K~^T */
+                rf::bulk_load(&sg.u[0][0], src + kSlotU, kTileBytes, &s.landed[st]);
+                rf::bulk_load(&sg.gl[0], src + kSlotGl, 16, &s.landed[st]);
+                ++issued;
+            }
+            /* the copies still in flight land before the CTA leaves (bounded) */
+            for (int64_t i = issued > kTcStages ? issued - kTcStages : 0; i < issued; ++i) {
+                const uint64_t t0 = rf::global_ns();
+                while (!rf::mbar_try_wait(&s.landed[i % kTcStages], (uint32_t)((i / kTcStages) & 1)) &&
+                       rf::global_ns() - t0 < rf::kWaitTimeoutNs) {
+                }
+            }
+        }
+    } else if (w == kTcEpi + 1) {
+        /* ------------------------------------------------------------ the product issuer (one lane) */
+        if (l == 0) {
+            for (int64_t c = 0; c < chunks; ++c) {
+                const int st = (int)(c % kTcStages);
+                const uint32_t par = (uint32_t)(c & 1);
+                const uint32_t wt = rf::saddr(&s.st[st].w[0][0][0]), kt = rf::saddr(&s.st[st].kt[0][0]);
+                /* D1 = S W^T: the chunk's inputs landed and the lanes wrote this chunk's f16 state */
+                if (!rf::mbar_wait(&s.landed[st], (uint32_t)((c / kTcStages) & 1), abort, rf::kErrGdnWait) ||
+                    !rf::mbar_wait(&s.as_ready, par, abort, rf::kErrGdnWait))
+                    break;
+                rf::tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    rf::umma_f16(tmem, rf::sw128_kmajor_desc(a_s + (k >> 2) * 16384 + (k & 3) * 32),
+                                 rf::sw128_kmajor_desc(wt + (k >> 2) * 8192 + (k & 3) * 32), kIdescPv, k > 0);
+                rf::mma_commit(&s.d1_full);
+                /* D2 += V'^T K~: the lanes wrote V' and put gamma_L S into D2 */
+                if (!rf::mbar_wait(&s.av_ready, par, abort, rf::kErrGdnWait) || !rf::mbar_wait(&s.d2_ready, par, abort, rf::kErrGdnWait))
+                    break;
+                rf::tc_fence_after();
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    rf::umma_f16(tmem + 128, rf::sw128_kmajor_desc(a_v + k * 32), rf::sw128_kmajor_desc(kt + k * 32), kIdescUp, 1);
+                rf::mma_commit(&s.consumed[st]);   /* the stage is free once these products have read it */
+                rf::mma_commit(&s.d2_full);
+            }
+        }
+    } else {
+        /* ------------------------------------------------------------ the lanes (warps 0-7) */
+        const int q = w & 3, ch = w >> 2, i = 32 * q + l;   /* dv row i; columns of half ch */
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+        const uint32_t d1 = lane_base + 32 * ch, d2 = lane_base + 128 + 64 * ch;
+        float* srow = g.state + state_slot * g.st_slot + h * g.st_head + (int64_t)i * D + 64 * ch;
+        auto arrive = [&](uint64_t* bar) {   /* this warp's writes are done: one arrival a warp */
+            __syncwarp();
+            if (l == 0) rf::mbar_arrive(bar);
+        };
+        /* f16 state into the first product's A (columns 64 ch..+64 of row i) */
+        auto put_as = [&](const uint32_t (&r)[2][32]) {
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    uint32_t o[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) o[e] = rf::pack_f16(__uint_as_float(r[hf][8 * j + 2 * e]), __uint_as_float(r[hf][8 * j + 2 * e + 1]));
+                    sts128(a_s + ch * 16384 + rf::sw128_off(i, 32 * hf + 8 * j, 0), make_uint4(o[0], o[1], o[2], o[3]));
+                }
+            rf::fence_proxy_async_smem();
+        };
+        /* gamma * S into D2 */
+        auto put_d2 = [&](uint32_t (&r)[2][32], float gam) {
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+                for (int e = 0; e < 32; ++e) r[hf][e] = __float_as_uint(gam * __uint_as_float(r[hf][e]));
+                rf::tmem_st32(d2 + 32 * hf, r[hf]);
+            }
+            rf::tmem_st_wait();
+            rf::tc_fence_before();
+        };
+
+        uint32_t r[2][32];
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float4 x = *(const float4*)(srow + 32 * hf + 4 * j);
+                r[hf][4 * j] = __float_as_uint(x.x);
+                r[hf][4 * j + 1] = __float_as_uint(x.y);
+                r[hf][4 * j + 2] = __float_as_uint(x.z);
+                r[hf][4 * j + 3] = __float_as_uint(x.w);
+            }
+        put_as(r);
+        arrive(&s.as_ready);
+        bool ok = rf::mbar_wait(&s.landed[0], 0, abort, rf::kErrGdnWait);
+        if (ok) {
+            put_d2(r, s.st[0].gl[0]);
+            arrive(&s.d2_ready);
+        }
+        for (int64_t c = 0; c < chunks && ok; ++c) {
+            const uint32_t par = (uint32_t)(c & 1);
+            const uint32_t ut = rf::saddr(&s.st[c % kTcStages].u[0][0]);
+            /* V' = U~ - D1 for rows 32 ch..+32 of the chunk, f16 into the second product's A */
+            if (!(ok = rf::mbar_wait(&s.d1_full, par, abort, rf::kErrGdnWait))) break;
+            rf::tc_fence_after();
+            {
+                uint32_t d[32];
+                rf::tmem_ld32(d1, d);
+                rf::tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t off = rf::sw128_off(i, 32 * ch + 8 * j, 0);
+                    const uint4 uu = lds128(ut + off);
+                    const uint32_t uw[4] = { uu.x, uu.y, uu.z, uu.w };
+                    uint32_t o[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 uf = __half22float2(*(const __half2*)&uw[e]);
+                        o[e] = rf::pack_f16(uf.x - __uint_as_float(d[8 * j + 2 * e]), uf.y - __uint_as_float(d[8 * j + 2 * e + 1]));
+                    }
+                    sts128(a_v + off, make_uint4(o[0], o[1], o[2], o[3]));
+                }
+            }
+            rf::fence_proxy_async_smem();
+            rf::tc_fence_before();
+            arrive(&s.av_ready);
+            /* the updated state: the next chunk's f16 state first (its first product waits on it), then
+             * gamma_L(next) S into D2; the final state to memory */
+            if (!(ok = rf::mbar_wait(&s.d2_full, par, abort, rf::kErrGdnWait))) break;
+            rf::tc_fence_after();
+            rf::tmem_ld32(d2, r[0]);
+            rf::tmem_ld32(d2 + 32, r[1]);
+            rf::tmem_ld_wait();
+            if (c + 1 == chunks) {
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        *(float4*)(srow + 32 * hf + 4 * j) = make_float4(__uint_as_float(r[hf][4 * j]), __uint_as_float(r[hf][4 * j + 1]),
+                                                                         __uint_as_float(r[hf][4 * j + 2]), __uint_as_float(r[hf][4 * j + 3]));
+                break;
+            }
+            put_as(r);
+            arrive(&s.as_ready);
+            const int nst = (int)((c + 1) % kTcStages);
+            if (!(ok = rf::mbar_wait(&s.landed[nst], (uint32_t)(((c + 1) / kTcStages) & 1), abort, rf::kErrGdnWait))) break;
+            put_d2(r, s.st[nst].gl[0]);
+            arrive(&s.d2_ready);
+        }
+    }
+    rf::tc_fence_before();
+    __syncthreads();
+    if (w == 0) {
+        rf::tc_fence_after();
+        rf::tmem_free<kTmemTc>(tmem);
+    }
+}
+
 /* ------------------------------------------------------------------ output (o present) */
 
 /* o_i = scale * S_i q_i over a chunk, from its start state S0 and corrected values U:
@@ -958,8 +1195,14 @@ extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
     const int64_t grid1 = items < 2LL * rf::sm_count() ? items : 2LL * rf::sm_count();
     gdn_prep_kernel<<<(unsigned)grid1, kPrepThreads, smem1, stream>>>(kmap, vmap, p);
     if (cudaGetLastError() != cudaSuccess) return RAD_E_DEVICE;
+    if (!g.o) {   /* the state-only form: the chain on tensor memory */
+        const int smem_tc = (int)sizeof(TcSmem) + 1024;
+        if (cudaFuncSetAttribute(gdn_chain_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_tc) != cudaSuccess)
+            return RAD_E_DEVICE;
+        gdn_chain_tc_kernel<<<dim3((unsigned)g.n_head_v, (unsigned)g.n_seq), kTcThreads, smem_tc, stream>>>(p);
+        return rf::launch_status();
+    }
     gdn_chain_kernel<<<dim3(D / VS, (unsigned)g.n_head_v, (unsigned)g.n_seq), kChainThreads, smem2, stream>>>(p);
-    if (!g.o) return rf::launch_status();
     if (cudaGetLastError() != cudaSuccess) return RAD_E_DEVICE;
     gdn_out_kernel<<<(unsigned)grid1, kOutThreads, smem3, stream>>>(qmap, kmap, p);
     return rf::launch_status();
