@@ -57,11 +57,18 @@ constexpr int kSlotW = 0, kSlotK = 16384, kSlotU = 32768, kSlotMeta = 49152, kSl
 constexpr int kSlotBytes = kSlotGl + 16;
 constexpr uint32_t kTileBytes = C * D * 2;   /* one [64][128] b16 tile, and one TMA pair of [64][64] boxes */
 
-enum { kBarChain = 1, kBarPair0 = 2 };   /* named barriers (0 is __syncthreads) */
+enum { kBarChain = 1, kBarPair0 = 2 };   /* named barriers of the output form's chain (0 is __syncthreads) */
 
-/* The scratch: the sequence table (int32 r0[n], r1[n], base[n + 1], padded to 256 bytes), then the
- * chunk slots. base[i] is the number of chunks before sequence i, capped at max_slots. */
+/* The scratch: the sequence table (int32 r0[n], r1[n], base[n + 1]; base[i] is the number of chunks before
+ * sequence i, capped at max_slots), the work counter, one ready flag per chunk slot and v-head, then the
+ * chunk slots; each part padded to 256 bytes. */
 int64_t table_bytes(int64_t n_seq) { return (3 * n_seq + 1) * 4 + 255 & ~(int64_t)255; }
+constexpr int64_t kCtlBytes = 256;
+int64_t flag_bytes(int64_t items) { return items * 4 + 255 & ~(int64_t)255; }
+
+struct FillCtl {
+    int next_item;    /* the transform's next (chunk slot, v-head) item */
+};
 
 /* Output form only: per (chunk slot, v-head), the state at the chunk's start S0 f16 [dv][SP] and the
  * corrected values U^T f16 [dv][TP] (rows of the chunk along the pitch), written by phase 2 for the
@@ -72,6 +79,8 @@ constexpr int kOutS0 = 0, kOutU = D * SP * 2, kOutBytes = kOutU + D * TP * 2;
 struct GdnPlan {
     RidgeFillGdn g;
     int32_t* tab;     /* the sequence table */
+    FillCtl* ctl;     /* the work counter (zeroed by the plan kernel) */
+    int* flags;       /* item i's slot is written (1) or not yet (0); zeroed by the plan kernel */
     uint8_t* slots;   /* the chunk slots */
     uint8_t* outws;   /* output form: S0 and U^T per chunk slot and v-head; null for the state-only fill */
     int max_slots;
@@ -133,7 +142,11 @@ __global__ void __launch_bounds__(kPlanThreads) gdn_plan_kernel(const GdnPlan p)
     int32_t* r0t = p.tab;
     int32_t* r1t = p.tab + n;
     int32_t* bt = p.tab + 2 * n;
-    if (threadIdx.x == 0) carry = 0;
+    if (threadIdx.x == 0) {
+        carry = 0;
+        p.ctl->next_item = 0;
+    }
+    for (int64_t i = threadIdx.x; i < (int64_t)p.max_slots * g.n_head_v; i += kPlanThreads) p.flags[i] = 0;
     __syncthreads();
     for (int i0 = 0; i0 < n; i0 += kPlanThreads) {
         const int i = i0 + threadIdx.x;
@@ -189,7 +202,7 @@ struct PrepSmem {
     uint16_t tmp[3][16][24];     /* per-warp 16x16 staging */
     int32_t r0[kSeqCache], base[kSeqCache + 1];
     uint64_t landed[2];          /* the k and v rows of buffer b have landed */
-    int abort, ok, n_cached;
+    int abort, ok, n_cached, claim;
 };
 static_assert(offsetof(PrepSmem, vraw) % 1024 == 0, "TMA 128-byte swizzle destinations");
 static_assert(sizeof(PrepSmem::Meta) == kSlotBytes - kSlotMeta && offsetof(PrepSmem, meta) % 16 == 0, "the slot's meta, one bulk store");
@@ -263,33 +276,43 @@ __device__ void tri_offdiag_block(PrepSmem& s, int bi, int bj, int w) {
  * each, rows past the end read as zero) completing on landed[buf], and g, beta (cp.async; zero past the
  * chunk). */
 __device__ void prep_issue(const GdnPlan& p, const CUtensorMap* kmap, const CUtensorMap* vmap, PrepSmem& s, int64_t item,
-                           int buf) {
+                           int buf, int tid) {
     const RidgeFillGdn& g = p.g;
     const int64_t slot = item / g.n_head_v, h = item % g.n_head_v, hk = h / (g.n_head_v / g.n_head_k);
     int64_t row0 = 0;
     int len = 0;
     locate_chunk(p, s.r0, s.base, s.n_cached, slot, &row0, &len);
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
         rf::mbar_arrive_expect_tx(&s.landed[buf], 2 * kTileBytes);
         rf::tma_load_3d(&s.kraw[buf][0][0][0], kmap, &s.landed[buf], 0, (int)hk, (int)row0);
         rf::tma_load_3d(&s.kraw[buf][1][0][0], kmap, &s.landed[buf], C, (int)hk, (int)row0);
         rf::tma_load_3d(&s.vraw[buf][0][0][0], vmap, &s.landed[buf], 0, (int)h, (int)row0);
         rf::tma_load_3d(&s.vraw[buf][1][0][0], vmap, &s.landed[buf], C, (int)h, (int)row0);
     }
-    if (threadIdx.x < C) {
-        const int r = threadIdx.x;
+    if (tid < C) {
+        const int r = tid;
         const int64_t row = row0 + (r < len ? r : 0);
         cp_async4(&s.graw[buf][r], g.g + row * g.g_row + h, r < len ? 4 : 0);
         cp_async4(&s.braw[buf][r], g.beta + row * g.b_row + h, r < len ? 4 : 0);
     }
 }
 
-__global__ void __launch_bounds__(kPrepThreads, 2)
-gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const GdnPlan p) {
-    extern __shared__ __align__(16) uint8_t smem_raw[];
-    PrepSmem& s = *(PrepSmem*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+/* Item `it`'s slot is complete: its bulk stores have completed (the caller waited for them) and the K~^T
+ * stores of every transform thread precede a transform barrier the caller passed since; made visible at
+ * GPU scope, then flagged. One thread. */
+__device__ void publish_item(const GdnPlan& p, int64_t it) {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    __threadfence();
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p.flags + it), "r"(1) : "memory");
+}
+
+/* Phase 1 for one group of 8 warps (thread `tid` of 256, named barrier `bar`): items claimed in increasing
+ * order from the global counter, each slot flagged once it is written. It never waits on phase 2. */
+__device__ void prep_role(const CUtensorMap& kmap, const CUtensorMap& vmap, const GdnPlan& p, PrepSmem& s, const int tid,
+                          const int bar) {
     const RidgeFillGdn& g = p.g;
-    const int tid = threadIdx.x, w = tid >> 5, l = tid & 31, gq = l >> 2, tq = l & 3;
+    const int w = tid >> 5, l = tid & 31, gq = l >> 2, tq = l & 3;
+    auto sync = [&]() { bar_sync(bar, kPrepThreads); };
     const int n_seq = (int)g.n_seq;
     const int n_cached = n_seq < kSeqCache ? n_seq : kSeqCache;
     for (int i = tid; i <= n_cached; i += kPrepThreads) {
@@ -304,19 +327,24 @@ gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
         rf::mbar_init_fence();
         rf::tma_prefetch_map(&kmap);
         rf::tma_prefetch_map(&vmap);
+        s.claim = atomicAdd(&p.ctl->next_item, 1);
     }
-    __syncthreads();
+    sync();
     const int64_t items = (int64_t)p.tab[3 * n_seq] * g.n_head_v;
+    int64_t item = s.claim;
 
-    if ((int64_t)blockIdx.x < items) prep_issue(p, &kmap, &vmap, s, blockIdx.x, 0);
+    if (item < items) prep_issue(p, &kmap, &vmap, s, item, 0, tid);
     rf::cp_async_commit();
     int buf = 0;
-    int64_t waited = 0, issued = (int64_t)blockIdx.x < items ? 1 : 0;
-    for (int64_t item = blockIdx.x; item < items; item += gridDim.x, buf ^= 1) {
+    int64_t waited = 0, issued = item < items ? 1 : 0;
+    int64_t pending = -1;   /* thread 0: the item whose slot stores are issued but not yet published */
+    while (item < items) {
+        if (tid == 0) s.claim = atomicAdd(&p.ctl->next_item, 1);   /* the item after this one */
         rf::cp_async_wait<0>();
         if (tid == 0) s.ok = rf::mbar_wait(&s.landed[buf], (uint32_t)((waited >> 1) & 1), &s.abort, rf::kErrGdnWait);
-        __syncthreads();
+        sync();
         if (!s.ok) break;
+        const int64_t next = s.claim;
         ++waited;
         const int64_t slot = item / g.n_head_v, h = item % g.n_head_v;
         int64_t row0 = 0;
@@ -339,7 +367,7 @@ gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
         } else if (w == 1) {
             *(float2*)&mt.beta[2 * l] = *(const float2*)&s.braw[buf][2 * l];
         }
-        __syncthreads();
+        sync();
         const float gl = mt.G[len - 1];
         if (tid < 4) mt.gl[tid] = tid == 0 ? __expf(gl) : 0.0f;
         const float* G = mt.G;
@@ -381,14 +409,19 @@ gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
                     if ((i >> 4) == (j >> 4)) *(float2*)&s.a32[i >> 4][i & 15][j & 15] = make_float2(v[0], v[1]);
                 }
         }
-        /* The next item's loads, into the other buffer once the previous item's slot stores have read it. */
-        if (item + gridDim.x < items) {
-            if (tid == 0) rf::bulk_store_wait_read();
-            prep_issue(p, &kmap, &vmap, s, item + gridDim.x, buf ^ 1);
+        /* The previous item's slot stores are complete: publish it, and start the next item's loads into
+         * the buffer those stores read. */
+        if (tid == 0 && pending >= 0) {
+            rf::bulk_store_wait();
+            publish_item(p, pending);
+            pending = -1;
+        }
+        if (next < items) {
+            prep_issue(p, &kmap, &vmap, s, next, buf ^ 1, tid);
             ++issued;
         }
         rf::cp_async_commit();
-        __syncthreads();
+        sync();
 
         /* In place, 16-byte chunks at their swizzled places: k -> x1 = beta gamma k (f16); v -> x2 = beta v
          * (f16); and K~^T (K~ = k exp(G_L - G), f16) to the slot, transposed: lane l of warp w holds row
@@ -421,7 +454,7 @@ gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
             const int bi = blk < 3 ? 0 : blk < 5 ? 1 : 2, bj = blk < 3 ? blk + 1 : blk < 5 ? blk - 1 : 3;
             *(uint32_t*)&s.t16[16 * bi + r][16 * bj + 2 * cp] = 0u;
         }
-        __syncthreads();
+        sync();
 
         /* Diagonal blocks of T, by substitution in f32: warp w solves block w >> 1 for columns
          * 8 (w & 1)..+8, lane l holding row l & 15 of 4 columns; row j is final at step j and is
@@ -449,13 +482,13 @@ gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
                 }
             *(uint2*)&s.t16[16 * b + r][16 * b + c0] = make_uint2(rf::pack_f16(x[0], x[1]), rf::pack_f16(x[2], x[3]));
         }
-        __syncthreads();
+        sync();
         if (w < 3) tri_offdiag_block(s, w + 1, w, w);            /* T10, T21, T32 */
-        __syncthreads();
+        sync();
         if (w < 2) tri_offdiag_block(s, w + 2, w, w);            /* T20, T31 */
-        __syncthreads();
+        sync();
         if (w == 0) tri_offdiag_block(s, 3, 0, 0);               /* T30 */
-        __syncthreads();
+        sync();
 
         /* W = T x1 (warp w: rows 16 (w & 3), dk 64 (w >> 2)..+64), staged over x1 once every warp has
          * read it. */
@@ -479,7 +512,7 @@ gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
                     rf::mma_f16(acc[2 * pr + 1], ta[ks], fw[pr & 1][ks][2], fw[pr & 1][ks][3]);
                 }
             }
-            __syncthreads();
+            sync();
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const int c = cb + 8 * j + 2 * tq;
@@ -508,7 +541,7 @@ gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
                     rf::mma_f16(acc[2 * pr + 1], fa[cur], fu[cur][pr][2], fu[cur][pr][3]);
                 }
             }
-            __syncthreads();
+            sync();
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const int c = 8 * j + 2 * tq;
@@ -517,17 +550,21 @@ gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
             }
         }
         rf::fence_proxy_async_smem();
-        __syncthreads();
+        sync();
         if (tid == 0) {   /* W, U~^T and G|beta|gamma_L to the slot; the next issue into this buffer waits for them */
             rf::bulk_store(out + kSlotW, &s.kraw[buf][0][0][0], kTileBytes);
             rf::bulk_store(out + kSlotU, &s.vraw[buf][0][0][0], kTileBytes);
             rf::bulk_store(out + kSlotMeta, &mt, sizeof(mt));
             rf::bulk_store_commit();
+            pending = item;
         }
+        item = next;
+        buf ^= 1;
     }
     rf::cp_async_wait<0>();
     if (tid == 0) {
         rf::bulk_store_wait();
+        if (pending >= 0 && s.ok) publish_item(p, pending);
         /* After a timed-out wait: let the copies already issued land before the CTA's shared memory is
          * released (bounded too). */
         for (int64_t i = waited; i < issued; ++i) {
@@ -536,6 +573,12 @@ gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant_
             }
         }
     }
+}
+
+__global__ void __launch_bounds__(kPrepThreads, 2)
+gdn_prep_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const GdnPlan p) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    prep_role(kmap, vmap, p, *(PrepSmem*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023), threadIdx.x, 1);
 }
 
 /* ------------------------------------------------------------------ phase 2 */
@@ -762,19 +805,38 @@ struct TcSmem {
 static_assert(offsetof(TcSmem, a_v) % 1024 == 0 && offsetof(TcSmem, st) % 1024 == 0 && sizeof(TcStage) % 1024 == 0,
               "tile alignment");
 
-__global__ void __launch_bounds__(kTcThreads, 1) gdn_chain_tc_kernel(const GdnPlan p) {
-    extern __shared__ __align__(16) uint8_t smem_raw[];
-    TcSmem& s = *(TcSmem*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+__device__ __forceinline__ int ld_acquire(const int* ptr) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+    return v;
+}
+
+/* Wait (bounded) until item `it`'s slot is flagged written, then order the async-proxy reads that follow. */
+__device__ bool wait_item(const GdnPlan& p, int64_t it, volatile int* abort) {
+    if (ld_acquire(p.flags + it) == 0) {
+        const uint64_t t0 = rf::global_ns();
+        while (ld_acquire(p.flags + it) == 0) {
+            if (*abort) return false;
+            if (rf::global_ns() - t0 > rf::kWaitTimeoutNs) {
+                *abort = 1;
+                atomicCAS(&rf::g_device_error, 0, (int)rf::kErrGdnWait);
+                return false;
+            }
+            __nanosleep(100);
+        }
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    return true;
+}
+
+/* The chains first, first + step, ... (chain = v-head + Hv * sequence) on threads 0..kTcThreads-1 of one CTA.
+ * Every stage and hand-over index runs on across chains (k: the chunks this CTA has taken so far). */
+__device__ void chain_tc_role(const GdnPlan& p, TcSmem& s, int64_t first, int64_t step) {
     const RidgeFillGdn& g = p.g;
-    const int64_t h = blockIdx.x, seq = blockIdx.y;
-    const int64_t state_slot = g.state_idx[seq * g.idx_pitch];
-    if (state_slot < 0 || state_slot >= g.n_states) return;
     const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
     const int n = (int)g.n_seq;
-    const int64_t r0 = p.tab[seq], r1 = p.tab[n + seq], base = p.tab[2 * n + seq];
-    const int64_t chunks = max((int64_t)0, min((r1 - r0 + C - 1) / C, (int64_t)p.max_slots - base));
-    if (chunks == 0) return;
-
+    const int64_t n_chains = g.n_head_v * g.n_seq;
+    auto role_sync = [&]() { bar_sync(3, kTcThreads); };
     if (tid == 0) {
         for (int b = 0; b < kTcStages; ++b) {
             rf::mbar_init(&s.landed[b], 1);
@@ -790,173 +852,214 @@ __global__ void __launch_bounds__(kTcThreads, 1) gdn_chain_tc_kernel(const GdnPl
     }
     if (w == 0) rf::tmem_alloc<kTmemTc>(&s.tmem);
     rf::tc_fence_before();
-    __syncthreads();
+    role_sync();
     rf::tc_fence_after();
     const uint32_t tmem = s.tmem;
     volatile int* abort = &s.abort;
     const uint32_t a_s = rf::saddr(&s.a_s[0][0][0]), a_v = rf::saddr(&s.a_v[0][0]);
+    int64_t k0 = 0;          /* chunks taken by this CTA before the current chain */
+    int64_t issued = 0;      /* the loader's copies */
+    for (int64_t cid = first; cid < n_chains && !*abort; cid += step) {
+        const int64_t h = cid % g.n_head_v, seq = cid / g.n_head_v;
+        const int64_t state_slot = g.state_idx[seq * g.idx_pitch];
+        if (state_slot < 0 || state_slot >= g.n_states) continue;
+        const int64_t r0 = p.tab[seq], r1 = p.tab[n + seq], base = p.tab[2 * n + seq];
+        const int64_t chunks = max((int64_t)0, min((r1 - r0 + C - 1) / C, (int64_t)p.max_slots - base));
+        if (chunks == 0) continue;
 
-    if (w == kTcEpi) {
-        /* ------------------------------------------------------------ the loader (one lane) */
-        if (l == 0) {
-            int64_t issued = 0;
-            for (int64_t c = 0; c < chunks; ++c) {
-                const int st = (int)(c % kTcStages);
-                if (c >= kTcStages && !rf::mbar_wait(&s.consumed[st], (uint32_t)((c / kTcStages - 1) & 1), abort, rf::kErrGdnWait))
-                    break;
-                const uint8_t* src = slot_ptr(p, base + c, h);
-                TcStage& sg = s.st[st];
-                rf::mbar_arrive_expect_tx(&s.landed[st], 3 * kTileBytes + 16);
-                rf::bulk_load(&sg.w[0][0][0], src + kSlotW, 2 * kTileBytes, &s.landed[st]);   /* W and K~^T */
-                rf::bulk_load(&sg.u[0][0], src + kSlotU, kTileBytes, &s.landed[st]);
-                rf::bulk_load(&sg.gl[0], src + kSlotGl, 16, &s.landed[st]);
-                ++issued;
-            }
-            /* the copies still in flight land before the CTA leaves (bounded) */
-            for (int64_t i = issued > kTcStages ? issued - kTcStages : 0; i < issued; ++i) {
-                const uint64_t t0 = rf::global_ns();
-                while (!rf::mbar_try_wait(&s.landed[i % kTcStages], (uint32_t)((i / kTcStages) & 1)) &&
-                       rf::global_ns() - t0 < rf::kWaitTimeoutNs) {
+        if (w == kTcEpi) {
+            /* -------------------------------------------------------- the loader (one lane) */
+            if (l == 0) {
+                for (int64_t c = 0; c < chunks; ++c) {
+                    const int64_t k = k0 + c;
+                    const int st = (int)(k % kTcStages);
+                    if (k >= kTcStages && !rf::mbar_wait(&s.consumed[st], (uint32_t)((k / kTcStages - 1) & 1), abort, rf::kErrGdnWait))
+                        break;
+                    if (!wait_item(p, (base + c) * g.n_head_v + h, abort)) break;
+                    const uint8_t* src = slot_ptr(p, base + c, h);
+                    TcStage& sg = s.st[st];
+                    rf::mbar_arrive_expect_tx(&s.landed[st], 3 * kTileBytes + 16);
+                    rf::bulk_load(&sg.w[0][0][0], src + kSlotW, 2 * kTileBytes, &s.landed[st]);   /* W and K~^T */
+                    rf::bulk_load(&sg.u[0][0], src + kSlotU, kTileBytes, &s.landed[st]);
+                    rf::bulk_load(&sg.gl[0], src + kSlotGl, 16, &s.landed[st]);
+                    ++issued;
                 }
             }
-        }
-    } else if (w == kTcEpi + 1) {
-        /* ------------------------------------------------------------ the product issuer (one lane) */
-        if (l == 0) {
-            for (int64_t c = 0; c < chunks; ++c) {
-                const int st = (int)(c % kTcStages);
-                const uint32_t par = (uint32_t)(c & 1);
-                const uint32_t wt = rf::saddr(&s.st[st].w[0][0][0]), kt = rf::saddr(&s.st[st].kt[0][0]);
-                /* D1 = S W^T: the chunk's inputs landed and the lanes wrote this chunk's f16 state */
-                if (!rf::mbar_wait(&s.landed[st], (uint32_t)((c / kTcStages) & 1), abort, rf::kErrGdnWait) ||
-                    !rf::mbar_wait(&s.as_ready, par, abort, rf::kErrGdnWait))
-                    break;
-                rf::tc_fence_after();
+        } else if (w == kTcEpi + 1) {
+            /* -------------------------------------------------------- the product issuer (one lane) */
+            if (l == 0) {
+                for (int64_t c = 0; c < chunks; ++c) {
+                    const int64_t k = k0 + c;
+                    const int st = (int)(k % kTcStages);
+                    const uint32_t par = (uint32_t)(k & 1);
+                    const uint32_t wt = rf::saddr(&s.st[st].w[0][0][0]), kt = rf::saddr(&s.st[st].kt[0][0]);
+                    /* D1 = S W^T: the chunk's inputs landed and the lanes wrote this chunk's f16 state */
+                    if (!rf::mbar_wait(&s.landed[st], (uint32_t)((k / kTcStages) & 1), abort, rf::kErrGdnWait) ||
+                        !rf::mbar_wait(&s.as_ready, par, abort, rf::kErrGdnWait))
+                        break;
+                    rf::tc_fence_after();
 #pragma unroll
-                for (int k = 0; k < 8; ++k)
-                    rf::umma_f16(tmem, rf::sw128_kmajor_desc(a_s + (k >> 2) * 16384 + (k & 3) * 32),
-                                 rf::sw128_kmajor_desc(wt + (k >> 2) * 8192 + (k & 3) * 32), kIdescPv, k > 0);
-                rf::mma_commit(&s.d1_full);
-                /* D2 += V'^T K~: the lanes wrote V' and put gamma_L S into D2 */
-                if (!rf::mbar_wait(&s.av_ready, par, abort, rf::kErrGdnWait) || !rf::mbar_wait(&s.d2_ready, par, abort, rf::kErrGdnWait))
-                    break;
-                rf::tc_fence_after();
+                    for (int kk = 0; kk < 8; ++kk)
+                        rf::umma_f16(tmem, rf::sw128_kmajor_desc(a_s + (kk >> 2) * 16384 + (kk & 3) * 32),
+                                     rf::sw128_kmajor_desc(wt + (kk >> 2) * 8192 + (kk & 3) * 32), kIdescPv, kk > 0);
+                    rf::mma_commit(&s.d1_full);
+                    /* D2 += V'^T K~: the lanes wrote V' and put gamma_L S into D2 */
+                    if (!rf::mbar_wait(&s.av_ready, par, abort, rf::kErrGdnWait) ||
+                        !rf::mbar_wait(&s.d2_ready, par, abort, rf::kErrGdnWait))
+                        break;
+                    rf::tc_fence_after();
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    rf::umma_f16(tmem + 128, rf::sw128_kmajor_desc(a_v + k * 32), rf::sw128_kmajor_desc(kt + k * 32), kIdescUp, 1);
-                rf::mma_commit(&s.consumed[st]);   /* the stage is free once these products have read it */
-                rf::mma_commit(&s.d2_full);
-            }
-        }
-    } else {
-        /* ------------------------------------------------------------ the lanes (warps 0-7) */
-        const int q = w & 3, ch = w >> 2, i = 32 * q + l;   /* dv row i; columns of half ch */
-        const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-        const uint32_t d1 = lane_base + 32 * ch, d2 = lane_base + 128 + 64 * ch;
-        float* srow = g.state + state_slot * g.st_slot + h * g.st_head + (int64_t)i * D + 64 * ch;
-        auto arrive = [&](uint64_t* bar) {   /* this warp's writes are done: one arrival a warp */
-            __syncwarp();
-            if (l == 0) rf::mbar_arrive(bar);
-        };
-        /* f16 state into the first product's A (columns 64 ch..+64 of row i) */
-        auto put_as = [&](const uint32_t (&r)[2][32]) {
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    uint32_t o[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) o[e] = rf::pack_f16(__uint_as_float(r[hf][8 * j + 2 * e]), __uint_as_float(r[hf][8 * j + 2 * e + 1]));
-                    sts128(a_s + ch * 16384 + rf::sw128_off(i, 32 * hf + 8 * j, 0), make_uint4(o[0], o[1], o[2], o[3]));
-                }
-            rf::fence_proxy_async_smem();
-        };
-        /* gamma * S into D2 */
-        auto put_d2 = [&](uint32_t (&r)[2][32], float gam) {
-#pragma unroll
-            for (int hf = 0; hf < 2; ++hf) {
-#pragma unroll
-                for (int e = 0; e < 32; ++e) r[hf][e] = __float_as_uint(gam * __uint_as_float(r[hf][e]));
-                rf::tmem_st32(d2 + 32 * hf, r[hf]);
-            }
-            rf::tmem_st_wait();
-            rf::tc_fence_before();
-        };
-
-        uint32_t r[2][32];
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf)
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float4 x = *(const float4*)(srow + 32 * hf + 4 * j);
-                r[hf][4 * j] = __float_as_uint(x.x);
-                r[hf][4 * j + 1] = __float_as_uint(x.y);
-                r[hf][4 * j + 2] = __float_as_uint(x.z);
-                r[hf][4 * j + 3] = __float_as_uint(x.w);
-            }
-        put_as(r);
-        arrive(&s.as_ready);
-        bool ok = rf::mbar_wait(&s.landed[0], 0, abort, rf::kErrGdnWait);
-        if (ok) {
-            put_d2(r, s.st[0].gl[0]);
-            arrive(&s.d2_ready);
-        }
-        for (int64_t c = 0; c < chunks && ok; ++c) {
-            const uint32_t par = (uint32_t)(c & 1);
-            const uint32_t ut = rf::saddr(&s.st[c % kTcStages].u[0][0]);
-            /* V' = U~ - D1 for rows 32 ch..+32 of the chunk, f16 into the second product's A */
-            if (!(ok = rf::mbar_wait(&s.d1_full, par, abort, rf::kErrGdnWait))) break;
-            rf::tc_fence_after();
-            {
-                uint32_t d[32];
-                rf::tmem_ld32(d1, d);
-                rf::tmem_ld_wait();
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const uint32_t off = rf::sw128_off(i, 32 * ch + 8 * j, 0);
-                    const uint4 uu = lds128(ut + off);
-                    const uint32_t uw[4] = { uu.x, uu.y, uu.z, uu.w };
-                    uint32_t o[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 uf = __half22float2(*(const __half2*)&uw[e]);
-                        o[e] = rf::pack_f16(uf.x - __uint_as_float(d[8 * j + 2 * e]), uf.y - __uint_as_float(d[8 * j + 2 * e + 1]));
-                    }
-                    sts128(a_v + off, make_uint4(o[0], o[1], o[2], o[3]));
+                    for (int kk = 0; kk < 4; ++kk)
+                        rf::umma_f16(tmem + 128, rf::sw128_kmajor_desc(a_v + kk * 32), rf::sw128_kmajor_desc(kt + kk * 32), kIdescUp, 1);
+                    rf::mma_commit(&s.consumed[st]);   /* the stage is free once these products have read it */
+                    rf::mma_commit(&s.d2_full);
                 }
             }
-            rf::fence_proxy_async_smem();
-            rf::tc_fence_before();
-            arrive(&s.av_ready);
-            /* the updated state: the next chunk's f16 state first (its first product waits on it), then
-             * gamma_L(next) S into D2; the final state to memory */
-            if (!(ok = rf::mbar_wait(&s.d2_full, par, abort, rf::kErrGdnWait))) break;
-            rf::tc_fence_after();
-            rf::tmem_ld32(d2, r[0]);
-            rf::tmem_ld32(d2 + 32, r[1]);
-            rf::tmem_ld_wait();
-            if (c + 1 == chunks) {
+        } else {
+            /* -------------------------------------------------------- the lanes (warps 0-7) */
+            const int q = w & 3, ch = w >> 2, i = 32 * q + l;   /* dv row i; columns of half ch */
+            const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+            const uint32_t d1 = lane_base + 32 * ch, d2 = lane_base + 128 + 64 * ch;
+            float* srow = g.state + state_slot * g.st_slot + h * g.st_head + (int64_t)i * D + 64 * ch;
+            auto arrive = [&](uint64_t* bar) {   /* this warp's writes are done: one arrival a warp */
+                __syncwarp();
+                if (l == 0) rf::mbar_arrive(bar);
+            };
+            auto put_as = [&](const uint32_t (&r)[2][32]) {   /* f16 state into the first product's A */
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf)
 #pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        *(float4*)(srow + 32 * hf + 4 * j) = make_float4(__uint_as_float(r[hf][4 * j]), __uint_as_float(r[hf][4 * j + 1]),
-                                                                         __uint_as_float(r[hf][4 * j + 2]), __uint_as_float(r[hf][4 * j + 3]));
-                break;
-            }
+                    for (int j = 0; j < 4; ++j) {
+                        uint32_t o[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            o[e] = rf::pack_f16(__uint_as_float(r[hf][8 * j + 2 * e]), __uint_as_float(r[hf][8 * j + 2 * e + 1]));
+                        sts128(a_s + ch * 16384 + rf::sw128_off(i, 32 * hf + 8 * j, 0), make_uint4(o[0], o[1], o[2], o[3]));
+                    }
+                rf::fence_proxy_async_smem();
+            };
+            auto put_d2 = [&](uint32_t (&r)[2][32], float gam) {   /* gamma * S into D2 */
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) r[hf][e] = __float_as_uint(gam * __uint_as_float(r[hf][e]));
+                    rf::tmem_st32(d2 + 32 * hf, r[hf]);
+                }
+                rf::tmem_st_wait();
+                rf::tc_fence_before();
+            };
+
+            uint32_t r[2][32];
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float4 x = *(const float4*)(srow + 32 * hf + 4 * j);
+                    r[hf][4 * j] = __float_as_uint(x.x);
+                    r[hf][4 * j + 1] = __float_as_uint(x.y);
+                    r[hf][4 * j + 2] = __float_as_uint(x.z);
+                    r[hf][4 * j + 3] = __float_as_uint(x.w);
+                }
             put_as(r);
             arrive(&s.as_ready);
-            const int nst = (int)((c + 1) % kTcStages);
-            if (!(ok = rf::mbar_wait(&s.landed[nst], (uint32_t)(((c + 1) / kTcStages) & 1), abort, rf::kErrGdnWait))) break;
-            put_d2(r, s.st[nst].gl[0]);
-            arrive(&s.d2_ready);
+            bool ok = rf::mbar_wait(&s.landed[k0 % kTcStages], (uint32_t)((k0 / kTcStages) & 1), abort, rf::kErrGdnWait);
+            if (ok) {
+                put_d2(r, s.st[k0 % kTcStages].gl[0]);
+                arrive(&s.d2_ready);
+            }
+            for (int64_t c = 0; c < chunks && ok; ++c) {
+                const int64_t k = k0 + c;
+                const uint32_t par = (uint32_t)(k & 1);
+                const uint32_t ut = rf::saddr(&s.st[k % kTcStages].u[0][0]);
+                /* V' = U~ - D1 for rows 32 ch..+32 of the chunk, f16 into the second product's A */
+                if (!(ok = rf::mbar_wait(&s.d1_full, par, abort, rf::kErrGdnWait))) break;
+                rf::tc_fence_after();
+                {
+                    uint32_t d[32];
+                    rf::tmem_ld32(d1, d);
+                    rf::tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint32_t off = rf::sw128_off(i, 32 * ch + 8 * j, 0);
+                        const uint4 uu = lds128(ut + off);
+                        const uint32_t uw[4] = { uu.x, uu.y, uu.z, uu.w };
+                        uint32_t o[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 uf = __half22float2(*(const __half2*)&uw[e]);
+                            o[e] = rf::pack_f16(uf.x - __uint_as_float(d[8 * j + 2 * e]), uf.y - __uint_as_float(d[8 * j + 2 * e + 1]));
+                        }
+                        sts128(a_v + off, make_uint4(o[0], o[1], o[2], o[3]));
+                    }
+                }
+                rf::fence_proxy_async_smem();
+                rf::tc_fence_before();
+                arrive(&s.av_ready);
+                /* the updated state: the next chunk's f16 state first (its first product waits on it), then
+                 * gamma_L(next) S into D2; the final state to memory */
+                if (!(ok = rf::mbar_wait(&s.d2_full, par, abort, rf::kErrGdnWait))) break;
+                rf::tc_fence_after();
+                rf::tmem_ld32(d2, r[0]);
+                rf::tmem_ld32(d2 + 32, r[1]);
+                rf::tmem_ld_wait();
+                if (c + 1 == chunks) {
+#pragma unroll
+                    for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+                        for (int j = 0; j < 8; ++j)
+                            *(float4*)(srow + 32 * hf + 4 * j) = make_float4(__uint_as_float(r[hf][4 * j]), __uint_as_float(r[hf][4 * j + 1]),
+                                                                             __uint_as_float(r[hf][4 * j + 2]), __uint_as_float(r[hf][4 * j + 3]));
+                    break;
+                }
+                put_as(r);
+                arrive(&s.as_ready);
+                const int nst = (int)((k + 1) % kTcStages);
+                if (!(ok = rf::mbar_wait(&s.landed[nst], (uint32_t)(((k + 1) / kTcStages) & 1), abort, rf::kErrGdnWait))) break;
+                put_d2(r, s.st[nst].gl[0]);
+                arrive(&s.d2_ready);
+            }
+            /* D2's reads of the last chunk precede the next chain's first stores into it (a later barrier) */
+            rf::tc_fence_before();
         }
+        k0 += chunks;
+        role_sync();   /* every role is done with the chain before the next one starts */
     }
+    /* the loader's copies still in flight land before the CTA leaves (bounded) */
+    if (w == kTcEpi && l == 0)
+        for (int64_t i = issued > kTcStages ? issued - kTcStages : 0; i < issued; ++i) {
+            const uint64_t t0 = rf::global_ns();
+            while (!rf::mbar_try_wait(&s.landed[i % kTcStages], (uint32_t)((i / kTcStages) & 1)) &&
+                   rf::global_ns() - t0 < rf::kWaitTimeoutNs) {
+            }
+        }
     rf::tc_fence_before();
-    __syncthreads();
+    role_sync();
     if (w == 0) {
         rf::tc_fence_after();
         rf::tmem_free<kTmemTc>(tmem);
+    }
+}
+
+/* ------------------------------------------------------------------ the state-only fill, one kernel */
+
+/* One CTA per SM, launched cooperatively (all resident): CTAs [0, chain_ctas) run the tensor-memory chains,
+ * the others run phase 1 as two independent 8-warp groups. The chains read each chunk's slot once phase 1
+ * has flagged it; phase 1 never waits on the chains. */
+constexpr int kFusedThreads = 2 * kPrepThreads;
+constexpr int kPrepStride = (int)((sizeof(PrepSmem) + 1023) / 1024 * 1024);
+constexpr int kFusedSmem = (sizeof(TcSmem) > 2 * (size_t)kPrepStride ? (int)sizeof(TcSmem) : 2 * kPrepStride) + 1024;
+static_assert(kTcThreads <= kFusedThreads, "roles fit the block");
+
+__global__ void __launch_bounds__(kFusedThreads, 1)
+gdn_fill_fused_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const GdnPlan p,
+                      int chain_ctas) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    uint8_t* base = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    if ((int)blockIdx.x < chain_ctas) {
+        if (threadIdx.x < kTcThreads) chain_tc_role(p, *(TcSmem*)base, blockIdx.x, chain_ctas);
+    } else {
+        const int grp = threadIdx.x / kPrepThreads;
+        prep_role(kmap, vmap, p, *(PrepSmem*)(base + grp * kPrepStride), threadIdx.x % kPrepThreads, 1 + grp);
     }
 }
 
@@ -1150,8 +1253,8 @@ bool head_rows_map(CUtensorMap* map, const void* base, int64_t T, int64_t heads,
 extern "C" int64_t ridgefill_gdn_fill_scratch(const RadArgs* a) {
     RidgeFillGdn g;
     if (ridgefill_gdn_parse(a, &g) != RAD_OK) return 0;
-    const int64_t per_slot = kSlotBytes + (g.o ? kOutBytes : 0);
-    return table_bytes(g.n_seq) + max_slots_of(g) * g.n_head_v * per_slot;
+    const int64_t items = max_slots_of(g) * g.n_head_v;
+    return table_bytes(g.n_seq) + kCtlBytes + flag_bytes(items) + items * (kSlotBytes + (g.o ? kOutBytes : 0));
 }
 
 extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
@@ -1160,11 +1263,11 @@ extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
     if (rc != RAD_OK) return rc;
     if (g.n_seq == 0 || g.T == 0) return RAD_OK;
     if (g.n_seq > 65535 || g.n_head_v > 65535 || g.T > 0x7fffffffLL) return RAD_E_SHAPE;
-    const int64_t slots = max_slots_of(g);
-    const int64_t slot_bytes = slots * g.n_head_v * (int64_t)kSlotBytes;
-    const int64_t need = table_bytes(g.n_seq) + slot_bytes + (g.o ? slots * g.n_head_v * (int64_t)kOutBytes : 0);
+    const int64_t slots = max_slots_of(g), items = slots * g.n_head_v;
+    const int64_t head = table_bytes(g.n_seq) + kCtlBytes + flag_bytes(items);
+    const int64_t need = head + items * (kSlotBytes + (g.o ? kOutBytes : 0));
     if (!a->scratch || a->scratch_bytes < need || (uintptr_t)a->scratch % 16) return RAD_E_INVAL;
-    if (slots > 0x7fffffffLL) return RAD_E_SHAPE;
+    if (items > 0x7fffffffLL) return RAD_E_SHAPE;
     /* k and v are read through TMA tensor maps: positive strides below 2^39 elements. */
     const int64_t lim = 1LL << 39;
     if (g.k_row <= 0 || g.k_head <= 0 || g.v_row <= 0 || g.v_head <= 0 || g.k_row >= lim || g.k_head >= lim ||
@@ -1177,9 +1280,12 @@ extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
         return RAD_E_DEVICE;
     GdnPlan p;
     p.g = g;
-    p.tab = (int32_t*)a->scratch;
-    p.slots = (uint8_t*)a->scratch + table_bytes(g.n_seq);
-    p.outws = g.o ? p.slots + slot_bytes : nullptr;
+    uint8_t* ws = (uint8_t*)a->scratch;
+    p.tab = (int32_t*)ws;
+    p.ctl = (FillCtl*)(ws + table_bytes(g.n_seq));
+    p.flags = (int*)(ws + table_bytes(g.n_seq) + kCtlBytes);
+    p.slots = ws + head;
+    p.outws = g.o ? p.slots + items * (int64_t)kSlotBytes : nullptr;
     p.max_slots = (int)slots;
     cudaStream_t stream = rf::as_stream(s);
     const int smem1 = (int)sizeof(PrepSmem) + 1024, smem2 = (int)sizeof(ChainSmem) + 128, smem3 = (int)sizeof(OutSmem) + 1024;
@@ -1189,19 +1295,31 @@ extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
         return RAD_E_DEVICE;
     gdn_plan_kernel<<<1, kPlanThreads, 0, stream>>>(p);
     if (cudaGetLastError() != cudaSuccess) return RAD_E_DEVICE;
-    /* Phase 1 sizes its grid by the rows alone (the chunk count is on the device); CTAs past the
-     * chunk count find no item. */
-    const int64_t items = slots * g.n_head_v;
+    if (!g.o) {
+        /* The state-only form: one cooperative kernel, one CTA per SM (all resident); a quarter of them
+         * (at most one a chain) run the chains, the rest phase 1. */
+        if (cudaFuncSetAttribute(gdn_fill_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFusedSmem) != cudaSuccess)
+            return RAD_E_DEVICE;
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gdn_fill_fused_kernel, kFusedThreads, kFusedSmem) != cudaSuccess ||
+            per_sm < 1)
+            return RAD_E_DEVICE;
+        const int grid = per_sm * rf::sm_count();
+        const int64_t chains = g.n_head_v * g.n_seq;
+        int chain_ctas = (int)(chains < grid / 4 ? chains : grid / 4);
+        if (chain_ctas < 1) chain_ctas = 1;
+        if (chain_ctas >= grid) return RAD_E_DEVICE;
+        void* args[] = { (void*)&kmap, (void*)&vmap, (void*)&p, (void*)&chain_ctas };
+        if (cudaLaunchCooperativeKernel((const void*)gdn_fill_fused_kernel, dim3((unsigned)grid), dim3(kFusedThreads), args,
+                                        kFusedSmem, stream) != cudaSuccess)
+            return RAD_E_DEVICE;
+        return rf::launch_status();
+    }
+    /* The output form: phase 1 (its grid sized by the rows alone: the chunk count is on the device, CTAs
+     * past it find no item), the register chain, the output kernel. */
     const int64_t grid1 = items < 2LL * rf::sm_count() ? items : 2LL * rf::sm_count();
     gdn_prep_kernel<<<(unsigned)grid1, kPrepThreads, smem1, stream>>>(kmap, vmap, p);
     if (cudaGetLastError() != cudaSuccess) return RAD_E_DEVICE;
-    if (!g.o) {   /* the state-only form: the chain on tensor memory */
-        const int smem_tc = (int)sizeof(TcSmem) + 1024;
-        if (cudaFuncSetAttribute(gdn_chain_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_tc) != cudaSuccess)
-            return RAD_E_DEVICE;
-        gdn_chain_tc_kernel<<<dim3((unsigned)g.n_head_v, (unsigned)g.n_seq), kTcThreads, smem_tc, stream>>>(p);
-        return rf::launch_status();
-    }
     gdn_chain_kernel<<<dim3(D / VS, (unsigned)g.n_head_v, (unsigned)g.n_seq), kChainThreads, smem2, stream>>>(p);
     if (cudaGetLastError() != cudaSuccess) return RAD_E_DEVICE;
     gdn_out_kernel<<<(unsigned)grid1, kOutThreads, smem3, stream>>>(qmap, kmap, p);
