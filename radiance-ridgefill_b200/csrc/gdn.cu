@@ -779,7 +779,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const GdnPl
  *   warp 8      lane 0 keeps three chunks' inputs in flight (bulk copies of the slot's W|K~^T, U~^T, gamma_L)
  *   warp 9      lane 0 issues the products as their operands are ready */
 constexpr int kTcEpi = 8, kTcThreads = 32 * (kTcEpi + 2), kTcStages = 3;
-constexpr uint32_t kTmemTc = 256;   /* D1 at column 0 (64 columns), D2 at column 128 (128 columns) */
+/* Tensor-memory columns: D1 (64), the f16 state A_S (64: two dk a column), D2 (128), V'^T A_V (32). */
+constexpr uint32_t kTmemTc = 512, kColD1 = 0, kColAs = 64, kColD2 = 128, kColAv = 256;
 /* Instruction descriptors, kind::f16: D f32 (bit 4), A and B f16, both K-major, N >> 3 at bit 17, M >> 4 at 24. */
 constexpr uint32_t kIdescPv = (1u << 4) | ((uint32_t)(64 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 constexpr uint32_t kIdescUp = (1u << 4) | ((uint32_t)(128 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
@@ -792,8 +793,6 @@ struct TcStage {
 };
 
 struct TcSmem {
-    uint16_t a_s[2][D][C];     /* the state in f16, [128 dv][128 dk]: two 64-column halves (first product's A) */
-    uint16_t a_v[D][C];        /* V'^T in f16, [128 dv][64 rows] (second product's A) */
     TcStage st[kTcStages];
     uint64_t landed[kTcStages], consumed[kTcStages];
     uint64_t d1_full, d2_full;           /* a product completed (tcgen05.commit) */
@@ -802,8 +801,7 @@ struct TcSmem {
     int abort;
 };
 /* the hardware swizzles by shared-memory address bits: every tile starts on 1024 bytes */
-static_assert(offsetof(TcSmem, a_v) % 1024 == 0 && offsetof(TcSmem, st) % 1024 == 0 && sizeof(TcStage) % 1024 == 0,
-              "tile alignment");
+static_assert(offsetof(TcSmem, st) % 1024 == 0 && sizeof(TcStage) % 1024 == 0, "tile alignment");
 
 __device__ __forceinline__ int ld_acquire(const int* ptr) {
     int v;
@@ -856,7 +854,6 @@ __device__ void chain_tc_role(const GdnPlan& p, TcSmem& s, int64_t first, int64_
     rf::tc_fence_after();
     const uint32_t tmem = s.tmem;
     volatile int* abort = &s.abort;
-    const uint32_t a_s = rf::saddr(&s.a_s[0][0][0]), a_v = rf::saddr(&s.a_v[0][0]);
     int64_t k0 = 0;          /* chunks taken by this CTA before the current chain */
     int64_t issued = 0;      /* the loader's copies */
     for (int64_t cid = first; cid < n_chains && !*abort; cid += step) {
@@ -900,8 +897,8 @@ __device__ void chain_tc_role(const GdnPlan& p, TcSmem& s, int64_t first, int64_
                     rf::tc_fence_after();
 #pragma unroll
                     for (int kk = 0; kk < 8; ++kk)
-                        rf::umma_f16(tmem, rf::sw128_kmajor_desc(a_s + (kk >> 2) * 16384 + (kk & 3) * 32),
-                                     rf::sw128_kmajor_desc(wt + (kk >> 2) * 8192 + (kk & 3) * 32), kIdescPv, kk > 0);
+                        rf::umma_f16_ts(tmem + kColD1, tmem + kColAs + 8 * kk, rf::sw128_kmajor_desc(wt + (kk >> 2) * 8192 + (kk & 3) * 32),
+                                        kIdescPv, kk > 0);
                     rf::mma_commit(&s.d1_full);
                     /* D2 += V'^T K~: the lanes wrote V' and put gamma_L S into D2 */
                     if (!rf::mbar_wait(&s.av_ready, par, abort, rf::kErrGdnWait) ||
@@ -910,7 +907,7 @@ __device__ void chain_tc_role(const GdnPlan& p, TcSmem& s, int64_t first, int64_
                     rf::tc_fence_after();
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        rf::umma_f16(tmem + 128, rf::sw128_kmajor_desc(a_v + kk * 32), rf::sw128_kmajor_desc(kt + kk * 32), kIdescUp, 1);
+                        rf::umma_f16_ts(tmem + kColD2, tmem + kColAv + 8 * kk, rf::sw128_kmajor_desc(kt + kk * 32), kIdescUp, 1);
                     rf::mma_commit(&s.consumed[st]);   /* the stage is free once these products have read it */
                     rf::mma_commit(&s.d2_full);
                 }
@@ -919,24 +916,21 @@ __device__ void chain_tc_role(const GdnPlan& p, TcSmem& s, int64_t first, int64_
             /* -------------------------------------------------------- the lanes (warps 0-7) */
             const int q = w & 3, ch = w >> 2, i = 32 * q + l;   /* dv row i; columns of half ch */
             const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
-            const uint32_t d1 = lane_base + 32 * ch, d2 = lane_base + 128 + 64 * ch;
+            const uint32_t d1 = lane_base + kColD1 + 32 * ch, d2 = lane_base + kColD2 + 64 * ch;
+            const uint32_t as = lane_base + kColAs + 32 * ch, av = lane_base + kColAv + 16 * ch;
             float* srow = g.state + state_slot * g.st_slot + h * g.st_head + (int64_t)i * D + 64 * ch;
             auto arrive = [&](uint64_t* bar) {   /* this warp's writes are done: one arrival a warp */
                 __syncwarp();
                 if (l == 0) rf::mbar_arrive(bar);
             };
-            auto put_as = [&](const uint32_t (&r)[2][32]) {   /* f16 state into the first product's A */
+            auto put_as = [&](const uint32_t (&r)[2][32]) {   /* f16 state into the first product's A (tensor memory) */
+                uint32_t o[32];
 #pragma unroll
-                for (int hf = 0; hf < 2; ++hf)
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        uint32_t o[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e)
-                            o[e] = rf::pack_f16(__uint_as_float(r[hf][8 * j + 2 * e]), __uint_as_float(r[hf][8 * j + 2 * e + 1]));
-                        sts128(a_s + ch * 16384 + rf::sw128_off(i, 32 * hf + 8 * j, 0), make_uint4(o[0], o[1], o[2], o[3]));
-                    }
-                rf::fence_proxy_async_smem();
+                for (int e = 0; e < 32; ++e)
+                    o[e] = rf::pack_f16(__uint_as_float(r[e >> 4][(2 * e) & 31]), __uint_as_float(r[e >> 4][(2 * e + 1) & 31]));
+                rf::tmem_st32(as, o);
+                rf::tmem_st_wait();
+                rf::tc_fence_before();
             };
             auto put_d2 = [&](uint32_t (&r)[2][32], float gam) {   /* gamma * S into D2 */
 #pragma unroll
@@ -975,24 +969,22 @@ __device__ void chain_tc_role(const GdnPlan& p, TcSmem& s, int64_t first, int64_
                 if (!(ok = rf::mbar_wait(&s.d1_full, par, abort, rf::kErrGdnWait))) break;
                 rf::tc_fence_after();
                 {
-                    uint32_t d[32];
+                    uint32_t d[32], o[16];
                     rf::tmem_ld32(d1, d);
                     rf::tmem_ld_wait();
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        const uint32_t off = rf::sw128_off(i, 32 * ch + 8 * j, 0);
-                        const uint4 uu = lds128(ut + off);
+                        const uint4 uu = lds128(ut + rf::sw128_off(i, 32 * ch + 8 * j, 0));
                         const uint32_t uw[4] = { uu.x, uu.y, uu.z, uu.w };
-                        uint32_t o[4];
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
                             const float2 uf = __half22float2(*(const __half2*)&uw[e]);
-                            o[e] = rf::pack_f16(uf.x - __uint_as_float(d[8 * j + 2 * e]), uf.y - __uint_as_float(d[8 * j + 2 * e + 1]));
+                            o[4 * j + e] = rf::pack_f16(uf.x - __uint_as_float(d[8 * j + 2 * e]), uf.y - __uint_as_float(d[8 * j + 2 * e + 1]));
                         }
-                        sts128(a_v + off, make_uint4(o[0], o[1], o[2], o[3]));
                     }
+                    rf::tmem_st16(av, o);   /* V'^T, f16, into the second product's A (tensor memory) */
+                    rf::tmem_st_wait();
                 }
-                rf::fence_proxy_async_smem();
                 rf::tc_fence_before();
                 arrive(&s.av_ready);
                 /* the updated state: the next chunk's f16 state first (its first product waits on it), then
