@@ -203,11 +203,9 @@ def run_mine(args):
     barrier()
     e2e_ms = e_start.elapsed_time(e_end) / args.steps
 
-    # max over ranks
-    vals = torch.tensor([ms, e2e_ms, dom_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    ms, e2e_ms, dom_ms = vals.tolist()
+    # the job's time is its slowest rank's
+    import shard
+    ms, e2e_ms, dom_ms = shard.max_over_ranks([ms, e2e_ms, dom_ms], dist if world > 1 else None)
 
     if rank == 0:
         pk = peaks()

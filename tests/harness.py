@@ -288,9 +288,11 @@ def oracle_gdn(k, v, g, beta, state, idx, cu, q=None, scale=None, f64=True, head
     o = np.zeros((T, Hv, dv), np.uint16) if q is not None else None
     fn = lib.oracle_gdn_fill_f64 if f64 else lib.oracle_gdn_fill_f32
     h0, h1 = heads or (0, Hv)
-    fn(_p(None if q is None else np.ascontiguousarray(q, np.uint16)), _p(np.ascontiguousarray(k, np.uint16)),
-       _p(np.ascontiguousarray(v, np.uint16)), _p(np.ascontiguousarray(g, np.float32)),
-       _p(np.ascontiguousarray(beta, np.float32)), _p(st), _p(idx), 1, st.shape[0], _p(cu), len(cu) - 1, _p(o),
+    # contiguous copies held here for the call (a pointer to a temporary would outlive its array)
+    qc = None if q is None else np.ascontiguousarray(q, np.uint16)
+    kc, vc = np.ascontiguousarray(k, np.uint16), np.ascontiguousarray(v, np.uint16)
+    gc, bc = np.ascontiguousarray(g, np.float32), np.ascontiguousarray(beta, np.float32)
+    fn(_p(qc), _p(kc), _p(vc), _p(gc), _p(bc), _p(st), _p(idx), 1, st.shape[0], _p(cu), len(cu) - 1, _p(o),
        Hk, Hv, dk, dv, float(scale if scale is not None else 1.0 / math.sqrt(dk)), h0, h1)
     return st, o
 

@@ -114,6 +114,37 @@ def test_fill_output_varlen_and_skipped(cuda, product_lib):
         assert H.rel_l2(got[slot], want[slot]) <= STATE_TOL
 
 
+@pytest.mark.parametrize("with_o", [False, True])
+def test_fill_head_spans_are_slices_of_one_call(cuda, product_lib, with_o):
+    """Tensor parallelism over value heads (shard.head_span, the reference's spans, uneven at TP3): each rank's
+    call over views of its heads writes, byte for byte, its slice of the one-rank call's state (and o)."""
+    import shard
+    torch = cuda
+    T, hk, hv = 700, 16, 48
+    q, k, v, g, beta, state = H.gdn_inputs(11, T, hk, hv, "fast", slots=2)
+    K = torch.from_numpy(k.view(np.int16)).cuda()
+    V = torch.from_numpy(v.view(np.int16)).cuda()
+    Q = torch.from_numpy(q.view(np.int16)).cuda()
+    G, BT = torch.from_numpy(g).cuda(), torch.from_numpy(beta).cuda()
+    I, CU = torch.tensor([1], dtype=torch.int32).cuda(), torch.tensor([0, T], dtype=torch.int32).cuda()
+
+    def call(S, O, ks, vs):
+        ops = [H.dev(Q[:, ks], abi.BF16) if with_o else abi.absent(), H.dev(K[:, ks], abi.BF16), H.dev(V[:, vs], abi.BF16),
+               H.dev(G[:, vs]), H.dev(BT[:, vs]), H.dev(S[:, vs]), H.dev(I), H.dev(CU),
+               H.dev(O[:, vs], abi.BF16) if with_o else abi.absent()]
+        return H.launch(product_lib, "ridgefill_gdn_fill", ops, H.gdn_params(T, ks.stop - ks.start, vs.stop - vs.start))
+
+    S1, O1 = torch.from_numpy(state.copy()).cuda(), torch.zeros((T, hv, 128), dtype=torch.int16, device="cuda")
+    assert call(S1, O1, slice(0, hk), slice(0, hv)) == abi.OK
+    for world in (2, 3):
+        S, O = torch.from_numpy(state.copy()).cuda(), torch.zeros((T, hv, 128), dtype=torch.int16, device="cuda")
+        for r in range(world):
+            (v0, v1), (k0, k1) = shard.head_span(hk, hv, r, world)
+            assert call(S, O, slice(k0, k1), slice(v0, v1)) == abi.OK
+        assert torch.equal(S.view(torch.int32), S1.view(torch.int32)), world
+        assert torch.equal(O, O1), world
+
+
 def test_fill_refusals(cuda, product_lib):
     torch = cuda
     q, k, v, g, beta, state = H.gdn_inputs(7, 64, 1, 2, "fast")
