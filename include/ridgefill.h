@@ -331,6 +331,14 @@ int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s);
  * a launch path. -1 when the device could not be read. */
 int ridgefill_device_error(int reset);
 
+/* Failure-detection self-test (no counterpart in the reference): launches, on stream `s`, one kernel that runs
+ * the two waits the library's kernels block on against a barrier phase and a flag that nothing completes: an
+ * mbarrier wait (every tensor-core hand-over) and the DeltaNet chain's wait for a slot flag (`*flag`, device
+ * memory, must be 0 and stay 0). Each gives up after its limit (2 s), records its code for
+ * ridgefill_device_error and writes 0 into status[0] / status[1] (device memory; 1 would mean it completed).
+ * The kernel then returns: no trap, no fault, the context stays usable. RAD_E_INVAL on null pointers. */
+int ridgefill_wait_selftest(int* flag, int* status, RadStream s);
+
 /* ridgefill_gdn_fill without a workspace operand (no counterpart in the reference): for callers that
  * cannot allocate device memory where they launch the fill -- an FFI host with no device allocator of
  * its own, or an engine step whose memory is fixed before the pass and which may not cudaMalloc inside

@@ -1318,6 +1318,39 @@ extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
     return rf::launch_status();
 }
 
+namespace {
+
+/* The two waits the fill's kernels block on, each against something nothing completes: an mbarrier phase
+ * nobody arrives on (every tensor-core hand-over) and a slot flag nobody sets (a chain waiting for phase 1).
+ * Each gives up after its limit, records kErrGdnWait and reports false; status[0], status[1] get the two
+ * outcomes (1 = completed). */
+__global__ void wait_selftest_kernel(int* flag, int* status) {
+    __shared__ uint64_t bar;
+    __shared__ int abort;
+    if (threadIdx.x == 0) {
+        rf::mbar_init(&bar, 1);
+        abort = 0;
+        rf::mbar_init_fence();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        status[0] = rf::mbar_wait(&bar, 0, &abort, rf::kErrGdnWait) ? 1 : 0;
+        abort = 0;
+        GdnPlan p{};
+        p.flags = flag;
+        status[1] = wait_item(p, 0, &abort) ? 1 : 0;
+    }
+}
+
+}  // namespace
+
+/* Failure detection without a fault: see include/ridgefill.h. */
+extern "C" int ridgefill_wait_selftest(int* flag, int* status, RadStream s) {
+    if (!flag || !status) return RAD_E_INVAL;
+    wait_selftest_kernel<<<1, 32, 0, rf::as_stream(s)>>>(flag, status);
+    return rf::launch_status();
+}
+
 /* This translation unit's copy of the device error word (sm100.cuh), for ridgefill_device_error. */
 namespace rf {
 int gdn_device_error(int reset) { return read_device_error(reset); }

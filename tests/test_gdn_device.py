@@ -164,3 +164,27 @@ def test_fill_refusals(cuda, product_lib):
     bad = list(ops)
     bad[0] = H.dev(K, abi.BF16)   # q without o
     assert H.launch(product_lib, "ridgefill_gdn_fill", bad, H.gdn_params(64, 1, 2)) == abi.E_INVAL
+
+
+def test_waits_give_up_and_the_context_survives(cuda, product_lib):
+    """Failure detection without a fault: the library's two waits, run against a barrier phase and a flag
+    that nothing completes, give up after their limit with the fill's error code, and the same context then
+    runs a fill correctly."""
+    import ctypes
+    torch = cuda
+    lib = product_lib.lib
+    lib.ridgefill_device_error(1)   # clear
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    status = torch.full((2,), 7, dtype=torch.int32, device="cuda")
+    fn = lib.ridgefill_wait_selftest
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    assert fn(flag.data_ptr(), status.data_ptr(), torch.cuda.current_stream().cuda_stream) == abi.OK
+    torch.cuda.synchronize()
+    assert status.tolist() == [0, 0]
+    assert lib.ridgefill_device_error(1) == 0x201
+    assert lib.ridgefill_device_error(0) == 0
+    q, k, v, g, beta, state = H.gdn_inputs(3, 300, 2, 4, "fast")
+    rc, got, _ = run_fill(product_lib, torch, k, v, g, beta, state, [1], [0, 300], 2, 4)
+    assert rc == abi.OK
+    want, _ = H.oracle_gdn(k, v, g, beta, state, [1], [0, 300])
+    assert H.rel_l2(got[1], want[1]) <= STATE_TOL
