@@ -11,7 +11,8 @@ ABI. Synthetic inputs with BASELINE's shapes and distributions, seeded; inputs (
 
 value   device time of K passes with inputs resident in HBM (CUDA events, max over ranks)
 e2e     the same passes with each step's inputs copied host->device from pinned memory and the results
-        (projected block input x, DeltaNet state, mask) copied back, inside the timed region
+        (projected block input x, DeltaNet state, mask) copied back, inside the timed region; two buffer sets
+        let one step's copies overlap the neighbouring steps' passes (copy engines and SMs run together)
 N > 1   one process per GPU (torchrun), each rank an independent 32K prompt: prompts are independent
         units, no data-path collective ("scaling": "weak"); value = all ranks' tokens / max rank time.
 --impl reference   the CPU arm: the reference's own host rows (compiled from kernels/host_ref.cpp into
@@ -175,31 +176,55 @@ def run_mine(args):
     dom_ms = statistics.mean(a.elapsed_time(b) for a, b in dom_ev)
 
     # ---------------------------------------------------------- end to end through the C ABI, host buffers
-    inputs = [step.h_s, step.k, step.v, step.g, step.beta, step.ab, step.token_ids, step.positions]
-    outputs = [step.x, step.state, step.mask]
-    host_in = [t.cpu().pin_memory() for t in inputs]
-    host_out = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in outputs]
+    # Each step uploads its inputs from pinned host memory, runs the pass and reads its results back. Two
+    # buffer sets (two Step objects) and three streams let step i+1's upload and step i-1's readback run on
+    # the copy engines while step i computes; a set is reused only after its previous pass and readback.
+    steps2 = [step, RS.Step(RS.StepShape(T=T_FULL), device=str(dev), seed=4321 + rank)]
+    ins = [[s_.h_s, s_.k, s_.v, s_.g, s_.beta, s_.ab, s_.token_ids, s_.positions] for s_ in steps2]
+    outs = [[s_.x, s_.state, s_.mask] for s_ in steps2]
+    host_in = [t.cpu().pin_memory() for t in ins[0]]
+    host_out = [[torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in o] for o in outs]
     h2d = sum(t.numel() * t.element_size() for t in host_in)
-    d2h = sum(t.numel() * t.element_size() for t in host_out)
+    d2h = sum(t.numel() * t.element_size() for t in host_out[0])
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+
+    def e2e_steps(n, start_event=None, end_event=None):
+        done_comp, done_out = [None, None], [None, None]
+        if start_event is not None:
+            start_event.record(s_in)
+        for i in range(n):
+            b_ = i % 2
+            with torch.cuda.stream(s_in):
+                if done_comp[b_] is not None:
+                    s_in.wait_event(done_comp[b_])
+                for d_, h in zip(ins[b_], host_in):
+                    d_.copy_(h, non_blocking=True)
+                ev_in = torch.cuda.Event()
+                ev_in.record(s_in)
+            stream.wait_event(ev_in)
+            if done_out[b_] is not None:
+                stream.wait_event(done_out[b_])
+            steps2[b_].run(stream.cuda_stream)
+            done_comp[b_] = torch.cuda.Event()
+            done_comp[b_].record(stream)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done_comp[b_])
+                for h, d_ in zip(host_out[b_], outs[b_]):
+                    h.copy_(d_, non_blocking=True)
+                done_out[b_] = torch.cuda.Event()
+                done_out[b_].record(s_out)
+        if end_event is not None:
+            for e in done_out:
+                if e is not None:
+                    s_out.wait_event(e)
+            end_event.record(s_out)
+
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        for _ in range(2):
-            for d_, h in zip(inputs, host_in):
-                d_.copy_(h, non_blocking=True)
-            step.run(stream.cuda_stream)
-            for h, d_ in zip(host_out, outputs):
-                h.copy_(d_, non_blocking=True)
-        stream.synchronize()
-        barrier()
-        e_start.record()
-        for _ in range(args.steps):
-            for d_, h in zip(inputs, host_in):
-                d_.copy_(h, non_blocking=True)
-            step.run(stream.cuda_stream)
-            for h, d_ in zip(host_out, outputs):
-                h.copy_(d_, non_blocking=True)
-        e_end.record()
-        stream.synchronize()
+    e2e_steps(3)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_steps(args.steps, e_start, e_end)
+    torch.cuda.synchronize()
     barrier()
     e2e_ms = e_start.elapsed_time(e_end) / args.steps
 
@@ -220,10 +245,10 @@ def run_mine(args):
             roof = {"bound": "hbm", "achieved": by / (dom_ms * 1e-3) / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
                     "traffic": None, "note": f"peak {pk['source']}"}
             if dominant == "ridgefill_gdn_fill":
-                # DRAM bytes of one fill from an ncu capture at 16,384 rows (plan + prep + chain kernels:
-                # 0.007 + 389.6 + 507.4 MB), scaled by rows: every term (k, v, g, beta reads, the chunk slots
-                # written and read back) grows in proportion to the rows.
-                roof["traffic"] = 897.0e6 * T_FULL / 16384
+                # DRAM bytes of one fill from an ncu capture at 16,384 rows (plan + fill kernels: 0.009 + 564.9
+                # MB: 208.1 read, 356.9 written), scaled by rows: every term (k, v, g, beta reads, the chunk
+                # slots written and read back) grows in proportion to the rows.
+                roof["traffic"] = 564.9e6 * T_FULL / 16384
                 roof["traffic_note"] = "ncu dram__bytes_read+write at 16,384 rows, scaled by rows"
                 roof["tensor"] = {"achieved": alg["gdn_chunk_flops"] / (dom_ms * 1e-3) / 1e12, "peak": pk["bf16_tflops"],
                                   "unit": "TFLOP/s"}

@@ -142,8 +142,8 @@ class Step:
             scratch = None
             self._args.append((name, r, tens, params))
 
-    # kernels a pass launches (the GDN fill is three: the sequence plan, the per-chunk transform, the carry)
-    LAUNCHES_PER_PASS = 11
+    # kernels a pass launches (the GDN fill is two: the sequence plan, then the fill kernel)
+    LAUNCHES_PER_PASS = 10
 
     def run(self, stream: int, events=None) -> None:
         """Issue one pass on `stream`. `events` (optional) maps an op name to a pair of CUDA events recorded
