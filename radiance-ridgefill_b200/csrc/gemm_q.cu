@@ -278,6 +278,115 @@ __global__ void __launch_bounds__(256) quant_kernel(RidgeFillQuant g) {
     }
 }
 
+/* One pass over HBM when the groups tile 2,048-column segments (K % 2048 == 0, group a power of two
+ * <= 2048): a CTA takes a segment of a row at a time, thread t holds columns 8t..8t+7 (one 16-byte load),
+ * a group's absmax is reduced in the warp (group <= 256) or over its warps in shared memory, then every
+ * thread writes its 8 codes and each group's first thread its scale. The same arithmetic as quant_kernel. */
+constexpr int kQSeg = 2048, kQThreads = kQSeg / 8, kQRows = 4;
+
+__global__ void __launch_bounds__(kQThreads) quant_seg_kernel(RidgeFillQuant g) {
+    __shared__ float wmax[kQRows][kQThreads / 32];
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int64_t segs = g.K / kQSeg, work = g.M * segs;
+    const int tpg = (int)(g.group / 8);   /* threads a group: a power of two, 1..256 */
+    const int lanes = tpg < 32 ? tpg : 32;
+    /* kQRows segments an iteration, their loads issued together */
+    for (int64_t w0 = (int64_t)blockIdx.x * kQRows; w0 < work; w0 += (int64_t)gridDim.x * kQRows) {
+        uint4 v[kQRows];
+#pragma unroll
+        for (int r = 0; r < kQRows; ++r) {
+            const int64_t wk = w0 + r < work ? w0 + r : work - 1;
+            const int64_t m = wk / segs, c0 = (wk - m * segs) * kQSeg + 8 * t;
+            v[r] = *(const uint4*)(g.x + m * g.ldx + c0);
+        }
+        float amax[kQRows];
+#pragma unroll
+        for (int r = 0; r < kQRows; ++r) {
+            const uint32_t vw[4] = { v[r].x, v[r].y, v[r].z, v[r].w };
+            float a = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) a = fmaxf(a, fmaxf(fabsf(__uint_as_float(vw[e] << 16)), fabsf(__uint_as_float(vw[e] & 0xffff0000u))));
+            for (int o = 1; o < lanes; o <<= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+            amax[r] = a;
+        }
+        if (tpg > 32) {
+            const int wpg = tpg / 32, g0 = warp / wpg * wpg;
+            if (lane == 0)
+#pragma unroll
+                for (int r = 0; r < kQRows; ++r) wmax[r][warp] = amax[r];
+            __syncthreads();
+#pragma unroll
+            for (int r = 0; r < kQRows; ++r) {
+                float a = wmax[r][g0];
+                for (int q = 1; q < wpg; ++q) a = fmaxf(a, wmax[r][g0 + q]);
+                amax[r] = a;
+            }
+            __syncthreads();   /* wmax is read before the next iteration writes it */
+        }
+#pragma unroll
+        for (int r = 0; r < kQRows; ++r) {
+            if (w0 + r >= work) break;
+            const int64_t wk = w0 + r, m = wk / segs, c0 = (wk - m * segs) * kQSeg + 8 * t;
+            const float sc = amax[r] == 0.0f ? 1.0f : __fdiv_rn(amax[r], 127.0f);
+            if ((t & (tpg - 1)) == 0) g.s[m * g.lds + c0 / g.group] = sc;
+            const uint32_t vw[4] = { v[r].x, v[r].y, v[r].z, v[r].w };
+            uint32_t lo = 0, hi = 0;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float x = __uint_as_float((e & 1) ? (vw[e >> 1] & 0xffff0000u) : (vw[e >> 1] << 16));
+                int q = __float2int_rn(__fdiv_rn(x, sc));
+                q = q > 127 ? 127 : (q < -127 ? -127 : q);
+                if (e < 4) lo |= (uint32_t)(uint8_t)(int8_t)q << (8 * e);
+                else hi |= (uint32_t)(uint8_t)(int8_t)q << (8 * (e - 4));
+            }
+            *(uint2*)(g.q + m * g.ldq + c0) = make_uint2(lo, hi);
+        }
+    }
+}
+
+/* One pass over HBM for a group of 256 NV columns held in registers: a warp per (row, group), lane l holds
+ * the 16-byte chunks l, l + 32, ... (coalesced 512-byte warp loads); absmax by shuffles, then the codes.
+ * The same arithmetic as quant_kernel. */
+template <int NV>
+__global__ void __launch_bounds__(256) quant_reg_kernel(RidgeFillQuant g) {
+    const int lane = threadIdx.x & 31;
+    const int64_t groups = g.K / g.group, work = g.M * groups;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); w < work; w += warps) {
+        const int64_t m = w / groups, j = w - m * groups;
+        const uint16_t* x = g.x + m * g.ldx + j * g.group;
+        uint4 v[NV];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) v[i] = *(const uint4*)(x + 8 * (lane + 32 * i));
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const uint32_t vw[4] = { v[i].x, v[i].y, v[i].z, v[i].w };
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                amax = fmaxf(amax, fmaxf(fabsf(__uint_as_float(vw[e] << 16)), fabsf(__uint_as_float(vw[e] & 0xffff0000u))));
+        }
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float sc = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 127.0f);
+        if (lane == 0) g.s[m * g.lds + j] = sc;
+        int8_t* q = g.q + m * g.ldq + j * g.group;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const uint32_t vw[4] = { v[i].x, v[i].y, v[i].z, v[i].w };
+            uint32_t lo = 0, hi = 0;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float xv = __uint_as_float((e & 1) ? (vw[e >> 1] & 0xffff0000u) : (vw[e >> 1] << 16));
+                int r = __float2int_rn(__fdiv_rn(xv, sc));
+                r = r > 127 ? 127 : (r < -127 ? -127 : r);
+                if (e < 4) lo |= (uint32_t)(uint8_t)(int8_t)r << (8 * e);
+                else hi |= (uint32_t)(uint8_t)(int8_t)r << (8 * (e - 4));
+            }
+            *(uint2*)(q + 8 * (lane + 32 * i)) = make_uint2(lo, hi);
+        }
+    }
+}
+
 /* ------------------------------------------------------------------ host side */
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -360,9 +469,24 @@ extern "C" int ridgefill_quant_act_device(const RadArgs* a, RadStream s) {
     const int rc = ridgefill_quant_parse(a, &g);
     if (rc != RAD_OK) return rc;
     if (g.M == 0) return RAD_OK;
+    const bool pow2 = (g.group & (g.group - 1)) == 0;
     const int64_t warps = g.M * (g.K / g.group);
     const int64_t blocks = (warps + 7) / 8, cap = (int64_t)rf::sm_count() * 8;
-    quant_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, rf::as_stream(s)>>>(g);
+    const unsigned grid = (unsigned)(blocks < cap ? blocks : cap);
+    switch (g.group) {   /* a group of 256 NV columns in registers */
+        case 256: quant_reg_kernel<1><<<grid, 256, 0, rf::as_stream(s)>>>(g); return rf::launch_status();
+        case 512: quant_reg_kernel<2><<<grid, 256, 0, rf::as_stream(s)>>>(g); return rf::launch_status();
+        case 1024: quant_reg_kernel<4><<<grid, 256, 0, rf::as_stream(s)>>>(g); return rf::launch_status();
+        case 2048: quant_reg_kernel<8><<<grid, 256, 0, rf::as_stream(s)>>>(g); return rf::launch_status();
+        case 4096: quant_reg_kernel<16><<<grid, 256, 0, rf::as_stream(s)>>>(g); return rf::launch_status();
+        default: break;
+    }
+    if (g.K % kQSeg == 0 && pow2 && g.group < 256) {   /* small groups: a CTA a 2,048-column segment */
+        const int64_t iters = (g.M * (g.K / kQSeg) + kQRows - 1) / kQRows, cap = (int64_t)rf::sm_count() * 8;
+        quant_seg_kernel<<<(unsigned)(iters < cap ? iters : cap), kQThreads, 0, rf::as_stream(s)>>>(g);
+        return rf::launch_status();
+    }
+    quant_kernel<<<grid, 256, 0, rf::as_stream(s)>>>(g);
     return rf::launch_status();
 }
 

@@ -20,7 +20,9 @@ def _quant_inputs(rng, M, K):
     return H.f32_to_bf16_bits(x)
 
 
-@pytest.mark.parametrize("M,K,group", [(1, 256, 128), (37, 2048, 128), (300, 2048, 2048), (64, 10240, 128), (5, 10240, 10240)])
+@pytest.mark.parametrize("M,K,group", [(1, 256, 128), (37, 2048, 128), (300, 2048, 2048), (64, 10240, 128), (5, 10240, 10240),
+                                       (7, 4096, 512), (3, 2048, 8), (9, 6144, 1024), (2, 2048, 32), (4, 4096, 4096),
+                                       (6, 1024, 256)])
 def test_quantiser_matches_oracle(cuda, product_lib, M, K, group):
     torch = cuda
     rng = np.random.default_rng(M + K)
