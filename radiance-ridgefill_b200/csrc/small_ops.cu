@@ -27,12 +27,21 @@ namespace {
 
 constexpr int kRowWarps = 8;   /* warps per CTA of the row kernels */
 
+/* A row's words, lane l taking words l, l + 32, ...; eight of a lane's loads are issued before their stores. */
 template <typename Word>
 __device__ __forceinline__ void copy_row(const RidgeFillCopy& p, int64_t row, int lane) {
     const Word* src = (const Word*)(p.src + row * p.src_pitch);
     Word* dst = (Word*)(p.dst + row * p.dst_pitch);
     const int64_t words = p.row_bytes / (int64_t)sizeof(Word);
-    for (int64_t w = lane; w < words; w += 32) dst[w] = src[w];
+    int64_t w = lane;
+    for (; w + 32 * 7 < words; w += 32 * 8) {
+        Word v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = src[w + 32 * u];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) dst[w + 32 * u] = v[u];
+    }
+    for (; w < words; w += 32) dst[w] = src[w];
 }
 
 __global__ void __launch_bounds__(32 * kRowWarps) select_kernel(RidgeFillSelect g) {
