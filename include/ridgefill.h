@@ -52,6 +52,8 @@ enum { HZ_CU = 0, HZ_POS, HZ_BOUNDS, HZ_SPAN, HZ_META, HZ_META_IDX, HZ_COUNT };
 enum { GQ_A = 0, GQ_A_SCALE, GQ_B, GQ_B_SCALE, GQ_Y, GQ_A_SUM, GQ_B_REF };
 /* ridgefill_gemm_nt_q_bias (new): gemm_nt_q's operands, then the bias and an int32 debug output. */
 enum { GB_A = 0, GB_A_SCALE, GB_B, GB_B_SCALE, GB_BIAS, GB_Y, GB_ACC };
+/* ridgefill_gemm_nt_bias (kernels/rows.cpp:67-70, oGemm): a, b, bias, res (optional), y. */
+enum { GN_A = 0, GN_B, GN_BIAS, GN_RES, GN_Y };
 /* ridgefill_quant_act_i8g (new; libr4d's quant_act_i8g operands, arch/ridgefill_layer.h:74-76). */
 enum { QA_X = 0, QA_Q, QA_S };
 /* ridgefill_gdn_fill (new; the chunk scan's operands, arch/qwen4exp_fill.h:55-60, without kkt:
@@ -309,6 +311,23 @@ int ridgefill_select_parse(const RadArgs* a, RidgeFillSelect* out);
 int ridgefill_drop_parse(const RadArgs* a, RidgeFillDrop* out);
 int ridgefill_hazard_parse(const RadArgs* a, RidgeFillHazard* out);
 int ridgefill_gemm_q_parse(const RadArgs* a, int with_bias, RidgeFillGemmQ* out);
+
+/* ridgefill_gemm_nt_bias, the bf16 projector and the final map (schema kernels/rows.cpp:67-70,155-160; issue
+ * arch/ridgefill_declare.h:236-240, arch/ridgefill_final.h:40-44): y = res + act(a @ b^T + bias), rounded to
+ * bf16 after the biased product (accumulated in f32, the bias added in f32), after the activation and after
+ * the residual. a bf16 [M, K], b bf16 [N, K], bias bf16 or f32 [N], res bf16 [M, N] optional, y bf16 [M, N];
+ * dtype "bf16"; act absent / "none" or "silu" (x * sigmoid(x)); K a multiple of 64; rows 16-byte aligned. */
+enum { RIDGEFILL_ACT_NONE = 0, RIDGEFILL_ACT_SILU = 1 };
+typedef struct RidgeFillGemmBias {
+    const uint16_t* a;       int64_t lda;         /* [M, K] */
+    const uint16_t* b;       int64_t ldb;         /* [N, K] */
+    const void*    bias;     int bias_f32;        /* [N] bf16 (bias_f32 0) or f32 */
+    const uint16_t* res;     int64_t ldr;         /* [M, N] or null */
+    uint16_t*      y;        int64_t ldy;         /* [M, N] */
+    int64_t        M, N, K;
+    int            act;
+} RidgeFillGemmBias;
+int ridgefill_gemm_bias_parse(const RadArgs* a, RidgeFillGemmBias* out);
 int ridgefill_quant_parse(const RadArgs* a, RidgeFillQuant* out);
 int ridgefill_gdn_parse(const RadArgs* a, RidgeFillGdn* out);
 
@@ -323,6 +342,7 @@ int ridgefill_drop_device(const RadArgs* a, RadStream s);
 int ridgefill_hazard_device(const RadArgs* a, RadStream s);
 int ridgefill_gemm_nt_q_device(const RadArgs* a, RadStream s);
 int ridgefill_gemm_nt_q_bias_device(const RadArgs* a, RadStream s);
+int ridgefill_gemm_nt_bias_device(const RadArgs* a, RadStream s);
 int ridgefill_quant_act_device(const RadArgs* a, RadStream s);
 int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s);
 

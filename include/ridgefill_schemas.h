@@ -226,6 +226,12 @@ inline int shape_gemm_q_bias(const RadParam* p, int n_p, int operand, RadOpdDesc
                                 opd(RAD_BF16, { N }), opd(RAD_BF16, { M, N }), opd_absent() });
 }
 
+inline int shape_gemm_bias(const RadParam* p, int n_p, int operand, RadOpdDesc* out) {
+    const int64_t M = dim(p, n_p, "M"), N = dim(p, n_p, "N"), K = dim(p, n_p, "K");
+    return pick(out, operand, { opd(RAD_BF16, { M, K }), opd(RAD_BF16, { N, K }), opd(RAD_BF16, { N }),
+                                opd(RAD_BF16, { M, N }), opd(RAD_BF16, { M, N }) });
+}
+
 inline int shape_quant(const RadParam* p, int n_p, int operand, RadOpdDesc* out) {
     const int64_t M = dim(p, n_p, "M"), n = dim(p, n_p, "n"), g = dim(p, n_p, "group");
     const int64_t groups = g > 0 && n % g == 0 ? n / g : 0;

@@ -505,6 +505,33 @@ void oracle_gemm_nt_q(const int8_t* a, int64_t lda, const float* a_scale, int64_
         }
 }
 
+/* ridgefill_gemm_nt_bias (kernels/rows.cpp:155-160): y = res + act(a @ b^T + bias), bf16 a [M, K] and b [N, K],
+ * bias bf16 or f32 [N], optional bf16 res [M, N]; rounded to bf16 after the biased product, after the
+ * activation (act 1 = silu, x / (1 + e^-x)) and after the residual. The dot is summed in double (the exact
+ * products of bf16 pairs), the bias added to the f32 sum. `z` (optional) receives the value before the
+ * residual, for a tolerance that follows a residual's cancellation. Rows [m0, m1) only. */
+void oracle_gemm_nt_bias(const uint16_t* a, int64_t lda, const uint16_t* b, int64_t ldb, const void* bias,
+                         int bias_f32, const uint16_t* res, int64_t ldr, uint16_t* y, int64_t ldy, uint16_t* z,
+                         int64_t N, int64_t K, int act, int64_t m0, int64_t m1) {
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int64_t m = m0; m < m1; ++m)
+        for (int64_t n = 0; n < N; ++n) {
+            double dot = 0.0;
+            const uint16_t* pa = a + m * lda;
+            const uint16_t* pb = b + n * ldb;
+            for (int64_t k = 0; k < K; ++k) dot += (double)bf16f(pa[k]) * (double)bf16f(pb[k]);
+            const float bv = bias_f32 ? ((const float*)bias)[n] : bf16f(((const uint16_t*)bias)[n]);
+            uint16_t x = f2bf((float)dot + bv);
+            if (act == 1) {
+                const double v = bf16f(x);
+                x = f2bf((float)(v / (1.0 + std::exp(-v))));
+            }
+            if (z) z[m * N + n] = x;
+            if (res) x = f2bf(bf16f(x) + bf16f(res[m * ldr + n]));
+            y[m * ldy + n] = x;
+        }
+}
+
 }  // extern "C"
 
 /* The gated delta rule, one row at a time (Yang, Kautz & Hatamizadeh, "Gated Delta Networks",

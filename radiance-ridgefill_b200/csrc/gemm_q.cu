@@ -43,11 +43,30 @@ constexpr int kSmemBytes = kStages * kStageBytes + kStageOut + 1024 /* alignment
  * K-major, N >> 3 at bit 17, M >> 4 at bit 24. */
 constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 
+/* kind::f16 with bf16 A and B (bits 7-9, 10-12 = 1), D f32 (bit 4): the bf16 GEMM (ridgefill_gemm_nt_bias). */
+constexpr uint32_t kIdescBf16 = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
 struct GemmPlan {
-    RidgeFillGemmQ g;
+    RidgeFillGemmQ g;       /* the int8 form */
+    RidgeFillGemmBias gb;   /* the bf16 form */
     int n_tiles, tiles, folds, steps_per_fold;
 };
 
+/* kBf16 false: the int8 projector (kind::i8, int32 sums folded with the scales); true: the bf16 GEMM of
+ * ridgefill_gemm_nt_bias (kind::f16 with bf16 operands, f32 sums, one fold). The same tiles, the same
+ * 128-byte K steps (128 int8 or 64 bf16 columns), the same roles. */
+/* A warp's two [32 rows][64 columns] staging boxes to y at (n0, y0); a box that starts past the matrix is not
+ * issued (one that overlaps its edge is clipped by the copy). */
+__device__ __forceinline__ void store_boxes(const CUtensorMap* map_y, const uint8_t* stg, int64_t n0, int32_t y0, int64_t M,
+                                            int64_t N) {
+    if (y0 < M) {
+        if (n0 < N) rf::tma_store_2d(map_y, stg, (int32_t)n0, y0);
+        if (n0 + 64 < N) rf::tma_store_2d(map_y, stg + kOutBox, (int32_t)(n0 + 64), y0);
+    }
+    rf::bulk_store_commit();
+}
+
+template <bool kBf16>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
               const __grid_constant__ CUtensorMap map_y, const GemmPlan p) {
@@ -97,8 +116,9 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
                 for (int ks = 0; ks < steps; ++ks) {
                     if (!rf::mbar_wait(&empty[stage], phase ^ 1, abort, rf::kErrGemmWaitProducer)) break;
                     rf::mbar_arrive_expect_tx(&full[stage], kStageBytes);
-                    rf::tma_load_2d(tile_a + stage * kABytes, &map_a, &full[stage], ks * BK, m0);
-                    rf::tma_load_2d(tile_b + stage * kBBytes, &map_b, &full[stage], ks * BK, n0);
+                    const int kx = ks * (kBf16 ? BK / 2 : BK);   /* the K step's first column, in elements */
+                    rf::tma_load_2d(tile_a + stage * kABytes, &map_a, &full[stage], kx, m0);
+                    rf::tma_load_2d(tile_b + stage * kBBytes, &map_b, &full[stage], kx, n0);
                     ++issued;
                     if (++stage == kStages) { stage = 0; phase ^= 1; }
                 }
@@ -132,9 +152,14 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
                         const uint32_t a_addr = rf::smem_addr(tile_a + stage * kABytes);
                         const uint32_t b_addr = rf::smem_addr(tile_b + stage * kBBytes);
 #pragma unroll
-                        for (int kk = 0; kk < BK / 32; ++kk)
-                            rf::mma_i8(d, rf::sw128_kmajor_desc(a_addr + kk * 32), rf::sw128_kmajor_desc(b_addr + kk * 32),
-                                       kIdesc, (ks | kk) != 0);
+                        for (int kk = 0; kk < BK / 32; ++kk) {   /* 32 bytes of K a product: 32 int8 or 16 bf16 */
+                            if constexpr (kBf16)
+                                rf::umma_f16(d, rf::sw128_kmajor_desc(a_addr + kk * 32), rf::sw128_kmajor_desc(b_addr + kk * 32),
+                                             kIdescBf16, (ks | kk) != 0);
+                            else
+                                rf::mma_i8(d, rf::sw128_kmajor_desc(a_addr + kk * 32), rf::sw128_kmajor_desc(b_addr + kk * 32),
+                                           kIdesc, (ks | kk) != 0);
+                        }
                         rf::mma_commit(&empty[stage]);   /* the stage is free once these MMAs have read it */
                         if (++stage == kStages) { stage = 0; phase ^= 1; }
                     }
@@ -149,7 +174,87 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
         const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + half * 128;
         uint32_t fold = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
+        if constexpr (kBf16) {
+            /* y = res + act(acc + bias): 32 columns at a time from tensor memory, each rounding to bf16 where
+             * ridgefill_gemm_nt_bias rounds, into the staging tiles; the accumulator is released after its
+             * last read. */
+            const RidgeFillGemmBias& gb = p.gb;
+            for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x, ++fold) {
+                const int64_t m = (int64_t)(tile / p.n_tiles) * BM + row;
+                const int64_t n0 = (int64_t)(tile % p.n_tiles) * BN + half * 128;
+                const uint32_t buf = fold & 1, use = (fold >> 1) & 1;
+                if (!(ok = rf::mbar_wait(&acc_full[buf], use, abort, rf::kErrGemmWaitEpilogue))) break;
+                rf::tc_fence_after();
+                uint8_t* stg = stage_out + (warp - 2) * 2 * kOutBox;
+                if (lane == 0) rf::bulk_store_wait_read();
+                __syncwarp();
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t r[32];
+                    rf::tmem_ld32(lane_addr + buf * BN + c * 32, r);
+                    rf::tmem_ld_wait();
+                    if (c == 3) {
+                        rf::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) rf::mbar_arrive(&acc_empty[buf]);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int cc = c * 32 + j * 8;   /* column within this warp's half */
+                        const int64_t n = n0 + cc;
+                        float bv[8] = {}, rv[8] = {};
+                        if (n < gb.N) {
+                            if (gb.bias_f32) {
+                                const float4 b0 = __ldg((const float4*)((const float*)gb.bias + n));
+                                const float4 b1 = __ldg((const float4*)((const float*)gb.bias + n + 4));
+                                bv[0] = b0.x; bv[1] = b0.y; bv[2] = b0.z; bv[3] = b0.w;
+                                bv[4] = b1.x; bv[5] = b1.y; bv[6] = b1.z; bv[7] = b1.w;
+                            } else {
+                                const uint4 bb = __ldg((const uint4*)((const uint16_t*)gb.bias + n));
+                                const uint32_t bw[4] = { bb.x, bb.y, bb.z, bb.w };
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    bv[2 * e] = __uint_as_float(bw[e] << 16);
+                                    bv[2 * e + 1] = __uint_as_float(bw[e] & 0xffff0000u);
+                                }
+                            }
+                            if (gb.res && m < gb.M) {
+                                const uint4 rr = *(const uint4*)(gb.res + m * gb.ldr + n);
+                                const uint32_t rw[4] = { rr.x, rr.y, rr.z, rr.w };
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    rv[2 * e] = __uint_as_float(rw[e] << 16);
+                                    rv[2 * e + 1] = __uint_as_float(rw[e] & 0xffff0000u);
+                                }
+                            }
+                        }
+                        uint32_t o[4];
+#pragma unroll
+                        for (int e = 0; e < 8; e += 2) {
+                            float v[2];
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                float x = rf::bf16_bits_to_f32(rf::f32_to_bf16_bits(__fadd_rn(__uint_as_float(r[j * 8 + e + h]), bv[e + h])));
+                                if (gb.act == RIDGEFILL_ACT_SILU)
+                                    x = rf::bf16_bits_to_f32(rf::f32_to_bf16_bits(__fdiv_rn(x, __fadd_rn(1.0f, expf(-x)))));
+                                if (gb.res) x = __fadd_rn(x, rv[e + h]);
+                                v[h] = x;
+                            }
+                            o[e >> 1] = rf::pack_bf16(v[0], v[1]);
+                        }
+                        *(uint4*)(stg + (cc >> 6) * kOutBox + lane * 128 + ((((cc & 63) >> 3) ^ (lane & 7)) << 4)) =
+                            make_uint4(o[0], o[1], o[2], o[3]);
+                    }
+                }
+                rf::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    const int32_t y0 = (int32_t)((tile / p.n_tiles) * BM + quarter * 32);
+                    store_boxes(&map_y, stg, n0, y0, gb.M, gb.N);
+                }
+            }
+        }
+        for (int tile = blockIdx.x; tile < p.tiles && ok && !kBf16; tile += gridDim.x) {
             const int64_t m = (int64_t)(tile / p.n_tiles) * BM + row;
             const int64_t n0 = (int64_t)(tile % p.n_tiles) * BN + half * 128;
             const bool row_live = m < g.M;
@@ -222,9 +327,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
             __syncwarp();
             if (lane == 0) {
                 const int32_t y0 = (int32_t)((tile / p.n_tiles) * BM + quarter * 32);
-                rf::tma_store_2d(&map_y, stg, (int32_t)n0, y0);
-                rf::tma_store_2d(&map_y, stg + kOutBox, (int32_t)(n0 + 64), y0);
-                rf::bulk_store_commit();
+                store_boxes(&map_y, stg, n0, y0, g.M, g.N);
             }
         }
         if (lane == 0) rf::bulk_store_wait();   /* the tile stores are complete before the CTA leaves */
@@ -443,10 +546,46 @@ int launch_gemm(const RidgeFillGemmQ& g, cudaStream_t stream) {
     p.tiles = (int)tiles;
     p.folds = (int)(g.K / g.group);
     p.steps_per_fold = (int)(g.group / BK);
-    if (cudaFuncSetAttribute(gemm_q_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+    if (cudaFuncSetAttribute(gemm_q_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
         return RAD_E_DEVICE;
     const int grid = p.tiles < rf::sm_count() ? p.tiles : rf::sm_count();
-    gemm_q_kernel<<<grid, kThreads, kSmemBytes, stream>>>(map_a, map_b, map_y, p);
+    gemm_q_kernel<false><<<grid, kThreads, kSmemBytes, stream>>>(map_a, map_b, map_y, p);
+    return rf::launch_status();
+}
+
+/* A [rows, cols] bf16 matrix with row pitch `pitch` elements, read in [box_rows, 64] tiles (128 bytes of K)
+ * with 128-byte swizzle; rows past the end read as zero. */
+bool bf16_tile_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t pitch, uint32_t box_rows) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = { (cuuint64_t)cols, (cuuint64_t)rows };
+    const cuuint64_t strides[1] = { (cuuint64_t)pitch * 2 };
+    const cuuint32_t box[2] = { (cuuint32_t)(BK / 2), box_rows };
+    const cuuint32_t estr[2] = { 1, 1 };
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int launch_gemm_bf16(const RidgeFillGemmBias& g, cudaStream_t stream) {
+    if (g.M == 0) return RAD_OK;
+    if (g.M > 0x7fffffffLL || g.N > 0x7fffffffLL || g.K > 0x7fffffffLL) return RAD_E_SHAPE;
+    CUtensorMap map_a, map_b, map_y;
+    if (!bf16_tile_map(&map_a, g.a, g.M, g.K, g.lda, BM) || !bf16_tile_map(&map_b, g.b, g.N, g.K, g.ldb, BN) ||
+        !bf16_store_map(&map_y, g.y, g.M, g.N, g.ldy))
+        return RAD_E_DEVICE;
+    GemmPlan p{};
+    p.gb = g;
+    p.n_tiles = (int)((g.N + BN - 1) / BN);
+    const int64_t tiles = ((g.M + BM - 1) / BM) * p.n_tiles;
+    if (tiles > 0x7fffffffLL) return RAD_E_SHAPE;
+    p.tiles = (int)tiles;
+    p.folds = 1;
+    p.steps_per_fold = (int)((g.K + BK / 2 - 1) / (BK / 2));   /* a ragged last step reads zeros past K */
+    if (cudaFuncSetAttribute(gemm_q_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+        return RAD_E_DEVICE;
+    const int grid = p.tiles < rf::sm_count() ? p.tiles : rf::sm_count();
+    gemm_q_kernel<true><<<grid, kThreads, kSmemBytes, stream>>>(map_a, map_b, map_y, p);
     return rf::launch_status();
 }
 
@@ -462,6 +601,12 @@ extern "C" int ridgefill_gemm_nt_q_bias_device(const RadArgs* a, RadStream s) {
     RidgeFillGemmQ g;
     const int rc = ridgefill_gemm_q_parse(a, 1, &g);
     return rc != RAD_OK ? rc : launch_gemm(g, rf::as_stream(s));
+}
+
+extern "C" int ridgefill_gemm_nt_bias_device(const RadArgs* a, RadStream s) {
+    RidgeFillGemmBias g;
+    const int rc = ridgefill_gemm_bias_parse(a, &g);
+    return rc != RAD_OK ? rc : launch_gemm_bf16(g, rf::as_stream(s));
 }
 
 extern "C" int ridgefill_quant_act_device(const RadArgs* a, RadStream s) {

@@ -374,6 +374,57 @@ extern "C" int ridgefill_gemm_q_parse(const RadArgs* a, int with_bias, RidgeFill
     return RAD_OK;
 }
 
+/* ridgefill_gemm_nt_bias: see include/ridgefill.h. */
+extern "C" int ridgefill_gemm_bias_parse(const RadArgs* a, RidgeFillGemmBias* g) {
+    *g = RidgeFillGemmBias{};
+    const RadTensor* A = rad_arg_in(a, GN_A);
+    const RadTensor* B = rad_arg_in(a, GN_B);
+    const RadTensor* bias = rad_arg_in(a, GN_BIAS);
+    const RadTensor* R = rad_arg_in(a, GN_RES);
+    const RadTensor* Y = rad_arg_in(a, GN_Y);
+    long long N = 0, K = 0;
+    const char* dt = rad_args_gets(a, "dtype");
+    if (!A || !B || !bias || !Y || !rad_args_geti(a, "N", &N) || !rad_args_geti(a, "K", &K) || !dt) return RAD_E_INVAL;
+    if (std::strcmp(dt, "bf16") != 0) return RAD_E_UNSUPPORTED;
+    const char* act = rad_args_gets(a, "act");
+    int act_code = RIDGEFILL_ACT_NONE;
+    if (act && std::strcmp(act, "none") != 0) {
+        if (std::strcmp(act, "silu") == 0) act_code = RIDGEFILL_ACT_SILU;
+        else return RAD_E_UNSUPPORTED;
+    }
+    if (A->dtype != RAD_BF16 || B->dtype != RAD_BF16 || (bias->dtype != RAD_BF16 && bias->dtype != RAD_F32) ||
+        (R && R->dtype != RAD_BF16) || Y->dtype != RAD_BF16)
+        return RAD_E_DTYPE;
+    if (A->rank != 2 || B->rank != 2 || Y->rank != 2 || (R && R->rank != 2)) return RAD_E_SHAPE;
+    const int64_t M = A->shape[0];
+    if (K <= 0 || N <= 0 || K % 8 != 0 || N % 8 != 0) return RAD_E_SHAPE;   /* 16-byte row pitches */
+    if (A->shape[1] != K || B->shape[0] != N || B->shape[1] != K || Y->shape[0] != M || Y->shape[1] != N ||
+        rad_tensor_numel(bias) != N || (R && (R->shape[0] != M || R->shape[1] != N)))
+        return RAD_E_SHAPE;
+    if (A->stride[1] != 1 || B->stride[1] != 1 || Y->stride[1] != 1 || !dense(bias) || (R && R->stride[1] != 1))
+        return RAD_E_STRIDE;
+    /* TMA tiles of a, b and y, 16-byte vector reads of the bias and the residual. */
+    if (((uintptr_t)A->data | (uintptr_t)B->data | (uintptr_t)Y->data | (uintptr_t)bias->data) % 16 ||
+        (A->stride[0] * 2) % 16 || (B->stride[0] * 2) % 16 || (Y->stride[0] * 2) % 16 ||
+        (R && ((uintptr_t)R->data % 16 || (R->stride[0] * 2) % 16)))
+        return RAD_E_STRIDE;
+    g->a = (const uint16_t*)A->data;
+    g->lda = A->stride[0];
+    g->b = (const uint16_t*)B->data;
+    g->ldb = B->stride[0];
+    g->bias = bias->data;
+    g->bias_f32 = bias->dtype == RAD_F32;
+    g->res = R ? (const uint16_t*)R->data : nullptr;
+    g->ldr = R ? R->stride[0] : 0;
+    g->y = (uint16_t*)Y->data;
+    g->ldy = Y->stride[0];
+    g->M = M;
+    g->N = N;
+    g->K = K;
+    g->act = act_code;
+    return RAD_OK;
+}
+
 /* ridgefill_quant_act_i8g: x bf16 [M, n] (row pitch free, last stride 1), q i8 [M, n], s f32 [M, n/group]. */
 extern "C" int ridgefill_quant_parse(const RadArgs* a, RidgeFillQuant* g) {
     *g = RidgeFillQuant{};

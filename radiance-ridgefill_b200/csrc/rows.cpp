@@ -28,6 +28,7 @@ const RadConstraint kMaskCons[] = { RAD_CIN("mode", "none class random all step"
 const RadConstraint kCorrectCons[] = { RAD_CIN("mode", "undo apply") };
 const RadConstraint kGemmCons[] = { RAD_CIN("dtype", "i8a8") };
 const RadConstraint kQuantCons[] = { RAD_CIN("dtype", "bf16") };
+const RadConstraint kGemmBiasCons[] = { RAD_CIN("dtype", "bf16") };
 
 /* ------------------------------------------------------------------ stored-form hooks */
 
@@ -139,6 +140,10 @@ const RadKernelInfo kRows[] = {
                "ridgefill_gemm_nt_q with the bias add fused into the epilogue", "K a multiple of 128, N of 16",
                "i8 a / b, f32 a_scale / stored b_scale, bf16 bias / y, i32 acc", kGemmCons, 1,
                ridgefill_gemm_nt_q_bias_device, nullptr, shape_gemm_q_bias, gemm_layout, gemm_relayout, gemm_unrelayout),
+    DEVICE_ROW("ridgefill_gemm_nt_bias_sm100", "ridgefill_gemm_nt_bias",
+               "tcgen05 kind::f16 (bf16 operands), TMEM f32 accumulators, TMA 128-B swizzled 128x256 tiles, bias / silu / "
+               "residual epilogue, TMA tile stores", "K a multiple of 64, N of 8", "bf16 a / b / res / y, bf16 or f32 bias",
+               kGemmBiasCons, 1, ridgefill_gemm_nt_bias_device, nullptr, shape_gemm_bias, nullptr, nullptr, nullptr),
     DEVICE_ROW("ridgefill_quant_act_i8g_sm100", "ridgefill_quant_act_i8g", "warp per row group, 16-byte loads",
                "n a multiple of group", "bf16 x, i8 q, f32 s", kQuantCons, 1, ridgefill_quant_act_device, nullptr,
                shape_quant, nullptr, nullptr, nullptr),

@@ -226,6 +226,7 @@ def _bind_oracle_functions(lib):
     lib.oracle_quant_act_i8g.argtypes = [P, i64, i64, i64, i64, P, i64, P, i64]
     lib.oracle_quantise_weight_i8.argtypes = [P, i64, i64, P, P]
     lib.oracle_gemm_nt_q.argtypes = [P, i64, P, i64, P, i64, P, P, P, i64, P, i64, i64, i64, i64, i64, i64]
+    lib.oracle_gemm_nt_bias.argtypes = [P, i64, P, i64, P, C.c_int, P, i64, P, i64, P, i64, i64, C.c_int, i64, i64]
     for f in (lib.oracle_gdn_fill_f64, lib.oracle_gdn_fill_f32):
         f.argtypes = [P, P, P, P, P, P, P, i64, i64, P, i64, P, i64, i64, i64, i64, C.c_float, i64, i64]
     lib.oracle_threads.restype = C.c_int
@@ -275,6 +276,27 @@ def oracle_gemm(a, a_scale, b, b_scale_kn, bias=None, group=None, with_acc=False
     lib.oracle_gemm_nt_q(_p(a), K, _p(a_scale), blocks, _p(b), K, _p(b_scale_kn), _p(bias), _p(y), N, _p(acc),
                          M, N, K, group, m0, m1)
     return (y, acc) if with_acc else y
+
+
+def oracle_gemm_bias(a, b, bias, res=None, act=0, rows=None):
+    """a bf16 bits [M, K], b bf16 bits [N, K], bias bf16 bits (uint16) or f32 [N], res bf16 bits [M, N] or None
+    -> (y, z) bf16 bits [M, N]: y = res + act(a @ b^T + bias), z the value before the residual."""
+    lib = oracle().lib
+    a = np.ascontiguousarray(a, np.uint16)
+    b = np.ascontiguousarray(b, np.uint16)
+    bias = np.ascontiguousarray(bias)
+    bias_f32 = bias.dtype == np.float32
+    if not bias_f32:
+        bias = bias.astype(np.uint16)
+    res = None if res is None else np.ascontiguousarray(res, np.uint16)
+    M, K = a.shape
+    N = b.shape[0]
+    y = np.zeros((M, N), np.uint16)
+    z = np.zeros((M, N), np.uint16)
+    m0, m1 = rows or (0, M)
+    lib.oracle_gemm_nt_bias(_p(a), K, _p(b), K, _p(bias), int(bias_f32), _p(res), N, _p(y), N, _p(z), N, K, act,
+                            m0, m1)
+    return y, z
 
 
 def oracle_gdn(k, v, g, beta, state, idx, cu, q=None, scale=None, f64=True, heads=None):

@@ -24,7 +24,7 @@ REFERENCE_SCHEMAS = [
     ("ridgefill_gemm_nt_q", ["M", "N", "K", "group", "dtype"], ["a", "a_scale", "b", "b_scale", "y", "a_sum", "b_ref"]),
 ]
 NEW_OPS = ["ridgefill_gemm_nt_q_bias", "ridgefill_quant_act_i8g", "ridgefill_gdn_fill"]
-DEVICE_OPS = [s[0] for s in REFERENCE_SCHEMAS if s[0] != "ridgefill_gemm_nt_bias"] + NEW_OPS
+DEVICE_OPS = [s[0] for s in REFERENCE_SCHEMAS] + NEW_OPS
 
 
 def described_params(op):
@@ -40,6 +40,7 @@ def described_params(op):
                                  H.pstr("dtype", "i8a8")],
          "ridgefill_gemm_nt_q_bias": [H.pint("M", 64), H.pint("N", 256), H.pint("K", 256), H.pint("group", 128),
                                       H.pstr("dtype", "i8a8")],
+         "ridgefill_gemm_nt_bias": [H.pint("M", 64), H.pint("N", 256), H.pint("K", 256), H.pstr("dtype", "bf16")],
          "ridgefill_quant_act_i8g": [H.pint("M", 64), H.pint("n", 256), H.pint("group", 128), H.pstr("dtype", "bf16")],
          "ridgefill_gdn_fill": [H.pint("M", 130), H.pint("n_head_k", 2), H.pint("n_head_v", 4), H.pint("head_k", 128),
                                 H.pint("head_v", 128), H.pint("chunk", 64)]}
@@ -82,7 +83,6 @@ def test_every_row_is_a_device_row(product_lib):
     assert all(r.domain == abi.DOMAIN_DEVICE for r in rows), "the B200 library has no host rows"
     for op in DEVICE_OPS:
         assert product_lib.find_row(op, abi.DOMAIN_DEVICE) is not None, op
-    assert product_lib.find_row("ridgefill_gemm_nt_bias", abi.DOMAIN_DEVICE) is None   # a later row
     assert product_lib.find_row("ridgefill_gdn_fill", abi.DOMAIN_DEVICE).scratch
 
 

@@ -219,6 +219,33 @@ def test_oracle_gemm_definition():
         assert np.array_equal(yb, want)
 
 
+@pytest.mark.parametrize("bias_f32,res,act", [(False, False, 0), (True, True, 0), (False, True, 1), (True, False, 1)])
+def test_oracle_gemm_bias_definition(bias_f32, res, act):
+    """ridgefill_gemm_nt_bias's oracle against numpy on small shapes (kernels/rows.cpp:155-160): the rounding
+    points of y = res + act(a @ b^T + bias) restated independently, bit for bit (the dots are exact in
+    float64 for these sizes), with row sampling giving the same rows."""
+    rng = np.random.default_rng(11 + act)
+    M, N, K = 9, 40, 136
+    a = H.f32_to_bf16_bits(rng.standard_normal((M, K)).astype(np.float32))
+    b = H.f32_to_bf16_bits(rng.standard_normal((N, K)).astype(np.float32))
+    bias = rng.standard_normal(N).astype(np.float32)
+    bias = bias if bias_f32 else H.f32_to_bf16_bits(bias)
+    r = H.f32_to_bf16_bits(rng.standard_normal((M, N)).astype(np.float32)) if res else None
+    y, z = H.oracle_gemm_bias(a, b, bias, r, act=act)
+    dot = H.bf16_bits_to_f32(a).astype(np.float64) @ H.bf16_bits_to_f32(b).astype(np.float64).T
+    bv = bias if bias_f32 else H.bf16_bits_to_f32(bias)
+    x = H.f32_to_bf16_bits(dot.astype(np.float32) + bv[None, :])
+    if act:
+        xv = H.bf16_bits_to_f32(x).astype(np.float64)
+        x = H.f32_to_bf16_bits((xv / (1.0 + np.exp(-xv))).astype(np.float32))
+    assert np.array_equal(z, x)
+    if res:
+        x = H.f32_to_bf16_bits(H.bf16_bits_to_f32(x) + H.bf16_bits_to_f32(r))
+    assert np.array_equal(y, x)
+    y2, _ = H.oracle_gemm_bias(a, b, bias, r, act=act, rows=(3, 7))
+    assert np.array_equal(y2[3:7], y[3:7]) and not y2[:3].any()
+
+
 def test_oracle_gdn_f32_tracks_f64():
     """The timed f32 baseline stays within the state tolerance of the f64 reference value."""
     rng = np.random.default_rng(9)
