@@ -10,11 +10,15 @@
  *     y = bf16(acc);   with a bias: y = bf16(float(y) + bias[n])
  * so the result is reproducible bit for bit by the CPU oracle.
  *
- * Kernel: persistent, one CTA per SM, 128 x 256 output tiles, 128-byte K steps.
- *   warp 0      TMA producer: A [128 x 128] and B [256 x 128] int8 tiles, 128-byte swizzle, 4-stage ring
- *   warp 1      tensor-memory allocator and MMA issuer: tcgen05.mma kind::i8 M128 N256 K32, four a step,
- *               int32 accumulators in tensor memory, two 256-column buffers so a block's MMAs overlap
- *               the previous block's fold
+ * Kernel: persistent 2-CTA clusters, one CTA per SM; a pair computes a 256 x 256 output tile with
+ * tcgen05.mma.cta_group::2 (each CTA holds 128 rows of A and 128 rows of B, so a CTA's shared memory moves
+ * half the operand bytes a one-CTA 128 x 256 tile needs), 128-byte K steps.
+ *   warp 0      TMA producer, both CTAs: this CTA's A [128 x 128] and B [128 x 128] int8 tiles, 128-byte
+ *               swizzle, 4-stage ring, the bytes completing on the even CTA's barrier
+ *   warp 1      tensor-memory allocator (both CTAs) and, in the even CTA, the MMA issuer: kind::i8 M256
+ *               N256 K32, four a step, int32 accumulators in each CTA's tensor memory (its 128 rows), two
+ *               256-column buffers so a block's MMAs overlap the previous block's fold; its commits release
+ *               the stage and hand over the accumulator in both CTAs
  *   warps 2-9   epilogue: each warp owns a 32-lane quarter of the tile rows and one 128-column half;
  *               it folds each finished K block into f32 registers and, at the tile's end, writes its
  *               32 x 128 bf16 block into its own 128-byte-swizzled staging tiles in shared memory and
@@ -29,9 +33,9 @@
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 128;
-constexpr int kStages = 3;
-constexpr int kABytes = BM * BK, kBBytes = BN * BK, kStageBytes = kABytes + kBBytes;
+constexpr int BM = 128, BM2 = 2 * BM, BN = 256, BK = 128;   /* a CTA's rows, a pair's rows and columns, K bytes a step */
+constexpr int kStages = 4;
+constexpr int kABytes = BM * BK, kBBytes = (BN / 2) * BK, kStageBytes = kABytes + kBBytes;   /* one CTA's halves */
 constexpr uint32_t kTmemCols = 512;
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 32 * (2 + kEpiWarps);
@@ -39,12 +43,12 @@ constexpr int kOutBox = 32 * 64 * 2;                  /* one [32 rows][64 cols] 
 constexpr int kStageOut = kEpiWarps * 2 * kOutBox;    /* the epilogue warps' staging tiles */
 constexpr int kSmemBytes = kStages * kStageBytes + kStageOut + 1024 /* alignment slack */ + 256 /* barriers */;
 
-/* Instruction descriptor: D s32 (bits 4-5 = 2), A and B signed int8 (bits 7-9, 10-12 = 1), both
- * K-major, N >> 3 at bit 17, M >> 4 at bit 24. */
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+/* Instruction descriptor of the pair's M256 N256 product: D s32 (bits 4-5 = 2), A and B signed int8 (bits
+ * 7-9, 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24. */
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM2 >> 4) << 24);
 
 /* kind::f16 with bf16 A and B (bits 7-9, 10-12 = 1), D f32 (bit 4): the bf16 GEMM (ridgefill_gemm_nt_bias). */
-constexpr uint32_t kIdescBf16 = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+constexpr uint32_t kIdescBf16 = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM2 >> 4) << 24);
 
 struct GemmPlan {
     RidgeFillGemmQ g;       /* the int8 form */
@@ -67,7 +71,7 @@ __device__ __forceinline__ void store_boxes(const CUtensorMap* map_y, const uint
 }
 
 template <bool kBf16>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
               const __grid_constant__ CUtensorMap map_y, const GemmPlan p) {
     extern __shared__ uint8_t smem_raw[];
@@ -83,14 +87,16 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
     volatile int* abort = (volatile int*)(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = rf::cluster_rank();   /* 0: the CTA that issues the pair's MMAs */
+    const int pair = (int)rf::cluster_id_x(), pairs = (int)rf::cluster_count_x();
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
-            rf::mbar_init(&full[s], 1);
-            rf::mbar_init(&empty[s], 1);
+            rf::mbar_init(&full[s], 1);    /* rank 0's: its producer's expect_tx, both CTAs' bytes */
+            rf::mbar_init(&empty[s], 1);   /* each CTA's: the MMA warp's commit */
         }
         for (int b = 0; b < 2; ++b) {
-            rf::mbar_init(&acc_full[b], 1);
-            rf::mbar_init(&acc_empty[b], kEpiWarps);
+            rf::mbar_init(&acc_full[b], 1);                /* each CTA's: the MMA warp's commit */
+            rf::mbar_init(&acc_empty[b], 2 * kEpiWarps);   /* rank 0's: both CTAs' epilogue warps */
         }
         *abort = 0;
         rf::mbar_init_fence();
@@ -98,36 +104,38 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
         rf::tma_prefetch_map(&map_b);
         rf::tma_prefetch_map(&map_y);
     }
-    if (warp == 1) rf::tmem_alloc<kTmemCols>(tmem_slot);
+    if (warp == 1) rf::tmem_alloc_pair<kTmemCols>(tmem_slot);
     rf::tc_fence_before();
-    __syncthreads();
+    rf::cluster_sync_all();   /* both CTAs' barriers are initialised before either signals the other's */
     rf::tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
     const RidgeFillGemmQ& g = p.g;
 
     if (warp == 0) {
-        /* ---------------------------------------------------------- producer */
+        /* ---------------------------------------------------------- producer (both CTAs) */
         if (lane == 0) {
             uint32_t stage = 0, phase = 0;
             int64_t issued = 0;
             const int steps = p.folds * p.steps_per_fold;
-            for (int tile = blockIdx.x; tile < p.tiles && !*abort; tile += gridDim.x) {
-                const int m0 = (tile / p.n_tiles) * BM, n0 = (tile % p.n_tiles) * BN;
+            for (int tile = pair; tile < p.tiles && !*abort; tile += pairs) {
+                const int m0 = (tile / p.n_tiles) * BM2 + (int)rank * BM, n0 = (tile % p.n_tiles) * BN + (int)rank * (BN / 2);
                 for (int ks = 0; ks < steps; ++ks) {
                     if (!rf::mbar_wait(&empty[stage], phase ^ 1, abort, rf::kErrGemmWaitProducer)) break;
-                    rf::mbar_arrive_expect_tx(&full[stage], kStageBytes);
+                    if (rank == 0) rf::mbar_arrive_expect_tx(&full[stage], 2 * kStageBytes);
                     const int kx = ks * (kBf16 ? BK / 2 : BK);   /* the K step's first column, in elements */
-                    rf::tma_load_2d(tile_a + stage * kABytes, &map_a, &full[stage], kx, m0);
-                    rf::tma_load_2d(tile_b + stage * kBBytes, &map_b, &full[stage], kx, n0);
+                    const uint32_t bar = rf::map_rank(rf::smem_addr(&full[stage]), 0);   /* rank 0's */
+                    rf::tma_load_2d_pair(tile_a + stage * kABytes, &map_a, bar, kx, m0);
+                    rf::tma_load_2d_pair(tile_b + stage * kBBytes, &map_b, bar, kx, n0);
                     ++issued;
                     if (++stage == kStages) { stage = 0; phase ^= 1; }
                 }
             }
-            /* Drain: every load this CTA issued has landed before its shared memory is released. */
+            /* Drain: the MMAs have released every stage this CTA loaded (so its loads have landed and the
+             * pair's MMAs no longer read its shared memory) before the CTA leaves. One deadline. */
             const int64_t first = issued > kStages ? issued - kStages : 0;
+            const uint64_t t0 = rf::global_ns();
             for (int64_t i = first; i < issued; ++i) {
-                const uint64_t t0 = rf::global_ns();
-                while (!rf::mbar_try_wait(&full[i % kStages], (uint32_t)((i / kStages) & 1))) {
+                while (!rf::mbar_try_wait(&empty[i % kStages], (uint32_t)((i / kStages) & 1))) {
                     if (rf::global_ns() - t0 > rf::kWaitTimeoutNs) {
                         atomicCAS(&rf::g_device_error, 0, (int)rf::kErrGemmDrain);
                         break;
@@ -136,11 +144,11 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
             }
         }
     } else if (warp == 1) {
-        /* ---------------------------------------------------------- MMA issuer */
-        if (lane == 0) {
+        /* ---------------------------------------------------------- MMA issuer (rank 0) */
+        if (lane == 0 && rank == 0) {
             uint32_t stage = 0, phase = 0, fold = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
+            for (int tile = pair; tile < p.tiles && ok; tile += pairs) {
                 for (int f = 0; f < p.folds && ok; ++f, ++fold) {
                     const uint32_t buf = fold & 1, use = (fold >> 1) & 1;
                     if (!(ok = rf::mbar_wait(&acc_empty[buf], use ^ 1, abort, rf::kErrGemmWaitMma))) break;
@@ -154,16 +162,21 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
 #pragma unroll
                         for (int kk = 0; kk < BK / 32; ++kk) {   /* 32 bytes of K a product: 32 int8 or 16 bf16 */
                             if constexpr (kBf16)
-                                rf::umma_f16(d, rf::sw128_kmajor_desc(a_addr + kk * 32), rf::sw128_kmajor_desc(b_addr + kk * 32),
-                                             kIdescBf16, (ks | kk) != 0);
+                                rf::umma_f16_pair(d, rf::sw128_kmajor_desc(a_addr + kk * 32), rf::sw128_kmajor_desc(b_addr + kk * 32),
+                                                  kIdescBf16, (ks | kk) != 0);
                             else
-                                rf::mma_i8(d, rf::sw128_kmajor_desc(a_addr + kk * 32), rf::sw128_kmajor_desc(b_addr + kk * 32),
-                                           kIdesc, (ks | kk) != 0);
+                                rf::mma_i8_pair(d, rf::sw128_kmajor_desc(a_addr + kk * 32), rf::sw128_kmajor_desc(b_addr + kk * 32),
+                                                kIdesc, (ks | kk) != 0);
                         }
-                        rf::mma_commit(&empty[stage]);   /* the stage is free once these MMAs have read it */
+                        /* the stage is free in both CTAs once these MMAs have read it */
+                        rf::mma_commit_pair(rf::smem_addr(&empty[stage]));
+                        rf::mma_commit_pair(rf::map_rank(rf::smem_addr(&empty[stage]), 1));
                         if (++stage == kStages) { stage = 0; phase ^= 1; }
                     }
-                    if (ok) rf::mma_commit(&acc_full[buf]);   /* the block's sums are final */
+                    if (ok) {   /* the block's sums are final, in both CTAs' tensor memory */
+                        rf::mma_commit_pair(rf::smem_addr(&acc_full[buf]));
+                        rf::mma_commit_pair(rf::map_rank(rf::smem_addr(&acc_full[buf]), 1));
+                    }
                 }
             }
         }
@@ -179,8 +192,8 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
              * ridgefill_gemm_nt_bias rounds, into the staging tiles; the accumulator is released after its
              * last read. */
             const RidgeFillGemmBias& gb = p.gb;
-            for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x, ++fold) {
-                const int64_t m = (int64_t)(tile / p.n_tiles) * BM + row;
+            for (int tile = pair; tile < p.tiles && ok; tile += pairs, ++fold) {
+                const int64_t m = (int64_t)(tile / p.n_tiles) * BM2 + rank * BM + row;
                 const int64_t n0 = (int64_t)(tile % p.n_tiles) * BN + half * 128;
                 const uint32_t buf = fold & 1, use = (fold >> 1) & 1;
                 if (!(ok = rf::mbar_wait(&acc_full[buf], use, abort, rf::kErrGemmWaitEpilogue))) break;
@@ -196,7 +209,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
                     if (c == 3) {
                         rf::tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) rf::mbar_arrive(&acc_empty[buf]);
+                        if (lane == 0) rf::mbar_arrive_cluster(rf::map_rank(rf::smem_addr(&acc_empty[buf]), 0));
                     }
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
@@ -249,13 +262,13 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
                 rf::fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    const int32_t y0 = (int32_t)((tile / p.n_tiles) * BM + quarter * 32);
+                    const int32_t y0 = (int32_t)((tile / p.n_tiles) * BM2 + rank * BM + quarter * 32);
                     store_boxes(&map_y, stg, n0, y0, gb.M, gb.N);
                 }
             }
         }
-        for (int tile = blockIdx.x; tile < p.tiles && ok && !kBf16; tile += gridDim.x) {
-            const int64_t m = (int64_t)(tile / p.n_tiles) * BM + row;
+        for (int tile = pair; tile < p.tiles && ok && !kBf16; tile += pairs) {
+            const int64_t m = (int64_t)(tile / p.n_tiles) * BM2 + rank * BM + row;
             const int64_t n0 = (int64_t)(tile % p.n_tiles) * BN + half * 128;
             const bool row_live = m < g.M;
             float acc[128];
@@ -295,7 +308,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
                 }
                 rf::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) rf::mbar_arrive(&acc_empty[buf]);
+                if (lane == 0) rf::mbar_arrive_cluster(rf::map_rank(rf::smem_addr(&acc_empty[buf]), 0));
             }
             if (!ok) break;
             /* bf16 (and the bias) into this warp's staging tiles, once the previous tile's stores have read them. */
@@ -326,18 +339,20 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
             rf::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-                const int32_t y0 = (int32_t)((tile / p.n_tiles) * BM + quarter * 32);
+                const int32_t y0 = (int32_t)((tile / p.n_tiles) * BM2 + rank * BM + quarter * 32);
                 store_boxes(&map_y, stg, n0, y0, g.M, g.N);
             }
         }
         if (lane == 0) rf::bulk_store_wait();   /* the tile stores are complete before the CTA leaves */
     }
 
+    /* Neither CTA leaves while the other may still signal its barriers; then both free the pair's columns. */
     rf::tc_fence_before();
-    __syncthreads();
+    __syncwarp();
+    rf::cluster_sync_all();
     if (warp == 1) {
         rf::tc_fence_after();
-        rf::tmem_free<kTmemCols>(tmem_base);
+        rf::tmem_free_pair<kTmemCols>(tmem_base);
     }
 }
 
@@ -531,26 +546,43 @@ bool int8_tile_map(CUtensorMap* map, const void* base, int64_t rows, int64_t col
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+/* One 2-CTA cluster per pair tile, as many pairs as the device holds at once (persistent). */
+template <bool kBf16>
+int launch_pairs(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap& map_y, const GemmPlan& p,
+                 cudaStream_t stream) {
+    static int max_pairs[2] = { 0, 0 };
+    if (cudaFuncSetAttribute(gemm_q_kernel<kBf16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+        return RAD_E_DEVICE;
+    if (!max_pairs[kBf16]) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (unsigned)(rf::sm_count() / 2));
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = kSmemBytes;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_q_kernel<kBf16>, &cfg) != cudaSuccess || n <= 0) return RAD_E_DEVICE;
+        max_pairs[kBf16] = n;
+    }
+    const int pairs = p.tiles < max_pairs[kBf16] ? p.tiles : max_pairs[kBf16];
+    gemm_q_kernel<kBf16><<<2 * pairs, kThreads, kSmemBytes, stream>>>(map_a, map_b, map_y, p);
+    return rf::launch_status();
+}
+
 int launch_gemm(const RidgeFillGemmQ& g, cudaStream_t stream) {
     if (g.M == 0) return RAD_OK;
     if (g.M > 0x7fffffffLL || g.N > 0x7fffffffLL || g.K > 0x7fffffffLL) return RAD_E_SHAPE;
     CUtensorMap map_a, map_b, map_y;
-    if (!int8_tile_map(&map_a, g.a, g.M, g.K, g.lda, BM) || !int8_tile_map(&map_b, g.b, g.N, g.K, g.ldb, BN) ||
+    if (!int8_tile_map(&map_a, g.a, g.M, g.K, g.lda, BM) || !int8_tile_map(&map_b, g.b, g.N, g.K, g.ldb, BN / 2) ||
         !bf16_store_map(&map_y, g.y, g.M, g.N, g.ldy))
         return RAD_E_DEVICE;
     GemmPlan p;
     p.g = g;
     p.n_tiles = (int)((g.N + BN - 1) / BN);
-    const int64_t tiles = ((g.M + BM - 1) / BM) * p.n_tiles;
+    const int64_t tiles = ((g.M + BM2 - 1) / BM2) * p.n_tiles;
     if (tiles > 0x7fffffffLL) return RAD_E_SHAPE;
     p.tiles = (int)tiles;
     p.folds = (int)(g.K / g.group);
     p.steps_per_fold = (int)(g.group / BK);
-    if (cudaFuncSetAttribute(gemm_q_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
-        return RAD_E_DEVICE;
-    const int grid = p.tiles < rf::sm_count() ? p.tiles : rf::sm_count();
-    gemm_q_kernel<false><<<grid, kThreads, kSmemBytes, stream>>>(map_a, map_b, map_y, p);
-    return rf::launch_status();
+    return launch_pairs<false>(map_a, map_b, map_y, p, stream);
 }
 
 /* A [rows, cols] bf16 matrix with row pitch `pitch` elements, read in [box_rows, 64] tiles (128 bytes of K)
@@ -571,22 +603,18 @@ int launch_gemm_bf16(const RidgeFillGemmBias& g, cudaStream_t stream) {
     if (g.M == 0) return RAD_OK;
     if (g.M > 0x7fffffffLL || g.N > 0x7fffffffLL || g.K > 0x7fffffffLL) return RAD_E_SHAPE;
     CUtensorMap map_a, map_b, map_y;
-    if (!bf16_tile_map(&map_a, g.a, g.M, g.K, g.lda, BM) || !bf16_tile_map(&map_b, g.b, g.N, g.K, g.ldb, BN) ||
+    if (!bf16_tile_map(&map_a, g.a, g.M, g.K, g.lda, BM) || !bf16_tile_map(&map_b, g.b, g.N, g.K, g.ldb, BN / 2) ||
         !bf16_store_map(&map_y, g.y, g.M, g.N, g.ldy))
         return RAD_E_DEVICE;
     GemmPlan p{};
     p.gb = g;
     p.n_tiles = (int)((g.N + BN - 1) / BN);
-    const int64_t tiles = ((g.M + BM - 1) / BM) * p.n_tiles;
+    const int64_t tiles = ((g.M + BM2 - 1) / BM2) * p.n_tiles;
     if (tiles > 0x7fffffffLL) return RAD_E_SHAPE;
     p.tiles = (int)tiles;
     p.folds = 1;
     p.steps_per_fold = (int)((g.K + BK / 2 - 1) / (BK / 2));   /* a ragged last step reads zeros past K */
-    if (cudaFuncSetAttribute(gemm_q_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
-        return RAD_E_DEVICE;
-    const int grid = p.tiles < rf::sm_count() ? p.tiles : rf::sm_count();
-    gemm_q_kernel<true><<<grid, kThreads, kSmemBytes, stream>>>(map_a, map_b, map_y, p);
-    return rf::launch_status();
+    return launch_pairs<true>(map_a, map_b, map_y, p, stream);
 }
 
 }  // namespace

@@ -99,7 +99,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 /* 2-D TMA tile load into shared memory, completing `bytes` on `bar`. (x, y): innermost coordinate
- * first, in elements. No multicast. */
+ * first, in elements. One destination CTA. */
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t x, int32_t y) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
@@ -107,7 +107,7 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
         : "memory");
 }
 
-/* 3-D TMA tile load (coordinates innermost first, in elements), completing on `bar`. No multicast. */
+/* 3-D TMA tile load (coordinates innermost first, in elements), completing on `bar`. One destination CTA. */
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t x, int32_t y, int32_t z) {
     asm volatile(
         "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
@@ -116,7 +116,7 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
 }
 
 /* Bulk (non-tensor) copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from global to
- * shared memory, completing on `bar`. No multicast. */
+ * shared memory, completing on `bar`. One destination CTA. */
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                  ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar))
@@ -221,6 +221,95 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n"
         ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
+}
+
+/* ------------------------------------------------------------------ CTA pairs (cta_group::2)
+ * Two CTAs of a 2-CTA cluster share one tcgen05.mma: A's M = 256 rows are split 128 / 128 between the CTAs'
+ * shared memory, B's N columns likewise split in halves, and each CTA's tensor memory holds the D rows of its
+ * own A rows (all N columns). The even CTA (rank 0) issues the MMAs; every tcgen05 instruction of such a
+ * kernel uses cta_group::2. */
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_count_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+
+/* The shared::cluster address of the object at this CTA's shared address `saddr` in CTA `rank`. */
+__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+
+/* Every thread of every CTA of the cluster; orders the threads' prior memory operations (barrier
+ * initialisation included) before any thread's later ones. */
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+/* Arrive (release, cluster scope) on an mbarrier given by its shared::cluster address, in any CTA of the cluster. */
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+
+/* Tensor memory of a CTA pair: the same warp of both CTAs allocates, each CTA receiving kCols columns at the
+ * same address (written to its own `slot`). */
+template <uint32_t kCols>
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* slot) {   /* whole warp, both CTAs */
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(slot)), "r"(kCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+template <uint32_t kCols>
+__device__ __forceinline__ void tmem_free_pair(uint32_t base) {   /* whole warp, both CTAs */
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(base), "r"(kCols) : "memory");
+}
+
+/* 2-D TMA tile load into this CTA's shared memory whose bytes complete on the mbarrier at shared::cluster
+ * address `bar_caddr`, which may be the pair's other CTA's. One destination CTA. */
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_caddr, int32_t x, int32_t y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(smem_addr(dst)), "l"((uint64_t)map), "r"(bar_caddr), "r"(x), "r"(y)
+        : "memory");
+}
+
+/* D[tmem] (+)= A[smem] * B[smem]^T over the CTA pair, int8 x int8 -> int32. Rank 0 issues. */
+__device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}\n"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+/* D[tmem] (+)= A[smem] * B[smem]^T over the CTA pair, f16 / bf16 -> f32 (kind::f16). Rank 0 issues. */
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+/* Arrive on the mbarrier at shared::cluster address `bar_caddr` (either CTA of the pair) once every pair MMA
+ * this thread issued so far has completed. */
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar_caddr) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_caddr) : "memory");
 }
 
 /* Arrive on `bar` once every tcgen05.mma this thread issued so far has completed. */
