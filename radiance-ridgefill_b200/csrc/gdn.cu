@@ -50,9 +50,9 @@ constexpr int PP = C + 8;      /* pitch of the f32 exchange tiles (float2 stores
 constexpr int kStages = 4;     /* phase 2: chunks in flight */
 
 /* A chunk's scratch slot, per (chunk, v-head), f16 tiles in the 128-byte-swizzled layout of sw128_off:
- * W [64 rows][128 dk] (two 64-column halves), K~^T [128 dk][64 rows] and U~^T [128 dv][64 rows] (dv slice s
- * of phase 2 at 4096 s), then G f32 [64], beta f32 [64] and gamma_L (16 bytes). Every tile is K-major for
- * the chain's products (its rows are the products' M or N). */
+ * W [64 rows][128 dk] (two 64-column halves), K~ [64 rows][128 dk] (two halves, the k tile's own layout) and
+ * U~^T [128 dv][64 rows] (dv slice s of phase 2 at 4096 s), then G f32 [64], beta f32 [64] and gamma_L
+ * (16 bytes). W and U~^T are K-major operands of the chain's products, K~ an MN-major one. */
 constexpr int kSlotW = 0, kSlotK = 16384, kSlotU = 32768, kSlotMeta = 49152, kSlotGl = kSlotMeta + 512;
 constexpr int kSlotBytes = kSlotGl + 16;
 constexpr uint32_t kTileBytes = C * D * 2;   /* one [64][128] b16 tile, and one TMA pair of [64][64] boxes */
@@ -186,12 +186,16 @@ __global__ void __launch_bounds__(kPlanThreads) gdn_plan_kernel(const GdnPlan p)
 /* ------------------------------------------------------------------ phase 1 */
 
 constexpr int kPrepThreads = 256;
+/* The thread that issues a group's bulk copies (TMA loads, slot stores) and publishes its slots: lane 0 of warp
+ * 4, which has no block of K K^T, so its waits on the stores overlap that product. */
+constexpr int kStoreTid = 128;
 constexpr int kSeqCache = 256;   /* sequences whose table rows a CTA keeps in shared memory */
 
 struct PrepSmem {
     uint16_t kraw[2][2][C][C];   /* k rows of the current and the next item (TMA, 128-byte swizzled); then
                                     beta gamma k in f16 in place; then W (staging for the slot) */
     uint16_t vraw[2][2][C][C];   /* v rows; then beta v in f16 in place; then U~^T (staging) */
+    uint16_t kt[2][C][C];        /* K~ [64 rows][128 dk] in the k tile's layout (staging for one bulk store) */
     float graw[2][C], braw[2][C];
     float a32[4][16][20];        /* the diagonal 16x16 blocks of A, f32 */
     uint16_t l16[C][TP];         /* A, f16 (its off-diagonal blocks are read) */
@@ -202,7 +206,7 @@ struct PrepSmem {
     uint16_t tmp[3][16][24];     /* per-warp 16x16 staging */
     int32_t r0[kSeqCache], base[kSeqCache + 1];
     uint64_t landed[2];          /* the k and v rows of buffer b have landed */
-    int abort, ok, n_cached, claim;
+    int abort, ok, n_cached, claim, claim_next;   /* claim_next: the item after the current one */
 };
 static_assert(offsetof(PrepSmem, vraw) % 1024 == 0, "TMA 128-byte swizzle destinations");
 static_assert(sizeof(PrepSmem::Meta) == kSlotBytes - kSlotMeta && offsetof(PrepSmem, meta) % 16 == 0, "the slot's meta, one bulk store");
@@ -282,7 +286,7 @@ __device__ void prep_issue(const GdnPlan& p, const CUtensorMap* kmap, const CUte
     int64_t row0 = 0;
     int len = 0;
     locate_chunk(p, s.r0, s.base, s.n_cached, slot, &row0, &len);
-    if (tid == 0) {
+    if (tid == kStoreTid) {
         rf::mbar_arrive_expect_tx(&s.landed[buf], 2 * kTileBytes);
         rf::tma_load_3d(&s.kraw[buf][0][0][0], kmap, &s.landed[buf], 0, (int)hk, (int)row0);
         rf::tma_load_3d(&s.kraw[buf][1][0][0], kmap, &s.landed[buf], C, (int)hk, (int)row0);
@@ -297,9 +301,8 @@ __device__ void prep_issue(const GdnPlan& p, const CUtensorMap* kmap, const CUte
     }
 }
 
-/* Item `it`'s slot is complete: its bulk stores have completed (the caller waited for them) and the K~^T
- * stores of every transform thread precede a transform barrier the caller passed since; made visible at
- * GPU scope, then flagged. One thread. */
+/* Item `it`'s slot is complete: its bulk stores (K~, then W, U~^T and the meta) have completed (the caller
+ * waited for them); made visible at GPU scope, then flagged. One thread. */
 __device__ void publish_item(const GdnPlan& p, int64_t it) {
     asm volatile("fence.proxy.async.global;" ::: "memory");
     __threadfence();
@@ -328,6 +331,7 @@ __device__ void prep_role(const CUtensorMap& kmap, const CUtensorMap& vmap, cons
         rf::tma_prefetch_map(&kmap);
         rf::tma_prefetch_map(&vmap);
         s.claim = atomicAdd(&p.ctl->next_item, 1);
+        s.claim_next = atomicAdd(&p.ctl->next_item, 1);
     }
     sync();
     const int64_t items = (int64_t)p.tab[3 * n_seq] * g.n_head_v;
@@ -337,14 +341,14 @@ __device__ void prep_role(const CUtensorMap& kmap, const CUtensorMap& vmap, cons
     rf::cp_async_commit();
     int buf = 0;
     int64_t waited = 0, issued = item < items ? 1 : 0;
-    int64_t pending = -1;   /* thread 0: the item whose slot stores are issued but not yet published */
+    int64_t pending = -1;   /* kStoreTid: the item whose slot stores are issued but not yet published */
+    int claim = 0;          /* kStoreTid: the item after the next one, claimed during this item */
     while (item < items) {
-        if (tid == 0) s.claim = atomicAdd(&p.ctl->next_item, 1);   /* the item after this one */
         rf::cp_async_wait<0>();
         if (tid == 0) s.ok = rf::mbar_wait(&s.landed[buf], (uint32_t)((waited >> 1) & 1), &s.abort, rf::kErrGdnWait);
         sync();
         if (!s.ok) break;
-        const int64_t next = s.claim;
+        const int64_t next = s.claim_next;   /* claimed an item ago (the counter's latency stays off the path) */
         ++waited;
         const int64_t slot = item / g.n_head_v, h = item % g.n_head_v;
         int64_t row0 = 0;
@@ -409,12 +413,13 @@ __device__ void prep_role(const CUtensorMap& kmap, const CUtensorMap& vmap, cons
                     if ((i >> 4) == (j >> 4)) *(float2*)&s.a32[i >> 4][i & 15][j & 15] = make_float2(v[0], v[1]);
                 }
         }
-        /* The previous item's slot stores are complete: publish it, and start the next item's loads into
-         * the buffer those stores read. */
-        if (tid == 0 && pending >= 0) {
+        /* While the other warps form K K^T: the previous item's slot stores are complete, so it is published,
+         * the other k / v buffer and the K~ staging are free, and the next item's loads start. */
+        if (tid == kStoreTid) {
             rf::bulk_store_wait();
-            publish_item(p, pending);
+            if (pending >= 0) publish_item(p, pending);
             pending = -1;
+            claim = atomicAdd(&p.ctl->next_item, 1);   /* its result is first needed at the item's end */
         }
         if (next < items) {
             prep_issue(p, &kmap, &vmap, s, next, buf ^ 1, tid);
@@ -424,27 +429,21 @@ __device__ void prep_role(const CUtensorMap& kmap, const CUtensorMap& vmap, cons
         sync();
 
         /* In place, 16-byte chunks at their swizzled places: k -> x1 = beta gamma k (f16); v -> x2 = beta v
-         * (f16); and K~^T (K~ = k exp(G_L - G), f16) to the slot, transposed: lane l of warp w holds row
-         * 32 (w & 1) + l, so each 2-byte store of a warp fills 64 contiguous bytes of one K~^T row. Rows past
-         * the chunk zero. The blocks of T above the diagonal zero. */
+         * (f16); and K~ = k exp(G_L - G) (f16) into the staging tile, in the k tile's own layout (the chain
+         * reads it as an MN-major operand). Lane l of warp w holds row 32 (w & 1) + l. Rows past the chunk
+         * zero. The blocks of T above the diagonal zero. */
         {
             const int r = 32 * (w & 1) + l;
             const bool in = r < len;
             const float gr = G[r], br = beta[r];
             const float fk = in ? __expf(gl - gr) : 0.0f, fx = in ? br * __expf(gr) : 0.0f;
-            uint16_t* kt = (uint16_t*)(out + kSlotK);
+            const uint32_t kst = rf::saddr(&s.kt[0][0][0]);
 #pragma unroll
             for (int it = 0; it < 4; ++it) {
                 const int seg = (w >> 1) + 4 * it;
                 const uint32_t off = rf::sw128_off(r, seg * 8);
                 const uint4 kr = lds128(ktile + off), vr = lds128(vtile + off);
-                const uint32_t rw[4] = { kr.x, kr.y, kr.z, kr.w };
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const uint32_t pk = in ? rf::pack_f16(fk * __uint_as_float(rw[e] << 16), fk * __uint_as_float(rw[e] & 0xffff0000u)) : 0u;
-                    kt[rf::sw128_off(seg * 8 + 2 * e, r, 0) >> 1] = (uint16_t)pk;
-                    kt[rf::sw128_off(seg * 8 + 2 * e + 1, r, 0) >> 1] = (uint16_t)(pk >> 16);
-                }
+                sts128(kst + off, scale_bf16x8_to_f16(kr, fk, in));
                 sts128(ktile + off, scale_bf16x8_to_f16(kr, fx, in));
                 sts128(vtile + off, scale_bf16x8_to_f16(vr, br, in));
             }
@@ -454,7 +453,12 @@ __device__ void prep_role(const CUtensorMap& kmap, const CUtensorMap& vmap, cons
             const int bi = blk < 3 ? 0 : blk < 5 ? 1 : 2, bj = blk < 3 ? blk + 1 : blk < 5 ? blk - 1 : 3;
             *(uint32_t*)&s.t16[16 * bi + r][16 * bj + 2 * cp] = 0u;
         }
+        rf::fence_proxy_async_smem();   /* K~ staged by every thread, for the bulk store */
         sync();
+        if (tid == kStoreTid) {
+            rf::bulk_store(out + kSlotK, &s.kt[0][0][0], kTileBytes);
+            rf::bulk_store_commit();
+        }
 
         /* Diagonal blocks of T, by substitution in f32: warp w solves block w >> 1 for columns
          * 8 (w & 1)..+8, lane l holding row l & 15 of 4 columns; row j is final at step j and is
@@ -551,18 +555,19 @@ __device__ void prep_role(const CUtensorMap& kmap, const CUtensorMap& vmap, cons
         }
         rf::fence_proxy_async_smem();
         sync();
-        if (tid == 0) {   /* W, U~^T and G|beta|gamma_L to the slot; the next issue into this buffer waits for them */
+        if (tid == kStoreTid) {   /* W, U~^T and G|beta|gamma_L to the slot; published during the next item */
             rf::bulk_store(out + kSlotW, &s.kraw[buf][0][0][0], kTileBytes);
             rf::bulk_store(out + kSlotU, &s.vraw[buf][0][0][0], kTileBytes);
             rf::bulk_store(out + kSlotMeta, &mt, sizeof(mt));
             rf::bulk_store_commit();
             pending = item;
+            s.claim_next = claim;   /* read after the next item's first barrier */
         }
         item = next;
         buf ^= 1;
     }
     rf::cp_async_wait<0>();
-    if (tid == 0) {
+    if (tid == kStoreTid) {
         rf::bulk_store_wait();
         if (pending >= 0 && s.ok) publish_item(p, pending);
         /* After a timed-out wait: let the copies already issued land before the CTA's shared memory is
@@ -704,9 +709,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const GdnPl
                 rf::mma_f16(pv[2 * pr + 1], a, fb[ks & 1][pr][2], fb[ks & 1][pr][3]);
             }
         }
-        /* K~'s first k-step, ahead of the exchange (K~^T [dk][rows]: B[k = row][n = dk]). */
+        /* K~'s first k-step, ahead of the exchange (K~ [rows][dk]: B[k = row][n = dk], transposing loads). */
 #pragma unroll
-        for (int pr = 0; pr < 4; ++pr) rf::load_b_nk_sw(fb[0][pr], kttile, 64 * kh + 16 * pr, 0);
+        for (int pr = 0; pr < 4; ++pr) rf::load_b_kn_sw(fb[0][pr], kttile, 0, 64 * kh + 16 * pr);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             *(float2*)&s.part[b][w][gq][8 * j + 2 * tq] = make_float2(pv[j][0], pv[j][1]);
@@ -736,7 +741,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const GdnPl
         for (int ks = 0; ks < 4; ++ks) {
             if (ks < 3)
 #pragma unroll
-                for (int pr = 0; pr < 4; ++pr) rf::load_b_nk_sw(fb[(ks + 1) & 1][pr], kttile, 64 * kh + 16 * pr, 16 * (ks + 1));
+                for (int pr = 0; pr < 4; ++pr) rf::load_b_kn_sw(fb[(ks + 1) & 1][pr], kttile, 16 * (ks + 1), 64 * kh + 16 * pr);
             uint32_t a[4];
             rf::c_to_a(a, pv[2 * ks], pv[2 * ks + 1]);
             if (ow && (ks >> 1) == kh) {   /* output form: U^T in f16 (the two dk halves hold the same V') */
@@ -769,25 +774,25 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const GdnPl
 /* ------------------------------------------------------------------ phase 2 on tensor memory (state-only form) */
 
 /* One CTA per (v-head, sequence): the whole 128 x 128 state in tensor memory, the chunk's two products as
- * tcgen05.mma (kind::f16, f32 accumulation, every operand K-major in 128-byte-swizzled shared memory):
+ * tcgen05.mma (kind::f16, f32 accumulation, operands in 128-byte-swizzled shared memory, K~ MN-major):
  *     D1 = S W^T           (M 128 dv, N 64 chunk rows, K 128 dk)      eight K-16 steps
  *     D2 += V'^T K~        (M 128 dv, N 128 dk, K 64 chunk rows)      four K-16 steps, D2 = gamma_L S before
  * Roles, handing over through mbarriers only (every wait bounded):
  *   warps 0-7   tensor-memory lane quarter w & 3 (dv rows 32 (w & 3)..+32), column half w >> 2; a thread is
  *               one dv row: V' = U~ - D1 in f16 (the second product's A), then the next chunk's f16 state
  *               (the first product's A) and gamma_L(next) S back into D2
- *   warp 8      lane 0 keeps three chunks' inputs in flight (bulk copies of the slot's W|K~^T, U~^T, gamma_L)
+ *   warp 8      lane 0 keeps three chunks' inputs in flight (bulk copies of the slot's W|K~, U~^T, gamma_L)
  *   warp 9      lane 0 issues the products as their operands are ready */
 constexpr int kTcEpi = 8, kTcThreads = 32 * (kTcEpi + 2), kTcStages = 3;
 /* Tensor-memory columns: D1 (64), the f16 state A_S (64: two dk a column), D2 (128), V'^T A_V (32). */
 constexpr uint32_t kTmemTc = 512, kColD1 = 0, kColAs = 64, kColD2 = 128, kColAv = 256;
 /* Instruction descriptors, kind::f16: D f32 (bit 4), A and B f16, both K-major, N >> 3 at bit 17, M >> 4 at 24. */
 constexpr uint32_t kIdescPv = (1u << 4) | ((uint32_t)(64 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-constexpr uint32_t kIdescUp = (1u << 4) | ((uint32_t)(128 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+constexpr uint32_t kIdescUp = (1u << 4) | (1u << 16) /* B MN-major */ | ((uint32_t)(128 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 
 struct TcStage {
     uint16_t w[2][C][C];       /* W [64 rows][128 dk]: two 64-column halves */
-    uint16_t kt[D][C];         /* K~^T [128 dk][64 rows] */
+    uint16_t kt[2][C][C];      /* K~ [64 rows][128 dk]: two 64-column halves (an MN-major operand) */
     uint16_t u[D][C];          /* U~^T [128 dv][64 rows] */
     float gl[256];             /* gamma_L (first word); the stage padded to 1024 bytes */
 };
@@ -876,7 +881,7 @@ __device__ void chain_tc_role(const GdnPlan& p, TcSmem& s, int64_t first, int64_
                     const uint8_t* src = slot_ptr(p, base + c, h);
                     TcStage& sg = s.st[st];
                     rf::mbar_arrive_expect_tx(&s.landed[st], 3 * kTileBytes + 16);
-                    rf::bulk_load(&sg.w[0][0][0], src + kSlotW, 2 * kTileBytes, &s.landed[st]);   /* W and K~^T */
+                    rf::bulk_load(&sg.w[0][0][0], src + kSlotW, 2 * kTileBytes, &s.landed[st]);   /* W and K~ */
                     rf::bulk_load(&sg.u[0][0], src + kSlotU, kTileBytes, &s.landed[st]);
                     rf::bulk_load(&sg.gl[0], src + kSlotGl, 16, &s.landed[st]);
                     ++issued;
@@ -889,7 +894,7 @@ __device__ void chain_tc_role(const GdnPlan& p, TcSmem& s, int64_t first, int64_
                     const int64_t k = k0 + c;
                     const int st = (int)(k % kTcStages);
                     const uint32_t par = (uint32_t)(k & 1);
-                    const uint32_t wt = rf::saddr(&s.st[st].w[0][0][0]), kt = rf::saddr(&s.st[st].kt[0][0]);
+                    const uint32_t wt = rf::saddr(&s.st[st].w[0][0][0]), kt = rf::saddr(&s.st[st].kt[0][0][0]);
                     /* D1 = S W^T: the chunk's inputs landed and the lanes wrote this chunk's f16 state */
                     if (!rf::mbar_wait(&s.landed[st], (uint32_t)((k / kTcStages) & 1), abort, rf::kErrGdnWait) ||
                         !rf::mbar_wait(&s.as_ready, par, abort, rf::kErrGdnWait))
@@ -907,7 +912,7 @@ __device__ void chain_tc_role(const GdnPlan& p, TcSmem& s, int64_t first, int64_
                     rf::tc_fence_after();
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
-                        rf::umma_f16_ts(tmem + kColD2, tmem + kColAv + 8 * kk, rf::sw128_kmajor_desc(kt + kk * 32), kIdescUp, 1);
+                        rf::umma_f16_ts(tmem + kColD2, tmem + kColAv + 8 * kk, rf::sw128_mnmajor_desc(kt + kk * 2048, 8192), kIdescUp, 1);
                     rf::mma_commit(&s.consumed[st]);   /* the stage is free once these products have read it */
                     rf::mma_commit(&s.d2_full);
                 }

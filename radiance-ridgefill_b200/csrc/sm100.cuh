@@ -144,6 +144,8 @@ __device__ __forceinline__ void bulk_store_commit() { asm volatile("cp.async.bul
 __device__ __forceinline__ void bulk_store_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 /* The committed bulk stores are complete. */
 __device__ __forceinline__ void bulk_store_wait() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+/* Every committed bulk store group but the most recent one is complete. */
+__device__ __forceinline__ void bulk_store_wait_prior() { asm volatile("cp.async.bulk.wait_group 1;" ::: "memory"); }
 /* Generic-proxy writes to shared memory become visible to the async proxy (bulk copies, TMA). */
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -186,6 +188,18 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
     uint64_t d = (uint64_t)((saddr & 0x3ffffu) >> 4);
     d |= (uint64_t)1 << 16;
+    d |= (uint64_t)(1024 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+/* Shared-memory matrix descriptor of an MN-major operand tile with 128-byte swizzle: 64 consecutive 16-bit
+ * MN elements a 128-byte row, consecutive K in consecutive rows, 8-row groups 1024 bytes apart (SBO), the
+ * next 64 MN elements `mn_block_bytes` further (LBO); descriptor version 1. */
+__device__ __forceinline__ uint64_t sw128_mnmajor_desc(uint32_t saddr, uint32_t mn_block_bytes) {
+    uint64_t d = (uint64_t)((saddr & 0x3ffffu) >> 4);
+    d |= (uint64_t)((mn_block_bytes >> 4) & 0x3fffu) << 16;
     d |= (uint64_t)(1024 >> 4) << 32;
     d |= (uint64_t)1 << 46;
     d |= (uint64_t)2 << 61;
