@@ -38,6 +38,30 @@ def test_quantiser_matches_oracle(cuda, product_lib, M, K, group):
     assert np.array_equal(s.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
 
 
+def test_quantiser_near_half_integers(cuda, product_lib):
+    """The codes are rint(x / s) with the quotient correctly rounded. Rows whose x * (1 / s) rounds to a
+    different integer than x / s (both in f32) are present here by construction of the data (checked), and
+    the device's codes still equal the oracle's bit for bit."""
+    torch = cuda
+    M, K, group = 512, 2048, 2048
+    rng = np.random.default_rng(5)
+    xb = H.f32_to_bf16_bits(rng.standard_normal((M, K)).astype(np.float32))
+    xf = H.bf16_bits_to_f32(xb)
+    sc = (np.abs(xf).max(1) / np.float32(127)).astype(np.float32)
+    naive = np.rint((xf * (np.float32(1) / sc)[:, None]).astype(np.float32))
+    exact = np.rint((xf / sc[:, None]).astype(np.float32))
+    assert int((naive != exact).sum()) >= 100   # the data does reach the half-integer cases
+    q_ref, s_ref = H.oracle_quant(xb, group)
+    x = torch.from_numpy(xb.view(np.int16)).cuda()
+    q = torch.full((M, K), 99, dtype=torch.int8, device="cuda")
+    s = torch.full((M, 1), -1.0, dtype=torch.float32, device="cuda")
+    rc = H.launch(product_lib, "ridgefill_quant_act_i8g", [H.dev(x, abi.BF16), H.dev(q), H.dev(s)],
+                  [H.pint("M", M), H.pint("n", K), H.pint("group", group), H.pstr("dtype", "bf16")])
+    assert rc == abi.OK
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), s_ref.view(np.uint32))
+
+
 def _gemm_case(rng, M, N, K, group):
     a = rng.integers(-127, 128, (M, K)).astype(np.int8)
     b = rng.integers(-127, 128, (N, K)).astype(np.int8)
