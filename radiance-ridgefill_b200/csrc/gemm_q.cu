@@ -462,9 +462,43 @@ __global__ void __launch_bounds__(kQThreads) quant_seg_kernel(RidgeFillQuant g) 
     }
 }
 
+/* The int8 codes of eight bf16 values (a 16-byte chunk) at scale sc (inv = 1 / sc, rounded), packed in order:
+ * rint(x / sc) with the quotient correctly rounded, clamped to [-127, 127] — the oracle's arithmetic. The fast
+ * path forms y = fma(x, inv, 1.5 * 2^23), which rounds the exact product x * inv to an integer (to nearest, ties
+ * to even) in y's low mantissa bits, so y's low byte is the code in two's complement (|x * inv| <= 127 (1 + 2^-23)
+ * here: no clamp), and e = fma(x, inv, -(y - 1.5 * 2^23)), the product's distance from that integer. The exact
+ * product lies within 2^-17 of the exact quotient and the rounded quotient within 2^-17 of it, so both round to
+ * the same integer unless |e| is within 2^-16 of 1/2; a chunk with any |e| above 1/2 - 2^-15 (or not finite)
+ * forms every quotient exactly. */
+__device__ __forceinline__ uint2 quant_chunk8(uint4 v, float sc, float inv) {
+    constexpr float kMagic = 12582912.0f;   /* 1.5 * 2^23 */
+    const uint32_t vw[4] = { v.x, v.y, v.z, v.w };
+    uint32_t rb[8];
+    bool near = false;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const float xv = __uint_as_float((e & 1) ? (vw[e >> 1] & 0xffff0000u) : (vw[e >> 1] << 16));
+        const float y = fmaf(xv, inv, kMagic);
+        const float d = fmaf(xv, inv, -(y - kMagic));
+        near |= !(fabsf(d) <= 0.5f - 0x1p-15f);
+        rb[e] = __float_as_uint(y);
+    }
+    if (near) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float xv = __uint_as_float((e & 1) ? (vw[e >> 1] & 0xffff0000u) : (vw[e >> 1] << 16));
+            const int r = __float2int_rn(__fdiv_rn(xv, sc));
+            rb[e] = (uint32_t)(r > 127 ? 127 : (r < -127 ? -127 : r));
+        }
+    }
+    const uint32_t lo = __byte_perm(__byte_perm(rb[0], rb[1], 0x0040), __byte_perm(rb[2], rb[3], 0x0040), 0x5410);
+    const uint32_t hi = __byte_perm(__byte_perm(rb[4], rb[5], 0x0040), __byte_perm(rb[6], rb[7], 0x0040), 0x5410);
+    return make_uint2(lo, hi);
+}
+
 /* One pass over HBM for a group of 256 NV columns held in registers: a warp per (row, group), lane l holds
- * the 16-byte chunks l, l + 32, ... (coalesced 512-byte warp loads); absmax by shuffles, then the codes.
- * The same arithmetic as quant_kernel. */
+ * the 16-byte chunks l, l + 32, ... (coalesced 512-byte warp loads); absmax by shuffles, then the codes
+ * (quant_chunk8). The same arithmetic as quant_kernel. */
 template <int NV>
 __global__ void __launch_bounds__(256) quant_reg_kernel(RidgeFillQuant g) {
     const int lane = threadIdx.x & 31;
@@ -487,21 +521,10 @@ __global__ void __launch_bounds__(256) quant_reg_kernel(RidgeFillQuant g) {
         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         const float sc = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 127.0f);
         if (lane == 0) g.s[m * g.lds + j] = sc;
+        const float inv = __frcp_rn(sc);
         int8_t* q = g.q + m * g.ldq + j * g.group;
 #pragma unroll
-        for (int i = 0; i < NV; ++i) {
-            const uint32_t vw[4] = { v[i].x, v[i].y, v[i].z, v[i].w };
-            uint32_t lo = 0, hi = 0;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const float xv = __uint_as_float((e & 1) ? (vw[e >> 1] & 0xffff0000u) : (vw[e >> 1] << 16));
-                int r = __float2int_rn(__fdiv_rn(xv, sc));
-                r = r > 127 ? 127 : (r < -127 ? -127 : r);
-                if (e < 4) lo |= (uint32_t)(uint8_t)(int8_t)r << (8 * e);
-                else hi |= (uint32_t)(uint8_t)(int8_t)r << (8 * (e - 4));
-            }
-            *(uint2*)(q + 8 * (lane + 32 * i)) = make_uint2(lo, hi);
-        }
+        for (int i = 0; i < NV; ++i) *(uint2*)(q + 8 * (lane + 32 * i)) = quant_chunk8(v[i], sc, inv);
     }
 }
 
@@ -644,7 +667,7 @@ extern "C" int ridgefill_quant_act_device(const RadArgs* a, RadStream s) {
     if (g.M == 0) return RAD_OK;
     const bool pow2 = (g.group & (g.group - 1)) == 0;
     const int64_t warps = g.M * (g.K / g.group);
-    const int64_t blocks = (warps + 7) / 8, cap = (int64_t)rf::sm_count() * 8;
+    const int64_t blocks = (warps + 7) / 8, cap = (int64_t)rf::sm_count() * 16;
     const unsigned grid = (unsigned)(blocks < cap ? blocks : cap);
     switch (g.group) {   /* a group of 256 NV columns in registers */
         case 256: quant_reg_kernel<1><<<grid, 256, 0, rf::as_stream(s)>>>(g); return rf::launch_status();
