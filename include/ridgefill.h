@@ -59,6 +59,10 @@ enum { QA_X = 0, QA_Q, QA_S };
 /* ridgefill_gdn_fill (new; the chunk scan's operands, arch/qwen4exp_fill.h:55-60, without kkt:
  * the intra-chunk transform is computed inside the op). */
 enum { GD_Q = 0, GD_K, GD_V, GD_G, GD_BETA, GD_STATE, GD_STATE_IDX, GD_CU, GD_O };
+/* ridgefill_gdn_conv_prep (new; the operands of the DeltaNet block's conv_prep issue, arch/qwen4exp_fill.h:44-50,
+ * with the gate written per row rather than in its in-chunk cumulative form). */
+enum { CP_X = 0, CP_W, CP_BIAS, CP_A_LOG, CP_DT_BIAS, CP_STATE, CP_CU, CP_A, CP_B, CP_IDX, CP_CTX, CP_Q, CP_K, CP_V,
+       CP_G, CP_BETA };
 
 /* ------------------------------------------------------------------ the shared formulas */
 
@@ -297,6 +301,36 @@ typedef struct RidgeFillGdn {
     float          scale;
 } RidgeFillGdn;
 
+/* ridgefill_gdn_conv_prep: the DeltaNet block's input preparation over each sequence [cu[i], cu[i+1]).
+ * x bf16 [T, C] holds the projected q|k|v channels (C = 2 Hk dk + Hv dv, that order); per channel c and row t a
+ * causal depthwise convolution of width 4 over the sequence's rows, the rows before its start taken from the
+ * conv state (ctx_lens[i] > 0) or zero:
+ *     u = bias[c] + w[c,0] x[t-3,c] + w[c,1] x[t-2,c] + w[c,2] x[t-1,c] + w[c,3] x[t,c]   (f32, in that order)
+ *     y = u / (1 + exp(-u))                                                               (SiLU)
+ * q and k heads are L2-normalised, y / sqrt(sum_head y^2 + 1e-6); q, k, v rounded to bf16. Per v-head h:
+ *     g[t,h] = -exp(A_log[h]) * softplus(a[t,h] + dt_bias[h]),  beta[t,h] = 1 / (1 + exp(-b[t,h])).
+ * The conv state [slots, 3, C] bf16 of each sequence's slot idx[i] is then the last three input rows of
+ * (state, rows) (a slot outside the pool: zero history, nothing written). Rows outside every sequence are not
+ * written. */
+typedef struct RidgeFillConvPrep {
+    const uint16_t* x;       int64_t x_row;
+    const uint16_t* w;                          /* [C, 4] bf16, dense */
+    const uint16_t* bias;                       /* [C] bf16 or null */
+    const float*   a_log;    const float* dt_bias;
+    uint16_t*      state;    int64_t st_slot, n_states;
+    const int32_t* cu;       int64_t n_seq;
+    const uint16_t* a;       int64_t a_row;
+    const uint16_t* b;       int64_t b_row;
+    const int32_t* idx;      int64_t idx_pitch;
+    const int32_t* ctx;                         /* [n_seq] or null (every sequence starts fresh) */
+    uint16_t*      q;        int64_t q_row, q_head;
+    uint16_t*      k;        int64_t k_row, k_head;
+    uint16_t*      v;        int64_t v_row, v_head;
+    float*         g;        int64_t g_row;
+    float*         beta;     int64_t beta_row;
+    int64_t        T, n_head_k, n_head_v, dk, dv, width;
+} RidgeFillConvPrep;
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -330,6 +364,7 @@ typedef struct RidgeFillGemmBias {
 int ridgefill_gemm_bias_parse(const RadArgs* a, RidgeFillGemmBias* out);
 int ridgefill_quant_parse(const RadArgs* a, RidgeFillQuant* out);
 int ridgefill_gdn_parse(const RadArgs* a, RidgeFillGdn* out);
+int ridgefill_conv_prep_parse(const RadArgs* a, RidgeFillConvPrep* out);
 
 /* The device rows (kernels/ridgefill.h:304-310 and the new ops): async launches on `s` (a
  * cudaStream_t); no allocation, no synchronisation. */
@@ -345,6 +380,7 @@ int ridgefill_gemm_nt_q_bias_device(const RadArgs* a, RadStream s);
 int ridgefill_gemm_nt_bias_device(const RadArgs* a, RadStream s);
 int ridgefill_quant_act_device(const RadArgs* a, RadStream s);
 int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s);
+int ridgefill_gdn_conv_prep_device(const RadArgs* a, RadStream s);
 
 /* The first error code a tensor-core kernel of this library recorded after giving up on a bounded
  * wait (0: none), optionally cleared. Synchronises the current device: a diagnostic, never called on

@@ -68,6 +68,12 @@ static const RadParamSpec pGdn[] = { RF_P_INT("M"), RF_P_INT("n_head_k"), RF_P_I
                                      RF_P_INT("head_v"), RF_P_INT("chunk"), RF_P_OPT("scale", RAD_P_F64) };
 static const RadOperandSpec oGdn[] = { RF_IN_OPT("q"), RF_IN("k"), RF_IN("v"), RF_IN("g"), RF_IN("beta"),
                                        RF_INOUT("state"), RF_IN("state_idx"), RF_IN("cu_seqlens"), RF_OUT_OPT("o") };
+static const RadParamSpec pConv[] = { RF_P_INT("M"), RF_P_INT("n_head_k"), RF_P_INT("n_head_v"), RF_P_INT("head_k"),
+                                      RF_P_INT("head_v"), RF_P_INT("conv") };
+static const RadOperandSpec oConv[] = { RF_IN("x"), RF_IN("w_conv"), RF_IN_OPT("conv_bias"), RF_IN("A_log"),
+                                        RF_IN("dt_bias"), RF_INOUT("conv_state"), RF_IN("cu_seqlens"), RF_IN("a"),
+                                        RF_IN("b"), RF_IN("conv_idx"), RF_IN_OPT("ctx_lens"), RF_OUT("q"), RF_OUT("k"),
+                                        RF_OUT("v"), RF_OUT("g"), RF_OUT("beta") };
 
 /* The reference's nine schemas come first, in its order (kernels/rows.cpp:84-168). */
 enum { kReferenceSchemas = 9 };
@@ -119,6 +125,14 @@ static const RadOpSchema kSchemas[] = {
   "pool: skipped), state f32 [slots, Hv, dv, dk] updated in place; per row t and v-head h (k-head "
   "h / (Hv/Hk)): S = exp(g[t,h]) S; S += beta[t,h] (v_t - S k_t) k_t^T; o_t = scale * S q_t (o and q optional "
   "together: absent = state-only fill). Chunked (WY form) on the device, `chunk` rows a tile." },
+{ "ridgefill_gdn_conv_prep", RF_ARR(pConv), RF_ARR(oConv),
+  "The DeltaNet block's input preparation over each sequence [cu[i], cu[i+1]): x bf16 [T, C] = q|k|v channels "
+  "(C = 2 Hk dk + Hv dv); per channel a causal depthwise convolution of width `conv` (4) over the sequence's rows, "
+  "u = bias + sum_j w[c, j] x[t - 3 + j] in f32 in j order, the rows before the start from conv_state[conv_idx[i]] "
+  "(ctx_lens[i] > 0) or zero; y = u / (1 + exp(-u)); q and k heads divided by sqrt(sum y^2 + 1e-6); q, k, v bf16. "
+  "g[t, h] = -exp(A_log[h]) softplus(a[t, h] + dt_bias[h]) (threshold 20), beta = sigmoid(b); f32. conv_state "
+  "bf16 [slots, 3, C] then holds each sequence's last three input rows (a slot outside the pool: zero history, "
+  "not written). Rows outside every sequence are not written." },
 };
 
 /* ------------------------------------------------------------------ cold-call descriptions */
@@ -245,6 +259,16 @@ inline int shape_gdn(const RadParam* p, int n_p, int operand, RadOpdDesc* out) {
                                 opd(RAD_F32, { T, hv }, RAD_FILL_SIGMOID), opd(RAD_F32, { T, hv }, RAD_FILL_SIGMOID),
                                 opd(RAD_F32, { slots, hv, dv, dk }), opd_idx({ 1, 1 }, slots),
                                 opd_idx({ 2 }, T, RAD_OPD_F_IDX_CU), opd(RAD_BF16, { T, hv, dv }) });
+}
+
+inline int shape_conv_prep(const RadParam* p, int n_p, int operand, RadOpdDesc* out) {
+    const int64_t T = dim(p, n_p, "M"), hk = dim(p, n_p, "n_head_k"), hv = dim(p, n_p, "n_head_v");
+    const int64_t dk = dim(p, n_p, "head_k"), dv = dim(p, n_p, "head_v"), C = 2 * hk * dk + hv * dv, slots = 3;
+    return pick(out, operand, { opd(RAD_BF16, { T, C }), opd(RAD_BF16, { C, 4 }), opd(RAD_BF16, { C }), opd(RAD_F32, { hv }),
+                                opd(RAD_F32, { hv }), opd(RAD_BF16, { slots, 3, C }), opd_idx({ 2 }, T, RAD_OPD_F_IDX_CU),
+                                opd(RAD_BF16, { T, hv }), opd(RAD_BF16, { T, hv }), opd_idx({ 1 }, slots),
+                                opd(RAD_I32, { 1 }), opd(RAD_BF16, { T, hk, dk }), opd(RAD_BF16, { T, hk, dk }),
+                                opd(RAD_BF16, { T, hv, dv }), opd(RAD_F32, { T, hv }), opd(RAD_F32, { T, hv }) });
 }
 
 }  // namespace ridgefill_schema

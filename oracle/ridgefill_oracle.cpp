@@ -12,10 +12,12 @@
  *     pass against this library, and tests compare it with the reference's host rows compiled from
  *     source (oracle/_ref).
  *  2. Plain-pointer oracles for the ops the reference does not contain (their arithmetic lives in
- *     radiance's libr4d, absent): the activation quantiser, the int8 projector GEMM with its f32
- *     block fold, and the gated delta rule. PARITY UNPINNED for the GEMM and the delta rule (no
- *     reference source, test or fixture exists for them); the quantiser's rounding rule is the
- *     reference's quantise_i8 (tools/ridgefill_projector.py:333-344) with an f32 scale.
+ *     radiance's libr4d and in-tree ops, absent): the activation quantiser, the int8 projector GEMM with
+ *     its f32 block fold, the bf16 GEMM with bias / SiLU / residual, the gated delta rule and the DeltaNet
+ *     input preparation (convolution, SiLU, L2 norm, gate). PARITY UNPINNED for all but the quantiser's
+ *     rounding rule (no reference source, test or fixture exists for them; the gate is the reference's
+ *     softplus rule, kernels/ridgefill.h:93-97); the quantiser's rounding rule is the reference's
+ *     quantise_i8 (tools/ridgefill_projector.py:333-344) with an f32 scale.
  *
  * Built with -ffp-contract=off so `x + s*c` rounds twice, as the reference's host rows do
  * (kernels/CMakeLists.txt:48-51).
@@ -503,6 +505,65 @@ void oracle_gemm_nt_q(const int8_t* a, int64_t lda, const float* a_scale, int64_
             if (bias) out = f2bf(bf16f(out) + bf16f(bias[n]));
             y[m * ldy + n] = out;
         }
+}
+
+/* ridgefill_gdn_conv_prep: the DeltaNet block's input preparation (issue site arch/qwen4exp_fill.h:41-50; the
+ * op itself is radiance's and absent, so this is the published Gated DeltaNet input path restated, with the
+ * reference's gate, kernels/ridgefill.h:93-97). x bf16 [T, C] (row pitch x_row), C = 2 Hk 128 + Hv 128 channels
+ * q|k|v; per sequence i of cu (bounds clamped into [0, T]) and row t, channel c:
+ *     u = bias[c] + w[c,0] x[t-3] + w[c,1] x[t-2] + w[c,2] x[t-1] + w[c,3] x[t]   (f32 fma in that order; rows
+ *         before the sequence start from state[idx[i]] when ctx[i] > 0 and the slot is in the pool, else zero)
+ *     y = u / (1 + exp(-u));  q, k heads: y / sqrt(sum_head y^2 + 1e-6);  bf16
+ *     g[t,h] = -exp(A_log[h]) softplus(a[t,h] + dt_bias[h]);  beta[t,h] = 1 / (1 + exp(-b[t,h]))
+ * then state[idx[i]] = the last three input rows of (history, rows). Outputs dense: q, k [T, Hk, 128],
+ * v [T, Hv, 128], g, beta [T, Hv]; rows outside every sequence are left as they are. */
+void oracle_gdn_conv_prep(const uint16_t* x, int64_t x_row, const uint16_t* w, const uint16_t* bias, const float* a_log,
+                          const float* dt_bias, uint16_t* state, int64_t n_states, const int32_t* cu, int64_t n_seq,
+                          const uint16_t* a, const uint16_t* b, const int32_t* idx, const int32_t* ctx, uint16_t* q,
+                          uint16_t* k, uint16_t* v, float* g, float* beta, int64_t T, int64_t Hk, int64_t Hv) {
+    const int64_t C = 2 * Hk * 128 + Hv * 128;
+    std::vector<float> hist((size_t)(3 * C)), y((size_t)C);
+    for (int64_t i = 0; i < n_seq; ++i) {
+        const int64_t s0 = std::min(std::max((int64_t)cu[i], (int64_t)0), T);
+        const int64_t e0 = std::min(std::max((int64_t)cu[i + 1], s0), T);
+        const int64_t slot = idx[i];
+        const bool in_pool = slot >= 0 && slot < n_states;
+        const bool has = ctx && ctx[i] > 0 && in_pool;
+        for (int64_t j = 0; j < 3 * C; ++j) hist[(size_t)j] = has ? bf16f(state[slot * 3 * C + j]) : 0.0f;
+        auto at = [&](int64_t row, int64_t c) {   /* input row `row` (>= s0 - 3) of this sequence */
+            return row >= s0 ? bf16f(x[row * x_row + c]) : hist[(size_t)((3 - (s0 - row)) * C + c)];
+        };
+        for (int64_t t = s0; t < e0; ++t) {
+            for (int64_t c = 0; c < C; ++c) {
+                float u = bias ? bf16f(bias[c]) : 0.0f;
+                for (int j = 0; j < 4; ++j) u = std::fma(bf16f(w[c * 4 + j]), at(t - 3 + j, c), u);
+                y[(size_t)c] = u / (1.0f + std::exp(-u));
+            }
+            for (int64_t hc = 0; hc < C / 128; ++hc) {
+                float* yy = &y[(size_t)(hc * 128)];
+                if (hc < 2 * Hk) {
+                    float ss = 0.0f;
+                    for (int e = 0; e < 128; ++e) ss += yy[e] * yy[e];
+                    const float inv = 1.0f / std::sqrt(ss + 1e-6f);
+                    for (int e = 0; e < 128; ++e) yy[e] *= inv;
+                }
+                uint16_t* out = hc < Hk ? q + (t * Hk + hc) * 128
+                                        : hc < 2 * Hk ? k + (t * Hk + hc - Hk) * 128 : v + (t * Hv + hc - 2 * Hk) * 128;
+                for (int e = 0; e < 128; ++e) out[e] = f2bf(yy[e]);
+            }
+            for (int64_t h = 0; h < Hv; ++h) {
+                g[t * Hv + h] = -std::exp(a_log[h]) * softplus2(bf16f(a[t * Hv + h]) + dt_bias[h]);
+                beta[t * Hv + h] = 1.0f / (1.0f + std::exp(-bf16f(b[t * Hv + h])));
+            }
+        }
+        if (in_pool) {
+            const int64_t L = e0 - s0;
+            for (int j = 0; j < 3; ++j)
+                for (int64_t c = 0; c < C; ++c)
+                    state[slot * 3 * C + j * C + c] =
+                        L + j < 3 ? f2bf(hist[(size_t)((L + j) * C + c)]) : x[(e0 - 3 + j) * x_row + c];
+        }
+    }
 }
 
 /* ridgefill_gemm_nt_bias (kernels/rows.cpp:155-160): y = res + act(a @ b^T + bias), bf16 a [M, K] and b [N, K],

@@ -151,6 +151,11 @@ const RadKernelInfo kRows[] = {
                "chunked gated delta rule: per-chunk WY transform on tensor cores, then the inter-chunk state carry",
                "head dims 128, chunk 64", "bf16 q / k / v / o, f32 g / beta / state", nullptr, 0, ridgefill_gdn_fill_device,
                ridgefill_gdn_fill_scratch, shape_gdn, nullptr, nullptr, nullptr),
+    DEVICE_ROW("ridgefill_gdn_conv_prep_sm100", "ridgefill_gdn_conv_prep",
+               "warp per 32 rows of a 128-channel head column, the convolution window in registers, eight rows of "
+               "loads in flight; a second kernel updates the conv state in place", "head dims 128, conv width 4",
+               "bf16 x / w / state / a / b / q / k / v, f32 A_log / dt_bias / g / beta", nullptr, 0,
+               ridgefill_gdn_conv_prep_device, nullptr, shape_conv_prep, nullptr, nullptr, nullptr),
 };
 
 #ifndef RIDGEFILL_BUILD_TARGET
@@ -161,7 +166,8 @@ const RadPluginInfo kInfo = {
     RAD_PLUGIN_KERNEL, "ridgefill", "0.2.0",
     "RidgeFill prefill ops on B200 (sm_100a): ridgefill_mask, ridgefill_select, ridgefill_drop_rows, "
     "ridgefill_rho_update, ridgefill_state_correct, ridgefill_state_read, ridgefill_hazard, the int8 projector "
-    "ridgefill_gemm_nt_q (+ fused bias), its activation quantiser and the Gated DeltaNet chunk fill. Device rows only.",
+    "ridgefill_gemm_nt_q (+ fused bias), its activation quantiser, the bf16 ridgefill_gemm_nt_bias, the Gated DeltaNet "
+    "chunk fill and its input preparation (ridgefill_gdn_conv_prep). Device rows only.",
     RIDGEFILL_BUILD_TARGET
 };
 

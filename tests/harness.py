@@ -227,6 +227,7 @@ def _bind_oracle_functions(lib):
     lib.oracle_quantise_weight_i8.argtypes = [P, i64, i64, P, P]
     lib.oracle_gemm_nt_q.argtypes = [P, i64, P, i64, P, i64, P, P, P, i64, P, i64, i64, i64, i64, i64, i64]
     lib.oracle_gemm_nt_bias.argtypes = [P, i64, P, i64, P, C.c_int, P, i64, P, i64, P, i64, i64, C.c_int, i64, i64]
+    lib.oracle_gdn_conv_prep.argtypes = [P, i64, P, P, P, P, P, i64, P, i64, P, P, P, P, P, P, P, P, P, i64, i64, i64]
     for f in (lib.oracle_gdn_fill_f64, lib.oracle_gdn_fill_f32):
         f.argtypes = [P, P, P, P, P, P, P, i64, i64, P, i64, P, i64, i64, i64, i64, C.c_float, i64, i64]
     lib.oracle_threads.restype = C.c_int
@@ -297,6 +298,33 @@ def oracle_gemm_bias(a, b, bias, res=None, act=0, rows=None):
     lib.oracle_gemm_nt_bias(_p(a), K, _p(b), K, _p(bias), int(bias_f32), _p(res), N, _p(y), N, _p(z), N, K, act,
                             m0, m1)
     return y, z
+
+
+def oracle_conv_prep(x, w, a_log, dt_bias, state, cu, a, b, idx, ctx=None, bias=None, hk=16, hv=32, out=None):
+    """ridgefill_gdn_conv_prep on the CPU. x bf16 bits [T, C]; w bf16 bits [C, 4]; a_log, dt_bias f32 [Hv];
+    state bf16 bits [slots, 3, C] (updated in a copy, returned); cu, idx, ctx i32; a, b bf16 bits [T, Hv].
+    `out` (optional): initial (q, k, v, g, beta) arrays, for the rows the op leaves alone. Returns
+    (q, k, v, g, beta, state)."""
+    lib = oracle().lib
+    x = np.ascontiguousarray(x, np.uint16)
+    T, Cc = x.shape
+    w = np.ascontiguousarray(w, np.uint16)
+    a_log = np.ascontiguousarray(a_log, np.float32)
+    dt_bias = np.ascontiguousarray(dt_bias, np.float32)
+    st = np.ascontiguousarray(state, np.uint16).copy()
+    cu = np.ascontiguousarray(cu, np.int32)
+    idx = np.ascontiguousarray(idx, np.int32).reshape(-1)
+    ctx = None if ctx is None else np.ascontiguousarray(ctx, np.int32)
+    bias = None if bias is None else np.ascontiguousarray(bias, np.uint16)
+    a = np.ascontiguousarray(a, np.uint16)
+    b = np.ascontiguousarray(b, np.uint16)
+    if out is None:
+        out = (np.zeros((T, hk, 128), np.uint16), np.zeros((T, hk, 128), np.uint16), np.zeros((T, hv, 128), np.uint16),
+               np.zeros((T, hv), np.float32), np.zeros((T, hv), np.float32))
+    q, k, v, g, beta = (np.ascontiguousarray(o).copy() for o in out)
+    lib.oracle_gdn_conv_prep(_p(x), Cc, _p(w), _p(bias), _p(a_log), _p(dt_bias), _p(st), st.shape[0], _p(cu), len(cu) - 1,
+                             _p(a), _p(b), _p(idx), _p(ctx), _p(q), _p(k), _p(v), _p(g), _p(beta), T, hk, hv)
+    return q, k, v, g, beta, st
 
 
 def oracle_gdn(k, v, g, beta, state, idx, cu, q=None, scale=None, f64=True, heads=None):

@@ -1,0 +1,131 @@
+"""ridgefill_gdn_conv_prep on B200 against the CPU oracle (oracle/ridgefill_oracle.cpp oracle_gdn_conv_prep): q, k, v
+within 2 bf16 ulp (the bf16 bound stated for this library's outputs; the device's exp and the warp's sum of squares
+may differ from the host's in the last f32 bits), g and beta within 1e-5 relative (f32 exp / log1p), the conv state
+bit for bit, and rows outside every sequence untouched. Shapes: ragged batches with history, short sequences (one
+and two rows), slots outside the pool, a bias and none, and the real layer (16 qk / 32 v heads x 128)."""
+import numpy as np
+import pytest
+
+import harness as H
+from harness import abi
+
+pytestmark = pytest.mark.gpu
+SENT = 0x5A5A
+
+
+def _case(seed, T, hk, hv, slots=4, bias=True):
+    rng = np.random.default_rng(seed)
+    C = 2 * hk * 128 + hv * 128
+    d = {
+        "x": H.f32_to_bf16_bits(rng.standard_normal((T, C)).astype(np.float32)),
+        "w": H.f32_to_bf16_bits((0.5 * rng.standard_normal((C, 4))).astype(np.float32)),
+        "bias": H.f32_to_bf16_bits((0.1 * rng.standard_normal(C)).astype(np.float32)) if bias else None,
+        "a_log": (0.5 * rng.standard_normal(hv)).astype(np.float32),
+        "dt_bias": (0.5 * rng.standard_normal(hv)).astype(np.float32),
+        "a": H.f32_to_bf16_bits((3 * rng.standard_normal((T, hv))).astype(np.float32)),
+        "b": H.f32_to_bf16_bits(rng.standard_normal((T, hv)).astype(np.float32)),
+        "state": H.f32_to_bf16_bits(rng.standard_normal((slots, 3, C)).astype(np.float32)),
+    }
+    return d
+
+
+def _run(product_lib, torch, d, cu, idx, ctx, hk, hv):
+    T, C = d["x"].shape
+    t16 = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda()   # noqa: E731
+    X, W = t16(d["x"]), t16(d["w"])
+    B0 = t16(d["bias"]) if d["bias"] is not None else None
+    AL, DT = torch.from_numpy(d["a_log"]).cuda(), torch.from_numpy(d["dt_bias"]).cuda()
+    ST = t16(d["state"])
+    CU = torch.tensor(np.asarray(cu, np.int32)).cuda()
+    A, Bg = t16(d["a"]), t16(d["b"])
+    I = torch.tensor(np.asarray(idx, np.int32)).cuda()
+    CX = torch.tensor(np.asarray(ctx, np.int32)).cuda() if ctx is not None else None
+    Q = torch.full((T, hk, 128), SENT, dtype=torch.int16, device="cuda")
+    K = torch.full((T, hk, 128), SENT, dtype=torch.int16, device="cuda")
+    V = torch.full((T, hv, 128), SENT, dtype=torch.int16, device="cuda")
+    G = torch.full((T, hv), -7.0, dtype=torch.float32, device="cuda")
+    BE = torch.full((T, hv), -7.0, dtype=torch.float32, device="cuda")
+    ops = [H.dev(X, abi.BF16), H.dev(W, abi.BF16), H.dev(B0, abi.BF16) if B0 is not None else abi.absent(), H.dev(AL),
+           H.dev(DT), H.dev(ST, abi.BF16), H.dev(CU), H.dev(A, abi.BF16), H.dev(Bg, abi.BF16), H.dev(I),
+           H.dev(CX) if CX is not None else abi.absent(), H.dev(Q, abi.BF16), H.dev(K, abi.BF16), H.dev(V, abi.BF16),
+           H.dev(G), H.dev(BE)]
+    params = [H.pint("M", T), H.pint("n_head_k", hk), H.pint("n_head_v", hv), H.pint("head_k", 128), H.pint("head_v", 128),
+              H.pint("conv", 4)]
+    rc = H.launch(product_lib, "ridgefill_gdn_conv_prep", ops, params)
+    u16 = lambda t: t.cpu().numpy().view(np.uint16)   # noqa: E731
+    return rc, u16(Q), u16(K), u16(V), G.cpu().numpy(), BE.cpu().numpy(), u16(ST)
+
+
+def _check(d, got, cu, idx, ctx, hk, hv):
+    T = d["x"].shape[0]
+    init = (np.full((T, hk, 128), SENT, np.uint16), np.full((T, hk, 128), SENT, np.uint16), np.full((T, hv, 128), SENT, np.uint16),
+            np.full((T, hv), -7.0, np.float32), np.full((T, hv), -7.0, np.float32))
+    want = H.oracle_conv_prep(d["x"], d["w"], d["a_log"], d["dt_bias"], d["state"], cu, d["a"], d["b"], idx, ctx, bias=d["bias"],
+                              hk=hk, hv=hv, out=init)
+    rc, q, k, v, g, beta, st = got
+    assert rc == abi.OK
+    for name, x, y in (("q", q, want[0]), ("k", k, want[1]), ("v", v, want[2])):
+        same = x == y
+        xf, yf = H.bf16_bits_to_f32(x).astype(np.float64), H.bf16_bits_to_f32(y).astype(np.float64)
+        close = np.abs(xf - yf) <= np.ldexp(np.maximum(np.abs(xf), np.abs(yf)), -7)
+        assert np.all(same | close), f"{name}: {int((~(same | close)).sum())} outside 2 bf16 ulp"
+    for name, x, y in (("g", g, want[3]), ("beta", beta, want[4])):
+        assert np.allclose(x, y, rtol=1e-5, atol=0), name
+    assert np.array_equal(st, want[5]), "conv state"
+
+
+def test_ragged_batch_with_history(cuda, product_lib):
+    torch = cuda
+    hk, hv = 2, 4
+    d = _case(3, 200, hk, hv)
+    cu = [0, 1, 3, 70, 133, 190]      # lengths 1, 2, 67, 63, 57; rows 190.. outside every sequence
+    idx = [2, 0, 9, 1, 3]             # slot 9 lies outside the pool: zero history, nothing written
+    ctx = [4, 0, 6, 2, 0]
+    for bias in (True, False):
+        dd = dict(d, bias=d["bias"] if bias else None)
+        _check(dd, _run(product_lib, torch, dd, cu, idx, ctx, hk, hv), cu, idx, ctx, hk, hv)
+
+
+def test_without_ctx_lens_every_sequence_starts_fresh(cuda, product_lib):
+    torch = cuda
+    hk, hv = 1, 2
+    d = _case(5, 97, hk, hv)
+    cu, idx = [0, 40, 97], [[1], [0]]
+    _check(d, _run(product_lib, torch, d, cu, idx, None, hk, hv), cu, np.asarray(idx).reshape(-1), None, hk, hv)
+
+
+def test_layer_shape(cuda, product_lib):
+    """The DeltaNet layer's shape: 16 qk / 32 v heads x 128 (C 8,192), one 4,096-row sequence continuing a context."""
+    torch = cuda
+    hk, hv = 16, 32
+    d = _case(7, 4096, hk, hv, slots=2)
+    cu, idx, ctx = [0, 4096], [1], [100]
+    _check(d, _run(product_lib, torch, d, cu, idx, ctx, hk, hv), cu, idx, ctx, hk, hv)
+
+
+def test_split_calls_carry_the_window(cuda, product_lib):
+    """A sequence run as two calls (the second continuing the first through the conv state) gives the one call's
+    q, k, v, g, beta bit for bit."""
+    torch = cuda
+    hk, hv = 2, 2
+    d = _case(11, 300, hk, hv)
+    one = _run(product_lib, torch, d, [0, 300], [0], [1], hk, hv)
+    first = dict(d, x=d["x"][:117], a=d["a"][:117], b=d["b"][:117])
+    p1 = _run(product_lib, torch, first, [0, 117], [0], [1], hk, hv)
+    second = dict(d, x=d["x"][117:], a=d["a"][117:], b=d["b"][117:], state=p1[6])
+    p2 = _run(product_lib, torch, second, [0, 183], [0], [1], hk, hv)
+    for i in range(1, 6):
+        assert np.array_equal(np.concatenate([p1[i], p2[i]]), one[i])
+    assert np.array_equal(p2[6], one[6])
+
+
+def test_refusals(cuda, product_lib):
+    torch = cuda
+    d = _case(1, 8, 1, 1)
+    rc = _run(product_lib, torch, d, [0, 8], [0], None, 1, 1)[0]
+    assert rc == abi.OK
+    X = torch.zeros((8, 384), dtype=torch.int16, device="cuda")
+    params = [H.pint("M", 8), H.pint("n_head_k", 1), H.pint("n_head_v", 1), H.pint("head_k", 128), H.pint("head_v", 128),
+              H.pint("conv", 3)]
+    ops = [H.dev(X, abi.BF16)] + [abi.absent()] * 15
+    assert H.launch(product_lib, "ridgefill_gdn_conv_prep", ops, params) == abi.E_INVAL   # operands missing

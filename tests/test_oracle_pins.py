@@ -261,3 +261,66 @@ def test_oracle_gdn_f32_tracks_f64():
     s32, _ = H.oracle_gdn(kb, vb, g, beta, state, [1], [0, T], f64=False)
     assert np.linalg.norm(s32 - s64) / np.linalg.norm(s64) < 1e-5
     assert np.all(s64[0] == 0)   # slot 0 untouched
+
+
+def _conv_prep_numpy(x, w, a_log, dt_bias, state, cu, a, b, idx, ctx, bias, hk, hv):
+    """ridgefill_gdn_conv_prep restated in numpy (float64 arithmetic, the definition's rounding points)."""
+    xf = H.bf16_bits_to_f32(x).astype(np.float64)
+    wf = H.bf16_bits_to_f32(w).astype(np.float64)
+    bf = H.bf16_bits_to_f32(bias).astype(np.float64) if bias is not None else np.zeros(x.shape[1])
+    T, C = x.shape
+    st = state.copy()
+    q = np.zeros((T, hk, 128), np.float64); k = np.zeros_like(q); v = np.zeros((T, hv, 128))
+    g = np.zeros((T, hv)); beta = np.zeros((T, hv))
+    for i in range(len(cu) - 1):
+        s0 = min(max(cu[i], 0), T); e0 = min(max(cu[i + 1], s0), T)
+        slot = idx[i]
+        in_pool = 0 <= slot < st.shape[0]
+        hist = H.bf16_bits_to_f32(st[slot]).astype(np.float64) if (in_pool and ctx is not None and ctx[i] > 0) else np.zeros((3, C))
+        rows = np.concatenate([hist, xf[s0:e0]], 0)
+        for t in range(s0, e0):
+            win = rows[t - s0: t - s0 + 4]                   # rows t-3 .. t
+            u = bf + (wf * win.T).sum(1)
+            y = u / (1 + np.exp(-u))
+            yq, yk, yv = y[:hk * 128].reshape(hk, 128), y[hk * 128:2 * hk * 128].reshape(hk, 128), y[2 * hk * 128:].reshape(hv, 128)
+            q[t] = yq / np.sqrt((yq ** 2).sum(1, keepdims=True) + 1e-6)
+            k[t] = yk / np.sqrt((yk ** 2).sum(1, keepdims=True) + 1e-6)
+            v[t] = yv
+            av = H.bf16_bits_to_f32(a[t]).astype(np.float64) + dt_bias
+            sp = np.where(av > 20, av, np.log1p(np.exp(np.minimum(av, 20))))
+            g[t] = -np.exp(a_log.astype(np.float64)) * sp
+            beta[t] = 1 / (1 + np.exp(-H.bf16_bits_to_f32(b[t]).astype(np.float64)))
+        if in_pool:
+            allrows = np.concatenate([H.bf16_bits_to_f32(st[slot]) if (ctx is not None and ctx[i] > 0) else np.zeros((3, C), np.float32),
+                                      H.bf16_bits_to_f32(x[s0:e0])], 0)
+            st[slot] = H.f32_to_bf16_bits(allrows[-3:].astype(np.float32))
+    return q, k, v, g, beta, st
+
+
+def test_oracle_conv_prep_definition():
+    """The conv_prep oracle against a numpy restatement on small ragged batches with history: q, k, v within one
+    bf16 ulp, g and beta within 1e-5 relative, the conv state bit for bit, rows outside the sequences untouched."""
+    rng = np.random.default_rng(21)
+    hk, hv, T = 1, 2, 40
+    C = 2 * hk * 128 + hv * 128
+    x = H.f32_to_bf16_bits(rng.standard_normal((T, C)).astype(np.float32))
+    w = H.f32_to_bf16_bits((0.5 * rng.standard_normal((C, 4))).astype(np.float32))
+    bias = H.f32_to_bf16_bits((0.1 * rng.standard_normal(C)).astype(np.float32))
+    a_log = (0.5 * rng.standard_normal(hv)).astype(np.float32)
+    dt_bias = (0.5 * rng.standard_normal(hv)).astype(np.float32)
+    a = H.f32_to_bf16_bits((3 * rng.standard_normal((T, hv))).astype(np.float32))
+    a[0, 0] = H.f32_to_bf16_bits(np.array([30.0], np.float32))[0]   # above the softplus threshold
+    b = H.f32_to_bf16_bits(rng.standard_normal((T, hv)).astype(np.float32))
+    state = H.f32_to_bf16_bits(rng.standard_normal((4, 3, C)).astype(np.float32))
+    cu = np.array([0, 1, 3, 20, 37], np.int32)          # lengths 1, 2, 17, 17; rows 37.. outside
+    idx = np.array([2, 0, 7, 1], np.int32)               # slot 7 is outside the pool
+    ctx = np.array([5, 0, 3, 9], np.int32)
+    for bb in (bias, None):
+        q, k, v, g, beta, st = H.oracle_conv_prep(x, w, a_log, dt_bias, state, cu, a, b, idx, ctx, bias=bb, hk=hk, hv=hv)
+        nq, nk, nv, ng, nb, nst = _conv_prep_numpy(x, w, a_log, dt_bias, state, cu, a, b, idx, ctx, bb, hk, hv)
+        for got, want in ((q, nq), (k, nk), (v, nv)):
+            gf = H.bf16_bits_to_f32(got).astype(np.float64)
+            assert np.all(np.abs(gf - want) <= np.abs(want) * 2.0 ** -8 + 1e-30)
+        assert np.allclose(g[:37], ng[:37], rtol=1e-5, atol=0) and np.allclose(beta[:37], nb[:37], rtol=1e-5, atol=0)
+        assert np.array_equal(st, nst)
+        assert not q[37:].any() and not g[37:].any()
