@@ -79,7 +79,9 @@ unsigned row_grid(int64_t rows) {
 
 constexpr int kPlaneThreads = 256;
 
-__global__ void __launch_bounds__(kPlaneThreads) correct_kernel(RidgeFillCorrect g) {
+constexpr int kCorrThreads = 1024, kCorrLoads = 4;   /* a plane's CTA: four float4 of x and of C in flight a thread */
+
+__global__ void __launch_bounds__(kCorrThreads) correct_kernel(RidgeFillCorrect g) {
     const int64_t h = blockIdx.x, s = blockIdx.y;
     if (!ridgefill_correct_has_bulk(&g)) return;   /* bounds are device memory: read here */
     int64_t st = 0, ap = 0, nd = 0;
@@ -103,22 +105,36 @@ __global__ void __launch_bounds__(kPlaneThreads) correct_kernel(RidgeFillCorrect
         const bool vec = g.st_col == 1 && g.sd1 % 4 == 0 && g.st_row % 4 == 0 && ((uintptr_t)x & 15) == 0 &&
                          ((uintptr_t)c & 15) == 0;
         if (vec) {
-            for (int64_t e = (int64_t)threadIdx.x * 4; e < cells; e += kPlaneThreads * 4) {
-                const int64_t i = e / g.sd1, j = e - i * g.sd1;
-                float4* px = (float4*)(x + i * g.st_row + j);
-                const float4 cv = *(const float4*)(c + e);
-                float4 v = *px;
-                const float d0 = __fmul_rn(scale, cv.x), d1 = __fmul_rn(scale, cv.y);
-                const float d2 = __fmul_rn(scale, cv.z), d3 = __fmul_rn(scale, cv.w);
-                if (g.apply) {
-                    v.x = __fadd_rn(v.x, d0); v.y = __fadd_rn(v.y, d1); v.z = __fadd_rn(v.z, d2); v.w = __fadd_rn(v.w, d3);
-                } else {
-                    v.x = __fsub_rn(v.x, d0); v.y = __fsub_rn(v.y, d1); v.z = __fsub_rn(v.z, d2); v.w = __fsub_rn(v.w, d3);
+            /* kCorrLoads float4 of x and of C loaded before any is updated (x and C may not alias) */
+            for (int64_t e0 = (int64_t)threadIdx.x * 4; e0 < cells; e0 += (int64_t)kCorrThreads * 4 * kCorrLoads) {
+                float4 xv[kCorrLoads], cv[kCorrLoads];
+                float4* px[kCorrLoads];
+#pragma unroll
+                for (int u = 0; u < kCorrLoads; ++u) {
+                    const int64_t e = e0 + (int64_t)u * kCorrThreads * 4;
+                    const int64_t i = e / g.sd1, j = e - i * g.sd1;
+                    px[u] = (float4*)(x + i * g.st_row + j);
+                    if (e < cells) {
+                        cv[u] = *(const float4*)(c + e);
+                        xv[u] = *px[u];
+                    }
                 }
-                *px = v;
+#pragma unroll
+                for (int u = 0; u < kCorrLoads; ++u) {
+                    if (e0 + (int64_t)u * kCorrThreads * 4 >= cells) break;
+                    float4 v = xv[u];
+                    const float d0 = __fmul_rn(scale, cv[u].x), d1 = __fmul_rn(scale, cv[u].y);
+                    const float d2 = __fmul_rn(scale, cv[u].z), d3 = __fmul_rn(scale, cv[u].w);
+                    if (g.apply) {
+                        v.x = __fadd_rn(v.x, d0); v.y = __fadd_rn(v.y, d1); v.z = __fadd_rn(v.z, d2); v.w = __fadd_rn(v.w, d3);
+                    } else {
+                        v.x = __fsub_rn(v.x, d0); v.y = __fsub_rn(v.y, d1); v.z = __fsub_rn(v.z, d2); v.w = __fsub_rn(v.w, d3);
+                    }
+                    *px[u] = v;
+                }
             }
         } else {
-            for (int64_t e = threadIdx.x; e < cells; e += kPlaneThreads) {
+            for (int64_t e = threadIdx.x; e < cells; e += kCorrThreads) {
                 const int64_t i = e / g.sd1, j = e - i * g.sd1;
                 float* px = x + i * g.st_row + j * g.st_col;
                 const float d = __fmul_rn(scale, c[i * g.c_row + j]);
@@ -261,7 +277,7 @@ extern "C" int ridgefill_correct_device(const RadArgs* a, RadStream s) {
     if (rc != RAD_OK) return rc;
     if (g.n_seq == 0 || g.n_head == 0) return RAD_OK;
     if (g.n_head > 0x7fffffff || g.n_seq > 65535) return RAD_E_SHAPE;
-    correct_kernel<<<dim3((unsigned)g.n_head, (unsigned)g.n_seq), kPlaneThreads, 0, rf::as_stream(s)>>>(g);
+    correct_kernel<<<dim3((unsigned)g.n_head, (unsigned)g.n_seq), kCorrThreads, 0, rf::as_stream(s)>>>(g);
     return rf::launch_status();
 }
 
