@@ -63,6 +63,9 @@ enum { GD_Q = 0, GD_K, GD_V, GD_G, GD_BETA, GD_STATE, GD_STATE_IDX, GD_CU, GD_O 
  * with the gate written per row rather than in its in-chunk cumulative form). */
 enum { CP_X = 0, CP_W, CP_BIAS, CP_A_LOG, CP_DT_BIAS, CP_STATE, CP_CU, CP_A, CP_B, CP_IDX, CP_CTX, CP_Q, CP_K, CP_V,
        CP_G, CP_BETA };
+/* ridgefill_attn_kv_fill (new; the gated-attention block's K/V path in the lean fill, arch/qwen4exp_fill.h:104-114:
+ * the k_norm, rope_k and kv_store issues after the k and v projections, as one op). */
+enum { AK_K = 0, AK_V, AK_W, AK_POS, AK_SLOTS, AK_CACHE, AK_K_OUT };
 
 /* ------------------------------------------------------------------ the shared formulas */
 
@@ -331,6 +334,34 @@ typedef struct RidgeFillConvPrep {
     int64_t        T, n_head_k, n_head_v, dk, dv, width;
 } RidgeFillConvPrep;
 
+/* ridgefill_attn_kv_fill: the attention block's cache write for a prefill of T rows. Per row t and kv-head h
+ * (D = head_dim = 256, R = rope_dim, lane l = elements 8l..8l+7):
+ *   k_norm  ss = sum of k^2 (f32; each lane's 8 squares by fma in element order, then a butterfly over the 32
+ *           lane sums), r = 1 / sqrt(ss / D + eps), kn[i] = bf16((k[i] r) w[i]);
+ *   rope_k  for j < R/2: a = pos[p(j)][t] * theta^(-2j/R) (f64), c = f32(cos a), s = f32(sin a),
+ *           kr[j] = bf16(fma(kn[j], c, -(kn[j+R/2] s))), kr[j+R/2] = bf16(fma(kn[j+R/2], c, kn[j] s));
+ *           kr[i] = kn[i] for i >= R. p(j) is the position plane of rotary pair j: 0 for plain rope (or a
+ *           one-plane positions operand); for mrope sections (s0, s1, s2) plane 0 on [0, s0), 1 on
+ *           [s0, s0+s1), 2 after; for imrope plane 1 where j % 3 == 1 and j < 3 s1, 2 where j % 3 == 2 and
+ *           j < 3 s2, 0 elsewhere;
+ *   kv_store cache[0, slot, h] = kr, cache[1, slot, h] = v[t, h] for slot = slot_mapping[t] when
+ *           0 <= slot < slots (other rows store nothing); k_out[t, h] = kr when k_out is present. */
+enum { RIDGEFILL_ROPE_NEOX = 0, RIDGEFILL_ROPE_MROPE = 1, RIDGEFILL_ROPE_IMROPE = 2 };
+typedef struct RidgeFillAttnKv {
+    const uint16_t* k;       int64_t k_row, k_head;        /* [T, Hkv, D] */
+    const uint16_t* v;       int64_t v_row, v_head;        /* [T, Hkv, D] */
+    const void*    w;        int w_f32;                    /* [D] bf16 (w_f32 0) or f32 */
+    const int32_t* pos;      int64_t pos_plane; int n_planes;   /* [T] or [3, T] */
+    const int32_t* slots;                                  /* [T] */
+    uint16_t*      cache;    int64_t c_kv, c_slot, c_head, n_slots;   /* [2, slots, Hkv, D] */
+    uint16_t*      k_out;    int64_t ko_row, ko_head;      /* [T, Hkv, D] or null */
+    int64_t        T, n_head_kv, head_dim, rope_dim;
+    double         theta;
+    float          eps;
+    int            mode;
+    int            sections[3];
+} RidgeFillAttnKv;
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -365,6 +396,7 @@ int ridgefill_gemm_bias_parse(const RadArgs* a, RidgeFillGemmBias* out);
 int ridgefill_quant_parse(const RadArgs* a, RidgeFillQuant* out);
 int ridgefill_gdn_parse(const RadArgs* a, RidgeFillGdn* out);
 int ridgefill_conv_prep_parse(const RadArgs* a, RidgeFillConvPrep* out);
+int ridgefill_attn_kv_parse(const RadArgs* a, RidgeFillAttnKv* out);
 
 /* The device rows (kernels/ridgefill.h:304-310 and the new ops): async launches on `s` (a
  * cudaStream_t); no allocation, no synchronisation. */
@@ -381,6 +413,7 @@ int ridgefill_gemm_nt_bias_device(const RadArgs* a, RadStream s);
 int ridgefill_quant_act_device(const RadArgs* a, RadStream s);
 int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s);
 int ridgefill_gdn_conv_prep_device(const RadArgs* a, RadStream s);
+int ridgefill_attn_kv_fill_device(const RadArgs* a, RadStream s);
 
 /* The first error code a tensor-core kernel of this library recorded after giving up on a bounded
  * wait (0: none), optionally cleared. Synchronises the current device: a diagnostic, never called on

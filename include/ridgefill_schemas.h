@@ -74,6 +74,11 @@ static const RadOperandSpec oConv[] = { RF_IN("x"), RF_IN("w_conv"), RF_IN_OPT("
                                         RF_IN("dt_bias"), RF_INOUT("conv_state"), RF_IN("cu_seqlens"), RF_IN("a"),
                                         RF_IN("b"), RF_IN("conv_idx"), RF_IN_OPT("ctx_lens"), RF_OUT("q"), RF_OUT("k"),
                                         RF_OUT("v"), RF_OUT("g"), RF_OUT("beta") };
+static const RadParamSpec pAttnKv[] = { RF_P_INT("M"), RF_P_INT("n_head_kv"), RF_P_INT("head_dim"), RF_P_INT("rope_dim"),
+                                        RF_P_F64("rope_theta"), RF_P_OPT("eps", RAD_P_F64),
+                                        RF_P_OPT("rope_mode", RAD_P_STR), RF_P_OPT("rope_sections", RAD_P_STR) };
+static const RadOperandSpec oAttnKv[] = { RF_IN("k"), RF_IN("v"), RF_IN("k_norm"), RF_IN("positions"),
+                                          RF_IN("slot_mapping"), RF_INOUT("kv_cache"), RF_OUT_OPT("k_out") };
 
 /* The reference's nine schemas come first, in its order (kernels/rows.cpp:84-168). */
 enum { kReferenceSchemas = 9 };
@@ -133,6 +138,13 @@ static const RadOpSchema kSchemas[] = {
   "g[t, h] = -exp(A_log[h]) softplus(a[t, h] + dt_bias[h]) (threshold 20), beta = sigmoid(b); f32. conv_state "
   "bf16 [slots, 3, C] then holds each sequence's last three input rows (a slot outside the pool: zero history, "
   "not written). Rows outside every sequence are not written." },
+{ "ridgefill_attn_kv_fill", RF_ARR(pAttnKv), RF_ARR(oAttnKv),
+  "The attention block's K/V cache write for T prefill rows (k_norm, rope_k, kv_store as one op): per row t and "
+  "kv-head h, kn = bf16(k * w / sqrt(mean(k^2) + eps)) (f32), the first rope_dim elements rotated in half pairs "
+  "(j, j + rope_dim/2) by the angle pos[plane(j)][t] * rope_theta^(-2j/rope_dim) (f64 angle, f32 cos/sin, bf16 "
+  "result; plane(j) by rope_mode neox / mrope / imrope and rope_sections), then kv_cache[0, slot, h] = that k "
+  "and kv_cache[1, slot, h] = v[t, h] for slot = slot_mapping[t] inside [0, slots) (else nothing is stored); "
+  "k_out[t, h] = that k when present. head_dim 256." },
 };
 
 /* ------------------------------------------------------------------ cold-call descriptions */
@@ -269,6 +281,13 @@ inline int shape_conv_prep(const RadParam* p, int n_p, int operand, RadOpdDesc* 
                                 opd(RAD_BF16, { T, hv }), opd(RAD_BF16, { T, hv }), opd_idx({ 1 }, slots),
                                 opd(RAD_I32, { 1 }), opd(RAD_BF16, { T, hk, dk }), opd(RAD_BF16, { T, hk, dk }),
                                 opd(RAD_BF16, { T, hv, dv }), opd(RAD_F32, { T, hv }), opd(RAD_F32, { T, hv }) });
+}
+
+inline int shape_attn_kv(const RadParam* p, int n_p, int operand, RadOpdDesc* out) {
+    const int64_t T = dim(p, n_p, "M"), h = dim(p, n_p, "n_head_kv"), D = dim(p, n_p, "head_dim"), slots = 2 * T;
+    return pick(out, operand, { opd(RAD_BF16, { T, h, D }), opd(RAD_BF16, { T, h, D }), opd(RAD_F32, { D }),
+                                opd_idx({ T }, 1 << 20), opd_idx({ T }, slots, RAD_OPD_F_IDX_UNIQUE),
+                                opd(RAD_BF16, { 2, slots, h, D }), opd(RAD_BF16, { T, h, D }) });
 }
 
 }  // namespace ridgefill_schema

@@ -13,8 +13,9 @@
  *     source (oracle/_ref).
  *  2. Plain-pointer oracles for the ops the reference does not contain (their arithmetic lives in
  *     radiance's libr4d and in-tree ops, absent): the activation quantiser, the int8 projector GEMM with
- *     its f32 block fold, the bf16 GEMM with bias / SiLU / residual, the gated delta rule and the DeltaNet
- *     input preparation (convolution, SiLU, L2 norm, gate). PARITY UNPINNED for all but the quantiser's
+ *     its f32 block fold, the bf16 GEMM with bias / SiLU / residual, the gated delta rule, the DeltaNet
+ *     input preparation (convolution, SiLU, L2 norm, gate) and the attention block's K/V cache write (RMS
+ *     norm, rotary embedding, paged store). PARITY UNPINNED for all but the quantiser's
  *     rounding rule (no reference source, test or fixture exists for them; the gate is the reference's
  *     softplus rule, kernels/ridgefill.h:93-97); the quantiser's rounding rule is the reference's
  *     quantise_i8 (tools/ridgefill_projector.py:333-344) with an f32 scale.
@@ -591,6 +592,76 @@ void oracle_gemm_nt_bias(const uint16_t* a, int64_t lda, const uint16_t* b, int6
             if (res) x = f2bf(bf16f(x) + bf16f(res[m * ldr + n]));
             y[m * ldy + n] = x;
         }
+}
+
+/* ridgefill_attn_kv_fill: the gated-attention block's k_norm -> rope_k -> kv_store chain (issue site
+ * arch/qwen4exp_fill.h:104-114), each stage rounded to bf16. k, v dense [T, Hkv, D] (D = 256), w [D] bf16 or f32,
+ * pos [n_planes, T] (1 or 3 planes), slots [T], cache dense [2, n_slots, Hkv, D] (untouched where no row
+ * stores), k_out dense [T, Hkv, D] or null. Per row and head:
+ *   ss = the sum of squares in the order the device forms it: eight lane sums (fma, element order), then a
+ *        butterfly over the 32 lane sums (offsets 16, 8, 4, 2, 1);
+ *   kn = bf16((k r) w) with r = 1 / sqrt(ss / D + eps);
+ *   for j < R/2: a = pos[plane(j)][t] * theta^(-2j/R) in f64, c, s = cos a, sin a rounded to f32,
+ *        kr[j] = bf16(fma(kn[j], c, -(kn[j+R/2] s))), kr[j+R/2] = bf16(fma(kn[j+R/2], c, kn[j] s));
+ *   cache[0, slot, h] = kr, cache[1, slot, h] = v for 0 <= slot < n_slots; k_out = kr.
+ * plane(j): 0 unless three planes are given and mode is mrope (sections consecutive) or imrope (plane 1 at
+ * j % 3 == 1, j < 3 s1; plane 2 at j % 3 == 2, j < 3 s2). */
+void oracle_attn_kv_fill(const uint16_t* k, const uint16_t* v, const void* w, int w_f32, const int32_t* pos,
+                         int n_planes, const int32_t* slots, uint16_t* cache, int64_t n_slots, uint16_t* k_out,
+                         int64_t T, int64_t Hkv, int64_t R, double theta, float eps, int mode, const int32_t* sections) {
+    const int64_t D = 256, half = R / 2;
+    std::vector<double> inv_freq((size_t)half);
+    std::vector<int> pl((size_t)half, 0);
+    for (int64_t j = 0; j < half; ++j) {
+        inv_freq[(size_t)j] = std::pow(theta, -2.0 * (double)j / (double)R);
+        if (n_planes == 3 && mode == 1)
+            pl[(size_t)j] = j < sections[0] ? 0 : j < sections[0] + sections[1] ? 1 : 2;
+        else if (n_planes == 3 && mode == 2)
+            pl[(size_t)j] = (j % 3 == 1 && j < 3 * sections[1]) ? 1 : (j % 3 == 2 && j < 3 * sections[2]) ? 2 : 0;
+    }
+#pragma omp parallel for schedule(static)
+    for (int64_t t = 0; t < T; ++t) {
+        float x[256], kn[256], kr[256], lane[32], tmp[32];
+        std::vector<float> c((size_t)half), sn((size_t)half);
+        for (int64_t j = 0; j < half; ++j) {
+            const double ang = (double)pos[pl[(size_t)j] * T + t] * inv_freq[(size_t)j];
+            c[(size_t)j] = (float)std::cos(ang);
+            sn[(size_t)j] = (float)std::sin(ang);
+        }
+        for (int64_t h = 0; h < Hkv; ++h) {
+            const uint16_t* kp = k + (t * Hkv + h) * D;
+            for (int64_t i = 0; i < D; ++i) x[i] = bf16f(kp[i]);
+            for (int l = 0; l < 32; ++l) {
+                float acc = 0.0f;
+                for (int e = 0; e < 8; ++e) acc = std::fma(x[8 * l + e], x[8 * l + e], acc);
+                lane[l] = acc;
+            }
+            for (int off = 16; off > 0; off >>= 1) {
+                for (int l = 0; l < 32; ++l) tmp[l] = lane[l] + lane[l ^ off];
+                std::memcpy(lane, tmp, sizeof lane);
+            }
+            const float r = 1.0f / std::sqrt(lane[0] / 256.0f + eps);
+            for (int64_t i = 0; i < D; ++i) {
+                const float wi = w_f32 ? ((const float*)w)[i] : bf16f(((const uint16_t*)w)[i]);
+                kn[i] = bf16f(f2bf((x[i] * r) * wi));
+                kr[i] = kn[i];
+            }
+            for (int64_t j = 0; j < half; ++j) {
+                const float a1 = kn[j], a2 = kn[j + half], cj = c[(size_t)j], sj = sn[(size_t)j];
+                const float p2 = a2 * sj, p1 = a1 * sj;
+                kr[j] = std::fma(a1, cj, -p2);
+                kr[j + half] = std::fma(a2, cj, p1);
+            }
+            uint16_t out[256];
+            for (int64_t i = 0; i < D; ++i) out[i] = f2bf(kr[i]);
+            if (k_out) std::memcpy(k_out + (t * Hkv + h) * D, out, sizeof out);
+            const int64_t slot = slots[t];
+            if (slot >= 0 && slot < n_slots) {
+                std::memcpy(cache + (slot * Hkv + h) * D, out, sizeof out);
+                std::memcpy(cache + ((n_slots + slot) * Hkv + h) * D, v + (t * Hkv + h) * D, D * sizeof(uint16_t));
+            }
+        }
+    }
 }
 
 }  // extern "C"

@@ -22,7 +22,7 @@ CSRC = HERE / "csrc"
 OUT = HERE / "ridgefill.so"
 BUILD = HERE / "_build"
 
-CUDA_SOURCES = ["small_ops.cu", "mask.cu", "gemm_q.cu", "gdn.cu", "conv_prep.cu"]
+CUDA_SOURCES = ["small_ops.cu", "mask.cu", "gemm_q.cu", "gdn.cu", "conv_prep.cu", "attn_kv.cu"]
 HOST_SOURCES = ["parse.cpp", "rows.cpp"]
 HEADERS = ["common.cuh", "sm100.cuh", "mma.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

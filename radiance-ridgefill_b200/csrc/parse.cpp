@@ -524,6 +524,113 @@ extern "C" int ridgefill_conv_prep_parse(const RadArgs* a, RidgeFillConvPrep* g)
     return RAD_OK;
 }
 
+/* "s0,s1,s2" (optionally in brackets, spaces allowed): three non-negative counts; false otherwise. */
+static bool parse_sections(const char* s, int (&out)[3]) {
+    if (!s) return false;
+    int n = 0;
+    long long cur = -1;
+    for (const char* c = s;; ++c) {
+        if (*c >= '0' && *c <= '9') {
+            cur = (cur < 0 ? 0 : cur) * 10 + (*c - '0');
+            if (cur > 1 << 20) return false;
+        } else if (*c == ',' || *c == ']' || *c == '\0') {
+            if (cur < 0 || n >= 3) return false;
+            out[n++] = (int)cur;
+            cur = -1;
+            if (*c != ',') {
+                for (const char* d = *c ? c + 1 : c; *d; ++d)
+                    if (*d != ' ') return false;
+                return n == 3;
+            }
+        } else if (!(*c == ' ' || (*c == '[' && n == 0 && cur < 0))) {
+            return false;
+        }
+    }
+}
+
+/* ridgefill_attn_kv_fill: k, v bf16 [T, Hkv, 256] (last stride 1, rows and heads 16-byte aligned), k_norm bf16 or
+ * f32 [256] dense, positions i32 [T] or [3, T] (last stride 1), slot_mapping i32 [T] dense, cache bf16
+ * [2, slots, Hkv, 256] (last stride 1, its other strides and base 16-byte aligned), k_out bf16 [T, Hkv, 256] or
+ * absent (it may be k itself). rope_dim a multiple of 16 in [16, 256]; rope_theta > 1; eps >= 0 (1e-6 when
+ * absent); rope_mode absent / "neox", "mrope" or "imrope", the last two with rope_sections "s0,s1,s2" summing
+ * to rope_dim / 2. */
+extern "C" int ridgefill_attn_kv_parse(const RadArgs* a, RidgeFillAttnKv* g) {
+    *g = RidgeFillAttnKv{};
+    const RadTensor* K = rad_arg_in(a, AK_K);
+    const RadTensor* V = rad_arg_in(a, AK_V);
+    const RadTensor* W = rad_arg_in(a, AK_W);
+    const RadTensor* P = rad_arg_in(a, AK_POS);
+    const RadTensor* S = rad_arg_in(a, AK_SLOTS);
+    const RadTensor* C = rad_arg_in(a, AK_CACHE);
+    const RadTensor* KO = rad_arg_in(a, AK_K_OUT);
+    long long T = 0, hkv = 0, D = 0, R = 0;
+    if (!K || !V || !W || !P || !S || !C) return RAD_E_INVAL;
+    if (!rad_args_geti(a, "M", &T) || !rad_args_geti(a, "n_head_kv", &hkv) || !rad_args_geti(a, "head_dim", &D) ||
+        !rad_args_geti(a, "rope_dim", &R))
+        return RAD_E_INVAL;
+    const double theta = rad_args_getf_or(a, "rope_theta", NAN), eps = rad_args_getf_or(a, "eps", 1e-6);
+    if (!(theta > 1.0) || !std::isfinite(theta) || !(eps >= 0.0) || !std::isfinite(eps)) return RAD_E_INVAL;
+    static const char* const modes[] = { "neox", "mrope", "imrope" };
+    const char* m = rad_args_gets(a, "rope_mode");
+    const int mode = m ? which(m, modes, 3) : RIDGEFILL_ROPE_NEOX;
+    if (mode < 0) return RAD_E_INVAL;
+    int sec[3] = { 0, 0, 0 };
+    if (mode != RIDGEFILL_ROPE_NEOX && (!parse_sections(rad_args_gets(a, "rope_sections"), sec) ||
+                                        (long long)sec[0] + sec[1] + sec[2] != R / 2))
+        return RAD_E_INVAL;
+    if (D != 256 || R < 16 || R > D || R % 16) return RAD_E_UNSUPPORTED;
+    if (hkv <= 0 || T < 0) return RAD_E_SHAPE;
+    if (K->dtype != RAD_BF16 || V->dtype != RAD_BF16 || (W->dtype != RAD_BF16 && W->dtype != RAD_F32) ||
+        P->dtype != RAD_I32 || S->dtype != RAD_I32 || C->dtype != RAD_BF16 || (KO && KO->dtype != RAD_BF16))
+        return RAD_E_DTYPE;
+    const RadTensor* rows[3] = { K, V, KO };
+    for (const RadTensor* t : rows)
+        if (t && (t->rank != 3 || t->shape[0] != T || t->shape[1] != hkv || t->shape[2] != D || t->stride[2] != 1))
+            return RAD_E_SHAPE;
+    if (rad_tensor_numel(W) != D || !dense(W)) return RAD_E_SHAPE;
+    if (P->rank == 1 ? (P->shape[0] != T || P->stride[0] != 1)
+                     : (P->rank != 2 || P->shape[0] != 3 || P->shape[1] != T || P->stride[1] != 1))
+        return RAD_E_SHAPE;
+    if (rad_tensor_numel(S) != T || !dense(S)) return RAD_E_SHAPE;
+    if (C->rank != 4 || C->shape[0] != 2 || C->shape[2] != hkv || C->shape[3] != D || C->stride[3] != 1) return RAD_E_SHAPE;
+    /* 16-byte loads and stores: eight elements a lane. */
+    uint64_t align = (uint64_t)(uintptr_t)K->data | (uint64_t)(uintptr_t)V->data | (uint64_t)(uintptr_t)C->data |
+                     (uint64_t)(K->stride[0] * 2) | (uint64_t)(K->stride[1] * 2) | (uint64_t)(V->stride[0] * 2) |
+                     (uint64_t)(V->stride[1] * 2) | (uint64_t)(C->stride[0] * 2) | (uint64_t)(C->stride[1] * 2) |
+                     (uint64_t)(C->stride[2] * 2);
+    if (KO) align |= (uint64_t)(uintptr_t)KO->data | (uint64_t)(KO->stride[0] * 2) | (uint64_t)(KO->stride[1] * 2);
+    if (align % 16) return RAD_E_STRIDE;
+    g->k = (const uint16_t*)K->data;
+    g->k_row = K->stride[0];
+    g->k_head = K->stride[1];
+    g->v = (const uint16_t*)V->data;
+    g->v_row = V->stride[0];
+    g->v_head = V->stride[1];
+    g->w = W->data;
+    g->w_f32 = W->dtype == RAD_F32;
+    g->pos = (const int32_t*)P->data;
+    g->n_planes = P->rank == 1 ? 1 : 3;
+    g->pos_plane = P->rank == 1 ? 0 : P->stride[0];
+    g->slots = (const int32_t*)S->data;
+    g->cache = (uint16_t*)C->data;
+    g->c_kv = C->stride[0];
+    g->c_slot = C->stride[1];
+    g->c_head = C->stride[2];
+    g->n_slots = C->shape[1];
+    g->k_out = KO ? (uint16_t*)KO->data : nullptr;
+    g->ko_row = KO ? KO->stride[0] : 0;
+    g->ko_head = KO ? KO->stride[1] : 0;
+    g->T = T;
+    g->n_head_kv = hkv;
+    g->head_dim = D;
+    g->rope_dim = R;
+    g->theta = theta;
+    g->eps = (float)eps;
+    g->mode = mode;
+    for (int i = 0; i < 3; ++i) g->sections[i] = sec[i];
+    return RAD_OK;
+}
+
 /* ridgefill_quant_act_i8g: x bf16 [M, n] (row pitch free, last stride 1), q i8 [M, n], s f32 [M, n/group]. */
 extern "C" int ridgefill_quant_parse(const RadArgs* a, RidgeFillQuant* g) {
     *g = RidgeFillQuant{};

@@ -152,10 +152,15 @@ const RadKernelInfo kRows[] = {
                "head dims 128, chunk 64", "bf16 q / k / v / o, f32 g / beta / state", nullptr, 0, ridgefill_gdn_fill_device,
                ridgefill_gdn_fill_scratch, shape_gdn, nullptr, nullptr, nullptr),
     DEVICE_ROW("ridgefill_gdn_conv_prep_sm100", "ridgefill_gdn_conv_prep",
-               "warp per 32 rows of a 128-channel head column, the convolution window in registers, eight rows of "
-               "loads in flight; a second kernel updates the conv state in place", "head dims 128, conv width 4",
+               "warp per 16 rows of a pair of 128-channel head columns, all 16 rows' loads in flight as asynchronous "
+               "copies into shared memory; a second kernel updates the conv state in place", "head dims 128, conv width 4",
                "bf16 x / w / state / a / b / q / k / v, f32 A_log / dt_bias / g / beta", nullptr, 0,
                ridgefill_gdn_conv_prep_device, nullptr, shape_conv_prep, nullptr, nullptr, nullptr),
+    DEVICE_ROW("ridgefill_attn_kv_fill_sm100", "ridgefill_attn_kv_fill",
+               "warp per row: both heads' k and v rows in flight, k_norm by a warp butterfly, the row's rotary angles "
+               "one a lane (f64), rotation and the paged stores in the same pass", "head_dim 256, rope_dim a multiple of 16",
+               "bf16 k / v / cache / k_out, bf16 or f32 k_norm, i32 positions / slot_mapping", nullptr, 0,
+               ridgefill_attn_kv_fill_device, nullptr, shape_attn_kv, nullptr, nullptr, nullptr),
 };
 
 #ifndef RIDGEFILL_BUILD_TARGET
@@ -167,7 +172,8 @@ const RadPluginInfo kInfo = {
     "RidgeFill prefill ops on B200 (sm_100a): ridgefill_mask, ridgefill_select, ridgefill_drop_rows, "
     "ridgefill_rho_update, ridgefill_state_correct, ridgefill_state_read, ridgefill_hazard, the int8 projector "
     "ridgefill_gemm_nt_q (+ fused bias), its activation quantiser, the bf16 ridgefill_gemm_nt_bias, the Gated DeltaNet "
-    "chunk fill and its input preparation (ridgefill_gdn_conv_prep). Device rows only.",
+    "chunk fill and its input preparation (ridgefill_gdn_conv_prep), and the attention block's K/V cache write "
+    "(ridgefill_attn_kv_fill). Device rows only.",
     RIDGEFILL_BUILD_TARGET
 };
 

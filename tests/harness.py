@@ -228,6 +228,8 @@ def _bind_oracle_functions(lib):
     lib.oracle_gemm_nt_q.argtypes = [P, i64, P, i64, P, i64, P, P, P, i64, P, i64, i64, i64, i64, i64, i64]
     lib.oracle_gemm_nt_bias.argtypes = [P, i64, P, i64, P, C.c_int, P, i64, P, i64, P, i64, i64, C.c_int, i64, i64]
     lib.oracle_gdn_conv_prep.argtypes = [P, i64, P, P, P, P, P, i64, P, i64, P, P, P, P, P, P, P, P, P, i64, i64, i64]
+    lib.oracle_attn_kv_fill.argtypes = [P, P, P, C.c_int, P, C.c_int, P, P, i64, P, i64, i64, i64, C.c_double, C.c_float,
+                                        C.c_int, P]
     for f in (lib.oracle_gdn_fill_f64, lib.oracle_gdn_fill_f32):
         f.argtypes = [P, P, P, P, P, P, P, i64, i64, P, i64, P, i64, i64, i64, i64, C.c_float, i64, i64]
     lib.oracle_threads.restype = C.c_int
@@ -325,6 +327,29 @@ def oracle_conv_prep(x, w, a_log, dt_bias, state, cu, a, b, idx, ctx=None, bias=
     lib.oracle_gdn_conv_prep(_p(x), Cc, _p(w), _p(bias), _p(a_log), _p(dt_bias), _p(st), st.shape[0], _p(cu), len(cu) - 1,
                              _p(a), _p(b), _p(idx), _p(ctx), _p(q), _p(k), _p(v), _p(g), _p(beta), T, hk, hv)
     return q, k, v, g, beta, st
+
+
+ROPE_MODES = {"neox": 0, "mrope": 1, "imrope": 2}
+
+
+def oracle_attn_kv(k, v, w, pos, slots, cache, rope_dim, theta, eps=1e-6, mode="neox", sections=(0, 0, 0), k_out=False):
+    """ridgefill_attn_kv_fill on the CPU. k, v bf16 bits [T, Hkv, 256]; w bf16 bits (uint16) or f32 [256];
+    pos i32 [T] or [3, T]; slots i32 [T]; cache bf16 bits [2, slots, Hkv, 256] (updated in a copy). Returns
+    (cache, k_out or None)."""
+    lib = oracle().lib
+    k = np.ascontiguousarray(k, np.uint16)
+    v = np.ascontiguousarray(v, np.uint16)
+    T, hkv, _ = k.shape
+    w = np.ascontiguousarray(w)
+    pos = np.ascontiguousarray(pos, np.int32)
+    slots = np.ascontiguousarray(slots, np.int32)
+    cache = np.ascontiguousarray(cache, np.uint16).copy()
+    sec = np.asarray(sections, np.int32)
+    ko = np.zeros_like(k) if k_out else None
+    lib.oracle_attn_kv_fill(_p(k), _p(v), _p(w), int(w.dtype == np.float32), _p(pos), 1 if pos.ndim == 1 else 3,
+                            _p(slots), _p(cache), cache.shape[1], _p(ko), T, hkv, rope_dim, float(theta), float(eps),
+                            ROPE_MODES[mode], _p(sec))
+    return cache, ko
 
 
 def oracle_gdn(k, v, g, beta, state, idx, cu, q=None, scale=None, f64=True, heads=None):

@@ -129,3 +129,36 @@ def test_refusals(cuda, product_lib):
               H.pint("conv", 3)]
     ops = [H.dev(X, abi.BF16)] + [abi.absent()] * 15
     assert H.launch(product_lib, "ridgefill_gdn_conv_prep", ops, params) == abi.E_INVAL   # operands missing
+
+
+def test_conv_prep_feeds_the_fill(cuda, product_lib):
+    """The block's path on the device: conv_prep's q, k, v, g, beta straight into ridgefill_gdn_fill (state-only and
+    with o). Against the sequential rule on those same device outputs the fill keeps its own bounds (state 1e-3
+    relative L2, o 1e-2); against the oracle's whole chain (oracle conv_prep, then the rule) the two-ulp differences
+    conv_prep may carry are allowed to grow to 1e-2 in the state and 2e-2 in o."""
+    torch = cuda
+    hk, hv, T = 2, 4, 300
+    d = _case(17, T, hk, hv, bias=True)
+    d["a_log"] = (0.3 * np.random.default_rng(1).standard_normal(hv) - 1.0).astype(np.float32)
+    cu, idx, ctx = [0, 130, 300], [0, 1], [0, 3]
+    got = _run(product_lib, torch, d, cu, idx, ctx, hk, hv)
+    assert got[0] == abi.OK
+    q, k, v, g, beta = got[1:6]
+    want = H.oracle_conv_prep(d["x"], d["w"], d["a_log"], d["dt_bias"], d["state"], cu, d["a"], d["b"], idx, ctx, bias=d["bias"],
+                              hk=hk, hv=hv)
+    state0 = (0.1 * np.random.default_rng(2).standard_normal((2, hv, 128, 128))).astype(np.float32)
+    from test_gdn_device import run_fill, STATE_TOL, O_TOL
+    for with_o in (False, True):
+        rc, got_state, got_o = run_fill(product_lib, torch, k, v, g, beta, state0, [0, 1], cu, hk, hv,
+                                        q=q if with_o else None, o=with_o)
+        assert rc == abi.OK
+        same_state, same_o = H.oracle_gdn(k, v, g, beta, state0, [0, 1], cu, q=q if with_o else None)
+        chain_state, chain_o = H.oracle_gdn(want[1], want[2], want[3], want[4], state0, [0, 1], cu,
+                                            q=want[0] if with_o else None)
+        for sl in (0, 1):
+            assert H.rel_l2(got_state[sl], same_state[sl]) <= STATE_TOL
+            assert H.rel_l2(got_state[sl], chain_state[sl]) <= 1e-2
+        if with_o:
+            o = H.bf16_bits_to_f32(got_o)
+            assert H.rel_l2(o, H.bf16_bits_to_f32(same_o)) <= O_TOL
+            assert H.rel_l2(o, H.bf16_bits_to_f32(chain_o)) <= 2e-2

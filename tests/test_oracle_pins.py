@@ -324,3 +324,70 @@ def test_oracle_conv_prep_definition():
         assert np.allclose(g[:37], ng[:37], rtol=1e-5, atol=0) and np.allclose(beta[:37], nb[:37], rtol=1e-5, atol=0)
         assert np.array_equal(st, nst)
         assert not q[37:].any() and not g[37:].any()
+
+
+def _attn_kv_numpy(k, v, w, pos, slots, cache, R, theta, eps, planes):
+    """ridgefill_attn_kv_fill written plainly in numpy (f64 norm, f64 rotation products): an independent
+    statement of the op to hold the oracle to, up to its f32 rounding order."""
+    T, hkv, D = k.shape
+    x = H.bf16_bits_to_f32(k).astype(np.float64)
+    wf = (H.bf16_bits_to_f32(w) if w.dtype == np.uint16 else w).astype(np.float64)
+    r = 1.0 / np.sqrt((x * x).sum(-1, keepdims=True) / D + eps)
+    kn = H.bf16_bits_to_f32(H.f32_to_bf16_bits((x * r * wf).astype(np.float32))).astype(np.float64)
+    half = R // 2
+    j = np.arange(half)
+    inv = theta ** (-2.0 * j / R)
+    p = np.stack([pos] * 3) if pos.ndim == 1 else pos
+    ang = p[planes, :].T.astype(np.float64) * inv                       # [T, half]
+    c, s = np.cos(ang).astype(np.float32)[:, None, :], np.sin(ang).astype(np.float32)[:, None, :]
+    kr = kn.copy()
+    kr[..., :half] = kn[..., :half] * c - kn[..., half:R] * s
+    kr[..., half:R] = kn[..., half:R] * c + kn[..., :half] * s
+    out = H.f32_to_bf16_bits(kr.astype(np.float32))
+    cache = cache.copy()
+    for t in range(T):
+        if 0 <= slots[t] < cache.shape[1]:
+            cache[0, slots[t]] = out[t]
+            cache[1, slots[t]] = v[t]
+    return cache, out
+
+
+@pytest.mark.parametrize("mode,sections,three,w_f32", [("neox", (0, 0, 0), False, False), ("imrope", (11, 11, 10), True, True),
+                                                       ("mrope", (8, 12, 12), True, False)])
+def test_oracle_attn_kv_definition(mode, sections, three, w_f32):
+    """The oracle's K/V cache write against a plain numpy statement of the op: k in the cache within one bf16 ulp
+    plus 2^-22 of the largest k (the f32 rounding order of the norm and the rotation differs, and a rotation whose
+    two products cancel keeps their f32 rounding), v, the skipped slots and untouched rows bit
+    for bit, and the rotary pair -> position plane rule of each rope mode."""
+    rng = np.random.default_rng(5)
+    T, hkv, R, slots_n = 96, 2, 64, 150
+    k = H.f32_to_bf16_bits(rng.standard_normal((T, hkv, 256)).astype(np.float32) * 3)
+    v = H.f32_to_bf16_bits(rng.standard_normal((T, hkv, 256)).astype(np.float32))
+    w = (1 + 0.1 * rng.standard_normal(256)).astype(np.float32)
+    if not w_f32:
+        w = H.f32_to_bf16_bits(w)
+    pos = (rng.integers(0, 40000, (3, T)) if three else np.arange(1000, 1000 + T)).astype(np.int32)
+    slots = rng.permutation(slots_n)[:T].astype(np.int32)
+    slots[::7] = -1
+    slots[3] = slots_n + 5
+    cache = rng.integers(0, 1 << 16, (2, slots_n, hkv, 256)).astype(np.uint16)
+    got, ko = H.oracle_attn_kv(k, v, w, pos, slots, cache, R, 1e7, mode=mode, sections=sections, k_out=True)
+    half = R // 2
+    j = np.arange(half)
+    if mode == "mrope":
+        planes = np.where(j < sections[0], 0, np.where(j < sections[0] + sections[1], 1, 2))
+    elif mode == "imrope":
+        planes = np.where((j % 3 == 1) & (j < 3 * sections[1]), 1, np.where((j % 3 == 2) & (j < 3 * sections[2]), 2, 0))
+    else:
+        planes = np.zeros(half, int)
+    want, out = _attn_kv_numpy(k, v, w, pos, slots, cache, R, 1e7, 1e-6, planes)
+    def close(x, y):   # one bf16 ulp, plus the f32 rounding of a rotation product where the pair cancels
+        a, b = H.bf16_bits_to_f32(x).astype(np.float64), H.bf16_bits_to_f32(y).astype(np.float64)
+        return np.all(np.abs(a - b) <= np.ldexp(np.maximum(np.abs(a), np.abs(b)), -8) + np.ldexp(np.abs(b).max(), -22))
+    assert close(ko, out), "k_out"
+    assert np.mean(ko == out) > 0.99
+    assert np.array_equal(got[1], want[1]), "v plane"
+    stored = np.zeros(slots_n, bool)
+    stored[slots[(slots >= 0) & (slots < slots_n)]] = True
+    assert np.array_equal(got[0][~stored], cache[0][~stored]), "rows no slot names are untouched"
+    assert close(got[0][stored], want[0][stored]), "k plane"
