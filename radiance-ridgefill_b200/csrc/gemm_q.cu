@@ -19,10 +19,10 @@
  *               N256 K32, four a step, int32 accumulators in each CTA's tensor memory (its 128 rows), two
  *               256-column buffers so a block's MMAs overlap the previous block's fold; its commits release
  *               the stage and hand over the accumulator in both CTAs
- *   warps 2-9   epilogue: each warp owns a 32-lane quarter of the tile rows and one 128-column half;
+ *   warps 2-17  epilogue: each warp owns a 32-lane quarter of the tile rows and a 64-column slice;
  *               it folds each finished K block into f32 registers and, at the tile's end, writes its
- *               32 x 128 bf16 block into its own 128-byte-swizzled staging tiles in shared memory and
- *               stores them with two TMA tile stores (rows and columns past y's edge are clipped)
+ *               32 x 64 bf16 block into its own 128-byte-swizzled staging tile in shared memory and
+ *               stores it with a TMA tile store (rows and columns past y's edge are clipped)
  * A K block is `group` columns: 128 for the projector folder's i8*bf16[1x128] encoding, K itself
  * for per-row / per-column scaling (one fold a tile, the int32 accumulation running over all of K).
  */
@@ -37,11 +37,14 @@ constexpr int BM = 128, BM2 = 2 * BM, BN = 256, BK = 128;   /* a CTA's rows, a p
 constexpr int kStages = 4;
 constexpr int kABytes = BM * BK, kBBytes = (BN / 2) * BK, kStageBytes = kABytes + kBBytes;   /* one CTA's halves */
 constexpr uint32_t kTmemCols = 512;
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 16;
+constexpr int kWarpCols = BN * 4 / kEpiWarps;         /* columns an epilogue warp owns (of its 32 lanes' rows) */
+constexpr int kBoxes = kWarpCols / 64;                /* its [32 rows][64 cols] bf16 store boxes */
 constexpr int kThreads = 32 * (2 + kEpiWarps);
 constexpr int kOutBox = 32 * 64 * 2;                  /* one [32 rows][64 cols] bf16 store box */
-constexpr int kStageOut = kEpiWarps * 2 * kOutBox;    /* the epilogue warps' staging tiles */
-constexpr int kSmemBytes = kStages * kStageBytes + kStageOut + 1024 /* alignment slack */ + 256 /* barriers */;
+constexpr int kStageOut = kEpiWarps * kBoxes * kOutBox;        /* the epilogue warps' staging tiles */
+constexpr int kScaleSlots = kEpiWarps * 2 * kWarpCols * 4;     /* each epilogue warp's b_scale values of two K blocks */
+constexpr int kSmemBytes = kStages * kStageBytes + kStageOut + kScaleSlots + 1024 /* alignment slack */ + 256 /* barriers */;
 
 /* Instruction descriptor of the pair's M256 N256 product: D s32 (bits 4-5 = 2), A and B signed int8 (bits
  * 7-9, 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24. */
@@ -59,27 +62,73 @@ struct GemmPlan {
 /* kBf16 false: the int8 projector (kind::i8, int32 sums folded with the scales); true: the bf16 GEMM of
  * ridgefill_gemm_nt_bias (kind::f16 with bf16 operands, f32 sums, one fold). The same tiles, the same
  * 128-byte K steps (128 int8 or 64 bf16 columns), the same roles. */
-/* A warp's two [32 rows][64 columns] staging boxes to y at (n0, y0); a box that starts past the matrix is not
- * issued (one that overlaps its edge is clipped by the copy). */
+/* A warp's [32 rows][64 columns] staging boxes to y at (n0, y0); a box that starts past the matrix is not issued
+ * (one that overlaps its edge is clipped by the copy). */
 __device__ __forceinline__ void store_boxes(const CUtensorMap* map_y, const uint8_t* stg, int64_t n0, int32_t y0, int64_t M,
                                             int64_t N) {
     if (y0 < M) {
-        if (n0 < N) rf::tma_store_2d(map_y, stg, (int32_t)n0, y0);
-        if (n0 + 64 < N) rf::tma_store_2d(map_y, stg + kOutBox, (int32_t)(n0 + 64), y0);
+#pragma unroll
+        for (int b = 0; b < kBoxes; ++b)
+            if (n0 + 64 * b < N) rf::tma_store_2d(map_y, stg + b * kOutBox, (int32_t)(n0 + 64 * b), y0);
     }
     rf::bulk_store_commit();
 }
 
-template <bool kBf16>
+/* Eight columns of a finished K block folded into a lane's f32 sums: acc = fma(float(dot) * sa, sb[n], acc), two
+ * columns an instruction (packed f32x2, each lane rounded as the scalar form). kSmallBlock (a block of at most 256
+ * K columns, |dot| <= 256 * 128 * 128 = 2^22): float(dot) exactly as (the float whose bits are 0x4B400000 + dot)
+ * - 1.5 * 2^23, on the full-rate pipes instead of the conversion unit. */
+template <bool kSmallBlock>
+__device__ __forceinline__ void fold8(const uint32_t (&r)[8], float* acc8, const float* sb8, float sa) {
+    const float4 s0 = *(const float4*)sb8, s1 = *(const float4*)(sb8 + 4);
+    const float sv[8] = { s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w };
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+        float d0, d1, t0, t1;
+        if (kSmallBlock)
+            rf::add2_rn(d0, d1, __uint_as_float(0x4B400000u + r[e]), __uint_as_float(0x4B400000u + r[e + 1]), -12582912.0f,
+                        -12582912.0f);
+        else
+            d0 = __int2float_rn((int)r[e]), d1 = __int2float_rn((int)r[e + 1]);
+        rf::mul2_rn(t0, t1, d0, d1, sa, sa);
+        rf::fma2_rn(acc8[e], acc8[e + 1], t0, t1, sv[e], sv[e + 1]);
+    }
+}
+
+/* One finished K block (the lane's kWarpCols accumulator columns at `taddr`) folded into its f32 sums, eight
+ * columns a tensor-memory load. kDump: also the block's int32 sums into g.acc (the optional acc operand). */
+template <bool kSmallBlock, bool kDump>
+__device__ __forceinline__ void fold_block(uint32_t taddr, float (&acc)[kWarpCols], const float* sb, float sa,
+                                           const RidgeFillGemmQ& g, int64_t m, int64_t n0, bool row_live, int f, int blocks) {
+#pragma unroll
+    for (int c = 0; c < kWarpCols / 8; ++c) {
+        uint32_t r[8];
+        rf::tmem_ld8(taddr + c * 8, r);
+        rf::tmem_ld_wait();
+        if (kDump && row_live)
+            for (int i = 0; i < 8; ++i)
+                if (n0 + c * 8 + i < g.N) g.acc[(m * g.N + n0 + c * 8 + i) * blocks + f] = (int32_t)r[i];
+        fold8<kSmallBlock>(r, acc + c * 8, sb + c * 8, sa);
+    }
+}
+
+/* The kernel's forms: the bf16 GEMM, and the int8 projector with K blocks of at most 256 columns (the exact
+ * integer-to-float trick), with larger blocks (K itself: per-row / per-column scaling), or with the int32 block
+ * sums written out (any block size). Separate instantiations keep each form's registers to itself. */
+enum GemmMode { kModeBf16 = 0, kModeI8Small = 1, kModeI8Large = 2, kModeI8Dump = 3 };
+
+template <int kMode>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
               const __grid_constant__ CUtensorMap map_y, const GemmPlan p) {
+    constexpr bool kBf16 = kMode == kModeBf16;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* tile_a = smem;
     uint8_t* tile_b = smem + kStages * kABytes;
     uint8_t* stage_out = smem + kStages * kStageBytes;   /* 1024-byte aligned: kStageBytes is */
-    uint64_t* full = (uint64_t*)(stage_out + kStageOut);
+    float* scale_slots = (float*)(stage_out + kStageOut);
+    uint64_t* full = (uint64_t*)(stage_out + kStageOut + kScaleSlots);
     uint64_t* empty = full + kStages;
     uint64_t* acc_full = empty + kStages;
     uint64_t* acc_empty = acc_full + 2;
@@ -182,9 +231,9 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
         }
     } else {
         /* ---------------------------------------------------------- epilogue */
-        const int quarter = warp & 3, half = (warp - 2) >> 2;
+        const int quarter = warp & 3, slice = (warp - 2) >> 2;   /* a warp reads tensor-memory lanes 32 (warp % 4).. */
         const int row = quarter * 32 + lane;
-        const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + half * 128;
+        const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16) + slice * kWarpCols;
         uint32_t fold = 0;
         bool ok = true;
         if constexpr (kBf16) {
@@ -194,26 +243,26 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
             const RidgeFillGemmBias& gb = p.gb;
             for (int tile = pair; tile < p.tiles && ok; tile += pairs, ++fold) {
                 const int64_t m = (int64_t)(tile / p.n_tiles) * BM2 + rank * BM + row;
-                const int64_t n0 = (int64_t)(tile % p.n_tiles) * BN + half * 128;
+                const int64_t n0 = (int64_t)(tile % p.n_tiles) * BN + slice * kWarpCols;
                 const uint32_t buf = fold & 1, use = (fold >> 1) & 1;
                 if (!(ok = rf::mbar_wait(&acc_full[buf], use, abort, rf::kErrGemmWaitEpilogue))) break;
                 rf::tc_fence_after();
-                uint8_t* stg = stage_out + (warp - 2) * 2 * kOutBox;
+                uint8_t* stg = stage_out + (warp - 2) * kBoxes * kOutBox;
                 if (lane == 0) rf::bulk_store_wait_read();
                 __syncwarp();
 #pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
+                for (int c = 0; c < kWarpCols / 32; ++c) {
                     uint32_t r[32];
                     rf::tmem_ld32(lane_addr + buf * BN + c * 32, r);
                     rf::tmem_ld_wait();
-                    if (c == 3) {
+                    if (c == kWarpCols / 32 - 1) {
                         rf::tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) rf::mbar_arrive_cluster(rf::map_rank(rf::smem_addr(&acc_empty[buf]), 0));
+                        if (lane == 0) rf::mbar_arrive_cluster_relaxed(rf::map_rank(rf::smem_addr(&acc_empty[buf]), 0));
                     }
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        const int cc = c * 32 + j * 8;   /* column within this warp's half */
+                        const int cc = c * 32 + j * 8;   /* column within this warp's slice */
                         const int64_t n = n0 + cc;
                         float bv[8] = {}, rv[8] = {};
                         if (n < gb.N) {
@@ -269,54 +318,46 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
         }
         for (int tile = pair; tile < p.tiles && ok && !kBf16; tile += pairs) {
             const int64_t m = (int64_t)(tile / p.n_tiles) * BM2 + rank * BM + row;
-            const int64_t n0 = (int64_t)(tile % p.n_tiles) * BN + half * 128;
-            const bool row_live = m < g.M;
-            float acc[128];
+            const int64_t n0 = (int64_t)(tile % p.n_tiles) * BN + slice * kWarpCols;
+            const bool row_live = m < g.M, copies = lane < kWarpCols / 4;
+            const uint32_t col_bytes = copies && n0 + lane * 4 < g.N ? 16u : 0u;   /* N is a multiple of 16 */
+            float acc[kWarpCols];
 #pragma unroll
-            for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+            for (int i = 0; i < kWarpCols; ++i) acc[i] = 0.0f;
+            /* The scales of block f + 1 are fetched while block f waits and folds: a_scale into a register, this
+             * warp's b_scale values (four a lane) by asynchronous copy into the warp's other shared-memory slot
+             * (columns past N read as zero). */
+            float* slots = scale_slots + (warp - 2) * 2 * kWarpCols;
+            __syncwarp();   /* the previous tile's reads of the slots are done */
+            if (copies) rf::cp_async16_zfill(slots + lane * 4, g.b_scale + (col_bytes ? n0 + lane * 4 : 0), col_bytes);
+            float sa_next = row_live ? g.a_scale[m * g.ldas] : 0.0f;
             for (int f = 0; f < p.folds; ++f, ++fold) {
                 const uint32_t buf = fold & 1, use = (fold >> 1) & 1;
+                const float* sb = slots + (f & 1) * kWarpCols;
+                rf::cp_async_wait_all();
+                __syncwarp();   /* block f's scales are in, and every lane is done with block f - 1's slot */
+                const float sa = sa_next;
+                if (f + 1 < p.folds) {
+                    if (copies)
+                        rf::cp_async16_zfill(slots + ((f + 1) & 1) * kWarpCols + lane * 4,
+                                             g.b_scale + (col_bytes ? (int64_t)(f + 1) * g.N + n0 + lane * 4 : 0), col_bytes);
+                    sa_next = row_live ? g.a_scale[m * g.ldas + f + 1] : 0.0f;
+                }
                 if (!(ok = rf::mbar_wait(&acc_full[buf], use, abort, rf::kErrGemmWaitEpilogue))) break;
                 rf::tc_fence_after();
-                const float sa = row_live ? g.a_scale[m * g.ldas + f] : 0.0f;
-                const float* sb = g.b_scale + (int64_t)f * g.N + n0;
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t r[32];
-                    rf::tmem_ld32(lane_addr + buf * BN + c * 32, r);
-                    rf::tmem_ld_wait();
-                    if (g.acc && row_live) {
-                        const int64_t blocks = p.folds;
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            const int64_t n = n0 + c * 32 + i;
-                            if (n < g.N) g.acc[(m * g.N + n) * blocks + f] = (int32_t)r[i];
-                        }
-                    }
-#pragma unroll
-                    for (int i4 = 0; i4 < 8; ++i4) {
-                        const int64_t n = n0 + c * 32 + i4 * 4;
-                        const float4 s4 = n < g.N ? __ldg((const float4*)(sb + c * 32 + i4 * 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
-                        const float sv[4] = { s4.x, s4.y, s4.z, s4.w };
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int i = c * 32 + i4 * 4 + e;
-                            const float t = __fmul_rn(__int2float_rn((int)r[i4 * 4 + e]), sa);
-                            acc[i] = __fmaf_rn(t, sv[e], acc[i]);
-                        }
-                    }
-                }
+                fold_block<kMode == kModeI8Small, kMode == kModeI8Dump>(lane_addr + buf * BN, acc, sb, sa, g, m, n0, row_live,
+                                                                        f, p.folds);
                 rf::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) rf::mbar_arrive_cluster(rf::map_rank(rf::smem_addr(&acc_empty[buf]), 0));
+                if (lane == 0) rf::mbar_arrive_cluster_relaxed(rf::map_rank(rf::smem_addr(&acc_empty[buf]), 0));
             }
             if (!ok) break;
             /* bf16 (and the bias) into this warp's staging tiles, once the previous tile's stores have read them. */
-            uint8_t* stg = stage_out + (warp - 2) * 2 * kOutBox;
+            uint8_t* stg = stage_out + (warp - 2) * kBoxes * kOutBox;
             if (lane == 0) rf::bulk_store_wait_read();
             __syncwarp();
 #pragma unroll
-            for (int v = 0; v < 16; ++v) {
+            for (int v = 0; v < kWarpCols / 8; ++v) {
                 const int64_t n = n0 + v * 8;
                 uint32_t o[4];
 #pragma unroll
@@ -570,23 +611,23 @@ bool int8_tile_map(CUtensorMap* map, const void* base, int64_t rows, int64_t col
 }
 
 /* One 2-CTA cluster per pair tile, as many pairs as the device holds at once (persistent). */
-template <bool kBf16>
+template <int kMode>
 int launch_pairs(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap& map_y, const GemmPlan& p,
                  cudaStream_t stream) {
-    static int max_pairs[2] = { 0, 0 };
-    if (cudaFuncSetAttribute(gemm_q_kernel<kBf16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+    static int max_pairs[4] = { 0, 0, 0, 0 };
+    if (cudaFuncSetAttribute(gemm_q_kernel<kMode>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
         return RAD_E_DEVICE;
-    if (!max_pairs[kBf16]) {
+    if (!max_pairs[kMode]) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * (unsigned)(rf::sm_count() / 2));
         cfg.blockDim = dim3(kThreads);
         cfg.dynamicSmemBytes = kSmemBytes;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, gemm_q_kernel<kBf16>, &cfg) != cudaSuccess || n <= 0) return RAD_E_DEVICE;
-        max_pairs[kBf16] = n;
+        if (cudaOccupancyMaxActiveClusters(&n, gemm_q_kernel<kMode>, &cfg) != cudaSuccess || n <= 0) return RAD_E_DEVICE;
+        max_pairs[kMode] = n;
     }
-    const int pairs = p.tiles < max_pairs[kBf16] ? p.tiles : max_pairs[kBf16];
-    gemm_q_kernel<kBf16><<<2 * pairs, kThreads, kSmemBytes, stream>>>(map_a, map_b, map_y, p);
+    const int pairs = p.tiles < max_pairs[kMode] ? p.tiles : max_pairs[kMode];
+    gemm_q_kernel<kMode><<<2 * pairs, kThreads, kSmemBytes, stream>>>(map_a, map_b, map_y, p);
     return rf::launch_status();
 }
 
@@ -605,7 +646,9 @@ int launch_gemm(const RidgeFillGemmQ& g, cudaStream_t stream) {
     p.tiles = (int)tiles;
     p.folds = (int)(g.K / g.group);
     p.steps_per_fold = (int)(g.group / BK);
-    return launch_pairs<false>(map_a, map_b, map_y, p, stream);
+    if (g.acc) return launch_pairs<kModeI8Dump>(map_a, map_b, map_y, p, stream);
+    if (g.group <= 256) return launch_pairs<kModeI8Small>(map_a, map_b, map_y, p, stream);
+    return launch_pairs<kModeI8Large>(map_a, map_b, map_y, p, stream);
 }
 
 /* A [rows, cols] bf16 matrix with row pitch `pitch` elements, read in [box_rows, 64] tiles (128 bytes of K)
@@ -637,7 +680,7 @@ int launch_gemm_bf16(const RidgeFillGemmBias& g, cudaStream_t stream) {
     p.tiles = (int)tiles;
     p.folds = 1;
     p.steps_per_fold = (int)((g.K + BK / 2 - 1) / (BK / 2));   /* a ragged last step reads zeros past K */
-    return launch_pairs<true>(map_a, map_b, map_y, p, stream);
+    return launch_pairs<kModeBf16>(map_a, map_b, map_y, p, stream);
 }
 
 }  // namespace

@@ -277,6 +277,30 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
 }
 
+/* Packed f32x2 arithmetic (sm_100): two lanes of f32 per instruction, each rounded as its scalar form. */
+__device__ __forceinline__ void fma2_rn(float& a0, float& a1, float x0, float x1, float y0, float y1) {   /* a = x * y + a */
+    asm("{\n .reg .b64 a, x, y;\n mov.b64 a, {%0, %1};\n mov.b64 x, {%2, %3};\n mov.b64 y, {%4, %5};\n"
+        " fma.rn.f32x2 a, x, y, a;\n mov.b64 {%0, %1}, a;\n}"
+        : "+f"(a0), "+f"(a1) : "f"(x0), "f"(x1), "f"(y0), "f"(y1));
+}
+__device__ __forceinline__ void mul2_rn(float& d0, float& d1, float x0, float x1, float y0, float y1) {
+    asm("{\n .reg .b64 d, x, y;\n mov.b64 x, {%2, %3};\n mov.b64 y, {%4, %5};\n mul.rn.f32x2 d, x, y;\n"
+        " mov.b64 {%0, %1}, d;\n}"
+        : "=f"(d0), "=f"(d1) : "f"(x0), "f"(x1), "f"(y0), "f"(y1));
+}
+__device__ __forceinline__ void add2_rn(float& d0, float& d1, float x0, float x1, float y0, float y1) {
+    asm("{\n .reg .b64 d, x, y;\n mov.b64 x, {%2, %3};\n mov.b64 y, {%4, %5};\n add.rn.f32x2 d, x, y;\n"
+        " mov.b64 {%0, %1}, d;\n}"
+        : "=f"(d0), "=f"(d1) : "f"(x0), "f"(x1), "f"(y0), "f"(y1));
+}
+
+/* A relaxed arrive (no release fence) on a barrier of this cluster: for hand-overs whose data needs no
+ * ordering through memory -- a tensor-memory buffer whose reads the arriving thread has already waited for
+ * (tcgen05.wait::ld), so the arrive only says that the columns may be overwritten. */
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t caddr) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+
 /* Tensor memory of a CTA pair: the same warp of both CTAs allocates, each CTA receiving kCols columns at the
  * same address (written to its own `slot`). */
 template <uint32_t kCols>
@@ -343,6 +367,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
           "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
           "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
+}
+
+/* 16 bytes global -> shared through L2 (cp.async.cg); `bytes` 16 copies, 0 writes zeros and reads nothing. */
+__device__ __forceinline__ void cp_async16_zfill(void* dst, const void* src, uint32_t bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+/* 8 consecutive 32-bit columns of this thread's tensor-memory lane. */
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
 }
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }

@@ -11,6 +11,11 @@ Writes:
                       score[token_id], so the kept rows are unchanged; the real-text ids are not copied.
   quantise_i8.npz     tools/ridgefill_projector.py quantise_i8 (the folder's i8*bf16[1x128] encoder) applied
                       to seeded weights: inputs and the reference's codes and scales.
+  folder_bf16/        a small bf16 projector folder (late layers 4..6 of 7, n_embd 16, stream width 256, the
+                      correction on the recurrent layers 4 and 6, the three row tables over 40 ids), its
+                      manifest's hashes by the reference's own sha256_file.
+  folder_i8/          the reference's `ridgefill_projector.py int8` run on folder_bf16: its proj8 files
+                      (codes, bf16 scales, bias), the correction and row tables re-stamped, and its manifest.
 These files are the only place the reference's outputs enter this repository; tests read them, never
 the reference itself.
 """
@@ -69,6 +74,43 @@ def quantise_fixture(ref: Path) -> None:
                         codes=codes.numpy(), scale=scale.view(torch.int16).numpy().view(np.uint16))
 
 
+def folder_fixture(ref: Path) -> None:
+    import shutil
+    import torch
+    sys.path.insert(0, str(ref / "tools"))
+    sys.path.insert(0, str(ref / "tools" / "dev"))
+    spec = importlib.util.spec_from_file_location("ridgefill_projector", ref / "tools" / "ridgefill_projector.py")
+    P = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(P)
+    src, out = HERE / "folder_bf16", HERE / "folder_i8"
+    for d in (src, out):
+        if d.exists():
+            shutil.rmtree(d)
+    src.mkdir()
+    gen = torch.Generator().manual_seed(20261202)
+    layers = (4, 5, 6)
+    for layer in layers:
+        w = torch.randn(16, 256, generator=gen) * torch.exp(torch.rand(16, 1, generator=gen) * 4 - 2)
+        if layer == 5:
+            w[2, 128:] = 0.0   # an all-zero group: scale 1
+        P.save({f"proj.{layer}.weight": w.to(torch.bfloat16),
+                f"proj.{layer}.bias": torch.randn(16, generator=gen).to(torch.bfloat16)}, src / f"proj.L{layer}.safetensors")
+    P.save({"st.4": torch.randn(2, 8, 8, generator=gen), "st.6": torch.randn(2, 8, 8, generator=gen)},
+           src / "correction.safetensors")
+    P.save({"score": torch.randn(40, generator=gen), "score_none": torch.full((40,), float("-inf")),
+            "score_all": torch.zeros(40)}, src / "rowsel.safetensors")
+    (src / "README.md").write_text("a small projector folder for the loader's tests\n")
+    names = [f"proj.L{layer}.safetensors" for layer in layers] + ["correction.safetensors", "rowsel.safetensors"]
+    manifest = {"format": 1, "adapter": "qwen4exp", "split": 4, "stream_width": 256, "block_in_width": 16,
+                "layers": {"4": "recurrent", "5": "full_attn", "6": "recurrent"},
+                "correction": {"kind": "gdn_terminal_state", "heads": 2, "sd": [8, 8], "layers": [4, 6]},
+                "projector": {"dtype": "bf16", "layout": "plain_nk",
+                              "files": {str(layer): f"proj.L{layer}.safetensors" for layer in layers}},
+                "files": {n: P.S.sha256_file(src / n) for n in sorted(names)}}
+    (src / "ridgefill.json").write_text(json.dumps(manifest, indent=1) + "\n")
+    assert P.main(["int8", "--from", str(src), "--out", str(out)]) == 0
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -76,5 +118,6 @@ if __name__ == "__main__":
     rho_fixture(ref)
     rowsel_fixture(ref)
     quantise_fixture(ref)
+    folder_fixture(ref)
     for p in sorted(HERE.iterdir()):
         print(p.name, p.stat().st_size)
