@@ -74,30 +74,22 @@ __device__ __forceinline__ void store_boxes(const CUtensorMap* map_y, const uint
     rf::bulk_store_commit();
 }
 
-/* Eight columns of a finished K block folded into a lane's f32 sums: acc = fma(float(dot) * sa, sb[n], acc), two
- * columns an instruction (packed f32x2, each lane rounded as the scalar form). kSmallBlock (a block of at most 256
- * K columns, |dot| <= 256 * 128 * 128 = 2^22): float(dot) exactly as (the float whose bits are 0x4B400000 + dot)
- * - 1.5 * 2^23, on the full-rate pipes instead of the conversion unit. */
-template <bool kSmallBlock>
+/* Eight columns of a finished K block folded into a lane's f32 sums: acc = fma(float(dot) * sa, sb[n], acc), the
+ * product and the fma two columns an instruction (packed f32x2, each lane rounded as the scalar form). */
 __device__ __forceinline__ void fold8(const uint32_t (&r)[8], float* acc8, const float* sb8, float sa) {
     const float4 s0 = *(const float4*)sb8, s1 = *(const float4*)(sb8 + 4);
     const float sv[8] = { s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w };
 #pragma unroll
     for (int e = 0; e < 8; e += 2) {
-        float d0, d1, t0, t1;
-        if (kSmallBlock)
-            rf::add2_rn(d0, d1, __uint_as_float(0x4B400000u + r[e]), __uint_as_float(0x4B400000u + r[e + 1]), -12582912.0f,
-                        -12582912.0f);
-        else
-            d0 = __int2float_rn((int)r[e]), d1 = __int2float_rn((int)r[e + 1]);
-        rf::mul2_rn(t0, t1, d0, d1, sa, sa);
+        float t0, t1;
+        rf::mul2_rn(t0, t1, __int2float_rn((int)r[e]), __int2float_rn((int)r[e + 1]), sa, sa);
         rf::fma2_rn(acc8[e], acc8[e + 1], t0, t1, sv[e], sv[e + 1]);
     }
 }
 
 /* One finished K block (the lane's kWarpCols accumulator columns at `taddr`) folded into its f32 sums, eight
  * columns a tensor-memory load. kDump: also the block's int32 sums into g.acc (the optional acc operand). */
-template <bool kSmallBlock, bool kDump>
+template <bool kDump>
 __device__ __forceinline__ void fold_block(uint32_t taddr, float (&acc)[kWarpCols], const float* sb, float sa,
                                            const RidgeFillGemmQ& g, int64_t m, int64_t n0, bool row_live, int f, int blocks) {
 #pragma unroll
@@ -108,14 +100,13 @@ __device__ __forceinline__ void fold_block(uint32_t taddr, float (&acc)[kWarpCol
         if (kDump && row_live)
             for (int i = 0; i < 8; ++i)
                 if (n0 + c * 8 + i < g.N) g.acc[(m * g.N + n0 + c * 8 + i) * blocks + f] = (int32_t)r[i];
-        fold8<kSmallBlock>(r, acc + c * 8, sb + c * 8, sa);
+        fold8(r, acc + c * 8, sb + c * 8, sa);
     }
 }
 
-/* The kernel's forms: the bf16 GEMM, and the int8 projector with K blocks of at most 256 columns (the exact
- * integer-to-float trick), with larger blocks (K itself: per-row / per-column scaling), or with the int32 block
- * sums written out (any block size). Separate instantiations keep each form's registers to itself. */
-enum GemmMode { kModeBf16 = 0, kModeI8Small = 1, kModeI8Large = 2, kModeI8Dump = 3 };
+/* The kernel's forms: the bf16 GEMM, the int8 projector, and the int8 projector writing out its int32 block sums
+ * (the optional acc operand). Separate instantiations keep each form's registers to itself. */
+enum GemmMode { kModeBf16 = 0, kModeI8 = 1, kModeI8Dump = 2 };
 
 template <int kMode>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -345,8 +336,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
                 }
                 if (!(ok = rf::mbar_wait(&acc_full[buf], use, abort, rf::kErrGemmWaitEpilogue))) break;
                 rf::tc_fence_after();
-                fold_block<kMode == kModeI8Small, kMode == kModeI8Dump>(lane_addr + buf * BN, acc, sb, sa, g, m, n0, row_live,
-                                                                        f, p.folds);
+                fold_block<kMode == kModeI8Dump>(lane_addr + buf * BN, acc, sb, sa, g, m, n0, row_live, f, p.folds);
                 rf::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) rf::mbar_arrive_cluster_relaxed(rf::map_rank(rf::smem_addr(&acc_empty[buf]), 0));
@@ -614,7 +604,7 @@ bool int8_tile_map(CUtensorMap* map, const void* base, int64_t rows, int64_t col
 template <int kMode>
 int launch_pairs(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap& map_y, const GemmPlan& p,
                  cudaStream_t stream) {
-    static int max_pairs[4] = { 0, 0, 0, 0 };
+    static int max_pairs[3] = { 0, 0, 0 };
     if (cudaFuncSetAttribute(gemm_q_kernel<kMode>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
         return RAD_E_DEVICE;
     if (!max_pairs[kMode]) {
@@ -647,8 +637,7 @@ int launch_gemm(const RidgeFillGemmQ& g, cudaStream_t stream) {
     p.folds = (int)(g.K / g.group);
     p.steps_per_fold = (int)(g.group / BK);
     if (g.acc) return launch_pairs<kModeI8Dump>(map_a, map_b, map_y, p, stream);
-    if (g.group <= 256) return launch_pairs<kModeI8Small>(map_a, map_b, map_y, p, stream);
-    return launch_pairs<kModeI8Large>(map_a, map_b, map_y, p, stream);
+    return launch_pairs<kModeI8>(map_a, map_b, map_y, p, stream);
 }
 
 /* A [rows, cols] bf16 matrix with row pitch `pitch` elements, read in [box_rows, 64] tiles (128 bytes of K)
