@@ -327,7 +327,7 @@ extern "C" int ridgefill_gemm_q_parse(const RadArgs* a, int with_bias, RidgeFill
     const RadTensor* B = rad_arg_in(a, GQ_B);
     const RadTensor* BS = rad_arg_in(a, GQ_B_SCALE);
     const RadTensor* bias = with_bias ? rad_arg_in(a, GB_BIAS) : nullptr;
-    const RadTensor* Y = rad_arg_in(a, with_bias ? GB_Y : GQ_Y);
+    const RadTensor* Y = rad_arg_in(a, with_bias ? (int)GB_Y : (int)GQ_Y);
     const RadTensor* acc = with_bias ? rad_arg_in(a, GB_ACC) : nullptr;
     long long M = 0, N = 0, K = 0, group = 0;
     const char* dt = rad_args_gets(a, "dtype");
