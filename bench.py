@@ -7,7 +7,10 @@ mask -> activation codes -> int8 projector (d 2,048, per-column scales, fused bi
 state undo -> Gated DeltaNet chunk fill (16 q/k heads, 32 v heads, 128 dims, state [32,128,128] f32)
 -> rho -> state apply -> hazard, every op a launch of the library's sm_100a device rows through the C
 ABI. Synthetic inputs with BASELINE's shapes and distributions, seeded; inputs (> 700 MB) exceed the
-126 MB L2, so no flush is needed between steps.
+126 MB L2, so no flush is needed between steps. The timed passes are issued pipelined (Step.run_pipelined):
+the projector path (codes, projector, select) on a normal-priority stream beside the fill's high-priority
+stream, as a pass over the late layers runs the next layer's projection of the shared h_S beside this layer's
+fill; every op of every pass still runs, and a pass ends when both streams have finished it.
 
 value   device time of K passes with inputs resident in HBM (CUDA events, max over ranks)
 e2e     the same passes with each step's inputs copied host->device from pinned memory and the results
@@ -49,15 +52,39 @@ def peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms while the timed region runs."""
+    """SM clocks and clock-event (throttle) reasons sampled while the timed region runs: through NVML every
+    millisecond (a region of a few tens of milliseconds still gets samples), else nvidia-smi every 200 ms."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits (nvml.h): sw power cap 0x4, hw slowdown 0x8, sw thermal 0x20, hw thermal 0x40
+    NVML_BITS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+                 ("sw_power_cap", 0x4))
 
     def __init__(self, gpu_index: int):
-        self.idx, self.rows, self.proc = gpu_index, [], None
+        self.idx, self.rows, self.proc, self.nvml, self.samples = gpu_index, [], None, None, []
+        self.stop_flag = threading.Event()
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            import torch
+            pr = torch.cuda.get_device_properties(self.idx)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.idx)
 
     def start(self):
+        try:
+            self.nvml = self._nvml_handle()
+            self.max_mhz = self.nvml[0].nvmlDeviceGetMaxClockInfo(self.nvml[1], self.nvml[0].NVML_CLOCK_SM)
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
@@ -67,11 +94,32 @@ class ClockSampler:
         except OSError:
             self.proc = None
 
+    def _poll(self):
+        nv, h = self.nvml
+        while not self.stop_flag.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                try:
+                    bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                except AttributeError:
+                    bits = nv.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                self.samples.append((mhz, bits))
+            except Exception:
+                return
+            time.sleep(0.001)
+
     def _read(self):
         for line in self.proc.stdout:
             self.rows.append([x.strip() for x in line.split(",")])
 
     def stop(self) -> dict:
+        if self.nvml:
+            self.stop_flag.set()
+            self.thread.join(timeout=5)
+            sm = [float(m) for m, _ in self.samples]
+            reasons = sorted({name for _, b in self.samples for name, bit in self.NVML_BITS if b & bit})
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(self.max_mhz),
+                    "reasons": reasons, "samples": len(sm), "source": "nvml, 1 ms"}
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.proc.terminate()
@@ -84,7 +132,7 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in self.rows if len(r) >= 9 for i in range(4) if r[5 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(sm)}
+                "reasons": reasons, "samples": len(sm), "source": "nvidia-smi, 200 ms"}
 
 
 def dist_setup():
@@ -132,7 +180,9 @@ def run_mine(args):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     step = RS.Step(RS.StepShape(T=T_FULL), device=str(dev), seed=1234 + rank)
-    stream = torch.cuda.Stream(device=dev)
+    # the pass's main stream at high priority; the projector path beside it at normal priority (run_pipelined)
+    stream = torch.cuda.Stream(device=dev, priority=-1)
+    side = torch.cuda.Stream(device=dev, priority=0)
     alg = step.algorithmic()
 
     def barrier():
@@ -157,16 +207,20 @@ def run_mine(args):
     dom_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(local)
+    pipelined = dominant not in RS.Step.SIDE_OPS
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
-            step.run(stream.cuda_stream)
+            step.run_pipelined(stream, side)
         stream.synchronize()
         barrier()
         torch.cuda.synchronize()
         clocks.start()
         start.record()
         for i in range(args.steps):
-            step.run(stream.cuda_stream, events={dominant: dom_ev[i]})
+            if pipelined:
+                step.run_pipelined(stream, side, events={dominant: dom_ev[i]})
+            else:
+                step.run(stream.cuda_stream, events={dominant: dom_ev[i]})
         end.record()
         stream.synchronize()
     clock_info = clocks.stop()
@@ -204,7 +258,7 @@ def run_mine(args):
             stream.wait_event(ev_in)
             if done_out[b_] is not None:
                 stream.wait_event(done_out[b_])
-            steps2[b_].run(stream.cuda_stream)
+            steps2[b_].run_pipelined(stream, side)
             done_comp[b_] = torch.cuda.Event()
             done_comp[b_].record(stream)
             with torch.cuda.stream(s_out):
@@ -263,7 +317,8 @@ def run_mine(args):
                                        "(int8, per-column scales), Gated DeltaNet fill 16 qk / 32 v heads x 128, "
                                        "class mask share 0.30",
                            "rows": T_FULL, "d": 2048, "l2": "inputs larger than L2 (no flush)",
-                           "parallelism": f"independent prompts x{world}"},
+                           "parallelism": f"independent prompts x{world}",
+                           "streams": "projector path beside the fill (two streams, pipelined pass)"},
                 "gpu_launches": Step_launches(step) * args.steps,
                 "per_op_ms": {k: round(v, 4) for k, v in sorted(per_op.items(), key=lambda kv: -kv[1])},
                 "roofline": roof, "clocks": clock_info,

@@ -13,7 +13,12 @@ arch/ridgefill_layer.h:65-116, arch/qwen4exp_blocks.h:110-182):
     ridgefill_hazard            the prefix-cache hazard record
 
 Buffers live on one CUDA device (torch tensors: allocation and streams only); every op is a launch of a
-sm_100a device row. `Step.run()` issues one pass on a stream; nothing here computes on the host.
+sm_100a device row. `Step.run()` issues one pass on a stream, in the order above; nothing here computes on the
+host. `Step.run_pipelined()` issues the same launches on two streams: the projector path (quantiser, projector,
+select) on a lower-priority side stream after the mask, the rest on the main stream. Every late layer projects
+the same h_S (arch/ridgefill_layer.h:60-63), so in a pass over the late layers the projector path of the next
+layer does not wait for this layer's fill: issued beside it, it runs on the SMs the fill's phase-1 CTAs release
+while the fill's chains finish.
 """
 from __future__ import annotations
 
@@ -144,6 +149,38 @@ class Step:
 
     # kernels a pass launches (the GDN fill is two: the sequence plan, then the fill kernel)
     LAUNCHES_PER_PASS = 10
+    SIDE_OPS = ("ridgefill_quant_act_i8g", "ridgefill_gemm_nt_q_bias", "ridgefill_select")
+
+    def _launch(self, name, r, tens, params, stream: int) -> None:
+        sb = self.gdn_scratch if name == "ridgefill_gdn_fill" else 0
+        rc = self.lib.launch(r, tens, params, stream=stream, scratch=self.scratch.data_ptr() if sb else None,
+                             scratch_bytes=sb)
+        if rc != abi.OK:
+            raise RuntimeError(f"{name}: device row refused or failed (rc {rc})")
+
+    def run_pipelined(self, main, side, events=None) -> None:
+        """Issue one pass on two torch streams: the mask and the undo on `main`, then the projector path on
+        `side` (a stream of lower priority, made to wait for the undo) while `main` runs the fill, rho, the
+        apply and the hazard record; `main` then waits for `side`, so the pass is complete when `main` is.
+        `events` (optional) maps an op on `main` to a pair of CUDA events recorded around its launch."""
+        torch = self.torch
+        fork, join = torch.cuda.Event(), torch.cuda.Event()
+        main_ops = [a for a in self._args if a[0] not in self.SIDE_OPS]
+        side_ops = [a for a in self._args if a[0] in self.SIDE_OPS]
+        for i, (name, r, tens, params) in enumerate(main_ops):
+            if i == 2:   # after the mask and the undo: the side stream may start
+                fork.record(main)
+                side.wait_event(fork)
+                for a in side_ops:
+                    self._launch(*a, side.cuda_stream)
+                join.record(side)
+            ev = events.get(name) if events else None
+            if ev:
+                ev[0].record(main)
+            self._launch(name, r, tens, params, main.cuda_stream)
+            if ev:
+                ev[1].record(main)
+        main.wait_event(join)
 
     def run(self, stream: int, events=None) -> None:
         """Issue one pass on `stream`. `events` (optional) maps an op name to a pair of CUDA events recorded
@@ -152,13 +189,9 @@ class Step:
             ev = events.get(name) if events else None
             if ev:
                 ev[0].record()
-            sb = self.gdn_scratch if name == "ridgefill_gdn_fill" else 0
-            rc = self.lib.launch(r, tens, params, stream=stream, scratch=self.scratch.data_ptr() if sb else None,
-                                 scratch_bytes=sb)
+            self._launch(name, r, tens, params, stream)
             if ev:
                 ev[1].record()
-            if rc != abi.OK:
-                raise RuntimeError(f"{name}: device row refused or failed (rc {rc})")
 
     # --------------------------------------------------------------- algorithmic work of one pass
     def algorithmic(self) -> dict:
