@@ -274,6 +274,7 @@ typedef struct RidgeFillGemmQ {
     uint16_t*      y;        int64_t ldy;         /* [M, N] bf16 */
     int32_t*       acc;                           /* optional [M, N, K/group] int32 block sums (debug) */
     int64_t        M, N, K, group;
+    int64_t        max_ctas;                      /* at most this many CTAs (SMs), 0: the whole GPU */
 } RidgeFillGemmQ;
 
 /* ridgefill_quant_act_i8g: x bf16 [M, K] -> q i8 [M, K], s f32 [M, K/group]: per group of `group` columns,

@@ -60,6 +60,8 @@ static const RadParamSpec pGemmQ[] = { RF_P_INT("M"), RF_P_INT("N"), RF_P_INT("K
 static const RadOperandSpec oGemmQ[] = { RF_IN("a"), RF_IN_OPT("a_scale"), RF_IN("b"), RF_IN("b_scale"), RF_OUT("y"),
                                          RF_IN_OPT("a_sum"), RF_IN_OPT("b_ref") };
 /* new ops */
+static const RadParamSpec pGemmQBias[] = { RF_P_INT("M"), RF_P_INT("N"), RF_P_INT("K"), RF_P_INT("group"),
+                                           RF_P_STR("dtype"), RF_P_OPT("max_ctas", RAD_P_INT) };
 static const RadOperandSpec oGemmQBias[] = { RF_IN("a"), RF_IN("a_scale"), RF_IN("b"), RF_IN("b_scale"),
                                              RF_IN_OPT("bias"), RF_OUT("y"), RF_OUT_OPT("acc") };
 static const RadParamSpec pQuant[] = { RF_P_INT("M"), RF_P_INT("n"), RF_P_INT("group"), RF_P_STR("dtype") };
@@ -119,9 +121,10 @@ static const RadOpSchema kSchemas[] = {
   "y[m, n] = sum_j a_scale[m, j] * b_scale[n, j] * sum_{k in block j} a[m, k] * b[n, k], bf16; int32 within "
   "each `group`-column block, f32 fold in block order, one rounding. a i8 [M, K], a_scale f32 [M, K/group]; "
   "b and b_scale in the stored form this row's layout hook describes (codes [N, K] i8, scale f32 [K/group, N])." },
-{ "ridgefill_gemm_nt_q_bias", RF_ARR(pGemmQ), RF_ARR(oGemmQBias),
+{ "ridgefill_gemm_nt_q_bias", RF_ARR(pGemmQBias), RF_ARR(oGemmQBias),
   "ridgefill_gemm_nt_q followed by the row-broadcast bias add, in one pass: y = bf16(bf16(gemm) + bias), "
-  "equal bit for bit to the two ops in sequence. Optional acc i32 [M, N, K/group]: every block's int32 sum." },
+  "equal bit for bit to the two ops in sequence. Optional acc i32 [M, N, K/group]: every block's int32 sum. "
+  "Optional max_ctas: use at most that many SMs (a caller running another stream's kernels beside it)." },
 { "ridgefill_quant_act_i8g", RF_ARR(pQuant), RF_ARR(oQuant),
   "Activation codes for the int8 projector: per `group` columns of each row of x bf16 [M, n], "
   "s = absmax / 127 (1 for an all-zero group) in f32, q = round-half-even(x / s) clamped to +-127." },

@@ -616,7 +616,10 @@ int launch_pairs(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUten
         if (cudaOccupancyMaxActiveClusters(&n, gemm_q_kernel<kMode>, &cfg) != cudaSuccess || n <= 0) return RAD_E_DEVICE;
         max_pairs[kMode] = n;
     }
-    const int pairs = p.tiles < max_pairs[kMode] ? p.tiles : max_pairs[kMode];
+    int pairs = p.tiles < max_pairs[kMode] ? p.tiles : max_pairs[kMode];
+    if constexpr (kMode != kModeBf16) {
+        if (p.g.max_ctas > 0 && p.g.max_ctas / 2 < pairs) pairs = p.g.max_ctas / 2 > 0 ? (int)(p.g.max_ctas / 2) : 1;
+    }
     gemm_q_kernel<kMode><<<2 * pairs, kThreads, kSmemBytes, stream>>>(map_a, map_b, map_y, p);
     return rf::launch_status();
 }

@@ -371,6 +371,9 @@ extern "C" int ridgefill_gemm_q_parse(const RadArgs* a, int with_bias, RidgeFill
     g->N = N;
     g->K = K;
     g->group = group;
+    long long max_ctas = 0;   /* optional: a caller sharing the GPU with another stream's kernels bounds the grid */
+    if (rad_args_geti(a, "max_ctas", &max_ctas) && max_ctas < 0) return RAD_E_INVAL;
+    g->max_ctas = max_ctas;
     return RAD_OK;
 }
 

@@ -142,10 +142,13 @@ class Step:
         gdn = self.calls[5]
         self.gdn_scratch = self.lib.scratch_bytes(gdn[1], gdn[2], gdn[3])
         # the argument blocks are built once; a pass only calls the launch hooks
-        self._args = []
-        for name, r, tens, params in self.calls:
-            scratch = None
-            self._args.append((name, r, tens, params))
+        self._args = [(name, r, tens, params) for name, r, tens, params in self.calls]
+        # Beside the fill (run_pipelined) the projector is given the SMs the fill's chain CTAs leave: the fill's
+        # grid is one CTA a SM, min(v heads x sequences, SMs / 4) of them chains, the rest freed by phase 1.
+        sms = self.torch.cuda.get_device_properties(self.torch.cuda.current_device()).multi_processor_count
+        budget = sms - min(hv, sms // 4)
+        self._side_args = [(name, r, tens, params + [P("max_ctas", budget)] if name == "ridgefill_gemm_nt_q_bias" else params)
+                           for name, r, tens, params in self._args]
 
     # kernels a pass launches (the GDN fill is two: the sequence plan, then the fill kernel)
     LAUNCHES_PER_PASS = 10
@@ -166,7 +169,7 @@ class Step:
         torch = self.torch
         fork, join = torch.cuda.Event(), torch.cuda.Event()
         main_ops = [a for a in self._args if a[0] not in self.SIDE_OPS]
-        side_ops = [a for a in self._args if a[0] in self.SIDE_OPS]
+        side_ops = [a for a in self._side_args if a[0] in self.SIDE_OPS]
         for i, (name, r, tens, params) in enumerate(main_ops):
             if i == 2:   # after the mask and the undo: the side stream may start
                 fork.record(main)

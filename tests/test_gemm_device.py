@@ -196,3 +196,23 @@ def test_gemm_refusals(cuda, product_lib):
     bad = list(base)
     bad[0] = H.dev(A2)
     assert H.launch(product_lib, "ridgefill_gemm_nt_q", bad, H.gemm_params(64, 256, 256, 128)) == abi.E_STRIDE
+
+
+def test_sm_budget_changes_nothing_but_the_grid(cuda, product_lib):
+    """max_ctas (the SMs a caller leaves the projector beside another stream's kernels) bounds the grid only: 2, 30
+    and 116 CTAs write the same bits as the whole GPU, for the per-column and the group-128 forms."""
+    torch = cuda
+    rng = np.random.default_rng(77)
+    for M, N, K, group in ((1000, 512, 1024, 1024), (700, 768, 1024, 128)):
+        a, b, sa, sb, bias = _gemm_case(rng, M, N, K, group)
+        want, _ = _run_gemm(product_lib, torch, a, b, sa, sb, bias=bias, group=group)
+        A, B = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+        SA, SB = torch.from_numpy(sa).cuda(), torch.from_numpy(sb).cuda()
+        BI = torch.from_numpy(bias.view(np.int16)).cuda()
+        for ctas in (2, 30, 116):
+            Y = torch.full((M, N), 0x5A5A, dtype=torch.int16, device="cuda")
+            rc = H.launch(product_lib, "ridgefill_gemm_nt_q_bias",
+                          [H.dev(A), H.dev(SA), H.dev(B), H.dev(SB), H.dev(BI, abi.BF16), H.dev(Y, abi.BF16), abi.absent()],
+                          H.gemm_params(M, N, K, group) + [H.pint("max_ctas", ctas)])
+            assert rc == abi.OK
+            assert np.array_equal(Y.cpu().numpy().view(np.uint16), want), (M, N, K, group, ctas)
