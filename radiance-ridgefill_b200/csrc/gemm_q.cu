@@ -29,6 +29,7 @@
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
+#include "mma.cuh"
 #include "sm100.cuh"
 
 namespace {
@@ -559,6 +560,57 @@ __global__ void __launch_bounds__(256) quant_reg_kernel(RidgeFillQuant g) {
     }
 }
 
+/* The same one-pass quantiser with the data in shared memory instead of registers: a warp per (row, group) of
+ * 256 NV columns, the next item's columns copied asynchronously into the warp's other shared-memory slot while
+ * the current one is reduced and coded (its columns read from shared memory twice: the absmax, then the codes),
+ * so two items a warp are in flight with few registers (more warps a SM than the register form allows). The
+ * same arithmetic (quant_chunk8). */
+constexpr int kQStageThreads = 256;
+template <int NV>
+__global__ void __launch_bounds__(kQStageThreads) quant_stage_kernel(RidgeFillQuant g) {
+    extern __shared__ uint4 qstage[];   /* [warp][2][NV * 32] */
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    uint4* slots = qstage + wib * 2 * NV * 32;
+    const int64_t groups = g.K / g.group, work = g.M * groups;
+    const int64_t warps = (int64_t)gridDim.x * (kQStageThreads >> 5);
+    int64_t w = (int64_t)blockIdx.x * (kQStageThreads >> 5) + wib;
+    auto fetch = [&](int64_t item, int slot) {
+        const int64_t m = item / groups, j = item - m * groups;
+        const uint16_t* x = g.x + m * g.ldx + j * g.group;
+#pragma unroll
+        for (int i = 0; i < NV; ++i)
+            rf::cp_async16_zfill(&slots[slot * NV * 32 + lane + 32 * i], x + 8 * (lane + 32 * i), 16u);
+    };
+    if (w < work) fetch(w, 0);
+    rf::cp_async_commit();
+    for (int slot = 0; w < work; w += warps, slot ^= 1) {
+        __syncwarp();   /* every lane is done with the other slot (the item before this one) */
+        if (w + warps < work) fetch(w + warps, slot ^ 1);
+        rf::cp_async_commit();
+        rf::cp_async_wait<1>();   /* this item's copies are in */
+        __syncwarp();
+        const uint4* cur = slots + slot * NV * 32;
+        float amax = 0.0f;
+#pragma unroll 4
+        for (int i = 0; i < NV; ++i) {
+            const uint4 v = cur[lane + 32 * i];
+            const uint32_t vw[4] = { v.x, v.y, v.z, v.w };
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                amax = fmaxf(amax, fmaxf(fabsf(__uint_as_float(vw[e] << 16)), fabsf(__uint_as_float(vw[e] & 0xffff0000u))));
+        }
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const int64_t m = w / groups, j = w - m * groups;
+        const float sc = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 127.0f);
+        if (lane == 0) g.s[m * g.lds + j] = sc;
+        const float inv = __frcp_rn(sc);
+        int8_t* q = g.q + m * g.ldq + j * g.group;
+#pragma unroll 2
+        for (int i = 0; i < NV; ++i) *(uint2*)(q + 8 * (lane + 32 * i)) = quant_chunk8(cur[lane + 32 * i], sc, inv);
+    }
+    rf::cp_async_wait_all();
+}
+
 /* ------------------------------------------------------------------ host side */
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -695,6 +747,24 @@ extern "C" int ridgefill_gemm_nt_bias_device(const RadArgs* a, RadStream s) {
     return rc != RAD_OK ? rc : launch_gemm_bf16(g, rf::as_stream(s));
 }
 
+template <int NV>
+int launch_quant_stage(const RidgeFillQuant& g, RadStream s) {
+    constexpr int smem = (kQStageThreads / 32) * 2 * NV * 32 * 16;
+    static int per_sm = 0;
+    if (!per_sm) {
+        if (smem > 48 * 1024 &&
+            cudaFuncSetAttribute(quant_stage_kernel<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+            return RAD_E_DEVICE;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, quant_stage_kernel<NV>, kQStageThreads, smem) != cudaSuccess ||
+            per_sm <= 0)
+            return RAD_E_DEVICE;
+    }
+    const int64_t items = g.M * (g.K / g.group);
+    const int64_t blocks = (items + kQStageThreads / 32 - 1) / (kQStageThreads / 32), cap = (int64_t)rf::sm_count() * per_sm;
+    quant_stage_kernel<NV><<<(unsigned)(blocks < cap ? blocks : cap), kQStageThreads, smem, rf::as_stream(s)>>>(g);
+    return rf::launch_status();
+}
+
 extern "C" int ridgefill_quant_act_device(const RadArgs* a, RadStream s) {
     RidgeFillQuant g;
     const int rc = ridgefill_quant_parse(a, &g);
@@ -704,11 +774,11 @@ extern "C" int ridgefill_quant_act_device(const RadArgs* a, RadStream s) {
     const int64_t warps = g.M * (g.K / g.group);
     const int64_t blocks = (warps + 7) / 8, cap = (int64_t)rf::sm_count() * 16;
     const unsigned grid = (unsigned)(blocks < cap ? blocks : cap);
-    switch (g.group) {   /* a group of 256 NV columns in registers */
-        case 256: quant_reg_kernel<1><<<grid, 256, 0, rf::as_stream(s)>>>(g); return rf::launch_status();
-        case 512: quant_reg_kernel<2><<<grid, 256, 0, rf::as_stream(s)>>>(g); return rf::launch_status();
-        case 1024: quant_reg_kernel<4><<<grid, 256, 0, rf::as_stream(s)>>>(g); return rf::launch_status();
-        case 2048: quant_reg_kernel<8><<<grid, 256, 0, rf::as_stream(s)>>>(g); return rf::launch_status();
+    switch (g.group) {   /* a group of 256 NV columns, staged in shared memory */
+        case 256: return launch_quant_stage<1>(g, s);
+        case 512: return launch_quant_stage<2>(g, s);
+        case 1024: return launch_quant_stage<4>(g, s);
+        case 2048: return launch_quant_stage<8>(g, s);
         case 4096: quant_reg_kernel<16><<<grid, 256, 0, rf::as_stream(s)>>>(g); return rf::launch_status();
         default: break;
     }
