@@ -22,7 +22,10 @@ def _quant_inputs(rng, M, K):
 
 @pytest.mark.parametrize("M,K,group", [(1, 256, 128), (37, 2048, 128), (300, 2048, 2048), (64, 10240, 128), (5, 10240, 10240),
                                        (7, 4096, 512), (3, 2048, 8), (9, 6144, 1024), (2, 2048, 32), (4, 4096, 4096),
-                                       (6, 1024, 256)])
+                                       (6, 1024, 256),
+                                       # more (row, group) items than warps: each warp codes one item while the next
+                                       # one's columns are copied into its other shared-memory slot
+                                       (20000, 2048, 2048), (9000, 4096, 512), (3000, 2048, 256)])
 def test_quantiser_matches_oracle(cuda, product_lib, M, K, group):
     torch = cuda
     rng = np.random.default_rng(M + K)
