@@ -611,6 +611,7 @@ extern "C" int ridgefill_folder_check(const RidgeFillFolder* f, const RidgeFillM
 
 struct RidgeFillResident {
     void* block = nullptr;
+    int device = 0;   /* the device the block was allocated on */
     int64_t bytes = 0;
     int64_t n_embd = 0, wide = 0, split = 0, n_layer = 0, heads = 0, sd0 = 0, sd1 = 0, n_vocab = 0;
     bool int8 = false;
@@ -619,7 +620,11 @@ struct RidgeFillResident {
     int64_t final_w_at = -1, final_b_at = -1;
 
     ~RidgeFillResident() {
-        if (block) cudaFree(block);
+        if (!block) return;
+        int cur = 0;
+        const bool switched = cudaGetDevice(&cur) == cudaSuccess && cur != device && cudaSetDevice(device) == cudaSuccess;
+        cudaFree(block);
+        if (switched) cudaSetDevice(cur);
     }
 
     void* at(int64_t off) const { return (char*)block + off; }
@@ -750,7 +755,7 @@ extern "C" int ridgefill_folder_upload(const RidgeFillFolder* f, const RidgeFill
         *out = r.release();
         return RAD_OK;
     }
-    if (cudaMalloc(&r->block, (size_t)r->bytes) != cudaSuccess) {
+    if (cudaGetDevice(&r->device) != cudaSuccess || cudaMalloc(&r->block, (size_t)r->bytes) != cudaSuccess) {
         cudaGetLastError();
         r->block = nullptr;
         say(why, nw, "could not allocate %.1f MiB of device memory for the folder", (double)r->bytes / (1 << 20));
