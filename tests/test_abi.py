@@ -55,12 +55,13 @@ def described_params(op):
 def test_exports_every_declared_entry_point(product_lib):
     lib = product_lib.lib
     names = set()
-    for header in ("ridgefill.h", "rad_plugin.h"):
+    for header in ("ridgefill.h", "rad_plugin.h", "ridgefill_folder.h"):
         text = (H.ROOT / "include" / header).read_text()
         block = text[text.find('extern "C" {'):]
         names |= set(re.findall(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b(\w+)\s*\(", block, re.M))
     names -= {"rad_arg_in", "rad_args_geti", "rad_args_gets", "rad_args_getf_or"}   # header-inline readers
-    assert {"rad_plugin_abi_version", "ridgefill_mask_device", "ridgefill_gdn_fill_device"} <= names
+    assert {"rad_plugin_abi_version", "ridgefill_mask_device", "ridgefill_gdn_fill_device", "ridgefill_attn_kv_fill_device",
+            "ridgefill_folder_open", "ridgefill_folder_upload", "ridgefill_resident_map"} <= names
     missing = [n for n in sorted(names) if not hasattr(lib, n)]
     assert not missing, f"declared but not exported: {missing}"
 
