@@ -331,11 +331,81 @@ def run_mine(args):
         dist.destroy_process_group()
 
 
+def side_op_call(op: str, rows: int):
+    """Operands of a row the pass does not issue, at the served layer's shapes and `rows` rows (synthetic, seeded):
+    ridgefill_gdn_conv_prep (16 q/k and 32 v heads of 128, one sequence with a conv history) and
+    ridgefill_attn_kv_fill (2 kv heads of 256, rope 64 of imrope sections 11/11/10, every row stored). Returns
+    (row, tensors, params, keep) -- `keep` holds the torch buffers for as long as the launches run."""
+    import torch
+    import ridgefill_abi as abi
+    lib = abi.product()
+    g = torch.Generator(device="cuda").manual_seed(1234)
+    t = lambda x, code=None: abi.tensor(code or {torch.float32: abi.F32, torch.bfloat16: abi.BF16,   # noqa: E731
+                                                  torch.int32: abi.I32}[x.dtype], list(x.shape), x.data_ptr(), list(x.stride()))
+    T = rows
+    if op == "ridgefill_gdn_conv_prep":
+        hk, hv = 16, 32
+        C = 2 * hk * 128 + hv * 128
+        keep = dict(x=torch.randn(T, C, device="cuda", generator=g).bfloat16(),
+                    w=(0.5 * torch.randn(C, 4, device="cuda", generator=g)).bfloat16(),
+                    al=torch.randn(hv, device="cuda", generator=g), dt=torch.randn(hv, device="cuda", generator=g),
+                    st=torch.zeros(2, 3, C, device="cuda").bfloat16(), cu=torch.tensor([0, T], dtype=torch.int32, device="cuda"),
+                    ab=torch.randn(T, 2 * hv, device="cuda", generator=g).bfloat16(),
+                    idx=torch.tensor([1], dtype=torch.int32, device="cuda"), ctx=torch.tensor([5], dtype=torch.int32, device="cuda"),
+                    q=torch.empty(T, hk, 128, device="cuda").bfloat16(), k=torch.empty(T, hk, 128, device="cuda").bfloat16(),
+                    v=torch.empty(T, hv, 128, device="cuda").bfloat16(), g=torch.empty(T, hv, device="cuda"),
+                    be=torch.empty(T, hv, device="cuda"))
+        k = keep
+        tens = [t(k["x"]), t(k["w"]), abi.absent(), t(k["al"]), t(k["dt"]), t(k["st"]), t(k["cu"]),
+                abi.tensor(abi.BF16, [T, hv], k["ab"].data_ptr(), [2 * hv, 1]),
+                abi.tensor(abi.BF16, [T, hv], k["ab"].data_ptr() + 2 * hv, [2 * hv, 1]),
+                t(k["idx"]), t(k["ctx"]), t(k["q"]), t(k["k"]), t(k["v"]), t(k["g"]), t(k["be"])]
+        params = [abi.pint("M", T), abi.pint("n_head_k", hk), abi.pint("n_head_v", hv), abi.pint("head_k", 128),
+                  abi.pint("head_v", 128), abi.pint("conv", 4)]
+    elif op == "ridgefill_attn_kv_fill":
+        hkv = 2
+        keep = dict(k=torch.randn(T, hkv, 256, device="cuda", generator=g).bfloat16(),
+                    v=torch.randn(T, hkv, 256, device="cuda", generator=g).bfloat16(),
+                    w=torch.ones(256, device="cuda").bfloat16(),
+                    pos=(torch.arange(3 * T, dtype=torch.int32, device="cuda") % 30000).view(3, T),
+                    slots=torch.randperm(T + 1000, device="cuda", generator=g)[:T].int(),
+                    cache=torch.zeros(2, T + 1000, hkv, 256, device="cuda").bfloat16())
+        k = keep
+        tens = [t(k["k"]), t(k["v"]), t(k["w"]), t(k["pos"]), t(k["slots"]), t(k["cache"]), abi.absent()]
+        params = [abi.pint("M", T), abi.pint("n_head_kv", hkv), abi.pint("head_dim", 256), abi.pint("rope_dim", 64),
+                  abi.pf64("rope_theta", 1e7), abi.pstr("rope_mode", "imrope"), abi.pstr("rope_sections", "11,11,10")]
+    else:
+        return None
+    return lib.find_row(op, abi.DOMAIN_DEVICE), tens, params, keep
+
+
 def run_only(args):
     """Launch one op of the pass repeatedly at --rows rows (after --warmup full passes that fill its
-    inputs): a small, self-contained command for an ncu capture of that op's kernels."""
+    inputs), or one of the rows beside the pass (ridgefill_gdn_conv_prep, ridgefill_attn_kv_fill) on synthetic
+    operands: a small, self-contained command for an ncu capture of that op's kernels."""
     import torch
     import ridgefill_step as RS
+    side = side_op_call(args.only, args.rows)
+    if side is not None:
+        row, tens, params, keep = side
+        import ridgefill_abi as abi
+        lib = abi.product()
+        stream = torch.cuda.Stream()
+        for _ in range(args.warmup):
+            if lib.launch(row, tens, params, stream=stream.cuda_stream) != 0:
+                raise SystemExit(f"{args.only}: refused")
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        stream.synchronize()
+        a.record(stream)
+        for _ in range(args.steps):
+            if lib.launch(row, tens, params, stream=stream.cuda_stream) != 0:
+                raise SystemExit(f"{args.only}: refused")
+        b.record(stream)
+        stream.synchronize()
+        print(json.dumps({"op": args.only, "rows": args.rows, "launches": args.steps,
+                          "ms_per_launch": a.elapsed_time(b) / args.steps}), flush=True)
+        del keep
+        return
     step = RS.Step(RS.StepShape(T=args.rows), device="cuda", seed=1234)
     stream = torch.cuda.Stream()
     calls = [c for c in step._args if c[0] == args.only]
@@ -371,7 +441,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
-    ap.add_argument("--only", default=None, help="profile mode: launch only this op of the pass")
+    ap.add_argument("--only", default=None, help="profile mode: launch only this op of the pass, or ridgefill_gdn_conv_prep / ridgefill_attn_kv_fill on synthetic operands")
     ap.add_argument("--rows", type=int, default=T_FULL, help="rows of the chunk in --only mode")
     args = ap.parse_args()
     if args.only:
