@@ -162,3 +162,83 @@ def test_conv_prep_feeds_the_fill(cuda, product_lib):
             o = H.bf16_bits_to_f32(got_o)
             assert H.rel_l2(o, H.bf16_bits_to_f32(same_o)) <= O_TOL
             assert H.rel_l2(o, H.bf16_bits_to_f32(chain_o)) <= 2e-2
+
+
+def test_block_input_path_from_h(cuda, product_lib):
+    """The DeltaNet block from its input h on the device, every stage a row of this library fed the previous row's
+    device output: activation codes of h (group 128), the int8 mixed projection h -> x [T, 2 Hk 128 + Hv 128] with
+    no bias, the bf16 a|b projection h -> [T, 2 Hv] (a and b read as column views of that one output), conv_prep,
+    and the fill with o. Each stage is checked against the oracle on the same inputs: codes, scales and x bit for
+    bit, a|b within the bf16 GEMM bound, q, k, v within 2 bf16 ulp, g and beta within 1e-5, the state within 1e-3
+    relative L2 and o within 1e-2."""
+    torch = cuda
+    rng = np.random.default_rng(23)
+    T, d, hk, hv = 300, 256, 2, 4
+    C = 2 * hk * 128 + hv * 128
+    h = H.f32_to_bf16_bits(rng.standard_normal((T, d)).astype(np.float32))
+    codes, wscale = H.oracle_quantise_weight((rng.standard_normal((C, d)) / np.sqrt(d)).astype(np.float32))
+    scale_kn = np.ascontiguousarray(H.bf16_bits_to_f32(wscale).T)
+    w_ab = H.f32_to_bf16_bits((2 * rng.standard_normal((2 * hv, d)) / np.sqrt(d)).astype(np.float32))
+    conv = _case(24, T, hk, hv, bias=False)
+    conv["a_log"] = (0.3 * rng.standard_normal(hv) - 1.0).astype(np.float32)
+    cu, idx, ctx = [0, 170, 300], [2, 0], [4, 0]
+    t16 = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda()   # noqa: E731
+    u16 = lambda t: t.cpu().numpy().view(np.uint16)   # noqa: E731
+
+    Hd = t16(h)
+    Qa = torch.empty((T, d), dtype=torch.int8, device="cuda")
+    Sa = torch.empty((T, d // 128), dtype=torch.float32, device="cuda")
+    assert H.launch(product_lib, "ridgefill_quant_act_i8g", [H.dev(Hd, abi.BF16), H.dev(Qa), H.dev(Sa)],
+                    [H.pint("M", T), H.pint("n", d), H.pint("group", 128), H.pstr("dtype", "bf16")]) == abi.OK
+    q_ref, s_ref = H.oracle_quant(h, 128)
+    assert np.array_equal(Qa.cpu().numpy(), q_ref) and np.array_equal(Sa.cpu().numpy(), s_ref)
+
+    Wc, SW = torch.from_numpy(codes).cuda(), torch.from_numpy(scale_kn).cuda()
+    X = torch.full((T, C), SENT, dtype=torch.int16, device="cuda")
+    assert H.launch(product_lib, "ridgefill_gemm_nt_q_bias", [H.dev(Qa), H.dev(Sa), H.dev(Wc), H.dev(SW), abi.absent(),
+                                                              H.dev(X, abi.BF16), abi.absent()],
+                    H.gemm_params(T, C, d, 128)) == abi.OK
+    x = u16(X)
+    assert np.array_equal(x, H.oracle_gemm(q_ref, s_ref, codes, scale_kn, group=128))
+
+    Wab, Bz = t16(w_ab), torch.zeros(2 * hv, dtype=torch.int16, device="cuda")
+    AB = torch.full((T, 2 * hv), SENT, dtype=torch.int16, device="cuda")
+    assert H.launch(product_lib, "ridgefill_gemm_nt_bias", [H.dev(Hd, abi.BF16), H.dev(Wab, abi.BF16), H.dev(Bz, abi.BF16),
+                                                            abi.absent(), H.dev(AB, abi.BF16)],
+                    [H.pint("M", T), H.pint("N", 2 * hv), H.pint("K", d), H.pstr("dtype", "bf16")]) == abi.OK
+    ab = u16(AB)
+    want_ab, _ = H.oracle_gemm_bias(h, w_ab, np.zeros(2 * hv, np.uint16))
+    xf, yf = H.bf16_bits_to_f32(ab).astype(np.float64), H.bf16_bits_to_f32(want_ab).astype(np.float64)
+    rms = np.sqrt(np.mean(yf ** 2))
+    assert np.all(np.abs(xf - yf) <= 2.0 ** -7 * np.maximum(np.abs(xf), np.abs(yf)) + 2.0 ** -9 * rms)
+
+    Wcv = t16(conv["w"])
+    AL, DT = torch.from_numpy(conv["a_log"]).cuda(), torch.from_numpy(conv["dt_bias"]).cuda()
+    ST = t16(conv["state"])
+    CU, I, CX = (torch.tensor(np.asarray(v_, np.int32)).cuda() for v_ in (cu, idx, ctx))
+    q = torch.full((T, hk, 128), SENT, dtype=torch.int16, device="cuda")
+    k, v = torch.full_like(q, SENT), torch.full((T, hv, 128), SENT, dtype=torch.int16, device="cuda")
+    g = torch.full((T, hv), -7.0, dtype=torch.float32, device="cuda")
+    beta = torch.full_like(g, -7.0)
+    assert H.launch(product_lib, "ridgefill_gdn_conv_prep",
+                    [H.dev(X, abi.BF16), H.dev(Wcv, abi.BF16), abi.absent(), H.dev(AL), H.dev(DT), H.dev(ST, abi.BF16),
+                     H.dev(CU), H.dev(AB[:, :hv], abi.BF16), H.dev(AB[:, hv:], abi.BF16), H.dev(I), H.dev(CX),
+                     H.dev(q, abi.BF16), H.dev(k, abi.BF16), H.dev(v, abi.BF16), H.dev(g), H.dev(beta)],
+                    [H.pint("M", T), H.pint("n_head_k", hk), H.pint("n_head_v", hv), H.pint("head_k", 128),
+                     H.pint("head_v", 128), H.pint("conv", 4)]) == abi.OK
+    d_ = dict(conv, x=x, a=np.ascontiguousarray(ab[:, :hv]), b=np.ascontiguousarray(ab[:, hv:]))
+    _check(d_, (abi.OK, u16(q), u16(k), u16(v), g.cpu().numpy(), beta.cpu().numpy(), u16(ST)), cu, idx, ctx, hk, hv)
+
+    from test_gdn_device import STATE_TOL, O_TOL
+    state0 = (0.1 * rng.standard_normal((3, hv, 128, 128))).astype(np.float32)
+    S = torch.from_numpy(state0.copy()).cuda()
+    O = torch.zeros((T, hv, 128), dtype=torch.int16, device="cuda")
+    assert H.launch(product_lib, "ridgefill_gdn_fill", [H.dev(q, abi.BF16), H.dev(k, abi.BF16), H.dev(v, abi.BF16), H.dev(g),
+                                                        H.dev(beta), H.dev(S), H.dev(I), H.dev(CU), H.dev(O, abi.BF16)],
+                    H.gdn_params(T, hk, hv)) == abi.OK
+    want_s, want_o = H.oracle_gdn(u16(k), u16(v), g.cpu().numpy(), beta.cpu().numpy(), state0, idx, cu, q=u16(q))
+    got_s = S.cpu().numpy()
+    for sl in idx:
+        assert H.rel_l2(got_s[sl], want_s[sl]) <= STATE_TOL
+    assert np.array_equal(got_s[1], state0[1])   # the slot no sequence names
+    assert H.rel_l2(H.bf16_bits_to_f32(u16(O)), H.bf16_bits_to_f32(want_o)) <= O_TOL
