@@ -8,9 +8,10 @@ state undo -> Gated DeltaNet chunk fill (16 q/k heads, 32 v heads, 128 dims, sta
 -> rho -> state apply -> hazard, every op a launch of the library's sm_100a device rows through the C
 ABI. Synthetic inputs with BASELINE's shapes and distributions, seeded; inputs (> 700 MB) exceed the
 126 MB L2, so no flush is needed between steps. The timed passes are issued pipelined (Step.run_pipelined):
-the projector path (codes, projector, select) on a normal-priority stream beside the fill's high-priority
-stream, as a pass over the late layers runs the next layer's projection of the shared h_S beside this layer's
-fill; every op of every pass still runs, and a pass ends when both streams have finished it.
+the projector path (codes, projector) from the top of the pass and select after the mask on a normal-priority
+stream, the rest (mask, undo, fill, rho, apply, hazard) on a high-priority stream, as a pass over the late layers
+runs the next layer's projection of the shared h_S beside this layer's fill; every op of every pass still runs,
+and a pass ends when both streams have finished it.
 
 value   device time of K passes with inputs resident in HBM (CUDA events, max over ranks)
 e2e     the same passes with each step's inputs copied host->device from pinned memory and the results
@@ -180,7 +181,7 @@ def run_mine(args):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     step = RS.Step(RS.StepShape(T=T_FULL), device=str(dev), seed=1234 + rank)
-    # the pass's main stream at high priority; the projector path beside it at normal priority (run_pipelined)
+    # the pass's main stream at high priority; the projector path and select beside it at normal priority (run_pipelined)
     stream = torch.cuda.Stream(device=dev, priority=-1)
     side = torch.cuda.Stream(device=dev, priority=0)
     alg = step.algorithmic()

@@ -14,11 +14,11 @@ arch/ridgefill_layer.h:65-116, arch/qwen4exp_blocks.h:110-182):
 
 Buffers live on one CUDA device (torch tensors: allocation and streams only); every op is a launch of a
 sm_100a device row. `Step.run()` issues one pass on a stream, in the order above; nothing here computes on the
-host. `Step.run_pipelined()` issues the same launches on two streams: the projector path (quantiser, projector,
-select) on a lower-priority side stream after the mask, the rest on the main stream. Every late layer projects
-the same h_S (arch/ridgefill_layer.h:60-63), so in a pass over the late layers the projector path of the next
-layer does not wait for this layer's fill: issued beside it, it runs on the SMs the fill's phase-1 CTAs release
-while the fill's chains finish.
+host. `Step.run_pipelined()` issues the same launches on two streams: the projector path (quantiser, projector) from
+the top of the pass and select once the mask is written, on a lower-priority side stream; the rest on the main
+stream. Every late layer projects the same h_S (arch/ridgefill_layer.h:60-63), so in a pass over the late layers
+the projector path of the next layer does not wait for this layer's fill: issued beside it, it runs on the SMs
+the fill's phase-1 CTAs release while the fill's chains finish.
 """
 from __future__ import annotations
 
@@ -152,6 +152,11 @@ class Step:
 
     # kernels a pass launches (the GDN fill is two: the sequence plan, then the fill kernel)
     LAUNCHES_PER_PASS = 10
+    # the issue order of `calls` (and of run())
+    ORDER = ("ridgefill_mask", "ridgefill_quant_act_i8g", "ridgefill_gemm_nt_q_bias", "ridgefill_select",
+             "ridgefill_state_correct", "ridgefill_gdn_fill", "ridgefill_rho_update", "ridgefill_state_correct",
+             "ridgefill_hazard")
+    # ops run_pipelined issues on the side stream
     SIDE_OPS = ("ridgefill_quant_act_i8g", "ridgefill_gemm_nt_q_bias", "ridgefill_select")
 
     def _launch(self, name, r, tens, params, stream: int) -> None:
@@ -162,27 +167,36 @@ class Step:
             raise RuntimeError(f"{name}: device row refused or failed (rc {rc})")
 
     def run_pipelined(self, main, side, events=None) -> None:
-        """Issue one pass on two torch streams: the mask and the undo on `main`, then the projector path on
-        `side` (a stream of lower priority, made to wait for the undo) while `main` runs the fill, rho, the
-        apply and the hazard record; `main` then waits for `side`, so the pass is complete when `main` is.
-        `events` (optional) maps an op on `main` to a pair of CUDA events recorded around its launch."""
+        """Issue one pass on two torch streams. On `side` (a stream of lower priority): from the top of the pass
+        the projector path (codes, projector), which reads only the pass's inputs, then, once the mask is
+        written, select. The rest runs on `main` in the pass's order (mask, undo, the fill, rho, apply, the
+        hazard record), and `main` then waits for `side`, so the pass is complete when `main` is. Every buffer one
+        stream writes is read or written by the other only across these waits. `events` (optional) maps an op on
+        `main` to a pair of CUDA events recorded around its launch."""
         torch = self.torch
-        fork, join = torch.cuda.Event(), torch.cuda.Event()
-        main_ops = [a for a in self._args if a[0] not in self.SIDE_OPS]
-        side_ops = [a for a in self._side_args if a[0] in self.SIDE_OPS]
-        for i, (name, r, tens, params) in enumerate(main_ops):
-            if i == 2:   # after the mask and the undo: the side stream may start
-                fork.record(main)
-                side.wait_event(fork)
-                for a in side_ops:
-                    self._launch(*a, side.cuda_stream)
-                join.record(side)
-            ev = events.get(name) if events else None
+        a, sa = self._args, self._side_args
+        assert tuple(op[0] for op in a) == self.ORDER
+        fork, masked, join = torch.cuda.Event(), torch.cuda.Event(), torch.cuda.Event()
+
+        def on_main(op):
+            ev = events.get(op[0]) if events else None
             if ev:
                 ev[0].record(main)
-            self._launch(name, r, tens, params, main.cuda_stream)
+            self._launch(*op, main.cuda_stream)
             if ev:
                 ev[1].record(main)
+
+        fork.record(main)                    # after the previous pass, whole
+        side.wait_event(fork)
+        for op in (sa[1], sa[2]):            # codes, projector
+            self._launch(*op, side.cuda_stream)
+        on_main(a[0])                        # mask
+        masked.record(main)
+        side.wait_event(masked)
+        self._launch(*sa[3], side.cuda_stream)   # select
+        join.record(side)
+        for op in a[4:]:                     # undo, fill, rho, apply, hazard
+            on_main(op)
         main.wait_event(join)
 
     def run(self, stream: int, events=None) -> None:
