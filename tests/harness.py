@@ -4,8 +4,8 @@ the reference: seeded splitmix64 draws, host buffers that cover padded strides, 
 outputs, and a device runner that copies every buffer to the GPU, launches the device row on a
 stream, and copies every buffer back.
 
-The checker is oracle/_build/libridgefill_oracle.so (the CPU restatement) and, when it was built here
-from the reference sources, oracle/_ref/ridgefill_ref.so (the reference's own host rows).
+The expected values come from the oracle, oracle/_build/libridgefill_oracle.so (the CPU restatement), and,
+when it was built from the reference sources, oracle/_ref/ridgefill_ref.so (the reference's own host rows).
 """
 from __future__ import annotations
 
