@@ -40,6 +40,8 @@ sys.path.insert(0, str(ROOT / "radiance-ridgefill_b200"))
 sys.path.insert(0, str(ROOT / "oracle"))
 
 METRIC = "prefill tokens/s at 32K (RidgeFill step)"
+WORKLOAD = ("RidgeFill approximate pass over a 32,768-row prefill chunk: projector d 2,048 (int8, per-column scales), "
+            "Gated DeltaNet fill 16 qk / 32 v heads x 128, class mask share 0.30")
 T_FULL = 32768
 CPU_SAMPLE_ROWS = 2048
 
@@ -162,8 +164,8 @@ def run_reference(args):
             "warmup": args.warmup, "ms_per_step": base["sec_per_pass"] * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "i8/bf16/f32", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": f"RidgeFill approximate pass, {CPU_SAMPLE_ROWS}-row sample of the 32K chunk, host CPU",
-                       "rows": CPU_SAMPLE_ROWS, "d": 2048, "delta_heads": "16 qk / 32 v x 128"},
+            "config": {"workload": WORKLOAD, "rows": T_FULL, "d": 2048,
+                       "parallelism": "host cores of rank 0 (each step a bounded sample: cpu_baseline.sample)"},
             "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -314,10 +316,7 @@ def run_mine(args):
         line = {"metric": METRIC, "value": world * T_FULL / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "i8/bf16/f32", "data": "synthetic",
-                "config": {"workload": "RidgeFill approximate pass over a 32,768-row prefill chunk: projector d 2,048 "
-                                       "(int8, per-column scales), Gated DeltaNet fill 16 qk / 32 v heads x 128, "
-                                       "class mask share 0.30",
-                           "rows": T_FULL, "d": 2048, "l2": "inputs larger than L2 (no flush)",
+                "config": {"workload": WORKLOAD, "rows": T_FULL, "d": 2048, "l2": "inputs larger than L2 (no flush)",
                            "parallelism": f"independent prompts x{world}",
                            "streams": "projector path beside the fill (two streams, pipelined pass)"},
                 "gpu_launches": Step_launches(step) * args.steps,
