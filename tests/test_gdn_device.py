@@ -188,3 +188,27 @@ def test_waits_give_up_and_the_context_survives(cuda, product_lib):
     assert rc == abi.OK
     want, _ = H.oracle_gdn(k, v, g, beta, state, [1], [0, 300])
     assert H.rel_l2(got[1], want[1]) <= STATE_TOL
+
+
+def test_fill_state_is_affine_in_its_start(cuda, product_lib):
+    """The segment composition on the device, in one varlen call of three sequences: rows [0, m) from S_0, rows
+    [m, n) from zero, and rows [m, n) again with v = 0 from the identity (its end state is the segment's transition
+    M). S_mid M + S_2 equals the one-sequence call's end state, and the f64 rule's, within 3e-3 relative L2 (three
+    fills' 1e-3 bounds composed)."""
+    torch = cuda
+    n, m, hk, hv = 300, 131, 2, 4
+    _, k, v, g, beta, state = H.gdn_inputs(41, n, hk, hv, decay="very slow", slots=1)
+    rows = np.r_[0:n, m:n]
+    v3 = v[rows].copy()
+    v3[n:] = 0
+    st3 = np.zeros((3, hv, 128, 128), np.float32)
+    st3[0] = state[0]
+    st3[2] = np.eye(128, dtype=np.float32)
+    rc, got3, _ = run_fill(product_lib, torch, k[rows], v3, g[rows], beta[rows], st3, [0, 1, 2], [0, m, n, 2 * n - m], hk, hv)
+    assert rc == abi.OK
+    composed = np.einsum("hij,hjk->hik", got3[0].astype(np.float64), got3[2].astype(np.float64)) + got3[1]
+    rc, full, _ = run_fill(product_lib, torch, k, v, g, beta, state, [0], [0, n], hk, hv)
+    assert rc == abi.OK
+    want, _ = H.oracle_gdn(k, v, g, beta, state, [0], [0, n])
+    assert H.rel_l2(composed, full[0]) <= 3e-3
+    assert H.rel_l2(composed, want[0]) <= 3e-3
