@@ -220,27 +220,33 @@ typedef struct RidgeFillHazard {
     float*         count;
 } RidgeFillHazard;
 
-/* The branch hazard rule on the step's last sequence (kernels/ridgefill.h:232-249): tail positions
- * that came from the prefix cache at or below the slot's last approximated position are counted
- * once; an approximate pass then records its last bulk position. */
+/* The branch hazard rule on the step's last sequence (the reference's rule, kernels/ridgefill.h:232-249).
+ * The slot's record holds rec[0] = one past the last position an approximate pass covered and rec[1] = how
+ * far hazards have been counted. The sequence's exact tail spans `span` positions, of which the q rows of
+ * this pass are the last: the `span - q` before them, positions [first - (span - q), first), came from the
+ * prefix cache. Those of them below rec[0] and not yet counted (at or above rec[1]) were approximated by
+ * whoever wrote the cached state: they are added to the count once, and rec[1] moves past them. Then a pass
+ * with bulk rows records its last bulk position + 1 in rec[0]. */
 RIDGEFILL_HD void ridgefill_hazard_step(const RidgeFillHazard* g) {
     const int32_t slot = g->meta_idx[0];
     if (slot < 0 || slot >= g->meta_states) return;
-    float* m = g->meta + slot * g->meta_slot;
-    const int64_t s = g->cu_last[0], e = g->cu_last[1];
-    if (g->span > 0 && e > s) {
-        const int64_t p0 = g->positions[s * g->pos_stride];
-        const int64_t before = g->span - (e - s);
-        const int64_t counted = (int64_t)m[1], last = (int64_t)m[0];
-        const int64_t lo = p0 - before > counted ? p0 - before : counted;
-        const int64_t hi = p0 < last ? p0 : last;
-        if (before > 0 && hi > lo) {
-            g->count[0] += (float)(hi - lo);
-            m[1] = (float)hi;
+    float* rec = g->meta + slot * g->meta_slot;
+    const int64_t q = (int64_t)g->cu_last[1] - (int64_t)g->cu_last[0];
+    const int64_t cached = g->span - q;
+    if (g->span > 0 && q > 0 && cached > 0) {
+        const int64_t first = g->positions[(int64_t)g->cu_last[0] * g->pos_stride];
+        const int64_t covered = (int64_t)rec[0], counted = (int64_t)rec[1];
+        const int64_t from = counted > first - cached ? counted : first - cached;   /* window start, past the counted */
+        const int64_t to = covered < first ? covered : first;                       /* window end, within the covered */
+        if (to > from) {
+            g->count[0] += (float)(to - from);
+            rec[1] = (float)to;
         }
     }
-    if (g->bounds && g->bounds[1] > g->bounds[0])
-        m[0] = (float)(g->positions[(int64_t)(g->bounds[1] - 1) * g->pos_stride] + 1);
+    if (g->bounds && g->bounds[0] < g->bounds[1]) {
+        const int64_t last_bulk = (int64_t)g->bounds[1] - 1;
+        rec[0] = (float)(g->positions[last_bulk * g->pos_stride] + 1);
+    }
 }
 
 /* One ridgefill_select (source, destination) pair in bytes; `word` is 16, 4 or 1 (the widest unit every

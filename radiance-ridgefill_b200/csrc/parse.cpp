@@ -1,219 +1,331 @@
 /* parse.cpp -- operand checks for every row of the B200 RidgeFill library: a RadArgs reduced to one of
  * the parsed structs of ridgefill.h, or a named refusal.
  *
- * The reference ops refuse exactly what the reference parse refuses, with the same code
- * (kernels/host_ref.cpp:16-282, 435-463); the new ops follow the same conventions. Nothing here
- * reads an operand's VALUES (they are device memory on a device row): values such as cu_last are
- * checked where the kernel reads them, with the reference's fail-safe.
+ * Each parse is written as the list of what its operands and parameters must be, in the order in which
+ * their refusals take precedence, on a `Gate` (below): the first requirement that fails fixes the code,
+ * and every later one is skipped. After the gate, an op's shape relations (one predicate) and then the
+ * parsed struct's fields. The reference ops refuse what the reference plugin refuses, with the same code
+ * and the same code winning when an operand set breaks several rules (kernels/host_ref.cpp:16-282,
+ * 435-463; the new ops follow the same conventions). Nothing here reads an operand's VALUES (they are
+ * device memory on a device row): values such as cu_last are checked where the kernel reads them, with
+ * the reference's fail-safe.
  */
 #include "ridgefill.h"
 
 #include <cmath>
 #include <cstring>
+#include <initializer_list>
+#include <type_traits>
 
 namespace {
 
-bool dense(const RadTensor* t) { return rad_tensor_is_contiguous(t) != 0; }
+bool packed(const RadTensor* t) { return rad_tensor_is_contiguous(t) != 0; }
 
-int64_t per_slot_head(const RadTensor* t) {   /* extent of axes 2.. */
-    int64_t n = 1;
-    for (uint32_t i = 2; i < t->rank; ++i) n *= t->shape[i];
-    return n;
-}
-
-/* The stride between N and D in an ND pool [.., 1, 2] or [.., 2, 1]; 0 if not such a pair
- * (kernels/host_ref.cpp:27-34). */
-int64_t pair_stride(const RadTensor* t) {
-    if (t->rank < 3 || per_slot_head(t) != 2) return 0;
-    for (uint32_t i = 2; i < t->rank; ++i)
-        if (t->shape[i] == 2) return t->stride[i];
-    return 0;
-}
-
-int index_rows(const RadTensor* t, int64_t* rows, int64_t* pitch) {   /* host_ref.cpp:37-43 */
-    if (t->dtype != RAD_I32) return RAD_E_DTYPE;
-    if (t->rank < 1 || t->rank > 2 || t->stride[t->rank - 1] != 1) return RAD_E_STRIDE;
-    *rows = t->shape[0];
-    *pitch = t->rank == 2 ? t->stride[0] : 1;
-    return RAD_OK;
-}
-
-int optional_bounds(const RadTensor* t, int64_t need, const int32_t** out) {   /* host_ref.cpp:46-54 */
-    *out = nullptr;
-    if (!t) return RAD_OK;
-    if (t->dtype != RAD_I32) return RAD_E_DTYPE;
-    if (!dense(t)) return RAD_E_STRIDE;
-    if (rad_tensor_numel(t) < need) return RAD_E_SHAPE;
-    *out = (const int32_t*)t->data;
-    return RAD_OK;
-}
-
-int which(const char* s, const char* const* names, int n) {
-    for (int i = 0; s && i < n; ++i)
-        if (std::strcmp(s, names[i]) == 0) return i;
+/* The position of `s` in `names`, -1 when it names none (or is null). */
+int name_index(const char* s, const char* const* names, int n) {
+    if (!s) return -1;
+    for (int i = 0; i < n; ++i)
+        if (!std::strcmp(s, names[i])) return i;
     return -1;
 }
 
-int copy_word(const RidgeFillCopy& p) {   /* host_ref.cpp:226-230 */
-    const uint64_t all = (uint64_t)(uintptr_t)p.src | (uint64_t)(uintptr_t)p.dst | (uint64_t)p.src_pitch |
-                         (uint64_t)p.dst_pitch | (uint64_t)p.row_bytes;
-    return all % 16 == 0 ? 16 : (all % 4 == 0 ? 4 : 1);
+/* Elements one (slot, head) of a [slots, heads, ...] pool holds: the product of the axes after the second. */
+int64_t cell_elems(const RadTensor* t) {
+    int64_t n = 1;
+    for (uint32_t ax = 2; ax < t->rank; ++ax) n *= t->shape[ax];
+    return n;
 }
 
-int select_pair(const RadTensor* src, const RadTensor* dst, int64_t n, RidgeFillCopy* p) {   /* :234-251 */
-    *p = RidgeFillCopy{};
-    if (!src && !dst) return RAD_OK;
-    if (!src || !dst) return RAD_E_INVAL;
-    const int bits = rad_dtype_bits(src->dtype);
-    if (dst->dtype != src->dtype || bits <= 0 || bits % 8 != 0) return RAD_E_DTYPE;
-    if (src->rank != 2 || dst->rank != 2 || src->shape[1] != dst->shape[1] || src->shape[0] < n || dst->shape[0] < n)
-        return RAD_E_SHAPE;
-    if (src->stride[1] != 1 || dst->stride[1] != 1) return RAD_E_STRIDE;
-    const int64_t bytes = bits / 8;
-    p->src = (const unsigned char*)src->data;
-    p->dst = (unsigned char*)dst->data;
-    p->src_pitch = src->stride[0] * bytes;
-    p->dst_pitch = dst->stride[0] * bytes;
-    p->row_bytes = src->shape[1] * bytes;
-    p->word = copy_word(*p);
+/* An N|D pair pool [slots, heads, 1, 2] or [slots, heads, 2, 1]: the element distance from N to D, which
+ * is the stride of the cell's axis of extent 2; 0 when the cell is not such a pair. */
+int64_t pair_gap(const RadTensor* t) {
+    if (t->rank < 3 || cell_elems(t) != 2) return 0;
+    for (uint32_t ax = 2; ax < t->rank; ++ax)
+        if (t->shape[ax] == 2) return t->stride[ax];
+    return 0;
+}
+
+/* A slot index operand, [n_seq] or [n_seq, pitch]: the sequence count and the row pitch. */
+struct SlotRows {
+    int64_t rows = 0, pitch = 0;
+};
+
+/* The refusal of one parse. Every requirement is a no-op once one has failed, so a parse is a chain of
+ * requirements; conditions that look inside an operand are callables, evaluated only while the operands
+ * they read are known to be given. */
+class Gate {
+   public:
+    explicit Gate(const RadArgs* a) : a_(a) {}
+
+    int code() const { return rc_; }
+    bool open() const { return rc_ == RAD_OK; }
+    const RadTensor* at(int pos) const { return rad_arg_in(a_, pos); }
+
+    /* RAD_E_INVAL unless every listed operand is given. */
+    Gate& given(std::initializer_list<int> pos) {
+        for (int p : pos)
+            if (!at(p)) return fail(RAD_E_INVAL);
+        return *this;
+    }
+    /* RAD_E_INVAL unless the two operands are both given or both absent. */
+    Gate& paired(int p, int q) { return (!at(p)) != (!at(q)) ? fail(RAD_E_INVAL) : *this; }
+    /* `code` unless `ok` (a bool, or a callable returning one, called only while the gate is open). */
+    template <class F>
+    Gate& holds(int code, F&& ok) {
+        if (open() && !test(ok)) rc_ = code;
+        return *this;
+    }
+    /* RAD_E_INVAL unless integer parameter `key` is given; its value into *out. */
+    Gate& integer(const char* key, long long* out) {
+        if (open() && !rad_args_geti(a_, key, out)) rc_ = RAD_E_INVAL;
+        return *this;
+    }
+    /* RAD_E_DTYPE unless each listed operand is absent or of type `dt`. */
+    Gate& typed(uint32_t dt, std::initializer_list<int> pos) {
+        for (int p : pos)
+            if (at(p) && at(p)->dtype != dt) return fail(RAD_E_DTYPE);
+        return *this;
+    }
+    /* RAD_E_STRIDE unless each listed operand is absent or packed. */
+    Gate& compact(std::initializer_list<int> pos) {
+        for (int p : pos)
+            if (at(p) && !packed(at(p))) return fail(RAD_E_STRIDE);
+        return *this;
+    }
+    /* A slot index operand: i32 (else RAD_E_DTYPE), rank 1 or 2 with a unit last stride (else
+     * RAD_E_STRIDE). An absent optional index passes. */
+    Gate& slots(int pos, SlotRows* out) {
+        const RadTensor* t = open() ? at(pos) : nullptr;
+        if (!t) return *this;
+        if (t->dtype != RAD_I32) return fail(RAD_E_DTYPE);
+        if (t->rank != 1 && t->rank != 2) return fail(RAD_E_STRIDE);
+        if (t->stride[t->rank - 1] != 1) return fail(RAD_E_STRIDE);
+        out->rows = t->shape[0];
+        out->pitch = t->rank == 1 ? 1 : t->stride[0];
+        return *this;
+    }
+    /* An optional ridgefill_mask `bounds` operand read by another op: absent, or i32 (RAD_E_DTYPE),
+     * packed (RAD_E_STRIDE) and of at least `need` elements (RAD_E_SHAPE). */
+    Gate& limits(int pos, int64_t need, const int32_t** out) {
+        *out = nullptr;
+        const RadTensor* t = open() ? at(pos) : nullptr;
+        if (!t) return *this;
+        if (t->dtype != RAD_I32) return fail(RAD_E_DTYPE);
+        if (!packed(t)) return fail(RAD_E_STRIDE);
+        if (rad_tensor_numel(t) < need) return fail(RAD_E_SHAPE);
+        *out = (const int32_t*)t->data;
+        return *this;
+    }
+
+   private:
+    Gate& fail(int code) {
+        if (open()) rc_ = code;
+        return *this;
+    }
+    template <class F>
+    static bool test(F& f) {
+        if constexpr (std::is_invocable_v<F&>) return f();
+        else return static_cast<bool>(f);
+    }
+
+    const RadArgs* a_;
+    int rc_ = RAD_OK;
+};
+
+/* A state pool [slots, heads, sd0, sd1] at its own strides. */
+struct Pool4 {
+    int64_t slot, head, row, col, slots;
+};
+Pool4 pool4(const RadTensor* t) { return { t->stride[0], t->stride[1], t->stride[2], t->stride[3], t->shape[0] }; }
+
+/* The widest word every address, pitch and row width of a select pair is a multiple of: 16, 4 or 1
+ * bytes (the device row moves a row in such words). */
+int copy_unit(const RidgeFillCopy& c) {
+    const uint64_t bits = (uint64_t)(uintptr_t)c.src | (uint64_t)(uintptr_t)c.dst | (uint64_t)c.src_pitch |
+                          (uint64_t)c.dst_pitch | (uint64_t)c.row_bytes;
+    const uint64_t low = bits & (~bits + 1);   /* the lowest set bit; 0 when every term is 0 */
+    if (low == 0 || low >= 16) return 16;
+    return low >= 4 ? 4 : 1;
+}
+
+/* Select pair k (source `from`, destination `to`): absent together, or one whole-byte dtype, rank 2 with
+ * the same row width and at least n rows each, unit last strides. */
+int select_pair(const RadArgs* a, int from, int to, int64_t n, RidgeFillCopy* c) {
+    *c = RidgeFillCopy{};
+    Gate gate(a);
+    gate.paired(from, to);
+    const RadTensor* s = gate.at(from);
+    const RadTensor* d = gate.at(to);
+    if (!gate.open() || !s) return gate.code();
+    const int bits = rad_dtype_bits(s->dtype);
+    gate.holds(RAD_E_DTYPE, d->dtype == s->dtype && bits > 0 && bits % 8 == 0)
+        .holds(RAD_E_SHAPE, s->rank == 2 && d->rank == 2 && s->shape[1] == d->shape[1] && s->shape[0] >= n &&
+                                d->shape[0] >= n)
+        .holds(RAD_E_STRIDE, [&] { return s->stride[1] == 1 && d->stride[1] == 1; });
+    if (!gate.open()) return gate.code();
+    const int64_t elem = bits / 8;
+    c->src = (const unsigned char*)s->data;
+    c->dst = (unsigned char*)d->data;
+    c->src_pitch = elem * s->stride[0];
+    c->dst_pitch = elem * d->stride[0];
+    c->row_bytes = elem * s->shape[1];
+    c->word = copy_unit(*c);
     return RAD_OK;
 }
 
 }  // namespace
 
-extern "C" int ridgefill_mask_parse(const RadArgs* a, RidgeFillMask* g) {   /* host_ref.cpp:64-104 */
-    const RadTensor* cu = rad_arg_in(a, MK_CU);
-    const RadTensor* tok = rad_arg_in(a, MK_TOKENS);
-    const RadTensor* pos = rad_arg_in(a, MK_POS);
-    const RadTensor* score = rad_arg_in(a, MK_SCORE);
-    const RadTensor* mask = rad_arg_in(a, MK_MASK);
-    const RadTensor* bounds = rad_arg_in(a, MK_BOUNDS);
-    const RadTensor* zeros = rad_arg_in(a, MK_ZEROS);
-    static const char* const modes[] = { "none", "class", "random", "all", "step" };
+/* ridgefill_mask: cu_last, token ids, positions ([b], or [c, b] whose row 0 is the index), the class score
+ * table (needed by the class and random modes only), the mask, its bounds and the optional zeroed rows. */
+extern "C" int ridgefill_mask_parse(const RadArgs* a, RidgeFillMask* g) {
+    static const char* const kModes[] = { "none", "class", "random", "all", "step" };
     *g = RidgeFillMask{};
-    g->mode = which(rad_args_gets(a, "mode"), modes, 5);
+    g->mode = name_index(rad_args_gets(a, "mode"), kModes, 5);
     g->share = rad_args_getf_or(a, "share", NAN);
-    long long seed = 0;
     const bool ranked = g->mode == RIDGEFILL_MODE_CLASS || g->mode == RIDGEFILL_MODE_RANDOM;
-    if (!cu || !tok || !pos || !mask || !bounds || (ranked && !score) || g->mode < 0 ||
-        !rad_args_geti(a, "seed", &seed) || !(g->share >= 0.0 && g->share <= 1.0))
-        return RAD_E_INVAL;
-    if (cu->dtype != RAD_I32 || tok->dtype != RAD_I32 || pos->dtype != RAD_I32 || mask->dtype != RAD_I32 ||
-        bounds->dtype != RAD_I32 || (score && score->dtype != RAD_F32) || (zeros && zeros->dtype != RAD_I32))
-        return RAD_E_DTYPE;
-    if (!dense(cu) || !dense(tok) || !dense(mask) || !dense(bounds) || (score && !dense(score)) ||
-        (zeros && !dense(zeros)))
-        return RAD_E_STRIDE;
-    g->b = rad_tensor_numel(tok);
-    if (pos->rank < 1 || pos->rank > 2 || pos->shape[pos->rank - 1] < g->b || rad_tensor_numel(cu) < 2 ||
-        rad_tensor_numel(bounds) < 4)
-        return RAD_E_SHAPE;
-    g->cu_last = (const int32_t*)cu->data;
-    g->tokens = (const int32_t*)tok->data;
+    long long seed = 0;
+    Gate gate(a);
+    gate.given({ MK_CU, MK_TOKENS, MK_POS, MK_MASK, MK_BOUNDS })
+        .holds(RAD_E_INVAL, !ranked || gate.at(MK_SCORE))
+        .holds(RAD_E_INVAL, g->mode >= 0)
+        .integer("seed", &seed)
+        .holds(RAD_E_INVAL, g->share >= 0.0 && g->share <= 1.0)
+        .typed(RAD_I32, { MK_CU, MK_TOKENS, MK_POS, MK_MASK, MK_BOUNDS })
+        .typed(RAD_F32, { MK_SCORE })
+        .typed(RAD_I32, { MK_ZEROS })
+        .compact({ MK_CU, MK_TOKENS, MK_MASK, MK_BOUNDS, MK_SCORE, MK_ZEROS });
+    if (!gate.open()) return gate.code();
+    const RadTensor* pos = gate.at(MK_POS);
+    const RadTensor* score = gate.at(MK_SCORE);
+    const RadTensor* zeros = gate.at(MK_ZEROS);
+    const int64_t b = rad_tensor_numel(gate.at(MK_TOKENS));
+    const bool fits = (pos->rank == 1 || pos->rank == 2) && pos->shape[pos->rank - 1] >= b &&
+                      rad_tensor_numel(gate.at(MK_CU)) >= 2 && rad_tensor_numel(gate.at(MK_BOUNDS)) >= 4;
+    if (!fits) return RAD_E_SHAPE;
+    g->cu_last = (const int32_t*)gate.at(MK_CU)->data;
+    g->tokens = (const int32_t*)gate.at(MK_TOKENS)->data;
+    g->b = b;
     g->positions = (const int32_t*)pos->data;
     g->pos_stride = pos->stride[pos->rank - 1];
-    g->score = score ? (const float*)score->data : nullptr;
-    g->vocab = score ? rad_tensor_numel(score) : 0;
-    g->mask = (int32_t*)mask->data;
-    g->n = rad_tensor_numel(mask);
-    g->bounds = (int32_t*)bounds->data;
-    g->zeros = zeros ? (int32_t*)zeros->data : nullptr;
-    g->n_zeros = zeros ? rad_tensor_numel(zeros) : 0;
+    if (score) {
+        g->score = (const float*)score->data;
+        g->vocab = rad_tensor_numel(score);
+    }
+    g->mask = (int32_t*)gate.at(MK_MASK)->data;
+    g->n = rad_tensor_numel(gate.at(MK_MASK));
+    g->bounds = (int32_t*)gate.at(MK_BOUNDS)->data;
+    if (zeros) {
+        g->zeros = (int32_t*)zeros->data;
+        g->n_zeros = rad_tensor_numel(zeros);
+    }
     g->seed = seed;
     return RAD_OK;
 }
 
-extern "C" int ridgefill_rho_parse(const RadArgs* a, RidgeFillRho* g) {   /* host_ref.cpp:106-145 */
-    const RadTensor* av = rad_arg_in(a, RH_A);
-    const RadTensor* mask = rad_arg_in(a, RH_MASK);
-    const RadTensor* alog = rad_arg_in(a, RH_ALOG);
-    const RadTensor* dtb = rad_arg_in(a, RH_DTBIAS);
-    const RadTensor* nd = rad_arg_in(a, RH_ND);
-    const RadTensor* sidx = rad_arg_in(a, RH_SIDX);
+/* ridgefill_rho_update: a [n, heads] at any strides (bf16 or f32), the mask, A_log and dt_bias per head, the
+ * N|D pair pool, one sequence's slot index, optional bounds. */
+extern "C" int ridgefill_rho_parse(const RadArgs* a, RidgeFillRho* g) {
     *g = RidgeFillRho{};
-    if (!av || !mask || !alog || !dtb || !nd || !sidx) return RAD_E_INVAL;
-    if ((av->dtype != RAD_BF16 && av->dtype != RAD_F32) || mask->dtype != RAD_I32 || alog->dtype != RAD_F32 ||
-        dtb->dtype != RAD_F32 || nd->dtype != RAD_F32)
-        return RAD_E_DTYPE;
-    int64_t n_seq = 0, pitch = 0;
-    int rc = index_rows(sidx, &n_seq, &pitch);
-    if (rc == RAD_OK) rc = optional_bounds(rad_arg_in(a, RH_BOUNDS), 1, &g->bounds);
-    if (rc != RAD_OK) return rc;
-    if (av->rank != 2 || !dense(mask) || !dense(alog) || !dense(dtb)) return RAD_E_STRIDE;
+    SlotRows idx;
     long long heads = 0;
-    if (!rad_args_geti(a, "n_head", &heads)) return RAD_E_INVAL;
-    g->n = av->shape[0];
-    g->n_head = av->shape[1];
-    g->nd_inner = pair_stride(nd);
-    if (heads != g->n_head || rad_tensor_numel(mask) < g->n || rad_tensor_numel(alog) != heads ||
-        rad_tensor_numel(dtb) != heads || nd->shape[1] != heads || g->nd_inner == 0 || n_seq != 1)
-        return RAD_E_SHAPE;
+    Gate gate(a);
+    gate.given({ RH_A, RH_MASK, RH_ALOG, RH_DTBIAS, RH_ND, RH_SIDX })
+        .holds(RAD_E_DTYPE, [&] { return gate.at(RH_A)->dtype == RAD_BF16 || gate.at(RH_A)->dtype == RAD_F32; })
+        .typed(RAD_I32, { RH_MASK })
+        .typed(RAD_F32, { RH_ALOG, RH_DTBIAS, RH_ND })
+        .slots(RH_SIDX, &idx)
+        .limits(RH_BOUNDS, 1, &g->bounds)
+        .holds(RAD_E_STRIDE, [&] { return gate.at(RH_A)->rank == 2; })
+        .compact({ RH_MASK, RH_ALOG, RH_DTBIAS })
+        .integer("n_head", &heads);
+    if (!gate.open()) return gate.code();
+    const RadTensor* av = gate.at(RH_A);
+    const RadTensor* nd = gate.at(RH_ND);
+    const int64_t gap = pair_gap(nd);
+    const bool fits = av->shape[1] == heads && rad_tensor_numel(gate.at(RH_MASK)) >= av->shape[0] &&
+                      rad_tensor_numel(gate.at(RH_ALOG)) == heads && rad_tensor_numel(gate.at(RH_DTBIAS)) == heads &&
+                      nd->shape[1] == heads && gap != 0 && idx.rows == 1;   /* one sequence a call */
+    if (!fits) return RAD_E_SHAPE;
     g->a = av->data;
     g->a_pitch = av->stride[0];
     g->a_col = av->stride[1];
     g->a_bf16 = av->dtype == RAD_BF16;
-    g->mask = (const int32_t*)mask->data;
-    g->a_log = (const float*)alog->data;
-    g->dt_bias = (const float*)dtb->data;
+    g->mask = (const int32_t*)gate.at(RH_MASK)->data;
+    g->a_log = (const float*)gate.at(RH_ALOG)->data;
+    g->dt_bias = (const float*)gate.at(RH_DTBIAS)->data;
     g->nd = (float*)nd->data;
     g->nd_slot = nd->stride[0];
     g->nd_head = nd->stride[1];
+    g->nd_inner = gap;
     g->n_states = nd->shape[0];
-    g->state_idx = (const int32_t*)sidx->data;
+    g->state_idx = (const int32_t*)gate.at(RH_SIDX)->data;
+    g->n = av->shape[0];
+    g->n_head = av->shape[1];
     return RAD_OK;
 }
 
-extern "C" int ridgefill_correct_parse(const RadArgs* a, RidgeFillCorrect* g) {   /* host_ref.cpp:147-197 */
-    const RadTensor* st = rad_arg_in(a, SC_STATE);
-    const RadTensor* sidx = rad_arg_in(a, SC_STATE_IDX);
-    const RadTensor* ap = rad_arg_in(a, SC_APPLIED);
-    const RadTensor* aidx = rad_arg_in(a, SC_APPLIED_IDX);
-    const RadTensor* c = rad_arg_in(a, SC_C);
-    const RadTensor* nd = rad_arg_in(a, SC_ND);
-    const RadTensor* nidx = rad_arg_in(a, SC_ND_IDX);
+/* ridgefill_state_correct: the state pool [slots, heads, sd0, sd1] at any strides, the applied-scale pool
+ * [slots, heads, 1...], C packed as [heads, sd0, sd1] whatever its rank, the optional N|D pool with its
+ * index, three slot indices of equal rows, optional bounds. */
+extern "C" int ridgefill_correct_parse(const RadArgs* a, RidgeFillCorrect* g) {
+    static const char* const kModes[] = { "undo", "apply" };
     *g = RidgeFillCorrect{};
-    if (!st || !sidx || !ap || !aidx || !c || !nd != !nidx) return RAD_E_INVAL;
-    if (st->dtype != RAD_F32 || ap->dtype != RAD_F32 || c->dtype != RAD_F32 || (nd && nd->dtype != RAD_F32))
-        return RAD_E_DTYPE;
-    static const char* const modes[] = { "undo", "apply" };
     long long heads = 0, sd0 = 0, sd1 = 0;
-    g->apply = which(rad_args_gets(a, "mode"), modes, 2);
+    SlotRows st_rows, ap_rows, nd_rows;
+    g->apply = name_index(rad_args_gets(a, "mode"), kModes, 2);
     const double alpha = rad_args_getf_or(a, "alpha", NAN);
-    if (g->apply < 0 || !rad_args_geti(a, "n_head", &heads) || !rad_args_geti(a, "sd0", &sd0) ||
-        !rad_args_geti(a, "sd1", &sd1) || (g->apply && !std::isfinite(alpha)))
-        return RAD_E_INVAL;
-    int64_t ap_rows = 0, nd_rows = 0;
-    int rc = index_rows(sidx, &g->n_seq, &g->st_pitch);
-    if (rc == RAD_OK) rc = index_rows(aidx, &ap_rows, &g->ap_pitch);
-    if (rc == RAD_OK && nidx) rc = index_rows(nidx, &nd_rows, &g->nd_pitch);
-    if (rc == RAD_OK) rc = optional_bounds(rad_arg_in(a, SC_BOUNDS), 2, &g->bounds);
-    if (rc != RAD_OK) return rc;
-    if (ap_rows != g->n_seq || (nidx && nd_rows != g->n_seq)) return RAD_E_SHAPE;
-    if (st->rank != 4 || st->shape[1] != heads || st->shape[2] != sd0 || st->shape[3] != sd1 || !dense(c) ||
-        rad_tensor_numel(c) != heads * sd0 * sd1 || ap->rank < 2 || ap->shape[1] != heads || per_slot_head(ap) != 1 ||
-        (nd && (nd->shape[1] != heads || pair_stride(nd) == 0)))
-        return RAD_E_SHAPE;
+    Gate gate(a);
+    gate.given({ SC_STATE, SC_STATE_IDX, SC_APPLIED, SC_APPLIED_IDX, SC_C })
+        .paired(SC_ND, SC_ND_IDX)
+        .typed(RAD_F32, { SC_STATE, SC_APPLIED, SC_C, SC_ND })
+        .holds(RAD_E_INVAL, g->apply >= 0)
+        .integer("n_head", &heads)
+        .integer("sd0", &sd0)
+        .integer("sd1", &sd1)
+        .holds(RAD_E_INVAL, g->apply == 0 || std::isfinite(alpha))
+        .slots(SC_STATE_IDX, &st_rows)
+        .slots(SC_APPLIED_IDX, &ap_rows)
+        .slots(SC_ND_IDX, &nd_rows)
+        .limits(SC_BOUNDS, 2, &g->bounds)
+        .holds(RAD_E_SHAPE, [&] { return ap_rows.rows == st_rows.rows && (!gate.at(SC_ND_IDX) || nd_rows.rows == st_rows.rows); });
+    if (!gate.open()) return gate.code();
+    const RadTensor* st = gate.at(SC_STATE);
+    const RadTensor* ap = gate.at(SC_APPLIED);
+    const RadTensor* c = gate.at(SC_C);
+    const RadTensor* nd = gate.at(SC_ND);
+    const bool state_ok = st->rank == 4 && st->shape[1] == heads && st->shape[2] == sd0 && st->shape[3] == sd1;
+    const bool c_ok = packed(c) && rad_tensor_numel(c) == heads * sd0 * sd1;
+    const bool applied_ok = ap->rank >= 2 && ap->shape[1] == heads && cell_elems(ap) == 1;
+    const bool nd_ok = !nd || (nd->shape[1] == heads && pair_gap(nd) != 0);
+    if (!(state_ok && c_ok && applied_ok && nd_ok)) return RAD_E_SHAPE;
+    const Pool4 sp = pool4(st);
     g->state = (float*)st->data;
-    g->st_slot = st->stride[0];
-    g->st_head = st->stride[1];
-    g->st_row = st->stride[2];
-    g->st_col = st->stride[3];
+    g->st_slot = sp.slot;
+    g->st_head = sp.head;
+    g->st_row = sp.row;
+    g->st_col = sp.col;
+    g->st_states = sp.slots;
     g->applied = (float*)ap->data;
     g->ap_slot = ap->stride[0];
     g->ap_head = ap->stride[1];
-    g->c = (const float*)c->data;
-    g->c_head = sd0 * sd1;   /* C is read packed [heads, sd0, sd1] whatever its rank (host_ref.cpp:181-183) */
-    g->c_row = sd1;
-    g->nd = nd ? (const float*)nd->data : nullptr;
-    g->nd_slot = nd ? nd->stride[0] : 0;
-    g->nd_head = nd ? nd->stride[1] : 0;
-    g->nd_inner = nd ? pair_stride(nd) : 0;
-    g->st_idx = (const int32_t*)sidx->data;
-    g->ap_idx = (const int32_t*)aidx->data;
-    g->nd_idx = nidx ? (const int32_t*)nidx->data : nullptr;
-    g->st_states = st->shape[0];
     g->ap_states = ap->shape[0];
-    g->nd_states = nd ? nd->shape[0] : 0;
+    g->c = (const float*)c->data;
+    g->c_head = sd0 * sd1;   /* C is read packed: its element count, not its rank, is the contract */
+    g->c_row = sd1;
+    if (nd) {
+        g->nd = (const float*)nd->data;
+        g->nd_slot = nd->stride[0];
+        g->nd_head = nd->stride[1];
+        g->nd_inner = pair_gap(nd);
+        g->nd_states = nd->shape[0];
+        g->nd_idx = (const int32_t*)gate.at(SC_ND_IDX)->data;
+        g->nd_pitch = nd_rows.pitch;
+    }
+    g->st_idx = (const int32_t*)gate.at(SC_STATE_IDX)->data;
+    g->st_pitch = st_rows.pitch;
+    g->ap_idx = (const int32_t*)gate.at(SC_APPLIED_IDX)->data;
+    g->ap_pitch = ap_rows.pitch;
+    g->n_seq = st_rows.rows;
     g->n_head = heads;
     g->sd0 = sd0;
     g->sd1 = sd1;
@@ -221,96 +333,108 @@ extern "C" int ridgefill_correct_parse(const RadArgs* a, RidgeFillCorrect* g) { 
     return RAD_OK;
 }
 
-extern "C" int ridgefill_state_read_parse(const RadArgs* a, RidgeFillStateRead* g) {   /* host_ref.cpp:199-221 */
-    const RadTensor* st = rad_arg_in(a, SR_STATE);
-    const RadTensor* sidx = rad_arg_in(a, SR_STATE_IDX);
-    const RadTensor* out = rad_arg_in(a, SR_OUT);
-    long long heads = 0, sd0 = 0, sd1 = 0;
+/* ridgefill_state_read: the state pool, a slot index, and a packed f32 output of at least
+ * n_seq * heads * sd0 * sd1 elements, written from its first element. */
+extern "C" int ridgefill_state_read_parse(const RadArgs* a, RidgeFillStateRead* g) {
     *g = RidgeFillStateRead{};
-    if (!st || !sidx || !out || !rad_args_geti(a, "n_head", &heads) || !rad_args_geti(a, "sd0", &sd0) ||
-        !rad_args_geti(a, "sd1", &sd1))
-        return RAD_E_INVAL;
-    if (st->dtype != RAD_F32 || out->dtype != RAD_F32) return RAD_E_DTYPE;
-    const int rc = index_rows(sidx, &g->n_seq, &g->idx_pitch);
-    if (rc != RAD_OK) return rc;
-    if (!dense(out)) return RAD_E_STRIDE;
-    if (st->rank != 4 || st->shape[1] != heads || st->shape[2] != sd0 || st->shape[3] != sd1 ||
-        rad_tensor_numel(out) < g->n_seq * heads * sd0 * sd1)
+    long long heads = 0, sd0 = 0, sd1 = 0;
+    SlotRows rows;
+    Gate gate(a);
+    gate.given({ SR_STATE, SR_STATE_IDX, SR_OUT })
+        .integer("n_head", &heads)
+        .integer("sd0", &sd0)
+        .integer("sd1", &sd1)
+        .typed(RAD_F32, { SR_STATE, SR_OUT })
+        .slots(SR_STATE_IDX, &rows)
+        .compact({ SR_OUT });
+    if (!gate.open()) return gate.code();
+    const RadTensor* st = gate.at(SR_STATE);
+    const RadTensor* out = gate.at(SR_OUT);
+    if (!(st->rank == 4 && st->shape[1] == heads && st->shape[2] == sd0 && st->shape[3] == sd1 &&
+          rad_tensor_numel(out) >= rows.rows * heads * sd0 * sd1))
         return RAD_E_SHAPE;
+    const Pool4 sp = pool4(st);
     g->state = (const float*)st->data;
-    g->st_slot = st->stride[0];
-    g->st_head = st->stride[1];
-    g->st_row = st->stride[2];
-    g->st_col = st->stride[3];
-    g->n_states = st->shape[0];
-    g->idx = (const int32_t*)sidx->data;
+    g->st_slot = sp.slot;
+    g->st_head = sp.head;
+    g->st_row = sp.row;
+    g->st_col = sp.col;
+    g->n_states = sp.slots;
+    g->idx = (const int32_t*)gate.at(SR_STATE_IDX)->data;
+    g->idx_pitch = rows.pitch;
     g->out = (float*)out->data;
+    g->n_seq = rows.rows;
     g->n_head = heads;
     g->sd0 = sd0;
     g->sd1 = sd1;
     return RAD_OK;
 }
 
-extern "C" int ridgefill_select_parse(const RadArgs* a, RidgeFillSelect* g) {   /* host_ref.cpp:253-266 */
-    const RadTensor* mask = rad_arg_in(a, SL_MASK);
+/* ridgefill_select: the mask, then the x pair (required) and the q and s pairs (each optional as a pair). */
+extern "C" int ridgefill_select_parse(const RadArgs* a, RidgeFillSelect* g) {
     *g = RidgeFillSelect{};
-    if (!mask || !rad_arg_in(a, SL_X_SRC) || !rad_arg_in(a, SL_X)) return RAD_E_INVAL;
-    if (mask->dtype != RAD_I32) return RAD_E_DTYPE;
-    if (!dense(mask)) return RAD_E_STRIDE;
-    g->mask = (const int32_t*)mask->data;
-    g->n = rad_tensor_numel(mask);
-    for (int k = 0; k < RIDGEFILL_SELECT_PAIRS; ++k) {
-        const int rc = select_pair(rad_arg_in(a, SL_X_SRC + k), rad_arg_in(a, SL_X + k), g->n, &g->pair[k]);
-        if (rc != RAD_OK) return rc;
-    }
+    Gate gate(a);
+    gate.given({ SL_MASK, SL_X_SRC, SL_X }).typed(RAD_I32, { SL_MASK }).compact({ SL_MASK });
+    if (!gate.open()) return gate.code();
+    g->mask = (const int32_t*)gate.at(SL_MASK)->data;
+    g->n = rad_tensor_numel(gate.at(SL_MASK));
+    for (int k = 0; k < RIDGEFILL_SELECT_PAIRS; ++k)
+        if (const int rc = select_pair(a, SL_X_SRC + k, SL_X + k, g->n, &g->pair[k])) return rc;
     return RAD_OK;
 }
 
-extern "C" int ridgefill_drop_parse(const RadArgs* a, RidgeFillDrop* g) {   /* host_ref.cpp:268-282 */
-    const RadTensor* mask = rad_arg_in(a, DR_MASK);
-    const RadTensor* ids = rad_arg_in(a, DR_IDS);
-    long long top_k = -1;
+/* ridgefill_drop_rows: the mask and the routing ids [>= n, >= top_k] with a unit last stride. */
+extern "C" int ridgefill_drop_parse(const RadArgs* a, RidgeFillDrop* g) {
     *g = RidgeFillDrop{};
-    if (!mask || !ids || !rad_args_geti(a, "top_k", &top_k) || top_k < 0) return RAD_E_INVAL;
-    if (mask->dtype != RAD_I32 || ids->dtype != RAD_I32) return RAD_E_DTYPE;
-    if (!dense(mask) || (ids->rank == 2 && ids->stride[1] != 1)) return RAD_E_STRIDE;
-    g->n = rad_tensor_numel(mask);
-    if (ids->rank != 2 || ids->shape[0] < g->n || ids->shape[1] < top_k) return RAD_E_SHAPE;
-    g->mask = (const int32_t*)mask->data;
+    long long top_k = -1;
+    Gate gate(a);
+    gate.given({ DR_MASK, DR_IDS })
+        .integer("top_k", &top_k)
+        .holds(RAD_E_INVAL, [&] { return top_k >= 0; })
+        .typed(RAD_I32, { DR_MASK, DR_IDS })
+        .compact({ DR_MASK })
+        .holds(RAD_E_STRIDE, [&] { return gate.at(DR_IDS)->rank != 2 || gate.at(DR_IDS)->stride[1] == 1; });
+    if (!gate.open()) return gate.code();
+    const RadTensor* ids = gate.at(DR_IDS);
+    const int64_t n = rad_tensor_numel(gate.at(DR_MASK));
+    if (!(ids->rank == 2 && ids->shape[0] >= n && ids->shape[1] >= top_k)) return RAD_E_SHAPE;
+    g->mask = (const int32_t*)gate.at(DR_MASK)->data;
+    g->n = n;
     g->ids = (int32_t*)ids->data;
     g->pitch = ids->stride[0];
     g->top_k = top_k;
     return RAD_OK;
 }
 
-extern "C" int ridgefill_hazard_parse(const RadArgs* a, RidgeFillHazard* g) {   /* host_ref.cpp:435-463 */
-    const RadTensor* cu = rad_arg_in(a, HZ_CU);
-    const RadTensor* pos = rad_arg_in(a, HZ_POS);
-    const RadTensor* span = rad_arg_in(a, HZ_SPAN);
-    const RadTensor* meta = rad_arg_in(a, HZ_META);
-    const RadTensor* idx = rad_arg_in(a, HZ_META_IDX);
-    const RadTensor* cnt = rad_arg_in(a, HZ_COUNT);
+/* ridgefill_hazard: cu_last, positions ([n] or [c, n]), optional bounds, the optional span (its extent is
+ * all that is read), the meta pool [slots, ..., 2] with a unit last stride, its slot index, the count. */
+extern "C" int ridgefill_hazard_parse(const RadArgs* a, RidgeFillHazard* g) {
     *g = RidgeFillHazard{};
-    if (!cu || !pos || !meta || !idx || !cnt) return RAD_E_INVAL;
-    if (cu->dtype != RAD_I32 || pos->dtype != RAD_I32 || meta->dtype != RAD_F32 || cnt->dtype != RAD_F32)
-        return RAD_E_DTYPE;
-    if (!dense(cu) || !dense(cnt)) return RAD_E_STRIDE;
-    int64_t rows = 0, pitch = 0;
-    int rc = index_rows(idx, &rows, &pitch);
-    if (rc == RAD_OK) rc = optional_bounds(rad_arg_in(a, HZ_BOUNDS), 2, &g->bounds);
-    if (rc != RAD_OK) return rc;
-    if (rows < 1 || rad_tensor_numel(cu) < 2 || rad_tensor_numel(cnt) < 1 || pos->rank < 1 || pos->rank > 2 ||
-        meta->rank < 2 || meta->shape[meta->rank - 1] != 2 || meta->stride[meta->rank - 1] != 1)
-        return RAD_E_SHAPE;
-    g->cu_last = (const int32_t*)cu->data;
+    SlotRows rows;
+    Gate gate(a);
+    gate.given({ HZ_CU, HZ_POS, HZ_META, HZ_META_IDX, HZ_COUNT })
+        .typed(RAD_I32, { HZ_CU, HZ_POS })
+        .typed(RAD_F32, { HZ_META, HZ_COUNT })
+        .compact({ HZ_CU, HZ_COUNT })
+        .slots(HZ_META_IDX, &rows)
+        .limits(HZ_BOUNDS, 2, &g->bounds);
+    if (!gate.open()) return gate.code();
+    const RadTensor* pos = gate.at(HZ_POS);
+    const RadTensor* meta = gate.at(HZ_META);
+    const RadTensor* span = gate.at(HZ_SPAN);
+    const bool fits = rows.rows >= 1 && rad_tensor_numel(gate.at(HZ_CU)) >= 2 && rad_tensor_numel(gate.at(HZ_COUNT)) >= 1 &&
+                      (pos->rank == 1 || pos->rank == 2) && meta->rank >= 2 && meta->shape[meta->rank - 1] == 2 &&
+                      meta->stride[meta->rank - 1] == 1;
+    if (!fits) return RAD_E_SHAPE;
+    g->cu_last = (const int32_t*)gate.at(HZ_CU)->data;
     g->positions = (const int32_t*)pos->data;
     g->pos_stride = pos->stride[pos->rank - 1];
     g->span = span ? rad_tensor_numel(span) : 0;
     g->meta = (float*)meta->data;
     g->meta_slot = meta->stride[0];
     g->meta_states = meta->shape[0];
-    g->meta_idx = (const int32_t*)idx->data;
-    g->count = (float*)cnt->data;
+    g->meta_idx = (const int32_t*)gate.at(HZ_META_IDX)->data;
+    g->count = (float*)gate.at(HZ_COUNT)->data;
     return RAD_OK;
 }
 
@@ -347,10 +471,10 @@ extern "C" int ridgefill_gemm_q_parse(const RadArgs* a, int with_bias, RidgeFill
         rad_tensor_numel(AS) != M * blocks || rad_tensor_numel(BS) != blocks * N || (bias && rad_tensor_numel(bias) != N) ||
         (acc && rad_tensor_numel(acc) != M * N * blocks))
         return RAD_E_SHAPE;
-    if (A->stride[1] != 1 || B->stride[1] != 1 || Y->stride[1] != 1 || !dense(BS) || (bias && !dense(bias)) ||
-        (acc && !dense(acc)))
+    if (A->stride[1] != 1 || B->stride[1] != 1 || Y->stride[1] != 1 || !packed(BS) || (bias && !packed(bias)) ||
+        (acc && !packed(acc)))
         return RAD_E_STRIDE;
-    if (AS->rank == 2 ? (AS->stride[1] != 1) : !dense(AS)) return RAD_E_STRIDE;
+    if (AS->rank == 2 ? (AS->stride[1] != 1) : !packed(AS)) return RAD_E_STRIDE;
     /* TMA: 16-byte aligned bases and row pitches. */
     if (((uintptr_t)A->data | (uintptr_t)B->data) % 16 || A->stride[0] % 16 || B->stride[0] % 16 ||
         ((uintptr_t)Y->data % 16) || (Y->stride[0] * 2) % 16 || (uintptr_t)BS->data % 16 ||
@@ -404,7 +528,7 @@ extern "C" int ridgefill_gemm_bias_parse(const RadArgs* a, RidgeFillGemmBias* g)
     if (A->shape[1] != K || B->shape[0] != N || B->shape[1] != K || Y->shape[0] != M || Y->shape[1] != N ||
         rad_tensor_numel(bias) != N || (R && (R->shape[0] != M || R->shape[1] != N)))
         return RAD_E_SHAPE;
-    if (A->stride[1] != 1 || B->stride[1] != 1 || Y->stride[1] != 1 || !dense(bias) || (R && R->stride[1] != 1))
+    if (A->stride[1] != 1 || B->stride[1] != 1 || Y->stride[1] != 1 || !packed(bias) || (R && R->stride[1] != 1))
         return RAD_E_STRIDE;
     /* TMA tiles of a, b and y, 16-byte vector reads of the bias and the residual. */
     if (((uintptr_t)A->data | (uintptr_t)B->data | (uintptr_t)Y->data | (uintptr_t)bias->data) % 16 ||
@@ -465,10 +589,10 @@ extern "C" int ridgefill_conv_prep_parse(const RadArgs* a, RidgeFillConvPrep* g)
         K->dtype != RAD_BF16 || V->dtype != RAD_BF16 || G->dtype != RAD_F32 || BE->dtype != RAD_F32)
         return RAD_E_DTYPE;
     if (X->rank != 2 || X->shape[0] != T || X->shape[1] != C || X->stride[1] != 1) return X->rank == 2 && X->stride[1] != 1 ? RAD_E_STRIDE : RAD_E_SHAPE;
-    if (W->rank != 2 || W->shape[0] != C || W->shape[1] != 4 || !dense(W)) return RAD_E_SHAPE;
-    if (B0 && (rad_tensor_numel(B0) != C || !dense(B0))) return RAD_E_SHAPE;
+    if (W->rank != 2 || W->shape[0] != C || W->shape[1] != 4 || !packed(W)) return RAD_E_SHAPE;
+    if (B0 && (rad_tensor_numel(B0) != C || !packed(B0))) return RAD_E_SHAPE;
     if (B0 && (uintptr_t)B0->data % 16) return RAD_E_STRIDE;
-    if (rad_tensor_numel(AL) != hv || rad_tensor_numel(DT) != hv || !dense(AL) || !dense(DT)) return RAD_E_SHAPE;
+    if (rad_tensor_numel(AL) != hv || rad_tensor_numel(DT) != hv || !packed(AL) || !packed(DT)) return RAD_E_SHAPE;
     if (ST->rank != 3 || ST->shape[1] != 3 || ST->shape[2] != C || ST->stride[2] != 1 || ST->stride[1] != C) return RAD_E_SHAPE;
     if (CU->rank != 1 || CU->shape[0] < 1 || CU->stride[0] != 1) return RAD_E_SHAPE;
     const int64_t n_seq = CU->shape[0] - 1;
@@ -575,7 +699,7 @@ extern "C" int ridgefill_attn_kv_parse(const RadArgs* a, RidgeFillAttnKv* g) {
     if (!(theta > 1.0) || !std::isfinite(theta) || !(eps >= 0.0) || !std::isfinite(eps)) return RAD_E_INVAL;
     static const char* const modes[] = { "neox", "mrope", "imrope" };
     const char* m = rad_args_gets(a, "rope_mode");
-    const int mode = m ? which(m, modes, 3) : RIDGEFILL_ROPE_NEOX;
+    const int mode = m ? name_index(m, modes, 3) : RIDGEFILL_ROPE_NEOX;
     if (mode < 0) return RAD_E_INVAL;
     int sec[3] = { 0, 0, 0 };
     if (mode != RIDGEFILL_ROPE_NEOX && (!parse_sections(rad_args_gets(a, "rope_sections"), sec) ||
@@ -590,11 +714,11 @@ extern "C" int ridgefill_attn_kv_parse(const RadArgs* a, RidgeFillAttnKv* g) {
     for (const RadTensor* t : rows)
         if (t && (t->rank != 3 || t->shape[0] != T || t->shape[1] != hkv || t->shape[2] != D || t->stride[2] != 1))
             return RAD_E_SHAPE;
-    if (rad_tensor_numel(W) != D || !dense(W)) return RAD_E_SHAPE;
+    if (rad_tensor_numel(W) != D || !packed(W)) return RAD_E_SHAPE;
     if (P->rank == 1 ? (P->shape[0] != T || P->stride[0] != 1)
                      : (P->rank != 2 || P->shape[0] != 3 || P->shape[1] != T || P->stride[1] != 1))
         return RAD_E_SHAPE;
-    if (rad_tensor_numel(S) != T || !dense(S)) return RAD_E_SHAPE;
+    if (rad_tensor_numel(S) != T || !packed(S)) return RAD_E_SHAPE;
     if (C->rank != 4 || C->shape[0] != 2 || C->shape[2] != hkv || C->shape[3] != D || C->stride[3] != 1) return RAD_E_SHAPE;
     /* 16-byte loads and stores: eight elements a lane. */
     uint64_t align = (uint64_t)(uintptr_t)K->data | (uint64_t)(uintptr_t)V->data | (uint64_t)(uintptr_t)C->data |
@@ -687,9 +811,11 @@ extern "C" int ridgefill_gdn_parse(const RadArgs* a, RidgeFillGdn* g) {
     if (Kt->dtype != RAD_BF16 || V->dtype != RAD_BF16 || (Q && Q->dtype != RAD_BF16) || (O && O->dtype != RAD_BF16) ||
         G->dtype != RAD_F32 || Bt->dtype != RAD_F32 || St->dtype != RAD_F32 || Cu->dtype != RAD_I32)
         return RAD_E_DTYPE;
-    int64_t n_seq = 0, pitch = 0;
-    const int rc = index_rows(Si, &n_seq, &pitch);
-    if (rc != RAD_OK) return rc;
+    SlotRows rows;
+    Gate gate(a);
+    gate.slots(GD_STATE_IDX, &rows);
+    if (!gate.open()) return gate.code();
+    const int64_t n_seq = rows.rows, pitch = rows.pitch;
     if (hk <= 0 || hv <= 0 || hv % hk != 0 || dk != 128 || dv != 128 || chunk != 64) return RAD_E_UNSUPPORTED;
     if (Kt->rank != 3 || V->rank != 3 || G->rank != 2 || Bt->rank != 2 || St->rank != 4 ||
         (Q && Q->rank != 3) || (O && O->rank != 3))
@@ -701,7 +827,7 @@ extern "C" int ridgefill_gdn_parse(const RadArgs* a, RidgeFillGdn* g) {
         (Q && (Q->shape[0] != T || Q->shape[1] != hk || Q->shape[2] != dk)) ||
         (O && (O->shape[0] != T || O->shape[1] != hv || O->shape[2] != dv)))
         return RAD_E_SHAPE;
-    if (Kt->stride[2] != 1 || V->stride[2] != 1 || G->stride[1] != 1 || Bt->stride[1] != 1 || !dense(Cu) ||
+    if (Kt->stride[2] != 1 || V->stride[2] != 1 || G->stride[1] != 1 || Bt->stride[1] != 1 || !packed(Cu) ||
         St->stride[3] != 1 || St->stride[2] != dk || (Q && Q->stride[2] != 1) || (O && O->stride[2] != 1))
         return RAD_E_STRIDE;
     /* 16-byte vector loads of k, v, q rows and of the state plane. */
