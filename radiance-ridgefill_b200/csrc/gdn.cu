@@ -84,7 +84,30 @@ struct GdnPlan {
     uint8_t* slots;   /* the chunk slots */
     uint8_t* outws;   /* output form: S0 and U^T per chunk slot and v-head; null for the state-only fill */
     int max_slots;
+    int head_block;   /* phase 1 takes the v-heads in blocks of this many (item_at); the chains the same (chain_at) */
 };
+
+/* Phase 1's item i (of slots x Hv, slots = every sequence's chunks): the v-heads in blocks of head_block, every
+ * chunk slot of one block's heads before the next block's, slot-major inside a block. With head_block = the
+ * number of chain CTAs, block b holds exactly the chains the chain CTAs run b-th (chain_at), so phase 1 makes
+ * the chunks in the order the chains read them, however many heads the launch holds. */
+__device__ __forceinline__ void item_at(const GdnPlan& p, int64_t item, int64_t slots, int64_t* slot, int64_t* h) {
+    const int64_t hb = p.head_block, Hv = p.g.n_head_v;
+    const int64_t blk = item / (slots * hb), j = item - blk * slots * hb;
+    const int64_t nh = min(hb, Hv - blk * hb);
+    *slot = j / nh;
+    *h = blk * hb + j % nh;
+}
+
+/* Chain cid (of Hv x n_seq): the same head blocks; inside a block sequence-major, so chain CTA c (taking
+ * chains c, c + head_block, ...) runs head b * head_block + c of every sequence in turn, block by block. */
+__device__ __forceinline__ void chain_at(const GdnPlan& p, int64_t cid, int64_t* h, int64_t* seq) {
+    const int64_t hb = p.head_block, Hv = p.g.n_head_v, n = p.g.n_seq;
+    const int64_t blk = cid / (hb * n), r = cid - blk * hb * n;
+    const int64_t nh = min(hb, Hv - blk * hb);
+    *seq = r / nh;
+    *h = blk * hb + r % nh;
+}
 
 __device__ __forceinline__ uint8_t* out_ptr(const GdnPlan& p, int64_t slot, int64_t h) {
     return p.outws + (slot * p.g.n_head_v + h) * (int64_t)kOutBytes;
@@ -276,13 +299,14 @@ __device__ void tri_offdiag_block(PrepSmem& s, int bi, int bj, int w) {
     }
 }
 
-/* Item i = (chunk slot i / Hv, v-head i % Hv): start its k and v rows (two TMA boxes of [64 rows][64]
- * each, rows past the end read as zero) completing on landed[buf], and g, beta (cp.async; zero past the
- * chunk). */
+/* Item i = (chunk slot, v-head) by item_at: start its k and v rows (two TMA boxes of [64 rows][64] each, rows
+ * past the end read as zero) completing on landed[buf], and g, beta (cp.async; zero past the chunk). */
 __device__ void prep_issue(const GdnPlan& p, const CUtensorMap* kmap, const CUtensorMap* vmap, PrepSmem& s, int64_t item,
-                           int buf, int tid) {
+                           int64_t slots, int buf, int tid) {
     const RidgeFillGdn& g = p.g;
-    const int64_t slot = item / g.n_head_v, h = item % g.n_head_v, hk = h / (g.n_head_v / g.n_head_k);
+    int64_t slot, h;
+    item_at(p, item, slots, &slot, &h);
+    const int64_t hk = h / (g.n_head_v / g.n_head_k);
     int64_t row0 = 0;
     int len = 0;
     locate_chunk(p, s.r0, s.base, s.n_cached, slot, &row0, &len);
@@ -301,8 +325,8 @@ __device__ void prep_issue(const GdnPlan& p, const CUtensorMap* kmap, const CUte
     }
 }
 
-/* Item `it`'s slot is complete: its bulk stores (K~, then W, U~^T and the meta) have completed (the caller
- * waited for them); made visible at GPU scope, then flagged. One thread. */
+/* The slot of flag `it` (chunk slot x Hv + v-head) is complete: its bulk stores (K~, then W, U~^T and the meta)
+ * have completed (the caller waited for them); made visible at GPU scope, then flagged. One thread. */
 __device__ void publish_item(const GdnPlan& p, int64_t it) {
     asm volatile("fence.proxy.async.global;" ::: "memory");
     __threadfence();
@@ -334,14 +358,15 @@ __device__ void prep_role(const CUtensorMap& kmap, const CUtensorMap& vmap, cons
         s.claim_next = atomicAdd(&p.ctl->next_item, 1);
     }
     sync();
-    const int64_t items = (int64_t)p.tab[3 * n_seq] * g.n_head_v;
+    const int64_t slots = p.tab[3 * n_seq], items = slots * g.n_head_v;
     int64_t item = s.claim;
 
-    if (item < items) prep_issue(p, &kmap, &vmap, s, item, 0, tid);
+    if (item < items) prep_issue(p, &kmap, &vmap, s, item, slots, 0, tid);
     rf::cp_async_commit();
     int buf = 0;
     int64_t waited = 0, issued = item < items ? 1 : 0;
-    int64_t pending = -1;   /* kStoreTid: the item whose slot stores are issued but not yet published */
+    int64_t pending = -1;   /* kStoreTid: the flag (slot x Hv + head) of the item whose slot stores are issued but
+                               not yet published */
     int claim = 0;          /* kStoreTid: the item after the next one, claimed during this item */
     while (item < items) {
         rf::cp_async_wait<0>();
@@ -350,7 +375,8 @@ __device__ void prep_role(const CUtensorMap& kmap, const CUtensorMap& vmap, cons
         if (!s.ok) break;
         const int64_t next = s.claim_next;   /* claimed an item ago (the counter's latency stays off the path) */
         ++waited;
-        const int64_t slot = item / g.n_head_v, h = item % g.n_head_v;
+        int64_t slot, h;
+        item_at(p, item, slots, &slot, &h);
         int64_t row0 = 0;
         int len = 0;
         locate_chunk(p, s.r0, s.base, s.n_cached, slot, &row0, &len);
@@ -422,7 +448,7 @@ __device__ void prep_role(const CUtensorMap& kmap, const CUtensorMap& vmap, cons
             claim = atomicAdd(&p.ctl->next_item, 1);   /* its result is first needed at the item's end */
         }
         if (next < items) {
-            prep_issue(p, &kmap, &vmap, s, next, buf ^ 1, tid);
+            prep_issue(p, &kmap, &vmap, s, next, slots, buf ^ 1, tid);
             ++issued;
         }
         rf::cp_async_commit();
@@ -560,7 +586,7 @@ __device__ void prep_role(const CUtensorMap& kmap, const CUtensorMap& vmap, cons
             rf::bulk_store(out + kSlotU, &s.vraw[buf][0][0][0], kTileBytes);
             rf::bulk_store(out + kSlotMeta, &mt, sizeof(mt));
             rf::bulk_store_commit();
-            pending = item;
+            pending = slot * g.n_head_v + h;
             s.claim_next = claim;   /* read after the next item's first barrier */
         }
         item = next;
@@ -862,7 +888,8 @@ __device__ void chain_tc_role(const GdnPlan& p, TcSmem& s, int64_t first, int64_
     int64_t k0 = 0;          /* chunks taken by this CTA before the current chain */
     int64_t issued = 0;      /* the loader's copies */
     for (int64_t cid = first; cid < n_chains && !*abort; cid += step) {
-        const int64_t h = cid % g.n_head_v, seq = cid / g.n_head_v;
+        int64_t h, seq;
+        chain_at(p, cid, &h, &seq);
         const int64_t state_slot = g.state_idx[seq * g.idx_pitch];
         if (state_slot < 0 || state_slot >= g.n_states) continue;
         const int64_t r0 = p.tab[seq], r1 = p.tab[n + seq], base = p.tab[2 * n + seq];
@@ -1228,6 +1255,65 @@ gdn_out_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__
         }
 }
 
+/* ------------------------------------------------------------------ small heads (dk, dv <= 64)
+
+ * The rule row by row, for heads too narrow for the chunked tensor-core form (the reference's CPU mini
+ * model has head dims 32): one CTA per (v-head, sequence), thread i < dv holding state row S[i][0..dk) in
+ * registers; each row's k (and q) staged in shared memory by the CTA, then per thread
+ *     S_i <- exp(g_t) S_i;   S_i <- S_i + beta_t (v_ti - S_i.k_t) k_t;   o_ti = scale * S_i.q_t
+ * in f32. Needs no workspace. */
+template <int DK>
+__global__ void __launch_bounds__(64) gdn_small_kernel(const RidgeFillGdn g) {
+    __shared__ float kq[2][DK];
+    const int64_t h = blockIdx.x, seq = blockIdx.y;
+    const int64_t slot = g.state_idx[seq * g.idx_pitch];
+    if (slot < 0 || slot >= g.n_states) return;
+    const int64_t a = min(max((int64_t)g.cu[seq], (int64_t)0), g.T);
+    const int64_t b = min(max((int64_t)g.cu[seq + 1], a), g.T);
+    const int i = threadIdx.x, dk = (int)g.dk;
+    const bool mine = i < g.dv;
+    const int64_t hk = h / (g.n_head_v / g.n_head_k);
+    float* srow = g.state + slot * g.st_slot + h * g.st_head + (int64_t)i * dk;
+    float S[DK];
+#pragma unroll
+    for (int j = 0; j < DK; ++j) S[j] = (mine && j < dk) ? srow[j] : 0.0f;
+    for (int64_t t = a; t < b; ++t) {
+        __syncthreads();   /* the previous row's k and q are read */
+        for (int j = i; j < DK; j += blockDim.x) {
+            kq[0][j] = j < dk ? ridgefill_bf16_to_f32(g.k[t * g.k_row + hk * g.k_head + j]) : 0.0f;
+            kq[1][j] = (g.o && j < dk) ? ridgefill_bf16_to_f32(g.q[t * g.q_row + hk * g.q_head + j]) : 0.0f;
+        }
+        __syncthreads();
+        if (!mine) continue;
+        const float decay = expf(g.g[t * g.g_row + h]), beta = g.beta[t * g.b_row + h];
+        float pred = 0.0f;
+#pragma unroll
+        for (int j = 0; j < DK; ++j) {
+            S[j] *= decay;
+            pred = fmaf(S[j], kq[0][j], pred);
+        }
+        const float u = beta * (ridgefill_bf16_to_f32(g.v[t * g.v_row + h * g.v_head + i]) - pred);
+        float out = 0.0f;
+#pragma unroll
+        for (int j = 0; j < DK; ++j) {
+            S[j] = fmaf(u, kq[0][j], S[j]);
+            out = fmaf(S[j], kq[1][j], out);
+        }
+        if (g.o) g.o[t * g.o_row + h * g.o_head + i] = rf::f32_to_bf16_bits(g.scale * out);
+    }
+    if (mine)
+        for (int j = 0; j < dk; ++j) srow[j] = S[j];
+}
+
+int launch_small(const RidgeFillGdn& g, cudaStream_t stream) {
+    const dim3 grid((unsigned)g.n_head_v, (unsigned)g.n_seq);
+    const unsigned threads = g.dv > 32 ? 64 : 32;
+    if (g.dk <= 16) gdn_small_kernel<16><<<grid, threads, 0, stream>>>(g);
+    else if (g.dk <= 32) gdn_small_kernel<32><<<grid, threads, 0, stream>>>(g);
+    else gdn_small_kernel<64><<<grid, threads, 0, stream>>>(g);
+    return rf::launch_status();
+}
+
 int64_t max_slots_of(const RidgeFillGdn& g) { return (g.T + C - 1) / C + g.n_seq; }
 
 /* A [T, heads, 128] bf16 operand (element strides row, head; 1 within a head) as a 3-D tensor map read in
@@ -1249,7 +1335,7 @@ bool head_rows_map(CUtensorMap* map, const void* base, int64_t T, int64_t heads,
 
 extern "C" int64_t ridgefill_gdn_fill_scratch(const RadArgs* a) {
     RidgeFillGdn g;
-    if (ridgefill_gdn_parse(a, &g) != RAD_OK) return 0;
+    if (ridgefill_gdn_parse(a, &g) != RAD_OK || g.dk != D) return 0;   /* the per-row form needs none */
     const int64_t items = max_slots_of(g) * g.n_head_v;
     return table_bytes(g.n_seq) + kCtlBytes + flag_bytes(items) + items * (kSlotBytes + (g.o ? kOutBytes : 0));
 }
@@ -1260,6 +1346,7 @@ extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
     if (rc != RAD_OK) return rc;
     if (g.n_seq == 0 || g.T == 0) return RAD_OK;
     if (g.n_seq > 65535 || g.n_head_v > 65535 || g.T > 0x7fffffffLL) return RAD_E_SHAPE;
+    if (g.dk != D) return launch_small(g, rf::as_stream(s));
     const int64_t slots = max_slots_of(g), items = slots * g.n_head_v;
     const int64_t head = table_bytes(g.n_seq) + kCtlBytes + flag_bytes(items);
     const int64_t need = head + items * (kSlotBytes + (g.o ? kOutBytes : 0));
@@ -1284,6 +1371,7 @@ extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
     p.slots = ws + head;
     p.outws = g.o ? p.slots + items * (int64_t)kSlotBytes : nullptr;
     p.max_slots = (int)slots;
+    p.head_block = (int)g.n_head_v;   /* the output form: slot-major over every head */
     cudaStream_t stream = rf::as_stream(s);
     const int smem1 = (int)sizeof(PrepSmem) + 1024, smem2 = (int)sizeof(ChainSmem) + 128, smem3 = (int)sizeof(OutSmem) + 1024;
     if (cudaFuncSetAttribute(gdn_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem1) != cudaSuccess ||
@@ -1306,6 +1394,7 @@ extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
         int chain_ctas = (int)(chains < grid / 4 ? chains : grid / 4);
         if (chain_ctas < 1) chain_ctas = 1;
         if (chain_ctas >= grid) return RAD_E_DEVICE;
+        p.head_block = chain_ctas;   /* phase 1 makes the chunks in the order the chain CTAs read them */
         void* args[] = { (void*)&kmap, (void*)&vmap, (void*)&p, (void*)&chain_ctas };
         if (cudaLaunchCooperativeKernel((const void*)gdn_fill_fused_kernel, dim3((unsigned)grid), dim3(kFusedThreads), args,
                                         kFusedSmem, stream) != cudaSuccess)

@@ -816,7 +816,9 @@ extern "C" int ridgefill_gdn_parse(const RadArgs* a, RidgeFillGdn* g) {
     gate.slots(GD_STATE_IDX, &rows);
     if (!gate.open()) return gate.code();
     const int64_t n_seq = rows.rows, pitch = rows.pitch;
-    if (hk <= 0 || hv <= 0 || hv % hk != 0 || dk != 128 || dv != 128 || chunk != 64) return RAD_E_UNSUPPORTED;
+    /* head dims 128 (the chunked tensor-core fill) or at most 64 each (the per-row fill), dk whole 16-byte rows */
+    const bool wide = dk == 128 && dv == 128, small = dk >= 8 && dk <= 64 && dk % 8 == 0 && dv >= 1 && dv <= 64;
+    if (hk <= 0 || hv <= 0 || hv % hk != 0 || !(wide || small) || chunk != 64) return RAD_E_UNSUPPORTED;
     if (Kt->rank != 3 || V->rank != 3 || G->rank != 2 || Bt->rank != 2 || St->rank != 4 ||
         (Q && Q->rank != 3) || (O && O->rank != 3))
         return RAD_E_SHAPE;

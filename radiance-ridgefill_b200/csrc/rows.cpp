@@ -133,7 +133,7 @@ const RadKernelInfo kRows[] = {
                "i32 cu_last / positions / slots, f32 meta / count", nullptr, 0, ridgefill_hazard_device, nullptr,
                shape_hazard, nullptr, nullptr, nullptr),
     DEVICE_ROW("ridgefill_gemm_nt_q_sm100", "ridgefill_gemm_nt_q",
-               "tcgen05 kind::i8 into tensor memory, TMA-fed, persistent 128x256 tiles, f32 block fold in the epilogue",
+               "tcgen05 kind::i8 (cta_group::2) into tensor memory, TMA-fed, persistent 256x256 tiles on 2-CTA pairs, f32 block fold in the epilogue",
                "K a multiple of 128, N of 16", "i8 a / b, f32 a_scale / stored b_scale, bf16 y", kGemmCons, 1,
                ridgefill_gemm_nt_q_device, nullptr, shape_gemm_q, gemm_layout, gemm_relayout, gemm_unrelayout),
     DEVICE_ROW("ridgefill_gemm_nt_q_bias_sm100", "ridgefill_gemm_nt_q_bias",
@@ -141,7 +141,7 @@ const RadKernelInfo kRows[] = {
                "i8 a / b, f32 a_scale / stored b_scale, bf16 bias / y, i32 acc", kGemmCons, 1,
                ridgefill_gemm_nt_q_bias_device, nullptr, shape_gemm_q_bias, gemm_layout, gemm_relayout, gemm_unrelayout),
     DEVICE_ROW("ridgefill_gemm_nt_bias_sm100", "ridgefill_gemm_nt_bias",
-               "tcgen05 kind::f16 (bf16 operands), TMEM f32 accumulators, TMA 128-B swizzled 128x256 tiles, bias / silu / "
+               "tcgen05 kind::f16 (bf16 operands), TMEM f32 accumulators, TMA 128-B swizzled 256x256 tiles on 2-CTA pairs, bias / silu / "
                "residual epilogue, TMA tile stores", "K a multiple of 64, N of 8", "bf16 a / b / res / y, bf16 or f32 bias",
                kGemmBiasCons, 1, ridgefill_gemm_nt_bias_device, nullptr, shape_gemm_bias, nullptr, nullptr, nullptr),
     DEVICE_ROW("ridgefill_quant_act_i8g_sm100", "ridgefill_quant_act_i8g", "warp per row group, 16-byte loads",
@@ -149,7 +149,7 @@ const RadKernelInfo kRows[] = {
                shape_quant, nullptr, nullptr, nullptr),
     DEVICE_ROW("ridgefill_gdn_fill_sm100", "ridgefill_gdn_fill",
                "chunked gated delta rule: per-chunk WY transform on tensor cores, then the inter-chunk state carry",
-               "head dims 128, chunk 64", "bf16 q / k / v / o, f32 g / beta / state", nullptr, 0, ridgefill_gdn_fill_device,
+               "head dims 128 (chunked, tensor cores) or at most 64 (row by row), chunk 64", "bf16 q / k / v / o, f32 g / beta / state", nullptr, 0, ridgefill_gdn_fill_device,
                ridgefill_gdn_fill_scratch, shape_gdn, nullptr, nullptr, nullptr),
     DEVICE_ROW("ridgefill_gdn_conv_prep_sm100", "ridgefill_gdn_conv_prep",
                "warp per 16 rows of a pair of 128-channel head columns, all 16 rows' loads in flight as asynchronous "

@@ -20,6 +20,7 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent.parent
 PKG = ROOT / "radiance-ridgefill_b200"
 sys.path.insert(0, str(PKG))
+sys.path.insert(0, str(ROOT / "oracle"))   # cpu_path: the pass on host buffers (test infrastructure)
 
 import ridgefill_abi as abi  # noqa: E402
 

@@ -1,0 +1,61 @@
+"""The late-layer pass's launch list on the CPU: built over host tensors, every launch's operands and parameters
+pass its device row's operand checks (the rows' exported parse functions, called directly: nothing is launched),
+the pass issues the reference's op order, and its CPU twin (oracle/cpu_path.CpuLatePass) runs the same shapes."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import harness as H  # noqa: F401  (puts the package on the path)
+import late_pass as LP
+import cpu_path as CP
+from harness import abi
+
+PARSE = {"ridgefill_mask": "ridgefill_mask_parse", "ridgefill_quant_act_i8g": "ridgefill_quant_parse",
+         "ridgefill_select": "ridgefill_select_parse", "ridgefill_gemm_nt_bias": "ridgefill_gemm_bias_parse",
+         "ridgefill_gdn_conv_prep": "ridgefill_conv_prep_parse", "ridgefill_attn_kv_fill": "ridgefill_attn_kv_parse",
+         "ridgefill_state_correct": "ridgefill_correct_parse", "ridgefill_gdn_fill": "ridgefill_gdn_parse",
+         "ridgefill_rho_update": "ridgefill_rho_parse", "ridgefill_hazard": "ridgefill_hazard_parse"}
+
+SHAPES = [LP.config0(), LP.LateShape(T=256, d=256, hk=2, hv=4), LP.LateShape(T=300, d=256, layers="GA", hk=2, hv=4,
+                                                                              seqlens=(100, 80, 120))]
+
+
+def _parse(lib, op, tens, params):
+    args, keep = abi.Plugin.args(tens, params)
+    out = (C.c_uint8 * 4096)()
+    if op == "ridgefill_gemm_nt_q_bias":
+        fn = lib.lib.ridgefill_gemm_q_parse
+        fn.restype = C.c_int
+        rc = fn(C.byref(args), 1, out)
+    else:
+        fn = getattr(lib.lib, PARSE[op])
+        fn.restype = C.c_int
+        rc = fn(C.byref(args), out)
+    del keep
+    return rc
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=["config0", "all24_small", "ragged"])
+def test_every_launch_passes_its_operand_checks(shape, product_lib):
+    p = LP.LatePass(shape, "cpu", seed=1)
+    for op, _row, tens, params, tag in p.calls:
+        assert _parse(product_lib, op, tens, params) == abi.OK, (op, tag)
+    counts = p.op_counts()
+    G, A, L = shape.n_gdn, shape.n_attn, len(shape.layers)
+    assert counts["ridgefill_gemm_nt_q_bias"] == L + (G if shape.block_inputs else 0) + A
+    assert counts["ridgefill_gdn_fill"] == 1 and counts["ridgefill_rho_update"] == G
+    assert counts["ridgefill_state_correct"] == 2 and counts["ridgefill_mask"] == 1 and counts["ridgefill_hazard"] == 1
+    order = [c[0] for c in p.calls]
+    assert order[0] == "ridgefill_mask" and order[-1] == "ridgefill_hazard"
+    assert order.index("ridgefill_gdn_fill") > max(i for i, o in enumerate(order) if o == "ridgefill_select")
+
+
+def test_cpu_twin_runs_the_same_pass(oracle_lib):
+    shape = LP.LateShape(T=200, d=256, layers="GGA", hk=2, hv=4, seqlens=(120, 80))
+    host = CP.to_host(LP.late_inputs(shape, "cpu", 2))
+    cpu = CP.CpuLatePass(shape, host)
+    cpu.run()
+    assert cpu.mask[:120].sum() == 0 and cpu.mask[120:].sum() > 0    # only the last sequence is approximated
+    assert np.isfinite(cpu.state).all() and np.abs(cpu.nd[-1]).sum() > 0 and np.abs(cpu.nd[0]).sum() == 0
+    assert (cpu.cache[0][0] != 0).any()

@@ -1,0 +1,126 @@
+"""The whole approximate pass over the late layers on the device (late_pass.LatePass, every op a device row) against
+the same pass on the host (oracle/cpu_path.CpuLatePass: the reference's own host rows for mask, select, the state
+correction, rho and the hazard record where oracle/_ref was built, the restatement's oracles for the rest), fed
+the same seeded inputs. Every buffer the pass writes is compared:
+
+    mask, bounds, the hazard record                    equal
+    every layer's block input after select             bit for bit (the int8 projector is exact)
+    attention caches, conv states                      bit for bit
+    a|b projections                                    the reference's bf16 GEMM bound (2^-7 |y| + 2^-9 RMS)
+    k, v (conv_prep)                                   2 bf16 ulp (2^-7 of the larger magnitude), plus the
+                                                       smallest normal f32: the device flushes f32 subnormal
+                                                       results (|y| < 1.2e-38) to zero, the host keeps them
+    g, beta                                            1e-5 wherever a|b agree bit for bit
+    DeltaNet state, every layer and slot               1e-3 relative L2 (f32 sequential rule)
+    N|D decay sums, applied scales                     1e-4 relative (the reference's rho bound)
+
+The shapes: the reference's CPU mini model (config 0: d 256, 512 rows, 4 DeltaNet layers of 4 / 8 heads of 32), a
+2,048-row sample of the full step's first four late layers (G G G A) at full width, all 24 late layers at 256 rows
+(the fill batched over 18 layers' heads), and a ragged batch of three sequences."""
+import numpy as np
+import pytest
+
+import harness as H  # noqa: F401  (puts the package on the path)
+import late_pass as LP
+import cpu_path as CP
+
+gpu = pytest.mark.gpu
+FLT_MIN = float(np.finfo(np.float32).tiny)
+
+SHAPES = {
+    "config0": LP.config0(),
+    "config3_T2048_first4": LP.LateShape(T=2048, layers="GGGA"),
+    "config3_T256_all24": LP.LateShape(T=256),
+    "ragged_3seq": LP.LateShape(T=1400, layers="GGA", seqlens=(300, 100, 1000)),
+}
+
+
+def _u16(t):
+    import torch
+    t = t.detach().cpu()
+    return t.view(torch.int16).numpy().view(np.uint16) if t.dtype == torch.bfloat16 else t.numpy()
+
+
+def _rel(a, b):
+    return float(np.linalg.norm((a - b).ravel()) / max(np.linalg.norm(b.ravel()), 1e-30))
+
+
+@gpu
+@pytest.mark.parametrize("name", list(SHAPES))
+def test_late_pass_matches_the_cpu_path(name, cuda):
+    torch = cuda
+    shape = SHAPES[name]
+    dev = LP.LatePass(shape, "cuda", seed=17)
+    host = CP.to_host(dev.inp)
+    cpu = CP.CpuLatePass(shape, host)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        dev.run(stream.cuda_stream)
+    stream.synchronize()
+    cpu.run()
+    s = shape
+    G, hv, hk = s.n_gdn, s.hv, s.hk
+
+    assert np.array_equal(_u16(dev.mask), cpu.mask)
+    assert np.array_equal(_u16(dev.bounds), cpu.bounds)
+    assert np.array_equal(_u16(dev.meta), cpu.meta) and np.array_equal(_u16(dev.count), cpu.count)
+    for li in range(len(s.layers)):
+        assert np.array_equal(_u16(dev.x[li]), cpu.xl[li]), f"layer {li}: block input after select"
+    for ai in range(s.n_attn):
+        assert np.array_equal(_u16(dev.cache[ai]), cpu.cache[ai]), f"attention layer {ai}: cache"
+    same_ab = np.ones((s.T, G * hv), bool)
+    if s.block_inputs:
+        for j in range(G):
+            assert np.array_equal(_u16(dev.conv_state[j]), cpu.conv_state[j]), f"DeltaNet layer {j}: conv state"
+            got, want = _u16(dev.ab[j]), cpu.ab[j]
+            xf, yf = H.bf16_bits_to_f32(got).astype(np.float64), H.bf16_bits_to_f32(want).astype(np.float64)
+            rms = np.sqrt(np.mean(yf ** 2))
+            assert np.all(np.abs(xf - yf) <= 2.0 ** -7 * np.maximum(np.abs(xf), np.abs(yf)) + 2.0 ** -9 * rms)
+            eq = got == want
+            same_ab[:, j * hv:(j + 1) * hv] = eq[:, :hv] & eq[:, hv:]
+        for name, got, want in (("k", _u16(dev.k), cpu.k), ("v", _u16(dev.v), cpu.v)):
+            xf, yf = H.bf16_bits_to_f32(got).astype(np.float64), H.bf16_bits_to_f32(want).astype(np.float64)
+            bad = ~((got == want) | (np.abs(xf - yf) <= np.ldexp(np.maximum(np.abs(xf), np.abs(yf)), -7) + FLT_MIN))
+            assert not bad.any(), (name, int(bad.sum()), [(tuple(i), xf[tuple(i)], yf[tuple(i)]) for i in np.argwhere(bad)[:4]])
+        for got, want in ((_u16(dev.g), cpu.g), (_u16(dev.beta), cpu.beta)):
+            err = np.abs(got - want) / np.maximum(np.abs(want), 1.0)
+            assert err[same_ab].max() <= 1e-5
+    state, want_state = _u16(dev.state), cpu.state
+    for sl in range(s.n_seq):
+        for j in range(G):
+            blk = slice(j * hv, (j + 1) * hv)
+            assert _rel(state[sl, blk], want_state[sl, blk]) <= 1e-3, (sl, j)
+    nd, want_nd = _u16(dev.nd), cpu.nd
+    assert np.all(np.abs(nd - want_nd) <= 1e-4 * np.maximum(np.abs(want_nd), 1.0))
+    ap, want_ap = _u16(dev.applied), cpu.applied
+    assert np.all(np.abs(ap - want_ap) <= 1e-4 * np.maximum(np.abs(want_ap), 1.0))
+
+
+@gpu
+def test_batched_fill_equals_one_fill_per_layer(cuda, product_lib):
+    """The late pass's single fill launch over every DeltaNet layer's heads writes, bit for bit, what one fill
+    launch per layer writes: the heads are independent chains and each is computed the same way whatever else
+    the launch holds."""
+    torch = cuda
+    shape = LP.LateShape(T=1000, d=256, layers="GGG", block_inputs=False, seqlens=(400, 600))
+    dev = LP.LatePass(shape, "cuda", seed=5)
+    G, hk, hv, D, T = shape.n_gdn, shape.hk, shape.hv, shape.head, shape.T
+    state0 = dev.state.clone()
+    fill = [c for c in dev.calls if c[0] == "ridgefill_gdn_fill"][0]
+    stream = torch.cuda.Stream()
+    dev._launch(fill[0], fill[1], fill[2], fill[3], stream.cuda_stream)
+    stream.synchronize()
+    batched = dev.state.clone()
+    per_layer = state0.clone()
+    from harness import abi
+    for j in range(G):
+        k = dev.k[:, j * hk:(j + 1) * hk]
+        v = dev.v[:, j * hv:(j + 1) * hv]
+        g = dev.g[:, j * hv:(j + 1) * hv]
+        b = dev.beta[:, j * hv:(j + 1) * hv]
+        st = per_layer[:, j * hv:(j + 1) * hv]
+        tens = [abi.absent(), H.dev(k, abi.BF16), H.dev(v, abi.BF16), H.dev(g), H.dev(b), H.dev(st), H.dev(dev.slots_all),
+                H.dev(dev.inp["cu_seqlens"]), abi.absent()]
+        assert H.launch(product_lib, "ridgefill_gdn_fill", tens, H.gdn_params(T, hk, hv)) == abi.OK
+    torch.cuda.synchronize()
+    assert torch.equal(batched, per_layer)
