@@ -1,27 +1,31 @@
-"""bench.py -- prefill tokens/s of one RidgeFill approximate pass at 32K on B200.
+"""bench.py -- prefill tokens/s of the full RidgeFill step at 32K on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mine|reference]
 
-A step is one pass of the RidgeFill hot path over a 32,768-row prefill chunk (ridgefill_step.Step):
-mask -> activation codes -> int8 projector (d 2,048, per-column scales, fused bias) -> select ->
-state undo -> Gated DeltaNet chunk fill (16 q/k heads, 32 v heads, 128 dims, state [32,128,128] f32)
--> rho -> state apply -> hazard, every op a launch of the library's sm_100a device rows through the C
-ABI. Synthetic inputs with BASELINE's shapes and distributions, seeded; inputs (> 700 MB) exceed the
-126 MB L2, so no flush is needed between steps. The timed passes are issued pipelined (Step.run_pipelined):
-the projector path (codes, projector) from the top of the pass and select after the mask on a normal-priority
-stream, the rest (mask, undo, fill, rho, apply, hazard) on a high-priority stream, as a pass over the late layers
-runs the next layer's projection of the shared h_S beside this layer's fill; every op of every pass still runs,
-and a pass ends when both streams have finished it.
+A step is one approximate pass of the RidgeFill step over a 32,768-row prefill chunk of the 48-layer stack
+the 24 late layers, 18 Gated DeltaNet and 6 attention layers, through this library's sm_100a
+device rows (late_pass.LatePass): the class mask (30 % of rows exact) and the layer-S stream's codes once, then per
+layer the int8 projector d 2,048 (per-column scales, fused bias), select and the block input's codes; per DeltaNet
+layer the int8 mixed q|k|v projection, the bf16 a|b projection and conv_prep (16 q/k, 32 v heads x 128); per
+attention layer the int8 k|v projection and the K/V cache write (2 kv heads x 256, imrope); then one fill launch over
+all 18 DeltaNet layers' 576 heads between a state undo and apply over the same heads, rho per layer, the hazard record.
+Synthetic inputs with BASELINE's shapes and distributions, seeded; the pass reads > 10 GB, far past the 126 MB L2, so
+no flush is needed between steps.
 
 value   device time of K passes with inputs resident in HBM (CUDA events, max over ranks)
-e2e     the same passes with each step's inputs copied host->device from pinned memory and the results
-        (projected block input x, DeltaNet state, mask) copied back, inside the timed region; two buffer sets
-        let one step's copies overlap the neighbouring steps' passes (copy engines and SMs run together)
-N > 1   one process per GPU (torchrun), each rank an independent 32K prompt: prompts are independent
-        units, no data-path collective ("scaling": "weak"); value = all ranks' tokens / max rank time.
---impl reference   the CPU arm: the reference's own host rows (compiled from kernels/host_ref.cpp into
-        oracle/_ref) plus the CPU restatement of the projector and the fill it lacks, on a 2,048-row
-        sample of the workload, all host threads; rank 0 only.
+e2e     the same passes through the same C-ABI rows with each step's inputs (h_S, token ids, positions) copied
+        host->device from pinned memory and its results (every DeltaNet state, every attention cache, the mask,
+        the decay sums, the hazard record) copied back, inside the timed region; two buffer sets let one step's copies
+        overlap the neighbouring steps' passes
+N > 1   one process per GPU (torchrun), tensor parallel over ONE prompt: each rank the DeltaNet value heads of its
+        span (with their k heads) and its attention kv heads, the projector's output columns split across ranks and
+        all-gathered over NVLink by the library's peer kernels ("scaling": "strong"; value = the prompt's tokens / the
+        slowest rank's time)
+extra   the config-5 ragged batch (one 32K prompt after six of U[256, 2,048] rows) and the one-layer pass, device time
+--impl reference   the CPU arm: the same pass on the host -- the reference's own host rows compiled from its sources
+        (oracle/_ref) for mask, select, correction, rho, hazard, and the CPU restatement for the GEMMs, quantiser,
+        conv_prep, K/V write and fill the reference does not contain -- on a bounded sample (2,048 rows, the first 4
+        late layers), scaled to the pass; every host core; rank 0 only.
 """
 from __future__ import annotations
 
@@ -40,10 +44,10 @@ sys.path.insert(0, str(ROOT / "radiance-ridgefill_b200"))
 sys.path.insert(0, str(ROOT / "oracle"))
 
 METRIC = "prefill tokens/s at 32K (RidgeFill step)"
-WORKLOAD = ("RidgeFill approximate pass over a 32,768-row prefill chunk: projector d 2,048 (int8, per-column scales), "
-            "Gated DeltaNet fill 16 qk / 32 v heads x 128, class mask share 0.30")
 T_FULL = 32768
-CPU_SAMPLE_ROWS = 2048
+WORKLOAD = ("BASELINE config 3: the full RidgeFill step over the 24 late layers of a 48-layer stack (18 Gated "
+            "DeltaNet + 6 attention), hidden 2,048, int8 per-column projectors, 32,768-row prompt, 30 % of rows exact")
+CPU_ROWS, CPU_LAYERS = 2048, 4
 
 
 def peaks() -> dict:
@@ -145,14 +149,27 @@ def dist_setup():
     return world, rank, local
 
 
-def cpu_arm(steps: int, warmup: int) -> dict:
+# ------------------------------------------------------------------------------------------ the CPU arm
+
+def cpu_arm(passes: int, warmup: int) -> dict:
+    """The pass on the host over a bounded sample: CPU_ROWS rows of the prompt through the first CPU_LAYERS late
+    layers (one period of the 3:1 DeltaNet / attention interleave); the whole pass's time is taken as the sample's
+    time x 24 / CPU_LAYERS, and the rows per second of the sample stand for the chunk's (the CPU rows are linear in
+    the rows, except the mask's O(w^2) rank count, which is a small part at this size)."""
     import cpu_path
-    s = cpu_path.CpuStep(CPU_SAMPLE_ROWS)
-    sec = s.time_steps(steps, warmup)
-    return {"value": CPU_SAMPLE_ROWS / sec, "unit": "tokens/s", "cores": s.threads, "kind": s.kind,
-            "sample": f"the same pass on a {CPU_SAMPLE_ROWS}-row chunk (T={CPU_SAMPLE_ROWS} of {T_FULL}; "
-                      f"the mask's rank count is O(w^2), so the full chunk is slower per row on the CPU), "
-                      f"{steps} timed passes", "sec_per_pass": sec}
+    import late_pass as LP
+    shape = LP.config3(CPU_ROWS)
+    inputs = cpu_path.to_host(LP.late_inputs(shape, "cpu", 7))
+    c = cpu_path.CpuLatePass(shape, inputs, layers=CPU_LAYERS)
+    sec = c.time_passes(passes, warmup)
+    scale = len(shape.layers) / CPU_LAYERS
+    per_pass = sec * scale
+    return {"value": CPU_ROWS / per_pass, "unit": "tokens/s", "cores": c.threads, "kind": c.kind,
+            "sample": f"{CPU_ROWS} rows of the prompt through the first {CPU_LAYERS} of the 24 late layers "
+                      f"(G G G A), {passes} timed passes of {sec:.2f} s; the full pass taken as x{scale:g} (24 layers); "
+                      f"mask, select, correction, rho, hazard: the reference's host rows ({c.kind}); GEMMs, quantiser, "
+                      f"conv_prep, K/V write, fill: the CPU restatement, OpenMP on {c.threads} threads",
+            "sec_per_pass": per_pass}
 
 
 def run_reference(args):
@@ -162,19 +179,59 @@ def run_reference(args):
     base = cpu_arm(args.steps, args.warmup)
     line = {"metric": METRIC, "value": base["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": base["sec_per_pass"] * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "i8/bf16/f32", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": "i8/bf16/f32", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": WORKLOAD, "rows": T_FULL, "d": 2048,
+            "config": {"workload": WORKLOAD, "rows": T_FULL, "d": 2048, "late_layers": 24,
                        "parallelism": "host cores of rank 0 (each step a bounded sample: cpu_baseline.sample)"},
             "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------------------------------ the device arm
+
+def per_op_times(p, stream, reps: int = 2) -> dict:
+    """Device milliseconds per pass of each row (every launch of it), from an ordered pass with events."""
+    import torch
+    counts = p.op_counts()
+    total = {op: 0.0 for op in counts}
+    for _ in range(reps):
+        ev = {op: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+              for op, n in counts.items()}
+        with torch.cuda.stream(stream):
+            p.run(stream.cuda_stream, events=ev)
+        stream.synchronize()
+        for op, pairs in ev.items():
+            total[op] += sum(a.elapsed_time(b) for a, b in pairs) / reps
+    return total
+
+
+def roofline(op: str, ms: float, alg: dict, pk: dict) -> dict:
+    """The roofline of one row's launches in a pass (all of its launches: `ms` their summed device time)."""
+    if op == "ridgefill_gemm_nt_q_bias":
+        peak = 2.0 * pk["bf16_tflops"]
+        r = {"bound": "tensor", "achieved": alg["int8_ops"] / (ms * 1e-3) / 1e12, "peak": peak, "unit": "TOP/s",
+             "traffic": None, "note": f"int8 dense peak = 2 x the {pk['source']} bf16 figure ({pk['bf16_tflops']} TF/s); "
+                                      "the pass's int8 GEMM launches together (projectors, mixed and k|v projections)"}
+    elif op == "ridgefill_gdn_fill":
+        r = {"bound": "hbm", "achieved": alg["fill_bytes"] / (ms * 1e-3) / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
+             "traffic": None, "note": f"the batched fill (state-only bytes: k, v, g, beta read, state read and written); "
+                                      f"peak {pk['source']}"}
+        r["tensor"] = {"achieved": alg["fill_chunk_flops"] / (ms * 1e-3) / 1e12, "peak": pk["bf16_tflops"],
+                       "unit": "TFLOP/s"}
+        r["tensor"]["frac"] = r["tensor"]["achieved"] / r["tensor"]["peak"]
+    else:
+        return {"kernel": op, "kernel_ms": ms}
+    r["frac"] = r["achieved"] / r["peak"]
+    r["kernel"] = op
+    r["kernel_ms"] = ms
+    return r
+
+
 def run_mine(args):
     import torch
     import torch.distributed as dist
-    import ridgefill_step as RS
+    import late_pass as LP
 
     world, rank, local = dist_setup()
     if world > 1:
@@ -182,63 +239,50 @@ def run_mine(args):
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    step = RS.Step(RS.StepShape(T=T_FULL), device=str(dev), seed=1234 + rank)
-    # the pass's main stream at high priority; the projector path and select beside it at normal priority (run_pipelined)
-    stream = torch.cuda.Stream(device=dev, priority=-1)
-    side = torch.cuda.Stream(device=dev, priority=0)
-    alg = step.algorithmic()
+    shape = LP.config3(T_FULL)
+    team = LP.Team.create(world, rank, dist) if world > 1 else None
+    p = LP.LatePass(shape, str(dev), seed=1234, team=team)
+    stream = torch.cuda.Stream(device=dev)
+    alg = p.algorithmic()
+    kernels = p.kernels
 
     def barrier():
         if world > 1:
             dist.barrier()
 
-    # per-op device times (untimed pass), to name the dominant kernel
     with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 3)):
-            step.run(stream.cuda_stream)
-        ops = {name: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for name in {c[0] for c in step.calls}}
-        per_op = {n: 0.0 for n in ops}
-        for _ in range(3):
-            step.run(stream.cuda_stream, events=ops)
-            stream.synchronize()
-            for n, (a, b) in ops.items():
-                per_op[n] += a.elapsed_time(b) / 3
+            p.run(stream.cuda_stream)
+    stream.synchronize()
+    per_op = per_op_times(p, stream)
     dominant = max(per_op, key=per_op.get)
 
     # ---------------------------------------------------------- device-resident timing
-    dom_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(local)
-    pipelined = dominant not in RS.Step.SIDE_OPS
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
-            step.run_pipelined(stream, side)
+            p.run(stream.cuda_stream)
         stream.synchronize()
         barrier()
         torch.cuda.synchronize()
         clocks.start()
-        start.record()
-        for i in range(args.steps):
-            if pipelined:
-                step.run_pipelined(stream, side, events={dominant: dom_ev[i]})
-            else:
-                step.run(stream.cuda_stream, events={dominant: dom_ev[i]})
-        end.record()
+        start.record(stream)
+        for _ in range(args.steps):
+            p.run(stream.cuda_stream)
+        end.record(stream)
         stream.synchronize()
     clock_info = clocks.stop()
     torch.cuda.synchronize()
     barrier()
     ms = start.elapsed_time(end) / args.steps
-    dom_ms = statistics.mean(a.elapsed_time(b) for a, b in dom_ev)
 
-    # ---------------------------------------------------------- end to end through the C ABI, host buffers
-    # Each step uploads its inputs from pinned host memory, runs the pass and reads its results back. Two
-    # buffer sets (two Step objects) and three streams let step i+1's upload and step i-1's readback run on
-    # the copy engines while step i computes; a set is reused only after its previous pass and readback.
-    steps2 = [step, RS.Step(RS.StepShape(T=T_FULL), device=str(dev), seed=4321 + rank)]
-    ins = [[s_.h_s, s_.k, s_.v, s_.g, s_.beta, s_.ab, s_.token_ids, s_.positions] for s_ in steps2]
-    outs = [[s_.x, s_.state, s_.mask] for s_ in steps2]
+    # ---------------------------------------------------------- end to end, host buffers in and out
+    # Two buffer sets (two passes' buffers) and three streams: step i+1's upload and step i-1's readback run on the
+    # copy engines while step i computes; a set is reused only after its previous pass and readback.
+    sets = [p, LP.LatePass(shape, str(dev), seed=4321, team=team)]
+    ins = [s_.inputs_per_step() for s_ in sets]
+    outs = [s_.results() for s_ in sets]
     host_in = [t.cpu().pin_memory() for t in ins[0]]
     host_out = [[torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in o] for o in outs]
     h2d = sum(t.numel() * t.element_size() for t in host_in)
@@ -261,7 +305,8 @@ def run_mine(args):
             stream.wait_event(ev_in)
             if done_out[b_] is not None:
                 stream.wait_event(done_out[b_])
-            steps2[b_].run_pipelined(stream, side)
+            with torch.cuda.stream(stream):
+                sets[b_].run(stream.cuda_stream)
             done_comp[b_] = torch.cuda.Event()
             done_comp[b_].record(stream)
             with torch.cuda.stream(s_out):
@@ -284,165 +329,128 @@ def run_mine(args):
     torch.cuda.synchronize()
     barrier()
     e2e_ms = e_start.elapsed_time(e_end) / args.steps
+    del sets[1]
 
-    # the job's time is its slowest rank's
+    # ---------------------------------------------------------- extras (one GPU): config 5 and the one-layer pass
+    extra = {}
+    if world == 1 and not args.no_extra:
+        del p
+        torch.cuda.empty_cache()
+        extra["config5_ragged"] = time_extra(LP.LatePass(LP.config5(), str(dev), seed=99), stream, args.steps)
+        torch.cuda.empty_cache()
+        extra["one_layer_pass"] = time_one_layer(stream, args.steps)
+
     import shard
+    dom_ms = per_op[dominant]
     ms, e2e_ms, dom_ms = shard.max_over_ranks([ms, e2e_ms, dom_ms], dist if world > 1 else None)
 
     if rank == 0:
         pk = peaks()
-        if dominant == "ridgefill_gemm_nt_q_bias":
-            int8_peak = 2.0 * pk["bf16_tflops"]
-            roof = {"bound": "tensor", "achieved": alg["gemm_ops"] / (dom_ms * 1e-3) / 1e12, "peak": int8_peak,
-                    "unit": "TOP/s", "traffic": None,
-                    "note": f"int8 dense peak = 2 x the {pk['source']} bf16 figure ({pk['bf16_tflops']} TF/s)"}
-        else:
-            by = {"ridgefill_gdn_fill": alg["gdn_bytes"], "ridgefill_quant_act_i8g": alg["quant_bytes"],
-                  "ridgefill_select": alg["select_bytes"]}.get(dominant, 0)
-            roof = {"bound": "hbm", "achieved": by / (dom_ms * 1e-3) / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                    "traffic": None, "note": f"peak {pk['source']}"}
-            if dominant == "ridgefill_gdn_fill":
-                # DRAM bytes of one fill from an ncu capture at 16,384 rows (plan + fill kernels: 0.009 + 564.9
-                # MB: 208.1 read, 356.9 written), scaled by rows: every term (k, v, g, beta reads, the chunk
-                # slots written and read back) grows in proportion to the rows.
-                roof["traffic"] = 564.9e6 * T_FULL / 16384
-                roof["traffic_note"] = "ncu dram__bytes_read+write at 16,384 rows, scaled by rows"
-                roof["tensor"] = {"achieved": alg["gdn_chunk_flops"] / (dom_ms * 1e-3) / 1e12, "peak": pk["bf16_tflops"],
-                                  "unit": "TFLOP/s"}
-                roof["tensor"]["frac"] = roof["tensor"]["achieved"] / roof["tensor"]["peak"]
-        roof["frac"] = roof["achieved"] / roof["peak"]
-        roof["kernel"] = dominant
-        roof["kernel_ms"] = dom_ms
-        line = {"metric": METRIC, "value": world * T_FULL / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+        roof = roofline(dominant, dom_ms, alg, pk)
+        second = max((op for op in per_op if op != dominant), key=per_op.get)
+        fill_key = "ridgefill_gdn_fill"
+        line = {"metric": METRIC, "value": T_FULL / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "i8/bf16/f32", "data": "synthetic",
-                "config": {"workload": WORKLOAD, "rows": T_FULL, "d": 2048, "l2": "inputs larger than L2 (no flush)",
-                           "parallelism": f"independent prompts x{world}",
-                           "streams": "projector path beside the fill (two streams, pipelined pass)"},
-                "gpu_launches": Step_launches(step) * args.steps,
+                "scaling": "strong", "vs_baseline": None, "dtype": "i8/bf16/f32", "data": "synthetic",
+                "config": {"workload": WORKLOAD, "rows": T_FULL, "d": 2048, "late_layers": "GGGA x 6",
+                           "l2": "inputs larger than L2 (no flush)",
+                           "parallelism": (f"tp{world}: value heads and attention kv heads by rank span, projector "
+                                           f"columns split and all-gathered by peer kernels" if world > 1 else "tp1")},
+                "gpu_launches": kernels * args.steps,
                 "per_op_ms": {k: round(v, 4) for k, v in sorted(per_op.items(), key=lambda kv: -kv[1])},
-                "roofline": roof, "clocks": clock_info,
-                "e2e": {"value": world * T_FULL / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "roofline": roof,
+                "roofline_next": roofline(second, per_op[second], alg, pk) if second in (fill_key, "ridgefill_gemm_nt_q_bias") else None,
+                "clocks": clock_info,
+                "e2e": {"value": T_FULL / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h}}
+        if extra:
+            line["extra"] = extra
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = {k: v for k, v in cpu_arm(2, 1).items() if k != "sec_per_pass"}
         print(json.dumps(line), flush=True)
+    if team is not None:
+        team.close()
     if world > 1:
         dist.destroy_process_group()
 
 
-def side_op_call(op: str, rows: int):
-    """Operands of a row the pass does not issue, at the served layer's shapes and `rows` rows (synthetic, seeded):
-    ridgefill_gdn_conv_prep (16 q/k and 32 v heads of 128, one sequence with a conv history) and
-    ridgefill_attn_kv_fill (2 kv heads of 256, rope 64 of imrope sections 11/11/10, every row stored). Returns
-    (row, tensors, params, keep) -- `keep` holds the torch buffers for as long as the launches run."""
+def time_extra(p, stream, steps: int) -> dict:
     import torch
-    import ridgefill_abi as abi
-    lib = abi.product()
-    g = torch.Generator(device="cuda").manual_seed(1234)
-    t = lambda x, code=None: abi.tensor(code or {torch.float32: abi.F32, torch.bfloat16: abi.BF16,   # noqa: E731
-                                                  torch.int32: abi.I32}[x.dtype], list(x.shape), x.data_ptr(), list(x.stride()))
-    T = rows
-    if op == "ridgefill_gdn_conv_prep":
-        hk, hv = 16, 32
-        C = 2 * hk * 128 + hv * 128
-        keep = dict(x=torch.randn(T, C, device="cuda", generator=g).bfloat16(),
-                    w=(0.5 * torch.randn(C, 4, device="cuda", generator=g)).bfloat16(),
-                    al=torch.randn(hv, device="cuda", generator=g), dt=torch.randn(hv, device="cuda", generator=g),
-                    st=torch.zeros(2, 3, C, device="cuda").bfloat16(), cu=torch.tensor([0, T], dtype=torch.int32, device="cuda"),
-                    ab=torch.randn(T, 2 * hv, device="cuda", generator=g).bfloat16(),
-                    idx=torch.tensor([1], dtype=torch.int32, device="cuda"), ctx=torch.tensor([5], dtype=torch.int32, device="cuda"),
-                    q=torch.empty(T, hk, 128, device="cuda").bfloat16(), k=torch.empty(T, hk, 128, device="cuda").bfloat16(),
-                    v=torch.empty(T, hv, 128, device="cuda").bfloat16(), g=torch.empty(T, hv, device="cuda"),
-                    be=torch.empty(T, hv, device="cuda"))
-        k = keep
-        tens = [t(k["x"]), t(k["w"]), abi.absent(), t(k["al"]), t(k["dt"]), t(k["st"]), t(k["cu"]),
-                abi.tensor(abi.BF16, [T, hv], k["ab"].data_ptr(), [2 * hv, 1]),
-                abi.tensor(abi.BF16, [T, hv], k["ab"].data_ptr() + 2 * hv, [2 * hv, 1]),
-                t(k["idx"]), t(k["ctx"]), t(k["q"]), t(k["k"]), t(k["v"]), t(k["g"]), t(k["be"])]
-        params = [abi.pint("M", T), abi.pint("n_head_k", hk), abi.pint("n_head_v", hv), abi.pint("head_k", 128),
-                  abi.pint("head_v", 128), abi.pint("conv", 4)]
-    elif op == "ridgefill_attn_kv_fill":
-        hkv = 2
-        keep = dict(k=torch.randn(T, hkv, 256, device="cuda", generator=g).bfloat16(),
-                    v=torch.randn(T, hkv, 256, device="cuda", generator=g).bfloat16(),
-                    w=torch.ones(256, device="cuda").bfloat16(),
-                    pos=(torch.arange(3 * T, dtype=torch.int32, device="cuda") % 30000).view(3, T),
-                    slots=torch.randperm(T + 1000, device="cuda", generator=g)[:T].int(),
-                    cache=torch.zeros(2, T + 1000, hkv, 256, device="cuda").bfloat16())
-        k = keep
-        tens = [t(k["k"]), t(k["v"]), t(k["w"]), t(k["pos"]), t(k["slots"]), t(k["cache"]), abi.absent()]
-        params = [abi.pint("M", T), abi.pint("n_head_kv", hkv), abi.pint("head_dim", 256), abi.pint("rope_dim", 64),
-                  abi.pf64("rope_theta", 1e7), abi.pstr("rope_mode", "imrope"), abi.pstr("rope_sections", "11,11,10")]
-    else:
-        return None
-    return lib.find_row(op, abi.DOMAIN_DEVICE), tens, params, keep
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            p.run(stream.cuda_stream)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        stream.synchronize()
+        a.record(stream)
+        for _ in range(steps):
+            p.run(stream.cuda_stream)
+        b.record(stream)
+        stream.synchronize()
+    ms = a.elapsed_time(b) / steps
+    s = p.s
+    return {"workload": f"BASELINE config 5: prompts of {list(s.lengths)} rows, the last approximated, the 24 late "
+                        f"layers; the fill over every sequence (varlen)", "rows": s.T, "ms_per_step": ms,
+            "tokens_per_s": s.T / (ms * 1e-3)}
+
+
+def time_one_layer(stream, steps: int) -> dict:
+    import torch
+    import ridgefill_step as RS
+    step = RS.Step(RS.StepShape(T=T_FULL), device="cuda", seed=1234)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            step.run(stream.cuda_stream)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        stream.synchronize()
+        a.record(stream)
+        for _ in range(steps):
+            step.run(stream.cuda_stream)
+        b.record(stream)
+        stream.synchronize()
+    ms = a.elapsed_time(b) / steps
+    return {"workload": "one late layer: projector d 2,048 + DeltaNet fill (config 2 shapes, inputs given) + mask, "
+                        "select, correction, rho, hazard", "rows": T_FULL, "ms_per_step": ms,
+            "tokens_per_s": T_FULL / (ms * 1e-3)}
 
 
 def run_only(args):
-    """Launch one op of the pass repeatedly at --rows rows (after --warmup full passes that fill its
-    inputs), or one of the rows beside the pass (ridgefill_gdn_conv_prep, ridgefill_attn_kv_fill) on synthetic
-    operands: a small, self-contained command for an ncu capture of that op's kernels."""
+    """Launch only one row's launches of the pass (every launch of it, in the pass's order), after --warmup whole
+    passes that fill their inputs, at --rows rows and --layers late layers: a small, self-contained command for an
+    ncu capture of that row's kernels."""
     import torch
-    import ridgefill_step as RS
-    side = side_op_call(args.only, args.rows)
-    if side is not None:
-        row, tens, params, keep = side
-        import ridgefill_abi as abi
-        lib = abi.product()
-        stream = torch.cuda.Stream()
+    import late_pass as LP
+    shape = LP.LateShape(T=args.rows, layers=args.layers)
+    p = LP.LatePass(shape, "cuda", seed=1234)
+    calls = [c for c in p.calls if c[0] == args.only]
+    if not calls:
+        raise SystemExit(f"--only {args.only}: not a row of the pass")
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
         for _ in range(args.warmup):
-            if lib.launch(row, tens, params, stream=stream.cuda_stream) != 0:
-                raise SystemExit(f"{args.only}: refused")
+            p.run(stream.cuda_stream)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         stream.synchronize()
         a.record(stream)
         for _ in range(args.steps):
-            if lib.launch(row, tens, params, stream=stream.cuda_stream) != 0:
-                raise SystemExit(f"{args.only}: refused")
+            for op, r, tens, params, _tag in calls:
+                p._launch(op, r, tens, params, stream.cuda_stream)
         b.record(stream)
         stream.synchronize()
-        print(json.dumps({"op": args.only, "rows": args.rows, "launches": args.steps,
-                          "ms_per_launch": a.elapsed_time(b) / args.steps}), flush=True)
-        del keep
-        return
-    step = RS.Step(RS.StepShape(T=args.rows), device="cuda", seed=1234)
-    stream = torch.cuda.Stream()
-    calls = [c for c in step._args if c[0] == args.only]
-    if not calls:
-        raise SystemExit(f"--only {args.only}: not an op of the pass")
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            step.run(stream.cuda_stream)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        stream.synchronize()
-        a.record()
-        for _ in range(args.steps):
-            for name, r, tens, params in calls:
-                sb = step.gdn_scratch if name == "ridgefill_gdn_fill" else 0
-                rc = step.lib.launch(r, tens, params, stream=stream.cuda_stream,
-                                     scratch=step.scratch.data_ptr() if sb else None, scratch_bytes=sb)
-                if rc != 0:
-                    raise SystemExit(f"{name}: rc {rc}")
-        b.record()
-        stream.synchronize()
-    print(json.dumps({"op": args.only, "rows": args.rows, "launches": args.steps * len(calls),
+    print(json.dumps({"op": args.only, "rows": args.rows, "layers": args.layers, "launches": args.steps * len(calls),
                       "ms_per_launch": a.elapsed_time(b) / (args.steps * len(calls))}), flush=True)
-
-
-def Step_launches(step) -> int:
-    return step.LAUNCHES_PER_PASS
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
-    ap.add_argument("--only", default=None, help="profile mode: launch only this op of the pass, or ridgefill_gdn_conv_prep / ridgefill_attn_kv_fill on synthetic operands")
+    ap.add_argument("--no-extra", action="store_true", help="skip the config-5 and one-layer extras")
+    ap.add_argument("--only", default=None, help="profile mode: launch only this row's launches of the pass")
     ap.add_argument("--rows", type=int, default=T_FULL, help="rows of the chunk in --only mode")
+    ap.add_argument("--layers", default="GGGA" * 6, help="late layers in --only mode (G DeltaNet, A attention)")
     args = ap.parse_args()
     if args.only:
         run_only(args)

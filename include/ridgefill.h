@@ -440,9 +440,10 @@ int ridgefill_wait_selftest(int* flag, int* status, RadStream s);
  * its own, or an engine step whose memory is fixed before the pass and which may not cudaMalloc inside
  * it. Same operands as the row; RadArgs::scratch is ignored and a 64 MiB workspace compiled into the
  * library is used instead (held on every GPU that loads the library until exit). RAD_E_SHAPE when the
- * call needs more than 64 MiB (a one-sequence 2,048-row call at up to 40 value heads fits). The first
- * call on a device resolves the workspace's address there: make it before any stream capture. Calls
- * share the workspace: calls that overlap on the GPU race. Allocates and frees nothing. */
+ * call needs more than 64 MiB: a one-sequence 2,048-row call fits at up to 40 value heads for the state
+ * alone, at up to 19 with the output o. The first call on a device resolves the workspace's address there
+ * (again after the device's context changes, e.g. after cudaDeviceReset): make it before any stream
+ * capture. Calls share the workspace: calls that overlap on the GPU race. Allocates and frees nothing. */
 int ridgefill_gdn_fill_noalloc(const RadArgs* a, RadStream s);
 
 /* ridgefill_gdn_fill's scratch hook: device bytes the row needs in RadArgs::scratch. */

@@ -27,12 +27,22 @@ ORACLE_SO = ROOT / "oracle" / "_build" / "libridgefill_oracle.so"
 REF_SO = ROOT / "oracle" / "_ref" / "ridgefill_ref.so"
 
 
+def host_cores() -> int:
+    """The host threads this process may run on (its CPU affinity), whatever OMP_NUM_THREADS says."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def load():
-    """(rows plugin, kind, oracle plugin): the reference's host rows when built, else the restatement."""
-    if not ORACLE_SO.exists():
+    """(rows plugin, kind, oracle plugin): the reference's host rows when built, else the restatement. The
+    restatement's OpenMP loops are given every host core."""
+    if not ORACLE_SO.exists() or ORACLE_SO.stat().st_mtime < (ROOT / "oracle" / "ridgefill_oracle.cpp").stat().st_mtime:
         subprocess.run(["make", "-s", "-C", str(ROOT / "oracle"), "all"], check=True)
     oracle = abi.Plugin(ORACLE_SO)
     bind(oracle.lib)
+    oracle.lib.oracle_set_threads(host_cores())
     if REF_SO.exists():
         return abi.Plugin(REF_SO), "reference", oracle
     return oracle, "port", oracle
@@ -49,6 +59,7 @@ def bind(lib):
     for f in (lib.oracle_gdn_fill_f32, lib.oracle_gdn_fill_f64):
         f.argtypes = [P, P, P, P, P, P, P, i64, i64, P, i64, P, i64, i64, i64, i64, C.c_float, i64, i64]
     lib.oracle_threads.restype = C.c_int
+    lib.oracle_set_threads.argtypes = [C.c_int]
 
 
 def _bf16(x: np.ndarray) -> np.ndarray:

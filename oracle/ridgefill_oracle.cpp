@@ -744,4 +744,14 @@ int oracle_threads(void) {
 #endif
 }
 
+/* Sets the OpenMP thread count of the oracle's parallel loops (a launcher such as torchrun sets
+ * OMP_NUM_THREADS=1 in every process it starts; the CPU baseline asks for the host's cores itself). */
+void oracle_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
 }  // extern "C"

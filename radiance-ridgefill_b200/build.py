@@ -22,7 +22,7 @@ CSRC = HERE / "csrc"
 OUT = HERE / "ridgefill.so"
 BUILD = HERE / "_build"
 
-CUDA_SOURCES = ["small_ops.cu", "mask.cu", "gemm_q.cu", "gdn.cu", "conv_prep.cu", "attn_kv.cu"]
+CUDA_SOURCES = ["small_ops.cu", "mask.cu", "gemm_q.cu", "gdn.cu", "conv_prep.cu", "attn_kv.cu", "peer.cu"]
 HOST_SOURCES = ["parse.cpp", "rows.cpp", "folder.cpp"]
 HEADERS = ["common.cuh", "sm100.cuh", "mma.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -42,7 +42,7 @@ def host_cxx() -> str:
 def _inputs() -> list[Path]:
     inc = ROOT / "include"
     return ([CSRC / s for s in CUDA_SOURCES + HOST_SOURCES + HEADERS] +
-            [inc / h for h in ("rad_abi.h", "rad_plugin.h", "ridgefill.h", "ridgefill_schemas.h", "ridgefill_folder.h")] + [Path(__file__)])
+            [inc / h for h in ("rad_abi.h", "rad_plugin.h", "ridgefill.h", "ridgefill_schemas.h", "ridgefill_folder.h", "ridgefill_team.h")] + [Path(__file__)])
 
 
 def up_to_date() -> bool:

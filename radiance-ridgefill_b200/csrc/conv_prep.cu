@@ -82,6 +82,14 @@ __device__ __forceinline__ uint4 window_row(const RidgeFillConvPrep& g, int64_t 
 
 /* A warp takes kRows rows of a pair of 128-channel head columns (2 j, 2 j + 1; the pair is q / k or v alike,
  * as 2 Hk is even): half-warp hw owns column 2 j + hw, lane l of the half channels 8 l..8 l + 7. */
+/* SiLU u / (1 + e^-u) with the fast exp and divide (well inside bf16's rounding), except where the fast divide
+ * returns 0: a denominator above 2^126 (u below about -87.3, where the value is about u e^u, under 1e-36 in
+ * magnitude) takes the exact division, so those rows keep their tiny values as the f32 rule gives them. */
+__device__ __forceinline__ float silu(float u) {
+    const float den = 1.0f + __expf(-u);
+    return den < 0x1p126f ? __fdividef(u, den) : u / den;
+}
+
 __global__ void __launch_bounds__(kThreads) conv_prep_kernel(RidgeFillConvPrep g) {
     extern __shared__ uint4 rows_smem[];   /* [warp][kRows][lane] */
     const int lane = threadIdx.x & 31, hw = lane >> 4, hl = lane & 15;
@@ -140,8 +148,8 @@ __global__ void __launch_bounds__(kThreads) conv_prep_kernel(RidgeFillConvPrep g
                 rf::fma2_rn(u0, u1, wt[e][1], wt[e + 1][1], w1[e], w1[e + 1]);
                 rf::fma2_rn(u0, u1, wt[e][2], wt[e + 1][2], w2[e], w2[e + 1]);
                 rf::fma2_rn(u0, u1, wt[e][3], wt[e + 1][3], cur[e], cur[e + 1]);
-                y[e] = __fdividef(u0, 1.0f + __expf(-u0));   /* SiLU; fast exp and divide: well inside bf16's rounding */
-                y[e + 1] = __fdividef(u1, 1.0f + __expf(-u1));
+                y[e] = silu(u0);
+                y[e + 1] = silu(u1);
             }
             if (norm) {
                 float ss = 0.0f;

@@ -1460,16 +1460,20 @@ int gdn_device_error(int reset) { return read_device_error(reset); }
  * every stream of the step). This entry point takes the same operands as the ridgefill_gdn_fill row,
  * ignores RadArgs::scratch, and uses instead a workspace compiled into the library: a file-scope device
  * array of kNoAllocScratchBytes (64 MiB), which every GPU that loads the library holds until the
- * process exits. 64 MiB holds the fill's workspace (48.5 KiB per 64-row chunk and value head, one chunk
- * more per sequence) for a one-sequence 2,048-row call -- the engine's default chunk -- at up to 40 value
- * heads, or a 4,096-row call at up to 20; a call that needs more returns RAD_E_SHAPE and launches nothing.
+ * process exits. The fill's workspace is 48.5 KiB per 64-row chunk and value head (one chunk more per
+ * sequence), plus 52 KiB more per chunk and head when the output o is asked for. So 64 MiB holds a
+ * one-sequence 2,048-row call -- the engine's default chunk -- at up to 40 value heads for the state
+ * alone, or up to 19 value heads with o; a 4,096-row call at up to 20 (state only). Heads of at most 64
+ * dims need no workspace at all. A call that needs more returns RAD_E_SHAPE and launches nothing.
  *
- * The first call on each device resolves the array's device address there (cudaGetSymbolAddress, once
- * per device, with that device current); make that first call before any stream capture. No call
- * allocates or frees device memory. Every call shares the one array and the array keeps the last call's
- * contents: nothing in it needs to start at zero (each call writes every byte of the workspace it reads
- * before reading it, in stream order), but two calls that overlap on the GPU -- on different streams,
- * or from different threads, without an ordering between them -- race on it.
+ * The first call on each device resolves the array's device address there (cudaGetSymbolAddress, with
+ * that device current), and again whenever the device's current context is not the one it was resolved
+ * in (after a cudaDeviceReset the library's module is loaded anew and the array may move); make that first
+ * call before any stream capture. No call allocates or frees device memory. Every call shares the one
+ * array and the array keeps the last call's contents: nothing in it needs to start at zero (each call
+ * writes every byte of the workspace it reads before reading it, in stream order), but two calls that
+ * overlap on the GPU -- on different streams, or from different threads, without an ordering between
+ * them -- race on it.
  */
 namespace {
 constexpr int64_t kNoAllocScratchBytes = 64ll << 20;
@@ -1480,19 +1484,43 @@ static __device__ __align__(256) uint8_t g_gdn_noalloc_scratch[kNoAllocScratchBy
 
 namespace {
 std::mutex g_noalloc_mutex;
-void* g_noalloc_address[kNoAllocMaxDevices];
+struct NoAllocEntry {
+    void* context;   /* the driver context the address was resolved in */
+    void* address;
+};
+NoAllocEntry g_noalloc[kNoAllocMaxDevices];
 
-/* The array's device address on the current device; resolved on the first call there. */
+/* The current driver context (cuCtxGetCurrent through the runtime's entry-point query); null when there is
+ * none yet or the query is unavailable. */
+void* current_context() {
+    typedef int (*CtxGetCurrent)(void**);
+    static CtxGetCurrent fn = nullptr;
+    if (!fn) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (CtxGetCurrent)f;
+    }
+    void* ctx = nullptr;
+    return fn && fn(&ctx) == 0 ? ctx : nullptr;
+}
+
+/* The array's device address on the current device, resolved on the first call there and again when the
+ * device's context changed. */
 int noalloc_workspace(void** out) {
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) return RAD_E_DEVICE;
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (!g_noalloc_address[dev]) {
+    NoAllocEntry& e = g_noalloc[dev];
+    void* ctx = current_context();
+    if (!e.address || !ctx || ctx != e.context) {
         void* ptr = nullptr;
         if (cudaGetSymbolAddress(&ptr, g_gdn_noalloc_scratch) != cudaSuccess || !ptr) return RAD_E_DEVICE;
-        g_noalloc_address[dev] = ptr;
+        e.address = ptr;
+        e.context = current_context();   /* the resolution above made the context current if there was none */
     }
-    *out = g_noalloc_address[dev];
+    *out = e.address;
     return RAD_OK;
 }
 }   // namespace

@@ -794,7 +794,7 @@ extern "C" int ridgefill_quant_act_device(const RadArgs* a, RadStream s) {
 /* The first device-side wait error any kernel of this library recorded (0: none), optionally
  * clearing it. Synchronises the current device: a diagnostic, never called on the launch path. */
 extern "C" int ridgefill_device_error(int reset) {
-    const int gemm = rf::read_device_error(reset), fill = rf::gdn_device_error(reset);
-    if (gemm < 0 || fill < 0) return -1;
-    return gemm ? gemm : fill;
+    const int gemm = rf::read_device_error(reset), fill = rf::gdn_device_error(reset), team = rf::peer_device_error(reset);
+    if (gemm < 0 || fill < 0 || team < 0) return -1;
+    return gemm ? gemm : fill ? fill : team;
 }

@@ -33,6 +33,7 @@ static inline int read_device_error(int reset) {
 
 /* The DeltaNet fill's copy (gdn.cu). */
 int gdn_device_error(int reset);
+int peer_device_error(int reset);
 
 enum DeviceError : int {
     kErrNone = 0,

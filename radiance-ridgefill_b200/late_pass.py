@@ -186,26 +186,153 @@ def _t(t, shape=None, strides=None, offset_elems=0, dtype=None):
                       t.data_ptr() + offset_elems * t.element_size(), list(t.stride()) if strides is None else strides)
 
 
+# ============================================================================ tensor parallelism over one prompt
+
+class Team:
+    """The ranks of a tensor-parallel pass over one prompt (one process per GPU, torch.distributed for the
+    rendezvous only): this rank, the world, and the mapping of device buffers across processes. A buffer is
+    shared by `share`: every rank exports its own (CUDA IPC, ridgefill_peer_export) and maps everyone else's,
+    and gets back the list of every rank's pointer as seen from here."""
+
+    def __init__(self, world: int, rank: int, dist=None):
+        self.world, self.rank, self.dist = world, rank, dist
+        self.lib = abi.product().lib
+        self._mapped = []   # (pointer, offset) pairs to unmap on close
+
+    @classmethod
+    def create(cls, world: int, rank: int, dist):
+        return cls(world, rank, dist)
+
+    def share(self, t) -> list[int]:
+        """Every rank's pointer to its copy of the buffer `t` (one allocation per rank, the same shape
+        everywhere), as device addresses valid in this process."""
+        import ctypes as C
+        L = self.lib
+        L.ridgefill_peer_export.argtypes = [C.c_void_p, C.c_void_p, C.POINTER(C.c_int64)]
+        L.ridgefill_peer_import.argtypes = [C.c_void_p, C.c_int64, C.POINTER(C.c_void_p)]
+        handle = (C.c_uint8 * 64)()
+        off = C.c_int64(0)
+        if L.ridgefill_peer_export(C.c_void_p(t.data_ptr()), handle, C.byref(off)) != abi.OK:
+            raise RuntimeError("ridgefill_peer_export failed")
+        mine = (bytes(handle), off.value)
+        everyone = [None] * self.world
+        self.dist.all_gather_object(everyone, mine)
+        ptrs = []
+        for r, (h, o) in enumerate(everyone):
+            if r == self.rank:
+                ptrs.append(t.data_ptr())
+                continue
+            buf = (C.c_uint8 * 64).from_buffer_copy(h)
+            out = C.c_void_p(0)
+            if L.ridgefill_peer_import(buf, C.c_int64(o), C.byref(out)) != abi.OK:
+                raise RuntimeError(f"ridgefill_peer_import of rank {r}'s buffer failed")
+            self._mapped.append((out.value, o))
+            ptrs.append(out.value)
+        return ptrs
+
+    def close(self):
+        import ctypes as C
+        L = self.lib
+        L.ridgefill_peer_release.argtypes = [C.c_void_p, C.c_int64]
+        for ptr, o in self._mapped:
+            L.ridgefill_peer_release(C.c_void_p(ptr), C.c_int64(o))
+        self._mapped = []
+
+
+def attn_heads(hkv: int, rank: int, world: int) -> tuple[int, int]:
+    """The attention kv heads [h0, h1) rank `rank` of `world` holds: an even split when world divides hkv, else one
+    head each to the first hkv ranks and none to the others (ranks with no attention cache)."""
+    if hkv % world == 0:
+        per = hkv // world
+        return rank * per, (rank + 1) * per
+    return (rank, rank + 1) if rank < hkv else (0, 0)
+
+
+def local_inputs(s: LateShape, x: dict, team: Team | None) -> tuple[dict, dict]:
+    """This rank's slices of the pass's weights and inputs (the whole of them without a team), and the rank's
+    geometry: the value and k heads of its DeltaNet span (shard.head_span, the reference's spans), its attention kv
+    heads and its block of projector output columns. Every slice is a contiguous copy, so each rank's rows read
+    operands laid out as a one-rank pass's are."""
+    import torch
+    import shard
+    if team is None or team.world == 1:
+        geo = {"v": (0, s.hv), "k": (0, s.hk), "a": (0, s.hkv), "cols": (0, s.d), "world": 1, "rank": 0}
+        return x, geo
+    world, rank = team.world, team.rank
+    (v0, v1), (k0, k1) = shard.head_span(s.hk, s.hv, rank, world)
+    a0, a1 = attn_heads(s.hkv, rank, world)
+    if s.d % world or (s.d // world) % 16:
+        raise ValueError(f"d {s.d} does not split into 16-column blocks over {world} ranks")
+    c0, c1 = rank * s.d // world, (rank + 1) * s.d // world
+    geo = {"v": (v0, v1), "k": (k0, k1), "a": (a0, a1), "cols": (c0, c1), "world": world, "rank": rank}
+    D, hk, hv, G = s.head, s.hk, s.hv, s.n_gdn
+    dev = x["h_s"].device
+    y = dict(x)
+    y["w_proj"] = [w[c0:c1].contiguous() for w in x["w_proj"]]
+    y["s_proj"] = [t[:, c0:c1].contiguous() for t in x["s_proj"]]
+    y["b_proj"] = [t[c0:c1].contiguous() for t in x["b_proj"]]
+    heads_v = torch.cat([torch.arange(j * hv + v0, j * hv + v1) for j in range(G)]).to(dev)
+    heads_k = torch.cat([torch.arange(j * hk + k0, j * hk + k1) for j in range(G)]).to(dev)
+    y["state"] = x["state"][:, heads_v].contiguous()
+    y["C"] = x["C"][heads_v].contiguous()
+    if s.block_inputs:
+        ch = torch.cat([torch.arange(k0 * D, k1 * D), torch.arange((hk + k0) * D, (hk + k1) * D),
+                        torch.arange((2 * hk + v0) * D, (2 * hk + v1) * D)]).to(dev)
+        ab_rows = torch.cat([torch.arange(v0, v1), torch.arange(hv + v0, hv + v1)]).to(dev)
+        y["w_in"] = [w[ch].contiguous() for w in x["w_in"]]
+        y["s_in"] = [t[:, ch].contiguous() for t in x["s_in"]]
+        y["w_conv"] = [w[ch].contiguous() for w in x["w_conv"]]
+        y["conv_state"] = [t[:, :, ch].contiguous() for t in x["conv_state"]]
+        y["w_ab"] = [w[ab_rows].contiguous() for w in x["w_ab"]]
+    else:
+        y["k"] = x["k"][:, heads_k].contiguous()
+        y["v"] = x["v"][:, heads_v].contiguous()
+        y["g"] = x["g"][:, heads_v].contiguous()
+        y["beta"] = x["beta"][:, heads_v].contiguous()
+        ab_cols = torch.cat([torch.arange(v0, v1), torch.arange(hv + v0, hv + v1)]).to(dev)
+        y["ab"] = [t[:, ab_cols].contiguous() for t in x["ab"]]
+    y["a_log"] = [t[v0:v1].contiguous() for t in x["a_log"]]
+    y["dt_bias"] = [t[v0:v1].contiguous() for t in x["dt_bias"]]
+    if s.n_attn:
+        Dh, Ha = s.head_attn, s.hkv
+        rows_kv = torch.cat([torch.arange(a0 * Dh, a1 * Dh), torch.arange((Ha + a0) * Dh, (Ha + a1) * Dh)]).to(dev)
+        y["w_kv"] = [w[rows_kv].contiguous() for w in x["w_kv"]]
+        y["s_kv"] = [t[:, rows_kv].contiguous() for t in x["s_kv"]]
+    return y, geo
+
+
 class LatePass:
-    """The buffers of one approximate pass over the late layers and the row launches that fill them."""
+    """The buffers of one approximate pass over the late layers and the row launches that fill them, on one GPU or
+    as one rank of a tensor-parallel team (`team`): the rank's DeltaNet value heads (with their k heads), its
+    attention kv heads and its block of each projector's output columns, the blocks gathered into every rank's
+    block input by the library's peer kernels. Each rank's state, decay sums and caches are then its heads' slices
+    of the one-GPU pass's, bit for bit."""
 
     # kernels a launch of each row starts (the fill: its sequence plan and the fused kernel; the per-row
     # form for small heads is one kernel)
     KERNELS = {"ridgefill_mask": 1, "ridgefill_quant_act_i8g": 1, "ridgefill_gemm_nt_q_bias": 1, "ridgefill_select": 1,
                "ridgefill_gemm_nt_bias": 1, "ridgefill_gdn_conv_prep": 2, "ridgefill_attn_kv_fill": 1,
-               "ridgefill_state_correct": 1, "ridgefill_gdn_fill": 2, "ridgefill_rho_update": 1, "ridgefill_hazard": 1}
+               "ridgefill_state_correct": 1, "ridgefill_gdn_fill": 2, "ridgefill_rho_update": 1, "ridgefill_hazard": 1,
+               "team_barrier": 1, "gather_columns": 1, "team_wait": 1}
 
-    def __init__(self, shape: LateShape, device: str = "cuda", seed: int = 0, inputs: dict | None = None):
+    def __init__(self, shape: LateShape, device: str = "cuda", seed: int = 0, inputs: dict | None = None,
+                 team: Team | None = None):
         import torch
         self.torch = torch
         self.s = s = shape
         self.lib = abi.product()
         dev = torch.device(device)
+        self.dev = dev
+        self.team = team if team is not None and team.world > 1 else None
         self.inp = inputs if inputs is not None else late_inputs(s, dev, seed)
-        x = self.inp
+        self.w, self.geo = local_inputs(s, self.inp, self.team)
+        x = self.w
         T, d, G, D = s.T, s.d, s.n_gdn, s.head
         grp = s.group or d
         self.grp = grp
+        (v0, v1), (k0, k1), (a0, a1), (c0, c1) = self.geo["v"], self.geo["k"], self.geo["a"], self.geo["cols"]
+        self.hv_r, self.hk_r, self.hkv_r, self.cols = v1 - v0, k1 - k0, a1 - a0, c1 - c0
+        hv, hk = self.hv_r, self.hk_r
 
         def empty(*sz, dtype):
             return torch.empty(*sz, dtype=dtype, device=dev)
@@ -215,125 +342,151 @@ class LatePass:
         self.bounds = torch.zeros(4, dtype=torch.int32, device=dev)
         self.codes_h = empty(T, d, dtype=torch.int8)
         self.scale_h = empty(T, d // grp, dtype=torch.float32)
-        self.x_proj = empty(T, d, dtype=torch.bfloat16)
-        self.x = [t.clone() for t in x["x_exact"]]           # each layer's block input, the select writes into it
+        self.x_proj = empty(T, self.cols, dtype=torch.bfloat16)
+        # every layer's block input, one allocation (mapped by the team's peers), the exact rows copied in
+        self.x_all = torch.stack(self.inp["x_exact"])
+        self.x = list(self.x_all.unbind(0))
         self.codes_x = empty(T, d, dtype=torch.int8)
         self.scale_x = empty(T, d // grp, dtype=torch.float32)
         self.state = x["state"].clone()
-        self.applied = torch.zeros(s.n_seq, G * s.hv, 1, 1, dtype=torch.float32, device=dev)
-        self.nd = torch.zeros(s.n_seq, G * s.hv, 1, 2, dtype=torch.float32, device=dev)
+        self.applied = torch.zeros(s.n_seq, G * hv, 1, 1, dtype=torch.float32, device=dev)
+        self.nd = torch.zeros(s.n_seq, G * hv, 1, 2, dtype=torch.float32, device=dev)
         self.meta = torch.zeros(s.n_seq, 1, 1, 2, dtype=torch.float32, device=dev)
         self.count = torch.zeros(1, dtype=torch.float32, device=dev)
         self.slot_last = torch.tensor([[s.n_seq - 1]], dtype=torch.int32, device=dev)   # the approximated sequence
         self.slots_all = torch.arange(s.n_seq, dtype=torch.int32, device=dev).view(-1, 1)
+        self.conv_dim_r = 2 * hk * D + hv * D
         if s.block_inputs:
-            C = s.conv_dim
+            C = self.conv_dim_r
             self.mixed = empty(T, C, dtype=torch.bfloat16)
-            self.ab = [empty(T, 2 * s.hv, dtype=torch.bfloat16) for _ in range(G)]
-            self.q = empty(T, s.hk, D, dtype=torch.bfloat16)   # the state-only fill reads no q: one buffer for all
-            self.k = empty(T, G * s.hk, D, dtype=torch.bfloat16)
-            self.v = empty(T, G * s.hv, D, dtype=torch.bfloat16)
-            self.g = empty(T, G * s.hv, dtype=torch.float32)
-            self.beta = empty(T, G * s.hv, dtype=torch.float32)
+            self.ab = [empty(T, 2 * hv, dtype=torch.bfloat16) for _ in range(G)]
+            self.q = empty(T, hk, D, dtype=torch.bfloat16)   # the state-only fill reads no q: one buffer for all
+            self.k = empty(T, G * hk, D, dtype=torch.bfloat16)
+            self.v = empty(T, G * hv, D, dtype=torch.bfloat16)
+            self.g = empty(T, G * hv, dtype=torch.float32)
+            self.beta = empty(T, G * hv, dtype=torch.float32)
             self.conv_state = [t.clone() for t in x["conv_state"]]
-            self.zero_ab = torch.zeros(2 * s.hv, dtype=torch.bfloat16, device=dev)
+            self.zero_ab = torch.zeros(2 * hv, dtype=torch.bfloat16, device=dev)
             self.ctx = torch.zeros(s.n_seq, dtype=torch.int32, device=dev)   # fresh prompts: no conv history
         else:
             self.ab, self.k, self.v, self.g, self.beta = x["ab"], x["k"], x["v"], x["g"], x["beta"]
-        if s.n_attn:
-            Ha, Dh = s.hkv, s.head_attn
-            self.kv = empty(T, 2 * Ha * Dh, dtype=torch.bfloat16)
-            self.cache = [torch.zeros(2, T + 1024, Ha, Dh, dtype=torch.bfloat16, device=dev) for _ in range(s.n_attn)]
-            self.rope_pos = x["positions"].view(1, T).expand(3, T).contiguous()   # text rows: every plane the index
+        self.cache = []
+        if s.n_attn and self.hkv_r:
+            Dh = s.head_attn
+            self.kv = empty(T, 2 * self.hkv_r * Dh, dtype=torch.bfloat16)
+            self.cache = [torch.zeros(2, T + 1024, self.hkv_r, Dh, dtype=torch.bfloat16, device=dev) for _ in range(s.n_attn)]
+            self.rope_pos = self.inp["positions"].view(1, T).expand(3, T).contiguous()   # text rows: every plane the index
+        self.epoch = 0
+        if self.team is not None:
+            L = len(s.layers)
+            # counters: one slot a layer (its gathered block input), then the pass barrier's
+            self.counters = torch.zeros(L + 1, dtype=torch.int64, device=dev)
+            self.peer_x = self.team.share(self.x_all)
+            self.peer_flags = self.team.share(self.counters)
+            self.comm = torch.cuda.Stream(device=dev)
         self._build()
         self.scratch = torch.empty(max(self.fill_scratch, 16), dtype=torch.uint8, device=dev)
 
     # --------------------------------------------------------------- the launch list
     def _build(self):
-        s, x = self.s, self.inp
+        s, x, inp = self.s, self.w, self.inp
         P, S, F = abi.pint, abi.pstr, abi.pf64
         A_ = abi.absent()
-        T, d, G, hk, hv, D = s.T, s.d, s.n_gdn, s.hk, s.hv, s.head
+        T, d, G, D = s.T, s.d, s.n_gdn, s.head
+        hk, hv = self.hk_r, self.hv_r
         row = lambda op: self.lib.find_row(op, abi.DOMAIN_DEVICE)   # noqa: E731
-        calls = []
+        c0 = self.geo["cols"][0]
+        head, layers, tail = [], [], []   # the pass's launches: before the layers, per layer (list), after
 
-        def add(op, tens, params, tag=""):
-            calls.append((op, row(op), tens, params, tag))
+        def call(op, tens, params, tag=""):
+            return (op, row(op), tens, params, tag)
 
         def gemm_q(a, sa, w, sw, bias, y, N, tag):
-            add("ridgefill_gemm_nt_q_bias", [_t(a), _t(sa), _t(w), _t(sw), A_ if bias is None else _t(bias), y, A_],
-                [P("M", T), P("N", N), P("K", d), P("group", self.grp), S("dtype", "i8a8")], tag)
+            return call("ridgefill_gemm_nt_q_bias", [_t(a), _t(sa), _t(w), _t(sw), A_ if bias is None else _t(bias), y, A_],
+                        [P("M", T), P("N", N), P("K", d), P("group", self.grp), S("dtype", "i8a8")], tag)
 
         def quant(src, codes, scale, tag):
-            add("ridgefill_quant_act_i8g", [_t(src), _t(codes), _t(scale)],
-                [P("M", T), P("n", d), P("group", self.grp), S("dtype", "bf16")], tag)
+            return call("ridgefill_quant_act_i8g", [_t(src), _t(codes), _t(scale)],
+                        [P("M", T), P("n", d), P("group", self.grp), S("dtype", "bf16")], tag)
 
         def correct(mode):
             tens = [_t(self.state), _t(self.slot_last), _t(self.applied), _t(self.slot_last), _t(x["C"])]
             tens += [_t(self.nd), _t(self.slot_last)] if mode == "apply" else [A_, A_]
-            add("ridgefill_state_correct", tens + [_t(self.bounds)],
-                [P("M", 1), S("mode", mode), F("alpha", s.alpha), P("n_head", G * hv), P("sd0", D), P("sd1", D)], mode)
+            return call("ridgefill_state_correct", tens + [_t(self.bounds)],
+                        [P("M", 1), S("mode", mode), F("alpha", s.alpha), P("n_head", G * hv), P("sd0", D), P("sd1", D)], mode)
 
-        add("ridgefill_mask", [_t(x["cu_last"]), _t(x["token_ids"]), _t(x["positions"]), _t(x["score"]), _t(self.mask),
-                               _t(self.bounds), A_],
-            [P("M", T), F("share", s.share), P("seed", 0), S("mode", "class")])
-        quant(x["h_s"], self.codes_h, self.scale_h, "h_S")
+        head.append(call("ridgefill_mask", [_t(inp["cu_last"]), _t(inp["token_ids"]), _t(inp["positions"]), _t(inp["score"]),
+                                            _t(self.mask), _t(self.bounds), A_],
+                         [P("M", T), F("share", s.share), P("seed", 0), S("mode", "class")]))
+        head.append(quant(inp["h_s"], self.codes_h, self.scale_h, "h_S"))
         if G:
-            correct("undo")
+            head.append(correct("undo"))
         gi = ai = 0
         for li, kind in enumerate(s.layers):
-            gemm_q(self.codes_h, self.scale_h, x["w_proj"][li], x["s_proj"][li], x["b_proj"][li], _t(self.x_proj), d, f"proj {li}")
-            add("ridgefill_select", [_t(self.mask), _t(self.x_proj), A_, A_, _t(self.x[li]), A_, A_], [P("M", T)], f"{li}")
+            proj = [gemm_q(self.codes_h, self.scale_h, x["w_proj"][li], x["s_proj"][li], x["b_proj"][li], _t(self.x_proj),
+                           self.cols, f"proj {li}"),
+                    call("ridgefill_select", [_t(self.mask), _t(self.x_proj), A_, A_,
+                                              _t(self.x[li], [T, self.cols], list(self.x[li].stride()), offset_elems=c0),
+                                              A_, A_], [P("M", T)], f"{li}")]
+            block = []
             if kind == "G" and s.block_inputs:
-                quant(self.x[li], self.codes_x, self.scale_x, f"x {li}")
-                C = s.conv_dim
-                gemm_q(self.codes_x, self.scale_x, x["w_in"][gi], x["s_in"][gi], None, _t(self.mixed), C, f"in {li}")
-                add("ridgefill_gemm_nt_bias", [_t(self.x[li]), _t(x["w_ab"][gi]), _t(self.zero_ab), A_, _t(self.ab[gi])],
-                    [P("M", T), P("N", 2 * hv), P("K", d), S("dtype", "bf16")], f"ab {li}")
+                C = self.conv_dim_r
+                block.append(quant(self.x[li], self.codes_x, self.scale_x, f"x {li}"))
+                block.append(gemm_q(self.codes_x, self.scale_x, x["w_in"][gi], x["s_in"][gi], None, _t(self.mixed), C, f"in {li}"))
+                block.append(call("ridgefill_gemm_nt_bias", [_t(self.x[li]), _t(x["w_ab"][gi]), _t(self.zero_ab), A_,
+                                                             _t(self.ab[gi])],
+                                  [P("M", T), P("N", 2 * hv), P("K", d), S("dtype", "bf16")], f"ab {li}"))
                 ab = self.ab[gi]
-                add("ridgefill_gdn_conv_prep",
-                    [_t(self.mixed), _t(x["w_conv"][gi]), A_, _t(x["a_log"][gi]), _t(x["dt_bias"][gi]),
-                     _t(self.conv_state[gi]), _t(x["cu_seqlens"]), _t(ab, [T, hv], [2 * hv, 1]),
-                     _t(ab, [T, hv], [2 * hv, 1], offset_elems=hv), _t(self.slots_all.view(-1)), _t(self.ctx),
-                     _t(self.q),
-                     _t(self.k, [T, hk, D], list(self.k.stride()), offset_elems=gi * hk * D),
-                     _t(self.v, [T, hv, D], list(self.v.stride()), offset_elems=gi * hv * D),
-                     _t(self.g, [T, hv], [G * hv, 1], offset_elems=gi * hv),
-                     _t(self.beta, [T, hv], [G * hv, 1], offset_elems=gi * hv)],
-                    [P("M", T), P("n_head_k", hk), P("n_head_v", hv), P("head_k", D), P("head_v", D), P("conv", 4)], f"{li}")
-            elif kind == "A":
-                Ha, Dh = s.hkv, s.head_attn
-                quant(self.x[li], self.codes_x, self.scale_x, f"x {li}")
-                gemm_q(self.codes_x, self.scale_x, x["w_kv"][ai], x["s_kv"][ai], None, _t(self.kv), 2 * Ha * Dh, f"kv {li}")
-                add("ridgefill_attn_kv_fill",
-                    [_t(self.kv, [T, Ha, Dh], [2 * Ha * Dh, Dh, 1]),
-                     _t(self.kv, [T, Ha, Dh], [2 * Ha * Dh, Dh, 1], offset_elems=Ha * Dh), _t(x["k_norm"][ai]),
-                     _t(self.rope_pos), _t(x["slot_mapping"]), _t(self.cache[ai]), A_],
-                    [P("M", T), P("n_head_kv", Ha), P("head_dim", Dh), P("rope_dim", s.rope_dim),
-                     F("rope_theta", s.rope_theta), S("rope_mode", "imrope"),
-                     S("rope_sections", ",".join(str(v) for v in s.rope_sections))], f"{li}")
+                block.append(call("ridgefill_gdn_conv_prep",
+                                  [_t(self.mixed), _t(x["w_conv"][gi]), A_, _t(x["a_log"][gi]), _t(x["dt_bias"][gi]),
+                                   _t(self.conv_state[gi]), _t(inp["cu_seqlens"]), _t(ab, [T, hv], [2 * hv, 1]),
+                                   _t(ab, [T, hv], [2 * hv, 1], offset_elems=hv), _t(self.slots_all.view(-1)), _t(self.ctx),
+                                   _t(self.q),
+                                   _t(self.k, [T, hk, D], list(self.k.stride()), offset_elems=gi * hk * D),
+                                   _t(self.v, [T, hv, D], list(self.v.stride()), offset_elems=gi * hv * D),
+                                   _t(self.g, [T, hv], [G * hv, 1], offset_elems=gi * hv),
+                                   _t(self.beta, [T, hv], [G * hv, 1], offset_elems=gi * hv)],
+                                  [P("M", T), P("n_head_k", hk), P("n_head_v", hv), P("head_k", D), P("head_v", D),
+                                   P("conv", 4)], f"{li}"))
+            elif kind == "A" and self.hkv_r:
+                Ha, Dh = self.hkv_r, s.head_attn
+                block.append(quant(self.x[li], self.codes_x, self.scale_x, f"x {li}"))
+                block.append(gemm_q(self.codes_x, self.scale_x, x["w_kv"][ai], x["s_kv"][ai], None, _t(self.kv), 2 * Ha * Dh,
+                                    f"kv {li}"))
+                block.append(call("ridgefill_attn_kv_fill",
+                                  [_t(self.kv, [T, Ha, Dh], [2 * Ha * Dh, Dh, 1]),
+                                   _t(self.kv, [T, Ha, Dh], [2 * Ha * Dh, Dh, 1], offset_elems=Ha * Dh), _t(inp["k_norm"][ai]),
+                                   _t(self.rope_pos), _t(inp["slot_mapping"]), _t(self.cache[ai]), A_],
+                                  [P("M", T), P("n_head_kv", Ha), P("head_dim", Dh), P("rope_dim", s.rope_dim),
+                                   F("rope_theta", s.rope_theta), S("rope_mode", "imrope"),
+                                   S("rope_sections", ",".join(str(v) for v in s.rope_sections))], f"{li}"))
+            if kind == "A":
                 ai += 1
             if kind == "G":
                 gi += 1
+            layers.append((proj, block))
+        self.fill_scratch = 0
         if G:
-            add("ridgefill_gdn_fill", [A_, _t(self.k), _t(self.v), _t(self.g), _t(self.beta), _t(self.state),
-                                       _t(self.slots_all), _t(x["cu_seqlens"]), A_],
-                [P("M", T), P("n_head_k", G * hk), P("n_head_v", G * hv), P("head_k", D), P("head_v", D), P("chunk", 64)])
-            fill = calls[-1]
+            tail.append(call("ridgefill_gdn_fill", [A_, _t(self.k), _t(self.v), _t(self.g), _t(self.beta), _t(self.state),
+                                                    _t(self.slots_all), _t(inp["cu_seqlens"]), A_],
+                             [P("M", T), P("n_head_k", G * hk), P("n_head_v", G * hv), P("head_k", D), P("head_v", D),
+                              P("chunk", 64)]))
+            fill = tail[-1]
             self.fill_scratch = self.lib.scratch_bytes(fill[1], fill[2], fill[3])
             for j in range(G):
-                add("ridgefill_rho_update",
-                    [_t(self.ab[j], [T, hv], [2 * hv, 1]), _t(self.mask), _t(x["a_log"][j]), _t(x["dt_bias"][j]),
-                     _t(self.nd, [s.n_seq, hv, 1, 2], list(self.nd.stride()), offset_elems=j * hv * 2),
-                     _t(self.slot_last), _t(self.bounds)], [P("M", T), P("n_head", hv)], f"{j}")
-            correct("apply")
-        else:
-            self.fill_scratch = 0
-        add("ridgefill_hazard", [_t(x["cu_last"]), _t(x["positions"]), _t(self.bounds), A_, _t(self.meta),
-                                 _t(self.slot_last), _t(self.count)], [P("M", 1)])
-        self.calls = calls
+                tail.append(call("ridgefill_rho_update",
+                                 [_t(self.ab[j], [T, hv], [2 * hv, 1]), _t(self.mask), _t(x["a_log"][j]), _t(x["dt_bias"][j]),
+                                  _t(self.nd, [s.n_seq, hv, 1, 2], list(self.nd.stride()), offset_elems=j * hv * 2),
+                                  _t(self.slot_last), _t(self.bounds)], [P("M", T), P("n_head", hv)], f"{j}"))
+            tail.append(correct("apply"))
+        tail.append(call("ridgefill_hazard", [_t(inp["cu_last"]), _t(inp["positions"]), _t(self.bounds), A_, _t(self.meta),
+                                              _t(self.slot_last), _t(self.count)], [P("M", 1)]))
+        self.head, self.layers, self.tail = head, layers, tail
+        self.calls = head + [c for proj, block in layers for c in proj + block] + tail
         small = D != 128
-        self.kernels = sum(1 if (c[0] == "ridgefill_gdn_fill" and small) else self.KERNELS[c[0]] for c in calls)
+        self.kernels = sum(1 if (c[0] == "ridgefill_gdn_fill" and small) else self.KERNELS[c[0]] for c in self.calls)
+        if self.team is not None:   # the barrier, one gather and one wait a layer
+            self.kernels += 1 + 2 * len(s.layers)
 
     def _launch(self, op, r, tens, params, stream: int) -> None:
         sb = self.fill_scratch if op == "ridgefill_gdn_fill" else 0
@@ -343,18 +496,81 @@ class LatePass:
             raise RuntimeError(f"{op}: device row refused or failed (rc {rc})")
 
     def run(self, stream: int, events=None) -> None:
-        """Issue one pass on `stream`. `events` (optional) maps an op name to a list of (start, end) CUDA event
-        pairs, one pair per launch of that op, recorded on the current torch stream around each launch."""
+        """Issue one pass on `stream` (and, on a team, the column gathers on a second stream). `events` (optional)
+        maps an op name to a list of (start, end) CUDA event pairs, one pair per launch of that op, recorded on the
+        current torch stream around each launch."""
         counts = {}
-        for op, r, tens, params, _tag in self.calls:
+
+        def emit(c):
+            op = c[0]
             ev = events.get(op) if events else None
             if ev is not None:
                 i = counts.get(op, 0)
                 counts[op] = i + 1
                 ev[i][0].record()
-            self._launch(op, r, tens, params, stream)
+            self._launch(op, c[1], c[2], c[3], stream)
             if ev is not None:
                 ev[i][1].record()
+
+        if self.team is not None:
+            self._run_team(stream, emit)
+            return
+        for c in self.calls:
+            emit(c)
+
+    def _run_team(self, stream: int, emit) -> None:
+        """One rank's pass: the barrier (every rank has finished its previous pass), the head of the pass, then per
+        layer its projector block and select on `stream` and that block's gather to the peers on the comm stream,
+        while `stream` goes on with the previous layer's block (after waiting for all of its columns); the fill and
+        the rest once every layer is done."""
+        import ctypes as C
+        torch = self.torch
+        team, L = self.team, self.lib.lib
+        main = torch.cuda.ExternalStream(stream, device=self.dev)
+        self.epoch += 1
+        e, R = self.epoch, team.world
+        ctas = L.ridgefill_team_gather_ctas()
+        flags = (C.c_void_p * R)(*self.peer_flags)
+        layer_bytes = self.s.T * self.s.d * 2
+        own = C.c_void_p(self.counters.data_ptr())
+        n_layers = len(self.s.layers)
+        L.ridgefill_team_barrier.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_ulonglong, C.c_void_p]
+        L.ridgefill_gather_columns.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int64, C.c_int64,
+                                               C.c_int64, C.c_int64, C.c_int, C.c_void_p]
+        L.ridgefill_team_wait.argtypes = [C.c_void_p, C.c_int, C.c_ulonglong, C.c_void_p]
+        if L.ridgefill_team_barrier(flags, team.rank, R, n_layers, e * (R - 1), C.c_void_p(stream)) != abi.OK:
+            raise RuntimeError("ridgefill_team_barrier failed")
+        for c in self.head:
+            emit(c)
+        c0, c1 = self.geo["cols"]
+        T, d = self.s.T, self.s.d
+        comm = self.comm
+
+        def block(li):
+            if L.ridgefill_team_wait(own, li, e * (R - 1) * ctas, C.c_void_p(stream)) != abi.OK:
+                raise RuntimeError("ridgefill_team_wait failed")
+            for c in self.layers[li][1]:
+                emit(c)
+
+        for li, (proj, _block) in enumerate(self.layers):
+            for c in proj:
+                emit(c)
+            ready = torch.cuda.Event()
+            ready.record(main)
+            comm.wait_event(ready)
+            dsts = (C.c_void_p * R)(*[ptr + li * layer_bytes for ptr in self.peer_x])   # every rank's layer-li input
+            if L.ridgefill_gather_columns(C.c_void_p(self.x[li].data_ptr()), dsts, flags, team.rank, R, T, d, c0, c1, li,
+                                          C.c_void_p(comm.cuda_stream)) != abi.OK:
+                raise RuntimeError("ridgefill_gather_columns failed")
+            if li:
+                block(li - 1)
+        if self.layers:
+            block(len(self.layers) - 1)
+        done = torch.cuda.Event()
+        done.record(comm)
+        main.wait_event(done)   # the last gathers read this rank's block inputs: done before the next pass writes them
+        for c in self.tail:
+            emit(c)
 
     def op_counts(self) -> dict:
         out = {}
@@ -362,13 +578,26 @@ class LatePass:
             out[c[0]] = out.get(c[0], 0) + 1
         return out
 
+    def inputs_per_step(self) -> list:
+        """The tensors a pass reads that change from prompt to prompt: h_S, the token ids and the positions."""
+        return [self.inp["h_s"], self.inp["token_ids"], self.inp["positions"]]
+
+    def results(self) -> list:
+        """The buffers a pass leaves for the engine: every DeltaNet state and conv state, every attention cache,
+        the mask, the decay sums and the hazard record."""
+        out = [self.state, self.mask, self.nd, self.meta, self.count] + list(self.cache)
+        if self.s.block_inputs:
+            out += list(self.conv_state)
+        return out
+
     # --------------------------------------------------------------- algorithmic work of one pass
     def algorithmic(self) -> dict:
         s = self.s
         T, d, G, A = s.T, s.d, s.n_gdn, s.n_attn
-        hk, hv, D = s.hk, s.hv, s.head
+        hk, hv, D = self.hk_r, self.hv_r, s.head
         L = len(s.layers)
-        n_int8_cols = L * d + (G * s.conv_dim if s.block_inputs else 0) + A * 2 * s.hkv * s.head_attn
+        n_int8_cols = L * self.cols + (G * self.conv_dim_r if s.block_inputs else 0) + \
+            (A * 2 * self.hkv_r * s.head_attn if self.hkv_r else 0)
         chunks = sum((n + 63) // 64 for n in s.lengths)
         return {
             "int8_ops": 2 * T * d * n_int8_cols,

@@ -18,8 +18,9 @@ def _run(env_extra):
 
 
 def test_reference_arm_line():
+    """Under a launcher that sets OMP_NUM_THREADS=1 (torchrun does), the arm still uses every host core."""
     import bench
-    p = _run({"RANK": "0", "WORLD_SIZE": "1"})
+    p = _run({"RANK": "0", "WORLD_SIZE": "1", "OMP_NUM_THREADS": "1"})
     assert p.returncode == 0, p.stderr[-2000:]
     lines = [ln for ln in p.stdout.splitlines() if ln.startswith("{")]
     assert len(lines) == 1
@@ -28,7 +29,8 @@ def test_reference_arm_line():
     assert d["higher_is_better"] is True and d["steps"] == 1 and d["value"] > 0
     assert d["config"]["workload"] == bench.WORKLOAD and d["config"]["rows"] == bench.T_FULL
     cb = d["cpu_baseline"]
-    assert cb["value"] == d["value"] and cb["kind"] in ("reference", "port") and cb["cores"] >= 1 and cb["sample"]
+    assert cb["value"] == d["value"] and cb["kind"] in ("reference", "port") and cb["sample"]
+    assert cb["cores"] == len(os.sched_getaffinity(0))
     assert d["e2e"] == {"value": d["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
 
 

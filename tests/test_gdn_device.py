@@ -82,6 +82,49 @@ def test_fill_full_size_split_is_one_call(cuda, product_lib):
     assert np.array_equal(one.view(np.uint32), two.view(np.uint32))
     want, _ = H.oracle_gdn(k, v, g, beta, state, [0], [0, T], heads=(5, 7))
     assert H.rel_l2(one[0, 5:7], want[0, 5:7]) <= STATE_TOL
+    # every head against the float32 rule (the f64 one takes minutes at this size); per head, the same bound
+    want32, _ = H.oracle_gdn(k, v, g, beta, state, [0], [0, T], f64=False)
+    errs = [H.rel_l2(one[0, h], want32[0, h]) for h in range(hv)]
+    assert max(errs) <= STATE_TOL, errs
+
+
+@pytest.mark.parametrize("T,hk,hv,dk,o", [(512, 4, 8, 32, False), (300, 2, 4, 32, True), (200, 1, 3, 64, True),
+                                          (129, 2, 2, 16, False)])
+def test_small_heads_follow_the_rule(cuda, product_lib, T, hk, hv, dk, o):
+    """Head dims of at most 64 (the reference's CPU mini model has 32) run the per-row form: state within the
+    same 1e-3 relative L2 of the float64 rule, o within 1e-2, over two sequences with one slot skipped."""
+    torch = cuda
+    rng = np.random.default_rng(T + dk)
+    k = rng.standard_normal((T, hk, dk)).astype(np.float32)
+    k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    q = rng.standard_normal((T, hk, dk)).astype(np.float32)
+    q /= np.linalg.norm(q, axis=-1, keepdims=True)
+    v = rng.standard_normal((T, hv, dk)).astype(np.float32)
+    g = -np.log1p(np.exp(rng.standard_normal((T, hv)))).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.standard_normal((T, hv))))).astype(np.float32)
+    state = (0.1 * rng.standard_normal((3, hv, dk, dk))).astype(np.float32)
+    kb, vb, qb = H.f32_to_bf16_bits(k), H.f32_to_bf16_bits(v), H.f32_to_bf16_bits(q)
+    cu, idx = [0, T // 3, T], [2, -1]
+    S = torch.from_numpy(state.copy()).cuda()
+    O = torch.zeros((T, hv, dk), dtype=torch.int16, device="cuda") if o else None
+    t16 = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda()   # noqa: E731
+    Kd, Vd, Qd = t16(kb), t16(vb), (t16(qb) if o else None)
+    G, B = torch.from_numpy(g).cuda(), torch.from_numpy(beta).cuda()
+    I, CU = torch.tensor(idx, dtype=torch.int32).cuda(), torch.tensor(cu, dtype=torch.int32).cuda()
+    params = [H.pint("M", T), H.pint("n_head_k", hk), H.pint("n_head_v", hv), H.pint("head_k", dk), H.pint("head_v", dk),
+              H.pint("chunk", 64)]
+    assert H.launch(product_lib, "ridgefill_gdn_fill", [H.dev(Qd, abi.BF16), H.dev(Kd, abi.BF16), H.dev(Vd, abi.BF16), H.dev(G),
+                                                        H.dev(B), H.dev(S), H.dev(I), H.dev(CU), H.dev(O, abi.BF16)],
+                    params) == abi.OK
+    want, want_o = H.oracle_gdn(kb, vb, g, beta, state, idx, cu, q=qb if o else None)
+    got = S.cpu().numpy()
+    assert H.rel_l2(got[2], want[2]) <= STATE_TOL
+    assert np.array_equal(got[0], state[0]) and np.array_equal(got[1], state[1])
+    if o:
+        got_o = O.cpu().numpy().view(np.uint16)
+        assert not got_o[T // 3:].any()   # the skipped sequence's rows are left as they were
+        rows = slice(0, T // 3)
+        assert H.rel_l2(H.bf16_bits_to_f32(got_o[rows]), H.bf16_bits_to_f32(want_o[rows])) <= O_TOL
 
 
 @pytest.mark.parametrize("T,hk,hv,decay", [(64, 1, 1, "fast"), (130, 2, 4, "slow"), (777, 1, 2, "very slow"),

@@ -343,6 +343,23 @@ def test_rho_device_matches_oracle(cuda, product_lib, oracle_lib):
 
 
 @gpu
+@pytest.mark.parametrize("n", [32768, 32767])
+def test_rho_device_at_the_full_chunk(cuda, product_lib, oracle_lib, n):
+    """The pass's size: 32,768 rows (and an odd 32,767) x 32 heads, 30 % of the rows exact, two chunks; rho within
+    the reference's 1e-5 of the sequential host rule, whatever the composition over row runs does to rounding."""
+    dev, host = rows("ridgefill_rho_update", product_lib, oracle_lib)
+    r = H.Rng(n)
+    h = K.random_rho(r, n, 32, 0.30, True)
+    h.pitch = 64
+    d = h.copy()
+    for _ in range(2):
+        assert K.run_rho(oracle_lib, host, h) == abi.OK
+        assert K.run_rho(product_lib, dev, d) == abi.OK
+    worst = max(abs(K.nd_rho(h, k) - K.nd_rho(d, k)) for k in range(32))
+    assert worst <= 1e-5, worst
+
+
+@gpu
 def test_rho_bounds_device_is_the_slice(cuda, product_lib, oracle_lib):
     """With bounds {s, ..} the device row equals itself run on rows [s, n) bit for bit, and the oracle
     within 1e-5 (kernel_test.cpp:1807-1832)."""
@@ -372,7 +389,7 @@ def test_rho_bounds_device_is_the_slice(cuda, product_lib, oracle_lib):
 def test_select_device_matches_oracle(cuda, product_lib, oracle_lib):
     dev, host = rows("ridgefill_select", product_lib, oracle_lib)
     r = H.Rng(111)
-    for n in (1, 300, 8192):
+    for n in (1, 300, 8192, 32768):
         for variant in range(3):
             exact = r.uniform()
             mask = [2 if r.uniform() < 0.02 else (0 if r.uniform() < exact else 1) for _ in range(n)]
@@ -402,7 +419,7 @@ def test_select_device_matches_oracle(cuda, product_lib, oracle_lib):
 def test_drop_rows_device_matches_oracle(cuda, product_lib, oracle_lib):
     dev, host = rows("ridgefill_drop_rows", product_lib, oracle_lib)
     r = H.Rng(121)
-    for n in (1, 300, 8192):
+    for n in (1, 300, 8192, 32768):
         for top_k in (0, 1, 7, 300):
             mask = [2 if r.uniform() < 0.02 else (0 if r.uniform() < 0.3 else 1) for _ in range(n)]
             ids = Buf(abi.I32, [n + 1, top_k + 4], [top_k + 7, 1])
