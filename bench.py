@@ -440,6 +440,21 @@ def run_only(args):
                       "ms_per_launch": a.elapsed_time(b) / (args.steps * len(calls))}), flush=True)
 
 
+def run_profile_pass(args):
+    """Issue --warmup whole passes of the config-3 step, then one more, and nothing else (no timing, no extras):
+    the command an ncu launch list of one pass runs (skip the warm-up passes' launches)."""
+    import torch
+    import late_pass as LP
+    p = LP.LatePass(LP.LateShape(T=args.rows, layers=args.layers), "cuda", seed=1234)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup + 1):
+            p.run(stream.cuda_stream)
+    stream.synchronize()
+    print(json.dumps({"profile_pass": True, "rows": args.rows, "layers": args.layers, "kernels_per_pass": p.kernels}),
+          flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -450,9 +465,12 @@ def main():
     ap.add_argument("--no-extra", action="store_true", help="skip the config-5 and one-layer extras")
     ap.add_argument("--only", default=None, help="profile mode: launch only this row's launches of the pass")
     ap.add_argument("--rows", type=int, default=T_FULL, help="rows of the chunk in --only mode")
-    ap.add_argument("--layers", default="GGGA" * 6, help="late layers in --only mode (G DeltaNet, A attention)")
+    ap.add_argument("--layers", default="GGGA" * 6, help="late layers in --only / --profile-pass mode (G DeltaNet, A attention)")
+    ap.add_argument("--profile-pass", action="store_true", help="profile mode: --warmup passes, then one pass, untimed")
     args = ap.parse_args()
-    if args.only:
+    if args.profile_pass:
+        run_profile_pass(args)
+    elif args.only:
         run_only(args)
     elif args.impl == "reference":
         run_reference(args)

@@ -1,6 +1,6 @@
 """Regenerate the golden fixtures under tests/golden/ from the reference checkout (read-only).
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference checkout>   (or RIDGEFILL_REFERENCE in the environment)
 
 Writes:
   rho_numpy.txt       the reference's own rho fixture, produced by running its tests/rho_ref.py (the NumPy
@@ -22,6 +22,7 @@ the reference itself.
 from __future__ import annotations
 
 import argparse
+import os
 import importlib.util
 import json
 import subprocess
@@ -113,7 +114,7 @@ def folder_fixture(ref: Path) -> None:
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("RIDGEFILL_REFERENCE"), required="RIDGEFILL_REFERENCE" not in os.environ)
     ref = Path(ap.parse_args().reference)
     rho_fixture(ref)
     rowsel_fixture(ref)

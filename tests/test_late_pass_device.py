@@ -12,7 +12,10 @@ the same seeded inputs. Every buffer the pass writes is compared:
                                                        results (|y| < 1.2e-38) to zero, the host keeps them
     g, beta                                            1e-5 wherever a|b agree bit for bit
     DeltaNet state, every layer and slot               1e-3 relative L2 (f32 sequential rule)
-    N|D decay sums, applied scales                     1e-4 relative (the reference's rho bound)
+    N|D decay sums, rho, applied scales                1e-4 relative on N and D, 1e-5 on rho (the reference's
+                                                       bounds) for every head whose a values (from the bf16 a|b
+                                                       projection) are bit for bit the host's; 1e-3 on rho for a
+                                                       head that read an a value one bf16 ulp off
 
 The shapes: the reference's CPU mini model (config 0: d 256, 512 rows, 4 DeltaNet layers of 4 / 8 heads of 32), a
 2,048-row sample of the full step's first four late layers (G G G A) at full width, all 24 late layers at 256 rows
@@ -90,10 +93,19 @@ def test_late_pass_matches_the_cpu_path(name, cuda):
         for j in range(G):
             blk = slice(j * hv, (j + 1) * hv)
             assert _rel(state[sl, blk], want_state[sl, blk]) <= 1e-3, (sl, j)
+    # decay sums and the applied scale: the reference's bounds on every head whose a values (rho's input, from the
+    # bf16 a|b projection) are bit for bit the host's; a head that read an a one bf16 ulp off (the bf16 GEMM's own
+    # rounding, which the reference bounds at 2 ulp) within 1e-3 of rho
     nd, want_nd = _u16(dev.nd), cpu.nd
-    assert np.all(np.abs(nd - want_nd) <= 1e-4 * np.maximum(np.abs(want_nd), 1.0))
-    ap, want_ap = _u16(dev.applied), cpu.applied
-    assert np.all(np.abs(ap - want_ap) <= 1e-4 * np.maximum(np.abs(want_ap), 1.0))
+    a_same = same_ab[:, :].all(axis=0)                      # [G hv]: every row of the head's a matched
+    rho = lambda x: np.clip(x[..., 0, 0] / np.where(x[..., 0, 1] > 0, x[..., 0, 1], 1.0), 0.0, 1.0)   # noqa: E731
+    exact = np.abs(nd - want_nd) <= 1e-4 * np.maximum(np.abs(want_nd), 1.0)
+    assert exact.all(axis=(2, 3))[:, a_same].all()
+    assert np.abs(rho(nd) - rho(want_nd))[:, a_same].max(initial=0.0) <= 1e-5
+    assert np.abs(rho(nd) - rho(want_nd)).max() <= 1e-3
+    ap, want_ap = _u16(dev.applied)[..., 0, 0], cpu.applied[..., 0, 0]
+    assert np.abs(ap - want_ap)[:, a_same].max(initial=0.0) <= 1e-5 * max(1.0, s.alpha)
+    assert np.abs(ap - want_ap).max() <= 1e-3 * max(1.0, s.alpha)
 
 
 @gpu
