@@ -321,7 +321,8 @@ typedef struct RidgeFillGdn {
  *     g[t,h] = -exp(A_log[h]) * softplus(a[t,h] + dt_bias[h]),  beta[t,h] = 1 / (1 + exp(-b[t,h])).
  * The conv state [slots, 3, C] bf16 of each sequence's slot idx[i] is then the last three input rows of
  * (state, rows) (a slot outside the pool: zero history, nothing written). Rows outside every sequence are not
- * written. */
+ * written. q is optional: without it the q columns are not computed (a state-only fill reads no q), and x's q
+ * columns are read only in each sequence's last three rows, for the conv state. */
 typedef struct RidgeFillConvPrep {
     const uint16_t* x;       int64_t x_row;
     const uint16_t* w;                          /* [C, 4] bf16, dense */

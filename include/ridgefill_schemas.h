@@ -74,7 +74,7 @@ static const RadParamSpec pConv[] = { RF_P_INT("M"), RF_P_INT("n_head_k"), RF_P_
                                       RF_P_INT("head_v"), RF_P_INT("conv") };
 static const RadOperandSpec oConv[] = { RF_IN("x"), RF_IN("w_conv"), RF_IN_OPT("conv_bias"), RF_IN("A_log"),
                                         RF_IN("dt_bias"), RF_INOUT("conv_state"), RF_IN("cu_seqlens"), RF_IN("a"),
-                                        RF_IN("b"), RF_IN("conv_idx"), RF_IN_OPT("ctx_lens"), RF_OUT("q"), RF_OUT("k"),
+                                        RF_IN("b"), RF_IN("conv_idx"), RF_IN_OPT("ctx_lens"), RF_OUT_OPT("q"), RF_OUT("k"),
                                         RF_OUT("v"), RF_OUT("g"), RF_OUT("beta") };
 static const RadParamSpec pAttnKv[] = { RF_P_INT("M"), RF_P_INT("n_head_kv"), RF_P_INT("head_dim"), RF_P_INT("rope_dim"),
                                         RF_P_F64("rope_theta"), RF_P_OPT("eps", RAD_P_F64),

@@ -5,7 +5,9 @@
  * depthwise convolution of width 4, SiLU, per-head L2 normalisation of q and k) and the reference's own gate
  * g = -exp(A_log) softplus(a + dt_bias) (kernels/ridgefill.h:93-97), written per row for ridgefill_gdn_fill.
  *
- * HBM-bound: x is read once and q, k, v written once (2 x 2 C bytes a row). A warp takes 16 rows of a pair of
+ * HBM-bound: x is read once and q, k, v written once (2 x 2 C bytes a row). Without a q operand (the state-only
+ * fill reads no q) the q columns are neither read nor computed; the conv state still takes every channel of each
+ * sequence's last three rows, so x's q columns need be valid only there. A warp takes 16 rows of a pair of
  * 128-channel head columns, lane l channels 8 (l % 16)..+8 of column l / 16 (16-byte loads and stores, a
  * warp's row 512 contiguous bytes); the convolution's three earlier rows ride in registers; when the 16 rows
  * lie in one sequence, all their loads are in flight at once as asynchronous copies into the lane's own
@@ -80,8 +82,6 @@ __device__ __forceinline__ uint4 window_row(const RidgeFillConvPrep& g, int64_t 
     return *(const uint4*)(g.state + slot * g.st_slot + (3 - (s0 - row)) * C + c);
 }
 
-/* A warp takes kRows rows of a pair of 128-channel head columns (2 j, 2 j + 1; the pair is q / k or v alike,
- * as 2 Hk is even): half-warp hw owns column 2 j + hw, lane l of the half channels 8 l..8 l + 7. */
 /* SiLU u / (1 + e^-u) with the fast exp and divide (well inside bf16's rounding), except where the fast divide
  * returns 0: a denominator above 2^126 (u below about -87.3, where the value is about u e^u, under 1e-36 in
  * magnitude) takes the exact division, so those rows keep their tiny values as the f32 rule gives them. */
@@ -90,18 +90,23 @@ __device__ __forceinline__ float silu(float u) {
     return den < 0x1p126f ? __fdividef(u, den) : u / den;
 }
 
+/* A warp takes kRows rows of a pair of 128-channel head columns (2 j, 2 j + 1; the pair is q / k or v alike,
+ * as 2 Hk is even): half-warp hw owns column 2 j + hw, lane l of the half channels 8 l..8 l + 7. */
 __global__ void __launch_bounds__(kThreads) conv_prep_kernel(RidgeFillConvPrep g) {
     extern __shared__ uint4 rows_smem[];   /* [warp][kRows][lane] */
     const int lane = threadIdx.x & 31, hw = lane >> 4, hl = lane & 15;
     uint4* stage = rows_smem + (threadIdx.x >> 5) * kRows * 32 + lane;
     const int64_t hk = g.n_head_k, hv = g.n_head_v;
     const int64_t C = 2 * hk * 128 + hv * 128, n_hc = C / 128, n_pairs = (n_hc + 1) / 2;
-    const int64_t tasks = (g.T + kRows - 1) / kRows * n_pairs;
+    /* without a q output the q columns are not computed: the pairs start at the first that holds a k column */
+    const int64_t first = g.q ? 0 : hk / 2, pairs = n_pairs - first;
+    const int64_t tasks = (g.T + kRows - 1) / kRows * pairs;
     const int64_t stride = (int64_t)gridDim.x * (kThreads / 32);
     for (int64_t task = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); task < tasks; task += stride) {
-        const int64_t pair = task % n_pairs, r0 = task / n_pairs * kRows, r1 = min(r0 + kRows, g.T);
+        const int64_t pair = first + task % pairs, r0 = task / pairs * kRows, r1 = min(r0 + kRows, g.T);
         const int64_t hc = 2 * pair + hw;
-        const bool live = hc < n_hc;                 /* an odd column count leaves the last pair's second half idle */
+        /* an odd column count leaves the last pair's second half idle; an odd hk without q, the first pair's first */
+        const bool live = hc < n_hc && (g.q != nullptr || hc >= hk);
         const int64_t c = (live ? hc : 2 * pair) * 128 + 8 * hl;
         const bool norm = 2 * pair < 2 * hk;         /* q and k columns are L2-normalised; the pair is alike */
         float wt[8][4], bs[8];
@@ -257,7 +262,7 @@ extern "C" int ridgefill_gdn_conv_prep_device(const RadArgs* a, RadStream s) {
     if (rc != RAD_OK) return rc;
     cudaStream_t stream = rf::as_stream(s);
     const int64_t C = 2 * g.n_head_k * 128 + g.n_head_v * 128;
-    const int64_t tasks = (g.T + kRows - 1) / kRows * (C / 128);
+    const int64_t tasks = (g.T + kRows - 1) / kRows * ((C / 128 + 1) / 2 - (g.q ? 0 : g.n_head_k / 2));
     if (tasks > 0) {
         static int per_sm = 0;   /* resident CTAs a SM (registers and the 64 KiB stage bound it) */
         if (!per_sm) {

@@ -1302,7 +1302,9 @@ __global__ void __launch_bounds__(64) gdn_small_kernel(const RidgeFillGdn g) {
         if (g.o) g.o[t * g.o_row + h * g.o_head + i] = rf::f32_to_bf16_bits(g.scale * out);
     }
     if (mine)
-        for (int j = 0; j < dk; ++j) srow[j] = S[j];
+#pragma unroll
+        for (int j = 0; j < DK; ++j)
+            if (j < dk) srow[j] = S[j];
 }
 
 int launch_small(const RidgeFillGdn& g, cudaStream_t stream) {

@@ -555,8 +555,8 @@ extern "C" int ridgefill_gemm_bias_parse(const RadArgs* a, RidgeFillGemmBias* g)
 /* ridgefill_gdn_conv_prep: x bf16 [T, C] (C = 2 Hk dk + Hv dv, rows 16-byte aligned), w bf16 [C, 4] dense,
  * bias bf16 [C] or absent (16-byte aligned), A_log and dt_bias f32 [Hv], state bf16 [slots, 3, C] (a dense [3, C] per slot),
  * cu_seqlens i32 [n_seq + 1], a and b bf16 [T, Hv] (any row pitch, last stride 1), idx i32 [n_seq] or [n_seq, >= 1],
- * ctx_lens i32 [n_seq] or absent, q and k bf16 [T, Hk, dk], v bf16 [T, Hv, dv] (each head dense, rows and
- * heads 16-byte aligned), g and beta f32 [T, Hv]. Head dims 128, width 4. */
+ * ctx_lens i32 [n_seq] or absent, q (or absent: its columns are then not computed) and k bf16 [T, Hk, dk], v bf16
+ * [T, Hv, dv] (each head dense, rows and heads 16-byte aligned), g and beta f32 [T, Hv]. Head dims 128, width 4. */
 extern "C" int ridgefill_conv_prep_parse(const RadArgs* a, RidgeFillConvPrep* g) {
     *g = RidgeFillConvPrep{};
     const RadTensor* X = rad_arg_in(a, CP_X);
@@ -576,7 +576,7 @@ extern "C" int ridgefill_conv_prep_parse(const RadArgs* a, RidgeFillConvPrep* g)
     const RadTensor* G = rad_arg_in(a, CP_G);
     const RadTensor* BE = rad_arg_in(a, CP_BETA);
     long long T = 0, hk = 0, hv = 0, dk = 0, dv = 0, width = 0;
-    if (!X || !W || !AL || !DT || !ST || !CU || !A || !Bg || !I || !Q || !K || !V || !G || !BE) return RAD_E_INVAL;
+    if (!X || !W || !AL || !DT || !ST || !CU || !A || !Bg || !I || !K || !V || !G || !BE) return RAD_E_INVAL;   /* q optional */
     if (!rad_args_geti(a, "M", &T) || !rad_args_geti(a, "n_head_k", &hk) || !rad_args_geti(a, "n_head_v", &hv) ||
         !rad_args_geti(a, "head_k", &dk) || !rad_args_geti(a, "head_v", &dv) || !rad_args_geti(a, "conv", &width))
         return RAD_E_INVAL;
@@ -585,7 +585,7 @@ extern "C" int ridgefill_conv_prep_parse(const RadArgs* a, RidgeFillConvPrep* g)
     const int64_t C = 2 * hk * dk + hv * dv;
     if (X->dtype != RAD_BF16 || W->dtype != RAD_BF16 || (B0 && B0->dtype != RAD_BF16) || AL->dtype != RAD_F32 ||
         DT->dtype != RAD_F32 || ST->dtype != RAD_BF16 || CU->dtype != RAD_I32 || A->dtype != RAD_BF16 ||
-        Bg->dtype != RAD_BF16 || I->dtype != RAD_I32 || (CX && CX->dtype != RAD_I32) || Q->dtype != RAD_BF16 ||
+        Bg->dtype != RAD_BF16 || I->dtype != RAD_I32 || (CX && CX->dtype != RAD_I32) || (Q && Q->dtype != RAD_BF16) ||
         K->dtype != RAD_BF16 || V->dtype != RAD_BF16 || G->dtype != RAD_F32 || BE->dtype != RAD_F32)
         return RAD_E_DTYPE;
     if (X->rank != 2 || X->shape[0] != T || X->shape[1] != C || X->stride[1] != 1) return X->rank == 2 && X->stride[1] != 1 ? RAD_E_STRIDE : RAD_E_SHAPE;
@@ -602,13 +602,13 @@ extern "C" int ridgefill_conv_prep_parse(const RadArgs* a, RidgeFillConvPrep* g)
     const RadTensor* per_head[4] = { A, Bg, G, BE };
     for (const RadTensor* t : per_head)
         if (t->rank != 2 || t->shape[0] != T || t->shape[1] != hv || t->stride[1] != 1) return RAD_E_SHAPE;
-    if (Q->rank != 3 || Q->shape[0] != T || Q->shape[1] != hk || Q->shape[2] != dk || Q->stride[2] != 1) return RAD_E_SHAPE;
+    if (Q && (Q->rank != 3 || Q->shape[0] != T || Q->shape[1] != hk || Q->shape[2] != dk || Q->stride[2] != 1)) return RAD_E_SHAPE;
     if (K->rank != 3 || K->shape[0] != T || K->shape[1] != hk || K->shape[2] != dk || K->stride[2] != 1) return RAD_E_SHAPE;
     if (V->rank != 3 || V->shape[0] != T || V->shape[1] != hv || V->shape[2] != dv || V->stride[2] != 1) return RAD_E_SHAPE;
     /* 16-byte loads of x, w, the bias and the state, 16-byte stores of q, k, v (eight channels a lane). */
-    if (((uintptr_t)X->data | (uintptr_t)Q->data | (uintptr_t)K->data | (uintptr_t)V->data | (uintptr_t)W->data |
+    if (((uintptr_t)X->data | (Q ? (uintptr_t)Q->data : 0) | (uintptr_t)K->data | (uintptr_t)V->data | (uintptr_t)W->data |
          (uintptr_t)ST->data) % 16 ||
-        (X->stride[0] * 2) % 16 || (Q->stride[0] * 2) % 16 || (Q->stride[1] * 2) % 16 || (K->stride[0] * 2) % 16 ||
+        (X->stride[0] * 2) % 16 || (Q && ((Q->stride[0] * 2) % 16 || (Q->stride[1] * 2) % 16)) || (K->stride[0] * 2) % 16 ||
         (K->stride[1] * 2) % 16 || (V->stride[0] * 2) % 16 || (V->stride[1] * 2) % 16 || (ST->stride[0] * 2) % 16)
         return RAD_E_STRIDE;
     g->x = (const uint16_t*)X->data;
@@ -629,9 +629,9 @@ extern "C" int ridgefill_conv_prep_parse(const RadArgs* a, RidgeFillConvPrep* g)
     g->idx = (const int32_t*)I->data;
     g->idx_pitch = I->rank == 1 ? 1 : I->stride[0];
     g->ctx = CX ? (const int32_t*)CX->data : nullptr;
-    g->q = (uint16_t*)Q->data;
-    g->q_row = Q->stride[0];
-    g->q_head = Q->stride[1];
+    g->q = Q ? (uint16_t*)Q->data : nullptr;
+    g->q_row = Q ? Q->stride[0] : 0;
+    g->q_head = Q ? Q->stride[1] : 0;
     g->k = (uint16_t*)K->data;
     g->k_row = K->stride[0];
     g->k_head = K->stride[1];

@@ -356,11 +356,19 @@ class LatePass:
         self.slot_last = torch.tensor([[s.n_seq - 1]], dtype=torch.int32, device=dev)   # the approximated sequence
         self.slots_all = torch.arange(s.n_seq, dtype=torch.int32, device=dev).view(-1, 1)
         self.conv_dim_r = 2 * hk * D + hv * D
+        starts = [0]
+        for n in s.lengths:
+            starts.append(starts[-1] + n)
+        self.seq_bounds = list(zip(starts[:-1], starts[1:]))
         if s.block_inputs:
             C = self.conv_dim_r
             self.mixed = empty(T, C, dtype=torch.bfloat16)
             self.ab = [empty(T, 2 * hv, dtype=torch.bfloat16) for _ in range(G)]
-            self.q = empty(T, hk, D, dtype=torch.bfloat16)   # the state-only fill reads no q: one buffer for all
+            Cq = hk * D
+            self.w_in_q = [w[:Cq].contiguous() for w in x["w_in"]]
+            self.w_in_kv = [w[Cq:].contiguous() for w in x["w_in"]]
+            self.s_in_q = [t[:, :Cq].contiguous() for t in x["s_in"]]
+            self.s_in_kv = [t[:, Cq:].contiguous() for t in x["s_in"]]
             self.k = empty(T, G * hk, D, dtype=torch.bfloat16)
             self.v = empty(T, G * hv, D, dtype=torch.bfloat16)
             self.g = empty(T, G * hv, dtype=torch.float32)
@@ -401,9 +409,11 @@ class LatePass:
         def call(op, tens, params, tag=""):
             return (op, row(op), tens, params, tag)
 
-        def gemm_q(a, sa, w, sw, bias, y, N, tag):
-            return call("ridgefill_gemm_nt_q_bias", [_t(a), _t(sa), _t(w), _t(sw), A_ if bias is None else _t(bias), y, A_],
-                        [P("M", T), P("N", N), P("K", d), P("group", self.grp), S("dtype", "i8a8")], tag)
+        def gemm_q(a, sa, w, sw, bias, y, N, tag, M=T):
+            return call("ridgefill_gemm_nt_q_bias", [a if isinstance(a, abi.RadTensor) else _t(a),
+                                                     sa if isinstance(sa, abi.RadTensor) else _t(sa), _t(w), _t(sw),
+                                                     A_ if bias is None else _t(bias), y, A_],
+                        [P("M", M), P("N", N), P("K", d), P("group", self.grp), S("dtype", "i8a8")], tag)
 
         def quant(src, codes, scale, tag):
             return call("ridgefill_quant_act_i8g", [_t(src), _t(codes), _t(scale)],
@@ -430,9 +440,21 @@ class LatePass:
                                               A_, A_], [P("M", T)], f"{li}")]
             block = []
             if kind == "G" and s.block_inputs:
-                C = self.conv_dim_r
+                C, Cq = self.conv_dim_r, hk * D
                 block.append(quant(self.x[li], self.codes_x, self.scale_x, f"x {li}"))
-                block.append(gemm_q(self.codes_x, self.scale_x, x["w_in"][gi], x["s_in"][gi], None, _t(self.mixed), C, f"in {li}"))
+                # the mixed projection's k|v columns over every row; its q columns only over each sequence's last
+                # three rows, the conv state's (the state-only fill reads no q, so conv_prep is given none)
+                block.append(gemm_q(self.codes_x, self.scale_x, self.w_in_kv[gi], self.s_in_kv[gi], None,
+                                    _t(self.mixed, [T, C - Cq], [C, 1], offset_elems=Cq), C - Cq, f"in kv {li}"))
+                for a_, b_ in self.seq_bounds:
+                    m0 = max(a_, b_ - 3)
+                    if b_ <= m0:
+                        continue
+                    M = b_ - m0
+                    block.append(gemm_q(_t(self.codes_x, [M, d], [d, 1], offset_elems=m0 * d),
+                                        _t(self.scale_x, [M, d // self.grp], [d // self.grp, 1], offset_elems=m0 * (d // self.grp)),
+                                        self.w_in_q[gi], self.s_in_q[gi], None, _t(self.mixed, [M, Cq], [C, 1], offset_elems=m0 * C),
+                                        Cq, f"in q {li}", M=M))
                 block.append(call("ridgefill_gemm_nt_bias", [_t(self.x[li]), _t(x["w_ab"][gi]), _t(self.zero_ab), A_,
                                                              _t(self.ab[gi])],
                                   [P("M", T), P("N", 2 * hv), P("K", d), S("dtype", "bf16")], f"ab {li}"))
@@ -441,7 +463,7 @@ class LatePass:
                                   [_t(self.mixed), _t(x["w_conv"][gi]), A_, _t(x["a_log"][gi]), _t(x["dt_bias"][gi]),
                                    _t(self.conv_state[gi]), _t(inp["cu_seqlens"]), _t(ab, [T, hv], [2 * hv, 1]),
                                    _t(ab, [T, hv], [2 * hv, 1], offset_elems=hv), _t(self.slots_all.view(-1)), _t(self.ctx),
-                                   _t(self.q),
+                                   A_,
                                    _t(self.k, [T, hk, D], list(self.k.stride()), offset_elems=gi * hk * D),
                                    _t(self.v, [T, hv, D], list(self.v.stride()), offset_elems=gi * hv * D),
                                    _t(self.g, [T, hv], [G * hv, 1], offset_elems=gi * hv),

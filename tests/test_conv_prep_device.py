@@ -29,7 +29,7 @@ def _case(seed, T, hk, hv, slots=4, bias=True):
     return d
 
 
-def _run(product_lib, torch, d, cu, idx, ctx, hk, hv):
+def _run(product_lib, torch, d, cu, idx, ctx, hk, hv, with_q=True):
     T, C = d["x"].shape
     t16 = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).cuda()   # noqa: E731
     X, W = t16(d["x"]), t16(d["w"])
@@ -47,7 +47,8 @@ def _run(product_lib, torch, d, cu, idx, ctx, hk, hv):
     BE = torch.full((T, hv), -7.0, dtype=torch.float32, device="cuda")
     ops = [H.dev(X, abi.BF16), H.dev(W, abi.BF16), H.dev(B0, abi.BF16) if B0 is not None else abi.absent(), H.dev(AL),
            H.dev(DT), H.dev(ST, abi.BF16), H.dev(CU), H.dev(A, abi.BF16), H.dev(Bg, abi.BF16), H.dev(I),
-           H.dev(CX) if CX is not None else abi.absent(), H.dev(Q, abi.BF16), H.dev(K, abi.BF16), H.dev(V, abi.BF16),
+           H.dev(CX) if CX is not None else abi.absent(), H.dev(Q, abi.BF16) if with_q else abi.absent(), H.dev(K, abi.BF16),
+           H.dev(V, abi.BF16),
            H.dev(G), H.dev(BE)]
     params = [H.pint("M", T), H.pint("n_head_k", hk), H.pint("n_head_v", hv), H.pint("head_k", 128), H.pint("head_v", 128),
               H.pint("conv", 4)]
@@ -242,3 +243,24 @@ def test_block_input_path_from_h(cuda, product_lib):
         assert H.rel_l2(got_s[sl], want_s[sl]) <= STATE_TOL
     assert np.array_equal(got_s[1], state0[1])   # the slot no sequence names
     assert H.rel_l2(H.bf16_bits_to_f32(u16(O)), H.bf16_bits_to_f32(want_o)) <= O_TOL
+
+
+@pytest.mark.parametrize("hk,hv", [(2, 4), (3, 6)])
+def test_without_q_the_rest_is_bit_for_bit_the_same(cuda, product_lib, hk, hv):
+    """With no q operand (what a state-only fill needs) the q columns are not computed and x's q columns are read
+    only in each sequence's last three rows (for the conv state): k, v, g, beta and the conv state are bit for bit
+    the call with q's, here with x's q columns garbage everywhere else. hk odd puts a q and a k column in one pair."""
+    torch = cuda
+    d = _case(41, 250, hk, hv)
+    cu, idx, ctx = [0, 2, 90, 250], [1, 3, 0], [2, 0, 5]
+    with_q = _run(product_lib, torch, d, cu, idx, ctx, hk, hv)
+    x = d["x"].copy()
+    keep = np.zeros(x.shape[0], bool)
+    for a_, b_ in zip(cu[:-1], cu[1:]):
+        keep[max(a_, b_ - 3):b_] = True
+    x[~keep, :hk * 128] = 0x7FC1   # q columns outside the kept rows: NaN bits nothing may read
+    no_q = _run(product_lib, torch, dict(d, x=x), cu, idx, ctx, hk, hv, with_q=False)
+    assert with_q[0] == no_q[0] == abi.OK
+    for a_, b_ in zip(with_q[2:], no_q[2:]):
+        assert np.array_equal(np.asarray(a_).view(np.uint32 if a_.dtype == np.float32 else np.uint16),
+                              np.asarray(b_).view(np.uint32 if b_.dtype == np.float32 else np.uint16))

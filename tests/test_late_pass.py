@@ -43,7 +43,8 @@ def test_every_launch_passes_its_operand_checks(shape, product_lib):
         assert _parse(product_lib, op, tens, params) == abi.OK, (op, tag)
     counts = p.op_counts()
     G, A, L = shape.n_gdn, shape.n_attn, len(shape.layers)
-    assert counts["ridgefill_gemm_nt_q_bias"] == L + (G if shape.block_inputs else 0) + A
+    # per DeltaNet layer: the mixed projection's k|v columns, then its q columns over each sequence's last rows
+    assert counts["ridgefill_gemm_nt_q_bias"] == L + (G * (1 + shape.n_seq) if shape.block_inputs else 0) + A
     assert counts["ridgefill_gdn_fill"] == 1 and counts["ridgefill_rho_update"] == G
     assert counts["ridgefill_state_correct"] == 2 and counts["ridgefill_mask"] == 1 and counts["ridgefill_hazard"] == 1
     order = [c[0] for c in p.calls]
