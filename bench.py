@@ -441,16 +441,22 @@ def run_only(args):
 
 
 def run_profile_pass(args):
-    """Issue --warmup whole passes of the config-3 step, then one more, and nothing else (no timing, no extras):
-    the command an ncu launch list of one pass runs (skip the warm-up passes' launches)."""
+    """Issue --warmup whole passes of the config-3 step, then one more between cudaProfilerStart and
+    cudaProfilerStop, and nothing else (no timing, no extras): the command an ncu launch list of one pass runs
+    (`ncu --profile-from-start off` sees that pass's launches only, not the input set-up's nor the warm-up's)."""
     import torch
     import late_pass as LP
     p = LP.LatePass(LP.LateShape(T=args.rows, layers=args.layers), "cuda", seed=1234)
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
-        for _ in range(args.warmup + 1):
+        for _ in range(args.warmup):
             p.run(stream.cuda_stream)
     stream.synchronize()
+    torch.cuda.cudart().cudaProfilerStart()
+    with torch.cuda.stream(stream):
+        p.run(stream.cuda_stream)
+    stream.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
     print(json.dumps({"profile_pass": True, "rows": args.rows, "layers": args.layers, "kernels_per_pass": p.kernels}),
           flush=True)
 
