@@ -7,12 +7,13 @@
  *
  * HBM-bound: x is read once and q, k, v written once (2 x 2 C bytes a row). Without a q operand (the state-only
  * fill reads no q) the q columns are neither read nor computed; the conv state still takes every channel of each
- * sequence's last three rows, so x's q columns need be valid only there. A warp takes 16 rows of a pair of
- * 128-channel head columns, lane l channels 8 (l % 16)..+8 of column l / 16 (16-byte loads and stores, a
- * warp's row 512 contiguous bytes); the convolution's three earlier rows ride in registers; when the 16 rows
- * lie in one sequence, all their loads are in flight at once as asynchronous copies into the lane's own
- * shared-memory slots (64 KiB a CTA). A second kernel then writes each sequence's last three input rows into its
- * conv-state slot (it reads the old state first, thread by thread, so the update is in place).
+ * sequence's last three rows, so x's q columns need be valid only there. A warp takes 16 rows of one 128-channel
+ * head column, lane l channels 4 l..4 l + 3 (8-byte loads and stores, a warp's row 256 contiguous bytes); the
+ * convolution's three earlier rows ride in registers; when the 16 rows lie in one sequence, all their loads are in
+ * flight at once as asynchronous copies into the lane's own shared-memory slots (32 KiB a CTA, three CTAs a SM). The
+ * gates of a row block are one more warp task, a lane per v-head. A second kernel then writes each sequence's last
+ * three input rows into its conv-state slot (it reads the old state first, thread by thread, so the update is in
+ * place).
  */
 #include <cuda_bf16.h>
 
@@ -23,20 +24,18 @@ namespace {
 
 constexpr int kRows = 16;        /* rows a warp task */
 constexpr int kThreads = 256;
-constexpr int kStageBytes = (kThreads / 32) * kRows * 512;   /* a warp's 16 rows of 512 bytes, for every warp */
+constexpr int kStageBytes = (kThreads / 32) * kRows * 256;   /* a warp's 16 rows of 256 bytes, for every warp */
 
-/* 16-byte asynchronous copy global -> shared (through L2 only), in the current cp.async group. */
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src) : "memory");
+/* 8-byte asynchronous copy global -> shared, in the current cp.async group. */
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src) : "memory");
 }
 
-__device__ __forceinline__ void unpack8(uint4 v, float (&f)[8]) {
-    const uint32_t w[4] = { v.x, v.y, v.z, v.w };
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        f[2 * e] = __uint_as_float(w[e] << 16);
-        f[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
-    }
+__device__ __forceinline__ void unpack4(uint2 v, float (&f)[4]) {
+    f[0] = __uint_as_float(v.x << 16);
+    f[1] = __uint_as_float(v.x & 0xffff0000u);
+    f[2] = __uint_as_float(v.y << 16);
+    f[3] = __uint_as_float(v.y & 0xffff0000u);
 }
 
 /* Two f32 as a bf16 pair, rounded to nearest even by the hardware conversion (one instruction for both). */
@@ -73,81 +72,100 @@ __device__ __forceinline__ int64_t history_slot(const RidgeFillConvPrep& g, int6
     return has ? slot : -1;
 }
 
-/* Channels c..c+7 of input row `row` of the sequence starting at s0 (row >= s0 - 3): x, or the state's
+/* Channels c..c+3 of input row `row` of the sequence starting at s0 (row >= s0 - 3): x, or the state's
  * history row (s0 - row rows back), or zero. */
-__device__ __forceinline__ uint4 window_row(const RidgeFillConvPrep& g, int64_t slot, int64_t s0, int64_t row, int64_t c,
+__device__ __forceinline__ uint2 window_row(const RidgeFillConvPrep& g, int64_t slot, int64_t s0, int64_t row, int64_t c,
                                             int64_t C) {
-    if (row >= s0) return *(const uint4*)(g.x + row * g.x_row + c);
-    if (slot < 0) return make_uint4(0u, 0u, 0u, 0u);
-    return *(const uint4*)(g.state + slot * g.st_slot + (3 - (s0 - row)) * C + c);
+    if (row >= s0) return *(const uint2*)(g.x + row * g.x_row + c);
+    if (slot < 0) return make_uint2(0u, 0u);
+    return *(const uint2*)(g.state + slot * g.st_slot + (3 - (s0 - row)) * C + c);
 }
 
-/* SiLU u / (1 + e^-u) with the fast exp and divide (well inside bf16's rounding), except where the fast divide
- * returns 0: a denominator above 2^126 (u below about -87.3, where the value is about u e^u, under 1e-36 in
- * magnitude) takes the exact division, so those rows keep their tiny values as the f32 rule gives them. */
+/* SiLU u / (1 + e^-u) as u times the approximate reciprocal (1 ulp) of the denominator, with the fast exp: well
+ * inside bf16's rounding. The reciprocal is the non-flushing form, so a denominator above 2^126 (u below about
+ * -87.3, where the value is about u e^u, under 1e-36 in magnitude) still gives the tiny value the f32 rule gives,
+ * not 0; an infinite one (u below about -88.7) gives -0, as the division does. */
 __device__ __forceinline__ float silu(float u) {
-    const float den = 1.0f + __expf(-u);
-    return den < 0x1p126f ? __fdividef(u, den) : u / den;
+    float r;
+    asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(1.0f + __expf(-u)));
+    return u * r;
 }
 
-/* A warp takes kRows rows of a pair of 128-channel head columns (2 j, 2 j + 1; the pair is q / k or v alike,
- * as 2 Hk is even): half-warp hw owns column 2 j + hw, lane l of the half channels 8 l..8 l + 7. */
-__global__ void __launch_bounds__(kThreads) conv_prep_kernel(RidgeFillConvPrep g) {
-    extern __shared__ uint4 rows_smem[];   /* [warp][kRows][lane] */
-    const int lane = threadIdx.x & 31, hw = lane >> 4, hl = lane & 15;
-    uint4* stage = rows_smem + (threadIdx.x >> 5) * kRows * 32 + lane;
-    const int64_t hk = g.n_head_k, hv = g.n_head_v;
-    const int64_t C = 2 * hk * 128 + hv * 128, n_hc = C / 128, n_pairs = (n_hc + 1) / 2;
-    /* without a q output the q columns are not computed: the pairs start at the first that holds a k column */
-    const int64_t first = g.q ? 0 : hk / 2, pairs = n_pairs - first;
-    const int64_t tasks = (g.T + kRows - 1) / kRows * pairs;
+/* The gates of rows [r0, r1) for every v-head, lane = head (coalesced over the heads): rows outside every sequence
+ * are left untouched. */
+__device__ void gate_rows(const RidgeFillConvPrep& g, int64_t r0, int64_t r1, int lane) {
+    int64_t s0 = 0, e0 = 0;
+    const int seq0 = find_seq(g, r0, &s0, &e0);
+    const bool all_in = seq0 >= 0 && e0 >= r1;
+    for (int64_t h = lane; h < g.n_head_v; h += 32) {
+        const float neg_a = -expf(g.a_log[h]), dtb = g.dt_bias[h];
+        int64_t s = s0, e = e0;
+        int seq = seq0;
+        for (int64_t r = r0; r < r1; ++r) {
+            if (!all_in && (seq < 0 || r >= e)) {
+                seq = find_seq(g, r, &s, &e);
+                if (seq < 0) continue;
+            }
+            const float av = rf::bf16_bits_to_f32(g.a[r * g.a_row + h]);
+            const float bv = rf::bf16_bits_to_f32(g.b[r * g.b_row + h]);
+            g.g[r * g.g_row + h] = neg_a * ridgefill_softplus(av + dtb);
+            g.beta[r * g.beta_row + h] = 1.0f / (1.0f + expf(-bv));
+        }
+    }
+}
+
+/* Tasks of kRows rows: per row block, one task per computed 128-channel head column (a warp; lane l channels
+ * 4 l..4 l + 3) and one gate task (gate_rows). The block's tasks are consecutive, so the warps of a wave share
+ * rows. In a head task the convolution's three earlier rows ride in registers; when the rows lie in one sequence
+ * all their loads are in flight at once as asynchronous copies into the lane's own shared-memory slots (4 KiB a
+ * warp), so 78 registers and 32 KiB a CTA leave room for three CTAs (24 warps) a SM. */
+__global__ void __launch_bounds__(kThreads, 3) conv_prep_kernel(RidgeFillConvPrep g) {
+    extern __shared__ uint2 rows_smem[];   /* [warp][kRows][lane] */
+    const int lane = threadIdx.x & 31;
+    uint2* stage = rows_smem + (threadIdx.x >> 5) * kRows * 32 + lane;
+    const int64_t hk = g.n_head_k;
+    const int64_t C = 2 * hk * 128 + g.n_head_v * 128, n_hc = C / 128;
+    /* without a q output the q columns are not computed */
+    const int64_t first = g.q ? 0 : hk, live = n_hc - first, per_block = live + 1;
+    const int64_t tasks = (g.T + kRows - 1) / kRows * per_block;
     const int64_t stride = (int64_t)gridDim.x * (kThreads / 32);
     for (int64_t task = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); task < tasks; task += stride) {
-        const int64_t pair = first + task % pairs, r0 = task / pairs * kRows, r1 = min(r0 + kRows, g.T);
-        const int64_t hc = 2 * pair + hw;
-        /* an odd column count leaves the last pair's second half idle; an odd hk without q, the first pair's first */
-        const bool live = hc < n_hc && (g.q != nullptr || hc >= hk);
-        const int64_t c = (live ? hc : 2 * pair) * 128 + 8 * hl;
-        const bool norm = 2 * pair < 2 * hk;         /* q and k columns are L2-normalised; the pair is alike */
-        float wt[8][4], bs[8];
+        const int64_t blk = task / per_block, j = task - blk * per_block;
+        const int64_t r0 = blk * kRows, r1 = min(r0 + kRows, g.T);
+        if (j == live) {
+            gate_rows(g, r0, r1, lane);
+            continue;
+        }
+        const int64_t hc = first + j, c = hc * 128 + 4 * lane;
+        const bool norm = hc < 2 * hk;   /* q and k columns are L2-normalised */
+        float wt[4][4], bs[4];
         {
+            const uint4 w01 = *(const uint4*)(g.w + c * 4), w23 = *(const uint4*)(g.w + c * 4 + 8);
+            const uint32_t ww[8] = { w01.x, w01.y, w01.z, w01.w, w23.x, w23.y, w23.z, w23.w };
 #pragma unroll
-            for (int q4 = 0; q4 < 4; ++q4) {         /* channels c + 2 q4, c + 2 q4 + 1: 16 bytes of taps */
-                const uint4 wv = *(const uint4*)(g.w + (c + 2 * q4) * 4);
-                const uint32_t ww[4] = { wv.x, wv.y, wv.z, wv.w };
+            for (int e = 0; e < 4; ++e)
 #pragma unroll
-                for (int h = 0; h < 2; ++h)
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const uint32_t word = ww[2 * h + (j >> 1)];
-                        wt[2 * q4 + h][j] = __uint_as_float((j & 1) ? (word & 0xffff0000u) : (word << 16));
-                    }
-            }
-            if (g.bias) unpack8(*(const uint4*)(g.bias + c), bs);
+                for (int t = 0; t < 4; ++t) {
+                    const uint32_t word = ww[2 * e + (t >> 1)];
+                    wt[e][t] = __uint_as_float((t & 1) ? (word & 0xffff0000u) : (word << 16));
+                }
+            if (g.bias) unpack4(*(const uint2*)(g.bias + c), bs);
             else {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) bs[e] = 0.0f;
+                for (int e = 0; e < 4; ++e) bs[e] = 0.0f;
             }
         }
         const int kind = hc < hk ? 0 : (hc < 2 * hk ? 1 : 2);   /* q, k, v */
         const int64_t head = kind == 0 ? hc : (kind == 1 ? hc - hk : hc - 2 * hk);
-        uint16_t* out = kind == 0 ? g.q + head * g.q_head : (kind == 1 ? g.k + head * g.k_head : g.v + head * g.v_head);
+        uint16_t* out = (kind == 0 ? g.q + head * g.q_head : (kind == 1 ? g.k + head * g.k_head : g.v + head * g.v_head)) + 4 * lane;
         const int64_t out_row = kind == 0 ? g.q_row : (kind == 1 ? g.k_row : g.v_row);
-        const bool gate = live && kind == 2 && hl == 0;   /* the row-by-row path's gate lane */
-        const float neg_a = live && kind == 2 ? -expf(g.a_log[head]) : 0.0f, dtb = live && kind == 2 ? g.dt_bias[head] : 0.0f;
 
-        float w0[8], w1[8], w2[8];   /* rows r-3, r-2, r-1 */
-        /* one row: the convolution over (w0, w1, w2, cur), SiLU, the head's L2 norm for q and k, bf16 out; the gate */
-        auto gate_row = [&](int64_t r) {   /* g and beta of row r for this half's v-head */
-            const float av = rf::bf16_bits_to_f32(g.a[r * g.a_row + head]);
-            const float bv = rf::bf16_bits_to_f32(g.b[r * g.b_row + head]);
-            g.g[r * g.g_row + head] = neg_a * ridgefill_softplus(av + dtb);
-            g.beta[r * g.beta_row + head] = 1.0f / (1.0f + expf(-bv));
-        };
-        auto emit = [&](int64_t r, const float (&cur)[8], bool with_gate) {
-            float y[8];
+        float w0[4], w1[4], w2[4];   /* rows r-3, r-2, r-1 */
+        /* one row: the convolution over (w0, w1, w2, cur), SiLU, the head's L2 norm for q and k, bf16 out */
+        auto emit = [&](uint16_t* dst, const float (&cur)[4]) {
+            float y[4];
 #pragma unroll
-            for (int e = 0; e < 8; e += 2) {   /* the taps two channels an instruction (packed f32x2, same roundings) */
+            for (int e = 0; e < 4; e += 2) {   /* the taps two channels an instruction (packed f32x2, same roundings) */
                 float u0 = bs[e], u1 = bs[e + 1];
                 rf::fma2_rn(u0, u1, wt[e][0], wt[e + 1][0], w0[e], w0[e + 1]);
                 rf::fma2_rn(u0, u1, wt[e][1], wt[e + 1][1], w1[e], w1[e + 1]);
@@ -159,18 +177,16 @@ __global__ void __launch_bounds__(kThreads) conv_prep_kernel(RidgeFillConvPrep g
             if (norm) {
                 float ss = 0.0f;
 #pragma unroll
-                for (int e = 0; e < 8; ++e) ss = fmaf(y[e], y[e], ss);
-                for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);   /* within the half */
+                for (int e = 0; e < 4; ++e) ss = fmaf(y[e], y[e], ss);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
                 const float inv = rsqrtf(ss + 1e-6f);   /* within 2 ulp: well inside bf16's rounding */
-#pragma unroll
-                for (int e = 0; e < 8; e += 2) rf::mul2_rn(y[e], y[e + 1], y[e], y[e + 1], inv, inv);
+                rf::mul2_rn(y[0], y[1], y[0], y[1], inv, inv);
+                rf::mul2_rn(y[2], y[3], y[2], y[3], inv, inv);
             }
-            if (live)
-                *(uint4*)(out + r * out_row + 8 * hl) = make_uint4(bf16x2(y[0], y[1]), bf16x2(y[2], y[3]), bf16x2(y[4], y[5]),
-                                                                   bf16x2(y[6], y[7]));
-            if (with_gate && gate) gate_row(r);
+            *(uint2*)dst = make_uint2(bf16x2(y[0], y[1]), bf16x2(y[2], y[3]));
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
+            for (int e = 0; e < 4; ++e) {
                 w0[e] = w1[e];
                 w1[e] = w2[e];
                 w2[e] = cur[e];
@@ -178,36 +194,29 @@ __global__ void __launch_bounds__(kThreads) conv_prep_kernel(RidgeFillConvPrep g
         };
         auto prime = [&](int64_t seq, int64_t s0, int64_t r) {
             const int64_t slot = history_slot(g, seq);
-            unpack8(window_row(g, slot, s0, r - 3, c, C), w0);
-            unpack8(window_row(g, slot, s0, r - 2, c, C), w1);
-            unpack8(window_row(g, slot, s0, r - 1, c, C), w2);
+            unpack4(window_row(g, slot, s0, r - 3, c, C), w0);
+            unpack4(window_row(g, slot, s0, r - 2, c, C), w1);
+            unpack4(window_row(g, slot, s0, r - 1, c, C), w2);
         };
 
         int64_t s0 = 0, e0 = 0;
         const int seq0 = find_seq(g, r0, &s0, &e0);
         if (seq0 >= 0 && e0 >= r1) {
-            /* the task's rows lie in one sequence: all their loads in flight at once, as asynchronous copies into
-             * this lane's own shared-memory slots (no register holds them meanwhile) */
+            /* the task's rows lie in one sequence: all their loads in flight at once (no register holds them) */
             const int n = (int)(r1 - r0);
-            const uint16_t* src = g.x + r0 * g.x_row + c;
-            for (int i = 0; i < n; ++i) cp_async16(stage + i * 32, src + i * g.x_row);
+            {
+                const uint16_t* src = g.x + r0 * g.x_row + c;
+                for (int i = 0; i < n; ++i, src += g.x_row) cp_async8(stage + i * 32, src);
+            }
             asm volatile("cp.async.commit_group;" ::: "memory");
             prime(seq0, s0, r0);
-            if (live && kind == 2 && hl < n) gate_row(r0 + hl);   /* the task's gates, a row a lane, up front */
             asm volatile("cp.async.wait_group 0;" ::: "memory");
-            if (n == kRows) {   /* fully unrolled: the window's shifts become register renames */
-#pragma unroll
-                for (int i = 0; i < kRows; ++i) {
-                    float cur[8];
-                    unpack8(stage[i * 32], cur);
-                    emit(r0 + i, cur, false);
-                }
-            } else {
-                for (int i = 0; i < n; ++i) {
-                    float cur[8];
-                    unpack8(stage[i * 32], cur);
-                    emit(r0 + i, cur, false);
-                }
+            uint16_t* dst = out + r0 * out_row;
+#pragma unroll 2
+            for (int i = 0; i < n; ++i, dst += out_row) {
+                float cur[4];
+                unpack4(stage[i * 32], cur);
+                emit(dst, cur);
             }
         } else {
             /* sequence boundaries (or rows outside every sequence) inside the task: row by row */
@@ -223,9 +232,9 @@ __global__ void __launch_bounds__(kThreads) conv_prep_kernel(RidgeFillConvPrep g
                     prime(seq, s0, r);
                     primed = true;
                 }
-                float cur[8];
-                unpack8(*(const uint4*)(g.x + r * g.x_row + c), cur);
-                emit(r, cur, true);
+                float cur[4];
+                unpack4(*(const uint2*)(g.x + r * g.x_row + c), cur);
+                emit(out + r * out_row, cur);
             }
         }
     }
@@ -262,9 +271,9 @@ extern "C" int ridgefill_gdn_conv_prep_device(const RadArgs* a, RadStream s) {
     if (rc != RAD_OK) return rc;
     cudaStream_t stream = rf::as_stream(s);
     const int64_t C = 2 * g.n_head_k * 128 + g.n_head_v * 128;
-    const int64_t tasks = (g.T + kRows - 1) / kRows * ((C / 128 + 1) / 2 - (g.q ? 0 : g.n_head_k / 2));
+    const int64_t tasks = (g.T + kRows - 1) / kRows * (C / 128 - (g.q ? 0 : g.n_head_k) + 1);
     if (tasks > 0) {
-        static int per_sm = 0;   /* resident CTAs a SM (registers and the 64 KiB stage bound it) */
+        static int per_sm = 0;   /* resident CTAs a SM (registers and the 32 KiB stage bound it) */
         if (!per_sm) {
             if (cudaFuncSetAttribute(conv_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStageBytes) != cudaSuccess ||
                 cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, conv_prep_kernel, kThreads, kStageBytes) != cudaSuccess ||

@@ -121,6 +121,15 @@ __device__ __forceinline__ void bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+/* Named barrier `id` over `threads` threads that also ORs `pred` across them: every thread gets the same answer. */
+__device__ __forceinline__ bool bar_any(int id, int threads, bool pred) {
+    uint32_t r;
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbarrier.red.or.pred q, %2, %3, p;\n\t"
+                 "selp.u32 %0, 1, 0, q;\n\t}\n"
+                 : "=r"(r) : "r"((uint32_t)pred), "r"(id), "r"(threads) : "memory");
+    return r != 0;
+}
+
 /* cp.async of 4 bytes (src_bytes 0: zero fill). */
 __device__ __forceinline__ void cp_async4(void* dst, const void* src, int src_bytes) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(rf::saddr(dst)), "l"(src), "r"(src_bytes) : "memory");
@@ -269,8 +278,10 @@ __device__ void locate_chunk(const GdnPlan& p, const int32_t* r0c, const int32_t
     if (seq) *seq = i;
 }
 
-/* T[bi][bj] = -T[bi][bi] * sum_{k=bj}^{bi-1} L[bi][k] T[k][bj] for one 16x16 block, one warp. */
-__device__ void tri_offdiag_block(PrepSmem& s, int bi, int bj, int w) {
+/* T[bi][bj] = -T[bi][bi] * sum_{k=bj}^{bi-1} L[bi][k] T[k][bj] for one 16x16 block, one warp (s: any shared
+ * layout with the f16 tiles l16, t16 of pitch TP and per-warp staging tmp). */
+template <class Smem>
+__device__ void tri_offdiag_block(Smem& s, int bi, int bj, int w) {
     const int l = threadIdx.x & 31, g = l >> 2, t = l & 3;
     float acc[2][4] = {};
     for (int k = bj; k < bi; ++k) {
@@ -1087,6 +1098,494 @@ gdn_fill_fused_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
     }
 }
 
+/* ------------------------------------------------------------------ the state-only fill, one CTA a head
+ *
+ * For launches with many chains (every DeltaNet layer of a pass side by side: hundreds of v-heads), one
+ * persistent CTA per SM takes whole chains (v-head, sequence) in turn and runs both phases of each itself, the
+ * transform of chunk c + 1 beside the chain's products of chunk c, handing everything over in shared and tensor
+ * memory (no workspace, no flags, no cross-CTA waits; a plain launch).
+ *
+ *   warps 0-3   the transform (lane quarter w): G, beta; x2 = beta v and, once K K^T is in tensor memory, the
+ *               rows of A (warps 0, 1) beside x1 = beta gamma k and K~ = exp(G_L - G) k (warps 2, 3), all f16
+ *               in shared memory; T = (I + A)^-1 by the blocked inversion of phase 1; T as a K-major operand;
+ *               then W^T from tensor memory into the chain's B operand (f16, MN-major [dk][rows])
+ *   warps 4-11  the chain's lanes (quarter w & 3, column half (w - 4) >> 2): V'^T = U~^T - S W^T straight from
+ *               tensor memory (U~^T never leaves it), the f16 state, gamma_L S; the final state to memory
+ *   warp 12     the loader: k and v rows by TMA, g and beta by cp.async, two chunks in flight
+ *   warp 13     lane 0 issues every product (kind::f16, f32 accumulation):
+ *                 K K^T   (M 128 rows of k (the upper 64 unused), N 64, K 128 dk; bf16)    -> tensor memory
+ *                 W^T     = x1^T T^T  (M 128 dk, N 64 rows, K 64; A MN-major)               -> tensor memory
+ *                 U~^T    = x2^T T^T  (M 128 dv, N 64, K 64; A MN-major)                    -> tensor memory
+ *                 D1      = S W^T     (M 128 dv, N 64, K 128; A the f16 state in tensor memory, B MN-major)
+ *                 D2     += V'^T K~   (M 128 dv, N 128 dk, K 64; B MN-major; D2 = gamma_L S before)
+ *               in the order K K^T(c+1), D1(c), D2(c), W^T(c+1), U~^T(c+1).
+ * Every hand-over is an mbarrier with a bounded wait; no barrier can run two phases ahead of a waiter (each
+ * completion needs the waiter's own previous step). */
+constexpr int kHdP = 4, kHdC = 8, kHdLoad = kHdP + kHdC, kHdMma = kHdLoad + 1;
+constexpr int kHdThreads = 32 * (kHdMma + 1);
+/* Tensor-memory columns: D1 (64), the f16 state A_S (64), D2 (128), K K^T (64), W^T (64), U~^T (64), V'^T A_V (32). */
+constexpr uint32_t kHdD1 = 0, kHdAs = 64, kHdD2 = 128, kHdKk = 256, kHdWt = 320, kHdUt = 384, kHdAv = 448;
+constexpr uint32_t kIdescKk = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(64 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+constexpr uint32_t kIdescWu = (1u << 4) | (1u << 15) /* A MN-major */ | ((uint32_t)(64 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+constexpr uint32_t kIdescD1 = (1u << 4) | (1u << 16) /* B MN-major */ | ((uint32_t)(64 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+/* Launches of at least this many chains take this form (fewer chains leave SMs idle; the cooperative form
+ * spreads a few chains' transforms over every SM). */
+constexpr int64_t kHeadFormChains = 64;
+
+struct HdStage {                 /* one chunk's inputs; x1 and x2 replace k and v in place */
+    uint16_t k[2][C][C];
+    uint16_t v[2][C][C];
+    float g[C], b[C];
+    uint8_t pad[512];
+};
+
+struct HdSmem {
+    HdStage in[2];
+    uint16_t kt[2][2][C][C];     /* K~ [rows][dk] (the k tile's layout), by chunk parity */
+    uint16_t wt[2][D][C];        /* W^T [dk][rows], 128-byte swizzled rows, by chunk parity */
+    uint16_t tsw[C][C];          /* T [rows][rows], 128-byte swizzled (K-major) */
+    uint16_t l16[C][TP];         /* A, f16 */
+    uint16_t t16[C][TP];         /* T, f16 */
+    float a32[4][16][20];        /* A's diagonal blocks, f32 */
+    uint16_t tmp[4][16][24];
+    struct Meta {
+        float G[C], beta[C], gl[4];
+    } meta[2];                   /* by chunk parity */
+    uint64_t landed[2], stage_free[2], buf_free[2];
+    uint64_t kk_full, t_ready, wt_full, ut_full, tsw_free, w_ready, d1_full, d2_full, as_ready, av_ready, d2_ready;
+    uint32_t tmem;
+    int abort;
+};
+static_assert(sizeof(HdStage) % 1024 == 0 && offsetof(HdSmem, kt) % 1024 == 0 && offsetof(HdSmem, wt) % 1024 == 0 &&
+              offsetof(HdSmem, tsw) % 1024 == 0, "operand tiles on 1024 bytes");
+constexpr int kHdSmem = (int)sizeof(HdSmem) + 1024;
+
+struct HdChain {
+    int64_t h, seq, slot, r0, r1, chunks;
+};
+
+/* Chain `cid` (v-head cid % Hv of sequence cid / Hv): its rows (cu_seqlens clamped into [0, T]) and state slot;
+ * chunks 0 when the slot lies outside the pool or the sequence is empty (the chain is skipped). */
+__device__ HdChain hd_chain(const RidgeFillGdn& g, int64_t cid) {
+    HdChain c;
+    c.h = cid % g.n_head_v;
+    c.seq = cid / g.n_head_v;
+    c.r0 = min(max((int64_t)g.cu[c.seq], (int64_t)0), g.T);
+    c.r1 = min(max((int64_t)g.cu[c.seq + 1], c.r0), g.T);
+    c.slot = g.state_idx[c.seq * g.idx_pitch];
+    c.chunks = (c.slot < 0 || c.slot >= g.n_states) ? 0 : (c.r1 - c.r0 + C - 1) / C;
+    return c;
+}
+
+__global__ void __launch_bounds__(kHdThreads, 1)
+gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const RidgeFillGdn g) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    HdSmem& s = *(HdSmem*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
+    const int64_t n_chains = g.n_head_v * g.n_seq;
+    volatile int* abort = &s.abort;
+    if (tid == 0) {
+        for (int b = 0; b < 2; ++b) {
+            rf::mbar_init(&s.landed[b], 1 + 32);   /* the TMA bytes' arrival and the loader's 32 lanes */
+            rf::mbar_init(&s.stage_free[b], 1);
+            rf::mbar_init(&s.buf_free[b], 1);
+        }
+        rf::mbar_init(&s.kk_full, 1);
+        rf::mbar_init(&s.wt_full, 1);
+        rf::mbar_init(&s.ut_full, 1);
+        rf::mbar_init(&s.tsw_free, 1);
+        rf::mbar_init(&s.d1_full, 1);
+        rf::mbar_init(&s.d2_full, 1);
+        rf::mbar_init(&s.t_ready, kHdP);
+        rf::mbar_init(&s.w_ready, kHdP);
+        rf::mbar_init(&s.as_ready, kHdC);
+        rf::mbar_init(&s.av_ready, kHdC);
+        rf::mbar_init(&s.d2_ready, kHdC);
+        s.abort = 0;
+        rf::mbar_init_fence();
+    }
+    if (w == kHdMma) rf::tmem_alloc<512>(&s.tmem);
+    /* T's blocks above the diagonal stay zero (nothing writes them) */
+    for (int i = tid; i < C * TP / 2; i += kHdThreads) ((uint32_t*)&s.t16[0][0])[i] = 0u;
+    rf::tc_fence_before();
+    __syncthreads();
+    rf::tc_fence_after();
+    const uint32_t tmem = s.tmem;
+    /* every role walks the same chains and numbers their chunks q = 0, 1, ... across them */
+    int64_t total = 0;
+    for (int64_t cid = blockIdx.x; cid < n_chains; cid += gridDim.x) total += hd_chain(g, cid).chunks;
+
+    if (w == kHdLoad) {
+        /* ------------------------------------------------------------ the loader (whole warp) */
+        int64_t q = 0;
+        bool ok = true;
+        for (int64_t cid = blockIdx.x; cid < n_chains && ok; cid += gridDim.x) {
+            const HdChain ch = hd_chain(g, cid);
+            const int64_t hk = ch.h / (g.n_head_v / g.n_head_k);
+            for (int64_t j = 0; j < ch.chunks; ++j, ++q) {
+                const int st = (int)(q & 1);
+                if (q >= 2) ok = rf::mbar_wait(&s.stage_free[st], (uint32_t)(((q >> 1) - 1) & 1), abort, rf::kErrGdnWait);
+                if (!__all_sync(0xffffffffu, ok)) {
+                    ok = false;
+                    break;
+                }
+                const int64_t row0 = ch.r0 + j * C;
+                const int len = (int)min((int64_t)C, ch.r1 - row0);
+                HdStage& sg = s.in[st];
+                if (l == 0) {
+                    rf::mbar_arrive_expect_tx(&s.landed[st], 2 * kTileBytes);
+                    rf::tma_load_3d(&sg.k[0][0][0], &kmap, &s.landed[st], 0, (int)hk, (int)row0);
+                    rf::tma_load_3d(&sg.k[1][0][0], &kmap, &s.landed[st], C, (int)hk, (int)row0);
+                    rf::tma_load_3d(&sg.v[0][0][0], &vmap, &s.landed[st], 0, (int)ch.h, (int)row0);
+                    rf::tma_load_3d(&sg.v[1][0][0], &vmap, &s.landed[st], C, (int)ch.h, (int)row0);
+                }
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                    const int r = l + 32 * hf;
+                    const int64_t row = row0 + (r < len ? r : 0);
+                    cp_async4(&sg.g[r], g.g + row * g.g_row + ch.h, r < len ? 4 : 0);
+                    cp_async4(&sg.b[r], g.beta + row * g.b_row + ch.h, r < len ? 4 : 0);
+                }
+                rf::cp_async_wait_all();
+                rf::mbar_arrive(&s.landed[st]);
+            }
+        }
+        /* copies still in flight land before the CTA leaves (bounded) */
+        if (l == 0)
+            for (int64_t i = q > 2 ? q - 2 : 0; i < q; ++i) {
+                const uint64_t t0 = rf::global_ns();
+                while (!rf::mbar_try_wait(&s.landed[i & 1], (uint32_t)((i >> 1) & 1)) && rf::global_ns() - t0 < rf::kWaitTimeoutNs) {
+                }
+            }
+    } else if (w == kHdMma) {
+        /* ------------------------------------------------------------ the product issuer (one lane) */
+        if (l == 0 && total > 0) {
+            auto kkt = [&](int64_t q) -> bool {   /* K K^T of chunk q */
+                const int st = (int)(q & 1);
+                if (!rf::mbar_wait(&s.landed[st], (uint32_t)((q >> 1) & 1), abort, rf::kErrGdnWait)) return false;
+                rf::tc_fence_after();
+                const uint32_t kt = rf::saddr(&s.in[st].k[0][0][0]);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint64_t d = rf::sw128_kmajor_desc(kt + (kk >> 2) * 8192 + (kk & 3) * 32);
+                    rf::umma_f16(tmem + kHdKk, d, d, kIdescKk, kk > 0);
+                }
+                rf::mma_commit(&s.kk_full);
+                return true;
+            };
+            auto wu = [&](int64_t q) -> bool {   /* W^T and U~^T of chunk q */
+                if (!rf::mbar_wait(&s.t_ready, (uint32_t)(q & 1), abort, rf::kErrGdnWait)) return false;
+                rf::tc_fence_after();
+                const int st = (int)(q & 1);
+                const uint32_t x1 = rf::saddr(&s.in[st].k[0][0][0]), x2 = rf::saddr(&s.in[st].v[0][0][0]);
+                const uint32_t tt = rf::saddr(&s.tsw[0][0]);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    rf::umma_f16(tmem + kHdWt, rf::sw128_mnmajor_desc(x1 + kk * 2048, 8192), rf::sw128_kmajor_desc(tt + kk * 32),
+                                 kIdescWu, kk > 0);
+                rf::mma_commit(&s.wt_full);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    rf::umma_f16(tmem + kHdUt, rf::sw128_mnmajor_desc(x2 + kk * 2048, 8192), rf::sw128_kmajor_desc(tt + kk * 32),
+                                 kIdescWu, kk > 0);
+                rf::mma_commit(&s.ut_full);
+                rf::mma_commit(&s.stage_free[st]);
+                rf::mma_commit(&s.tsw_free);
+                return true;
+            };
+            bool ok = kkt(0) && wu(0);
+            for (int64_t q = 0; q < total && ok; ++q) {
+                const uint32_t par = (uint32_t)(q & 1);
+                if (q + 1 < total && !(ok = kkt(q + 1))) break;
+                /* D1 = S W^T: the lanes wrote this chunk's f16 state, the transform its W^T tile */
+                if (!(ok = rf::mbar_wait(&s.as_ready, par, abort, rf::kErrGdnWait) &&
+                           rf::mbar_wait(&s.w_ready, par, abort, rf::kErrGdnWait)))
+                    break;
+                rf::tc_fence_after();
+                const uint32_t wt = rf::saddr(&s.wt[par][0][0]);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    rf::umma_f16_ts(tmem + kHdD1, tmem + kHdAs + 8 * kk, rf::sw128_mnmajor_desc(wt + kk * 2048, 8192), kIdescD1, kk > 0);
+                rf::mma_commit(&s.d1_full);
+                /* D2 += V'^T K~: the lanes wrote V' and put gamma_L S into D2 */
+                if (!(ok = rf::mbar_wait(&s.av_ready, par, abort, rf::kErrGdnWait) &&
+                           rf::mbar_wait(&s.d2_ready, par, abort, rf::kErrGdnWait)))
+                    break;
+                rf::tc_fence_after();
+                const uint32_t kt = rf::saddr(&s.kt[par][0][0][0]);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    rf::umma_f16_ts(tmem + kHdD2, tmem + kHdAv + 8 * kk, rf::sw128_mnmajor_desc(kt + kk * 2048, 8192), kIdescUp, 1);
+                rf::mma_commit(&s.d2_full);
+                rf::mma_commit(&s.buf_free[par]);   /* K~ and W^T of this parity are read */
+                if (q + 1 < total) ok = wu(q + 1);
+            }
+        }
+    } else if (w < kHdP) {
+        /* ------------------------------------------------------------ the transform (warps 0-3) */
+        auto psync = [&]() { bar_sync(1, 32 * kHdP); };
+        /* a barrier of the four warps that also tells all of them whether any thread's wait gave up */
+        auto failed = [&](bool ok) { return bar_any(1, 32 * kHdP, !ok || *abort); };
+        int64_t q = 0;
+        bool stop = false;
+        for (int64_t cid = blockIdx.x; cid < n_chains && !stop; cid += gridDim.x) {
+            const HdChain ch = hd_chain(g, cid);
+            for (int64_t j = 0; j < ch.chunks; ++j, ++q) {
+                const int st = (int)(q & 1), par = (int)(q & 1);
+                const int len = (int)min((int64_t)C, ch.r1 - (ch.r0 + j * C));
+                HdStage& sg = s.in[st];
+                HdSmem::Meta& mt = s.meta[par];
+                if ((stop = failed(rf::mbar_wait(&s.landed[st], (uint32_t)((q >> 1) & 1), abort, rf::kErrGdnWait)))) break;
+                /* G (inclusive cumulative log decay; zero past the chunk) by warp 0, two rows a lane; beta */
+                if (w == 0) {
+                    const float2 gg = *(const float2*)&sg.g[2 * l];
+                    const float pair = gg.x + gg.y;
+                    float x = pair;
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const float y = __shfl_up_sync(0xffffffffu, x, o);
+                        if (l >= o) x += y;
+                    }
+                    *(float2*)&mt.G[2 * l] = make_float2(x - pair + gg.x, x);
+                } else if (w == 1) {
+                    *(float2*)&mt.beta[2 * l] = *(const float2*)&sg.b[2 * l];
+                }
+                psync();
+                const float gl = mt.G[len - 1];
+                if (tid == 0) mt.gl[0] = __expf(gl);
+                const uint32_t ktile = rf::saddr(&sg.k[0][0][0]), vtile = rf::saddr(&sg.v[0][0][0]);
+                /* x2 = beta v in place: row tid & 63, column half tid >> 6 */
+                {
+                    const int r = tid & 63;
+                    const bool in = r < len;
+                    const float br = mt.beta[r];
+#pragma unroll
+                    for (int it = 0; it < 8; ++it) {
+                        const uint32_t off = rf::sw128_off(r, (8 * (tid >> 6) + it) * 8);
+                        sts128(vtile + off, scale_bf16x8_to_f16(lds128(vtile + off), br, in));
+                    }
+                }
+                /* K K^T landed in tensor memory (so x1 may replace the k tile); K~'s tile of this parity free once D2
+                 * of two chunks ago has read it */
+                bool ok = rf::mbar_wait(&s.kk_full, (uint32_t)par, abort, rf::kErrGdnWait);
+                if (w >= 2 && q >= 2) ok = ok && rf::mbar_wait(&s.buf_free[par], (uint32_t)(((q >> 1) - 1) & 1), abort, rf::kErrGdnWait);
+                if ((stop = failed(ok))) break;
+                rf::tc_fence_after();
+                if (w < 2) {
+                    /* A's rows: thread = row i, its 64 columns from tensor memory */
+                    const int i = 32 * w + l;
+                    uint32_t kk[2][32];
+                    const uint32_t base = tmem + ((uint32_t)(32 * w) << 16) + kHdKk;
+                    rf::tmem_ld32(base, kk[0]);
+                    rf::tmem_ld32(base + 32, kk[1]);
+                    rf::tmem_ld_wait();
+                    rf::tc_fence_before();
+                    const bool rowin = i < len;
+                    const float Gi = mt.G[i], bi = mt.beta[i];
+#pragma unroll
+                    for (int jj = 0; jj < C; jj += 2) {
+                        float v[2];
+#pragma unroll
+                        for (int e = 0; e < 2; ++e)
+                            v[e] = (jj + e < i && rowin) ? bi * __expf(Gi - mt.G[jj + e]) * __uint_as_float(kk[jj >> 5][(jj + e) & 31]) : 0.0f;
+                        *(uint32_t*)&s.l16[i][jj] = rf::pack_f16(v[0], v[1]);
+                        if ((jj >> 4) == (i >> 4)) *(float2*)&s.a32[i >> 4][i & 15][jj & 15] = make_float2(v[0], v[1]);
+                    }
+                } else {
+                    /* x1 = beta gamma k in place and K~ = exp(G_L - G) k into this parity's tile: thread = row r */
+                    const int r = tid - 64;
+                    const bool in = r < len;
+                    const float gr = mt.G[r], br = mt.beta[r];
+                    const float fk = in ? __expf(gl - gr) : 0.0f, fx = in ? br * __expf(gr) : 0.0f;
+                    const uint32_t kst = rf::saddr(&s.kt[par][0][0][0]);
+#pragma unroll 4
+                    for (int seg = 0; seg < 16; ++seg) {
+                        const uint32_t off = rf::sw128_off(r, seg * 8);
+                        const uint4 kr = lds128(ktile + off);
+                        sts128(kst + off, scale_bf16x8_to_f16(kr, fk, in));
+                        sts128(ktile + off, scale_bf16x8_to_f16(kr, fx, in));
+                    }
+                }
+                psync();
+                /* diagonal blocks of T by substitution in f32: warp w block w, lane l row l & 15 of 8 columns */
+                {
+                    const int r = l & 15, c0 = 8 * (l >> 4);
+                    float a[16];
+#pragma unroll
+                    for (int q4 = 0; q4 < 4; ++q4) {
+                        const float4 v = *(const float4*)&s.a32[w][r][4 * q4];
+                        a[4 * q4] = v.x;
+                        a[4 * q4 + 1] = v.y;
+                        a[4 * q4 + 2] = v.z;
+                        a[4 * q4 + 3] = v.w;
+                    }
+                    float x[8];
+#pragma unroll
+                    for (int cc = 0; cc < 8; ++cc) x[cc] = r == c0 + cc ? 1.0f : 0.0f;
+#pragma unroll
+                    for (int jj = 0; jj < 15; ++jj)
+#pragma unroll
+                        for (int cc = 0; cc < 8; ++cc) {
+                            const float xj = __shfl_sync(0xffffffffu, x[cc], (l & 16) | jj);
+                            x[cc] = fmaf(-(jj < r ? a[jj] : 0.0f), xj, x[cc]);
+                        }
+                    *(uint4*)&s.t16[16 * w + r][16 * w + c0] = make_uint4(rf::pack_f16(x[0], x[1]), rf::pack_f16(x[2], x[3]),
+                                                                          rf::pack_f16(x[4], x[5]), rf::pack_f16(x[6], x[7]));
+                }
+                psync();
+                if (w < 3) tri_offdiag_block(s, w + 1, w, w);   /* T10, T21, T32 */
+                psync();
+                if (w < 2) tri_offdiag_block(s, w + 2, w, w);   /* T20, T31 */
+                psync();
+                if (w == 0) tri_offdiag_block(s, 3, 0, 0);      /* T30 */
+                /* T into its operand tile, free once the previous chunk's W^T and U~^T have read it */
+                if ((stop = failed(q < 1 || rf::mbar_wait(&s.tsw_free, (uint32_t)((q - 1) & 1), abort, rf::kErrGdnWait)))) break;
+                {
+                    const uint32_t tt = rf::saddr(&s.tsw[0][0]);
+                    const int r = tid >> 1;
+#pragma unroll
+                    for (int c4 = 0; c4 < 4; ++c4) {
+                        const int cc = 4 * (tid & 1) + c4;
+                        sts128(tt + rf::sw128_off(r, 8 * cc), *(const uint4*)&s.t16[r][8 * cc]);
+                    }
+                }
+                rf::fence_proxy_async_smem();   /* x1, x2, K~ and T for the tensor cores */
+                __syncwarp();
+                if (l == 0) rf::mbar_arrive(&s.t_ready);
+                /* W^T from tensor memory into this parity's B tile of D1 (free: buf_free waited above): thread = dk
+                 * row 32 w + l */
+                if ((stop = failed(rf::mbar_wait(&s.wt_full, (uint32_t)par, abort, rf::kErrGdnWait)))) break;
+                rf::tc_fence_after();
+                {
+                    uint32_t wv[2][32];
+                    const uint32_t base = tmem + ((uint32_t)(32 * w) << 16) + kHdWt;
+                    rf::tmem_ld32(base, wv[0]);
+                    rf::tmem_ld32(base + 32, wv[1]);
+                    rf::tmem_ld_wait();
+                    rf::tc_fence_before();
+                    const uint32_t wtile = rf::saddr(&s.wt[par][0][0]);
+                    const int dk = 32 * w + l;
+#pragma unroll
+                    for (int c8 = 0; c8 < 8; ++c8) {
+                        const uint32_t* x = &wv[c8 >> 2][(c8 & 3) * 8];
+                        sts128(wtile + rf::sw128_off(dk, 8 * c8),
+                               make_uint4(rf::pack_f16(__uint_as_float(x[0]), __uint_as_float(x[1])),
+                                          rf::pack_f16(__uint_as_float(x[2]), __uint_as_float(x[3])),
+                                          rf::pack_f16(__uint_as_float(x[4]), __uint_as_float(x[5])),
+                                          rf::pack_f16(__uint_as_float(x[6]), __uint_as_float(x[7]))));
+                    }
+                }
+                rf::fence_proxy_async_smem();
+                __syncwarp();
+                if (l == 0) rf::mbar_arrive(&s.w_ready);
+            }
+        }
+    } else if (w < kHdLoad) {
+        /* ------------------------------------------------------------ the chain's lanes (warps 4-11) */
+        const int qd = w & 3, hf = (w - kHdP) >> 2, i = 32 * qd + l;   /* dv row i; columns of half hf */
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * qd) << 16);
+        const uint32_t d1 = lane_base + kHdD1 + 32 * hf, d2 = lane_base + kHdD2 + 64 * hf, ut = lane_base + kHdUt + 32 * hf;
+        const uint32_t as = lane_base + kHdAs + 32 * hf, av = lane_base + kHdAv + 16 * hf;
+        auto arrive = [&](uint64_t* bar) {   /* this warp's writes are done: one arrival a warp */
+            __syncwarp();
+            if (l == 0) rf::mbar_arrive(bar);
+        };
+        /* a wait the whole warp leaves together (its tensor-memory accesses are warp-wide) */
+        auto wwait = [&](uint64_t* bar, uint32_t par) {
+            return __all_sync(0xffffffffu, rf::mbar_wait(bar, par, abort, rf::kErrGdnWait));
+        };
+        auto put_as = [&](const uint32_t (&r)[2][32]) {   /* the f16 state into the first product's A (tensor memory) */
+            uint32_t o[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+                o[e] = rf::pack_f16(__uint_as_float(r[e >> 4][(2 * e) & 31]), __uint_as_float(r[e >> 4][(2 * e + 1) & 31]));
+            rf::tmem_st32(as, o);
+            rf::tmem_st_wait();
+            rf::tc_fence_before();
+        };
+        auto put_d2 = [&](uint32_t (&r)[2][32], float gam) {   /* gamma * S into D2 */
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+#pragma unroll
+                for (int e = 0; e < 32; ++e) r[h2][e] = __float_as_uint(gam * __uint_as_float(r[h2][e]));
+                rf::tmem_st32(d2 + 32 * h2, r[h2]);
+            }
+            rf::tmem_st_wait();
+            rf::tc_fence_before();
+        };
+        int64_t q = 0;
+        bool ok = true;
+        for (int64_t cid = blockIdx.x; cid < n_chains && ok; cid += gridDim.x) {
+            const HdChain ch = hd_chain(g, cid);
+            if (ch.chunks == 0) continue;
+            float* srow = g.state + ch.slot * g.st_slot + ch.h * g.st_head + (int64_t)i * D + 64 * hf;
+            uint32_t r[2][32];
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float4 x = *(const float4*)(srow + 32 * h2 + 4 * j);
+                    r[h2][4 * j] = __float_as_uint(x.x);
+                    r[h2][4 * j + 1] = __float_as_uint(x.y);
+                    r[h2][4 * j + 2] = __float_as_uint(x.z);
+                    r[h2][4 * j + 3] = __float_as_uint(x.w);
+                }
+            put_as(r);
+            arrive(&s.as_ready);
+            if (!(ok = wwait(&s.ut_full, (uint32_t)(q & 1)))) break;
+            put_d2(r, s.meta[q & 1].gl[0]);
+            arrive(&s.d2_ready);
+            for (int64_t j = 0; j < ch.chunks && ok; ++j, ++q) {
+                const uint32_t par = (uint32_t)(q & 1);
+                /* V'^T = U~^T - D1 for rows 32 hf..+32 of the chunk, f16 into the second product's A */
+                if (!(ok = wwait(&s.d1_full, par))) break;
+                rf::tc_fence_after();
+                {
+                    uint32_t d[32], u[32], o[16];
+                    rf::tmem_ld32(d1, d);
+                    rf::tmem_ld32(ut, u);
+                    rf::tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 16; ++e)
+                        o[e] = rf::pack_f16(__uint_as_float(u[2 * e]) - __uint_as_float(d[2 * e]),
+                                            __uint_as_float(u[2 * e + 1]) - __uint_as_float(d[2 * e + 1]));
+                    rf::tmem_st16(av, o);
+                    rf::tmem_st_wait();
+                }
+                rf::tc_fence_before();
+                arrive(&s.av_ready);
+                /* the updated state: the next chunk's f16 state first, then gamma_L(next) S into D2 */
+                if (!(ok = wwait(&s.d2_full, par))) break;
+                rf::tc_fence_after();
+                rf::tmem_ld32(d2, r[0]);
+                rf::tmem_ld32(d2 + 32, r[1]);
+                rf::tmem_ld_wait();
+                if (j + 1 == ch.chunks) {
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+                        for (int jj = 0; jj < 8; ++jj)
+                            *(float4*)(srow + 32 * h2 + 4 * jj) =
+                                make_float4(__uint_as_float(r[h2][4 * jj]), __uint_as_float(r[h2][4 * jj + 1]),
+                                            __uint_as_float(r[h2][4 * jj + 2]), __uint_as_float(r[h2][4 * jj + 3]));
+                    rf::tc_fence_before();
+                    continue;
+                }
+                put_as(r);
+                arrive(&s.as_ready);
+                if (!(ok = wwait(&s.ut_full, (uint32_t)((q + 1) & 1)))) break;
+                put_d2(r, s.meta[(q + 1) & 1].gl[0]);
+                arrive(&s.d2_ready);
+            }
+        }
+    }
+    rf::tc_fence_before();
+    __syncthreads();
+    if (w == kHdMma) {
+        rf::tc_fence_after();
+        rf::tmem_free<512>(tmem);
+    }
+}
+
 /* ------------------------------------------------------------------ output (o present) */
 
 /* o_i = scale * S_i q_i over a chunk, from its start state S0 and corrected values U:
@@ -1333,11 +1832,14 @@ bool head_rows_map(CUtensorMap* map, const void* base, int64_t T, int64_t heads,
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+/* The state-only form with at least kHeadFormChains chains runs one CTA a head and needs no workspace. */
+bool head_form(const RidgeFillGdn& g) { return !g.o && g.n_head_v * g.n_seq >= kHeadFormChains; }
+
 }  // namespace
 
 extern "C" int64_t ridgefill_gdn_fill_scratch(const RadArgs* a) {
     RidgeFillGdn g;
-    if (ridgefill_gdn_parse(a, &g) != RAD_OK || g.dk != D) return 0;   /* the per-row form needs none */
+    if (ridgefill_gdn_parse(a, &g) != RAD_OK || g.dk != D || head_form(g)) return 0;   /* the per-row and per-head forms need none */
     const int64_t items = max_slots_of(g) * g.n_head_v;
     return table_bytes(g.n_seq) + kCtlBytes + flag_bytes(items) + items * (kSlotBytes + (g.o ? kOutBytes : 0));
 }
@@ -1349,11 +1851,6 @@ extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
     if (g.n_seq == 0 || g.T == 0) return RAD_OK;
     if (g.n_seq > 65535 || g.n_head_v > 65535 || g.T > 0x7fffffffLL) return RAD_E_SHAPE;
     if (g.dk != D) return launch_small(g, rf::as_stream(s));
-    const int64_t slots = max_slots_of(g), items = slots * g.n_head_v;
-    const int64_t head = table_bytes(g.n_seq) + kCtlBytes + flag_bytes(items);
-    const int64_t need = head + items * (kSlotBytes + (g.o ? kOutBytes : 0));
-    if (!a->scratch || a->scratch_bytes < need || (uintptr_t)a->scratch % 16) return RAD_E_INVAL;
-    if (items > 0x7fffffffLL) return RAD_E_SHAPE;
     /* k and v are read through TMA tensor maps: positive strides below 2^39 elements. */
     const int64_t lim = 1LL << 39;
     if (g.k_row <= 0 || g.k_head <= 0 || g.v_row <= 0 || g.v_head <= 0 || g.k_row >= lim || g.k_head >= lim ||
@@ -1364,6 +1861,20 @@ extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
         !head_rows_map(&vmap, g.v, g.T, g.n_head_v, g.v_row, g.v_head, C, true) ||
         (g.q && !head_rows_map(&qmap, g.q, g.T, g.n_head_k, g.q_row, g.q_head, C, true)))
         return RAD_E_DEVICE;
+    if (head_form(g)) {
+        /* one CTA per SM, each taking whole chains (no workspace, no cross-CTA waits) */
+        if (cudaFuncSetAttribute(gdn_fill_heads_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHdSmem) != cudaSuccess)
+            return RAD_E_DEVICE;
+        const int64_t chains = g.n_head_v * g.n_seq;
+        const int grid = (int)(chains < rf::sm_count() ? chains : rf::sm_count());
+        gdn_fill_heads_kernel<<<grid, kHdThreads, kHdSmem, rf::as_stream(s)>>>(kmap, vmap, g);
+        return rf::launch_status();
+    }
+    const int64_t slots = max_slots_of(g), items = slots * g.n_head_v;
+    const int64_t head = table_bytes(g.n_seq) + kCtlBytes + flag_bytes(items);
+    const int64_t need = head + items * (kSlotBytes + (g.o ? kOutBytes : 0));
+    if (!a->scratch || a->scratch_bytes < need || (uintptr_t)a->scratch % 16) return RAD_E_INVAL;
+    if (items > 0x7fffffffLL) return RAD_E_SHAPE;
     GdnPlan p;
     p.g = g;
     uint8_t* ws = (uint8_t*)a->scratch;

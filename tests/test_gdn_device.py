@@ -255,3 +255,73 @@ def test_fill_state_is_affine_in_its_start(cuda, product_lib):
     want, _ = H.oracle_gdn(k, v, g, beta, state, [0], [0, n])
     assert H.rel_l2(composed, full[0]) <= 3e-3
     assert H.rel_l2(composed, want[0]) <= 3e-3
+
+
+# ------------------------------------------------------------------ the per-head form (>= 64 chains, state only)
+# A state-only call of at least 64 chains (v-heads x sequences) runs one CTA a head, the transform beside the chain
+# in each CTA; the tests above stay below that and exercise the cooperative form.
+
+@pytest.mark.parametrize("T,hk,hv,decay", [(600, 16, 64, "fast"), (333, 32, 64, "slow"), (1100, 8, 96, "very slow")])
+def test_head_form_matches_sequential_rule(cuda, product_lib, T, hk, hv, decay):
+    torch = cuda
+    q, k, v, g, beta, state = H.gdn_inputs(T + hv + 1, T, hk, hv, decay)
+    rc, got, _ = run_fill(product_lib, torch, k, v, g, beta, state, [1], [0, T], hk, hv)
+    assert rc == abi.OK
+    want, _ = H.oracle_gdn(k, v, g, beta, state, [1], [0, T])
+    errs = [H.rel_l2(got[1, h], want[1, h]) for h in range(hv)]
+    assert max(errs) <= STATE_TOL, max(errs)
+    assert np.array_equal(got[0], state[0]) and np.array_equal(got[2], state[2])
+
+
+def test_head_form_varlen_sequences_and_skipped_slots(cuda, product_lib):
+    """Four sequences of 1, 100, 300 and 64 rows over 24 v-heads (96 chains): chunks anchored at each start, the
+    second sequence with no state (slot -1) and the last with a slot outside the pool, both skipped."""
+    torch = cuda
+    q, k, v, g, beta, state = H.gdn_inputs(15, 465, 6, 24, "slow", slots=4)
+    cu, idx = [0, 1, 101, 401, 465], [3, -1, 0, 9]
+    rc, got, _ = run_fill(product_lib, torch, k, v, g, beta, state, idx, cu, 6, 24)
+    assert rc == abi.OK
+    want, _ = H.oracle_gdn(k, v, g, beta, state, idx, cu)
+    for slot in (3, 0):
+        assert H.rel_l2(got[slot], want[slot]) <= STATE_TOL
+    assert np.array_equal(got[1], state[1]) and np.array_equal(got[2], state[2])
+
+
+def test_head_form_agrees_with_the_cooperative_form(cuda, product_lib):
+    """The same 64 v-heads over 2,000 rows: one call (the per-head form) against four calls of 16 heads each (the
+    cooperative form), every head within the state tolerance of the other form."""
+    torch = cuda
+    T, hk, hv = 2000, 32, 64
+    q, k, v, g, beta, state = H.gdn_inputs(23, T, hk, hv, "fast", slots=1)
+    rc, one, _ = run_fill(product_lib, torch, k, v, g, beta, state, [0], [0, T], hk, hv)
+    assert rc == abi.OK
+    per = hv // 4
+    parts = []
+    for p in range(4):
+        hs, ks = slice(p * per, (p + 1) * per), slice(p * per // 2, (p + 1) * per // 2)
+        rc, got, _ = run_fill(product_lib, torch, np.ascontiguousarray(k[:, ks]), np.ascontiguousarray(v[:, hs]),
+                              np.ascontiguousarray(g[:, hs]), np.ascontiguousarray(beta[:, hs]),
+                              np.ascontiguousarray(state[:, hs]), [0], [0, T], per // 2, per)
+        assert rc == abi.OK
+        parts.append(got[0])
+    coop = np.concatenate(parts, axis=0)
+    errs = [H.rel_l2(one[0, h], coop[h]) for h in range(hv)]
+    assert max(errs) <= STATE_TOL, max(errs)
+
+
+def test_head_form_full_size_split_is_one_call(cuda, product_lib):
+    """32,768 rows over 64 v-heads: two calls over [0, T/2) and [T/2, T) with the state carried equal one call bit
+    for bit; four heads against the float32 rule."""
+    torch = cuda
+    T, hk, hv = 32768, 32, 64
+    q, k, v, g, beta, state = H.gdn_inputs(33, T, hk, hv, "fast", slots=1)
+    rc, one, _ = run_fill(product_lib, torch, k, v, g, beta, state, [0], [0, T], hk, hv)
+    assert rc == abi.OK
+    h = T // 2
+    rc1, mid, _ = run_fill(product_lib, torch, k[:h], v[:h], g[:h], beta[:h], state, [0], [0, h], hk, hv)
+    rc2, two, _ = run_fill(product_lib, torch, k[h:], v[h:], g[h:], beta[h:], mid, [0], [0, T - h], hk, hv)
+    assert rc1 == rc2 == abi.OK
+    assert np.array_equal(one.view(np.uint32), two.view(np.uint32))
+    for h0 in (0, 21, 42, 63):
+        want32, _ = H.oracle_gdn(k, v, g, beta, state, [0], [0, T], f64=False, heads=(h0, h0 + 1))
+        assert H.rel_l2(one[0, h0], want32[0, h0]) <= STATE_TOL
