@@ -5,7 +5,8 @@
 A step is one approximate pass of the RidgeFill step over a 32,768-row prefill chunk of the 48-layer stack
 the 24 late layers, 18 Gated DeltaNet and 6 attention layers, through this library's sm_100a
 device rows (late_pass.LatePass): the class mask (30 % of rows exact) and the layer-S stream's codes once, then per
-layer the int8 projector d 2,048 (per-column scales, fused bias), select and the block input's codes; per DeltaNet
+layer the int8 projector d 2,048 (per-column scales, fused bias, written straight into the block input's
+approximated rows: the select fused into its epilogue) and the block input's codes; per DeltaNet
 layer the int8 mixed q|k|v projection, the bf16 a|b projection and conv_prep (16 q/k, 32 v heads x 128); per
 attention layer the int8 k|v projection and the K/V cache write (2 kv heads x 256, imrope); then one fill launch over
 all 18 DeltaNet layers' 576 heads between a state undo and apply over the same heads, rho per layer, the hazard record.

@@ -50,8 +50,9 @@ enum { DR_MASK = 0, DR_IDS };
 enum { HZ_CU = 0, HZ_POS, HZ_BOUNDS, HZ_SPAN, HZ_META, HZ_META_IDX, HZ_COUNT };
 /* ridgefill_gemm_nt_q (kernels/rows.cpp:74-76): a, a_scale, b, b_scale, y, a_sum, b_ref. */
 enum { GQ_A = 0, GQ_A_SCALE, GQ_B, GQ_B_SCALE, GQ_Y, GQ_A_SUM, GQ_B_REF };
-/* ridgefill_gemm_nt_q_bias (new): gemm_nt_q's operands, then the bias and an int32 debug output. */
-enum { GB_A = 0, GB_A_SCALE, GB_B, GB_B_SCALE, GB_BIAS, GB_Y, GB_ACC };
+/* ridgefill_gemm_nt_q_bias (new): gemm_nt_q's operands, then the bias, an int32 debug output and the row
+ * selection (ridgefill_select's mask: only rows whose entry is 1 are written). */
+enum { GB_A = 0, GB_A_SCALE, GB_B, GB_B_SCALE, GB_BIAS, GB_Y, GB_ACC, GB_ROWS };
 /* ridgefill_gemm_nt_bias (kernels/rows.cpp:67-70, oGemm): a, b, bias, res (optional), y. */
 enum { GN_A = 0, GN_B, GN_BIAS, GN_RES, GN_Y };
 /* ridgefill_quant_act_i8g (new; libr4d's quant_act_i8g operands, arch/ridgefill_layer.h:74-76). */
@@ -279,6 +280,7 @@ typedef struct RidgeFillGemmQ {
     const uint16_t* bias;                         /* [N] bf16 or null */
     uint16_t*      y;        int64_t ldy;         /* [M, N] bf16 */
     int32_t*       acc;                           /* optional [M, N, K/group] int32 block sums (debug) */
+    const int32_t* rows;                          /* optional [M]: write row m only where rows[m] == 1 */
     int64_t        M, N, K, group;
     int64_t        max_ctas;                      /* at most this many CTAs (SMs), 0: the whole GPU */
 } RidgeFillGemmQ;
@@ -444,7 +446,8 @@ int ridgefill_wait_selftest(int* flag, int* status, RadStream s);
  * call needs more than 64 MiB: a one-sequence 2,048-row call fits at up to 40 value heads for the state
  * alone, at up to 19 with the output o. The first call on a device resolves the workspace's address there
  * (again after the device's context changes, e.g. after cudaDeviceReset): make it before any stream
- * capture. Calls share the workspace: calls that overlap on the GPU race. Allocates and frees nothing. */
+ * capture. Calls share the workspace: calls that overlap on the GPU race. Allocates and frees nothing. A state-only
+ * call of at least 64 chains (value heads x sequences) takes the per-head form, which uses no workspace. */
 int ridgefill_gdn_fill_noalloc(const RadArgs* a, RadStream s);
 
 /* ridgefill_gdn_fill's scratch hook: device bytes the row needs in RadArgs::scratch. */

@@ -63,7 +63,7 @@ static const RadOperandSpec oGemmQ[] = { RF_IN("a"), RF_IN_OPT("a_scale"), RF_IN
 static const RadParamSpec pGemmQBias[] = { RF_P_INT("M"), RF_P_INT("N"), RF_P_INT("K"), RF_P_INT("group"),
                                            RF_P_STR("dtype"), RF_P_OPT("max_ctas", RAD_P_INT) };
 static const RadOperandSpec oGemmQBias[] = { RF_IN("a"), RF_IN("a_scale"), RF_IN("b"), RF_IN("b_scale"),
-                                             RF_IN_OPT("bias"), RF_OUT("y"), RF_OUT_OPT("acc") };
+                                             RF_IN_OPT("bias"), RF_OUT("y"), RF_OUT_OPT("acc"), RF_IN_OPT("rows") };
 static const RadParamSpec pQuant[] = { RF_P_INT("M"), RF_P_INT("n"), RF_P_INT("group"), RF_P_STR("dtype") };
 static const RadOperandSpec oQuant[] = { RF_IN("x"), RF_OUT("q"), RF_OUT("s") };
 static const RadParamSpec pGdn[] = { RF_P_INT("M"), RF_P_INT("n_head_k"), RF_P_INT("n_head_v"), RF_P_INT("head_k"),
@@ -124,7 +124,9 @@ static const RadOpSchema kSchemas[] = {
 { "ridgefill_gemm_nt_q_bias", RF_ARR(pGemmQBias), RF_ARR(oGemmQBias),
   "ridgefill_gemm_nt_q followed by the row-broadcast bias add, in one pass: y = bf16(bf16(gemm) + bias), "
   "equal bit for bit to the two ops in sequence. Optional acc i32 [M, N, K/group]: every block's int32 sum. "
-  "Optional max_ctas: use at most that many SMs (a caller running another stream's kernels beside it)." },
+  "Optional max_ctas: use at most that many SMs (a caller running another stream's kernels beside it). "
+  "Optional rows i32 [M] (ridgefill_select's mask): only rows m with rows[m] == 1 are written, the others keep "
+  "y's contents -- the projector and ridgefill_select(rows, y_full -> y) in one pass, bit for bit." },
 { "ridgefill_quant_act_i8g", RF_ARR(pQuant), RF_ARR(oQuant),
   "Activation codes for the int8 projector: per `group` columns of each row of x bf16 [M, n], "
   "s = absmax / 127 (1 for an all-zero group) in f32, q = round-half-even(x / s) clamped to +-127." },
@@ -252,7 +254,7 @@ inline int shape_gemm_q_bias(const RadParam* p, int n_p, int operand, RadOpdDesc
     const int64_t blocks = g > 0 && K % g == 0 ? K / g : 0;
     return pick(out, operand, { opd(RAD_I8, { M, K }), opd(RAD_F32, { M, blocks }, RAD_FILL_SIGMOID),
                                 opd(RAD_I8, { N, K }), opd(RAD_F32, { blocks, N }, RAD_FILL_SIGMOID),
-                                opd(RAD_BF16, { N }), opd(RAD_BF16, { M, N }), opd_absent() });
+                                opd(RAD_BF16, { N }), opd(RAD_BF16, { M, N }), opd_absent(), opd_absent() });
 }
 
 inline int shape_gemm_bias(const RadParam* p, int n_p, int operand, RadOpdDesc* out) {

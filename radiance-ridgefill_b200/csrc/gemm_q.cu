@@ -22,7 +22,10 @@
  *   warps 2-17  epilogue: each warp owns a 32-lane quarter of the tile rows and a 64-column slice;
  *               it folds each finished K block into f32 registers and, at the tile's end, writes its
  *               32 x 64 bf16 block into its own 128-byte-swizzled staging tile in shared memory and
- *               stores it with a TMA tile store (rows and columns past y's edge are clipped)
+ *               stores it with a TMA tile store (rows and columns past y's edge are clipped); with a row
+ *               selection (the optional rows operand, ridgefill_select's mask) each lane instead stores its
+ *               own row's 64 columns straight to y when the row is selected, so the projection lands only
+ *               in the approximated rows of the block input and no separate select pass reads it back
  * A K block is `group` columns: 128 for the projector folder's i8*bf16[1x128] encoding, K itself
  * for per-row / per-column scaling (one fold a tile, the int32 accumulation running over all of K).
  */
@@ -105,9 +108,10 @@ __device__ __forceinline__ void fold_block(uint32_t taddr, float (&acc)[kWarpCol
     }
 }
 
-/* The kernel's forms: the bf16 GEMM, the int8 projector, and the int8 projector writing out its int32 block sums
- * (the optional acc operand). Separate instantiations keep each form's registers to itself. */
-enum GemmMode { kModeBf16 = 0, kModeI8 = 1, kModeI8Dump = 2 };
+/* The kernel's forms: the bf16 GEMM, the int8 projector, the int8 projector writing out its int32 block sums
+ * (the optional acc operand), and the int8 projector writing only the selected rows (the optional rows operand).
+ * Separate instantiations keep each form's registers to itself. */
+enum GemmMode { kModeBf16 = 0, kModeI8 = 1, kModeI8Dump = 2, kModeI8Rows = 3 };
 
 template <int kMode>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -343,10 +347,15 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
                 if (lane == 0) rf::mbar_arrive_cluster_relaxed(rf::map_rank(rf::smem_addr(&acc_empty[buf]), 0));
             }
             if (!ok) break;
-            /* bf16 (and the bias) into this warp's staging tiles, once the previous tile's stores have read them. */
+            /* bf16 (and the bias) into this warp's staging tiles, once the previous tile's stores have read them; or,
+             * with a row selection, straight from the lanes into the selected rows of y (a lane is one row). */
             uint8_t* stg = stage_out + (warp - 2) * kBoxes * kOutBox;
-            if (lane == 0) rf::bulk_store_wait_read();
-            __syncwarp();
+            constexpr bool direct = kMode == kModeI8Rows;
+            const bool write_row = direct && row_live && __ldg(g.rows + m) == 1;
+            if constexpr (!direct) {
+                if (lane == 0) rf::bulk_store_wait_read();
+                __syncwarp();
+            }
 #pragma unroll
             for (int v = 0; v < kWarpCols / 8; ++v) {
                 const int64_t n = n0 + v * 8;
@@ -365,9 +374,14 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
                         o[e] = (uint32_t)rf::f32_to_bf16_bits(lo) | ((uint32_t)rf::f32_to_bf16_bits(hi) << 16);
                     }
                 }
-                /* box v >> 3, row lane, 16-byte chunk (v & 7) at its 128-byte-swizzled place */
-                *(uint4*)(stg + (v >> 3) * kOutBox + lane * 128 + (((v & 7) ^ (lane & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                if constexpr (direct) {
+                    if (write_row && n < g.N) *(uint4*)(g.y + m * g.ldy + n) = make_uint4(o[0], o[1], o[2], o[3]);
+                } else {
+                    /* box v >> 3, row lane, 16-byte chunk (v & 7) at its 128-byte-swizzled place */
+                    *(uint4*)(stg + (v >> 3) * kOutBox + lane * 128 + (((v & 7) ^ (lane & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                }
             }
+            if constexpr (direct) continue;
             rf::fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
@@ -692,6 +706,7 @@ int launch_gemm(const RidgeFillGemmQ& g, cudaStream_t stream) {
     p.folds = (int)(g.K / g.group);
     p.steps_per_fold = (int)(g.group / BK);
     if (g.acc) return launch_pairs<kModeI8Dump>(map_a, map_b, map_y, p, stream);
+    if (g.rows) return launch_pairs<kModeI8Rows>(map_a, map_b, map_y, p, stream);
     return launch_pairs<kModeI8>(map_a, map_b, map_y, p, stream);
 }
 

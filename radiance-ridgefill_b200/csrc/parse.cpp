@@ -453,14 +453,17 @@ extern "C" int ridgefill_gemm_q_parse(const RadArgs* a, int with_bias, RidgeFill
     const RadTensor* bias = with_bias ? rad_arg_in(a, GB_BIAS) : nullptr;
     const RadTensor* Y = rad_arg_in(a, with_bias ? (int)GB_Y : (int)GQ_Y);
     const RadTensor* acc = with_bias ? rad_arg_in(a, GB_ACC) : nullptr;
+    const RadTensor* rows = with_bias ? rad_arg_in(a, GB_ROWS) : nullptr;
     long long M = 0, N = 0, K = 0, group = 0;
     const char* dt = rad_args_gets(a, "dtype");
     if (!A || !AS || !B || !BS || !Y || !rad_args_geti(a, "N", &N) || !rad_args_geti(a, "K", &K) ||
         !rad_args_geti(a, "group", &group) || !dt || std::strcmp(dt, "i8a8") != 0)
         return RAD_E_INVAL;
     if (!with_bias && (rad_arg_in(a, GQ_A_SUM) || rad_arg_in(a, GQ_B_REF))) return RAD_E_UNSUPPORTED;
+    if (acc && rows) return RAD_E_UNSUPPORTED;   /* the debug sums and the row selection are separate forms */
     if (A->dtype != RAD_I8 || AS->dtype != RAD_F32 || B->dtype != RAD_I8 || BS->dtype != RAD_F32 ||
-        Y->dtype != RAD_BF16 || (bias && bias->dtype != RAD_BF16) || (acc && acc->dtype != RAD_I32))
+        Y->dtype != RAD_BF16 || (bias && bias->dtype != RAD_BF16) || (acc && acc->dtype != RAD_I32) ||
+        (rows && rows->dtype != RAD_I32))
         return RAD_E_DTYPE;
     if (A->rank != 2 || B->rank != 2 || Y->rank != 2) return RAD_E_SHAPE;
     M = A->shape[0];
@@ -469,10 +472,10 @@ extern "C" int ridgefill_gemm_q_parse(const RadArgs* a, int with_bias, RidgeFill
     const int64_t blocks = K / group;
     if (A->shape[1] != K || B->shape[0] != N || B->shape[1] != K || Y->shape[0] != M || Y->shape[1] != N ||
         rad_tensor_numel(AS) != M * blocks || rad_tensor_numel(BS) != blocks * N || (bias && rad_tensor_numel(bias) != N) ||
-        (acc && rad_tensor_numel(acc) != M * N * blocks))
+        (acc && rad_tensor_numel(acc) != M * N * blocks) || (rows && rad_tensor_numel(rows) < M))
         return RAD_E_SHAPE;
     if (A->stride[1] != 1 || B->stride[1] != 1 || Y->stride[1] != 1 || !packed(BS) || (bias && !packed(bias)) ||
-        (acc && !packed(acc)))
+        (acc && !packed(acc)) || (rows && !packed(rows)))
         return RAD_E_STRIDE;
     if (AS->rank == 2 ? (AS->stride[1] != 1) : !packed(AS)) return RAD_E_STRIDE;
     /* TMA: 16-byte aligned bases and row pitches. */
@@ -491,6 +494,7 @@ extern "C" int ridgefill_gemm_q_parse(const RadArgs* a, int with_bias, RidgeFill
     g->y = (uint16_t*)Y->data;
     g->ldy = Y->stride[0];
     g->acc = acc ? (int32_t*)acc->data : nullptr;
+    g->rows = rows ? (const int32_t*)rows->data : nullptr;
     g->M = M;
     g->N = N;
     g->K = K;

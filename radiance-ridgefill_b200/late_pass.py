@@ -7,8 +7,9 @@ launch of this library's sm_100a device rows through the C ABI.
                                     arch/ridgefill_layer.h:60-63)
     ridgefill_state_correct undo    every DeltaNet layer's state at once (their pools are one array)
     for each late layer l:
-      ridgefill_gemm_nt_q_bias      the projector x = proj_l(h_S) + bias_l
-      ridgefill_select              the approximated rows of the layer's block input take the projection
+      ridgefill_gemm_nt_q_bias      the projector x = proj_l(h_S) + bias_l, written straight into the approximated
+                                    rows of the layer's block input (its rows operand is the mask: the select of
+                                    ridgefill_select fused into the projector's epilogue)
       ridgefill_quant_act_i8g       the block input's codes (what the int8 block reads)
       DeltaNet layer (arch/qwen4exp_fill.h:29-61):
         ridgefill_gemm_nt_q_bias    the mixed q|k|v projection (int8, no bias)
@@ -342,7 +343,6 @@ class LatePass:
         self.bounds = torch.zeros(4, dtype=torch.int32, device=dev)
         self.codes_h = empty(T, d, dtype=torch.int8)
         self.scale_h = empty(T, d // grp, dtype=torch.float32)
-        self.x_proj = empty(T, self.cols, dtype=torch.bfloat16)
         # every layer's block input, one allocation (mapped by the team's peers), the exact rows copied in
         self.x_all = torch.stack(self.inp["x_exact"])
         self.x = list(self.x_all.unbind(0))
@@ -409,10 +409,11 @@ class LatePass:
         def call(op, tens, params, tag=""):
             return (op, row(op), tens, params, tag)
 
-        def gemm_q(a, sa, w, sw, bias, y, N, tag, M=T):
+        def gemm_q(a, sa, w, sw, bias, y, N, tag, M=T, rows=None):
             return call("ridgefill_gemm_nt_q_bias", [a if isinstance(a, abi.RadTensor) else _t(a),
                                                      sa if isinstance(sa, abi.RadTensor) else _t(sa), _t(w), _t(sw),
-                                                     A_ if bias is None else _t(bias), y, A_],
+                                                     A_ if bias is None else _t(bias), y, A_,
+                                                     A_ if rows is None else _t(rows)],
                         [P("M", M), P("N", N), P("K", d), P("group", self.grp), S("dtype", "i8a8")], tag)
 
         def quant(src, codes, scale, tag):
@@ -433,11 +434,9 @@ class LatePass:
             head.append(correct("undo"))
         gi = ai = 0
         for li, kind in enumerate(s.layers):
-            proj = [gemm_q(self.codes_h, self.scale_h, x["w_proj"][li], x["s_proj"][li], x["b_proj"][li], _t(self.x_proj),
-                           self.cols, f"proj {li}"),
-                    call("ridgefill_select", [_t(self.mask), _t(self.x_proj), A_, A_,
-                                              _t(self.x[li], [T, self.cols], list(self.x[li].stride()), offset_elems=c0),
-                                              A_, A_], [P("M", T)], f"{li}")]
+            proj = [gemm_q(self.codes_h, self.scale_h, x["w_proj"][li], x["s_proj"][li], x["b_proj"][li],
+                           _t(self.x[li], [T, self.cols], list(self.x[li].stride()), offset_elems=c0), self.cols,
+                           f"proj {li}", rows=self.mask)]
             block = []
             if kind == "G" and s.block_inputs:
                 C, Cq = self.conv_dim_r, hk * D
@@ -542,7 +541,7 @@ class LatePass:
 
     def _run_team(self, stream: int, emit) -> None:
         """One rank's pass: the barrier (every rank has finished its previous pass), the head of the pass, then per
-        layer its projector block and select on `stream` and that block's gather to the peers on the comm stream,
+        layer its projector block (into the approximated rows) on `stream` and that block's gather to the peers on the comm stream,
         while `stream` goes on with the previous layer's block (after waiting for all of its columns); the fill and
         the rest once every layer is done."""
         import ctypes as C

@@ -219,3 +219,53 @@ def test_sm_budget_changes_nothing_but_the_grid(cuda, product_lib):
                           H.gemm_params(M, N, K, group) + [H.pint("max_ctas", ctas)])
             assert rc == abi.OK
             assert np.array_equal(Y.cpu().numpy().view(np.uint16), want), (M, N, K, group, ctas)
+
+
+@pytest.mark.parametrize("M,N,K,group,ld,c0", [(1000, 512, 1024, 1024, 512, 0), (700, 256, 2048, 2048, 1024, 512),
+                                                (300, 768, 1024, 128, 1024, 256), (32768, 2048, 2048, 2048, 2048, 0)])
+def test_row_selection_is_the_projector_then_select(cuda, product_lib, M, N, K, group, ld, c0):
+    """The rows operand (ridgefill_select's mask): the projector writes its bias-added bf16 rows only where
+    rows[m] == 1 (0, 2 and -1 leave the row alone), into a column block [c0, c0 + N) of a wider y as a tensor-
+    parallel rank does -- bit for bit what the projector into a scratch matrix followed by ridgefill_select
+    writes, every other element of y untouched."""
+    torch = cuda
+    rng = np.random.default_rng(M + N + c0)
+    g = torch.Generator(device="cuda").manual_seed(M + c0)
+    A = torch.randint(-127, 128, (M, K), dtype=torch.int8, device="cuda", generator=g)
+    B = torch.randint(-127, 128, (N, K), dtype=torch.int8, device="cuda", generator=g)
+    SA = torch.rand((M, K // group), device="cuda", generator=g) * 9e-3 + 1e-3
+    SB = torch.rand((K // group, N), device="cuda", generator=g) * 9e-3 + 1e-3
+    BI = torch.from_numpy(H.f32_to_bf16_bits(rng.standard_normal(N).astype(np.float32)).view(np.int16)).cuda()
+    rows = torch.from_numpy(rng.choice([0, 1, 1, 1, 2, -1], M).astype(np.int32)).cuda()
+    ops = lambda y, r: [H.dev(A), H.dev(SA), H.dev(B), H.dev(SB), H.dev(BI, abi.BF16), H.dev(y, abi.BF16), abi.absent(), H.dev(r)]  # noqa: E731
+    full = torch.empty((M, N), dtype=torch.int16, device="cuda")
+    assert H.launch(product_lib, "ridgefill_gemm_nt_q_bias", ops(full, None)[:7], H.gemm_params(M, N, K, group)) == abi.OK
+    base = torch.randint(-30000, 30000, (M, ld), dtype=torch.int16, device="cuda", generator=g)
+    want = base.clone()
+    assert H.launch(product_lib, "ridgefill_select", [H.dev(rows), H.dev(full, abi.BF16), abi.absent(), abi.absent(),
+                                                      H.dev(want[:, c0:c0 + N], abi.BF16), abi.absent(), abi.absent()],
+                    [H.pint("M", M)]) == abi.OK
+    got = base.clone()
+    assert H.launch(product_lib, "ridgefill_gemm_nt_q_bias", ops(got[:, c0:c0 + N], rows), H.gemm_params(M, N, K, group)) == abi.OK
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    sel = rows == 1
+    assert torch.equal(got[~sel], base[~sel]) and torch.equal(got[sel][:, c0:c0 + N], full[sel])
+
+
+def test_row_selection_refusals(cuda, product_lib):
+    torch = cuda
+    M, N, K = 64, 256, 256
+    A, B = torch.zeros((M, K), dtype=torch.int8, device="cuda"), torch.zeros((N, K), dtype=torch.int8, device="cuda")
+    SA, SB = torch.ones((M, 1), device="cuda"), torch.ones((1, N), device="cuda")
+    Y = torch.zeros((M, N), dtype=torch.int16, device="cuda")
+    ACC = torch.zeros((M, N, 1), dtype=torch.int32, device="cuda")
+    base = [H.dev(A), H.dev(SA), H.dev(B), H.dev(SB), abi.absent(), H.dev(Y, abi.BF16), abi.absent()]
+    p = H.gemm_params(M, N, K, K)
+    assert H.launch(product_lib, "ridgefill_gemm_nt_q_bias", base + [H.dev(torch.ones(M, device="cuda"))], p) == abi.E_DTYPE
+    assert H.launch(product_lib, "ridgefill_gemm_nt_q_bias", base + [H.dev(torch.ones(M - 1, dtype=torch.int32, device="cuda"))],
+                    p) == abi.E_SHAPE
+    with_acc = list(base)
+    with_acc[6] = H.dev(ACC)
+    assert H.launch(product_lib, "ridgefill_gemm_nt_q_bias", with_acc + [H.dev(torch.ones(M, dtype=torch.int32, device="cuda"))],
+                    p) == abi.E_UNSUPPORTED

@@ -49,7 +49,11 @@ def test_every_launch_passes_its_operand_checks(shape, product_lib):
     assert counts["ridgefill_state_correct"] == 2 and counts["ridgefill_mask"] == 1 and counts["ridgefill_hazard"] == 1
     order = [c[0] for c in p.calls]
     assert order[0] == "ridgefill_mask" and order[-1] == "ridgefill_hazard"
-    assert order.index("ridgefill_gdn_fill") > max(i for i, o in enumerate(order) if o == "ridgefill_select")
+    # the projectors write the approximated rows themselves (the mask as their rows operand): no select launch
+    assert "ridgefill_select" not in order
+    proj = [c for c in p.calls if c[0] == "ridgefill_gemm_nt_q_bias" and c[4].startswith("proj")]
+    assert len(proj) == L and all(c[2][7].data for c in proj)
+    assert order.index("ridgefill_gdn_fill") > max(i for i, c in enumerate(p.calls) if c[4].startswith("proj"))
 
 
 def test_cpu_twin_runs_the_same_pass(oracle_lib):
