@@ -1105,14 +1105,16 @@ gdn_fill_fused_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
  * transform of chunk c + 1 beside the chain's products of chunk c, handing everything over in shared and tensor
  * memory (no workspace, no flags, no cross-CTA waits; a plain launch).
  *
- *   warps 0-3   the transform (lane quarter w): G, beta; x2 = beta v and, once K K^T is in tensor memory, the
- *               rows of A (warps 0, 1) beside x1 = beta gamma k and K~ = exp(G_L - G) k (warps 2, 3), all f16
- *               in shared memory; T = (I + A)^-1 by the blocked inversion of phase 1; T as a K-major operand;
- *               then W^T from tensor memory into the chain's B operand (f16, MN-major [dk][rows])
- *   warps 4-11  the chain's lanes (quarter w & 3, column half (w - 4) >> 2): V'^T = U~^T - S W^T straight from
+ *   warps 0-7   the transform (lane quarter w & 3, column half w >> 2): G, beta; x2 = beta v and, once K K^T is
+ *               in tensor memory, the rows of A (warps 0, 1, 4, 5: rows 32 (w & 1).., columns 32 (w >> 2)..)
+ *               beside x1 = beta gamma k and K~ = exp(G_L - G) k (warps 2, 3, 6, 7), all f16 in shared memory;
+ *               T = (I + A)^-1 by the blocked inversion of phase 1; T as a K-major operand; then W^T from tensor
+ *               memory into the chain's B operand (f16, MN-major [dk][rows]). The transform's steps are short
+ *               dependent chains: eight warps (two a sub-partition) hide each other's latencies
+ *   warps 8-15  the chain's lanes (quarter w & 3, column half (w - 8) >> 2): V'^T = U~^T - S W^T straight from
  *               tensor memory (U~^T never leaves it), the f16 state, gamma_L S; the final state to memory
- *   warp 12     the loader: k and v rows by TMA, g and beta by cp.async, two chunks in flight
- *   warp 13     lane 0 issues every product (kind::f16, f32 accumulation):
+ *   warp 16     the loader: k and v rows by TMA, g and beta by cp.async, two chunks in flight
+ *   warp 17     lane 0 issues every product (kind::f16, f32 accumulation):
  *                 K K^T   (M 128 rows of k (the upper 64 unused), N 64, K 128 dk; bf16)    -> tensor memory
  *                 W^T     = x1^T T^T  (M 128 dk, N 64 rows, K 64; A MN-major)               -> tensor memory
  *                 U~^T    = x2^T T^T  (M 128 dv, N 64, K 64; A MN-major)                    -> tensor memory
@@ -1121,7 +1123,7 @@ gdn_fill_fused_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
  *               in the order K K^T(c+1), D1(c), D2(c), W^T(c+1), U~^T(c+1).
  * Every hand-over is an mbarrier with a bounded wait; no barrier can run two phases ahead of a waiter (each
  * completion needs the waiter's own previous step). */
-constexpr int kHdP = 4, kHdC = 8, kHdLoad = kHdP + kHdC, kHdMma = kHdLoad + 1;
+constexpr int kHdP = 8, kHdC = 8, kHdLoad = kHdP + kHdC, kHdMma = kHdLoad + 1;
 constexpr int kHdThreads = 32 * (kHdMma + 1);
 /* Tensor-memory columns: D1 (64), the f16 state A_S (64), D2 (128), K K^T (64), W^T (64), U~^T (64), V'^T A_V (32). */
 constexpr uint32_t kHdD1 = 0, kHdAs = 64, kHdD2 = 128, kHdKk = 256, kHdWt = 320, kHdUt = 384, kHdAv = 448;
@@ -1135,12 +1137,14 @@ constexpr int64_t kHeadFormChains = 64;
 struct HdStage {                 /* one chunk's inputs; x1 and x2 replace k and v in place */
     uint16_t k[2][C][C];
     uint16_t v[2][C][C];
-    float g[C], b[C];
-    uint8_t pad[512];
+    float g[C], b[C];            /* g and beta (zero past the chunk), by cp.async */
+    float G[C], gl[4];           /* the inclusive cumulative log decay and G_L, by the loader */
+    uint8_t pad[1024 - 3 * C * 4 - 16];
 };
+constexpr int kHdStages = 3;     /* chunks of input in flight (the loader two ahead of the transform) */
 
 struct HdSmem {
-    HdStage in[2];
+    HdStage in[kHdStages];
     uint16_t kt[2][2][C][C];     /* K~ [rows][dk] (the k tile's layout), by chunk parity */
     uint16_t wt[2][D][C];        /* W^T [dk][rows], 128-byte swizzled rows, by chunk parity */
     uint16_t tsw[C][C];          /* T [rows][rows], 128-byte swizzled (K-major) */
@@ -1149,9 +1153,9 @@ struct HdSmem {
     float a32[4][16][20];        /* A's diagonal blocks, f32 */
     uint16_t tmp[4][16][24];
     struct Meta {
-        float G[C], beta[C], gl[4];
-    } meta[2];                   /* by chunk parity */
-    uint64_t landed[2], stage_free[2], buf_free[2];
+        float gl[4];             /* gamma_L = exp(G_L) */
+    } meta[2];                   /* by chunk parity: the chain's lanes read it after the stage may be reused */
+    uint64_t landed[kHdStages], stage_free[kHdStages], buf_free[2];
     uint64_t kk_full, t_ready, wt_full, ut_full, tsw_free, w_ready, d1_full, d2_full, as_ready, av_ready, d2_ready;
     uint32_t tmem;
     int abort;
@@ -1185,11 +1189,11 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
     const int64_t n_chains = g.n_head_v * g.n_seq;
     volatile int* abort = &s.abort;
     if (tid == 0) {
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < kHdStages; ++b) {
             rf::mbar_init(&s.landed[b], 1 + 32);   /* the TMA bytes' arrival and the loader's 32 lanes */
             rf::mbar_init(&s.stage_free[b], 1);
-            rf::mbar_init(&s.buf_free[b], 1);
         }
+        for (int b = 0; b < 2; ++b) rf::mbar_init(&s.buf_free[b], 1);
         rf::mbar_init(&s.kk_full, 1);
         rf::mbar_init(&s.wt_full, 1);
         rf::mbar_init(&s.ut_full, 1);
@@ -1223,8 +1227,9 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
             const HdChain ch = hd_chain(g, cid);
             const int64_t hk = ch.h / (g.n_head_v / g.n_head_k);
             for (int64_t j = 0; j < ch.chunks; ++j, ++q) {
-                const int st = (int)(q & 1);
-                if (q >= 2) ok = rf::mbar_wait(&s.stage_free[st], (uint32_t)(((q >> 1) - 1) & 1), abort, rf::kErrGdnWait);
+                const int st = (int)(q % kHdStages);
+                if (q >= kHdStages)
+                    ok = rf::mbar_wait(&s.stage_free[st], (uint32_t)((q / kHdStages - 1) & 1), abort, rf::kErrGdnWait);
                 if (!__all_sync(0xffffffffu, ok)) {
                     ok = false;
                     break;
@@ -1247,22 +1252,38 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                     cp_async4(&sg.b[r], g.beta + row * g.b_row + ch.h, r < len ? 4 : 0);
                 }
                 rf::cp_async_wait_all();
+                __syncwarp();   /* every lane's g is in */
+                {
+                    /* G (inclusive cumulative log decay; zero past the chunk), two rows a lane, and G_L */
+                    const float2 gg = *(const float2*)&sg.g[2 * l];
+                    const float pair = gg.x + gg.y;
+                    float x = pair;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const float y = __shfl_up_sync(0xffffffffu, x, o);
+                        if (l >= o) x += y;
+                    }
+                    *(float2*)&sg.G[2 * l] = make_float2(x - pair + gg.x, x);
+                    const float last = __shfl_sync(0xffffffffu, (len - 1) & 1 ? x : x - pair + gg.x, (len - 1) >> 1);
+                    if (l == 0) sg.gl[0] = last;
+                }
                 rf::mbar_arrive(&s.landed[st]);
             }
         }
         /* copies still in flight land before the CTA leaves (bounded) */
         if (l == 0)
-            for (int64_t i = q > 2 ? q - 2 : 0; i < q; ++i) {
+            for (int64_t i = q > kHdStages ? q - kHdStages : 0; i < q; ++i) {
                 const uint64_t t0 = rf::global_ns();
-                while (!rf::mbar_try_wait(&s.landed[i & 1], (uint32_t)((i >> 1) & 1)) && rf::global_ns() - t0 < rf::kWaitTimeoutNs) {
+                while (!rf::mbar_try_wait(&s.landed[i % kHdStages], (uint32_t)((i / kHdStages) & 1)) &&
+                       rf::global_ns() - t0 < rf::kWaitTimeoutNs) {
                 }
             }
     } else if (w == kHdMma) {
         /* ------------------------------------------------------------ the product issuer (one lane) */
         if (l == 0 && total > 0) {
             auto kkt = [&](int64_t q) -> bool {   /* K K^T of chunk q */
-                const int st = (int)(q & 1);
-                if (!rf::mbar_wait(&s.landed[st], (uint32_t)((q >> 1) & 1), abort, rf::kErrGdnWait)) return false;
+                const int st = (int)(q % kHdStages);
+                if (!rf::mbar_wait(&s.landed[st], (uint32_t)((q / kHdStages) & 1), abort, rf::kErrGdnWait)) return false;
                 rf::tc_fence_after();
                 const uint32_t kt = rf::saddr(&s.in[st].k[0][0][0]);
 #pragma unroll
@@ -1276,7 +1297,7 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
             auto wu = [&](int64_t q) -> bool {   /* W^T and U~^T of chunk q */
                 if (!rf::mbar_wait(&s.t_ready, (uint32_t)(q & 1), abort, rf::kErrGdnWait)) return false;
                 rf::tc_fence_after();
-                const int st = (int)(q & 1);
+                const int st = (int)(q % kHdStages);
                 const uint32_t x1 = rf::saddr(&s.in[st].k[0][0][0]), x2 = rf::saddr(&s.in[st].v[0][0][0]);
                 const uint32_t tt = rf::saddr(&s.tsw[0][0]);
 #pragma unroll
@@ -1322,83 +1343,71 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
             }
         }
     } else if (w < kHdP) {
-        /* ------------------------------------------------------------ the transform (warps 0-3) */
+        /* ------------------------------------------------------------ the transform (warps 0-7) */
         auto psync = [&]() { bar_sync(1, 32 * kHdP); };
-        /* a barrier of the four warps that also tells all of them whether any thread's wait gave up */
+        /* a barrier of the eight warps that also tells all of them whether any thread's wait gave up */
         auto failed = [&](bool ok) { return bar_any(1, 32 * kHdP, !ok || *abort); };
         int64_t q = 0;
         bool stop = false;
         for (int64_t cid = blockIdx.x; cid < n_chains && !stop; cid += gridDim.x) {
             const HdChain ch = hd_chain(g, cid);
             for (int64_t j = 0; j < ch.chunks; ++j, ++q) {
-                const int st = (int)(q & 1), par = (int)(q & 1);
+                const int st = (int)(q % kHdStages), par = (int)(q & 1);
                 const int len = (int)min((int64_t)C, ch.r1 - (ch.r0 + j * C));
                 HdStage& sg = s.in[st];
                 HdSmem::Meta& mt = s.meta[par];
-                if ((stop = failed(rf::mbar_wait(&s.landed[st], (uint32_t)((q >> 1) & 1), abort, rf::kErrGdnWait)))) break;
-                /* G (inclusive cumulative log decay; zero past the chunk) by warp 0, two rows a lane; beta */
-                if (w == 0) {
-                    const float2 gg = *(const float2*)&sg.g[2 * l];
-                    const float pair = gg.x + gg.y;
-                    float x = pair;
-                    for (int o = 1; o < 32; o <<= 1) {
-                        const float y = __shfl_up_sync(0xffffffffu, x, o);
-                        if (l >= o) x += y;
-                    }
-                    *(float2*)&mt.G[2 * l] = make_float2(x - pair + gg.x, x);
-                } else if (w == 1) {
-                    *(float2*)&mt.beta[2 * l] = *(const float2*)&sg.b[2 * l];
-                }
-                psync();
-                const float gl = mt.G[len - 1];
-                if (tid == 0) mt.gl[0] = __expf(gl);
+                /* the chunk's k, v, g, beta and (by the loader) G and G_L are in */
+                if ((stop = failed(rf::mbar_wait(&s.landed[st], (uint32_t)((q / kHdStages) & 1), abort, rf::kErrGdnWait)))) break;
+                const float gl = sg.gl[0];
+                if (tid == 0) mt.gl[0] = __expf(gl);   /* gamma_L for the chain's lanes */
                 const uint32_t ktile = rf::saddr(&sg.k[0][0][0]), vtile = rf::saddr(&sg.v[0][0][0]);
-                /* x2 = beta v in place: row tid & 63, column half tid >> 6 */
+                /* x2 = beta v in place: row tid & 63, column quarter tid >> 6 */
                 {
                     const int r = tid & 63;
                     const bool in = r < len;
-                    const float br = mt.beta[r];
+                    const float br = sg.b[r];
 #pragma unroll
-                    for (int it = 0; it < 8; ++it) {
-                        const uint32_t off = rf::sw128_off(r, (8 * (tid >> 6) + it) * 8);
+                    for (int it = 0; it < 4; ++it) {
+                        const uint32_t off = rf::sw128_off(r, (4 * (tid >> 6) + it) * 8);
                         sts128(vtile + off, scale_bf16x8_to_f16(lds128(vtile + off), br, in));
                     }
                 }
                 /* K K^T landed in tensor memory (so x1 may replace the k tile); K~'s tile of this parity free once D2
                  * of two chunks ago has read it */
                 bool ok = rf::mbar_wait(&s.kk_full, (uint32_t)par, abort, rf::kErrGdnWait);
-                if (w >= 2 && q >= 2) ok = ok && rf::mbar_wait(&s.buf_free[par], (uint32_t)(((q >> 1) - 1) & 1), abort, rf::kErrGdnWait);
+                if ((w & 3) >= 2 && q >= 2) ok = ok && rf::mbar_wait(&s.buf_free[par], (uint32_t)(((q >> 1) - 1) & 1), abort, rf::kErrGdnWait);
                 if ((stop = failed(ok))) break;
                 rf::tc_fence_after();
-                if (w < 2) {
-                    /* A's rows: thread = row i, its 64 columns from tensor memory */
-                    const int i = 32 * w + l;
-                    uint32_t kk[2][32];
-                    const uint32_t base = tmem + ((uint32_t)(32 * w) << 16) + kHdKk;
-                    rf::tmem_ld32(base, kk[0]);
-                    rf::tmem_ld32(base + 32, kk[1]);
+                if ((w & 3) < 2) {
+                    /* A's rows: thread = row i (lane quarter w & 3), the 32 columns of half w >> 2 from tensor memory */
+                    const int i = 32 * (w & 3) + l, j0 = 32 * (w >> 2);
+                    uint32_t kk[32];
+                    rf::tmem_ld32(tmem + ((uint32_t)(32 * (w & 3)) << 16) + kHdKk + j0, kk);
                     rf::tmem_ld_wait();
                     rf::tc_fence_before();
                     const bool rowin = i < len;
-                    const float Gi = mt.G[i], bi = mt.beta[i];
+                    const float Gi = sg.G[i], bi = sg.b[i];
 #pragma unroll
-                    for (int jj = 0; jj < C; jj += 2) {
+                    for (int jj = 0; jj < 32; jj += 2) {
+                        const int j = j0 + jj;
                         float v[2];
 #pragma unroll
                         for (int e = 0; e < 2; ++e)
-                            v[e] = (jj + e < i && rowin) ? bi * __expf(Gi - mt.G[jj + e]) * __uint_as_float(kk[jj >> 5][(jj + e) & 31]) : 0.0f;
-                        *(uint32_t*)&s.l16[i][jj] = rf::pack_f16(v[0], v[1]);
-                        if ((jj >> 4) == (i >> 4)) *(float2*)&s.a32[i >> 4][i & 15][jj & 15] = make_float2(v[0], v[1]);
+                            v[e] = (j + e < i && rowin) ? bi * __expf(Gi - sg.G[j + e]) * __uint_as_float(kk[jj + e]) : 0.0f;
+                        *(uint32_t*)&s.l16[i][j] = rf::pack_f16(v[0], v[1]);
+                        if ((j >> 4) == (i >> 4)) *(float2*)&s.a32[i >> 4][i & 15][j & 15] = make_float2(v[0], v[1]);
                     }
                 } else {
-                    /* x1 = beta gamma k in place and K~ = exp(G_L - G) k into this parity's tile: thread = row r */
-                    const int r = tid - 64;
+                    /* x1 = beta gamma k in place and K~ = exp(G_L - G) k into this parity's tile: thread = row r,
+                     * column half t2 >> 6 */
+                    const int t2 = ((w >> 2) << 6) | ((w & 1) << 5) | l, r = t2 & 63;
                     const bool in = r < len;
-                    const float gr = mt.G[r], br = mt.beta[r];
+                    const float gr = sg.G[r], br = sg.b[r];
                     const float fk = in ? __expf(gl - gr) : 0.0f, fx = in ? br * __expf(gr) : 0.0f;
                     const uint32_t kst = rf::saddr(&s.kt[par][0][0][0]);
 #pragma unroll 4
-                    for (int seg = 0; seg < 16; ++seg) {
+                    for (int sg8 = 0; sg8 < 8; ++sg8) {
+                        const int seg = 8 * (t2 >> 6) + sg8;
                         const uint32_t off = rf::sw128_off(r, seg * 8);
                         const uint4 kr = lds128(ktile + off);
                         sts128(kst + off, scale_bf16x8_to_f16(kr, fk, in));
@@ -1406,30 +1415,30 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                     }
                 }
                 psync();
-                /* diagonal blocks of T by substitution in f32: warp w block w, lane l row l & 15 of 8 columns */
+                /* diagonal blocks of T by substitution in f32: warp w block w >> 1, columns 8 (w & 1)..+8, lane l row
+                 * l & 15 of 4 columns */
                 {
-                    const int r = l & 15, c0 = 8 * (l >> 4);
+                    const int b = w >> 1, r = l & 15, c0 = 8 * (w & 1) + 4 * (l >> 4);
                     float a[16];
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
-                        const float4 v = *(const float4*)&s.a32[w][r][4 * q4];
+                        const float4 v = *(const float4*)&s.a32[b][r][4 * q4];
                         a[4 * q4] = v.x;
                         a[4 * q4 + 1] = v.y;
                         a[4 * q4 + 2] = v.z;
                         a[4 * q4 + 3] = v.w;
                     }
-                    float x[8];
+                    float x[4];
 #pragma unroll
-                    for (int cc = 0; cc < 8; ++cc) x[cc] = r == c0 + cc ? 1.0f : 0.0f;
+                    for (int cc = 0; cc < 4; ++cc) x[cc] = r == c0 + cc ? 1.0f : 0.0f;
 #pragma unroll
                     for (int jj = 0; jj < 15; ++jj)
 #pragma unroll
-                        for (int cc = 0; cc < 8; ++cc) {
+                        for (int cc = 0; cc < 4; ++cc) {
                             const float xj = __shfl_sync(0xffffffffu, x[cc], (l & 16) | jj);
                             x[cc] = fmaf(-(jj < r ? a[jj] : 0.0f), xj, x[cc]);
                         }
-                    *(uint4*)&s.t16[16 * w + r][16 * w + c0] = make_uint4(rf::pack_f16(x[0], x[1]), rf::pack_f16(x[2], x[3]),
-                                                                          rf::pack_f16(x[4], x[5]), rf::pack_f16(x[6], x[7]));
+                    *(uint2*)&s.t16[16 * b + r][16 * b + c0] = make_uint2(rf::pack_f16(x[0], x[1]), rf::pack_f16(x[2], x[3]));
                 }
                 psync();
                 if (w < 3) tri_offdiag_block(s, w + 1, w, w);   /* T10, T21, T32 */
@@ -1441,10 +1450,10 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                 if ((stop = failed(q < 1 || rf::mbar_wait(&s.tsw_free, (uint32_t)((q - 1) & 1), abort, rf::kErrGdnWait)))) break;
                 {
                     const uint32_t tt = rf::saddr(&s.tsw[0][0]);
-                    const int r = tid >> 1;
+                    const int r = tid >> 2;
 #pragma unroll
-                    for (int c4 = 0; c4 < 4; ++c4) {
-                        const int cc = 4 * (tid & 1) + c4;
+                    for (int c2 = 0; c2 < 2; ++c2) {
+                        const int cc = 2 * (tid & 3) + c2;
                         sts128(tt + rf::sw128_off(r, 8 * cc), *(const uint4*)&s.t16[r][8 * cc]);
                     }
                 }
@@ -1452,22 +1461,21 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                 __syncwarp();
                 if (l == 0) rf::mbar_arrive(&s.t_ready);
                 /* W^T from tensor memory into this parity's B tile of D1 (free: buf_free waited above): thread = dk
-                 * row 32 w + l */
+                 * row 32 (w & 3) + l, the 32 columns of half w >> 2 */
                 if ((stop = failed(rf::mbar_wait(&s.wt_full, (uint32_t)par, abort, rf::kErrGdnWait)))) break;
                 rf::tc_fence_after();
                 {
-                    uint32_t wv[2][32];
-                    const uint32_t base = tmem + ((uint32_t)(32 * w) << 16) + kHdWt;
-                    rf::tmem_ld32(base, wv[0]);
-                    rf::tmem_ld32(base + 32, wv[1]);
+                    uint32_t wv[32];
+                    const int ch = w >> 2;
+                    rf::tmem_ld32(tmem + ((uint32_t)(32 * (w & 3)) << 16) + kHdWt + 32 * ch, wv);
                     rf::tmem_ld_wait();
                     rf::tc_fence_before();
                     const uint32_t wtile = rf::saddr(&s.wt[par][0][0]);
-                    const int dk = 32 * w + l;
+                    const int dk = 32 * (w & 3) + l;
 #pragma unroll
-                    for (int c8 = 0; c8 < 8; ++c8) {
-                        const uint32_t* x = &wv[c8 >> 2][(c8 & 3) * 8];
-                        sts128(wtile + rf::sw128_off(dk, 8 * c8),
+                    for (int c8 = 0; c8 < 4; ++c8) {
+                        const uint32_t* x = &wv[c8 * 8];
+                        sts128(wtile + rf::sw128_off(dk, 8 * (4 * ch + c8)),
                                make_uint4(rf::pack_f16(__uint_as_float(x[0]), __uint_as_float(x[1])),
                                           rf::pack_f16(__uint_as_float(x[2]), __uint_as_float(x[3])),
                                           rf::pack_f16(__uint_as_float(x[4]), __uint_as_float(x[5])),
@@ -1480,7 +1488,7 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
             }
         }
     } else if (w < kHdLoad) {
-        /* ------------------------------------------------------------ the chain's lanes (warps 4-11) */
+        /* ------------------------------------------------------------ the chain's lanes (warps 8-15) */
         const int qd = w & 3, hf = (w - kHdP) >> 2, i = 32 * qd + l;   /* dv row i; columns of half hf */
         const uint32_t lane_base = tmem + ((uint32_t)(32 * qd) << 16);
         const uint32_t d1 = lane_base + kHdD1 + 32 * hf, d2 = lane_base + kHdD2 + 64 * hf, ut = lane_base + kHdUt + 32 * hf;
@@ -1493,24 +1501,29 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
         auto wwait = [&](uint64_t* bar, uint32_t par) {
             return __all_sync(0xffffffffu, rf::mbar_wait(bar, par, abort, rf::kErrGdnWait));
         };
-        auto put_as = [&](const uint32_t (&r)[2][32]) {   /* the f16 state into the first product's A (tensor memory) */
-            uint32_t o[32];
+        /* The state row is moved 32 columns at a time (a half of this thread's 64), so no more than 32 of its values
+         * are live: into the first product's A as f16, and gamma S back into D2 (D2 is re-read for that: the tensor
+         * cores write it again only after this warp's d2_ready). */
+        auto as_half = [&](const uint32_t (&r)[32], int h2) {   /* f16 pairs of 32 state values into A_S */
+            uint32_t o[16];
 #pragma unroll
-            for (int e = 0; e < 32; ++e)
-                o[e] = rf::pack_f16(__uint_as_float(r[e >> 4][(2 * e) & 31]), __uint_as_float(r[e >> 4][(2 * e + 1) & 31]));
-            rf::tmem_st32(as, o);
-            rf::tmem_st_wait();
-            rf::tc_fence_before();
+            for (int e = 0; e < 16; ++e) o[e] = rf::pack_f16(__uint_as_float(r[2 * e]), __uint_as_float(r[2 * e + 1]));
+            rf::tmem_st16(as + 16 * h2, o);
         };
-        auto put_d2 = [&](uint32_t (&r)[2][32], float gam) {   /* gamma * S into D2 */
+        auto load_row = [&](const float* src, uint32_t (&r)[32]) {   /* 32 state values from memory */
 #pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2) {
-#pragma unroll
-                for (int e = 0; e < 32; ++e) r[h2][e] = __float_as_uint(gam * __uint_as_float(r[h2][e]));
-                rf::tmem_st32(d2 + 32 * h2, r[h2]);
+            for (int jj = 0; jj < 8; ++jj) {
+                const float4 x = *(const float4*)(src + 4 * jj);
+                r[4 * jj] = __float_as_uint(x.x);
+                r[4 * jj + 1] = __float_as_uint(x.y);
+                r[4 * jj + 2] = __float_as_uint(x.z);
+                r[4 * jj + 3] = __float_as_uint(x.w);
             }
-            rf::tmem_st_wait();
-            rf::tc_fence_before();
+        };
+        auto scale_into_d2 = [&](uint32_t (&r)[32], int h2, float gam) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(gam * __uint_as_float(r[e]));
+            rf::tmem_st32(d2 + 32 * h2, r);
         };
         int64_t q = 0;
         bool ok = true;
@@ -1518,62 +1531,91 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
             const HdChain ch = hd_chain(g, cid);
             if (ch.chunks == 0) continue;
             float* srow = g.state + ch.slot * g.st_slot + ch.h * g.st_head + (int64_t)i * D + 64 * hf;
-            uint32_t r[2][32];
+            /* the chain's start state: f16 into A_S, then (gamma_L of its first chunk known) gamma S into D2 */
 #pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2)
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float4 x = *(const float4*)(srow + 32 * h2 + 4 * j);
-                    r[h2][4 * j] = __float_as_uint(x.x);
-                    r[h2][4 * j + 1] = __float_as_uint(x.y);
-                    r[h2][4 * j + 2] = __float_as_uint(x.z);
-                    r[h2][4 * j + 3] = __float_as_uint(x.w);
-                }
-            put_as(r);
+            for (int h2 = 0; h2 < 2; ++h2) {
+                uint32_t r[32];
+                load_row(srow + 32 * h2, r);
+                as_half(r, h2);
+            }
+            rf::tmem_st_wait();
+            rf::tc_fence_before();
             arrive(&s.as_ready);
             if (!(ok = wwait(&s.ut_full, (uint32_t)(q & 1)))) break;
-            put_d2(r, s.meta[q & 1].gl[0]);
+            {
+                const float gam = s.meta[q & 1].gl[0];
+#pragma unroll
+                for (int h2 = 0; h2 < 2; ++h2) {
+                    uint32_t r[32];
+                    load_row(srow + 32 * h2, r);
+                    scale_into_d2(r, h2, gam);
+                }
+                rf::tmem_st_wait();
+                rf::tc_fence_before();
+            }
             arrive(&s.d2_ready);
             for (int64_t j = 0; j < ch.chunks && ok; ++j, ++q) {
                 const uint32_t par = (uint32_t)(q & 1);
                 /* V'^T = U~^T - D1 for rows 32 hf..+32 of the chunk, f16 into the second product's A */
                 if (!(ok = wwait(&s.d1_full, par))) break;
                 rf::tc_fence_after();
-                {
-                    uint32_t d[32], u[32], o[16];
-                    rf::tmem_ld32(d1, d);
-                    rf::tmem_ld32(ut, u);
+#pragma unroll
+                for (int x = 0; x < 2; ++x) {   /* 16 columns at a time: fewer live registers */
+                    uint32_t d[16], u[16], o[8];
+                    rf::tmem_ld16(d1 + 16 * x, d);
+                    rf::tmem_ld16(ut + 16 * x, u);
                     rf::tmem_ld_wait();
 #pragma unroll
-                    for (int e = 0; e < 16; ++e)
+                    for (int e = 0; e < 8; ++e)
                         o[e] = rf::pack_f16(__uint_as_float(u[2 * e]) - __uint_as_float(d[2 * e]),
                                             __uint_as_float(u[2 * e + 1]) - __uint_as_float(d[2 * e + 1]));
-                    rf::tmem_st16(av, o);
-                    rf::tmem_st_wait();
+                    rf::tmem_st8(av + 8 * x, o);
                 }
+                rf::tmem_st_wait();
                 rf::tc_fence_before();
                 arrive(&s.av_ready);
-                /* the updated state: the next chunk's f16 state first, then gamma_L(next) S into D2 */
+                /* the updated state: the next chunk's f16 state first, then gamma_L(next) S into D2; at the chain's
+                 * last chunk the state to memory */
                 if (!(ok = wwait(&s.d2_full, par))) break;
                 rf::tc_fence_after();
-                rf::tmem_ld32(d2, r[0]);
-                rf::tmem_ld32(d2 + 32, r[1]);
-                rf::tmem_ld_wait();
                 if (j + 1 == ch.chunks) {
 #pragma unroll
-                    for (int h2 = 0; h2 < 2; ++h2)
+                    for (int h2 = 0; h2 < 2; ++h2) {
+                        uint32_t r[32];
+                        rf::tmem_ld32(d2 + 32 * h2, r);
+                        rf::tmem_ld_wait();
 #pragma unroll
                         for (int jj = 0; jj < 8; ++jj)
                             *(float4*)(srow + 32 * h2 + 4 * jj) =
-                                make_float4(__uint_as_float(r[h2][4 * jj]), __uint_as_float(r[h2][4 * jj + 1]),
-                                            __uint_as_float(r[h2][4 * jj + 2]), __uint_as_float(r[h2][4 * jj + 3]));
+                                make_float4(__uint_as_float(r[4 * jj]), __uint_as_float(r[4 * jj + 1]),
+                                            __uint_as_float(r[4 * jj + 2]), __uint_as_float(r[4 * jj + 3]));
+                    }
                     rf::tc_fence_before();
                     continue;
                 }
-                put_as(r);
+#pragma unroll
+                for (int h2 = 0; h2 < 2; ++h2) {
+                    uint32_t r[32];
+                    rf::tmem_ld32(d2 + 32 * h2, r);
+                    rf::tmem_ld_wait();
+                    as_half(r, h2);
+                }
+                rf::tmem_st_wait();
+                rf::tc_fence_before();
                 arrive(&s.as_ready);
                 if (!(ok = wwait(&s.ut_full, (uint32_t)((q + 1) & 1)))) break;
-                put_d2(r, s.meta[(q + 1) & 1].gl[0]);
+                {
+                    const float gam = s.meta[(q + 1) & 1].gl[0];
+#pragma unroll
+                    for (int h2 = 0; h2 < 2; ++h2) {
+                        uint32_t r[32];
+                        rf::tmem_ld32(d2 + 32 * h2, r);
+                        rf::tmem_ld_wait();
+                        scale_into_d2(r, h2, gam);
+                    }
+                    rf::tmem_st_wait();
+                    rf::tc_fence_before();
+                }
                 arrive(&s.d2_ready);
             }
         }
@@ -1865,6 +1907,11 @@ extern "C" int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s) {
         /* one CTA per SM, each taking whole chains (no workspace, no cross-CTA waits) */
         if (cudaFuncSetAttribute(gdn_fill_heads_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHdSmem) != cudaSuccess)
             return RAD_E_DEVICE;
+        static int resident = -1;   /* CTAs a SM can hold (registers, shared memory): the form needs exactly 1 */
+        if (resident < 0 &&
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, gdn_fill_heads_kernel, kHdThreads, kHdSmem) != cudaSuccess)
+            return RAD_E_DEVICE;
+        if (resident != 1) return RAD_E_DEVICE;
         const int64_t chains = g.n_head_v * g.n_seq;
         const int grid = (int)(chains < rf::sm_count() ? chains : rf::sm_count());
         gdn_fill_heads_kernel<<<grid, kHdThreads, kHdSmem, rf::as_stream(s)>>>(kmap, vmap, g);
