@@ -504,8 +504,10 @@ class LatePass:
                                               _t(self.slot_last), _t(self.count)], [P("M", 1)]))
         self.head, self.layers, self.tail = head, layers, tail
         self.calls = head + [c for proj, block in layers for c in proj + block] + tail
-        small = D != 128
-        self.kernels = sum(1 if (c[0] == "ridgefill_gdn_fill" and small) else self.KERNELS[c[0]] for c in self.calls)
+        # the fill is one kernel in its per-row form (heads of at most 64 dims) and its per-head form (a state-only
+        # launch of at least 64 chains), two (plan + cooperative kernel) otherwise
+        one_kernel_fill = D != 128 or G * hv * s.n_seq >= 64
+        self.kernels = sum(1 if (c[0] == "ridgefill_gdn_fill" and one_kernel_fill) else self.KERNELS[c[0]] for c in self.calls)
         if self.team is not None:   # the barrier, one gather and one wait a layer
             self.kernels += 1 + 2 * len(s.layers)
 
@@ -617,11 +619,14 @@ class LatePass:
         T, d, G, A = s.T, s.d, s.n_gdn, s.n_attn
         hk, hv, D = self.hk_r, self.hv_r, s.head
         L = len(s.layers)
-        n_int8_cols = L * self.cols + (G * self.conv_dim_r if s.block_inputs else 0) + \
+        # the mixed projection's k|v columns over every row, its q columns over each sequence's last three rows only
+        q_cols = hk * D if s.block_inputs else 0
+        n_int8_cols = L * self.cols + (G * (self.conv_dim_r - q_cols) if s.block_inputs else 0) + \
             (A * 2 * self.hkv_r * s.head_attn if self.hkv_r else 0)
+        q_tail_rows = sum(min(n, 3) for n in s.lengths)
         chunks = sum((n + 63) // 64 for n in s.lengths)
         return {
-            "int8_ops": 2 * T * d * n_int8_cols,
+            "int8_ops": 2 * T * d * n_int8_cols + 2 * q_tail_rows * d * G * q_cols,
             # the batched fill, state-only form: read k, v, g, beta and the state, write the state
             "fill_bytes": 2 * T * G * hk * D + 2 * T * G * hv * D + 8 * T * G * hv + 2 * 4 * s.n_seq * G * hv * D * D,
             "fill_chunk_flops": chunks * G * hv * (6 * 64 * 64 * D + 4 * 64 * D * D + 64 ** 3 * 2 // 3),
