@@ -215,9 +215,14 @@ def roofline(op: str, ms: float, alg: dict, pk: dict) -> dict:
              "traffic": None, "note": f"int8 dense peak = 2 x the {pk['source']} bf16 figure ({pk['bf16_tflops']} TF/s); "
                                       "the pass's int8 GEMM launches together (projectors, mixed and k|v projections)"}
     elif op == "ridgefill_gdn_fill":
+        # DRAM bytes over algorithmic bytes of the per-head fill, from one ncu capture of it (8,192 rows, 128 heads:
+        # 424.2 MB read + written against 427.4 MB, profiles/gdn_fill_heads_T8192.md); the traffic grows with the
+        # heads and rows it processes, so the pass's launch is taken as that ratio times its algorithmic bytes
+        traffic_ratio = (419.5 + 4.7) / 427.4
         r = {"bound": "hbm", "achieved": alg["fill_bytes"] / (ms * 1e-3) / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
-             "traffic": None, "note": f"the batched fill (state-only bytes: k, v, g, beta read, state read and written); "
-                                      f"peak {pk['source']}"}
+             "traffic": alg["fill_bytes"] * traffic_ratio / 1e9, "traffic_unit": "GB per launch",
+             "note": f"the batched fill (state-only bytes: k, v, g, beta read, state read and written), one launch a "
+                     f"pass; traffic scaled from an ncu capture of 8,192 rows x 128 heads; peak {pk['source']}"}
         r["tensor"] = {"achieved": alg["fill_chunk_flops"] / (ms * 1e-3) / 1e12, "peak": pk["bf16_tflops"],
                        "unit": "TFLOP/s"}
         r["tensor"]["frac"] = r["tensor"]["achieved"] / r["tensor"]["peak"]
