@@ -1114,17 +1114,19 @@ gdn_fill_fused_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
  *   warps 8-15  the chain's lanes (quarter w & 3, column half (w - 8) >> 2): V'^T = U~^T - S W^T straight from
  *               tensor memory (U~^T never leaves it), the f16 state, gamma_L S; the final state to memory
  *   warp 16     the loader: k and v rows by TMA, g and beta by cp.async, two chunks in flight
- *   warp 17     lane 0 issues every product (kind::f16, f32 accumulation):
+ *   warp 17     lane 0 issues the products (kind::f16, f32 accumulation; K K^T by warp 18):
  *                 K K^T   (M 128 rows of k (the upper 64 unused), N 64, K 128 dk; bf16)    -> tensor memory
  *                 W^T     = x1^T T^T  (M 128 dk, N 64 rows, K 64; A MN-major)               -> tensor memory
  *                 U~^T    = x2^T T^T  (M 128 dv, N 64, K 64; A MN-major)                    -> tensor memory
  *                 D1      = S W^T     (M 128 dv, N 64, K 128; A the f16 state in tensor memory, B MN-major)
  *                 D2     += V'^T K~   (M 128 dv, N 128 dk, K 64; B MN-major; D2 = gamma_L S before)
- *               in the order K K^T(c+1), D1(c), D2(c), W^T(c+1), U~^T(c+1).
+ *               in the order D1(c), D2(c), W^T(c+1), U~^T(c+1)
+ *   warp 18     lane 0 issues each chunk's K K^T as soon as its rows have landed and the transform has read the
+ *               previous one (kk_free)
  * Every hand-over is an mbarrier with a bounded wait; no barrier can run two phases ahead of a waiter (each
  * completion needs the waiter's own previous step). */
-constexpr int kHdP = 8, kHdC = 8, kHdLoad = kHdP + kHdC, kHdMma = kHdLoad + 1;
-constexpr int kHdThreads = 32 * (kHdMma + 1);
+constexpr int kHdP = 8, kHdC = 8, kHdLoad = kHdP + kHdC, kHdMma = kHdLoad + 1, kHdKkw = kHdMma + 1;
+constexpr int kHdThreads = 32 * (kHdKkw + 1);
 /* Tensor-memory columns: D1 (64), the f16 state A_S (64), D2 (128), K K^T (64), W^T (64), U~^T (64), V'^T A_V (32). */
 constexpr uint32_t kHdD1 = 0, kHdAs = 64, kHdD2 = 128, kHdKk = 256, kHdWt = 320, kHdUt = 384, kHdAv = 448;
 constexpr uint32_t kIdescKk = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(64 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
@@ -1156,7 +1158,7 @@ struct HdSmem {
         float gl[4];             /* gamma_L = exp(G_L) */
     } meta[2];                   /* by chunk parity: the chain's lanes read it after the stage may be reused */
     uint64_t landed[kHdStages], stage_free[kHdStages], buf_free[2];
-    uint64_t kk_full, t_ready, wt_full, ut_full, tsw_free, w_ready, d1_full, d2_full, as_ready, av_ready, d2_ready;
+    uint64_t kk_full, kk_free, t_ready, wt_full, ut_full, tsw_free, w_ready, d1_full, d2_full, as_ready, av_ready, d2_ready;
     uint32_t tmem;
     int abort;
 };
@@ -1195,6 +1197,7 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
         }
         for (int b = 0; b < 2; ++b) rf::mbar_init(&s.buf_free[b], 1);
         rf::mbar_init(&s.kk_full, 1);
+        rf::mbar_init(&s.kk_free, 4);   /* the four warps that read K K^T's rows */
         rf::mbar_init(&s.wt_full, 1);
         rf::mbar_init(&s.ut_full, 1);
         rf::mbar_init(&s.tsw_free, 1);
@@ -1278,10 +1281,9 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                        rf::global_ns() - t0 < rf::kWaitTimeoutNs) {
                 }
             }
-    } else if (w == kHdMma) {
-        /* ------------------------------------------------------------ the product issuer (one lane) */
-        if (l == 0 && total > 0) {
-            auto kkt = [&](int64_t q) -> bool {   /* K K^T of chunk q */
+    } else if (w == kHdMma || w == kHdKkw) {
+        /* ------------------------------------------------------------ the product issuers: warp 18 K K^T, warp 17 the rest */
+        auto kkt = [&](int64_t q) -> bool {   /* K K^T of chunk q */
                 const int st = (int)(q % kHdStages);
                 if (!rf::mbar_wait(&s.landed[st], (uint32_t)((q / kHdStages) & 1), abort, rf::kErrGdnWait)) return false;
                 rf::tc_fence_after();
@@ -1293,7 +1295,17 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                 }
                 rf::mma_commit(&s.kk_full);
                 return true;
-            };
+        };
+        if (w == kHdKkw) {
+            /* K K^T of each chunk as soon as its rows have landed and the transform has read the previous one's rows
+             * (kk_free), so it is ready long before the transform needs it. A warp of its own: a lane of the issuer's
+             * warp spinning beside lane 0 would wait its turn behind lane 0's waits */
+            if (l == 0)
+                for (int64_t q = 0; q < total; ++q) {
+                    if (q >= 1 && !rf::mbar_wait(&s.kk_free, (uint32_t)((q - 1) & 1), abort, rf::kErrGdnWait)) break;
+                    if (!kkt(q)) break;
+                }
+        } else if (l == 0 && total > 0) {
             auto wu = [&](int64_t q) -> bool {   /* W^T and U~^T of chunk q */
                 if (!rf::mbar_wait(&s.t_ready, (uint32_t)(q & 1), abort, rf::kErrGdnWait)) return false;
                 rf::tc_fence_after();
@@ -1314,10 +1326,9 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                 rf::mma_commit(&s.tsw_free);
                 return true;
             };
-            bool ok = kkt(0) && wu(0);
+            bool ok = wu(0);
             for (int64_t q = 0; q < total && ok; ++q) {
                 const uint32_t par = (uint32_t)(q & 1);
-                if (q + 1 < total && !(ok = kkt(q + 1))) break;
                 /* D1 = S W^T: the lanes wrote this chunk's f16 state, the transform its W^T tile */
                 if (!(ok = rf::mbar_wait(&s.as_ready, par, abort, rf::kErrGdnWait) &&
                            rf::mbar_wait(&s.w_ready, par, abort, rf::kErrGdnWait)))
@@ -1347,6 +1358,34 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
         auto psync = [&]() { bar_sync(1, 32 * kHdP); };
         /* a barrier of the eight warps that also tells all of them whether any thread's wait gave up */
         auto failed = [&](bool ok) { return bar_any(1, 32 * kHdP, !ok || *abort); };
+        /* W^T of chunk qq from tensor memory into its parity's B tile of D1 (free: that chunk's buf_free wait came
+         * before a barrier of these warps): thread = dk row 32 (w & 3) + l, the 32 columns of half w >> 2. Done while
+         * the next chunk is in hand (after its x2), so the W^T product's latency is not waited for; true if a wait
+         * gave up */
+        auto read_back_wt = [&](int64_t qq) -> bool {
+            if (failed(rf::mbar_wait(&s.wt_full, (uint32_t)(qq & 1), abort, rf::kErrGdnWait))) return true;
+            rf::tc_fence_after();
+            uint32_t wv[32];
+            const int ch = w >> 2;
+            rf::tmem_ld32(tmem + ((uint32_t)(32 * (w & 3)) << 16) + kHdWt + 32 * ch, wv);
+            rf::tmem_ld_wait();
+            rf::tc_fence_before();
+            const uint32_t wtile = rf::saddr(&s.wt[qq & 1][0][0]);
+            const int dk = 32 * (w & 3) + l;
+#pragma unroll
+            for (int c8 = 0; c8 < 4; ++c8) {
+                const uint32_t* x = &wv[c8 * 8];
+                sts128(wtile + rf::sw128_off(dk, 8 * (4 * ch + c8)),
+                       make_uint4(rf::pack_f16(__uint_as_float(x[0]), __uint_as_float(x[1])),
+                                  rf::pack_f16(__uint_as_float(x[2]), __uint_as_float(x[3])),
+                                  rf::pack_f16(__uint_as_float(x[4]), __uint_as_float(x[5])),
+                                  rf::pack_f16(__uint_as_float(x[6]), __uint_as_float(x[7]))));
+            }
+            rf::fence_proxy_async_smem();
+            __syncwarp();
+            if (l == 0) rf::mbar_arrive(&s.w_ready);
+            return false;
+        };
         int64_t q = 0;
         bool stop = false;
         for (int64_t cid = blockIdx.x; cid < n_chains && !stop; cid += gridDim.x) {
@@ -1372,6 +1411,8 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                         sts128(vtile + off, scale_bf16x8_to_f16(lds128(vtile + off), br, in));
                     }
                 }
+                /* the previous chunk's W^T, its product long finished */
+                if (q > 0 && (stop = read_back_wt(q - 1))) break;
                 /* K K^T landed in tensor memory (so x1 may replace the k tile); K~'s tile of this parity free once D2
                  * of two chunks ago has read it */
                 bool ok = rf::mbar_wait(&s.kk_full, (uint32_t)par, abort, rf::kErrGdnWait);
@@ -1385,6 +1426,8 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                     rf::tmem_ld32(tmem + ((uint32_t)(32 * (w & 3)) << 16) + kHdKk + j0, kk);
                     rf::tmem_ld_wait();
                     rf::tc_fence_before();
+                    __syncwarp();
+                    if (l == 0) rf::mbar_arrive(&s.kk_free);   /* the next chunk's K K^T may overwrite it */
                     const bool rowin = i < len;
                     const float Gi = sg.G[i], bi = sg.b[i];
 #pragma unroll
@@ -1460,33 +1503,10 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                 rf::fence_proxy_async_smem();   /* x1, x2, K~ and T for the tensor cores */
                 __syncwarp();
                 if (l == 0) rf::mbar_arrive(&s.t_ready);
-                /* W^T from tensor memory into this parity's B tile of D1 (free: buf_free waited above): thread = dk
-                 * row 32 (w & 3) + l, the 32 columns of half w >> 2 */
-                if ((stop = failed(rf::mbar_wait(&s.wt_full, (uint32_t)par, abort, rf::kErrGdnWait)))) break;
-                rf::tc_fence_after();
-                {
-                    uint32_t wv[32];
-                    const int ch = w >> 2;
-                    rf::tmem_ld32(tmem + ((uint32_t)(32 * (w & 3)) << 16) + kHdWt + 32 * ch, wv);
-                    rf::tmem_ld_wait();
-                    rf::tc_fence_before();
-                    const uint32_t wtile = rf::saddr(&s.wt[par][0][0]);
-                    const int dk = 32 * (w & 3) + l;
-#pragma unroll
-                    for (int c8 = 0; c8 < 4; ++c8) {
-                        const uint32_t* x = &wv[c8 * 8];
-                        sts128(wtile + rf::sw128_off(dk, 8 * (4 * ch + c8)),
-                               make_uint4(rf::pack_f16(__uint_as_float(x[0]), __uint_as_float(x[1])),
-                                          rf::pack_f16(__uint_as_float(x[2]), __uint_as_float(x[3])),
-                                          rf::pack_f16(__uint_as_float(x[4]), __uint_as_float(x[5])),
-                                          rf::pack_f16(__uint_as_float(x[6]), __uint_as_float(x[7]))));
-                    }
-                }
-                rf::fence_proxy_async_smem();
-                __syncwarp();
-                if (l == 0) rf::mbar_arrive(&s.w_ready);
             }
         }
+        /* the last chunk's W^T */
+        if (!stop && q > 0) read_back_wt(q - 1);
     } else if (w < kHdLoad) {
         /* ------------------------------------------------------------ the chain's lanes (warps 8-15) */
         const int qd = w & 3, hf = (w - kHdP) >> 2, i = 32 * qd + l;   /* dv row i; columns of half hf */
