@@ -1149,21 +1149,26 @@ struct HdSmem {
     HdStage in[kHdStages];
     uint16_t kt[2][2][C][C];     /* K~ [rows][dk] (the k tile's layout), by chunk parity */
     uint16_t wt[2][D][C];        /* W^T [dk][rows], 128-byte swizzled rows, by chunk parity */
-    uint16_t tsw[C][C];          /* T [rows][rows], 128-byte swizzled (K-major) */
-    uint16_t l16[C][TP];         /* A, f16 */
-    uint16_t t16[C][TP];         /* T, f16 */
-    float a32[4][16][20];        /* A's diagonal blocks, f32 */
-    uint16_t tmp[4][16][24];
+    struct Work {                /* one transform group's inversion workspace (group = chunk parity) */
+        uint16_t l16[C][TP];     /* A, f16; once T is formed, its first 8 KB hold T [rows][rows] as a 128-byte
+                                    swizzled K-major operand (tile()) */
+        uint16_t t16[C][TP];     /* T, f16 */
+        float a32[4][16][20];    /* A's diagonal blocks, f32 */
+        uint16_t tmp[4][16][24];
+        __device__ uint16_t* tile() { return &l16[0][0]; }
+    } work[2];
     struct Meta {
         float gl[4];             /* gamma_L = exp(G_L) */
     } meta[2];                   /* by chunk parity: the chain's lanes read it after the stage may be reused */
     uint64_t landed[kHdStages], stage_free[kHdStages], buf_free[2];
-    uint64_t kk_full, kk_free, t_ready, wt_full, ut_full, tsw_free, w_ready, d1_full, d2_full, as_ready, av_ready, d2_ready;
+    uint64_t kk_full, kk_free, t_ready[2], wt_full, ut_full, tsw_free[2], w_ready[2], d1_full, d2_full, as_ready, av_ready,
+        d2_ready;
     uint32_t tmem;
     int abort;
 };
 static_assert(sizeof(HdStage) % 1024 == 0 && offsetof(HdSmem, kt) % 1024 == 0 && offsetof(HdSmem, wt) % 1024 == 0 &&
-              offsetof(HdSmem, tsw) % 1024 == 0, "operand tiles on 1024 bytes");
+              offsetof(HdSmem, work) % 1024 == 0 && sizeof(HdSmem::Work) % 1024 == 0, "operand tiles on 1024 bytes");
+static_assert(sizeof(HdSmem) + 1024 <= 227 * 1024, "one CTA a SM");
 constexpr int kHdSmem = (int)sizeof(HdSmem) + 1024;
 
 struct HdChain {
@@ -1197,14 +1202,16 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
         }
         for (int b = 0; b < 2; ++b) rf::mbar_init(&s.buf_free[b], 1);
         rf::mbar_init(&s.kk_full, 1);
-        rf::mbar_init(&s.kk_free, 4);   /* the four warps that read K K^T's rows */
+        rf::mbar_init(&s.kk_free, 2);   /* the two warps of a group that read K K^T's rows */
         rf::mbar_init(&s.wt_full, 1);
         rf::mbar_init(&s.ut_full, 1);
-        rf::mbar_init(&s.tsw_free, 1);
+        for (int b = 0; b < 2; ++b) {
+            rf::mbar_init(&s.tsw_free[b], 1);
+            rf::mbar_init(&s.t_ready[b], kHdP / 2);   /* one arrival a warp of the chunk's group */
+            rf::mbar_init(&s.w_ready[b], kHdP / 2);
+        }
         rf::mbar_init(&s.d1_full, 1);
         rf::mbar_init(&s.d2_full, 1);
-        rf::mbar_init(&s.t_ready, kHdP);
-        rf::mbar_init(&s.w_ready, kHdP);
         rf::mbar_init(&s.as_ready, kHdC);
         rf::mbar_init(&s.av_ready, kHdC);
         rf::mbar_init(&s.d2_ready, kHdC);
@@ -1213,7 +1220,7 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
     }
     if (w == kHdMma) rf::tmem_alloc<512>(&s.tmem);
     /* T's blocks above the diagonal stay zero (nothing writes them) */
-    for (int i = tid; i < C * TP / 2; i += kHdThreads) ((uint32_t*)&s.t16[0][0])[i] = 0u;
+    for (int i = tid; i < 2 * C * TP / 2; i += kHdThreads) ((uint32_t*)&s.work[i / (C * TP / 2)].t16[0][0])[i % (C * TP / 2)] = 0u;
     rf::tc_fence_before();
     __syncthreads();
     rf::tc_fence_after();
@@ -1307,11 +1314,11 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                 }
         } else if (l == 0 && total > 0) {
             auto wu = [&](int64_t q) -> bool {   /* W^T and U~^T of chunk q */
-                if (!rf::mbar_wait(&s.t_ready, (uint32_t)(q & 1), abort, rf::kErrGdnWait)) return false;
+                if (!rf::mbar_wait(&s.t_ready[q & 1], (uint32_t)((q >> 1) & 1), abort, rf::kErrGdnWait)) return false;
                 rf::tc_fence_after();
                 const int st = (int)(q % kHdStages);
                 const uint32_t x1 = rf::saddr(&s.in[st].k[0][0][0]), x2 = rf::saddr(&s.in[st].v[0][0][0]);
-                const uint32_t tt = rf::saddr(&s.tsw[0][0]);
+                const uint32_t tt = rf::saddr(s.work[q & 1].tile());
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk)
                     rf::umma_f16(tmem + kHdWt, rf::sw128_mnmajor_desc(x1 + kk * 2048, 8192), rf::sw128_kmajor_desc(tt + kk * 32),
@@ -1323,7 +1330,7 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                                  kIdescWu, kk > 0);
                 rf::mma_commit(&s.ut_full);
                 rf::mma_commit(&s.stage_free[st]);
-                rf::mma_commit(&s.tsw_free);
+                rf::mma_commit(&s.tsw_free[q & 1]);
                 return true;
             };
             bool ok = wu(0);
@@ -1331,7 +1338,7 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                 const uint32_t par = (uint32_t)(q & 1);
                 /* D1 = S W^T: the lanes wrote this chunk's f16 state, the transform its W^T tile */
                 if (!(ok = rf::mbar_wait(&s.as_ready, par, abort, rf::kErrGdnWait) &&
-                           rf::mbar_wait(&s.w_ready, par, abort, rf::kErrGdnWait)))
+                           rf::mbar_wait(&s.w_ready[par], (uint32_t)((q >> 1) & 1), abort, rf::kErrGdnWait)))
                     break;
                 rf::tc_fence_after();
                 const uint32_t wt = rf::saddr(&s.wt[par][0][0]);
@@ -1355,35 +1362,40 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
         }
     } else if (w < kHdP) {
         /* ------------------------------------------------------------ the transform (warps 0-7) */
-        auto psync = [&]() { bar_sync(1, 32 * kHdP); };
-        /* a barrier of the eight warps that also tells all of them whether any thread's wait gave up */
-        auto failed = [&](bool ok) { return bar_any(1, 32 * kHdP, !ok || *abort); };
-        /* W^T of chunk qq from tensor memory into its parity's B tile of D1 (free: that chunk's buf_free wait came
-         * before a barrier of these warps): thread = dk row 32 (w & 3) + l, the 32 columns of half w >> 2. Done while
-         * the next chunk is in hand (after its x2), so the W^T product's latency is not waited for; true if a wait
-         * gave up */
+        /* Two groups of four warps, group grp = (w >> 2) taking the chunks of parity grp, so two chunks' transforms
+         * are in flight: each is a string of short dependent steps that one chunk alone cannot spread over the SM.
+         * Within a group, warp lw = w & 3 is lane quarter lw of the tensor memory. */
+        const int grp = w >> 2, lw = w & 3, gt = tid & 127;
+        HdSmem::Work& wk = s.work[grp];
+        auto psync = [&]() { bar_sync(1 + grp, 128); };
+        /* a barrier of the group's four warps that also tells all of them whether any thread's wait gave up */
+        auto failed = [&](bool ok) { return bar_any(1 + grp, 128, !ok || *abort); };
+        /* W^T of chunk qq (this group's) from tensor memory into its parity's B tile of D1: thread = dk row 32 lw + l,
+         * the 64 columns in two halves; true if a wait gave up */
         auto read_back_wt = [&](int64_t qq) -> bool {
             if (failed(rf::mbar_wait(&s.wt_full, (uint32_t)(qq & 1), abort, rf::kErrGdnWait))) return true;
             rf::tc_fence_after();
-            uint32_t wv[32];
-            const int ch = w >> 2;
-            rf::tmem_ld32(tmem + ((uint32_t)(32 * (w & 3)) << 16) + kHdWt + 32 * ch, wv);
-            rf::tmem_ld_wait();
-            rf::tc_fence_before();
             const uint32_t wtile = rf::saddr(&s.wt[qq & 1][0][0]);
-            const int dk = 32 * (w & 3) + l;
+            const int dk = 32 * lw + l;
+#pragma unroll 1
+            for (int ch = 0; ch < 2; ++ch) {
+                uint32_t wv[32];
+                rf::tmem_ld32(tmem + ((uint32_t)(32 * lw) << 16) + kHdWt + 32 * ch, wv);
+                rf::tmem_ld_wait();
 #pragma unroll
-            for (int c8 = 0; c8 < 4; ++c8) {
-                const uint32_t* x = &wv[c8 * 8];
-                sts128(wtile + rf::sw128_off(dk, 8 * (4 * ch + c8)),
-                       make_uint4(rf::pack_f16(__uint_as_float(x[0]), __uint_as_float(x[1])),
-                                  rf::pack_f16(__uint_as_float(x[2]), __uint_as_float(x[3])),
-                                  rf::pack_f16(__uint_as_float(x[4]), __uint_as_float(x[5])),
-                                  rf::pack_f16(__uint_as_float(x[6]), __uint_as_float(x[7]))));
+                for (int c8 = 0; c8 < 4; ++c8) {
+                    const uint32_t* x = &wv[c8 * 8];
+                    sts128(wtile + rf::sw128_off(dk, 8 * (4 * ch + c8)),
+                           make_uint4(rf::pack_f16(__uint_as_float(x[0]), __uint_as_float(x[1])),
+                                      rf::pack_f16(__uint_as_float(x[2]), __uint_as_float(x[3])),
+                                      rf::pack_f16(__uint_as_float(x[4]), __uint_as_float(x[5])),
+                                      rf::pack_f16(__uint_as_float(x[6]), __uint_as_float(x[7]))));
+                }
             }
+            rf::tc_fence_before();
             rf::fence_proxy_async_smem();
             __syncwarp();
-            if (l == 0) rf::mbar_arrive(&s.w_ready);
+            if (l == 0) rf::mbar_arrive(&s.w_ready[grp]);
             return false;
         };
         int64_t q = 0;
@@ -1391,122 +1403,151 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
         for (int64_t cid = blockIdx.x; cid < n_chains && !stop; cid += gridDim.x) {
             const HdChain ch = hd_chain(g, cid);
             for (int64_t j = 0; j < ch.chunks; ++j, ++q) {
-                const int st = (int)(q % kHdStages), par = (int)(q & 1);
+                if ((q & 1) != grp) continue;   /* the other group's chunk */
+                const int st = (int)(q % kHdStages), par = grp;
                 const int len = (int)min((int64_t)C, ch.r1 - (ch.r0 + j * C));
                 HdStage& sg = s.in[st];
                 HdSmem::Meta& mt = s.meta[par];
                 /* the chunk's k, v, g, beta and (by the loader) G and G_L are in */
                 if ((stop = failed(rf::mbar_wait(&s.landed[st], (uint32_t)((q / kHdStages) & 1), abort, rf::kErrGdnWait)))) break;
                 const float gl = sg.gl[0];
-                if (tid == 0) mt.gl[0] = __expf(gl);   /* gamma_L for the chain's lanes */
+                if (gt == 0) mt.gl[0] = __expf(gl);   /* gamma_L for the chain's lanes */
                 const uint32_t ktile = rf::saddr(&sg.k[0][0][0]), vtile = rf::saddr(&sg.v[0][0][0]);
-                /* x2 = beta v in place: row tid & 63, column quarter tid >> 6 */
+                /* x2 = beta v in place: row gt & 63, column half gt >> 6; four segments' loads before their stores
+                 * (the shared-memory helpers keep their order as written) */
                 {
-                    const int r = tid & 63;
+                    const int r = gt & 63;
                     const bool in = r < len;
                     const float br = sg.b[r];
 #pragma unroll
-                    for (int it = 0; it < 4; ++it) {
-                        const uint32_t off = rf::sw128_off(r, (4 * (tid >> 6) + it) * 8);
-                        sts128(vtile + off, scale_bf16x8_to_f16(lds128(vtile + off), br, in));
+                    for (int b4 = 0; b4 < 8; b4 += 4) {
+                        uint4 raw[4];
+                        uint32_t off[4];
+#pragma unroll
+                        for (int it = 0; it < 4; ++it) {
+                            off[it] = rf::sw128_off(r, (8 * (gt >> 6) + b4 + it) * 8);
+                            raw[it] = lds128(vtile + off[it]);
+                        }
+#pragma unroll
+                        for (int it = 0; it < 4; ++it) sts128(vtile + off[it], scale_bf16x8_to_f16(raw[it], br, in));
                     }
                 }
-                /* the previous chunk's W^T, its product long finished */
-                if (q > 0 && (stop = read_back_wt(q - 1))) break;
-                /* K K^T landed in tensor memory (so x1 may replace the k tile); K~'s tile of this parity free once D2
-                 * of two chunks ago has read it */
-                bool ok = rf::mbar_wait(&s.kk_full, (uint32_t)par, abort, rf::kErrGdnWait);
-                if ((w & 3) >= 2 && q >= 2) ok = ok && rf::mbar_wait(&s.buf_free[par], (uint32_t)(((q >> 1) - 1) & 1), abort, rf::kErrGdnWait);
+                /* K K^T landed in tensor memory (so x1 may replace the k tile); this parity's K~ tile free once D2 of
+                 * two chunks ago has read it; this group's A / T tile free once W^T and U~^T of its previous chunk
+                 * have read T from it */
+                bool ok = rf::mbar_wait(&s.kk_full, (uint32_t)(q & 1), abort, rf::kErrGdnWait);
+                if (q >= 2) {
+                    ok = ok && rf::mbar_wait(&s.buf_free[par], (uint32_t)(((q >> 1) - 1) & 1), abort, rf::kErrGdnWait);
+                    ok = ok && rf::mbar_wait(&s.tsw_free[grp], (uint32_t)(((q >> 1) - 1) & 1), abort, rf::kErrGdnWait);
+                }
                 if ((stop = failed(ok))) break;
                 rf::tc_fence_after();
-                if ((w & 3) < 2) {
-                    /* A's rows: thread = row i (lane quarter w & 3), the 32 columns of half w >> 2 from tensor memory */
-                    const int i = 32 * (w & 3) + l, j0 = 32 * (w >> 2);
-                    uint32_t kk[32];
-                    rf::tmem_ld32(tmem + ((uint32_t)(32 * (w & 3)) << 16) + kHdKk + j0, kk);
-                    rf::tmem_ld_wait();
-                    rf::tc_fence_before();
-                    __syncwarp();
-                    if (l == 0) rf::mbar_arrive(&s.kk_free);   /* the next chunk's K K^T may overwrite it */
+                if (lw < 2) {
+                    /* A's rows: thread = row i (lane quarter lw), its 64 columns from tensor memory, 32 at a time */
+                    const int i = 32 * lw + l;
                     const bool rowin = i < len;
                     const float Gi = sg.G[i], bi = sg.b[i];
+                    const uint32_t base = tmem + ((uint32_t)(32 * lw) << 16) + kHdKk;
+#pragma unroll 1
+                    for (int j0 = 0; j0 < C; j0 += 16) {
+                        float gv[16];   /* G of the 16 columns, in registers (no load between the stores below) */
 #pragma unroll
-                    for (int jj = 0; jj < 32; jj += 2) {
-                        const int j = j0 + jj;
-                        float v[2];
+                        for (int x = 0; x < 4; ++x) *(float4*)&gv[4 * x] = *(const float4*)&sg.G[j0 + 4 * x];
+                        uint32_t kk[16];
+                        rf::tmem_ld16(base + j0, kk);
+                        rf::tmem_ld_wait();
+                        if (j0 + 16 == C) {
+                            rf::tc_fence_before();
+                            __syncwarp();
+                            if (l == 0) rf::mbar_arrive(&s.kk_free);   /* the next chunk's K K^T may overwrite it */
+                        }
+                        uint32_t pk[8];
 #pragma unroll
-                        for (int e = 0; e < 2; ++e)
-                            v[e] = (j + e < i && rowin) ? bi * __expf(Gi - sg.G[j + e]) * __uint_as_float(kk[jj + e]) : 0.0f;
-                        *(uint32_t*)&s.l16[i][j] = rf::pack_f16(v[0], v[1]);
-                        if ((j >> 4) == (i >> 4)) *(float2*)&s.a32[i >> 4][i & 15][j & 15] = make_float2(v[0], v[1]);
+                        for (int jj = 0; jj < 16; jj += 2) {
+                            const int jc = j0 + jj;
+                            float v[2];
+#pragma unroll
+                            for (int e = 0; e < 2; ++e)
+                                v[e] = (jc + e < i && rowin) ? bi * __expf(Gi - gv[jj + e]) * __uint_as_float(kk[jj + e]) : 0.0f;
+                            pk[jj >> 1] = rf::pack_f16(v[0], v[1]);
+                            if ((jc >> 4) == (i >> 4)) *(float2*)&wk.a32[i >> 4][i & 15][jc & 15] = make_float2(v[0], v[1]);
+                        }
+                        *(uint4*)&wk.l16[i][j0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                        *(uint4*)&wk.l16[i][j0 + 8] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
                     }
                 } else {
-                    /* x1 = beta gamma k in place and K~ = exp(G_L - G) k into this parity's tile: thread = row r,
-                     * column half t2 >> 6 */
-                    const int t2 = ((w >> 2) << 6) | ((w & 1) << 5) | l, r = t2 & 63;
+                    /* x1 = beta gamma k in place and K~ = exp(G_L - G) k into this parity's tile: thread = row r */
+                    const int r = gt - 64;
                     const bool in = r < len;
                     const float gr = sg.G[r], br = sg.b[r];
                     const float fk = in ? __expf(gl - gr) : 0.0f, fx = in ? br * __expf(gr) : 0.0f;
                     const uint32_t kst = rf::saddr(&s.kt[par][0][0][0]);
-#pragma unroll 4
-                    for (int sg8 = 0; sg8 < 8; ++sg8) {
-                        const int seg = 8 * (t2 >> 6) + sg8;
-                        const uint32_t off = rf::sw128_off(r, seg * 8);
-                        const uint4 kr = lds128(ktile + off);
-                        sts128(kst + off, scale_bf16x8_to_f16(kr, fk, in));
-                        sts128(ktile + off, scale_bf16x8_to_f16(kr, fx, in));
+#pragma unroll 1
+                    for (int b4 = 0; b4 < 16; b4 += 4) {   /* four segments' loads before their stores */
+                        uint4 kr[4];
+                        uint32_t off[4];
+#pragma unroll
+                        for (int it = 0; it < 4; ++it) {
+                            off[it] = rf::sw128_off(r, (b4 + it) * 8);
+                            kr[it] = lds128(ktile + off[it]);
+                        }
+#pragma unroll
+                        for (int it = 0; it < 4; ++it) {
+                            sts128(kst + off[it], scale_bf16x8_to_f16(kr[it], fk, in));
+                            sts128(ktile + off[it], scale_bf16x8_to_f16(kr[it], fx, in));
+                        }
                     }
                 }
                 psync();
-                /* diagonal blocks of T by substitution in f32: warp w block w >> 1, columns 8 (w & 1)..+8, lane l row
-                 * l & 15 of 4 columns */
+                /* diagonal blocks of T by substitution in f32: warp lw block lw, lane l row l & 15 of 8 columns */
                 {
-                    const int b = w >> 1, r = l & 15, c0 = 8 * (w & 1) + 4 * (l >> 4);
+                    const int r = l & 15, c0 = 8 * (l >> 4);
                     float a[16];
 #pragma unroll
                     for (int q4 = 0; q4 < 4; ++q4) {
-                        const float4 v = *(const float4*)&s.a32[b][r][4 * q4];
+                        const float4 v = *(const float4*)&wk.a32[lw][r][4 * q4];
                         a[4 * q4] = v.x;
                         a[4 * q4 + 1] = v.y;
                         a[4 * q4 + 2] = v.z;
                         a[4 * q4 + 3] = v.w;
                     }
-                    float x[4];
+                    float x[8];
 #pragma unroll
-                    for (int cc = 0; cc < 4; ++cc) x[cc] = r == c0 + cc ? 1.0f : 0.0f;
+                    for (int cc = 0; cc < 8; ++cc) x[cc] = r == c0 + cc ? 1.0f : 0.0f;
 #pragma unroll
                     for (int jj = 0; jj < 15; ++jj)
 #pragma unroll
-                        for (int cc = 0; cc < 4; ++cc) {
+                        for (int cc = 0; cc < 8; ++cc) {
                             const float xj = __shfl_sync(0xffffffffu, x[cc], (l & 16) | jj);
                             x[cc] = fmaf(-(jj < r ? a[jj] : 0.0f), xj, x[cc]);
                         }
-                    *(uint2*)&s.t16[16 * b + r][16 * b + c0] = make_uint2(rf::pack_f16(x[0], x[1]), rf::pack_f16(x[2], x[3]));
+                    *(uint4*)&wk.t16[16 * lw + r][16 * lw + c0] = make_uint4(rf::pack_f16(x[0], x[1]), rf::pack_f16(x[2], x[3]),
+                                                                             rf::pack_f16(x[4], x[5]), rf::pack_f16(x[6], x[7]));
                 }
                 psync();
-                if (w < 3) tri_offdiag_block(s, w + 1, w, w);   /* T10, T21, T32 */
+                if (lw < 3) tri_offdiag_block(wk, lw + 1, lw, lw);   /* T10, T21, T32 */
                 psync();
-                if (w < 2) tri_offdiag_block(s, w + 2, w, w);   /* T20, T31 */
+                if (lw < 2) tri_offdiag_block(wk, lw + 2, lw, lw);   /* T20, T31 */
                 psync();
-                if (w == 0) tri_offdiag_block(s, 3, 0, 0);      /* T30 */
-                /* T into its operand tile, free once the previous chunk's W^T and U~^T have read it */
-                if ((stop = failed(q < 1 || rf::mbar_wait(&s.tsw_free, (uint32_t)((q - 1) & 1), abort, rf::kErrGdnWait)))) break;
+                if (lw == 0) tri_offdiag_block(wk, 3, 0, 0);         /* T30 */
+                psync();
+                /* T into its operand tile over A's first 8 KB (A is no longer read) */
                 {
-                    const uint32_t tt = rf::saddr(&s.tsw[0][0]);
-                    const int r = tid >> 2;
+                    const uint32_t tt = rf::saddr(wk.tile());
+                    const int r = gt >> 1;
+                    uint4 v[4];
 #pragma unroll
-                    for (int c2 = 0; c2 < 2; ++c2) {
-                        const int cc = 2 * (tid & 3) + c2;
-                        sts128(tt + rf::sw128_off(r, 8 * cc), *(const uint4*)&s.t16[r][8 * cc]);
-                    }
+                    for (int c4 = 0; c4 < 4; ++c4) v[c4] = *(const uint4*)&wk.t16[r][8 * (4 * (gt & 1) + c4)];
+#pragma unroll
+                    for (int c4 = 0; c4 < 4; ++c4) sts128(tt + rf::sw128_off(r, 8 * (4 * (gt & 1) + c4)), v[c4]);
                 }
                 rf::fence_proxy_async_smem();   /* x1, x2, K~ and T for the tensor cores */
                 __syncwarp();
-                if (l == 0) rf::mbar_arrive(&s.t_ready);
+                if (l == 0) rf::mbar_arrive(&s.t_ready[grp]);
+                /* W^T (the product issued once t_ready is complete) into its tile */
+                if ((stop = read_back_wt(q))) break;
             }
         }
-        /* the last chunk's W^T */
-        if (!stop && q > 0) read_back_wt(q - 1);
     } else if (w < kHdLoad) {
         /* ------------------------------------------------------------ the chain's lanes (warps 8-15) */
         const int qd = w & 3, hf = (w - kHdP) >> 2, i = 32 * qd + l;   /* dv row i; columns of half hf */
