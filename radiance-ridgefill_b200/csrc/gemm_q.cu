@@ -111,7 +111,7 @@ __device__ __forceinline__ void fold_block(uint32_t taddr, float (&acc)[kWarpCol
 /* The kernel's forms: the bf16 GEMM, the int8 projector, the int8 projector writing out its int32 block sums
  * (the optional acc operand), and the int8 projector writing only the selected rows (the optional rows operand).
  * Separate instantiations keep each form's registers to itself. */
-enum GemmMode { kModeBf16 = 0, kModeI8 = 1, kModeI8Dump = 2, kModeI8Rows = 3 };
+enum GemmMode { kModeBf16 = 0, kModeI8 = 1, kModeI8Dump = 2, kModeI8Rows = 3, kModeCount = 4 };
 
 template <int kMode>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -670,7 +670,7 @@ bool int8_tile_map(CUtensorMap* map, const void* base, int64_t rows, int64_t col
 template <int kMode>
 int launch_pairs(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUtensorMap& map_y, const GemmPlan& p,
                  cudaStream_t stream) {
-    static int max_pairs[3] = { 0, 0, 0 };
+    static int max_pairs[kModeCount] = {};   /* per form: clusters of two a GPU can hold */
     if (cudaFuncSetAttribute(gemm_q_kernel<kMode>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
         return RAD_E_DEVICE;
     if (!max_pairs[kMode]) {
