@@ -213,7 +213,13 @@ def roofline(op: str, ms: float, alg: dict, pk: dict) -> dict:
         peak = 2.0 * pk["bf16_tflops"]
         r = {"bound": "tensor", "achieved": alg["int8_ops"] / (ms * 1e-3) / 1e12, "peak": peak, "unit": "TOP/s",
              "traffic": None, "note": f"int8 dense peak = 2 x the {pk['source']} bf16 figure ({pk['bf16_tflops']} TF/s); "
-                                      "the pass's int8 GEMM launches together (projectors, mixed and k|v projections)"}
+                                      "the pass's ridgefill_gemm_nt_q_bias launches together (projectors, q tails, attention k|v)"}
+    elif op == "ridgefill_gdn_in_proj":
+        peak = 2.0 * pk["bf16_tflops"]
+        r = {"bound": "tensor", "achieved": alg["int8_ops_in_proj"] / (ms * 1e-3) / 1e12, "peak": peak, "unit": "TOP/s",
+             "traffic": None, "note": f"int8 dense peak = 2 x the {pk['source']} bf16 figure ({pk['bf16_tflops']} TF/s); "
+                                      "the DeltaNet k|v projections with the convolution, SiLU and k norm in their "
+                                      "epilogue (the 3-row tile overlap's extra 2.4 % of MMAs not counted)"}
     elif op == "ridgefill_gdn_fill":
         # DRAM bytes over algorithmic bytes of the per-head fill, from one ncu capture of it (8,192 rows, 128 heads:
         # 424.2 MB read + written against 427.4 MB, profiles/gdn_fill_heads_T8192.md); the traffic grows with the
@@ -365,7 +371,7 @@ def run_mine(args):
                 "gpu_launches": kernels * args.steps,
                 "per_op_ms": {k: round(v, 4) for k, v in sorted(per_op.items(), key=lambda kv: -kv[1])},
                 "roofline": roof,
-                "roofline_next": roofline(second, per_op[second], alg, pk) if second in (fill_key, "ridgefill_gemm_nt_q_bias") else None,
+                "roofline_next": roofline(second, per_op[second], alg, pk) if second in (fill_key, "ridgefill_gemm_nt_q_bias", "ridgefill_gdn_in_proj") else None,
                 "clocks": clock_info,
                 "e2e": {"value": T_FULL / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                         "d2h_bytes_per_step": d2h}}

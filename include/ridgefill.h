@@ -64,6 +64,9 @@ enum { GD_Q = 0, GD_K, GD_V, GD_G, GD_BETA, GD_STATE, GD_STATE_IDX, GD_CU, GD_O 
  * with the gate written per row rather than in its in-chunk cumulative form). */
 enum { CP_X = 0, CP_W, CP_BIAS, CP_A_LOG, CP_DT_BIAS, CP_STATE, CP_CU, CP_A, CP_B, CP_IDX, CP_CTX, CP_Q, CP_K, CP_V,
        CP_G, CP_BETA };
+/* ridgefill_gdn_in_proj (new; the DeltaNet block's int8 in-projection of its k|v channels, arch/qwen4exp_fill.h:
+ * 36-40, with conv_prep's convolution, SiLU and k norm in the projection's epilogue). */
+enum { IP_A = 0, IP_A_SCALE, IP_B, IP_B_SCALE, IP_W, IP_BIAS, IP_STATE, IP_CU, IP_IDX, IP_CTX, IP_K, IP_V, IP_TAIL };
 /* ridgefill_attn_kv_fill (new; the gated-attention block's K/V path in the lean fill, arch/qwen4exp_fill.h:104-114:
  * the k_norm, rope_k and kv_store issues after the k and v projections, as one op). */
 enum { AK_K = 0, AK_V, AK_W, AK_POS, AK_SLOTS, AK_CACHE, AK_K_OUT };
@@ -342,7 +345,26 @@ typedef struct RidgeFillConvPrep {
     float*         g;        int64_t g_row;
     float*         beta;     int64_t beta_row;
     int64_t        T, n_head_k, n_head_v, dk, dv, width;
+    int            columns;                     /* 0: gates and conv state only (the columns come from in_proj) */
 } RidgeFillConvPrep;
+
+/* ridgefill_gdn_in_proj: x = bf16(a_scale[t] b_scale[n] sum_k a[t,k] b[n,k]) over the k|v channels n of the
+ * DeltaNet block's input (N = (Hk + Hv) 128: k heads first), then per channel the causal width-4 convolution over
+ * each sequence (the rows before its start from the conv state when ctx > 0, else zero), SiLU, the L2 norm of each
+ * k head (eps 1e-6), k and v rounded to bf16 -- conv_prep's arithmetic on the projection's rows, which never leave
+ * the SM except each sequence's last three, written to `tail` (what the conv-state update reads). */
+typedef struct RidgeFillInProj {
+    RidgeFillGemmQ gemm;                        /* a, a_scale, b, b_scale; y = tail; group = K */
+    const uint16_t* w;                          /* [N, 4] bf16 taps */
+    const uint16_t* bias;                       /* [N] bf16 or null */
+    const uint16_t* state;   int64_t st_slot, st_row, n_states;   /* history row t of slot s: state + s st_slot + t st_row */
+    const int32_t* cu;       int64_t n_seq;
+    const int32_t* idx;      int64_t idx_pitch;
+    const int32_t* ctx;                         /* [n_seq] or null */
+    uint16_t*      k;        int64_t k_row, k_head;
+    uint16_t*      v;        int64_t v_row, v_head;
+    int64_t        n_k;                         /* columns [0, n_k) are k channels (Hk 128) */
+} RidgeFillInProj;
 
 /* ridgefill_attn_kv_fill: the attention block's cache write for a prefill of T rows. Per row t and kv-head h
  * (D = head_dim = 256, R = rope_dim, lane l = elements 8l..8l+7):
@@ -406,6 +428,7 @@ int ridgefill_gemm_bias_parse(const RadArgs* a, RidgeFillGemmBias* out);
 int ridgefill_quant_parse(const RadArgs* a, RidgeFillQuant* out);
 int ridgefill_gdn_parse(const RadArgs* a, RidgeFillGdn* out);
 int ridgefill_conv_prep_parse(const RadArgs* a, RidgeFillConvPrep* out);
+int ridgefill_in_proj_parse(const RadArgs* a, RidgeFillInProj* out);
 int ridgefill_attn_kv_parse(const RadArgs* a, RidgeFillAttnKv* out);
 
 /* The device rows (kernels/ridgefill.h:304-310 and the new ops): async launches on `s` (a
@@ -423,6 +446,7 @@ int ridgefill_gemm_nt_bias_device(const RadArgs* a, RadStream s);
 int ridgefill_quant_act_device(const RadArgs* a, RadStream s);
 int ridgefill_gdn_fill_device(const RadArgs* a, RadStream s);
 int ridgefill_gdn_conv_prep_device(const RadArgs* a, RadStream s);
+int ridgefill_gdn_in_proj_device(const RadArgs* a, RadStream s);
 int ridgefill_attn_kv_fill_device(const RadArgs* a, RadStream s);
 
 /* The first error code a tensor-core kernel of this library recorded after giving up on a bounded

@@ -71,11 +71,17 @@ static const RadParamSpec pGdn[] = { RF_P_INT("M"), RF_P_INT("n_head_k"), RF_P_I
 static const RadOperandSpec oGdn[] = { RF_IN_OPT("q"), RF_IN("k"), RF_IN("v"), RF_IN("g"), RF_IN("beta"),
                                        RF_INOUT("state"), RF_IN("state_idx"), RF_IN("cu_seqlens"), RF_OUT_OPT("o") };
 static const RadParamSpec pConv[] = { RF_P_INT("M"), RF_P_INT("n_head_k"), RF_P_INT("n_head_v"), RF_P_INT("head_k"),
-                                      RF_P_INT("head_v"), RF_P_INT("conv") };
+                                      RF_P_INT("head_v"), RF_P_INT("conv"), RF_P_OPT("columns", RAD_P_INT) };
 static const RadOperandSpec oConv[] = { RF_IN("x"), RF_IN("w_conv"), RF_IN_OPT("conv_bias"), RF_IN("A_log"),
                                         RF_IN("dt_bias"), RF_INOUT("conv_state"), RF_IN("cu_seqlens"), RF_IN("a"),
                                         RF_IN("b"), RF_IN("conv_idx"), RF_IN_OPT("ctx_lens"), RF_OUT_OPT("q"), RF_OUT("k"),
                                         RF_OUT("v"), RF_OUT("g"), RF_OUT("beta") };
+static const RadParamSpec pInProj[] = { RF_P_INT("M"), RF_P_INT("N"), RF_P_INT("K"), RF_P_INT("n_head_k"),
+                                        RF_P_INT("n_head_v"), RF_P_INT("group"), RF_P_STR("dtype") };
+static const RadOperandSpec oInProj[] = { RF_IN("a"), RF_IN("a_scale"), RF_IN("b"), RF_IN("b_scale"), RF_IN("w_conv"),
+                                          RF_IN_OPT("conv_bias"), RF_IN("conv_state"), RF_IN("cu_seqlens"),
+                                          RF_IN("conv_idx"), RF_IN_OPT("ctx_lens"), RF_OUT("k"), RF_OUT("v"),
+                                          RF_OUT("tail") };
 static const RadParamSpec pAttnKv[] = { RF_P_INT("M"), RF_P_INT("n_head_kv"), RF_P_INT("head_dim"), RF_P_INT("rope_dim"),
                                         RF_P_F64("rope_theta"), RF_P_OPT("eps", RAD_P_F64),
                                         RF_P_OPT("rope_mode", RAD_P_STR), RF_P_OPT("rope_sections", RAD_P_STR) };
@@ -142,7 +148,16 @@ static const RadOpSchema kSchemas[] = {
   "(ctx_lens[i] > 0) or zero; y = u / (1 + exp(-u)); q and k heads divided by sqrt(sum y^2 + 1e-6); q, k, v bf16. "
   "g[t, h] = -exp(A_log[h]) softplus(a[t, h] + dt_bias[h]) (threshold 20), beta = sigmoid(b); f32. conv_state "
   "bf16 [slots, 3, C] then holds each sequence's last three input rows (a slot outside the pool: zero history, "
-  "not written). Rows outside every sequence are not written." },
+  "not written). Rows outside every sequence are not written. Optional columns = 0: only g, beta and the conv "
+  "state are written (k and v come from ridgefill_gdn_in_proj, which has read the old conv state)." },
+{ "ridgefill_gdn_in_proj", RF_ARR(pInProj), RF_ARR(oInProj),
+  "The DeltaNet block's int8 in-projection of its k|v channels with conv_prep's per-channel arithmetic in the "
+  "same pass: x[t, n] = bf16(a_scale[t] b_scale[n] sum_k a[t, k] b[n, k]) (group = K: int32 over all of K, one "
+  "f32 product, one rounding) for the N = (Hk + Hv) 128 channels (k heads first); then per sequence [cu[i], "
+  "cu[i+1]) ridgefill_gdn_conv_prep's convolution, SiLU and k-head L2 norm on those channels, bit for bit, into "
+  "k bf16 [T, Hk, 128] and v bf16 [T, Hv, 128]; x itself is written only on each sequence's last three rows, "
+  "into tail bf16 [T, N] (what the conv-state update reads). conv_state bf16 [slots, 3, N] is read, not written: "
+  "run ridgefill_gdn_conv_prep with columns = 0 afterwards for the gates and the state update." },
 { "ridgefill_attn_kv_fill", RF_ARR(pAttnKv), RF_ARR(oAttnKv),
   "The attention block's K/V cache write for T prefill rows (k_norm, rope_k, kv_store as one op): per row t and "
   "kv-head h, kn = bf16(k * w / sqrt(mean(k^2) + eps)) (f32), the first rope_dim elements rotated in half pairs "
@@ -286,6 +301,16 @@ inline int shape_conv_prep(const RadParam* p, int n_p, int operand, RadOpdDesc* 
                                 opd(RAD_BF16, { T, hv }), opd(RAD_BF16, { T, hv }), opd_idx({ 1 }, slots),
                                 opd(RAD_I32, { 1 }), opd(RAD_BF16, { T, hk, dk }), opd(RAD_BF16, { T, hk, dk }),
                                 opd(RAD_BF16, { T, hv, dv }), opd(RAD_F32, { T, hv }), opd(RAD_F32, { T, hv }) });
+}
+
+inline int shape_in_proj(const RadParam* p, int n_p, int operand, RadOpdDesc* out) {
+    const int64_t T = dim(p, n_p, "M"), K = dim(p, n_p, "K"), hk = dim(p, n_p, "n_head_k"), hv = dim(p, n_p, "n_head_v");
+    const int64_t N = (hk + hv) * 128, slots = 3;
+    return pick(out, operand, { opd(RAD_I8, { T, K }), opd(RAD_F32, { T, 1 }, RAD_FILL_SIGMOID), opd(RAD_I8, { N, K }),
+                                opd(RAD_F32, { 1, N }, RAD_FILL_SIGMOID), opd(RAD_BF16, { N, 4 }), opd(RAD_BF16, { N }),
+                                opd(RAD_BF16, { slots, 3, N }), opd_idx({ 2 }, T, RAD_OPD_F_IDX_CU), opd_idx({ 1 }, slots),
+                                opd(RAD_I32, { 1 }), opd(RAD_BF16, { T, hk, 128 }), opd(RAD_BF16, { T, hv, 128 }),
+                                opd(RAD_BF16, { T, N }) });
 }
 
 inline int shape_attn_kv(const RadParam* p, int n_p, int operand, RadOpdDesc* out) {

@@ -43,4 +43,27 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     return (uint32_t)f32_to_bf16_bits(lo) | ((uint32_t)f32_to_bf16_bits(hi) << 16);
 }
 
+/* Start of sequence i: cu[i] clamped to [0, T]. */
+__device__ __forceinline__ int64_t seq_start(const int32_t* cu, int64_t T, int64_t i) {
+    return min(max((int64_t)cu[i], (int64_t)0), T);
+}
+
+/* The sequence holding row r of a T-row batch split by cu_seqlens `cu` (n_seq + 1 entries): the last i whose clamped
+ * start is <= r, if r lies before its clamped end (its start and end in *s0, *e0); -1 otherwise. Values outside
+ * [0, T] are clamped, the fill's rule. */
+__device__ inline int find_seq(const int32_t* cu, int64_t n_seq, int64_t T, int64_t r, int64_t* s0, int64_t* e0) {
+    if (n_seq <= 0 || seq_start(cu, T, 0) > r) return -1;
+    int64_t lo = 0, hi = n_seq - 1;
+    while (lo < hi) {
+        const int64_t mid = (lo + hi + 1) >> 1;
+        if (seq_start(cu, T, mid) <= r) lo = mid;
+        else hi = mid - 1;
+    }
+    const int64_t a = seq_start(cu, T, lo), b = min(max((int64_t)cu[lo + 1], a), T);
+    if (r >= b) return -1;
+    *s0 = a;
+    *e0 = b;
+    return (int)lo;
+}
+
 }  // namespace rf

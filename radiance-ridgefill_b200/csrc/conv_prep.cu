@@ -13,7 +13,8 @@
  * flight at once as asynchronous copies into the lane's own shared-memory slots (32 KiB a CTA, three CTAs a SM). The
  * gates of a row block are one more warp task, a lane per v-head. A second kernel then writes each sequence's last
  * three input rows into its conv-state slot (it reads the old state first, thread by thread, so the update is in
- * place).
+ * place). With columns == 0 (ridgefill_gdn_in_proj has produced k and v) only the gates and the conv state are
+ * written.
  */
 #include <cuda_bf16.h>
 
@@ -44,25 +45,10 @@ __device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
     return *(const uint32_t*)&p;
 }
 
-__device__ __forceinline__ int64_t seq_start(const RidgeFillConvPrep& g, int64_t i) {
-    return min(max((int64_t)g.cu[i], (int64_t)0), g.T);
-}
+__device__ __forceinline__ int64_t seq_start(const RidgeFillConvPrep& g, int64_t i) { return rf::seq_start(g.cu, g.T, i); }
 
-/* The sequence holding row r: the last i whose clamped start is <= r, if r lies before its clamped end;
- * -1 otherwise. cu is read where it lies; values outside [0, T] are clamped (the fill's rule). */
-__device__ int find_seq(const RidgeFillConvPrep& g, int64_t r, int64_t* s0, int64_t* e0) {
-    if (g.n_seq <= 0 || seq_start(g, 0) > r) return -1;
-    int64_t lo = 0, hi = g.n_seq - 1;
-    while (lo < hi) {
-        const int64_t mid = (lo + hi + 1) >> 1;
-        if (seq_start(g, mid) <= r) lo = mid;
-        else hi = mid - 1;
-    }
-    const int64_t a = seq_start(g, lo), b = min(max((int64_t)g.cu[lo + 1], a), g.T);
-    if (r >= b) return -1;
-    *s0 = a;
-    *e0 = b;
-    return (int)lo;
+__device__ __forceinline__ int find_seq(const RidgeFillConvPrep& g, int64_t r, int64_t* s0, int64_t* e0) {
+    return rf::find_seq(g.cu, g.n_seq, g.T, r, s0, e0);
 }
 
 /* Whether sequence `seq` continues a context held in its conv-state slot; the slot (or -1). */
@@ -79,16 +65,6 @@ __device__ __forceinline__ uint2 window_row(const RidgeFillConvPrep& g, int64_t 
     if (row >= s0) return *(const uint2*)(g.x + row * g.x_row + c);
     if (slot < 0) return make_uint2(0u, 0u);
     return *(const uint2*)(g.state + slot * g.st_slot + (3 - (s0 - row)) * C + c);
-}
-
-/* SiLU u / (1 + e^-u) as u times the approximate reciprocal (1 ulp) of the denominator, with the fast exp: well
- * inside bf16's rounding. The reciprocal is the non-flushing form, so a denominator above 2^126 (u below about
- * -87.3, where the value is about u e^u, under 1e-36 in magnitude) still gives the tiny value the f32 rule gives,
- * not 0; an infinite one (u below about -88.7) gives -0, as the division does. */
-__device__ __forceinline__ float silu(float u) {
-    float r;
-    asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(1.0f + __expf(-u)));
-    return u * r;
 }
 
 /* The gates of rows [r0, r1) for every v-head, lane = head (coalesced over the heads): rows outside every sequence
@@ -125,8 +101,8 @@ __global__ void __launch_bounds__(kThreads, 3) conv_prep_kernel(RidgeFillConvPre
     uint2* stage = rows_smem + (threadIdx.x >> 5) * kRows * 32 + lane;
     const int64_t hk = g.n_head_k;
     const int64_t C = 2 * hk * 128 + g.n_head_v * 128, n_hc = C / 128;
-    /* without a q output the q columns are not computed */
-    const int64_t first = g.q ? 0 : hk, live = n_hc - first, per_block = live + 1;
+    /* without a q output the q columns are not computed; with columns == 0 none is (only the gates) */
+    const int64_t first = g.q ? 0 : hk, live = g.columns ? n_hc - first : 0, per_block = live + 1;
     const int64_t tasks = (g.T + kRows - 1) / kRows * per_block;
     const int64_t stride = (int64_t)gridDim.x * (kThreads / 32);
     for (int64_t task = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); task < tasks; task += stride) {
@@ -171,8 +147,8 @@ __global__ void __launch_bounds__(kThreads, 3) conv_prep_kernel(RidgeFillConvPre
                 rf::fma2_rn(u0, u1, wt[e][1], wt[e + 1][1], w1[e], w1[e + 1]);
                 rf::fma2_rn(u0, u1, wt[e][2], wt[e + 1][2], w2[e], w2[e + 1]);
                 rf::fma2_rn(u0, u1, wt[e][3], wt[e + 1][3], cur[e], cur[e + 1]);
-                y[e] = silu(u0);
-                y[e + 1] = silu(u1);
+                y[e] = rf::silu(u0);
+                y[e + 1] = rf::silu(u1);
             }
             if (norm) {
                 float ss = 0.0f;
@@ -271,7 +247,7 @@ extern "C" int ridgefill_gdn_conv_prep_device(const RadArgs* a, RadStream s) {
     if (rc != RAD_OK) return rc;
     cudaStream_t stream = rf::as_stream(s);
     const int64_t C = 2 * g.n_head_k * 128 + g.n_head_v * 128;
-    const int64_t tasks = (g.T + kRows - 1) / kRows * (C / 128 - (g.q ? 0 : g.n_head_k) + 1);
+    const int64_t tasks = (g.T + kRows - 1) / kRows * ((g.columns ? C / 128 - (g.q ? 0 : g.n_head_k) : 0) + 1);
     if (tasks > 0) {
         static int per_sm = 0;   /* resident CTAs a SM (registers and the 32 KiB stage bound it) */
         if (!per_sm) {

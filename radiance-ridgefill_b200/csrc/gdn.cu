@@ -117,19 +117,6 @@ __device__ __forceinline__ uint8_t* slot_ptr(const GdnPlan& p, int64_t slot, int
     return p.slots + (slot * p.g.n_head_v + h) * (int64_t)kSlotBytes;
 }
 
-__device__ __forceinline__ void bar_sync(int id, int threads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
-/* Named barrier `id` over `threads` threads that also ORs `pred` across them: every thread gets the same answer. */
-__device__ __forceinline__ bool bar_any(int id, int threads, bool pred) {
-    uint32_t r;
-    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbarrier.red.or.pred q, %2, %3, p;\n\t"
-                 "selp.u32 %0, 1, 0, q;\n\t}\n"
-                 : "=r"(r) : "r"((uint32_t)pred), "r"(id), "r"(threads) : "memory");
-    return r != 0;
-}
-
 /* cp.async of 4 bytes (src_bytes 0: zero fill). */
 __device__ __forceinline__ void cp_async4(void* dst, const void* src, int src_bytes) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(rf::saddr(dst)), "l"(src), "r"(src_bytes) : "memory");
@@ -350,7 +337,7 @@ __device__ void prep_role(const CUtensorMap& kmap, const CUtensorMap& vmap, cons
                           const int bar) {
     const RidgeFillGdn& g = p.g;
     const int w = tid >> 5, l = tid & 31, gq = l >> 2, tq = l & 3;
-    auto sync = [&]() { bar_sync(bar, kPrepThreads); };
+    auto sync = [&]() { rf::bar_sync(bar, kPrepThreads); };
     const int n_seq = (int)g.n_seq;
     const int n_cached = n_seq < kSeqCache ? n_seq : kSeqCache;
     for (int i = tid; i <= n_cached; i += kPrepThreads) {
@@ -714,7 +701,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const GdnPl
     for (int64_t c = 0; c < chunks; ++c) {
         const int st = (int)(c % kStages), b = (int)(c & 1);
         if (tid == 0) s.ok_chain = rf::mbar_wait(&s.landed[st], (uint32_t)((c / kStages) & 1), &s.abort, rf::kErrGdnWait);
-        bar_sync(kBarChain, 128);
+        rf::bar_sync(kBarChain, 128);
         if (!(ok = s.ok_chain)) break;
         const Stage& sg = s.st[st];
         const uint32_t wtile = rf::saddr(&sg.w[0][0][0]), kttile = rf::saddr(&sg.kt[0][0][0]), utile = rf::saddr(&sg.u[0][0]);
@@ -754,7 +741,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) gdn_chain_kernel(const GdnPl
             *(float2*)&s.part[b][w][gq][8 * j + 2 * tq] = make_float2(pv[j][0], pv[j][1]);
             *(float2*)&s.part[b][w][gq + 8][8 * j + 2 * tq] = make_float2(pv[j][2], pv[j][3]);
         }
-        bar_sync(kBarPair0 + vh, 64);
+        rf::bar_sync(kBarPair0 + vh, 64);
         const float gamma_l = sg.gl[0];
         /* V' = U~ - (both halves of S W^T). */
 #pragma unroll
@@ -876,7 +863,7 @@ __device__ void chain_tc_role(const GdnPlan& p, TcSmem& s, int64_t first, int64_
     const int tid = threadIdx.x, w = tid >> 5, l = tid & 31;
     const int n = (int)g.n_seq;
     const int64_t n_chains = g.n_head_v * g.n_seq;
-    auto role_sync = [&]() { bar_sync(3, kTcThreads); };
+    auto role_sync = [&]() { rf::bar_sync(3, kTcThreads); };
     if (tid == 0) {
         for (int b = 0; b < kTcStages; ++b) {
             rf::mbar_init(&s.landed[b], 1);
@@ -1367,9 +1354,9 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
          * Within a group, warp lw = w & 3 is lane quarter lw of the tensor memory. */
         const int grp = w >> 2, lw = w & 3, gt = tid & 127;
         HdSmem::Work& wk = s.work[grp];
-        auto psync = [&]() { bar_sync(1 + grp, 128); };
+        auto psync = [&]() { rf::bar_sync(1 + grp, 128); };
         /* a barrier of the group's four warps that also tells all of them whether any thread's wait gave up */
-        auto failed = [&](bool ok) { return bar_any(1 + grp, 128, !ok || *abort); };
+        auto failed = [&](bool ok) { return rf::bar_any(1 + grp, 128, !ok || *abort); };
         /* W^T of chunk qq (this group's) from tensor memory into its parity's B tile of D1: thread = dk row 32 lw + l,
          * the 64 columns in two halves; true if a wait gave up */
         auto read_back_wt = [&](int64_t qq) -> bool {

@@ -1,5 +1,5 @@
-/* gemm_q.cu -- the int8 projector on B200: ridgefill_gemm_nt_q, ridgefill_gemm_nt_q_bias and the
- * activation quantiser ridgefill_quant_act_i8g.
+/* gemm_q.cu -- the int8 projector on B200: ridgefill_gemm_nt_q, ridgefill_gemm_nt_q_bias, the DeltaNet block's
+ * fused k|v in-projection ridgefill_gdn_in_proj and the activation quantiser ridgefill_quant_act_i8g.
  *
  * The reference forwards this GEMM to radiance libr4d's int8 gemm_nt_q (kernels/forward.cpp:53-57;
  * issue site arch/ridgefill_layer.h:73-80), whose source is not available; its schema
@@ -26,6 +26,14 @@
  *               selection (the optional rows operand, ridgefill_select's mask) each lane instead stores its
  *               own row's 64 columns straight to y when the row is selected, so the projection lands only
  *               in the approximated rows of the block input and no separate select pass reads it back
+ * The in-projection form (ridgefill_gdn_in_proj) runs the same pipeline over row tiles that overlap by three rows:
+ * a CTA projects rows [m_c - 3, m_c + 125), so each of its 125 output rows finds the three rows before it (the
+ * causal convolution's window) in the CTA's own tile. Its epilogue rounds the projection to bf16 into a row-major
+ * tile in shared memory (the staging space), writes each sequence's last three rows to `tail` (what the conv-state
+ * update reads), and then, a lane per 8 channels and a warp per 8 rows, computes conv_prep's arithmetic on them:
+ * the width-4 convolution (the rows before a sequence's start from its conv-state slot or zero), SiLU, the L2 norm
+ * of each k head (the same summation tree as conv_prep, so the bits agree), k and v to bf16 -- the projection's
+ * rows never go to HBM.
  * A K block is `group` columns: 128 for the projector folder's i8*bf16[1x128] encoding, K itself
  * for per-row / per-column scaling (one fold a tile, the int32 accumulation running over all of K).
  */
@@ -34,6 +42,8 @@
 #include "common.cuh"
 #include "mma.cuh"
 #include "sm100.cuh"
+
+#include <cuda_bf16.h>
 
 namespace {
 
@@ -48,7 +58,11 @@ constexpr int kThreads = 32 * (2 + kEpiWarps);
 constexpr int kOutBox = 32 * 64 * 2;                  /* one [32 rows][64 cols] bf16 store box */
 constexpr int kStageOut = kEpiWarps * kBoxes * kOutBox;        /* the epilogue warps' staging tiles */
 constexpr int kScaleSlots = kEpiWarps * 2 * kWarpCols * 4;     /* each epilogue warp's b_scale values of two K blocks */
-constexpr int kSmemBytes = kStages * kStageBytes + kStageOut + kScaleSlots + 1024 /* alignment slack */ + 256 /* barriers */;
+constexpr int kMetaBytes = 2 * BM * 4;                         /* the in-projection's per-row sequence start and slot */
+constexpr int kSmemBytes = kStages * kStageBytes + kStageOut + kScaleSlots + kMetaBytes + 1024 /* alignment slack */ +
+                           256 /* barriers */;
+constexpr int kConvRows = BM - 3;   /* the in-projection's output rows a CTA: its tile less the 3-row window */
+constexpr int kEpiBar = 1;          /* named barrier of the 16 epilogue warps */
 
 /* Instruction descriptor of the pair's M256 N256 product: D s32 (bits 4-5 = 2), A and B signed int8 (bits
  * 7-9, 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24. */
@@ -60,6 +74,7 @@ constexpr uint32_t kIdescBf16 = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)
 struct GemmPlan {
     RidgeFillGemmQ g;       /* the int8 form */
     RidgeFillGemmBias gb;   /* the bf16 form */
+    RidgeFillInProj c;      /* the in-projection form (g = c.gemm) */
     int n_tiles, tiles, folds, steps_per_fold;
 };
 
@@ -109,9 +124,243 @@ __device__ __forceinline__ void fold_block(uint32_t taddr, float (&acc)[kWarpCol
 }
 
 /* The kernel's forms: the bf16 GEMM, the int8 projector, the int8 projector writing out its int32 block sums
- * (the optional acc operand), and the int8 projector writing only the selected rows (the optional rows operand).
- * Separate instantiations keep each form's registers to itself. */
-enum GemmMode { kModeBf16 = 0, kModeI8 = 1, kModeI8Dump = 2, kModeI8Rows = 3, kModeCount = 4 };
+ * (the optional acc operand), the int8 projector writing only the selected rows (the optional rows operand), and
+ * the DeltaNet in-projection with the convolution in its epilogue. Separate instantiations keep each form's
+ * registers to itself. */
+enum GemmMode { kModeBf16 = 0, kModeI8 = 1, kModeI8Dump = 2, kModeI8Rows = 3, kModeI8Conv = 4, kModeCount = 5 };
+
+/* The first row a CTA projects: 256-row pair tiles, or for the in-projection 250-row pair tiles each CTA of which
+ * starts three rows before its 125 output rows (a negative start reads zeros). */
+template <int kMode>
+__device__ __forceinline__ int64_t tile_row0(int tile, int n_tiles, uint32_t rank) {
+    if constexpr (kMode == kModeI8Conv) return (int64_t)(tile / n_tiles) * (2 * kConvRows) + (int64_t)rank * kConvRows - 3;
+    else return (int64_t)(tile / n_tiles) * BM2 + (int64_t)rank * BM;
+}
+
+/* The 16-byte chunk j (of 32) of row t in the in-projection's row-major [128][256] bf16 tile: XOR-swizzled by the
+ * row's low three bits, so a warp's lanes writing one chunk of 32 rows, or reading 16 chunks of a row, meet no
+ * bank conflict. */
+__device__ __forceinline__ int conv_chunk(int t, int j) { return t * 512 + ((j ^ (t & 7)) << 4); }
+
+/* The K blocks of one tile folded into a lane's f32 sums. The scales of block f + 1 are fetched while block f waits
+ * and folds: a_scale into a register, this warp's b_scale values (four a lane) by asynchronous copy into the warp's
+ * other shared-memory slot (columns past N read as zero). Each accumulator buffer goes back to the MMA warp once
+ * read. False when a wait gave up. */
+template <bool kDump>
+__device__ __forceinline__ bool fold_tile(const GemmPlan& p, float (&acc)[kWarpCols], float* slots, uint32_t lane_addr, int lane,
+                                          int64_t m, int64_t n0, bool row_live, uint32_t& fold, volatile int* abort,
+                                          uint64_t* acc_full, uint64_t* acc_empty) {
+    const RidgeFillGemmQ& g = p.g;
+    const bool copies = lane < kWarpCols / 4;
+    const uint32_t col_bytes = copies && n0 + lane * 4 < g.N ? 16u : 0u;   /* N is a multiple of 16 */
+#pragma unroll
+    for (int i = 0; i < kWarpCols; ++i) acc[i] = 0.0f;
+    __syncwarp();   /* the previous tile's reads of the slots are done */
+    if (copies) rf::cp_async16_zfill(slots + lane * 4, g.b_scale + (col_bytes ? n0 + lane * 4 : 0), col_bytes);
+    float sa_next = row_live ? g.a_scale[m * g.ldas] : 0.0f;
+    for (int f = 0; f < p.folds; ++f, ++fold) {
+        const uint32_t buf = fold & 1, use = (fold >> 1) & 1;
+        const float* sb = slots + (f & 1) * kWarpCols;
+        rf::cp_async_wait_all();
+        __syncwarp();   /* block f's scales are in, and every lane is done with block f - 1's slot */
+        const float sa = sa_next;
+        if (f + 1 < p.folds) {
+            if (copies)
+                rf::cp_async16_zfill(slots + ((f + 1) & 1) * kWarpCols + lane * 4,
+                                     g.b_scale + (col_bytes ? (int64_t)(f + 1) * g.N + n0 + lane * 4 : 0), col_bytes);
+            sa_next = row_live ? g.a_scale[m * g.ldas + f + 1] : 0.0f;
+        }
+        if (!rf::mbar_wait(&acc_full[buf], use, abort, rf::kErrGemmWaitEpilogue)) return false;
+        rf::tc_fence_after();
+        fold_block<kDump>(lane_addr + buf * BN, acc, sb, sa, g, m, n0, row_live, f, p.folds);
+        rf::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) rf::mbar_arrive_cluster_relaxed(rf::map_rank(rf::smem_addr(&acc_empty[buf]), 0));
+    }
+    return true;
+}
+
+/* Two f32 as a bf16 pair, rounded to nearest even by the hardware conversion: conv_prep's output rounding. */
+__device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *(const uint32_t*)&v;
+}
+
+__device__ __forceinline__ void unpack8(uint4 v, float (&f)[8]) {
+    const uint32_t w[4] = { v.x, v.y, v.z, v.w };
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        f[2 * e] = __uint_as_float(w[e] << 16);
+        f[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+    }
+}
+
+/* The in-projection's convolution over one CTA tile (rows_tile: the projection's rows m0 .. m0 + 127 as bf16; meta:
+ * each row's sequence start, -1 outside every sequence, and its history slot, -1 for none). Warp ew takes output
+ * rows 3 + 8 ew .. 10 + 8 ew of the tile, lane l channels nt0 + 8 l .. nt0 + 8 l + 7 (a half-warp is one 128-channel
+ * head); the window's three earlier rows ride in registers from row to row. Per channel, as conv_prep:
+ * u = bias; u = fma(w_j, x[r - 3 + j], u) for j = 0..3; y = silu(u); for k heads y *= rsqrt(ss + 1e-6) with ss summed
+ * in conv_prep's order (each 4-channel run by fma, then the head's butterfly), so the bits agree. */
+__device__ __forceinline__ void conv_rows(const GemmPlan& p, const uint8_t* rows_tile, const int32_t* meta_s0,
+                                          const int32_t* meta_slot, int64_t m0, int64_t nt0, int ew, int lane) {
+    const RidgeFillInProj& c = p.c;
+    const int64_t M = p.g.M, N = p.g.N;
+    const int64_t cn = nt0 + lane * 8;
+    const bool col_live = cn < N, is_k = cn < c.n_k, norm_tile = nt0 < c.n_k;
+    /* the taps as bf16 pairs: wv[i] holds channels 2 i and 2 i + 1, four taps each (words 0-1 and 2-3) */
+    uint4 wv[4] = {};
+    uint4 bv = {};
+    if (col_live) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) wv[i] = __ldg((const uint4*)(c.w + cn * 4) + i);
+        if (c.bias) bv = __ldg((const uint4*)(c.bias + cn));
+    }
+    uint16_t* out;
+    int64_t out_row;
+    if (is_k) {
+        out = c.k + (cn >> 7) * c.k_head + (cn & 127);
+        out_row = c.k_row;
+    } else {
+        const int64_t vc = cn - c.n_k;
+        out = c.v + (vc >> 7) * c.v_head + (vc & 127);
+        out_row = c.v_row;
+    }
+    const int tb = 3 + ew * 8, te = min(tb + 8, BM);
+    uint4 win[3] = {};   /* rows r - 3, r - 2, r - 1 */
+    int64_t win_r = -1;
+    int win_s0 = -1;
+    for (int t = tb; t < te; ++t) {
+        const int64_t r = m0 + t;
+        if (r >= M) break;
+        const int s0 = meta_s0[t];
+        if (s0 < 0) continue;   /* outside every sequence: left untouched */
+        if (win_r != r - 1 || win_s0 != s0) {
+            const int slot = meta_slot[t];
+#pragma unroll
+            for (int j = 1; j <= 3; ++j) {
+                const int64_t rr = r - j;
+                uint4 x = make_uint4(0u, 0u, 0u, 0u);
+                if (rr >= s0) x = *(const uint4*)(rows_tile + conv_chunk(t - j, lane));
+                else if (slot >= 0 && col_live) x = *(const uint4*)(c.state + slot * c.st_slot + (3 - (s0 - rr)) * c.st_row + cn);
+                win[3 - j] = x;
+            }
+        }
+        const uint4 cur = *(const uint4*)(rows_tile + conv_chunk(t, lane));
+        float x0[8], x1[8], x2[8], x3[8], y[8], bs[8];
+        unpack8(win[0], x0);
+        unpack8(win[1], x1);
+        unpack8(win[2], x2);
+        unpack8(cur, x3);
+        unpack8(bv, bs);
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+            float w0[4], w1[4];   /* channel e's and e + 1's taps */
+            {
+                float f[8];
+                unpack8(wv[e >> 1], f);
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    w0[t] = f[t];
+                    w1[t] = f[4 + t];
+                }
+            }
+            float u0 = bs[e], u1 = bs[e + 1];
+            rf::fma2_rn(u0, u1, w0[0], w1[0], x0[e], x0[e + 1]);
+            rf::fma2_rn(u0, u1, w0[1], w1[1], x1[e], x1[e + 1]);
+            rf::fma2_rn(u0, u1, w0[2], w1[2], x2[e], x2[e + 1]);
+            rf::fma2_rn(u0, u1, w0[3], w1[3], x3[e], x3[e + 1]);
+            y[e] = rf::silu(u0);
+            y[e + 1] = rf::silu(u1);
+        }
+        if (norm_tile) {   /* the tile holds a k head: every lane takes part in the butterflies */
+            float se = 0.0f, so = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                se = fmaf(y[e], y[e], se);
+                so = fmaf(y[4 + e], y[4 + e], so);
+            }
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) {
+                se += __shfl_xor_sync(0xffffffffu, se, o);
+                so += __shfl_xor_sync(0xffffffffu, so, o);
+            }
+            if (is_k) {
+                const float inv = rsqrtf((se + so) + 1e-6f);
+#pragma unroll
+                for (int e = 0; e < 8; e += 2) rf::mul2_rn(y[e], y[e + 1], y[e], y[e + 1], inv, inv);
+            }
+        }
+        if (col_live) *(uint4*)(out + r * out_row) = make_uint4(bf16x2(y[0], y[1]), bf16x2(y[2], y[3]), bf16x2(y[4], y[5]), bf16x2(y[6], y[7]));
+        win[0] = win[1];
+        win[1] = win[2];
+        win[2] = cur;
+        win_r = r;
+        win_s0 = s0;
+    }
+}
+
+/* The in-projection's epilogue warps. Per tile (one K block: group = K): the lane's row waits for its sums and looks up
+ * its sequence; the epilogue barrier, which also agrees on a failed wait (every warp then leaves together), ensures
+ * every warp is done with the previous tile's rows; the sums are folded eight columns at a time straight from
+ * tensor memory and rounded to bf16 into the row tile (each sequence's last three rows also to `tail`), the
+ * accumulator goes back to the MMA warp; a second barrier; the convolution. False when a wait gave up. */
+__device__ __forceinline__ bool conv_epilogue(const GemmPlan& p, uint8_t* rows_tile, int32_t* meta, uint32_t lane_addr, int warp,
+                                              int lane, int pair, int pairs, uint32_t rank, volatile int* abort,
+                                              uint64_t* acc_full, uint64_t* acc_empty) {
+    const RidgeFillGemmQ& g = p.g;
+    const RidgeFillInProj& c = p.c;
+    const int ew = warp - 2, slice = ew >> 2, row = (warp & 3) * 32 + lane;
+    int32_t* meta_s0 = meta;
+    int32_t* meta_slot = meta + BM;
+    uint32_t fold = 0;
+    for (int tile = pair; tile < p.tiles; tile += pairs, ++fold) {
+        const int64_t m0 = tile_row0<kModeI8Conv>(tile, p.n_tiles, rank), nt0 = (int64_t)(tile % p.n_tiles) * BN;
+        const int64_t m = m0 + row, n0 = nt0 + slice * kWarpCols;
+        const bool row_live = m >= 0 && m < g.M;
+        const float sa = row_live ? g.a_scale[m * g.ldas] : 0.0f;
+        const uint32_t buf = fold & 1, use = (fold >> 1) & 1;
+        const bool ok = rf::mbar_wait(&acc_full[buf], use, abort, rf::kErrGemmWaitEpilogue);
+        /* the row's sequence and the conv-state slot of its history */
+        int64_t s0 = -1, e0 = -1;
+        const int seq = ok && row_live ? rf::find_seq(c.cu, c.n_seq, g.M, m, &s0, &e0) : -1;
+        int32_t slot = -1;
+        if (seq >= 0 && c.ctx && c.ctx[seq] > 0) {
+            const int64_t sl = c.idx[seq * c.idx_pitch];
+            if (sl >= 0 && sl < c.n_states) slot = (int32_t)sl;
+        }
+        if (rf::bar_any(kEpiBar, 32 * kEpiWarps, !ok)) return false;
+        rf::tc_fence_after();
+        const bool tail_row = row >= 3 && seq >= 0 && m >= e0 - 3;
+#pragma unroll 2
+        for (int v = 0; v < kWarpCols / 8; ++v) {
+            const int64_t n = n0 + v * 8;
+            uint32_t r[8];
+            rf::tmem_ld8(lane_addr + buf * BN + v * 8, r);
+            float a8[8] = {}, sb[8] = {};
+            if (n < g.N) {   /* N is a multiple of 128 */
+                const float4 s0v = __ldg((const float4*)(g.b_scale + n)), s1v = __ldg((const float4*)(g.b_scale + n + 4));
+                sb[0] = s0v.x; sb[1] = s0v.y; sb[2] = s0v.z; sb[3] = s0v.w;
+                sb[4] = s1v.x; sb[5] = s1v.y; sb[6] = s1v.z; sb[7] = s1v.w;
+            }
+            rf::tmem_ld_wait();
+            fold8(r, a8, sb, sa);
+            const uint4 q = make_uint4(rf::pack_bf16(a8[0], a8[1]), rf::pack_bf16(a8[2], a8[3]), rf::pack_bf16(a8[4], a8[5]),
+                                       rf::pack_bf16(a8[6], a8[7]));
+            *(uint4*)(rows_tile + conv_chunk(row, slice * (kWarpCols / 8) + v)) = q;
+            if (tail_row && n < g.N) *(uint4*)(g.y + m * g.ldy + n) = q;
+        }
+        rf::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) rf::mbar_arrive_cluster_relaxed(rf::map_rank(rf::smem_addr(&acc_empty[buf]), 0));
+        if (slice == 0) {
+            meta_s0[row] = seq >= 0 ? (int32_t)s0 : -1;
+            meta_slot[row] = slot;
+        }
+        rf::bar_sync(kEpiBar, 32 * kEpiWarps);
+        conv_rows(p, rows_tile, meta_s0, meta_slot, m0, nt0, ew, lane);
+    }
+    return true;
+}
 
 template <int kMode>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -124,7 +373,8 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
     uint8_t* tile_b = smem + kStages * kABytes;
     uint8_t* stage_out = smem + kStages * kStageBytes;   /* 1024-byte aligned: kStageBytes is */
     float* scale_slots = (float*)(stage_out + kStageOut);
-    uint64_t* full = (uint64_t*)(stage_out + kStageOut + kScaleSlots);
+    int32_t* meta = (int32_t*)(stage_out + kStageOut + kScaleSlots);
+    uint64_t* full = (uint64_t*)(stage_out + kStageOut + kScaleSlots + kMetaBytes);
     uint64_t* empty = full + kStages;
     uint64_t* acc_full = empty + kStages;
     uint64_t* acc_empty = acc_full + 2;
@@ -163,7 +413,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
             int64_t issued = 0;
             const int steps = p.folds * p.steps_per_fold;
             for (int tile = pair; tile < p.tiles && !*abort; tile += pairs) {
-                const int m0 = (tile / p.n_tiles) * BM2 + (int)rank * BM, n0 = (tile % p.n_tiles) * BN + (int)rank * (BN / 2);
+                const int m0 = (int)tile_row0<kMode>(tile, p.n_tiles, rank), n0 = (tile % p.n_tiles) * BN + (int)rank * (BN / 2);
                 for (int ks = 0; ks < steps; ++ks) {
                     if (!rf::mbar_wait(&empty[stage], phase ^ 1, abort, rf::kErrGemmWaitProducer)) break;
                     if (rank == 0) rf::mbar_arrive_expect_tx(&full[stage], 2 * kStageBytes);
@@ -312,41 +562,16 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
                 }
             }
         }
-        for (int tile = pair; tile < p.tiles && ok && !kBf16; tile += pairs) {
+        if constexpr (kMode == kModeI8Conv)
+            ok = conv_epilogue(p, stage_out, meta, lane_addr, warp, lane, pair, pairs, rank, abort, acc_full, acc_empty);
+        for (int tile = pair; tile < p.tiles && ok && !kBf16 && kMode != kModeI8Conv; tile += pairs) {
             const int64_t m = (int64_t)(tile / p.n_tiles) * BM2 + rank * BM + row;
             const int64_t n0 = (int64_t)(tile % p.n_tiles) * BN + slice * kWarpCols;
-            const bool row_live = m < g.M, copies = lane < kWarpCols / 4;
-            const uint32_t col_bytes = copies && n0 + lane * 4 < g.N ? 16u : 0u;   /* N is a multiple of 16 */
+            const bool row_live = m < g.M;
             float acc[kWarpCols];
-#pragma unroll
-            for (int i = 0; i < kWarpCols; ++i) acc[i] = 0.0f;
-            /* The scales of block f + 1 are fetched while block f waits and folds: a_scale into a register, this
-             * warp's b_scale values (four a lane) by asynchronous copy into the warp's other shared-memory slot
-             * (columns past N read as zero). */
-            float* slots = scale_slots + (warp - 2) * 2 * kWarpCols;
-            __syncwarp();   /* the previous tile's reads of the slots are done */
-            if (copies) rf::cp_async16_zfill(slots + lane * 4, g.b_scale + (col_bytes ? n0 + lane * 4 : 0), col_bytes);
-            float sa_next = row_live ? g.a_scale[m * g.ldas] : 0.0f;
-            for (int f = 0; f < p.folds; ++f, ++fold) {
-                const uint32_t buf = fold & 1, use = (fold >> 1) & 1;
-                const float* sb = slots + (f & 1) * kWarpCols;
-                rf::cp_async_wait_all();
-                __syncwarp();   /* block f's scales are in, and every lane is done with block f - 1's slot */
-                const float sa = sa_next;
-                if (f + 1 < p.folds) {
-                    if (copies)
-                        rf::cp_async16_zfill(slots + ((f + 1) & 1) * kWarpCols + lane * 4,
-                                             g.b_scale + (col_bytes ? (int64_t)(f + 1) * g.N + n0 + lane * 4 : 0), col_bytes);
-                    sa_next = row_live ? g.a_scale[m * g.ldas + f + 1] : 0.0f;
-                }
-                if (!(ok = rf::mbar_wait(&acc_full[buf], use, abort, rf::kErrGemmWaitEpilogue))) break;
-                rf::tc_fence_after();
-                fold_block<kMode == kModeI8Dump>(lane_addr + buf * BN, acc, sb, sa, g, m, n0, row_live, f, p.folds);
-                rf::tc_fence_before();
-                __syncwarp();
-                if (lane == 0) rf::mbar_arrive_cluster_relaxed(rf::map_rank(rf::smem_addr(&acc_empty[buf]), 0));
-            }
-            if (!ok) break;
+            if (!(ok = fold_tile<kMode == kModeI8Dump>(p, acc, scale_slots + (warp - 2) * 2 * kWarpCols, lane_addr, lane, m, n0,
+                                                         row_live, fold, abort, acc_full, acc_empty)))
+                break;
             /* bf16 (and the bias) into this warp's staging tiles, once the previous tile's stores have read them; or,
              * with a row selection, straight from the lanes into the selected rows of y (a lane is one row). */
             uint8_t* stg = stage_out + (warp - 2) * kBoxes * kOutBox;
@@ -710,6 +935,28 @@ int launch_gemm(const RidgeFillGemmQ& g, cudaStream_t stream) {
     return launch_pairs<kModeI8>(map_a, map_b, map_y, p, stream);
 }
 
+/* The in-projection: 250-row pair tiles (each CTA's 128 rows start 3 before its 125 output rows), one fold a
+ * tile (per-row and per-column scaling). */
+int launch_in_proj(const RidgeFillInProj& c, cudaStream_t stream) {
+    const RidgeFillGemmQ& g = c.gemm;
+    if (g.M == 0) return RAD_OK;
+    if (g.M > 0x7fffffffLL || g.N > 0x7fffffffLL || g.K > 0x7fffffffLL) return RAD_E_SHAPE;
+    CUtensorMap map_a, map_b, map_y;
+    if (!int8_tile_map(&map_a, g.a, g.M, g.K, g.lda, BM) || !int8_tile_map(&map_b, g.b, g.N, g.K, g.ldb, BN / 2) ||
+        !bf16_store_map(&map_y, g.y, g.M, g.N, g.ldy))
+        return RAD_E_DEVICE;
+    GemmPlan p{};
+    p.g = g;
+    p.c = c;
+    p.n_tiles = (int)((g.N + BN - 1) / BN);
+    const int64_t tiles = ((g.M + 2 * kConvRows - 1) / (2 * kConvRows)) * p.n_tiles;
+    if (tiles > 0x7fffffffLL) return RAD_E_SHAPE;
+    p.tiles = (int)tiles;
+    p.folds = 1;
+    p.steps_per_fold = (int)(g.K / BK);
+    return launch_pairs<kModeI8Conv>(map_a, map_b, map_y, p, stream);
+}
+
 /* A [rows, cols] bf16 matrix with row pitch `pitch` elements, read in [box_rows, 64] tiles (128 bytes of K)
  * with 128-byte swizzle; rows past the end read as zero. */
 bool bf16_tile_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int64_t pitch, uint32_t box_rows) {
@@ -754,6 +1001,12 @@ extern "C" int ridgefill_gemm_nt_q_bias_device(const RadArgs* a, RadStream s) {
     RidgeFillGemmQ g;
     const int rc = ridgefill_gemm_q_parse(a, 1, &g);
     return rc != RAD_OK ? rc : launch_gemm(g, rf::as_stream(s));
+}
+
+extern "C" int ridgefill_gdn_in_proj_device(const RadArgs* a, RadStream s) {
+    RidgeFillInProj c;
+    const int rc = ridgefill_in_proj_parse(a, &c);
+    return rc != RAD_OK ? rc : launch_in_proj(c, rf::as_stream(s));
 }
 
 extern "C" int ridgefill_gemm_nt_bias_device(const RadArgs* a, RadStream s) {

@@ -652,6 +652,100 @@ extern "C" int ridgefill_conv_prep_parse(const RadArgs* a, RidgeFillConvPrep* g)
     g->dk = dk;
     g->dv = dv;
     g->width = width;
+    long long columns = 1;   /* optional: 0 computes only the gates and the conv state (ridgefill_gdn_in_proj wrote k, v) */
+    if (rad_args_geti(a, "columns", &columns) && columns != 0 && columns != 1) return RAD_E_INVAL;
+    g->columns = (int)columns;
+    return RAD_OK;
+}
+
+/* ridgefill_gdn_in_proj: a i8 [T, K] (rows 16-byte aligned), a_scale f32 [T, 1], b i8 [N, K] the k|v rows of the
+ * in-projection, b_scale f32 [1, N] (per-column scaling: group = K), w bf16 [N, 4] dense, bias bf16 [N] or absent,
+ * conv state bf16 [slots, 3, N] (any slot and row pitch, last stride 1: the k|v channels of the pool), cu_seqlens
+ * i32 [n_seq + 1], conv_idx i32 [n_seq] or [n_seq, >= 1], ctx_lens i32 [n_seq] or absent, k bf16 [T, Hk, 128],
+ * v bf16 [T, Hv, 128] (rows and heads 16-byte aligned), tail bf16 [T, N] (rows 16-byte aligned). N = (Hk + Hv) 128. */
+extern "C" int ridgefill_in_proj_parse(const RadArgs* a, RidgeFillInProj* g) {
+    *g = RidgeFillInProj{};
+    const RadTensor* A = rad_arg_in(a, IP_A);
+    const RadTensor* AS = rad_arg_in(a, IP_A_SCALE);
+    const RadTensor* B = rad_arg_in(a, IP_B);
+    const RadTensor* BS = rad_arg_in(a, IP_B_SCALE);
+    const RadTensor* W = rad_arg_in(a, IP_W);
+    const RadTensor* B0 = rad_arg_in(a, IP_BIAS);
+    const RadTensor* ST = rad_arg_in(a, IP_STATE);
+    const RadTensor* CU = rad_arg_in(a, IP_CU);
+    const RadTensor* I = rad_arg_in(a, IP_IDX);
+    const RadTensor* CX = rad_arg_in(a, IP_CTX);
+    const RadTensor* K = rad_arg_in(a, IP_K);
+    const RadTensor* V = rad_arg_in(a, IP_V);
+    const RadTensor* TL = rad_arg_in(a, IP_TAIL);
+    long long T = 0, N = 0, Kd = 0, hk = 0, hv = 0, group = 0;
+    const char* dt = rad_args_gets(a, "dtype");
+    if (!A || !AS || !B || !BS || !W || !ST || !CU || !I || !K || !V || !TL || !dt || !rad_args_geti(a, "M", &T) ||
+        !rad_args_geti(a, "N", &N) || !rad_args_geti(a, "K", &Kd) || !rad_args_geti(a, "n_head_k", &hk) ||
+        !rad_args_geti(a, "n_head_v", &hv) || !rad_args_geti(a, "group", &group))
+        return RAD_E_INVAL;
+    if (std::strcmp(dt, "i8a8") != 0) return RAD_E_UNSUPPORTED;
+    if (group != Kd) return RAD_E_UNSUPPORTED;   /* per-row activation, per-column weight scaling */
+    if (A->dtype != RAD_I8 || AS->dtype != RAD_F32 || B->dtype != RAD_I8 || BS->dtype != RAD_F32 || W->dtype != RAD_BF16 ||
+        (B0 && B0->dtype != RAD_BF16) || ST->dtype != RAD_BF16 || CU->dtype != RAD_I32 || I->dtype != RAD_I32 ||
+        (CX && CX->dtype != RAD_I32) || K->dtype != RAD_BF16 || V->dtype != RAD_BF16 || TL->dtype != RAD_BF16)
+        return RAD_E_DTYPE;
+    if (T < 0 || hk <= 0 || hv <= 0 || N != (hk + hv) * 128 || Kd <= 0 || Kd % 128 != 0) return RAD_E_SHAPE;
+    if (A->rank != 2 || A->shape[0] != T || A->shape[1] != Kd || B->rank != 2 || B->shape[0] != N || B->shape[1] != Kd ||
+        rad_tensor_numel(AS) != T || rad_tensor_numel(BS) != N || W->rank != 2 || W->shape[0] != N || W->shape[1] != 4 ||
+        (B0 && rad_tensor_numel(B0) != N) || ST->rank != 3 || ST->shape[1] != 3 || ST->shape[2] != N || TL->rank != 2 ||
+        TL->shape[0] != T || TL->shape[1] != N)
+        return RAD_E_SHAPE;
+    if (CU->rank != 1 || CU->shape[0] < 1 || CU->stride[0] != 1) return RAD_E_SHAPE;
+    const int64_t n_seq = CU->shape[0] - 1;
+    if (I->rank == 1 ? (I->shape[0] < n_seq || I->stride[0] != 1) : (I->rank != 2 || I->shape[0] < n_seq || I->shape[1] < 1))
+        return RAD_E_SHAPE;
+    if (CX && (CX->rank != 1 || CX->shape[0] < n_seq || CX->stride[0] != 1)) return RAD_E_SHAPE;
+    if (K->rank != 3 || K->shape[0] != T || K->shape[1] != hk || K->shape[2] != 128 || K->stride[2] != 1 ||
+        V->rank != 3 || V->shape[0] != T || V->shape[1] != hv || V->shape[2] != 128 || V->stride[2] != 1)
+        return RAD_E_SHAPE;
+    if (A->stride[1] != 1 || B->stride[1] != 1 || !packed(AS) || !packed(BS) || !packed(W) || (B0 && !packed(B0)) ||
+        ST->stride[2] != 1 || TL->stride[1] != 1)
+        return RAD_E_STRIDE;
+    /* TMA reads of a and b (16-byte bases and pitches); 16-byte loads and stores of b_scale, taps, state, k, v, tail */
+    if (((uintptr_t)A->data | (uintptr_t)B->data | (uintptr_t)W->data | (uintptr_t)ST->data | (uintptr_t)K->data |
+         (uintptr_t)V->data | (uintptr_t)TL->data | (uintptr_t)BS->data | (B0 ? (uintptr_t)B0->data : 0)) % 16 ||
+        A->stride[0] % 16 || B->stride[0] % 16 || (ST->stride[0] * 2) % 16 || (ST->stride[1] * 2) % 16 ||
+        (K->stride[0] * 2) % 16 || (K->stride[1] * 2) % 16 || (V->stride[0] * 2) % 16 || (V->stride[1] * 2) % 16 ||
+        (TL->stride[0] * 2) % 16)
+        return RAD_E_STRIDE;
+    RidgeFillGemmQ& q = g->gemm;
+    q.a = (const int8_t*)A->data;
+    q.lda = A->stride[0];
+    q.a_scale = (const float*)AS->data;
+    q.ldas = 1;
+    q.b = (const int8_t*)B->data;
+    q.ldb = B->stride[0];
+    q.b_scale = (const float*)BS->data;
+    q.y = (uint16_t*)TL->data;
+    q.ldy = TL->stride[0];
+    q.M = T;
+    q.N = N;
+    q.K = Kd;
+    q.group = Kd;
+    g->w = (const uint16_t*)W->data;
+    g->bias = B0 ? (const uint16_t*)B0->data : nullptr;
+    g->state = (const uint16_t*)ST->data;
+    g->st_slot = ST->stride[0];
+    g->st_row = ST->stride[1];
+    g->n_states = ST->shape[0];
+    g->cu = (const int32_t*)CU->data;
+    g->n_seq = n_seq;
+    g->idx = (const int32_t*)I->data;
+    g->idx_pitch = I->rank == 1 ? 1 : I->stride[0];
+    g->ctx = CX ? (const int32_t*)CX->data : nullptr;
+    g->k = (uint16_t*)K->data;
+    g->k_row = K->stride[0];
+    g->k_head = K->stride[1];
+    g->v = (uint16_t*)V->data;
+    g->v_row = V->stride[0];
+    g->v_head = V->stride[1];
+    g->n_k = hk * 128;
     return RAD_OK;
 }
 

@@ -156,6 +156,12 @@ const RadKernelInfo kRows[] = {
                "copies into shared memory; a second kernel updates the conv state in place", "head dims 128, conv width 4",
                "bf16 x / w / state / a / b / q / k / v, f32 A_log / dt_bias / g / beta", nullptr, 0,
                ridgefill_gdn_conv_prep_device, nullptr, shape_conv_prep, nullptr, nullptr, nullptr),
+    DEVICE_ROW("ridgefill_gdn_in_proj_sm100", "ridgefill_gdn_in_proj",
+               "the int8 projector's 2-CTA tcgen05 pipeline over 250-row pair tiles (each CTA's tile starts 3 rows early: "
+               "the convolution's window); the epilogue rounds the rows into shared memory and runs the convolution, "
+               "SiLU and k norm there, lane per 8 channels", "head dims 128, conv width 4, K a multiple of 128, group = K",
+               "i8 a / b, f32 a_scale / b_scale, bf16 w / bias / state / k / v / tail", nullptr, 0,
+               ridgefill_gdn_in_proj_device, nullptr, shape_in_proj, nullptr, nullptr, nullptr),
     DEVICE_ROW("ridgefill_attn_kv_fill_sm100", "ridgefill_attn_kv_fill",
                "warp per row: both heads' k and v rows in flight, k_norm by a warp butterfly, the row's rotary angles "
                "one a lane (f64), rotation and the paged stores in the same pass", "head_dim 256, rope_dim a multiple of 16",
@@ -172,7 +178,7 @@ const RadPluginInfo kInfo = {
     "RidgeFill prefill ops on B200 (sm_100a): ridgefill_mask, ridgefill_select, ridgefill_drop_rows, "
     "ridgefill_rho_update, ridgefill_state_correct, ridgefill_state_read, ridgefill_hazard, the int8 projector "
     "ridgefill_gemm_nt_q (+ fused bias), its activation quantiser, the bf16 ridgefill_gemm_nt_bias, the Gated DeltaNet "
-    "chunk fill and its input preparation (ridgefill_gdn_conv_prep), and the attention block's K/V cache write "
+    "chunk fill, its input preparation (ridgefill_gdn_conv_prep) and fused k|v in-projection (ridgefill_gdn_in_proj), and the attention block's K/V cache write "
     "(ridgefill_attn_kv_fill). Device rows only.",
     RIDGEFILL_BUILD_TARGET
 };

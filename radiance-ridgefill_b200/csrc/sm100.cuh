@@ -284,6 +284,30 @@ __device__ __forceinline__ void fma2_rn(float& a0, float& a1, float x0, float x1
         " fma.rn.f32x2 a, x, y, a;\n mov.b64 {%0, %1}, a;\n}"
         : "+f"(a0), "+f"(a1) : "f"(x0), "f"(x1), "f"(y0), "f"(y1));
 }
+/* Named barrier `id` over `threads` threads (a multiple of 32). */
+__device__ __forceinline__ void bar_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+/* Named barrier `id` over `threads` threads that also ORs `pred` across them: every thread gets the same answer. */
+__device__ __forceinline__ bool bar_any(int id, int threads, bool pred) {
+    uint32_t r;
+    asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbarrier.red.or.pred q, %2, %3, p;\n\t"
+                 "selp.u32 %0, 1, 0, q;\n\t}\n"
+                 : "=r"(r) : "r"((uint32_t)pred), "r"(id), "r"(threads) : "memory");
+    return r != 0;
+}
+
+/* SiLU u / (1 + e^-u) as u times the approximate reciprocal (1 ulp) of the denominator, with the fast exp: well
+ * inside bf16's rounding. The reciprocal is the non-flushing form, so a denominator above 2^126 (u below about
+ * -87.3, where the value is about u e^u, under 1e-36 in magnitude) still gives the tiny value the f32 rule gives,
+ * not 0; an infinite one (u below about -88.7) gives -0, as the division does. */
+__device__ __forceinline__ float silu(float u) {
+    float r;
+    asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(1.0f + __expf(-u)));
+    return u * r;
+}
+
 __device__ __forceinline__ void mul2_rn(float& d0, float& d1, float x0, float x1, float y0, float y1) {
     asm("{\n .reg .b64 d, x, y;\n mov.b64 x, {%2, %3};\n mov.b64 y, {%4, %5};\n mul.rn.f32x2 d, x, y;\n"
         " mov.b64 {%0, %1}, d;\n}"

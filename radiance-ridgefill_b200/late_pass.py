@@ -314,7 +314,7 @@ class LatePass:
     KERNELS = {"ridgefill_mask": 1, "ridgefill_quant_act_i8g": 1, "ridgefill_gemm_nt_q_bias": 1, "ridgefill_select": 1,
                "ridgefill_gemm_nt_bias": 1, "ridgefill_gdn_conv_prep": 2, "ridgefill_attn_kv_fill": 1,
                "ridgefill_state_correct": 1, "ridgefill_gdn_fill": 2, "ridgefill_rho_update": 1, "ridgefill_hazard": 1,
-               "team_barrier": 1, "gather_columns": 1, "team_wait": 1}
+               "ridgefill_gdn_in_proj": 1, "team_barrier": 1, "gather_columns": 1, "team_wait": 1}
 
     def __init__(self, shape: LateShape, device: str = "cuda", seed: int = 0, inputs: dict | None = None,
                  team: Team | None = None):
@@ -331,6 +331,8 @@ class LatePass:
         T, d, G, D = s.T, s.d, s.n_gdn, s.head
         grp = s.group or d
         self.grp = grp
+        # the DeltaNet k|v projection with conv_prep's arithmetic in its epilogue (per-row scales, 128-wide heads)
+        self.fused_in = grp == d and s.head == 128 and d % 128 == 0
         (v0, v1), (k0, k1), (a0, a1), (c0, c1) = self.geo["v"], self.geo["k"], self.geo["a"], self.geo["cols"]
         self.hv_r, self.hk_r, self.hkv_r, self.cols = v1 - v0, k1 - k0, a1 - a0, c1 - c0
         hv, hk = self.hv_r, self.hk_r
@@ -442,9 +444,25 @@ class LatePass:
                 C, Cq = self.conv_dim_r, hk * D
                 block.append(quant(self.x[li], self.codes_x, self.scale_x, f"x {li}"))
                 # the mixed projection's k|v columns over every row; its q columns only over each sequence's last
-                # three rows, the conv state's (the state-only fill reads no q, so conv_prep is given none)
-                block.append(gemm_q(self.codes_x, self.scale_x, self.w_in_kv[gi], self.s_in_kv[gi], None,
-                                    _t(self.mixed, [T, C - Cq], [C, 1], offset_elems=Cq), C - Cq, f"in kv {li}"))
+                # three rows, the conv state's (the state-only fill reads no q, so conv_prep is given none). With
+                # per-row scales the k|v projection carries the convolution, SiLU and k norm in its epilogue
+                # (ridgefill_gdn_in_proj: k and v straight from the tiles, only the sequences' last three rows of
+                # the projection to `mixed`), and conv_prep is left the gates and the conv-state update.
+                kv = _t(self.mixed, [T, C - Cq], [C, 1], offset_elems=Cq)
+                if self.fused_in:
+                    cs = self.conv_state[gi]
+                    block.append(call("ridgefill_gdn_in_proj",
+                                      [_t(self.codes_x), _t(self.scale_x), _t(self.w_in_kv[gi]), _t(self.s_in_kv[gi]),
+                                       _t(x["w_conv"][gi], [C - Cq, 4], [4, 1], offset_elems=Cq * 4), A_,
+                                       _t(cs, [cs.shape[0], 3, C - Cq], list(cs.stride()), offset_elems=Cq),
+                                       _t(inp["cu_seqlens"]), _t(self.slots_all.view(-1)), _t(self.ctx),
+                                       _t(self.k, [T, hk, D], list(self.k.stride()), offset_elems=gi * hk * D),
+                                       _t(self.v, [T, hv, D], list(self.v.stride()), offset_elems=gi * hv * D), kv],
+                                      [P("M", T), P("N", C - Cq), P("K", d), P("n_head_k", hk), P("n_head_v", hv),
+                                       P("group", self.grp), S("dtype", "i8a8")], f"in kv {li}"))
+                else:
+                    block.append(gemm_q(self.codes_x, self.scale_x, self.w_in_kv[gi], self.s_in_kv[gi], None, kv, C - Cq,
+                                        f"in kv {li}"))
                 for a_, b_ in self.seq_bounds:
                     m0 = max(a_, b_ - 3)
                     if b_ <= m0:
@@ -468,7 +486,7 @@ class LatePass:
                                    _t(self.g, [T, hv], [G * hv, 1], offset_elems=gi * hv),
                                    _t(self.beta, [T, hv], [G * hv, 1], offset_elems=gi * hv)],
                                   [P("M", T), P("n_head_k", hk), P("n_head_v", hv), P("head_k", D), P("head_v", D),
-                                   P("conv", 4)], f"{li}"))
+                                   P("conv", 4), P("columns", 0 if self.fused_in else 1)], f"{li}"))
             elif kind == "A" and self.hkv_r:
                 Ha, Dh = self.hkv_r, s.head_attn
                 block.append(quant(self.x[li], self.codes_x, self.scale_x, f"x {li}"))
@@ -625,8 +643,12 @@ class LatePass:
             (A * 2 * self.hkv_r * s.head_attn if self.hkv_r else 0)
         q_tail_rows = sum(min(n, 3) for n in s.lengths)
         chunks = sum((n + 63) // 64 for n in s.lengths)
+        # the k|v projections of the DeltaNet layers, when the fused in-projection row issues them
+        in_proj_ops = 2 * T * d * G * (self.conv_dim_r - q_cols) if s.block_inputs and self.fused_in else 0
         return {
-            "int8_ops": 2 * T * d * n_int8_cols + 2 * q_tail_rows * d * G * q_cols,
+            # ridgefill_gemm_nt_q_bias launches (projectors, q tails, attention k|v; the DeltaNet k|v when not fused)
+            "int8_ops": 2 * T * d * n_int8_cols + 2 * q_tail_rows * d * G * q_cols - in_proj_ops,
+            "int8_ops_in_proj": in_proj_ops,
             # the batched fill, state-only form: read k, v, g, beta and the state, write the state
             "fill_bytes": 2 * T * G * hk * D + 2 * T * G * hv * D + 8 * T * G * hv + 2 * 4 * s.n_seq * G * hv * D * D,
             "fill_chunk_flops": chunks * G * hv * (6 * 64 * 64 * D + 4 * 64 * D * D + 64 ** 3 * 2 // 3),

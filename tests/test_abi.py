@@ -24,7 +24,7 @@ REFERENCE_SCHEMAS = [
     ("ridgefill_gemm_nt_q", ["M", "N", "K", "group", "dtype"], ["a", "a_scale", "b", "b_scale", "y", "a_sum", "b_ref"]),
 ]
 NEW_OPS = ["ridgefill_gemm_nt_q_bias", "ridgefill_quant_act_i8g", "ridgefill_gdn_fill", "ridgefill_gdn_conv_prep",
-           "ridgefill_attn_kv_fill"]
+           "ridgefill_gdn_in_proj", "ridgefill_attn_kv_fill"]
 DEVICE_OPS = [s[0] for s in REFERENCE_SCHEMAS] + NEW_OPS
 
 
@@ -47,6 +47,8 @@ def described_params(op):
                                 H.pint("head_v", 128), H.pint("chunk", 64)],
          "ridgefill_gdn_conv_prep": [H.pint("M", 70), H.pint("n_head_k", 1), H.pint("n_head_v", 2), H.pint("head_k", 128),
                                      H.pint("head_v", 128), H.pint("conv", 4)],
+         "ridgefill_gdn_in_proj": [H.pint("M", 70), H.pint("N", 384), H.pint("K", 256), H.pint("n_head_k", 1),
+                                   H.pint("n_head_v", 2), H.pint("group", 256), H.pstr("dtype", "i8a8")],
          "ridgefill_attn_kv_fill": [H.pint("M", 40), H.pint("n_head_kv", 2), H.pint("head_dim", 256), H.pint("rope_dim", 64),
                                     H.pf64("rope_theta", 1e7)]}
     return P[op]

@@ -15,10 +15,12 @@ PARSE = {"ridgefill_mask": "ridgefill_mask_parse", "ridgefill_quant_act_i8g": "r
          "ridgefill_select": "ridgefill_select_parse", "ridgefill_gemm_nt_bias": "ridgefill_gemm_bias_parse",
          "ridgefill_gdn_conv_prep": "ridgefill_conv_prep_parse", "ridgefill_attn_kv_fill": "ridgefill_attn_kv_parse",
          "ridgefill_state_correct": "ridgefill_correct_parse", "ridgefill_gdn_fill": "ridgefill_gdn_parse",
-         "ridgefill_rho_update": "ridgefill_rho_parse", "ridgefill_hazard": "ridgefill_hazard_parse"}
+         "ridgefill_rho_update": "ridgefill_rho_parse", "ridgefill_hazard": "ridgefill_hazard_parse",
+         "ridgefill_gdn_in_proj": "ridgefill_in_proj_parse"}
 
 SHAPES = [LP.config0(), LP.LateShape(T=256, d=256, hk=2, hv=4), LP.LateShape(T=300, d=256, layers="GA", hk=2, hv=4,
-                                                                              seqlens=(100, 80, 120))]
+                                                                              seqlens=(100, 80, 120)),
+          LP.LateShape(T=256, d=256, hk=2, hv=4, group=128)]
 
 
 def _parse(lib, op, tens, params):
@@ -36,15 +38,23 @@ def _parse(lib, op, tens, params):
     return rc
 
 
-@pytest.mark.parametrize("shape", SHAPES, ids=["config0", "all24_small", "ragged"])
+@pytest.mark.parametrize("shape", SHAPES, ids=["config0", "all24_small", "ragged", "grouped"])
 def test_every_launch_passes_its_operand_checks(shape, product_lib):
     p = LP.LatePass(shape, "cpu", seed=1)
     for op, _row, tens, params, tag in p.calls:
         assert _parse(product_lib, op, tens, params) == abi.OK, (op, tag)
     counts = p.op_counts()
     G, A, L = shape.n_gdn, shape.n_attn, len(shape.layers)
-    # per DeltaNet layer: the mixed projection's k|v columns, then its q columns over each sequence's last rows
-    assert counts["ridgefill_gemm_nt_q_bias"] == L + (G * (1 + shape.n_seq) if shape.block_inputs else 0) + A
+    # per DeltaNet layer: the mixed projection's k|v columns (with per-row scales the fused in-projection, its
+    # convolution in the epilogue), then its q columns over each sequence's last rows
+    fused = shape.block_inputs and p.fused_in
+    assert p.fused_in == (shape.group in (0, shape.d) and shape.head == 128)
+    assert counts["ridgefill_gemm_nt_q_bias"] == L + (G * (int(not fused) + shape.n_seq) if shape.block_inputs else 0) + A
+    assert counts.get("ridgefill_gdn_in_proj", 0) == (G if fused else 0)
+    if fused:   # conv_prep is left the gates and the conv state, after the in-projection has read the old state
+        conv = [c for c in p.calls if c[0] == "ridgefill_gdn_conv_prep"]
+        assert all(dict((q.key.decode(), q.ival) for q in c[3]).get("columns") == 0 for c in conv)
+        assert order_index_ok(p)
     assert counts["ridgefill_gdn_fill"] == 1 and counts["ridgefill_rho_update"] == G
     assert counts["ridgefill_state_correct"] == 2 and counts["ridgefill_mask"] == 1 and counts["ridgefill_hazard"] == 1
     order = [c[0] for c in p.calls]
@@ -54,6 +64,17 @@ def test_every_launch_passes_its_operand_checks(shape, product_lib):
     proj = [c for c in p.calls if c[0] == "ridgefill_gemm_nt_q_bias" and c[4].startswith("proj")]
     assert len(proj) == L and all(c[2][7].data for c in proj)
     assert order.index("ridgefill_gdn_fill") > max(i for i, c in enumerate(p.calls) if c[4].startswith("proj"))
+
+
+def order_index_ok(p) -> bool:
+    """Each layer's conv_prep comes after its in-projection (which reads the conv state conv_prep then updates)."""
+    last_in = None
+    for op, _r, _t, _p, tag in p.calls:
+        if op == "ridgefill_gdn_in_proj":
+            last_in = tag.split()[-1]
+        if op == "ridgefill_gdn_conv_prep" and last_in != tag:
+            return False
+    return True
 
 
 def test_cpu_twin_runs_the_same_pass(oracle_lib):
