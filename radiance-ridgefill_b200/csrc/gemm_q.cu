@@ -30,10 +30,10 @@
  * a CTA projects rows [m_c - 3, m_c + 125), so each of its 125 output rows finds the three rows before it (the
  * causal convolution's window) in the CTA's own tile. Its epilogue rounds the projection to bf16 into a row-major
  * tile in shared memory (the staging space), writes each sequence's last three rows to `tail` (what the conv-state
- * update reads), and then, a lane per 8 channels and a warp per 8 rows, computes conv_prep's arithmetic on them:
- * the width-4 convolution (the rows before a sequence's start from its conv-state slot or zero), SiLU, the L2 norm
- * of each k head (the same summation tree as conv_prep, so the bits agree), k and v to bf16 -- the projection's
- * rows never go to HBM.
+ * update reads), and then, a warp per head and 16 rows and a lane per 4 channels (conv_prep's layout), computes
+ * conv_prep's arithmetic on them instruction for instruction, so the bits agree: the width-4 convolution (the rows
+ * before a sequence's start from its conv-state slot or zero), SiLU, the L2 norm of each k head, k and v to bf16 --
+ * the projection's rows never go to HBM.
  * A K block is `group` columns: 128 for the projector folder's i8*bf16[1x128] encoding, K itself
  * for per-row / per-column scaling (one fold a tile, the int32 accumulation running over all of K).
  */
@@ -62,6 +62,9 @@ constexpr int kMetaBytes = 2 * BM * 4;                         /* the in-project
 constexpr int kSmemBytes = kStages * kStageBytes + kStageOut + kScaleSlots + kMetaBytes + 1024 /* alignment slack */ +
                            256 /* barriers */;
 constexpr int kConvRows = BM - 3;   /* the in-projection's output rows a CTA: its tile less the 3-row window */
+/* The in-projection's epilogue warps: the 16 that fold also convolve; more that only convolve are possible (at 80
+ * registers a thread for 4 more) but measured no faster -- the convolution is bound by the SFU's exp and reciprocal. */
+constexpr int kConvWarps = kEpiWarps;
 constexpr int kEpiBar = 1;          /* named barrier of the 16 epilogue warps */
 
 /* Instruction descriptor of the pair's M256 N256 product: D s32 (bits 4-5 = 2), A and B signed int8 (bits
@@ -129,6 +132,10 @@ __device__ __forceinline__ void fold_block(uint32_t taddr, float (&acc)[kWarpCol
  * registers to itself. */
 enum GemmMode { kModeBf16 = 0, kModeI8 = 1, kModeI8Dump = 2, kModeI8Rows = 3, kModeI8Conv = 4, kModeCount = 5 };
 
+/* Threads a CTA of each form: the producer and MMA warps, then the epilogue warps. */
+template <int kMode>
+constexpr int threads_of() { return 32 * (2 + (kMode == kModeI8Conv ? kConvWarps : kEpiWarps)); }
+
 /* The first row a CTA projects: 256-row pair tiles, or for the in-projection 250-row pair tiles each CTA of which
  * starts three rows before its 125 output rows (a negative start reads zeros). */
 template <int kMode>
@@ -186,34 +193,73 @@ __device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
     return *(const uint32_t*)&v;
 }
 
-__device__ __forceinline__ void unpack8(uint4 v, float (&f)[8]) {
-    const uint32_t w[4] = { v.x, v.y, v.z, v.w };
+__device__ __forceinline__ void unpack4(uint2 v, float (&f)[4]) {
+    f[0] = __uint_as_float(v.x << 16);
+    f[1] = __uint_as_float(v.x & 0xffff0000u);
+    f[2] = __uint_as_float(v.y << 16);
+    f[3] = __uint_as_float(v.y & 0xffff0000u);
+}
+
+/* One output row of the in-projection's convolution for a lane's 4 channels, conv_prep's arithmetic (so the bits
+ * agree): x0..x3 the input rows r - 3 .. r; per channel u = bias, u = fma(w_j, x_j, u) for j = 0..3, y = silu(u); for a
+ * k head y *= rsqrt(ss + 1e-6), ss the lane's four squares by fma, then the warp's butterfly (xor 16, 8, 4, 2, 1: the
+ * warp is the head). The output row `dst`. */
+__device__ __forceinline__ void conv_out(const float (&w)[4][4], const float (&bs)[4], const float (&x0)[4], const float (&x1)[4],
+                                         const float (&x2)[4], const float (&x3)[4], bool is_k, bool col_live, uint16_t* dst) {
+    float y[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-        f[2 * e] = __uint_as_float(w[e] << 16);
-        f[2 * e + 1] = __uint_as_float(w[e] & 0xffff0000u);
+        float u = bs[e];
+        u = fmaf(w[e][0], x0[e], u);
+        u = fmaf(w[e][1], x1[e], u);
+        u = fmaf(w[e][2], x2[e], u);
+        u = fmaf(w[e][3], x3[e], u);
+        y[e] = rf::silu(u);
     }
+    if (is_k) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ss = fmaf(y[e], y[e], ss);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = rsqrtf(ss + 1e-6f);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) y[e] = __fmul_rn(y[e], inv);
+    }
+    if (col_live) *(uint2*)dst = make_uint2(bf16x2(y[0], y[1]), bf16x2(y[2], y[3]));
 }
 
 /* The in-projection's convolution over one CTA tile (rows_tile: the projection's rows m0 .. m0 + 127 as bf16; meta:
- * each row's sequence start, -1 outside every sequence, and its history slot, -1 for none). Warp ew takes output
- * rows 3 + 8 ew .. 10 + 8 ew of the tile, lane l channels nt0 + 8 l .. nt0 + 8 l + 7 (a half-warp is one 128-channel
- * head); the window's three earlier rows ride in registers from row to row. Per channel, as conv_prep:
- * u = bias; u = fma(w_j, x[r - 3 + j], u) for j = 0..3; y = silu(u); for k heads y *= rsqrt(ss + 1e-6) with ss summed
- * in conv_prep's order (each 4-channel run by fma, then the head's butterfly), so the bits agree. */
+ * each row's sequence start, -1 outside every sequence, and its history slot, -1 for none). Epilogue warp cw takes
+ * one of the tile's two 128-channel heads (cw & 1) over a run of output rows (16 rows for 16 warps), lane l its
+ * channels 4 l .. 4 l + 3 -- conv_prep's layout. Rows go in groups of four: when the four lie in one sequence (the
+ * common case) their seven input rows are loaded and widened once and the four rows computed side by side;
+ * otherwise row by row. An input row before the sequence's start comes from its conv-state slot, or is zero. */
 __device__ __forceinline__ void conv_rows(const GemmPlan& p, const uint8_t* rows_tile, const int32_t* meta_s0,
-                                          const int32_t* meta_slot, int64_t m0, int64_t nt0, int ew, int lane) {
+                                          const int32_t* meta_slot, int64_t m0, int64_t nt0, int cw, int lane) {
     const RidgeFillInProj& c = p.c;
     const int64_t M = p.g.M, N = p.g.N;
-    const int64_t cn = nt0 + lane * 8;
-    const bool col_live = cn < N, is_k = cn < c.n_k, norm_tile = nt0 < c.n_k;
-    /* the taps as bf16 pairs: wv[i] holds channels 2 i and 2 i + 1, four taps each (words 0-1 and 2-3) */
-    uint4 wv[4] = {};
-    uint4 bv = {};
-    if (col_live) {
+    const int hcol = cw & 1;
+    const int64_t cn = nt0 + hcol * 128 + lane * 4;
+    const bool col_live = cn < N, is_k = cn < c.n_k;   /* both the same over the warp */
+    float w[4][4], bs[4];   /* channel e's taps w[e][0..3] and bias, widened once a tile */
+    {
+        uint4 wv[2] = {};
+        uint2 bv = {};
+        if (col_live) {
+            wv[0] = __ldg((const uint4*)(c.w + cn * 4));
+            wv[1] = __ldg((const uint4*)(c.w + cn * 4 + 8));
+            if (c.bias) bv = __ldg((const uint2*)(c.bias + cn));
+        }
+        const uint32_t ww[8] = { wv[0].x, wv[0].y, wv[0].z, wv[0].w, wv[1].x, wv[1].y, wv[1].z, wv[1].w };
 #pragma unroll
-        for (int i = 0; i < 4; ++i) wv[i] = __ldg((const uint4*)(c.w + cn * 4) + i);
-        if (c.bias) bv = __ldg((const uint4*)(c.bias + cn));
+        for (int e = 0; e < 4; ++e)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t word = ww[2 * e + (j >> 1)];
+                w[e][j] = __uint_as_float((j & 1) ? (word & 0xffff0000u) : (word << 16));
+            }
+        unpack4(bv, bs);
     }
     uint16_t* out;
     int64_t out_row;
@@ -225,145 +271,138 @@ __device__ __forceinline__ void conv_rows(const GemmPlan& p, const uint8_t* rows
         out = c.v + (vc >> 7) * c.v_head + (vc & 127);
         out_row = c.v_row;
     }
-    const int tb = 3 + ew * 8, te = min(tb + 8, BM);
-    uint4 win[3] = {};   /* rows r - 3, r - 2, r - 1 */
-    int64_t win_r = -1;
-    int win_s0 = -1;
-    for (int t = tb; t < te; ++t) {
-        const int64_t r = m0 + t;
-        if (r >= M) break;
+    const uint8_t* my_tile = rows_tile + (lane & 1) * 8;
+    const int chunk = hcol * 16 + (lane >> 1);
+    /* input row t_in of an output row in the sequence starting at s0 with history slot `slot` */
+    auto fetch = [&](int t_in, int s0, int slot, float (&f)[4]) {
+        const int64_t rr = m0 + t_in;
+        uint2 v = make_uint2(0u, 0u);
+        if (rr >= s0) v = *(const uint2*)(my_tile + conv_chunk(t_in, chunk));
+        else if (slot >= 0 && col_live) v = *(const uint2*)(c.state + slot * c.st_slot + (3 - (s0 - rr)) * c.st_row + cn);
+        unpack4(v, f);
+    };
+    constexpr int kRowsPer = (kConvRows + kConvWarps / 2 - 1) / (kConvWarps / 2);
+    const int tb = 3 + (cw >> 1) * kRowsPer, te = min(tb + kRowsPer, BM);
+    for (int t = tb; t < te; t += 4) {
+        const int n = min(4, te - t);
         const int s0 = meta_s0[t];
-        if (s0 < 0) continue;   /* outside every sequence: left untouched */
-        if (win_r != r - 1 || win_s0 != s0) {
-            const int slot = meta_slot[t];
+        bool group = n == 4 && s0 >= 0 && m0 + t + 3 < M;
 #pragma unroll
-            for (int j = 1; j <= 3; ++j) {
-                const int64_t rr = r - j;
-                uint4 x = make_uint4(0u, 0u, 0u, 0u);
-                if (rr >= s0) x = *(const uint4*)(rows_tile + conv_chunk(t - j, lane));
-                else if (slot >= 0 && col_live) x = *(const uint4*)(c.state + slot * c.st_slot + (3 - (s0 - rr)) * c.st_row + cn);
-                win[3 - j] = x;
+        for (int i = 1; i < 4; ++i) group = group && meta_s0[min(t + i, BM - 1)] == s0;
+        if (group) {
+            float x[7][4];
+            if (m0 + t - 3 >= s0) {   /* the whole window inside the tile: plain loads */
+#pragma unroll
+                for (int j = 0; j < 7; ++j) unpack4(*(const uint2*)(my_tile + conv_chunk(t - 3 + j, chunk)), x[j]);
+            } else {
+                const int slot = meta_slot[t];
+#pragma unroll
+                for (int j = 0; j < 7; ++j) fetch(t - 3 + j, s0, slot, x[j]);
+            }
+            uint16_t* dst = out + (m0 + t) * out_row;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) conv_out(w, bs, x[i], x[i + 1], x[i + 2], x[i + 3], is_k, col_live, dst + i * out_row);
+        } else {
+            for (int i = 0; i < n; ++i) {
+                const int ti = t + i;
+                if (m0 + ti >= M) break;
+                const int si = meta_s0[ti];
+                if (si < 0) continue;   /* outside every sequence: left untouched */
+                const int sl = meta_slot[ti];
+                float x0[4], x1[4], x2[4], x3[4];
+                fetch(ti - 3, si, sl, x0);
+                fetch(ti - 2, si, sl, x1);
+                fetch(ti - 1, si, sl, x2);
+                fetch(ti, si, sl, x3);
+                conv_out(w, bs, x0, x1, x2, x3, is_k, col_live, out + (m0 + ti) * out_row);
             }
         }
-        const uint4 cur = *(const uint4*)(rows_tile + conv_chunk(t, lane));
-        float x0[8], x1[8], x2[8], x3[8], y[8], bs[8];
-        unpack8(win[0], x0);
-        unpack8(win[1], x1);
-        unpack8(win[2], x2);
-        unpack8(cur, x3);
-        unpack8(bv, bs);
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-            float w0[4], w1[4];   /* channel e's and e + 1's taps */
-            {
-                float f[8];
-                unpack8(wv[e >> 1], f);
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    w0[t] = f[t];
-                    w1[t] = f[4 + t];
-                }
-            }
-            float u0 = bs[e], u1 = bs[e + 1];
-            rf::fma2_rn(u0, u1, w0[0], w1[0], x0[e], x0[e + 1]);
-            rf::fma2_rn(u0, u1, w0[1], w1[1], x1[e], x1[e + 1]);
-            rf::fma2_rn(u0, u1, w0[2], w1[2], x2[e], x2[e + 1]);
-            rf::fma2_rn(u0, u1, w0[3], w1[3], x3[e], x3[e + 1]);
-            y[e] = rf::silu(u0);
-            y[e + 1] = rf::silu(u1);
-        }
-        if (norm_tile) {   /* the tile holds a k head: every lane takes part in the butterflies */
-            float se = 0.0f, so = 0.0f;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                se = fmaf(y[e], y[e], se);
-                so = fmaf(y[4 + e], y[4 + e], so);
-            }
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) {
-                se += __shfl_xor_sync(0xffffffffu, se, o);
-                so += __shfl_xor_sync(0xffffffffu, so, o);
-            }
-            if (is_k) {
-                const float inv = rsqrtf((se + so) + 1e-6f);
-#pragma unroll
-                for (int e = 0; e < 8; e += 2) rf::mul2_rn(y[e], y[e + 1], y[e], y[e + 1], inv, inv);
-            }
-        }
-        if (col_live) *(uint4*)(out + r * out_row) = make_uint4(bf16x2(y[0], y[1]), bf16x2(y[2], y[3]), bf16x2(y[4], y[5]), bf16x2(y[6], y[7]));
-        win[0] = win[1];
-        win[1] = win[2];
-        win[2] = cur;
-        win_r = r;
-        win_s0 = s0;
     }
 }
 
-/* The in-projection's epilogue warps. Per tile (one K block: group = K): the lane's row waits for its sums and looks up
- * its sequence; the epilogue barrier, which also agrees on a failed wait (every warp then leaves together), ensures
- * every warp is done with the previous tile's rows; the sums are folded eight columns at a time straight from
- * tensor memory and rounded to bf16 into the row tile (each sequence's last three rows also to `tail`), the
- * accumulator goes back to the MMA warp; a second barrier; the convolution. False when a wait gave up. */
-__device__ __forceinline__ bool conv_epilogue(const GemmPlan& p, uint8_t* rows_tile, int32_t* meta, uint32_t lane_addr, int warp,
-                                              int lane, int pair, int pairs, uint32_t rank, volatile int* abort,
-                                              uint64_t* acc_full, uint64_t* acc_empty) {
+/* The in-projection's epilogue warps (kConvWarps of them; the first kEpiWarps also fold). Per tile (one K block:
+ * group = K): a folding lane's row waits for its sums and looks up its sequence; the epilogue barrier, which also
+ * agrees on a failed wait (every warp then leaves together), ensures every warp is done with the previous tile's
+ * rows; the folding warps fold their sums 32 columns a tensor-memory load (the b_scale values prefetched into the
+ * warp's shared-memory slot), round them to bf16 into the row tile (each sequence's last three rows also to `tail`)
+ * and hand the accumulator back to the MMA warp; a second barrier; every warp convolves. False when a wait gave up. */
+__device__ __forceinline__ bool conv_epilogue(const GemmPlan& p, uint8_t* rows_tile, float* scale_slots, int32_t* meta,
+                                              uint32_t lane_addr, int warp, int lane, int pair, int pairs, uint32_t rank,
+                                              volatile int* abort, uint64_t* acc_full, uint64_t* acc_empty) {
     const RidgeFillGemmQ& g = p.g;
     const RidgeFillInProj& c = p.c;
     const int ew = warp - 2, slice = ew >> 2, row = (warp & 3) * 32 + lane;
+    const bool folds = ew < kEpiWarps;
+    float* sb = scale_slots + ew * 2 * kWarpCols;   /* a folding warp's b_scale values */
     int32_t* meta_s0 = meta;
     int32_t* meta_slot = meta + BM;
     uint32_t fold = 0;
     for (int tile = pair; tile < p.tiles; tile += pairs, ++fold) {
         const int64_t m0 = tile_row0<kModeI8Conv>(tile, p.n_tiles, rank), nt0 = (int64_t)(tile % p.n_tiles) * BN;
         const int64_t m = m0 + row, n0 = nt0 + slice * kWarpCols;
-        const bool row_live = m >= 0 && m < g.M;
-        const float sa = row_live ? g.a_scale[m * g.ldas] : 0.0f;
+        const bool row_live = folds && m >= 0 && m < g.M;
         const uint32_t buf = fold & 1, use = (fold >> 1) & 1;
-        const bool ok = rf::mbar_wait(&acc_full[buf], use, abort, rf::kErrGemmWaitEpilogue);
-        /* the row's sequence and the conv-state slot of its history */
+        float sa = 0.0f;
+        bool ok = true;
         int64_t s0 = -1, e0 = -1;
-        const int seq = ok && row_live ? rf::find_seq(c.cu, c.n_seq, g.M, m, &s0, &e0) : -1;
+        int seq = -1;
         int32_t slot = -1;
-        if (seq >= 0 && c.ctx && c.ctx[seq] > 0) {
-            const int64_t sl = c.idx[seq * c.idx_pitch];
-            if (sl >= 0 && sl < c.n_states) slot = (int32_t)sl;
-        }
-        if (rf::bar_any(kEpiBar, 32 * kEpiWarps, !ok)) return false;
-        rf::tc_fence_after();
-        const bool tail_row = row >= 3 && seq >= 0 && m >= e0 - 3;
-#pragma unroll 2
-        for (int v = 0; v < kWarpCols / 8; ++v) {
-            const int64_t n = n0 + v * 8;
-            uint32_t r[8];
-            rf::tmem_ld8(lane_addr + buf * BN + v * 8, r);
-            float a8[8] = {}, sb[8] = {};
-            if (n < g.N) {   /* N is a multiple of 128 */
-                const float4 s0v = __ldg((const float4*)(g.b_scale + n)), s1v = __ldg((const float4*)(g.b_scale + n + 4));
-                sb[0] = s0v.x; sb[1] = s0v.y; sb[2] = s0v.z; sb[3] = s0v.w;
-                sb[4] = s1v.x; sb[5] = s1v.y; sb[6] = s1v.z; sb[7] = s1v.w;
+        if (folds) {
+            sa = row_live ? g.a_scale[m * g.ldas] : 0.0f;
+            /* this warp's 64 b_scale values into its shared-memory slot while the sums are computed (the slot's reads
+             * of the previous tile ended before its second barrier); columns past N read as zero */
+            if (lane < kWarpCols / 4) {
+                const bool in = n0 + lane * 4 < g.N;   /* N is a multiple of 128 */
+                rf::cp_async16_zfill(sb + lane * 4, g.b_scale + (in ? n0 + lane * 4 : 0), in ? 16u : 0u);
             }
-            rf::tmem_ld_wait();
-            fold8(r, a8, sb, sa);
-            const uint4 q = make_uint4(rf::pack_bf16(a8[0], a8[1]), rf::pack_bf16(a8[2], a8[3]), rf::pack_bf16(a8[4], a8[5]),
-                                       rf::pack_bf16(a8[6], a8[7]));
-            *(uint4*)(rows_tile + conv_chunk(row, slice * (kWarpCols / 8) + v)) = q;
-            if (tail_row && n < g.N) *(uint4*)(g.y + m * g.ldy + n) = q;
+            ok = rf::mbar_wait(&acc_full[buf], use, abort, rf::kErrGemmWaitEpilogue);
+            /* the row's sequence and the conv-state slot of its history */
+            seq = ok && row_live ? rf::find_seq(c.cu, c.n_seq, g.M, m, &s0, &e0) : -1;
+            if (seq >= 0 && c.ctx && c.ctx[seq] > 0) {
+                const int64_t sl = c.idx[seq * c.idx_pitch];
+                if (sl >= 0 && sl < c.n_states) slot = (int32_t)sl;
+            }
+            rf::cp_async_wait_all();
         }
-        rf::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) rf::mbar_arrive_cluster_relaxed(rf::map_rank(rf::smem_addr(&acc_empty[buf]), 0));
-        if (slice == 0) {
-            meta_s0[row] = seq >= 0 ? (int32_t)s0 : -1;
-            meta_slot[row] = slot;
+        if (rf::bar_any(kEpiBar, 32 * kConvWarps, !ok)) return false;
+        if (folds) {
+            rf::tc_fence_after();
+            const bool tail_row = row >= 3 && seq >= 0 && m >= e0 - 3;
+#pragma unroll 1
+            for (int h = 0; h < kWarpCols / 32; ++h) {   /* 32 columns a tensor-memory load */
+                uint32_t r[32];
+                rf::tmem_ld32(lane_addr + buf * BN + h * 32, r);
+                rf::tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int v = h * 4 + j;
+                    const int64_t n = n0 + v * 8;
+                    float a8[8] = {};
+                    fold8(*(const uint32_t(*)[8])(r + j * 8), a8, sb + v * 8, sa);
+                    /* the hardware's round to nearest even: the GEMM's rounding for every value but a NaN (made
+                     * the canonical one) */
+                    const uint4 q = make_uint4(bf16x2(a8[0], a8[1]), bf16x2(a8[2], a8[3]), bf16x2(a8[4], a8[5]),
+                                               bf16x2(a8[6], a8[7]));
+                    *(uint4*)(rows_tile + conv_chunk(row, slice * (kWarpCols / 8) + v)) = q;
+                    if (tail_row && n < g.N) *(uint4*)(g.y + m * g.ldy + n) = q;
+                }
+            }
+            rf::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) rf::mbar_arrive_cluster_relaxed(rf::map_rank(rf::smem_addr(&acc_empty[buf]), 0));
+            if (slice == 0) {
+                meta_s0[row] = seq >= 0 ? (int32_t)s0 : -1;
+                meta_slot[row] = slot;
+            }
         }
-        rf::bar_sync(kEpiBar, 32 * kEpiWarps);
+        rf::bar_sync(kEpiBar, 32 * kConvWarps);
         conv_rows(p, rows_tile, meta_s0, meta_slot, m0, nt0, ew, lane);
     }
     return true;
 }
 
 template <int kMode>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_of<kMode>(), 1)
 gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
               const __grid_constant__ CUtensorMap map_y, const GemmPlan p) {
     constexpr bool kBf16 = kMode == kModeBf16;
@@ -563,7 +602,8 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
             }
         }
         if constexpr (kMode == kModeI8Conv)
-            ok = conv_epilogue(p, stage_out, meta, lane_addr, warp, lane, pair, pairs, rank, abort, acc_full, acc_empty);
+            ok = conv_epilogue(p, stage_out, scale_slots, meta, lane_addr, warp, lane, pair, pairs, rank, abort, acc_full,
+                               acc_empty);
         for (int tile = pair; tile < p.tiles && ok && !kBf16 && kMode != kModeI8Conv; tile += pairs) {
             const int64_t m = (int64_t)(tile / p.n_tiles) * BM2 + rank * BM + row;
             const int64_t n0 = (int64_t)(tile % p.n_tiles) * BN + slice * kWarpCols;
@@ -901,7 +941,7 @@ int launch_pairs(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUten
     if (!max_pairs[kMode]) {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * (unsigned)(rf::sm_count() / 2));
-        cfg.blockDim = dim3(kThreads);
+        cfg.blockDim = dim3(threads_of<kMode>());
         cfg.dynamicSmemBytes = kSmemBytes;
         int n = 0;
         if (cudaOccupancyMaxActiveClusters(&n, gemm_q_kernel<kMode>, &cfg) != cudaSuccess || n <= 0) return RAD_E_DEVICE;
@@ -911,7 +951,7 @@ int launch_pairs(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUten
     if constexpr (kMode != kModeBf16) {
         if (p.g.max_ctas > 0 && p.g.max_ctas / 2 < pairs) pairs = p.g.max_ctas / 2 > 0 ? (int)(p.g.max_ctas / 2) : 1;
     }
-    gemm_q_kernel<kMode><<<2 * pairs, kThreads, kSmemBytes, stream>>>(map_a, map_b, map_y, p);
+    gemm_q_kernel<kMode><<<2 * pairs, threads_of<kMode>(), kSmemBytes, stream>>>(map_a, map_b, map_y, p);
     return rf::launch_status();
 }
 

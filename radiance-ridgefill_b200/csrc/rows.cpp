@@ -159,7 +159,7 @@ const RadKernelInfo kRows[] = {
     DEVICE_ROW("ridgefill_gdn_in_proj_sm100", "ridgefill_gdn_in_proj",
                "the int8 projector's 2-CTA tcgen05 pipeline over 250-row pair tiles (each CTA's tile starts 3 rows early: "
                "the convolution's window); the epilogue rounds the rows into shared memory and runs the convolution, "
-               "SiLU and k norm there, lane per 8 channels", "head dims 128, conv width 4, K a multiple of 128, group = K",
+               "SiLU and k norm there, a warp per head and 16 rows, 4 channels a lane", "head dims 128, conv width 4, K a multiple of 128, group = K",
                "i8 a / b, f32 a_scale / b_scale, bf16 w / bias / state / k / v / tail", nullptr, 0,
                ridgefill_gdn_in_proj_device, nullptr, shape_in_proj, nullptr, nullptr, nullptr),
     DEVICE_ROW("ridgefill_attn_kv_fill_sm100", "ridgefill_attn_kv_fill",
