@@ -1146,7 +1146,8 @@ struct HdSmem {
     } work[2];
     struct Meta {
         float gl[4];             /* gamma_L = exp(G_L) */
-    } meta[2];                   /* by chunk parity: the chain's lanes read it after the stage may be reused */
+    } meta[2];                   /* by chunk parity: the chain's lanes read it after the stage may be reused; the
+                                    transform writes chunk q's only after buf_free of chunk q - 2 */
     uint64_t landed[kHdStages], stage_free[kHdStages], buf_free[2];
     uint64_t kk_full, kk_free, t_ready[2], wt_full, ut_full, tsw_free[2], w_ready[2], d1_full, d2_full, as_ready, av_ready,
         d2_ready;
@@ -1398,7 +1399,6 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                 /* the chunk's k, v, g, beta and (by the loader) G and G_L are in */
                 if ((stop = failed(rf::mbar_wait(&s.landed[st], (uint32_t)((q / kHdStages) & 1), abort, rf::kErrGdnWait)))) break;
                 const float gl = sg.gl[0];
-                if (gt == 0) mt.gl[0] = __expf(gl);   /* gamma_L for the chain's lanes */
                 const uint32_t ktile = rf::saddr(&sg.k[0][0][0]), vtile = rf::saddr(&sg.v[0][0][0]);
                 /* x2 = beta v in place: row gt & 63, column half gt >> 6; four segments' loads before their stores
                  * (the shared-memory helpers keep their order as written) */
@@ -1428,6 +1428,9 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                     ok = ok && rf::mbar_wait(&s.tsw_free[grp], (uint32_t)(((q >> 1) - 1) & 1), abort, rf::kErrGdnWait);
                 }
                 if ((stop = failed(ok))) break;
+                /* gamma_L for the chain's lanes, written only now: they read this parity's value of two chunks ago
+                 * before their d2_ready of that chunk, and buf_free (waited above) completes after its D2 */
+                if (gt == 0) mt.gl[0] = __expf(gl);
                 rf::tc_fence_after();
                 if (lw < 2) {
                     /* A's rows: thread = row i (lane quarter lw), its 64 columns from tensor memory, 32 at a time */

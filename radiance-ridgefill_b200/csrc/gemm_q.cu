@@ -34,6 +34,8 @@
  * conv_prep's arithmetic on them instruction for instruction, so the bits agree: the width-4 convolution (the rows
  * before a sequence's start from its conv-state slot or zero), SiLU, the L2 norm of each k head, k and v to bf16 --
  * the projection's rows never go to HBM.
+ * The bf16 GEMM with N <= 64 (the DeltaNet block's a|b projection) runs M256 N64 pair tiles: the same pipeline,
+ * a quarter of the wide tile's MMA work, which at that width would mostly multiply the B tile's zero rows.
  * A K block is `group` columns: 128 for the projector folder's i8*bf16[1x128] encoding, K itself
  * for per-row / per-column scaling (one fold a tile, the int32 accumulation running over all of K).
  */
@@ -71,8 +73,10 @@ constexpr int kEpiBar = 1;          /* named barrier of the 16 epilogue warps */
  * 7-9, 10-12 = 1), both K-major, N >> 3 at bit 17, M >> 4 at bit 24. */
 constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM2 >> 4) << 24);
 
-/* kind::f16 with bf16 A and B (bits 7-9, 10-12 = 1), D f32 (bit 4): the bf16 GEMM (ridgefill_gemm_nt_bias). */
-constexpr uint32_t kIdescBf16 = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM2 >> 4) << 24);
+/* kind::f16 with bf16 A and B (bits 7-9, 10-12 = 1), D f32 (bit 4): the bf16 GEMM (ridgefill_gemm_nt_bias), N columns. */
+__host__ __device__ constexpr uint32_t idesc_bf16(int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(BM2 >> 4) << 24);
+}
 
 struct GemmPlan {
     RidgeFillGemmQ g;       /* the int8 form */
@@ -130,7 +134,12 @@ __device__ __forceinline__ void fold_block(uint32_t taddr, float (&acc)[kWarpCol
  * (the optional acc operand), the int8 projector writing only the selected rows (the optional rows operand), and
  * the DeltaNet in-projection with the convolution in its epilogue. Separate instantiations keep each form's
  * registers to itself. */
-enum GemmMode { kModeBf16 = 0, kModeI8 = 1, kModeI8Dump = 2, kModeI8Rows = 3, kModeI8Conv = 4, kModeCount = 5 };
+enum GemmMode { kModeBf16 = 0, kModeI8 = 1, kModeI8Dump = 2, kModeI8Rows = 3, kModeI8Conv = 4, kModeBf16Narrow = 5, kModeCount = 6 };
+
+/* A pair tile's columns: 256, or 64 for the narrow bf16 form (N <= 64, e.g. the DeltaNet a|b projection), whose
+ * M256 N64 products leave the MMAs a quarter of the wide form's work when it would mostly multiply zero rows. */
+template <int kMode>
+__host__ __device__ constexpr int bn_of() { return kMode == kModeBf16Narrow ? 64 : BN; }
 
 /* Threads a CTA of each form: the producer and MMA warps, then the epilogue warps. */
 template <int kMode>
@@ -405,7 +414,9 @@ template <int kMode>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_of<kMode>(), 1)
 gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
               const __grid_constant__ CUtensorMap map_y, const GemmPlan p) {
-    constexpr bool kBf16 = kMode == kModeBf16;
+    constexpr bool kBf16 = kMode == kModeBf16 || kMode == kModeBf16Narrow;
+    constexpr int kBN = bn_of<kMode>();
+    constexpr uint32_t kTxBytes = 2 * (kABytes + (kBN / 2) * BK);   /* both CTAs' A and B halves a stage */
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* tile_a = smem;
@@ -452,10 +463,10 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
             int64_t issued = 0;
             const int steps = p.folds * p.steps_per_fold;
             for (int tile = pair; tile < p.tiles && !*abort; tile += pairs) {
-                const int m0 = (int)tile_row0<kMode>(tile, p.n_tiles, rank), n0 = (tile % p.n_tiles) * BN + (int)rank * (BN / 2);
+                const int m0 = (int)tile_row0<kMode>(tile, p.n_tiles, rank), n0 = (tile % p.n_tiles) * kBN + (int)rank * (kBN / 2);
                 for (int ks = 0; ks < steps; ++ks) {
                     if (!rf::mbar_wait(&empty[stage], phase ^ 1, abort, rf::kErrGemmWaitProducer)) break;
-                    if (rank == 0) rf::mbar_arrive_expect_tx(&full[stage], 2 * kStageBytes);
+                    if (rank == 0) rf::mbar_arrive_expect_tx(&full[stage], kTxBytes);
                     const int kx = ks * (kBf16 ? BK / 2 : BK);   /* the K step's first column, in elements */
                     const uint32_t bar = rf::map_rank(rf::smem_addr(&full[stage]), 0);   /* rank 0's */
                     rf::tma_load_2d_pair(tile_a + stage * kABytes, &map_a, bar, kx, m0);
@@ -497,7 +508,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
                         for (int kk = 0; kk < BK / 32; ++kk) {   /* 32 bytes of K a product: 32 int8 or 16 bf16 */
                             if constexpr (kBf16)
                                 rf::umma_f16_pair(d, rf::sw128_kmajor_desc(a_addr + kk * 32), rf::sw128_kmajor_desc(b_addr + kk * 32),
-                                                  kIdescBf16, (ks | kk) != 0);
+                                                  idesc_bf16(kBN), (ks | kk) != 0);
                             else
                                 rf::mma_i8_pair(d, rf::sw128_kmajor_desc(a_addr + kk * 32), rf::sw128_kmajor_desc(b_addr + kk * 32),
                                                 kIdesc, (ks | kk) != 0);
@@ -528,7 +539,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
             const RidgeFillGemmBias& gb = p.gb;
             for (int tile = pair; tile < p.tiles && ok; tile += pairs, ++fold) {
                 const int64_t m = (int64_t)(tile / p.n_tiles) * BM2 + rank * BM + row;
-                const int64_t n0 = (int64_t)(tile % p.n_tiles) * BN + slice * kWarpCols;
+                const int64_t n0 = (int64_t)(tile % p.n_tiles) * kBN + slice * kWarpCols;
                 const uint32_t buf = fold & 1, use = (fold >> 1) & 1;
                 if (!(ok = rf::mbar_wait(&acc_full[buf], use, abort, rf::kErrGemmWaitEpilogue))) break;
                 rf::tc_fence_after();
@@ -948,7 +959,7 @@ int launch_pairs(const CUtensorMap& map_a, const CUtensorMap& map_b, const CUten
         max_pairs[kMode] = n;
     }
     int pairs = p.tiles < max_pairs[kMode] ? p.tiles : max_pairs[kMode];
-    if constexpr (kMode != kModeBf16) {
+    if constexpr (kMode != kModeBf16 && kMode != kModeBf16Narrow) {
         if (p.g.max_ctas > 0 && p.g.max_ctas / 2 < pairs) pairs = p.g.max_ctas / 2 > 0 ? (int)(p.g.max_ctas / 2) : 1;
     }
     gemm_q_kernel<kMode><<<2 * pairs, threads_of<kMode>(), kSmemBytes, stream>>>(map_a, map_b, map_y, p);
@@ -1014,8 +1025,10 @@ bool bf16_tile_map(CUtensorMap* map, const void* base, int64_t rows, int64_t col
 int launch_gemm_bf16(const RidgeFillGemmBias& g, cudaStream_t stream) {
     if (g.M == 0) return RAD_OK;
     if (g.M > 0x7fffffffLL || g.N > 0x7fffffffLL || g.K > 0x7fffffffLL) return RAD_E_SHAPE;
+    const bool narrow = g.N <= bn_of<kModeBf16Narrow>();
+    const int bn = narrow ? bn_of<kModeBf16Narrow>() : BN;
     CUtensorMap map_a, map_b, map_y;
-    if (!bf16_tile_map(&map_a, g.a, g.M, g.K, g.lda, BM) || !bf16_tile_map(&map_b, g.b, g.N, g.K, g.ldb, BN / 2) ||
+    if (!bf16_tile_map(&map_a, g.a, g.M, g.K, g.lda, BM) || !bf16_tile_map(&map_b, g.b, g.N, g.K, g.ldb, bn / 2) ||
         !bf16_store_map(&map_y, g.y, g.M, g.N, g.ldy))
         return RAD_E_DEVICE;
     GemmPlan p{};
@@ -1026,7 +1039,8 @@ int launch_gemm_bf16(const RidgeFillGemmBias& g, cudaStream_t stream) {
     p.tiles = (int)tiles;
     p.folds = 1;
     p.steps_per_fold = (int)((g.K + BK / 2 - 1) / (BK / 2));   /* a ragged last step reads zeros past K */
-    return launch_pairs<kModeBf16>(map_a, map_b, map_y, p, stream);
+    return narrow ? launch_pairs<kModeBf16Narrow>(map_a, map_b, map_y, p, stream)
+                  : launch_pairs<kModeBf16>(map_a, map_b, map_y, p, stream);
 }
 
 }  // namespace

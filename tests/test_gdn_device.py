@@ -325,3 +325,4 @@ def test_head_form_full_size_split_is_one_call(cuda, product_lib):
     for h0 in (0, 21, 42, 63):
         want32, _ = H.oracle_gdn(k, v, g, beta, state, [0], [0, T], f64=False, heads=(h0, h0 + 1))
         assert H.rel_l2(one[0, h0], want32[0, h0]) <= STATE_TOL
+

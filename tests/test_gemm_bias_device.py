@@ -119,6 +119,10 @@ def test_projector_shape_matches_oracle(cuda, product_lib, M, variant):
     (257, 272, 1024, False, True, "silu"),  # ragged tiles on both axes, the activation and the residual
     (200, 2560, 512, True, False, "silu"),
     (129, 520, 328, True, True, "none"),
+    # the narrow form (N <= 64: M256 N64 pair tiles): the DeltaNet a|b projection's shape, and a ragged one
+    (4096, 64, 2048, False, False, None),
+    (515, 40, 200, True, True, "silu"),
+    (300, 72, 256, False, False, None),     # a column block past the narrow form: the wide one
 ])
 def test_ragged_shapes_match_oracle(cuda, product_lib, M, N, K, bias_f32, res, act):
     torch = cuda

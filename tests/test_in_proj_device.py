@@ -212,3 +212,37 @@ def test_refusals(cuda, product_lib):
     params = [H.pint("M", 16), H.pint("N", 256), H.pint("K", 256), H.pint("n_head_k", 1), H.pint("n_head_v", 1),
               H.pint("group", 256), H.pstr("dtype", "i8a8")]
     assert H.launch(product_lib, "ridgefill_gdn_in_proj", ops, params) == abi.E_INVAL
+
+
+@pytest.mark.parametrize("span", [(0, 8, 0, 16), (8, 16, 16, 32), (5, 11, 10, 22)])
+def test_head_span_equals_its_slice_of_the_full_call(cuda, product_lib, span):
+    """A tensor-parallel rank's call (its k heads k0..k1 and v heads v0..v1: the weight rows, scales, taps and conv
+    state of those channels) gives its slice of the full call's k and v, and its tail columns, bit for bit."""
+    torch = cuda
+    hk, hv = 16, 32
+    k0, k1, v0, v1 = span
+    d = _inputs(13, 640, hk, hv, 2048, slots=3)
+    cu, idx, ctx = [0, 200, 640], [2, 0], [1, 0]
+    rc, k, v, tail = _in_proj(product_lib, torch, d, cu, idx, ctx, hk, hv)
+    assert rc == abi.OK
+    ch = np.concatenate([np.arange(k0 * 128, k1 * 128), np.arange((hk + v0) * 128, (hk + v1) * 128)])
+    part = dict(d, b=np.ascontiguousarray(d["b"][ch]), sb=np.ascontiguousarray(d["sb"][:, ch]),
+                w=np.ascontiguousarray(d["w"][ch]), bias=np.ascontiguousarray(d["bias"][ch]),
+                state=np.ascontiguousarray(d["state"][:, :, ch]))
+    rc, kp, vp, tp = _in_proj(product_lib, torch, part, cu, idx, ctx, k1 - k0, v1 - v0)
+    assert rc == abi.OK
+    assert np.array_equal(kp, k[:, k0:k1]), "k"
+    assert np.array_equal(vp, v[:, v0:v1]), "v"
+    assert np.array_equal(tp, tail[:, ch]), "tail"
+
+
+def test_repeated_calls_agree(cuda, product_lib):
+    """The same call twice gives the same bits (no order-dependent step in the epilogue)."""
+    torch = cuda
+    d = _inputs(17, 3000, 16, 32, 2048)
+    cu, idx, ctx = [0, 700, 3000], [1, 0], [1, 1]
+    first = _in_proj(product_lib, torch, d, cu, idx, ctx, 16, 32)
+    for _ in range(3):
+        again = _in_proj(product_lib, torch, d, cu, idx, ctx, 16, 32)
+        for a, b in zip(first[1:], again[1:]):
+            assert np.array_equal(a, b)

@@ -136,3 +136,37 @@ def test_batched_fill_equals_one_fill_per_layer(cuda, product_lib):
         assert H.launch(product_lib, "ridgefill_gdn_fill", tens, H.gdn_params(T, hk, hv)) == abi.OK
     torch.cuda.synchronize()
     assert torch.equal(batched, per_layer)
+
+
+@gpu
+def test_the_pass_and_its_fill_repeat_bit_for_bit(cuda):
+    """The pass's own fill inputs (the second pass, up to its fill), the fill launched again and again from the same
+    state after the pass's other kernels: every run's state equal bit for bit, and two passes from fresh objects over
+    the same seeded inputs equal bit for bit. (The per-head fill once handed a chunk's gamma_L to the chain's lanes
+    through a slot the next chunk of that parity could overwrite first: the first fill after other kernels then
+    differed from the ones after it.)"""
+    torch = cuda
+    shape = LP.LateShape(T=640, layers="GGAG", seqlens=(200, 440))
+    passes = []
+    for _ in range(2):
+        p = LP.LatePass(shape, "cuda", seed=3)
+        s = torch.cuda.Stream()
+        for _ in range(2):
+            p.run(s.cuda_stream)
+        s.synchronize()
+        passes.append(p.state.clone())
+    assert torch.equal(passes[0], passes[1])
+    fill_i = [i for i, c in enumerate(p.calls) if c[0] == "ridgefill_gdn_fill"][0]
+    for c in p.calls[:fill_i]:
+        p._launch(c[0], c[1], c[2], c[3], s.cuda_stream)
+    s.synchronize()
+    st0 = p.state.clone()
+    c = p.calls[fill_i]
+    outs = []
+    for _ in range(6):
+        p.state.copy_(st0)
+        p._launch(c[0], c[1], c[2], c[3], s.cuda_stream)
+        s.synchronize()
+        outs.append(p.state.clone())
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
