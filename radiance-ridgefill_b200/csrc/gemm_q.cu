@@ -619,27 +619,18 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
             const int64_t m = (int64_t)(tile / p.n_tiles) * BM2 + rank * BM + row;
             const int64_t n0 = (int64_t)(tile % p.n_tiles) * BN + slice * kWarpCols;
             const bool row_live = m < g.M;
-            float acc[kWarpCols];
-            if (!(ok = fold_tile<kMode == kModeI8Dump>(p, acc, scale_slots + (warp - 2) * 2 * kWarpCols, lane_addr, lane, m, n0,
-                                                         row_live, fold, abort, acc_full, acc_empty)))
-                break;
             /* bf16 (and the bias) into this warp's staging tiles, once the previous tile's stores have read them; or,
-             * with a row selection, straight from the lanes into the selected rows of y (a lane is one row). */
+             * with a row selection, straight from the lanes into the selected rows of y (a lane is one row). The
+             * hardware's round to nearest even: the fold's rounding for every value but a NaN (made the canonical
+             * one). */
             uint8_t* stg = stage_out + (warp - 2) * kBoxes * kOutBox;
             constexpr bool direct = kMode == kModeI8Rows;
             const bool write_row = direct && row_live && __ldg(g.rows + m) == 1;
-            if constexpr (!direct) {
-                if (lane == 0) rf::bulk_store_wait_read();
-                __syncwarp();
-            }
-#pragma unroll
-            for (int v = 0; v < kWarpCols / 8; ++v) {
+            auto emit8 = [&](int v, const float* a8) {   /* columns n0 + 8 v .. + 7 */
                 const int64_t n = n0 + v * 8;
                 uint32_t o[4];
 #pragma unroll
-                for (int e = 0; e < 4; ++e)
-                    o[e] = (uint32_t)rf::f32_to_bf16_bits(acc[v * 8 + 2 * e]) |
-                           ((uint32_t)rf::f32_to_bf16_bits(acc[v * 8 + 2 * e + 1]) << 16);
+                for (int e = 0; e < 4; ++e) o[e] = bf16x2(a8[2 * e], a8[2 * e + 1]);
                 if (g.bias && n < g.N) {
                     const uint4 bv = __ldg((const uint4*)(g.bias + n));
                     const uint32_t bw[4] = { bv.x, bv.y, bv.z, bv.w };
@@ -647,7 +638,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
                     for (int e = 0; e < 4; ++e) {
                         const float lo = __fadd_rn(__uint_as_float(o[e] << 16), __uint_as_float(bw[e] << 16));
                         const float hi = __fadd_rn(__uint_as_float(o[e] & 0xffff0000u), __uint_as_float(bw[e] & 0xffff0000u));
-                        o[e] = (uint32_t)rf::f32_to_bf16_bits(lo) | ((uint32_t)rf::f32_to_bf16_bits(hi) << 16);
+                        o[e] = bf16x2(lo, hi);
                     }
                 }
                 if constexpr (direct) {
@@ -656,6 +647,54 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
                     /* box v >> 3, row lane, 16-byte chunk (v & 7) at its 128-byte-swizzled place */
                     *(uint4*)(stg + (v >> 3) * kOutBox + lane * 128 + (((v & 7) ^ (lane & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
                 }
+            };
+            if (kMode != kModeI8Dump && p.folds == 1) {
+                /* one K block (per-row and per-column scales): the sums folded 32 columns a tensor-memory load and
+                 * stored as they come, the b_scale values prefetched into the warp's shared-memory slot */
+                float* sb = scale_slots + (warp - 2) * 2 * kWarpCols;
+                __syncwarp();   /* the previous tile's reads of the slot are done */
+                if (lane < kWarpCols / 4) {
+                    const bool in = n0 + lane * 4 < g.N;   /* N is a multiple of 16 */
+                    rf::cp_async16_zfill(sb + lane * 4, g.b_scale + (in ? n0 + lane * 4 : 0), in ? 16u : 0u);
+                }
+                const float sa = row_live ? g.a_scale[m * g.ldas] : 0.0f;
+                const uint32_t buf = fold & 1, use = (fold >> 1) & 1;
+                ++fold;
+                if (!(ok = rf::mbar_wait(&acc_full[buf], use, abort, rf::kErrGemmWaitEpilogue))) break;
+                rf::cp_async_wait_all();
+                if constexpr (!direct) {
+                    if (lane == 0) rf::bulk_store_wait_read();
+                }
+                __syncwarp();
+                rf::tc_fence_after();
+#pragma unroll 1
+                for (int h = 0; h < kWarpCols / 32; ++h) {
+                    uint32_t r[32];
+                    rf::tmem_ld32(lane_addr + buf * BN + h * 32, r);
+                    rf::tmem_ld_wait();
+                    if (h == kWarpCols / 32 - 1) {   /* the accumulator's last read: back to the MMA warp */
+                        rf::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) rf::mbar_arrive_cluster_relaxed(rf::map_rank(rf::smem_addr(&acc_empty[buf]), 0));
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        float a8[8] = {};
+                        fold8(*(const uint32_t(*)[8])(r + j * 8), a8, sb + (h * 4 + j) * 8, sa);
+                        emit8(h * 4 + j, a8);
+                    }
+                }
+            } else {
+                float acc[kWarpCols];
+                if (!(ok = fold_tile<kMode == kModeI8Dump>(p, acc, scale_slots + (warp - 2) * 2 * kWarpCols, lane_addr, lane, m,
+                                                             n0, row_live, fold, abort, acc_full, acc_empty)))
+                    break;
+                if constexpr (!direct) {
+                    if (lane == 0) rf::bulk_store_wait_read();
+                    __syncwarp();
+                }
+#pragma unroll
+                for (int v = 0; v < kWarpCols / 8; ++v) emit8(v, acc + v * 8);
             }
             if constexpr (direct) continue;
             rf::fence_proxy_async_smem();
