@@ -217,13 +217,14 @@ __device__ __forceinline__ void conv_out(const float (&w)[4][4], const float (&b
                                          const float (&x2)[4], const float (&x3)[4], bool is_k, bool col_live, uint16_t* dst) {
     float y[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        float u = bs[e];
-        u = fmaf(w[e][0], x0[e], u);
-        u = fmaf(w[e][1], x1[e], u);
-        u = fmaf(w[e][2], x2[e], u);
-        u = fmaf(w[e][3], x3[e], u);
-        y[e] = rf::silu(u);
+    for (int e = 0; e < 4; e += 2) {   /* two channels an instruction (packed f32x2, each rounded as the scalar fma) */
+        float u0 = bs[e], u1 = bs[e + 1];
+        rf::fma2_rn(u0, u1, w[e][0], w[e + 1][0], x0[e], x0[e + 1]);
+        rf::fma2_rn(u0, u1, w[e][1], w[e + 1][1], x1[e], x1[e + 1]);
+        rf::fma2_rn(u0, u1, w[e][2], w[e + 1][2], x2[e], x2[e + 1]);
+        rf::fma2_rn(u0, u1, w[e][3], w[e + 1][3], x3[e], x3[e + 1]);
+        y[e] = rf::silu(u0);
+        y[e + 1] = rf::silu(u1);
     }
     if (is_k) {
         float ss = 0.0f;
@@ -232,8 +233,8 @@ __device__ __forceinline__ void conv_out(const float (&w)[4][4], const float (&b
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         const float inv = rsqrtf(ss + 1e-6f);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) y[e] = __fmul_rn(y[e], inv);
+        rf::mul2_rn(y[0], y[1], y[0], y[1], inv, inv);
+        rf::mul2_rn(y[2], y[3], y[2], y[3], inv, inv);
     }
     if (col_live) *(uint2*)dst = make_uint2(bf16x2(y[0], y[1]), bf16x2(y[2], y[3]));
 }
