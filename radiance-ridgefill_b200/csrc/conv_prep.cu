@@ -90,6 +90,43 @@ __device__ void gate_rows(const RidgeFillConvPrep& g, int64_t r0, int64_t r1, in
     }
 }
 
+/* The gates alone (columns == 0: ridgefill_gdn_in_proj has written k and v): a warp per 16-row block, a lane per
+ * v-head; when the block lies in one sequence, eight rows' a and b are in flight before their arithmetic. The same
+ * per-element arithmetic as gate_rows. */
+__global__ void __launch_bounds__(kThreads, 4) gate_kernel(RidgeFillConvPrep g) {
+    const int lane = threadIdx.x & 31;
+    const int64_t blocks = (g.T + kRows - 1) / kRows, stride = (int64_t)gridDim.x * (kThreads / 32);
+    for (int64_t blk = (int64_t)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); blk < blocks; blk += stride) {
+        const int64_t r0 = blk * kRows, r1 = min(r0 + kRows, g.T);
+        int64_t s0 = 0, e0 = 0;
+        const int seq0 = find_seq(g, r0, &s0, &e0);
+        if (seq0 < 0 || e0 < r1) {   /* sequence boundaries or rows outside every sequence inside the block */
+            gate_rows(g, r0, r1, lane);
+            continue;
+        }
+        for (int64_t h = lane; h < g.n_head_v; h += 32) {
+            const float neg_a = -expf(g.a_log[h]), dtb = g.dt_bias[h];
+            for (int64_t q0 = r0; q0 < r1; q0 += 8) {
+                const int n = (int)min((int64_t)8, r1 - q0);
+                uint16_t ab[8], bb[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    if (i < n) {
+                        ab[i] = __ldg(g.a + (q0 + i) * g.a_row + h);
+                        bb[i] = __ldg(g.b + (q0 + i) * g.b_row + h);
+                    }
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    if (i < n) {
+                        const int64_t r = q0 + i;
+                        g.g[r * g.g_row + h] = neg_a * ridgefill_softplus(rf::bf16_bits_to_f32(ab[i]) + dtb);
+                        g.beta[r * g.beta_row + h] = 1.0f / (1.0f + expf(-rf::bf16_bits_to_f32(bb[i])));
+                    }
+            }
+        }
+    }
+}
+
 /* Tasks of kRows rows: per row block, one task per computed 128-channel head column (a warp; lane l channels
  * 4 l..4 l + 3) and one gate task (gate_rows). The block's tasks are consecutive, so the warps of a wave share
  * rows. In a head task the convolution's three earlier rows ride in registers; when the rows lie in one sequence
@@ -248,7 +285,10 @@ extern "C" int ridgefill_gdn_conv_prep_device(const RadArgs* a, RadStream s) {
     cudaStream_t stream = rf::as_stream(s);
     const int64_t C = 2 * g.n_head_k * 128 + g.n_head_v * 128;
     const int64_t tasks = (g.T + kRows - 1) / kRows * ((g.columns ? C / 128 - (g.q ? 0 : g.n_head_k) : 0) + 1);
-    if (tasks > 0) {
+    if (!g.columns && tasks > 0) {
+        const int64_t blocks = (tasks + kThreads / 32 - 1) / (kThreads / 32), cap = (int64_t)rf::sm_count() * 8;
+        gate_kernel<<<(unsigned)(blocks < cap ? blocks : cap), kThreads, 0, stream>>>(g);
+    } else if (tasks > 0) {
         static int per_sm = 0;   /* resident CTAs a SM (registers and the 32 KiB stage bound it) */
         if (!per_sm) {
             if (cudaFuncSetAttribute(conv_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kStageBytes) != cudaSuccess ||

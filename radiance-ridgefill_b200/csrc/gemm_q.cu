@@ -543,6 +543,12 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
                 const int64_t n0 = (int64_t)(tile % p.n_tiles) * kBN + slice * kWarpCols;
                 const uint32_t buf = fold & 1, use = (fold >> 1) & 1;
                 if (!(ok = rf::mbar_wait(&acc_full[buf], use, abort, rf::kErrGemmWaitEpilogue))) break;
+                if (n0 >= gb.N) {   /* a slice past y's last column (the narrow form's slices 1-3): nothing to write */
+                    rf::tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) rf::mbar_arrive_cluster_relaxed(rf::map_rank(rf::smem_addr(&acc_empty[buf]), 0));
+                    continue;
+                }
                 rf::tc_fence_after();
                 uint8_t* stg = stage_out + (warp - 2) * kBoxes * kOutBox;
                 if (lane == 0) rf::bulk_store_wait_read();
