@@ -113,11 +113,30 @@ __device__ __forceinline__ void fold8(const uint32_t (&r)[8], float* acc8, const
     }
 }
 
+/* fold8 for a K block of at most 256 columns, whose sums stay below 2^22 in magnitude (256 x 127 x 127): the exact
+ * int -> float conversion by the 1.5 x 2^23 bias (the sum added to the bias's bit pattern is the float bias + sum,
+ * in one binade, and subtracting the bias is exact), on the integer and f32x2 pipes rather than the converter. */
+__device__ __forceinline__ void fold8_small(const uint32_t (&r)[8], float* acc8, const float* sb8, float sa) {
+    const float4 s0 = *(const float4*)sb8, s1 = *(const float4*)(sb8 + 4);
+    const float sv[8] = { s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w };
+    constexpr uint32_t kBiasBits = 0x4B400000u;   /* 12582912.0f = 1.5 x 2^23 */
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+        float d0, d1, t0, t1;
+        rf::add2_rn(d0, d1, __uint_as_float(kBiasBits + r[e]), __uint_as_float(kBiasBits + r[e + 1]), -12582912.0f,
+                    -12582912.0f);
+        rf::mul2_rn(t0, t1, d0, d1, sa, sa);
+        rf::fma2_rn(acc8[e], acc8[e + 1], t0, t1, sv[e], sv[e + 1]);
+    }
+}
+
 /* One finished K block (the lane's kWarpCols accumulator columns at `taddr`) folded into its f32 sums, eight
- * columns a tensor-memory load. kDump: also the block's int32 sums into g.acc (the optional acc operand). */
+ * columns a tensor-memory load. kDump: also the block's int32 sums into g.acc (the optional acc operand). small:
+ * the block is at most 256 columns (fold8_small's conversion). */
 template <bool kDump>
 __device__ __forceinline__ void fold_block(uint32_t taddr, float (&acc)[kWarpCols], const float* sb, float sa,
-                                           const RidgeFillGemmQ& g, int64_t m, int64_t n0, bool row_live, int f, int blocks) {
+                                           const RidgeFillGemmQ& g, int64_t m, int64_t n0, bool row_live, int f, int blocks,
+                                           bool small) {
 #pragma unroll
     for (int c = 0; c < kWarpCols / 8; ++c) {
         uint32_t r[8];
@@ -126,7 +145,8 @@ __device__ __forceinline__ void fold_block(uint32_t taddr, float (&acc)[kWarpCol
         if (kDump && row_live)
             for (int i = 0; i < 8; ++i)
                 if (n0 + c * 8 + i < g.N) g.acc[(m * g.N + n0 + c * 8 + i) * blocks + f] = (int32_t)r[i];
-        fold8(r, acc + c * 8, sb + c * 8, sa);
+        if (small) fold8_small(r, acc + c * 8, sb + c * 8, sa);
+        else fold8(r, acc + c * 8, sb + c * 8, sa);
     }
 }
 
@@ -188,7 +208,7 @@ __device__ __forceinline__ bool fold_tile(const GemmPlan& p, float (&acc)[kWarpC
         }
         if (!rf::mbar_wait(&acc_full[buf], use, abort, rf::kErrGemmWaitEpilogue)) return false;
         rf::tc_fence_after();
-        fold_block<kDump>(lane_addr + buf * BN, acc, sb, sa, g, m, n0, row_live, f, p.folds);
+        fold_block<kDump>(lane_addr + buf * BN, acc, sb, sa, g, m, n0, row_live, f, p.folds, p.steps_per_fold <= 2);
         rf::tc_fence_before();
         __syncwarp();
         if (lane == 0) rf::mbar_arrive_cluster_relaxed(rf::map_rank(rf::smem_addr(&acc_empty[buf]), 0));
