@@ -113,30 +113,11 @@ __device__ __forceinline__ void fold8(const uint32_t (&r)[8], float* acc8, const
     }
 }
 
-/* fold8 for a K block of at most 256 columns, whose sums stay below 2^22 in magnitude (256 x 127 x 127): the exact
- * int -> float conversion by the 1.5 x 2^23 bias (the sum added to the bias's bit pattern is the float bias + sum,
- * in one binade, and subtracting the bias is exact), on the integer and f32x2 pipes rather than the converter. */
-__device__ __forceinline__ void fold8_small(const uint32_t (&r)[8], float* acc8, const float* sb8, float sa) {
-    const float4 s0 = *(const float4*)sb8, s1 = *(const float4*)(sb8 + 4);
-    const float sv[8] = { s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w };
-    constexpr uint32_t kBiasBits = 0x4B400000u;   /* 12582912.0f = 1.5 x 2^23 */
-#pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-        float d0, d1, t0, t1;
-        rf::add2_rn(d0, d1, __uint_as_float(kBiasBits + r[e]), __uint_as_float(kBiasBits + r[e + 1]), -12582912.0f,
-                    -12582912.0f);
-        rf::mul2_rn(t0, t1, d0, d1, sa, sa);
-        rf::fma2_rn(acc8[e], acc8[e + 1], t0, t1, sv[e], sv[e + 1]);
-    }
-}
-
 /* One finished K block (the lane's kWarpCols accumulator columns at `taddr`) folded into its f32 sums, eight
- * columns a tensor-memory load. kDump: also the block's int32 sums into g.acc (the optional acc operand). small:
- * the block is at most 256 columns (fold8_small's conversion). */
+ * columns a tensor-memory load. kDump: also the block's int32 sums into g.acc (the optional acc operand). */
 template <bool kDump>
 __device__ __forceinline__ void fold_block(uint32_t taddr, float (&acc)[kWarpCols], const float* sb, float sa,
-                                           const RidgeFillGemmQ& g, int64_t m, int64_t n0, bool row_live, int f, int blocks,
-                                           bool small) {
+                                           const RidgeFillGemmQ& g, int64_t m, int64_t n0, bool row_live, int f, int blocks) {
 #pragma unroll
     for (int c = 0; c < kWarpCols / 8; ++c) {
         uint32_t r[8];
@@ -145,8 +126,7 @@ __device__ __forceinline__ void fold_block(uint32_t taddr, float (&acc)[kWarpCol
         if (kDump && row_live)
             for (int i = 0; i < 8; ++i)
                 if (n0 + c * 8 + i < g.N) g.acc[(m * g.N + n0 + c * 8 + i) * blocks + f] = (int32_t)r[i];
-        if (small) fold8_small(r, acc + c * 8, sb + c * 8, sa);
-        else fold8(r, acc + c * 8, sb + c * 8, sa);
+        fold8(r, acc + c * 8, sb + c * 8, sa);
     }
 }
 
@@ -154,7 +134,11 @@ __device__ __forceinline__ void fold_block(uint32_t taddr, float (&acc)[kWarpCol
  * (the optional acc operand), the int8 projector writing only the selected rows (the optional rows operand), and
  * the DeltaNet in-projection with the convolution in its epilogue. Separate instantiations keep each form's
  * registers to itself. */
-enum GemmMode { kModeBf16 = 0, kModeI8 = 1, kModeI8Dump = 2, kModeI8Rows = 3, kModeI8Conv = 4, kModeBf16Narrow = 5, kModeCount = 6 };
+enum GemmMode {
+    kModeBf16 = 0, kModeI8 = 1, kModeI8Dump = 2, kModeI8Rows = 3, kModeI8Conv = 4, kModeBf16Narrow = 5,
+    kModeI8One = 6, kModeI8RowsOne = 7,   /* kModeI8 / kModeI8Rows with one K block (group = K): the streamed fold */
+    kModeCount = 8
+};
 
 /* A pair tile's columns: 256, or 64 for the narrow bf16 form (N <= 64, e.g. the DeltaNet a|b projection), whose
  * M256 N64 products leave the MMAs a quarter of the wide form's work when it would mostly multiply zero rows. */
@@ -208,7 +192,7 @@ __device__ __forceinline__ bool fold_tile(const GemmPlan& p, float (&acc)[kWarpC
         }
         if (!rf::mbar_wait(&acc_full[buf], use, abort, rf::kErrGemmWaitEpilogue)) return false;
         rf::tc_fence_after();
-        fold_block<kDump>(lane_addr + buf * BN, acc, sb, sa, g, m, n0, row_live, f, p.folds, p.steps_per_fold <= 2);
+        fold_block<kDump>(lane_addr + buf * BN, acc, sb, sa, g, m, n0, row_live, f, p.folds);
         rf::tc_fence_before();
         __syncwarp();
         if (lane == 0) rf::mbar_arrive_cluster_relaxed(rf::map_rank(rf::smem_addr(&acc_empty[buf]), 0));
@@ -431,6 +415,34 @@ __device__ __forceinline__ bool conv_epilogue(const GemmPlan& p, uint8_t* rows_t
     return true;
 }
 
+/* Eight bf16 columns n0 + 8 v .. + 7 of a lane's row (its f32 sums a8), the bias added and rounded again, into the
+ * warp's staging tile (box v >> 3, row lane, 16-byte chunk v & 7 at its 128-byte-swizzled place) or, direct, into
+ * the row of y itself when the row is selected. The hardware's round to nearest even: the fold's rounding for every
+ * value but a NaN (made the canonical one). */
+template <bool kDirect>
+__device__ __forceinline__ void emit8(const RidgeFillGemmQ& g, uint8_t* stg, bool write_row, int64_t m, int64_t n0, int lane, int v,
+                                      const float* a8) {
+    const int64_t n = n0 + v * 8;
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] = bf16x2(a8[2 * e], a8[2 * e + 1]);
+    if (g.bias && n < g.N) {
+        const uint4 bv = __ldg((const uint4*)(g.bias + n));
+        const uint32_t bw[4] = { bv.x, bv.y, bv.z, bv.w };
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float lo = __fadd_rn(__uint_as_float(o[e] << 16), __uint_as_float(bw[e] << 16));
+            const float hi = __fadd_rn(__uint_as_float(o[e] & 0xffff0000u), __uint_as_float(bw[e] & 0xffff0000u));
+            o[e] = bf16x2(lo, hi);
+        }
+    }
+    if constexpr (kDirect) {
+        if (write_row && n < g.N) *(uint4*)(g.y + m * g.ldy + n) = make_uint4(o[0], o[1], o[2], o[3]);
+    } else {
+        *(uint4*)(stg + (v >> 3) * kOutBox + lane * 128 + (((v & 7) ^ (lane & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
 template <int kMode>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(threads_of<kMode>(), 1)
 gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -647,37 +659,14 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
             const int64_t n0 = (int64_t)(tile % p.n_tiles) * BN + slice * kWarpCols;
             const bool row_live = m < g.M;
             /* bf16 (and the bias) into this warp's staging tiles, once the previous tile's stores have read them; or,
-             * with a row selection, straight from the lanes into the selected rows of y (a lane is one row). The
-             * hardware's round to nearest even: the fold's rounding for every value but a NaN (made the canonical
-             * one). */
-            uint8_t* stg = stage_out + (warp - 2) * kBoxes * kOutBox;
-            constexpr bool direct = kMode == kModeI8Rows;
-            const bool write_row = direct && row_live && __ldg(g.rows + m) == 1;
-            auto emit8 = [&](int v, const float* a8) {   /* columns n0 + 8 v .. + 7 */
-                const int64_t n = n0 + v * 8;
-                uint32_t o[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) o[e] = bf16x2(a8[2 * e], a8[2 * e + 1]);
-                if (g.bias && n < g.N) {
-                    const uint4 bv = __ldg((const uint4*)(g.bias + n));
-                    const uint32_t bw[4] = { bv.x, bv.y, bv.z, bv.w };
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float lo = __fadd_rn(__uint_as_float(o[e] << 16), __uint_as_float(bw[e] << 16));
-                        const float hi = __fadd_rn(__uint_as_float(o[e] & 0xffff0000u), __uint_as_float(bw[e] & 0xffff0000u));
-                        o[e] = bf16x2(lo, hi);
-                    }
-                }
-                if constexpr (direct) {
-                    if (write_row && n < g.N) *(uint4*)(g.y + m * g.ldy + n) = make_uint4(o[0], o[1], o[2], o[3]);
-                } else {
-                    /* box v >> 3, row lane, 16-byte chunk (v & 7) at its 128-byte-swizzled place */
-                    *(uint4*)(stg + (v >> 3) * kOutBox + lane * 128 + (((v & 7) ^ (lane & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-                }
-            };
-            if (kMode != kModeI8Dump && p.folds == 1) {
+             * with a row selection, straight from the lanes into the selected rows of y (a lane is one row). */
+            constexpr bool direct = kMode == kModeI8Rows || kMode == kModeI8RowsOne;
+            constexpr bool kOne = kMode == kModeI8One || kMode == kModeI8RowsOne;
+            if constexpr (kOne) {
+                uint8_t* stg = stage_out + (warp - 2) * kBoxes * kOutBox;
                 /* one K block (per-row and per-column scales): the sums folded 32 columns a tensor-memory load and
                  * stored as they come, the b_scale values prefetched into the warp's shared-memory slot */
+                const bool write_row = direct && row_live && __ldg(g.rows + m) == 1;
                 float* sb = scale_slots + (warp - 2) * 2 * kWarpCols;
                 __syncwarp();   /* the previous tile's reads of the slot are done */
                 if (lane < kWarpCols / 4) {
@@ -708,7 +697,7 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
                     for (int j = 0; j < 4; ++j) {
                         float a8[8] = {};
                         fold8(*(const uint32_t(*)[8])(r + j * 8), a8, sb + (h * 4 + j) * 8, sa);
-                        emit8(h * 4 + j, a8);
+                        emit8<direct>(g, stg, write_row, m, n0, lane, h * 4 + j, a8);
                     }
                 }
             } else {
@@ -716,13 +705,38 @@ gemm_q_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__
                 if (!(ok = fold_tile<kMode == kModeI8Dump>(p, acc, scale_slots + (warp - 2) * 2 * kWarpCols, lane_addr, lane, m,
                                                              n0, row_live, fold, abort, acc_full, acc_empty)))
                     break;
+                uint8_t* stg = stage_out + (warp - 2) * kBoxes * kOutBox;
+                const bool write_row = direct && row_live && __ldg(g.rows + m) == 1;
                 if constexpr (!direct) {
                     if (lane == 0) rf::bulk_store_wait_read();
                     __syncwarp();
                 }
 #pragma unroll
-                for (int v = 0; v < kWarpCols / 8; ++v) emit8(v, acc + v * 8);
+                for (int v = 0; v < kWarpCols / 8; ++v) {
+                    const int64_t n = n0 + v * 8;
+                    uint32_t o[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e)
+                        o[e] = (uint32_t)rf::f32_to_bf16_bits(acc[v * 8 + 2 * e]) |
+                               ((uint32_t)rf::f32_to_bf16_bits(acc[v * 8 + 2 * e + 1]) << 16);
+                    if (g.bias && n < g.N) {
+                        const uint4 bv = __ldg((const uint4*)(g.bias + n));
+                        const uint32_t bw[4] = { bv.x, bv.y, bv.z, bv.w };
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float lo = __fadd_rn(__uint_as_float(o[e] << 16), __uint_as_float(bw[e] << 16));
+                            const float hi = __fadd_rn(__uint_as_float(o[e] & 0xffff0000u), __uint_as_float(bw[e] & 0xffff0000u));
+                            o[e] = (uint32_t)rf::f32_to_bf16_bits(lo) | ((uint32_t)rf::f32_to_bf16_bits(hi) << 16);
+                        }
+                    }
+                    if constexpr (direct) {
+                        if (write_row && n < g.N) *(uint4*)(g.y + m * g.ldy + n) = make_uint4(o[0], o[1], o[2], o[3]);
+                    } else {
+                        *(uint4*)(stg + (v >> 3) * kOutBox + lane * 128 + (((v & 7) ^ (lane & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                    }
+                }
             }
+            uint8_t* stg = stage_out + (warp - 2) * kBoxes * kOutBox;
             if constexpr (direct) continue;
             rf::fence_proxy_async_smem();
             __syncwarp();
@@ -1048,8 +1062,10 @@ int launch_gemm(const RidgeFillGemmQ& g, cudaStream_t stream) {
     p.folds = (int)(g.K / g.group);
     p.steps_per_fold = (int)(g.group / BK);
     if (g.acc) return launch_pairs<kModeI8Dump>(map_a, map_b, map_y, p, stream);
-    if (g.rows) return launch_pairs<kModeI8Rows>(map_a, map_b, map_y, p, stream);
-    return launch_pairs<kModeI8>(map_a, map_b, map_y, p, stream);
+    const bool one = p.folds == 1;   /* per-row and per-column scales: the streamed one-block fold */
+    if (g.rows) return one ? launch_pairs<kModeI8RowsOne>(map_a, map_b, map_y, p, stream)
+                           : launch_pairs<kModeI8Rows>(map_a, map_b, map_y, p, stream);
+    return one ? launch_pairs<kModeI8One>(map_a, map_b, map_y, p, stream) : launch_pairs<kModeI8>(map_a, map_b, map_y, p, stream);
 }
 
 /* The in-projection: 250-row pair tiles (each CTA's 128 rows start 3 before its 125 output rows), one fold a
