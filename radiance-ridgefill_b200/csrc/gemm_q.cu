@@ -878,12 +878,15 @@ __device__ __forceinline__ uint2 quant_chunk8(uint4 v, float sc, float inv) {
     uint32_t rb[8];
     bool near = false;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-        const float xv = __uint_as_float((e & 1) ? (vw[e >> 1] & 0xffff0000u) : (vw[e >> 1] << 16));
-        const float y = fmaf(xv, inv, kMagic);
-        const float d = fmaf(xv, inv, -(y - kMagic));
-        near |= !(fabsf(d) <= 0.5f - 0x1p-15f);
-        rb[e] = __float_as_uint(y);
+    for (int p = 0; p < 4; ++p) {   /* elements 2 p, 2 p + 1 two an instruction (packed f32x2, the same roundings) */
+        const float x0 = __uint_as_float(vw[p] << 16), x1 = __uint_as_float(vw[p] & 0xffff0000u);
+        float y0 = kMagic, y1 = kMagic, d0, d1;
+        rf::fma2_rn(y0, y1, x0, x1, inv, inv);                  /* y = x inv + 1.5 2^23 */
+        rf::sub2_rn(d0, d1, kMagic, kMagic, y0, y1);            /* -(y - 1.5 2^23), exact */
+        rf::fma2_rn(d0, d1, x0, x1, inv, inv);                  /* e = x inv - (y - 1.5 2^23) */
+        near |= !(fabsf(d0) <= 0.5f - 0x1p-15f) | !(fabsf(d1) <= 0.5f - 0x1p-15f);
+        rb[2 * p] = __float_as_uint(y0);
+        rb[2 * p + 1] = __float_as_uint(y1);
     }
     if (near) {
 #pragma unroll
@@ -960,15 +963,17 @@ __global__ void __launch_bounds__(kQStageThreads) quant_stage_kernel(RidgeFillQu
         rf::cp_async_wait<1>();   /* this item's copies are in */
         __syncwarp();
         const uint4* cur = slots + slot * NV * 32;
-        float amax = 0.0f;
+        /* absmax two values an instruction: the magnitudes' bf16 pairs (sign bits cleared) by the bf16x2 max, whose
+         * result is one of its inputs (exact); a NaN is passed over as fmaxf passes it */
+        __nv_bfloat162 m2 = __floats2bfloat162_rn(0.0f, 0.0f);
 #pragma unroll 4
         for (int i = 0; i < NV; ++i) {
             const uint4 v = cur[lane + 32 * i];
-            const uint32_t vw[4] = { v.x, v.y, v.z, v.w };
+            const uint32_t vw[4] = { v.x & 0x7fff7fffu, v.y & 0x7fff7fffu, v.z & 0x7fff7fffu, v.w & 0x7fff7fffu };
 #pragma unroll
-            for (int e = 0; e < 4; ++e)
-                amax = fmaxf(amax, fmaxf(fabsf(__uint_as_float(vw[e] << 16)), fabsf(__uint_as_float(vw[e] & 0xffff0000u))));
+            for (int e = 0; e < 4; ++e) m2 = __hmax2(m2, *(const __nv_bfloat162*)&vw[e]);
         }
+        float amax = fmaxf(__low2float(m2), __high2float(m2));
         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
         const int64_t m = w / groups, j = w - m * groups;
         const float sc = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 127.0f);

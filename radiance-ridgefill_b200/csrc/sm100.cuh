@@ -308,6 +308,12 @@ __device__ __forceinline__ float silu(float u) {
     return u * r;
 }
 
+__device__ __forceinline__ void sub2_rn(float& d0, float& d1, float x0, float x1, float y0, float y1) {   /* d = x - y */
+    asm("{\n .reg .b64 d, x, y;\n mov.b64 x, {%2, %3};\n mov.b64 y, {%4, %5};\n sub.rn.f32x2 d, x, y;\n"
+        " mov.b64 {%0, %1}, d;\n}"
+        : "=f"(d0), "=f"(d1) : "f"(x0), "f"(x1), "f"(y0), "f"(y1));
+}
+
 __device__ __forceinline__ void mul2_rn(float& d0, float& d1, float x0, float x1, float y0, float y1) {
     asm("{\n .reg .b64 d, x, y;\n mov.b64 x, {%2, %3};\n mov.b64 y, {%4, %5};\n mul.rn.f32x2 d, x, y;\n"
         " mov.b64 {%0, %1}, d;\n}"
