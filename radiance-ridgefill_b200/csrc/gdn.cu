@@ -1144,7 +1144,6 @@ struct HdSmem {
         uint16_t tmp[4][16][24];
         __device__ uint16_t* tile() { return &l16[0][0]; }
     } work[2];
-    float raw[2][32][36];        /* by group: K K^T rows 32-63 x columns 0-31 as f32 (padded rows: no bank conflict) */
     struct Meta {
         float gl[4];             /* gamma_L = exp(G_L) */
     } meta[2];                   /* by chunk parity: the chain's lanes read it after the stage may be reused; the
@@ -1434,36 +1433,24 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                 if (gt == 0) mt.gl[0] = __expf(gl);
                 rf::tc_fence_after();
                 if (lw < 2) {
-                    /* A's rows: thread = row i (lane quarter lw), its 32 columns jlo.. in one tensor-memory load. Warp
-                     * 1's rows 32-63 x columns 0-31 (a full block below the diagonal) go to the raw tile first, for
-                     * warps 2 and 3 to form; warp 0's columns 32-63 lie above its rows: zeros, no product read. */
+                    /* A's rows: thread = row i (lane quarter lw), its 64 columns from tensor memory, 32 at a time */
                     const int i = 32 * lw + l;
                     const bool rowin = i < len;
                     const float Gi = sg.G[i], bi = sg.b[i];
                     const uint32_t base = tmem + ((uint32_t)(32 * lw) << 16) + kHdKk;
-                    const int jlo = 32 * lw, jhi = 32 * lw + 32;   /* the columns this warp forms */
-                    if (lw == 1) {
-                        const uint32_t rrow = rf::saddr(&s.raw[grp][l][0]);
-                        uint32_t kr[32];
-                        rf::tmem_ld32(base, kr);
-                        rf::tmem_ld_wait();
-#pragma unroll
-                        for (int c4 = 0; c4 < 8; ++c4)
-                            sts128(rrow + 16 * c4, make_uint4(kr[4 * c4], kr[4 * c4 + 1], kr[4 * c4 + 2], kr[4 * c4 + 3]));
-                        rf::bar_arrive(3 + grp, 96);   /* warps 2 and 3 may read it */
-                    }
-                    uint32_t kk[32];   /* this warp's 32 columns, one tensor-memory load */
-                    rf::tmem_ld32(base + jlo, kk);
-                    rf::tmem_ld_wait();
-                    rf::tc_fence_before();
-                    __syncwarp();
-                    if (l == 0) rf::mbar_arrive(&s.kk_free);   /* the next chunk's K K^T may overwrite it */
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int j0 = jlo + 16 * h;
+#pragma unroll 1
+                    for (int j0 = 0; j0 < C; j0 += 16) {
                         float gv[16];   /* G of the 16 columns, in registers (no load between the stores below) */
 #pragma unroll
                         for (int x = 0; x < 4; ++x) *(float4*)&gv[4 * x] = *(const float4*)&sg.G[j0 + 4 * x];
+                        uint32_t kk[16];
+                        rf::tmem_ld16(base + j0, kk);
+                        rf::tmem_ld_wait();
+                        if (j0 + 16 == C) {
+                            rf::tc_fence_before();
+                            __syncwarp();
+                            if (l == 0) rf::mbar_arrive(&s.kk_free);   /* the next chunk's K K^T may overwrite it */
+                        }
                         uint32_t pk[8];
 #pragma unroll
                         for (int jj = 0; jj < 16; jj += 2) {
@@ -1471,17 +1458,13 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                             float v[2];
 #pragma unroll
                             for (int e = 0; e < 2; ++e)
-                                v[e] = (jc + e < i && rowin) ? bi * __expf(Gi - gv[jj + e]) * __uint_as_float(kk[16 * h + jj + e])
-                                                             : 0.0f;
+                                v[e] = (jc + e < i && rowin) ? bi * __expf(Gi - gv[jj + e]) * __uint_as_float(kk[jj + e]) : 0.0f;
                             pk[jj >> 1] = rf::pack_f16(v[0], v[1]);
                             if ((jc >> 4) == (i >> 4)) *(float2*)&wk.a32[i >> 4][i & 15][jc & 15] = make_float2(v[0], v[1]);
                         }
                         *(uint4*)&wk.l16[i][j0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                         *(uint4*)&wk.l16[i][j0 + 8] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
                     }
-                    if (lw == 0)   /* columns 32-63 lie above rows 0-31 */
-#pragma unroll
-                        for (int j0 = 32; j0 < C; j0 += 8) *(uint4*)&wk.l16[i][j0] = make_uint4(0u, 0u, 0u, 0u);
                 } else {
                     /* x1 = beta gamma k in place and K~ = exp(G_L - G) k into this parity's tile: thread = row r */
                     const int r = gt - 64;
@@ -1504,32 +1487,6 @@ gdn_fill_heads_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
                             sts128(ktile + off[it], scale_bf16x8_to_f16(kr[it], fx, in));
                         }
                     }
-                    /* A's rows 32-63 x columns 0-31 from warp 1's raw tile: warp lw, rows 32 + 16 (lw - 2) + (l & 15),
-                     * columns 16 (l >> 4) .. + 15 (all below the diagonal); the same arithmetic as warp 1's */
-                    rf::bar_sync(3 + grp, 96);
-                    const int i = 32 + 16 * (lw - 2) + (l & 15), jb = 16 * (l >> 4);
-                    const bool rowin = i < len;
-                    const float Gi = sg.G[i], bi = sg.b[i];
-                    const uint32_t rrow = rf::saddr(&s.raw[grp][i - 32][jb]);
-                    uint4 kv[4];
-#pragma unroll
-                    for (int c4 = 0; c4 < 4; ++c4) kv[c4] = lds128(rrow + 16 * c4);
-                    float gv[16];
-#pragma unroll
-                    for (int x = 0; x < 4; ++x) *(float4*)&gv[4 * x] = *(const float4*)&sg.G[jb + 4 * x];
-                    const uint32_t kk[16] = { kv[0].x, kv[0].y, kv[0].z, kv[0].w, kv[1].x, kv[1].y, kv[1].z, kv[1].w,
-                                              kv[2].x, kv[2].y, kv[2].z, kv[2].w, kv[3].x, kv[3].y, kv[3].z, kv[3].w };
-                    uint32_t pk[8];
-#pragma unroll
-                    for (int jj = 0; jj < 16; jj += 2) {
-                        float v[2];
-#pragma unroll
-                        for (int e = 0; e < 2; ++e)
-                            v[e] = rowin ? bi * __expf(Gi - gv[jj + e]) * __uint_as_float(kk[jj + e]) : 0.0f;
-                        pk[jj >> 1] = rf::pack_f16(v[0], v[1]);
-                    }
-                    *(uint4*)&wk.l16[i][jb] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                    *(uint4*)&wk.l16[i][jb + 8] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
                 }
                 psync();
                 /* diagonal blocks of T by substitution in f32: warp lw block lw, lane l row l & 15 of 8 columns */

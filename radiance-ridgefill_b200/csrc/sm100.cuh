@@ -289,11 +289,6 @@ __device__ __forceinline__ void bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-/* Arrive at named barrier `id` (of `threads` threads) without waiting: the producer's side of a bar_sync. */
-__device__ __forceinline__ void bar_arrive(int id, int threads) {
-    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
 /* Named barrier `id` over `threads` threads that also ORs `pred` across them: every thread gets the same answer. */
 __device__ __forceinline__ bool bar_any(int id, int threads, bool pred) {
     uint32_t r;
