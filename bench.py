@@ -291,14 +291,16 @@ def run_mine(args):
 
     # ---------------------------------------------------------- end to end, host buffers in and out
     # Two buffer sets (two passes' buffers) and three streams: step i+1's upload and step i-1's readback run on the
-    # copy engines while step i computes; a set is reused only after its previous pass and readback.
+    # copy engines while step i computes; a set is reused only after its previous pass and readback. The results
+    # final before the fill (the attention caches, the conv states, the mask) are read back while the fill runs,
+    # the rest once the pass is done.
     sets = [p, LP.LatePass(shape, str(dev), seed=4321, team=team)]
     ins = [s_.inputs_per_step() for s_ in sets]
-    outs = [s_.results() for s_ in sets]
+    outs = [s_.results_split() for s_ in sets]
     host_in = [t.cpu().pin_memory() for t in ins[0]]
-    host_out = [[torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in o] for o in outs]
+    host_out = [tuple([torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in part] for part in o) for o in outs]
     h2d = sum(t.numel() * t.element_size() for t in host_in)
-    d2h = sum(t.numel() * t.element_size() for t in host_out[0])
+    d2h = sum(t.numel() * t.element_size() for part in host_out[0] for t in part)
     s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
 
     def e2e_steps(n, start_event=None, end_event=None):
@@ -317,14 +319,17 @@ def run_mine(args):
             stream.wait_event(ev_in)
             if done_out[b_] is not None:
                 stream.wait_event(done_out[b_])
+            blocks_done = torch.cuda.Event()
             with torch.cuda.stream(stream):
-                sets[b_].run(stream.cuda_stream)
+                sets[b_].run(stream.cuda_stream, before_tail=lambda: blocks_done.record(stream))
             done_comp[b_] = torch.cuda.Event()
             done_comp[b_].record(stream)
             with torch.cuda.stream(s_out):
-                s_out.wait_event(done_comp[b_])
-                for h, d_ in zip(host_out[b_], outs[b_]):
-                    h.copy_(d_, non_blocking=True)
+                for ev_, h_part, d_part in ((blocks_done, host_out[b_][0], outs[b_][0]),
+                                            (done_comp[b_], host_out[b_][1], outs[b_][1])):
+                    s_out.wait_event(ev_)
+                    for h, d_ in zip(h_part, d_part):
+                        h.copy_(d_, non_blocking=True)
                 done_out[b_] = torch.cuda.Event()
                 done_out[b_].record(s_out)
         if end_event is not None:

@@ -536,10 +536,12 @@ class LatePass:
         if rc != abi.OK:
             raise RuntimeError(f"{op}: device row refused or failed (rc {rc})")
 
-    def run(self, stream: int, events=None) -> None:
+    def run(self, stream: int, events=None, before_tail=None) -> None:
         """Issue one pass on `stream` (and, on a team, the column gathers on a second stream). `events` (optional)
         maps an op name to a list of (start, end) CUDA event pairs, one pair per launch of that op, recorded on the
-        current torch stream around each launch."""
+        current torch stream around each launch. `before_tail` (optional) is called on the host once every layer's
+        launches are on `stream` and before the fill's: work the caller queues behind `stream` at that point (an
+        event) sees `results_split()[0]` final, so their readback can overlap the fill."""
         counts = {}
 
         def emit(c):
@@ -554,12 +556,16 @@ class LatePass:
                 ev[i][1].record()
 
         if self.team is not None:
-            self._run_team(stream, emit)
+            self._run_team(stream, emit, before_tail)
             return
-        for c in self.calls:
+        for c in self.calls[:len(self.calls) - len(self.tail)]:
+            emit(c)
+        if before_tail is not None:
+            before_tail()
+        for c in self.tail:
             emit(c)
 
-    def _run_team(self, stream: int, emit) -> None:
+    def _run_team(self, stream: int, emit, before_tail=None) -> None:
         """One rank's pass: the barrier (every rank has finished its previous pass), the head of the pass, then per
         layer its projector block (into the approximated rows) on `stream` and that block's gather to the peers on the comm stream,
         while `stream` goes on with the previous layer's block (after waiting for all of its columns); the fill and
@@ -610,6 +616,8 @@ class LatePass:
         done = torch.cuda.Event()
         done.record(comm)
         main.wait_event(done)   # the last gathers read this rank's block inputs: done before the next pass writes them
+        if before_tail is not None:
+            before_tail()
         for c in self.tail:
             emit(c)
 
@@ -630,6 +638,13 @@ class LatePass:
         if self.s.block_inputs:
             out += list(self.conv_state)
         return out
+
+    def results_split(self) -> tuple[list, list]:
+        """`results()` in two parts: those final once every layer's block has run (the mask, the attention caches,
+        the conv states: nothing in the fill and after it writes them), and those the fill and the ops after it
+        write (the states, the decay sums, the hazard record)."""
+        early = [self.mask] + list(self.cache) + (list(self.conv_state) if self.s.block_inputs else [])
+        return early, [self.state, self.nd, self.meta, self.count]
 
     # --------------------------------------------------------------- algorithmic work of one pass
     def algorithmic(self) -> dict:

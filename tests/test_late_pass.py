@@ -85,3 +85,27 @@ def test_cpu_twin_runs_the_same_pass(oracle_lib):
     assert cpu.mask[:120].sum() == 0 and cpu.mask[120:].sum() > 0    # only the last sequence is approximated
     assert np.isfinite(cpu.state).all() and np.abs(cpu.nd[-1]).sum() > 0 and np.abs(cpu.nd[0]).sum() == 0
     assert (cpu.cache[0][0] != 0).any()
+
+
+@pytest.mark.parametrize("shape", SHAPES[:3], ids=["config0", "all24_small", "ragged"])
+def test_results_before_the_fill_are_final_when_the_hook_runs(shape):
+    """run(before_tail=...) calls the hook once, after every layer's launches and before the fill's; the results
+    it declares final there (mask, attention caches, conv states) are written by no launch after it (the mask is
+    only read there: rho's row mask), and the two parts together are results()."""
+    p = LP.LatePass(shape, "cpu", seed=1)
+    order = []
+    p._launch = lambda op, r, tens, params, stream: order.append(op)   # noqa: E731  (nothing is launched)
+    p.run(0, before_tail=lambda: order.append("hook"))
+    assert order.count("hook") == 1
+    at = order.index("hook")
+    assert order[at + 1] == "ridgefill_gdn_fill" and "ridgefill_gdn_fill" not in order[:at]
+    early, late = p.results_split()
+    assert sorted(map(id, early + late)) == sorted(map(id, p.results()))
+    ranges = [(t.data_ptr(), t.data_ptr() + t.numel() * t.element_size()) for t in early if t.numel()]
+    mask = p.mask.data_ptr()
+    for op, _r, tens, _p, tag in p.tail:
+        for i, a in enumerate(tens):
+            ptr = getattr(a, "data", None) or 0
+            if not ptr or not any(lo <= ptr < hi for lo, hi in ranges):
+                continue
+            assert op == "ridgefill_rho_update" and ptr == mask and i == 1, (op, tag, i)
