@@ -937,7 +937,9 @@ __global__ void __launch_bounds__(256) quant_reg_kernel(RidgeFillQuant g) {
  * 256 NV columns, the next item's columns copied asynchronously into the warp's other shared-memory slot while
  * the current one is reduced and coded (its columns read from shared memory twice: the absmax, then the codes),
  * so two items a warp are in flight with few registers (more warps a SM than the register form allows). The
- * same arithmetic (quant_chunk8). */
+ * same arithmetic (quant_chunk8). The items are taken last row first: a producer that wrote x in row order
+ * (the projector's tiles) left its last rows in L2, and what reads x next in row order finds its first rows
+ * there. */
 constexpr int kQStageThreads = 256;
 template <int NV>
 __global__ void __launch_bounds__(kQStageThreads) quant_stage_kernel(RidgeFillQuant g) {
@@ -948,7 +950,7 @@ __global__ void __launch_bounds__(kQStageThreads) quant_stage_kernel(RidgeFillQu
     const int64_t warps = (int64_t)gridDim.x * (kQStageThreads >> 5);
     int64_t w = (int64_t)blockIdx.x * (kQStageThreads >> 5) + wib;
     auto fetch = [&](int64_t item, int slot) {
-        const int64_t m = item / groups, j = item - m * groups;
+        const int64_t r = work - 1 - item, m = r / groups, j = r - m * groups;
         const uint16_t* x = g.x + m * g.ldx + j * g.group;
 #pragma unroll
         for (int i = 0; i < NV; ++i)
@@ -975,7 +977,7 @@ __global__ void __launch_bounds__(kQStageThreads) quant_stage_kernel(RidgeFillQu
         }
         float amax = fmaxf(__low2float(m2), __high2float(m2));
         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        const int64_t m = w / groups, j = w - m * groups;
+        const int64_t r = work - 1 - w, m = r / groups, j = r - m * groups;
         const float sc = amax == 0.0f ? 1.0f : __fdiv_rn(amax, 127.0f);
         if (lane == 0) g.s[m * g.lds + j] = sc;
         const float inv = __frcp_rn(sc);

@@ -12,8 +12,8 @@ launch of this library's sm_100a device rows through the C ABI.
                                     ridgefill_select fused into the projector's epilogue)
       ridgefill_quant_act_i8g       the block input's codes (what the int8 block reads)
       DeltaNet layer (arch/qwen4exp_fill.h:29-61):
+        ridgefill_gemm_nt_bias      the a|b projection (bf16; first, while the block input is still in L2)
         ridgefill_gemm_nt_q_bias    the mixed q|k|v projection (int8, no bias)
-        ridgefill_gemm_nt_bias      the a|b projection (bf16)
         ridgefill_gdn_conv_prep     conv, SiLU, q/k norm, gate and beta, into this layer's heads of the
                                     pass-wide k, v, g, beta arrays
       attention layer (arch/qwen4exp_fill.h:100-115):
@@ -443,6 +443,11 @@ class LatePass:
             if kind == "G" and s.block_inputs:
                 C, Cq = self.conv_dim_r, hk * D
                 block.append(quant(self.x[li], self.codes_x, self.scale_x, f"x {li}"))
+                # the a|b projection straight after the codes: the quantiser reads the block input last row first,
+                # so the rows it read last (the first ones) are still in L2 when this reads them in order
+                block.append(call("ridgefill_gemm_nt_bias", [_t(self.x[li]), _t(x["w_ab"][gi]), _t(self.zero_ab), A_,
+                                                             _t(self.ab[gi])],
+                                  [P("M", T), P("N", 2 * hv), P("K", d), S("dtype", "bf16")], f"ab {li}"))
                 # the mixed projection's k|v columns over every row; its q columns only over each sequence's last
                 # three rows, the conv state's (the state-only fill reads no q, so conv_prep is given none). With
                 # per-row scales the k|v projection carries the convolution, SiLU and k norm in its epilogue
@@ -472,9 +477,6 @@ class LatePass:
                                         _t(self.scale_x, [M, d // self.grp], [d // self.grp, 1], offset_elems=m0 * (d // self.grp)),
                                         self.w_in_q[gi], self.s_in_q[gi], None, _t(self.mixed, [M, Cq], [C, 1], offset_elems=m0 * C),
                                         Cq, f"in q {li}", M=M))
-                block.append(call("ridgefill_gemm_nt_bias", [_t(self.x[li]), _t(x["w_ab"][gi]), _t(self.zero_ab), A_,
-                                                             _t(self.ab[gi])],
-                                  [P("M", T), P("N", 2 * hv), P("K", d), S("dtype", "bf16")], f"ab {li}"))
                 ab = self.ab[gi]
                 block.append(call("ridgefill_gdn_conv_prep",
                                   [_t(self.mixed), _t(x["w_conv"][gi]), A_, _t(x["a_log"][gi]), _t(x["dt_bias"][gi]),
