@@ -528,6 +528,11 @@ class LatePass:
         # launch of at least 64 chains), two (plan + cooperative kernel) otherwise
         one_kernel_fill = D != 128 or G * hv * s.n_seq >= 64
         self.kernels = sum(1 if (c[0] == "ridgefill_gdn_fill" and one_kernel_fill) else self.KERNELS[c[0]] for c in self.calls)
+        # In the per-head form the fill's CTAs wait on nothing but their own SM, and a launch of L Hv chains over the
+        # SMs leaves some of them idle in its last round: the decay sums (which read only a, the mask and the bounds)
+        # run there, on a second stream, instead of after the fill. The other forms keep the tail in order (the
+        # cooperative one needs all its CTAs resident at once).
+        self.rho_beside_fill = D == 128 and G * hv * s.n_seq >= 64
         if self.team is not None:   # the barrier, one gather and one wait a layer
             self.kernels += 1 + 2 * len(s.layers)
 
@@ -546,28 +551,52 @@ class LatePass:
         event) sees `results_split()[0]` final, so their readback can overlap the fill."""
         counts = {}
 
-        def emit(c):
+        def emit(c, on=None):
             op = c[0]
             ev = events.get(op) if events else None
             if ev is not None:
                 i = counts.get(op, 0)
                 counts[op] = i + 1
                 ev[i][0].record()
-            self._launch(op, c[1], c[2], c[3], stream)
+            self._launch(op, c[1], c[2], c[3], stream if on is None else on)
             if ev is not None:
                 ev[i][1].record()
 
         if self.team is not None:
-            self._run_team(stream, emit, before_tail)
+            self._run_team(stream, emit, before_tail, beside=events is None)
             return
         for c in self.calls[:len(self.calls) - len(self.tail)]:
             emit(c)
         if before_tail is not None:
             before_tail()
+        self._issue_tail(stream, emit, beside=events is None)
+
+    def _issue_tail(self, stream: int, emit, beside: bool) -> None:
+        """The fill and what follows it. With `beside` (and the fill in its per-head form) the decay sums go on a
+        second stream that starts with the fill; the correction waits for them."""
+        if not (beside and self.rho_beside_fill):
+            for c in self.tail:
+                emit(c)
+            return
+        torch = self.torch
+        if getattr(self, "side", None) is None:
+            self.side = torch.cuda.Stream(device=self.dev)
+        main, side = torch.cuda.ExternalStream(stream, device=self.dev), self.side
+        start = torch.cuda.Event()
+        start.record(main)
+        side.wait_event(start)
+        rho_done = None
         for c in self.tail:
+            if c[0] == "ridgefill_rho_update":
+                emit(c, side.cuda_stream)
+                continue
+            if rho_done is None and c[0] != "ridgefill_gdn_fill":
+                rho_done = torch.cuda.Event()
+                rho_done.record(side)
+                main.wait_event(rho_done)
             emit(c)
 
-    def _run_team(self, stream: int, emit, before_tail=None) -> None:
+    def _run_team(self, stream: int, emit, before_tail=None, beside: bool = False) -> None:
         """One rank's pass: the barrier (every rank has finished its previous pass), the head of the pass, then per
         layer its projector block (into the approximated rows) on `stream` and that block's gather to the peers on the comm stream,
         while `stream` goes on with the previous layer's block (after waiting for all of its columns); the fill and
@@ -620,8 +649,7 @@ class LatePass:
         main.wait_event(done)   # the last gathers read this rank's block inputs: done before the next pass writes them
         if before_tail is not None:
             before_tail()
-        for c in self.tail:
-            emit(c)
+        self._issue_tail(stream, emit, beside)
 
     def op_counts(self) -> dict:
         out = {}

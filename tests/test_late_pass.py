@@ -95,7 +95,7 @@ def test_results_before_the_fill_are_final_when_the_hook_runs(shape):
     p = LP.LatePass(shape, "cpu", seed=1)
     order = []
     p._launch = lambda op, r, tens, params, stream: order.append(op)   # noqa: E731  (nothing is launched)
-    p.run(0, before_tail=lambda: order.append("hook"))
+    p.run(0, events={}, before_tail=lambda: order.append("hook"))
     assert order.count("hook") == 1
     at = order.index("hook")
     assert order[at + 1] == "ridgefill_gdn_fill" and "ridgefill_gdn_fill" not in order[:at]
@@ -109,3 +109,66 @@ def test_results_before_the_fill_are_final_when_the_hook_runs(shape):
             if not ptr or not any(lo <= ptr < hi for lo, hi in ranges):
                 continue
             assert op == "ridgefill_rho_update" and ptr == mask and i == 1, (op, tag, i)
+
+
+class _Streams:
+    """Stand-ins for torch.cuda's Stream, ExternalStream and Event that log what the pass asks of them."""
+
+    def __init__(self):
+        self.log = []
+        outer = self
+
+        class _S:
+            def __init__(self, handle):
+                self.cuda_stream = handle
+
+            def wait_event(self, e):
+                outer.log.append(("wait", self.cuda_stream, e.on))
+
+        class _E:
+            def __init__(self):
+                self.on = None
+
+            def record(self, s=None):
+                self.on = s.cuda_stream
+                outer.log.append(("record", s.cuda_stream))
+
+        class _Cuda:
+            Event = _E
+
+            @staticmethod
+            def Stream(device=None):
+                return _S(777)
+
+            @staticmethod
+            def ExternalStream(handle, device=None):
+                return _S(handle)
+
+        self.cuda = _Cuda
+
+
+@pytest.mark.parametrize("shape", SHAPES[:3], ids=["config0", "all24_small", "ragged"])
+def test_decay_sums_run_beside_the_per_head_fill(shape):
+    """With the fill in its per-head form (head dim 128, at least 64 chains), the decay sums are issued on a second
+    stream that waits for everything before the fill, and the correction waits for them; otherwise the tail stays
+    in order on the pass's stream."""
+    p = LP.LatePass(shape, "cpu", seed=1)
+    fake = _Streams()
+    p.torch = fake
+    p._launch = lambda op, r, tens, params, stream: fake.log.append(("launch", op, stream))   # noqa: E731
+    p.run(5)
+    launches = [(e[1], e[2]) for e in fake.log if e[0] == "launch"]
+    G, hv = shape.n_gdn, shape.hv
+    beside = shape.head == 128 and G * hv * shape.n_seq >= 64
+    assert p.rho_beside_fill == beside
+    rho = [st for op, st in launches if op == "ridgefill_rho_update"]
+    assert len(rho) == G and all(st == (777 if beside else 5) for st in rho)
+    assert all(st == 5 for op, st in launches if op != "ridgefill_rho_update")
+    if beside:
+        log = fake.log
+        fill = log.index(("launch", "ridgefill_gdn_fill", 5))
+        # the side stream starts from an event recorded on the pass's stream just before the fill
+        assert log[fill - 2] == ("record", 5) and log[fill - 1] == ("wait", 777, 5)
+        last_rho = max(i for i, e in enumerate(log) if e[:2] == ("launch", "ridgefill_rho_update"))
+        corr = log.index(("launch", "ridgefill_state_correct", 5), fill)
+        assert ("record", 777) in log[last_rho:corr] and ("wait", 5, 777) in log[last_rho:corr]
