@@ -565,11 +565,58 @@ class LatePass:
         if self.team is not None:
             self._run_team(stream, emit, before_tail, beside=events is None)
             return
-        for c in self.calls[:len(self.calls) - len(self.tail)]:
+        for c in self.head:
             emit(c)
+        for proj, block in self.layers:
+            for c in proj:
+                emit(c)
+            self._issue_block(stream, emit, block, beside=events is None)
+        if getattr(self, "_prep_done", None) is not None:
+            self._wait_prep(self.torch.cuda.ExternalStream(stream, device=self.dev))
         if before_tail is not None:
             before_tail()
         self._issue_tail(stream, emit, beside=events is None)
+
+    def _issue_block(self, stream: int, emit, block, beside: bool) -> None:
+        """One layer's block. With `beside`, a DeltaNet layer's a|b projection goes on the second stream as soon as
+        the block input is complete (beside the codes and the in-projection), and its gates and conv-state update
+        (conv_prep) follow it there once the layer's in-projection and q tails are done, beside the next layer's
+        projector and codes; the next in-projection (which rewrites the shared tail rows conv_prep reads) and the
+        fill wait for them."""
+        if not (beside and any(c[0] == "ridgefill_gemm_nt_bias" for c in block)):
+            for c in block:
+                emit(c)
+            return
+        torch = self.torch
+        if getattr(self, "side", None) is None:
+            self.side = torch.cuda.Stream(device=self.dev)
+        main, side = torch.cuda.ExternalStream(stream, device=self.dev), self.side
+        ready = torch.cuda.Event()
+        ready.record(main)
+        side.wait_event(ready)
+        for c in block:
+            if c[0] == "ridgefill_gemm_nt_bias":
+                emit(c, side.cuda_stream)
+        for c in block:
+            if c[0] == "ridgefill_gemm_nt_bias":
+                continue
+            if c[0] == "ridgefill_gdn_conv_prep":
+                issued = torch.cuda.Event()
+                issued.record(main)
+                side.wait_event(issued)
+                emit(c, side.cuda_stream)
+                self._prep_done = torch.cuda.Event()
+                self._prep_done.record(side)
+                continue
+            if c[0] in ("ridgefill_gdn_in_proj", "ridgefill_gemm_nt_q_bias"):
+                self._wait_prep(main)
+            emit(c)
+
+    def _wait_prep(self, main) -> None:
+        """The pass's stream waits for the last conv_prep issued on the second stream (if one is pending)."""
+        if getattr(self, "_prep_done", None) is not None:
+            main.wait_event(self._prep_done)
+            self._prep_done = None
 
     def _issue_tail(self, stream: int, emit, beside: bool) -> None:
         """The fill and what follows it. With `beside` (and the fill in its per-head form) the decay sums go on a

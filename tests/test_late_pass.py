@@ -147,28 +147,60 @@ class _Streams:
         self.cuda = _Cuda
 
 
-@pytest.mark.parametrize("shape", SHAPES[:3], ids=["config0", "all24_small", "ragged"])
-def test_decay_sums_run_beside_the_per_head_fill(shape):
-    """With the fill in its per-head form (head dim 128, at least 64 chains), the decay sums are issued on a second
-    stream that waits for everything before the fill, and the correction waits for them; otherwise the tail stays
-    in order on the pass's stream."""
+SIDE_OPS = ("ridgefill_gemm_nt_bias", "ridgefill_gdn_conv_prep")
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=["config0", "all24_small", "ragged", "grouped"])
+def test_the_second_stream_plan(shape):
+    """The pass's second stream, checked on its issue log:
+    * each DeltaNet layer's a|b projection goes there after an event recorded once its projector is issued, and its
+      conv_prep after an event recorded once its in-projection and q tails are issued; the next in-projection (or
+      mixed projection) and the fill come after a wait for that conv_prep;
+    * with the fill in its per-head form (head dim 128, at least 64 chains) the decay sums go there too, from an
+      event recorded just before the fill, and the correction waits for them; otherwise they stay in order;
+    * everything else stays on the pass's stream, and an ordered pass (`events` given) uses no second stream."""
     p = LP.LatePass(shape, "cpu", seed=1)
     fake = _Streams()
     p.torch = fake
-    p._launch = lambda op, r, tens, params, stream: fake.log.append(("launch", op, stream))   # noqa: E731
+    mixed = getattr(p, "mixed", None)   # only passes with block inputs have the mixed projection's buffer
+    lo = mixed.data_ptr() if mixed is not None else 0
+    hi = lo + (mixed.numel() * mixed.element_size() if mixed is not None else 0)
+    writes_mixed = set()
+
+    def launch(op, r, tens, params, stream):
+        if op != "ridgefill_gdn_conv_prep" and any(lo <= (getattr(t, "data", None) or 0) < hi for t in tens):
+            writes_mixed.add(len(fake.log))
+        fake.log.append(("launch", op, stream))
+
+    p._launch = launch
     p.run(5)
-    launches = [(e[1], e[2]) for e in fake.log if e[0] == "launch"]
+    log = fake.log
+    launches = [(e[1], e[2]) for e in log if e[0] == "launch"]
     G, hv = shape.n_gdn, shape.hv
     beside = shape.head == 128 and G * hv * shape.n_seq >= 64
     assert p.rho_beside_fill == beside
-    rho = [st for op, st in launches if op == "ridgefill_rho_update"]
-    assert len(rho) == G and all(st == (777 if beside else 5) for st in rho)
-    assert all(st == 5 for op, st in launches if op != "ridgefill_rho_update")
-    if beside:
-        log = fake.log
+    for op, st in launches:
+        side = op in SIDE_OPS or (op == "ridgefill_rho_update" and beside)
+        assert st == (777 if side else 5), (op, st)
+    if shape.block_inputs and G:
+        ab = [i for i, e in enumerate(log) if e[:2] == ("launch", "ridgefill_gemm_nt_bias")]
+        prep = [i for i, e in enumerate(log) if e[:2] == ("launch", "ridgefill_gdn_conv_prep")]
+        assert len(ab) == len(prep) == G
+        for i in ab + prep:   # each side launch right after its wait on an event of the pass's stream
+            assert log[i - 1] == ("wait", 777, 5) and log[i - 2] == ("record", 5)
+        writers = sorted(writes_mixed)   # the in-projections and q tails (the rows conv_prep reads)
+        assert len(writers) >= G
         fill = log.index(("launch", "ridgefill_gdn_fill", 5))
-        # the side stream starts from an event recorded on the pass's stream just before the fill
+        for j in prep:
+            stop = min([w for w in writers if w > j] + [fill])
+            assert ("record", 777) in log[j:stop] and ("wait", 5, 777) in log[j:stop], (j, stop)
+    if beside:
+        fill = log.index(("launch", "ridgefill_gdn_fill", 5))
         assert log[fill - 2] == ("record", 5) and log[fill - 1] == ("wait", 777, 5)
         last_rho = max(i for i, e in enumerate(log) if e[:2] == ("launch", "ridgefill_rho_update"))
         corr = log.index(("launch", "ridgefill_state_correct", 5), fill)
         assert ("record", 777) in log[last_rho:corr] and ("wait", 5, 777) in log[last_rho:corr]
+    # the ordered pass
+    fake.log.clear()
+    p.run(5, events={})
+    assert all(e[0] == "launch" and e[2] == 5 for e in fake.log)
