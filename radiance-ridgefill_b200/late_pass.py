@@ -674,8 +674,7 @@ class LatePass:
         def block(li):
             if L.ridgefill_team_wait(own, li, e * (R - 1) * ctas, C.c_void_p(stream)) != abi.OK:
                 raise RuntimeError("ridgefill_team_wait failed")
-            for c in self.layers[li][1]:
-                emit(c)
+            self._issue_block(stream, emit, self.layers[li][1], beside)
 
         for li, (proj, _block) in enumerate(self.layers):
             for c in proj:
@@ -694,6 +693,7 @@ class LatePass:
         done = torch.cuda.Event()
         done.record(comm)
         main.wait_event(done)   # the last gathers read this rank's block inputs: done before the next pass writes them
+        self._wait_prep(main)
         if before_tail is not None:
             before_tail()
         self._issue_tail(stream, emit, beside)
