@@ -350,6 +350,9 @@ class LatePass:
         self.x = list(self.x_all.unbind(0))
         self.codes_x = empty(T, d, dtype=torch.int8)
         self.scale_x = empty(T, d // grp, dtype=torch.float32)
+        # the attention layers' block input codes: their own buffer, as their blocks run on the second stream
+        self.codes_a = empty(T, d, dtype=torch.int8) if s.n_attn else None
+        self.scale_a = empty(T, d // grp, dtype=torch.float32) if s.n_attn else None
         self.state = x["state"].clone()
         self.applied = torch.zeros(s.n_seq, G * hv, 1, 1, dtype=torch.float32, device=dev)
         self.nd = torch.zeros(s.n_seq, G * hv, 1, 2, dtype=torch.float32, device=dev)
@@ -491,8 +494,8 @@ class LatePass:
                                    P("conv", 4), P("columns", 0 if self.fused_in else 1)], f"{li}"))
             elif kind == "A" and self.hkv_r:
                 Ha, Dh = self.hkv_r, s.head_attn
-                block.append(quant(self.x[li], self.codes_x, self.scale_x, f"x {li}"))
-                block.append(gemm_q(self.codes_x, self.scale_x, x["w_kv"][ai], x["s_kv"][ai], None, _t(self.kv), 2 * Ha * Dh,
+                block.append(quant(self.x[li], self.codes_a, self.scale_a, f"x {li}"))
+                block.append(gemm_q(self.codes_a, self.scale_a, x["w_kv"][ai], x["s_kv"][ai], None, _t(self.kv), 2 * Ha * Dh,
                                     f"kv {li}"))
                 block.append(call("ridgefill_attn_kv_fill",
                                   [_t(self.kv, [T, Ha, Dh], [2 * Ha * Dh, Dh, 1]),
@@ -571,8 +574,8 @@ class LatePass:
             for c in proj:
                 emit(c)
             self._issue_block(stream, emit, block, beside=events is None)
-        if getattr(self, "_prep_done", None) is not None:
-            self._wait_prep(self.torch.cuda.ExternalStream(stream, device=self.dev))
+        if getattr(self, "_prep_done", None) is not None or getattr(self, "_side_used", False):
+            self._join_side(self.torch.cuda.ExternalStream(stream, device=self.dev))
         if before_tail is not None:
             before_tail()
         self._issue_tail(stream, emit, beside=events is None)
@@ -583,7 +586,8 @@ class LatePass:
         (conv_prep) follow it there once the layer's in-projection and q tails are done, beside the next layer's
         projector and codes; the next in-projection (which rewrites the shared tail rows conv_prep reads) and the
         fill wait for them."""
-        if not (beside and any(c[0] == "ridgefill_gemm_nt_bias" for c in block)):
+        attention = any(c[0] == "ridgefill_attn_kv_fill" for c in block) and self.codes_a is not None
+        if not (beside and (attention or any(c[0] == "ridgefill_gemm_nt_bias" for c in block))):
             for c in block:
                 emit(c)
             return
@@ -594,6 +598,13 @@ class LatePass:
         ready = torch.cuda.Event()
         ready.record(main)
         side.wait_event(ready)
+        if attention:
+            # an attention layer's whole block (its codes in their own buffer, the k|v projection, the cache
+            # write): nothing on the pass's stream reads what it writes before the fill
+            for c in block:
+                emit(c, side.cuda_stream)
+            self._side_used = True
+            return
         for c in block:
             if c[0] == "ridgefill_gemm_nt_bias":
                 emit(c, side.cuda_stream)
@@ -617,6 +628,15 @@ class LatePass:
         if getattr(self, "_prep_done", None) is not None:
             main.wait_event(self._prep_done)
             self._prep_done = None
+
+    def _join_side(self, main) -> None:
+        """The pass's stream waits for everything issued on the second stream so far (before the fill)."""
+        self._wait_prep(main)
+        if getattr(self, "_side_used", False):
+            done = self.torch.cuda.Event()
+            done.record(self.side)
+            main.wait_event(done)
+            self._side_used = False
 
     def _issue_tail(self, stream: int, emit, beside: bool) -> None:
         """The fill and what follows it. With `beside` (and the fill in its per-head form) the decay sums go on a
@@ -693,7 +713,7 @@ class LatePass:
         done = torch.cuda.Event()
         done.record(comm)
         main.wait_event(done)   # the last gathers read this rank's block inputs: done before the next pass writes them
-        self._wait_prep(main)
+        self._join_side(main)
         if before_tail is not None:
             before_tail()
         self._issue_tail(stream, emit, beside)

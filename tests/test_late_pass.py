@@ -1,6 +1,7 @@
 """The late-layer pass's launch list on the CPU: built over host tensors, every launch's operands and parameters
 pass its device row's operand checks (the rows' exported parse functions, called directly: nothing is launched),
 the pass issues the reference's op order, and its CPU twin (oracle/cpu_path.CpuLatePass) runs the same shapes."""
+import collections
 import ctypes as C
 
 import numpy as np
@@ -179,9 +180,18 @@ def test_the_second_stream_plan(shape):
     G, hv = shape.n_gdn, shape.hv
     beside = shape.head == 128 and G * hv * shape.n_seq >= 64
     assert p.rho_beside_fill == beside
-    for op, st in launches:
-        side = op in SIDE_OPS or (op == "ridgefill_rho_update" and beside)
-        assert st == (777 if side else 5), (op, st)
+    want = collections.Counter()
+    for c in p.head:
+        want[(c[0], 5)] += 1
+    for proj, block in p.layers:
+        attention = any(c[0] == "ridgefill_attn_kv_fill" for c in block)
+        for c in proj:
+            want[(c[0], 5)] += 1
+        for c in block:   # an attention layer's whole block, a DeltaNet layer's a|b and conv_prep: second stream
+            want[(c[0], 777 if attention or c[0] in SIDE_OPS else 5)] += 1
+    for c in p.tail:
+        want[(c[0], 777 if c[0] == "ridgefill_rho_update" and beside else 5)] += 1
+    assert collections.Counter(launches) == want
     if shape.block_inputs and G:
         ab = [i for i, e in enumerate(log) if e[:2] == ("launch", "ridgefill_gemm_nt_bias")]
         prep = [i for i, e in enumerate(log) if e[:2] == ("launch", "ridgefill_gdn_conv_prep")]
