@@ -532,7 +532,7 @@ class LatePass:
         one_kernel_fill = D != 128 or G * hv * s.n_seq >= 64
         self.kernels = sum(1 if (c[0] == "ridgefill_gdn_fill" and one_kernel_fill) else self.KERNELS[c[0]] for c in self.calls)
         # In the per-head form the fill's CTAs wait on nothing but their own SM, and a launch of L Hv chains over the
-        # SMs leaves some of them idle in its last round: the decay sums (which read only a, the mask and the bounds)
+        # SMs leaves some of them idle in its last wave: the decay sums (which read only a, the mask and the bounds)
         # run there, on a second stream, instead of after the fill. The other forms keep the tail in order (the
         # cooperative one needs all its CTAs resident at once).
         self.rho_beside_fill = D == 128 and G * hv * s.n_seq >= 64
