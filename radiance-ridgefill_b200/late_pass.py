@@ -12,13 +12,15 @@ launch of this library's sm_100a device rows through the C ABI.
                                     ridgefill_select fused into the projector's epilogue)
       ridgefill_quant_act_i8g       the block input's codes (what the int8 block reads)
       DeltaNet layer (arch/qwen4exp_fill.h:29-61):
-        ridgefill_gemm_nt_bias      the a|b projection (bf16; first, while the block input is still in L2)
+        ridgefill_gemm_nt_bias      the a|b projection (bf16)
         ridgefill_gemm_nt_q_bias    the mixed q|k|v projection (int8, no bias)
         ridgefill_gdn_conv_prep     conv, SiLU, q/k norm, gate and beta, into this layer's heads of the
                                     pass-wide k, v, g, beta arrays
       attention layer (arch/qwen4exp_fill.h:100-115):
         ridgefill_gemm_nt_q_bias    the k|v projection (int8, no bias)
         ridgefill_attn_kv_fill      k norm, rotary, the paged cache store
+      (a DeltaNet layer's a|b projection and conv_prep, and an attention layer's whole block, run on a second
+      stream beside the chain of projectors, codes and in-projections: LatePass._issue_block)
     ridgefill_gdn_fill              ONE launch for every DeltaNet layer's chunk fill (state only)
     ridgefill_rho_update            per DeltaNet layer, from its a values
     ridgefill_state_correct apply   every DeltaNet layer at once
@@ -446,8 +448,9 @@ class LatePass:
             if kind == "G" and s.block_inputs:
                 C, Cq = self.conv_dim_r, hk * D
                 block.append(quant(self.x[li], self.codes_x, self.scale_x, f"x {li}"))
-                # the a|b projection straight after the codes: the quantiser reads the block input last row first,
-                # so the rows it read last (the first ones) are still in L2 when this reads them in order
+                # the a|b projection: on the second stream it starts with the codes; in an ordered pass it follows
+                # them, and as the quantiser reads the block input last row first, the rows it read last (the first
+                # ones) are still in L2 when this reads them in order
                 block.append(call("ridgefill_gemm_nt_bias", [_t(self.x[li]), _t(x["w_ab"][gi]), _t(self.zero_ab), A_,
                                                              _t(self.ab[gi])],
                                   [P("M", T), P("N", 2 * hv), P("K", d), S("dtype", "bf16")], f"ab {li}"))
@@ -547,9 +550,10 @@ class LatePass:
             raise RuntimeError(f"{op}: device row refused or failed (rc {rc})")
 
     def run(self, stream: int, events=None, before_tail=None) -> None:
-        """Issue one pass on `stream` (and, on a team, the column gathers on a second stream). `events` (optional)
-        maps an op name to a list of (start, end) CUDA event pairs, one pair per launch of that op, recorded on the
-        current torch stream around each launch. `before_tail` (optional) is called on the host once every layer's
+        """Issue one pass on `stream`, with the work that can run beside the chain on this pass's second stream
+        (`_issue_block`, `_issue_tail`) and, on a team, the column gathers on a third. `events` (optional) maps an
+        op name to a list of (start, end) CUDA event pairs, one pair per launch of that op, recorded on the current
+        torch stream around each launch; such a pass is issued in order on `stream` alone. `before_tail` (optional) is called on the host once every layer's
         launches are on `stream` and before the fill's: work the caller queues behind `stream` at that point (an
         event) sees `results_split()[0]` final, so their readback can overlap the fill."""
         counts = {}
@@ -585,7 +589,8 @@ class LatePass:
         the block input is complete (beside the codes and the in-projection), and its gates and conv-state update
         (conv_prep) follow it there once the layer's in-projection and q tails are done, beside the next layer's
         projector and codes; the next in-projection (which rewrites the shared tail rows conv_prep reads) and the
-        fill wait for them."""
+        fill wait for them. An attention layer's whole block goes there too (its codes in their own buffer); the
+        fill waits for the second stream as a whole (`_join_side`)."""
         attention = any(c[0] == "ridgefill_attn_kv_fill" for c in block) and self.codes_a is not None
         if not (beside and (attention or any(c[0] == "ridgefill_gemm_nt_bias" for c in block))):
             for c in block:
