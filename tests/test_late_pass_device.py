@@ -170,3 +170,34 @@ def test_the_pass_and_its_fill_repeat_bit_for_bit(cuda):
         outs.append(p.state.clone())
     for o in outs[1:]:
         assert torch.equal(o, outs[0])
+
+
+@gpu
+def test_the_two_stream_pass_equals_the_ordered_pass(cuda):
+    """The pass as the bench times it (a|b projections, conv_prep, attention blocks and decay sums on a second
+    stream) against the same pass issued in order on one stream (`events` given), from fresh objects over the same
+    seeded inputs, two passes each: every result bit for bit. And the results `results_split()` declares final when
+    `before_tail` is called (mask, attention caches, conv states) are, at that point, what they are after the pass:
+    copies taken on another stream from an event recorded in the hook equal the buffers at the end."""
+    torch = cuda
+    shape = LP.LateShape(T=640, layers="GGAG", seqlens=(200, 440))   # 3 x 32 heads x 2 sequences: the per-head fill
+    two, one = LP.LatePass(shape, "cuda", seed=3), LP.LatePass(shape, "cuda", seed=3)
+    assert two.rho_beside_fill
+    s, copies = torch.cuda.Stream(), torch.cuda.Stream()
+    early, _ = two.results_split()
+    snaps = []
+
+    def hook():
+        at = torch.cuda.Event()
+        at.record(s)
+        copies.wait_event(at)
+        with torch.cuda.stream(copies):
+            snaps[:] = [t.clone() for t in early]
+
+    for _ in range(2):
+        two.run(s.cuda_stream, before_tail=hook)
+        one.run(s.cuda_stream, events={})
+    torch.cuda.synchronize()
+    for x, y in zip(two.results(), one.results()):
+        assert torch.equal(x, y)
+    assert len(snaps) == len(early) and all(torch.equal(x, y) for x, y in zip(snaps, early))
