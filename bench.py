@@ -2,15 +2,15 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl mine|reference]
 
-A step is one approximate pass of the RidgeFill step over a 32,768-row prefill chunk of the 48-layer stack
-(BASELINE config 3): the 24 late layers, 18 Gated DeltaNet and 6 attention layers, through this library's sm_100a
+A step is one approximate pass of the RidgeFill step over a 32,768-row prefill chunk of the 48-layer stack:
+the 24 late layers, 18 Gated DeltaNet and 6 attention layers, through this library's sm_100a
 device rows (late_pass.LatePass): the class mask (30 % of rows exact) and the layer-S stream's codes once, then per
 layer the int8 projector d 2,048 (per-column scales, fused bias, written straight into the block input's
 approximated rows: the select fused into its epilogue) and the block input's codes; per DeltaNet
 layer the int8 mixed q|k|v projection, the bf16 a|b projection and conv_prep (16 q/k, 32 v heads x 128); per
 attention layer the int8 k|v projection and the K/V cache write (2 kv heads x 256, imrope); then one fill launch over
 all 18 DeltaNet layers' 576 heads between a state undo and apply over the same heads, rho per layer, the hazard record.
-Synthetic inputs with BASELINE's shapes and distributions, seeded; the pass reads > 10 GB, far past the 126 MB L2, so
+Synthetic inputs with the published benchmark's shapes and distributions, seeded; the pass reads > 10 GB, far past the 126 MB L2, so
 no flush is needed between steps.
 
 value   device time of K passes with inputs resident in HBM (CUDA events, max over ranks)
@@ -22,7 +22,7 @@ N > 1   one process per GPU (torchrun), tensor parallel over ONE prompt: each ra
         span (with their k heads) and its attention kv heads, the projector's output columns split across ranks and
         all-gathered over NVLink by the library's peer kernels ("scaling": "strong"; value = the prompt's tokens / the
         slowest rank's time)
-extra   the config-5 ragged batch (one 32K prompt after six of U[256, 2,048] rows) and the one-layer pass, device time
+extra   the mixed ragged batch (one 32K prompt after six of U[256, 2,048] rows) and the one-layer pass, device time
 --impl reference   the CPU arm: the same pass on the host -- the reference's own host rows compiled from its sources
         (oracle/_ref) for mask, select, correction, rho, hazard, and the CPU restatement for the GEMMs, quantiser,
         conv_prep, K/V write and fill the reference does not contain -- on a bounded sample (2,048 rows, the first 4
@@ -46,7 +46,7 @@ sys.path.insert(0, str(ROOT / "oracle"))
 
 METRIC = "prefill tokens/s at 32K (RidgeFill step)"
 T_FULL = 32768
-WORKLOAD = ("BASELINE config 3: the full RidgeFill step over the 24 late layers of a 48-layer stack (18 Gated "
+WORKLOAD = ("the full RidgeFill step over the 24 late layers of a 48-layer stack (18 Gated "
             "DeltaNet + 6 attention), hidden 2,048, int8 per-column projectors, 32,768-row prompt, 30 % of rows exact")
 CPU_ROWS, CPU_LAYERS = 2048, 4
 
@@ -159,7 +159,7 @@ def cpu_arm(passes: int, warmup: int) -> dict:
     the rows, except the mask's O(w^2) rank count, which is a small part at this size)."""
     import cpu_path
     import late_pass as LP
-    shape = LP.config3(CPU_ROWS)
+    shape = LP.full_step(CPU_ROWS)
     inputs = cpu_path.to_host(LP.late_inputs(shape, "cpu", 7))
     c = cpu_path.CpuLatePass(shape, inputs, layers=CPU_LAYERS)
     sec = c.time_passes(passes, warmup)
@@ -251,7 +251,7 @@ def run_mine(args):
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=120))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    shape = LP.config3(T_FULL)
+    shape = LP.full_step(T_FULL)
     team = LP.Team.create(world, rank, dist) if world > 1 else None
     p = LP.LatePass(shape, str(dev), seed=1234, team=team)
     stream = torch.cuda.Stream(device=dev)
@@ -348,12 +348,12 @@ def run_mine(args):
     e2e_ms = e_start.elapsed_time(e_end) / args.steps
     del sets[1]
 
-    # ---------------------------------------------------------- extras (one GPU): config 5 and the one-layer pass
+    # ---------------------------------------------------------- extras (one GPU): the ragged batch and the one-layer pass
     extra = {}
     if world == 1 and not args.no_extra:
         del p
         torch.cuda.empty_cache()
-        extra["config5_ragged"] = time_extra(LP.LatePass(LP.config5(), str(dev), seed=99), stream, args.steps)
+        extra["ragged_batch"] = time_extra(LP.LatePass(LP.ragged_batch(), str(dev), seed=99), stream, args.steps)
         torch.cuda.empty_cache()
         extra["one_layer_pass"] = time_one_layer(stream, args.steps)
 
@@ -405,7 +405,7 @@ def time_extra(p, stream, steps: int) -> dict:
         stream.synchronize()
     ms = a.elapsed_time(b) / steps
     s = p.s
-    return {"workload": f"BASELINE config 5: prompts of {list(s.lengths)} rows, the last approximated, the 24 late "
+    return {"workload": f"mixed ragged batch: prompts of {list(s.lengths)} rows, the last approximated, the 24 late "
                         f"layers; the fill over every sequence (varlen)", "rows": s.T, "ms_per_step": ms,
             "tokens_per_s": s.T / (ms * 1e-3)}
 
@@ -425,7 +425,7 @@ def time_one_layer(stream, steps: int) -> dict:
         b.record(stream)
         stream.synchronize()
     ms = a.elapsed_time(b) / steps
-    return {"workload": "one late layer: projector d 2,048 + DeltaNet fill (config 2 shapes, inputs given) + mask, "
+    return {"workload": "one late layer: projector d 2,048 + DeltaNet fill (16 q/k and 32 v heads of 128, inputs given) + mask, "
                         "select, correction, rho, hazard", "rows": T_FULL, "ms_per_step": ms,
             "tokens_per_s": T_FULL / (ms * 1e-3)}
 
@@ -458,7 +458,7 @@ def run_only(args):
 
 
 def run_profile_pass(args):
-    """Issue --warmup whole passes of the config-3 step, then one more between cudaProfilerStart and
+    """Issue --warmup whole passes of the full step, then one more between cudaProfilerStart and
     cudaProfilerStop, and nothing else (no timing, no extras): the command an ncu launch list of one pass runs
     (`ncu --profile-from-start off` sees that pass's launches only, not the input set-up's nor the warm-up's)."""
     import torch
@@ -485,7 +485,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
-    ap.add_argument("--no-extra", action="store_true", help="skip the config-5 and one-layer extras")
+    ap.add_argument("--no-extra", action="store_true", help="skip the ragged-batch and one-layer extras")
     ap.add_argument("--only", default=None, help="profile mode: launch only this row's launches of the pass")
     ap.add_argument("--rows", type=int, default=T_FULL, help="rows of the chunk in --only mode")
     ap.add_argument("--layers", default="GGGA" * 6, help="late layers in --only / --profile-pass mode (G DeltaNet, A attention)")

@@ -442,7 +442,7 @@ extern "C" int ridgefill_hazard_parse(const RadArgs* a, RidgeFillHazard* g) {
  * ridgefill_gemm_nt_q_bias (with_bias 1: a, a_scale, b, b_scale, bias, y, acc). a_scale is required (an
  * i8a8 product has activation scales); a_sum and b_ref (zero-point terms of other dtypes) must be
  * absent. K must be a multiple of 128 and of `group`; `group` divides K (128, or K itself for
- * BASELINE's per-row / per-column scaling); rows of a and codes of b start 16-byte aligned (the TMA
+ * the late pass's per-row / per-column scaling); rows of a and codes of b start 16-byte aligned (the TMA
  * reads them in 128-byte rows). */
 extern "C" int ridgefill_gemm_q_parse(const RadArgs* a, int with_bias, RidgeFillGemmQ* g) {
     *g = RidgeFillGemmQ{};

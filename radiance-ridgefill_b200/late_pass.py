@@ -88,19 +88,19 @@ class LateShape:
         return len(self.lengths)
 
 
-def config0() -> LateShape:
+def mini_model() -> LateShape:
     """The reference's CPU mini model: d 256, 512 rows, 4 DeltaNet layers of 4 q/k and 8 v heads of 32, the fill's
     inputs given, 25 % of the rows kept exact."""
     return LateShape(T=512, d=256, layers="GGGG", hk=4, hv=8, head=32, share=0.25, vocab=4096, block_inputs=False)
 
 
-def config3(T: int = 32768) -> LateShape:
+def full_step(T: int = 32768) -> LateShape:
     """The full step over the 24 late layers of the 48-layer stack (18 DeltaNet + 6 attention), hidden 2,048,
     DeltaNet 16 q/k and 32 v heads of 128, attention 2 kv heads of 256, 30 % of the rows exact."""
     return LateShape(T=T)
 
 
-def config5(seed: int = 0, long: int = 32768, short: int = 6) -> LateShape:
+def ragged_batch(seed: int = 0, long: int = 32768, short: int = 6) -> LateShape:
     """The mixed ragged batch: six prompts of U[256, 2,048] rows, then one 32K prompt (the approximated one)."""
     import random
     r = random.Random(seed)
@@ -109,7 +109,7 @@ def config5(seed: int = 0, long: int = 32768, short: int = 6) -> LateShape:
 
 
 def late_inputs(s: LateShape, device, seed: int = 0) -> dict:
-    """Seeded synthetic inputs and weights of one pass, with BASELINE's distributions: h_S and the exact block
+    """Seeded synthetic inputs and weights of one pass, with the published benchmark's distributions: h_S and the exact block
     inputs ~N(0,1) bf16, int8 weights ~U[-127,127] with f32 per-column scales ~U(1e-3,1e-2), the DeltaNet and
     attention weights at the served model's scales. Torch tensors on `device` (a CPU device for the CPU arm)."""
     import torch

@@ -77,7 +77,7 @@ class Step:
         self.bias = (0.1 * normal(d)).to(torch.bfloat16)
         self.x_proj = torch.empty(T, d, dtype=torch.bfloat16, device=dev)
         self.x = normal(T, d).to(torch.bfloat16)          # the exact block input the select overwrites
-        # --- DeltaNet (config 2): q, k L2-normalised, beta = sigmoid(N), g = -softplus(N)
+        # --- DeltaNet (16 q/k and 32 v heads of 128): q, k L2-normalised, beta = sigmoid(N), g = -softplus(N)
         k = normal(T, hk, D)
         self.k = (k / k.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
         self.v = normal(T, hv, D).to(torch.bfloat16)

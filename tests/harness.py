@@ -411,7 +411,7 @@ def gdn_params(T, hk, hv, scale=None):
 
 
 def gdn_inputs(seed, T, hk, hv, decay="fast", slots=3):
-    """Config-2-style synthetic inputs: q, k L2-normalised bf16, v ~ N(0,1) bf16, beta = sigmoid(N(0,1)),
+    """Synthetic fill inputs of the single-layer benchmark's kind: q, k L2-normalised bf16, v ~ N(0,1) bf16, beta = sigmoid(N(0,1)),
     log decay g = -softplus(N(0,1)) ("fast": decay exp(g) about 0.5 a row) or a slow decay."""
     rng = np.random.default_rng(seed)
     k = rng.standard_normal((T, hk, 128)).astype(np.float32)

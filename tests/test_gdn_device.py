@@ -67,7 +67,7 @@ def test_fill_empty_sequence_keeps_state(cuda, product_lib):
 
 
 def test_fill_full_size_split_is_one_call(cuda, product_lib):
-    """Config 2 at full size: T = 32,768, 16 q/k heads, 32 v heads. Two calls over [0, T/2) and [T/2, T)
+    """The single-layer fill at full size: T = 32,768, 16 q/k heads, 32 v heads. Two calls over [0, T/2) and [T/2, T)
     with the state carried equal one call over [0, T) bit for bit (chunks are anchored at the call's
     sequence start and T/2 is a chunk boundary); two heads checked against the float64 rule."""
     torch = cuda

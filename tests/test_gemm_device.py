@@ -1,7 +1,7 @@
 """The int8 projector on B200 (ridgefill_gemm_nt_q, ridgefill_gemm_nt_q_bias, ridgefill_quant_act_i8g)
 against the CPU oracle: the activation codes and scales bit for bit, every int32 block sum bit for bit,
 and the bf16 outputs bit for bit (the f32 fold is defined exactly, in block order, with one fma a block:
-oracle/ridgefill_oracle.cpp oracle_gemm_nt_q). Shapes: BASELINE's per-column projector (group = K),
+oracle/ridgefill_oracle.cpp oracle_gemm_nt_q). Shapes: the late pass's per-column projector (group = K),
 the folder's i8*bf16[1x128] encoding (group 128) at the real model shape N 2,560 / K 10,240, row
 counts that are not tile multiples, and the folder path through the row's own stored-form hooks."""
 import numpy as np
@@ -113,7 +113,7 @@ def test_gemm_matches_oracle_bitwise(cuda, product_lib, M, N, K, group):
 
 
 def test_gemm_projector_full_size_sampled(cuda, product_lib):
-    """BASELINE's projector: T = 32,768 rows x d = 2,048, per-row activation and per-column weight
+    """The late pass's projector: T = 32,768 rows x d = 2,048, per-row activation and per-column weight
     scales (group = K). Every output row would take the CPU oracle minutes, so 96 sampled rows (each
     128-row tile band represented) are checked bit for bit, and the whole output against a float64
     evaluation on the GPU within one bf16 ulp."""

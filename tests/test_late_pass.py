@@ -19,7 +19,7 @@ PARSE = {"ridgefill_mask": "ridgefill_mask_parse", "ridgefill_quant_act_i8g": "r
          "ridgefill_rho_update": "ridgefill_rho_parse", "ridgefill_hazard": "ridgefill_hazard_parse",
          "ridgefill_gdn_in_proj": "ridgefill_in_proj_parse"}
 
-SHAPES = [LP.config0(), LP.LateShape(T=256, d=256, hk=2, hv=4), LP.LateShape(T=300, d=256, layers="GA", hk=2, hv=4,
+SHAPES = [LP.mini_model(), LP.LateShape(T=256, d=256, hk=2, hv=4), LP.LateShape(T=300, d=256, layers="GA", hk=2, hv=4,
                                                                               seqlens=(100, 80, 120)),
           LP.LateShape(T=256, d=256, hk=2, hv=4, group=128)]
 
@@ -39,7 +39,7 @@ def _parse(lib, op, tens, params):
     return rc
 
 
-@pytest.mark.parametrize("shape", SHAPES, ids=["config0", "all24_small", "ragged", "grouped"])
+@pytest.mark.parametrize("shape", SHAPES, ids=["mini_model", "all24_small", "ragged", "grouped"])
 def test_every_launch_passes_its_operand_checks(shape, product_lib):
     p = LP.LatePass(shape, "cpu", seed=1)
     for op, _row, tens, params, tag in p.calls:
@@ -88,7 +88,7 @@ def test_cpu_twin_runs_the_same_pass(oracle_lib):
     assert (cpu.cache[0][0] != 0).any()
 
 
-@pytest.mark.parametrize("shape", SHAPES[:3], ids=["config0", "all24_small", "ragged"])
+@pytest.mark.parametrize("shape", SHAPES[:3], ids=["mini_model", "all24_small", "ragged"])
 def test_results_before_the_fill_are_final_when_the_hook_runs(shape):
     """run(before_tail=...) calls the hook once, after every layer's launches and before the fill's; the results
     it declares final there (mask, attention caches, conv states) are written by no launch after it (the mask is
@@ -151,7 +151,7 @@ class _Streams:
 SIDE_OPS = ("ridgefill_gemm_nt_bias", "ridgefill_gdn_conv_prep")
 
 
-@pytest.mark.parametrize("shape", SHAPES, ids=["config0", "all24_small", "ragged", "grouped"])
+@pytest.mark.parametrize("shape", SHAPES, ids=["mini_model", "all24_small", "ragged", "grouped"])
 def test_the_second_stream_plan(shape):
     """The pass's second stream, checked on its issue log:
     * each DeltaNet layer's a|b projection goes there after an event recorded once its projector is issued, and its

@@ -17,7 +17,7 @@ the same seeded inputs. Every buffer the pass writes is compared:
                                                        projection) are bit for bit the host's; 1e-3 on rho for a
                                                        head that read an a value one bf16 ulp off
 
-The shapes: the reference's CPU mini model (config 0: d 256, 512 rows, 4 DeltaNet layers of 4 / 8 heads of 32), a
+The shapes: the reference's CPU mini model (d 256, 512 rows, 4 DeltaNet layers of 4 / 8 heads of 32), a
 2,048-row sample of the full step's first four late layers (G G G A) at full width, all 24 late layers at 256 rows
 (the fill batched over 18 layers' heads), and a ragged batch of three sequences."""
 import numpy as np
@@ -31,9 +31,9 @@ gpu = pytest.mark.gpu
 FLT_MIN = float(np.finfo(np.float32).tiny)
 
 SHAPES = {
-    "config0": LP.config0(),
-    "config3_T2048_first4": LP.LateShape(T=2048, layers="GGGA"),
-    "config3_T256_all24": LP.LateShape(T=256),
+    "mini_model": LP.mini_model(),
+    "full_step_T2048_first4": LP.LateShape(T=2048, layers="GGGA"),
+    "full_step_T256_all24": LP.LateShape(T=256),
     "ragged_3seq": LP.LateShape(T=1400, layers="GGA", seqlens=(300, 100, 1000)),
 }
 
